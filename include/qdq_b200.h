@@ -1,0 +1,93 @@
+/*
+ * qdq_b200.h — C ABI of the B200 (sm_100a) block-scaled FP4 hot path.
+ *
+ * Every entry point:
+ *   - takes plain device pointers, element counts/strides and a cudaStream_t
+ *     passed as `void*` (NULL = legacy default stream);
+ *   - is stream-ordered: it enqueues work and returns without a host sync;
+ *   - returns QDQ_OK (0) or one of the qdq_status_t codes below; the text of
+ *     the last failure on the calling thread is available from
+ *     qdq_last_error();
+ *   - never calls abort()/exit() and never allocates device memory unless the
+ *     comment says so (scratch comes from the caller's `workspace`).
+ *
+ * dtype codes: QDQ_DTYPE_BF16 = 0, QDQ_DTYPE_FP16 = 1.
+ * Strides (ldx, ldy, ...) are in ELEMENTS of the pointed-to type.
+ */
+#ifndef QDQ_B200_H_
+#define QDQ_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  QDQ_OK = 0,
+  QDQ_ERR_INVALID_ARG = 1,   /* bad shape / null pointer / unknown dtype      */
+  QDQ_ERR_UNSUPPORTED = 2,   /* valid request this build does not implement   */
+  QDQ_ERR_CUDA = 3,          /* a CUDA runtime call or launch failed          */
+  QDQ_ERR_TIMEOUT = 4,       /* a bounded device-side wait gave up            */
+  QDQ_ERR_ALIGNMENT = 5      /* pointer/stride alignment the kernel requires  */
+} qdq_status_t;
+
+enum { QDQ_DTYPE_BF16 = 0, QDQ_DTYPE_FP16 = 1 };
+
+/* Human-readable text of the last non-zero status returned on this thread. */
+const char* qdq_last_error(void);
+
+/* ABI version of this library (major * 100 + minor). */
+int qdq_abi_version(void);
+
+/*
+ * MXFP4 activation quant-dequant: E2M1 elements, one E8M0 scale per 32
+ * consecutive elements of a row.  Bit-exact with the reference
+ *   vllm_qdq_plugin/qdq/mxfp4.py:98-156  (mxfp4_qdq, group_size=32)
+ * including its amax rounding `(bits(amax) + 0x20) & 0xFF80` (bf16; fp16:
+ * `+0x100 & 0xFC00`), scale = 2^(clamp(floor(log2 amax_r) + 125, 0, 254) - 127)
+ * and round-to-nearest-even onto E2M1 with saturation at 6.
+ *
+ *   x      [M, K] bf16/fp16, row stride ldx   (input, not modified)
+ *   y      [M, K] same dtype, row stride ldy  (output; may alias x iff ldx == ldy;
+ *          may be NULL when `codes` is given, to emit only codes + scales)
+ *   codes  optional [M, Kp/2] uint8, Kp = round_up(K, 32): packed E2M1 codes,
+ *          element 2j in bits 0..3 and 2j+1 in bits 4..7 of byte j (NULL = skip)
+ *   scales optional [M, Kp/32] uint8 E8M0 exponents (value 2^(s-127)) (NULL = skip)
+ * group_size must be 32 (the only value the reference's callers use:
+ * vllm_qdq_plugin/patch.py:57,142,149).
+ */
+int qdq_mxfp4(const void* x, void* y, void* codes, void* scales, int64_t M,
+              int64_t K, int64_t ldx, int64_t ldy, int dtype, int group_size,
+              void* stream);
+
+/*
+ * NVFP4 quant-dequant with a given per-tensor global scale: E2M1 elements,
+ * one E4M3 scale per 16 elements, fp32 global scale `gs` read from device
+ * memory (`global_scale`, 1 float).  Bit-exact with the CPU branch of
+ *   vllm/model_executor/layers/quantization/utils/nvfp4_emulation_utils.py:
+ *   ref_nvfp4_quant (:439-452) + ref_nvfp4_quant_dequant (:455-478)
+ * (gs is vLLM's multiplier convention, 448*6/amax).  K % 16 == 0.
+ *   codes  optional [M, K/2] uint8 packed E2M1 (same packing as qdq_mxfp4)
+ *   scales optional [M, K/16] uint8 E4M3 block scales (NULL = skip)
+ */
+int qdq_nvfp4(const void* x, void* y, void* codes, void* scales,
+              const float* global_scale, int64_t M, int64_t K, int64_t ldx,
+              int64_t ldy, int dtype, void* stream);
+
+/*
+ * NVFP4 per-tensor global scale gs = 2688 / amax(|x|) in fp32 (2688 = 448*6),
+ * written to `global_scale_out` (1 float, device).  `workspace` must point to
+ * at least QDQ_AMAX_WORKSPACE_BYTES of device memory; it is cleared by this
+ * call on `stream` before use.
+ */
+#define QDQ_AMAX_WORKSPACE_BYTES 16
+int qdq_nvfp4_global_scale(const void* x, float* global_scale_out,
+                           void* workspace, int64_t M, int64_t K, int64_t ldx,
+                           int dtype, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* QDQ_B200_H_ */

@@ -1,0 +1,159 @@
+"""GPU parity of the MXFP4 / NVFP4 QDQ kernels (through the C ABI).
+
+Bar: bit-exact against (a) the reference's own outputs in tests/golden/ and
+(b) the pinned C oracle at larger, random, strided and odd shapes, including
+the full BASELINE config-1 and config-2 tensors.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import qdq as oq
+
+pytestmark = pytest.mark.gpu
+
+DT = {"bf16": torch.bfloat16, "fp16": torch.float16}
+
+
+def to_dev(bits: np.ndarray, tag: str, dev) -> torch.Tensor:
+    return torch.from_numpy(bits.astype(np.int16)).view(DT[tag]).to(dev)
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def assert_bits_equal(got: np.ndarray, want: np.ndarray, what: str):
+    bad = np.argwhere(got != want)
+    if len(bad):
+        r, c = bad[0]
+        raise AssertionError(f"{what}: {len(bad)} mismatches; first at {tuple(bad[0])}: "
+                             f"got {got[r, c]:#06x} want {want[r, c]:#06x}")
+
+
+# ------------------------------------------------------------------ golden
+@pytest.mark.parametrize("tag", ["bf16", "fp16"])
+@pytest.mark.parametrize("subset", ["natural", "context", "c1_slice", "odd_k"])
+def test_mxfp4_kernel_matches_reference_golden(cuda_device, tag, subset):
+    from vllm_qdq_plugin.qdq import mxfp4_qdq
+    d = golden(f"mxfp4_{tag}.npz")
+    y = mxfp4_qdq(to_dev(d[f"{subset}_x"], tag, cuda_device))
+    assert_bits_equal(bits(y), d[f"{subset}_y"], f"mxfp4 {tag} {subset}")
+
+
+@pytest.mark.parametrize("tag", ["bf16", "fp16"])
+def test_nvfp4_kernel_matches_reference_golden(cuda_device, tag):
+    from vllm_qdq_plugin.qdq import nvfp4_qdq
+    d = golden(f"nvfp4_{tag}.npz")
+    for key in d.files:
+        if not key.endswith("_y"):
+            continue
+        base = key[:-2]
+        gs = d["c2_slice_gs"] if base == "c2_slice" else d["gs" + base.split("_gs")[1]]
+        y = nvfp4_qdq(to_dev(d[base + "_x"], tag, cuda_device),
+                      global_scale=torch.from_numpy(gs.astype(np.float32)).to(cuda_device))
+        assert_bits_equal(bits(y), d[key], f"nvfp4 {tag} {base}")
+
+
+# ------------------------------------------------------------------ oracle
+def _random(m, k, dtype, seed, dev):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(m, k, generator=g) * torch.exp(torch.randn(m, 1, generator=g) * 3)
+    x.view(-1)[torch.randperm(m * k, generator=g)[: max(1, m * k // 500)]] *= 64
+    return x.to(dtype).to(dev)
+
+
+@pytest.mark.parametrize("tag", ["bf16", "fp16"])
+@pytest.mark.parametrize("shape", [(1, 32), (3, 64), (257, 4096), (33, 96), (5, 100), (2, 7),
+                                   (129, 1056)])
+def test_mxfp4_kernel_matches_oracle(cuda_device, tag, shape):
+    from vllm_qdq_plugin.qdq import mxfp4_qdq, mxfp4_quantize
+    x = _random(*shape, DT[tag], seed=shape[0] * 7 + shape[1], dev=cuda_device)
+    want, wcodes, wscales = oq.mxfp4_qdq(bits(x), fp16=(tag == "fp16"), codes=True)
+    assert_bits_equal(bits(mxfp4_qdq(x)), want, f"mxfp4 {tag} {shape}")
+    codes, scales = mxfp4_quantize(x)
+    np.testing.assert_array_equal(codes.cpu().numpy(), wcodes)
+    np.testing.assert_array_equal(scales.cpu().numpy(), wscales)
+
+
+@pytest.mark.parametrize("tag", ["bf16", "fp16"])
+@pytest.mark.parametrize("shape", [(1, 16), (3, 48), (257, 4096), (64, 8192), (7, 80)])
+def test_nvfp4_kernel_matches_oracle(cuda_device, tag, shape):
+    from vllm_qdq_plugin.qdq import nvfp4_global_scale, nvfp4_qdq, nvfp4_quantize
+    x = _random(*shape, DT[tag], seed=shape[0] * 11 + shape[1], dev=cuda_device)
+    gs_dev = nvfp4_global_scale(x)
+    gs = oq.nvfp4_global_scale(bits(x), fp16=(tag == "fp16"))
+    assert np.float32(gs_dev.item()) == np.float32(gs)
+    want, wc, ws = oq.nvfp4_qdq(bits(x), gs, fp16=(tag == "fp16"), codes=True)
+    assert_bits_equal(bits(nvfp4_qdq(x, global_scale=gs_dev)), want, f"nvfp4 {tag} {shape}")
+    assert_bits_equal(bits(nvfp4_qdq(x)), want, f"nvfp4 auto-gs {tag} {shape}")
+    codes, scales = nvfp4_quantize(x, gs_dev)
+    np.testing.assert_array_equal(codes.cpu().numpy(), wc)
+    np.testing.assert_array_equal(scales.cpu().numpy(), ws)
+
+
+def test_strided_rows_and_unaligned_views(cuda_device):
+    from vllm_qdq_plugin.qdq import mxfp4_qdq, nvfp4_qdq
+    base = _random(64, 4096 + 64, torch.bfloat16, seed=5, dev=cuda_device)
+    for view in (base[:, :4096], base[:, 8:8 + 4096 - 32], base[1:, 3:3 + 1024]):
+        want = oq.mxfp4_qdq(bits(view))
+        assert_bits_equal(bits(mxfp4_qdq(view)), want, f"mxfp4 view {tuple(view.stride())}")
+        if view.shape[1] % 16 == 0:
+            gs = torch.tensor([3.0], device=cuda_device)
+            assert_bits_equal(bits(nvfp4_qdq(view, global_scale=gs)),
+                              oq.nvfp4_qdq(bits(view), 3.0), "nvfp4 view")
+    t = base.t()  # column-major: made contiguous by the wrapper
+    assert_bits_equal(bits(mxfp4_qdq(t)), oq.mxfp4_qdq(bits(t)), "transposed")
+
+
+def test_empty_and_special_values(cuda_device):
+    from vllm_qdq_plugin.qdq import mxfp4_qdq, nvfp4_qdq
+    assert mxfp4_qdq(torch.empty(0, 64, dtype=torch.bfloat16, device=cuda_device)).shape == (0, 64)
+    x = torch.zeros(4, 64, dtype=torch.bfloat16, device=cuda_device)
+    x[1] = -0.0
+    x[2, 5] = float("inf")
+    x[2, 6] = -3.0
+    x[3, :32] = torch.finfo(torch.bfloat16).max
+    assert_bits_equal(bits(mxfp4_qdq(x)), oq.mxfp4_qdq(bits(x)), "specials mxfp4")
+    gs = torch.tensor([2.5], device=cuda_device)
+    assert_bits_equal(bits(nvfp4_qdq(x, global_scale=gs)), oq.nvfp4_qdq(bits(x), 2.5),
+                      "specials nvfp4")
+
+
+# ------------------------------------------------------------------ full size
+def test_config1_full_size_bit_exact_and_idempotent(cuda_device):
+    from bench import c1_input
+    from vllm_qdq_plugin.qdq import mxfp4_qdq
+    x = c1_input()
+    y = mxfp4_qdq(x.to(cuda_device))
+    assert_bits_equal(bits(y), oq.mxfp4_qdq(bits(x)), "config 1 full")
+    # QDQ'd activations are exactly MXFP4-representable: a second pass is a no-op
+    assert torch.equal(mxfp4_qdq(y).view(torch.int16), y.view(torch.int16))
+
+
+def test_config2_full_size_bit_exact(cuda_device):
+    from bench import c2_input, global_scale_of
+    from vllm_qdq_plugin.qdq import nvfp4_global_scale, nvfp4_qdq
+    x = c2_input()
+    gs = global_scale_of(x)
+    xd = x.to(cuda_device)
+    assert np.float32(nvfp4_global_scale(xd).item()) == np.float32(gs.item())
+    y = nvfp4_qdq(xd, global_scale=gs.to(cuda_device))
+    assert_bits_equal(bits(y), oq.nvfp4_qdq(bits(x), float(gs)), "config 2 full")
+
+
+def test_ops_trace_under_torch_compile(cuda_device):
+    from vllm_qdq_plugin.qdq import mxfp4_qdq, nvfp4_qdq
+
+    def f(a, gs):
+        return mxfp4_qdq(a * 2) + nvfp4_qdq(a, global_scale=gs)
+
+    a = _random(64, 256, torch.bfloat16, seed=9, dev=cuda_device)
+    gs = torch.tensor([1.5], device=cuda_device)
+    eager = f(a, gs)
+    compiled = torch.compile(f, fullgraph=True)(a, gs)
+    assert torch.equal(eager.view(torch.int16), compiled.view(torch.int16))

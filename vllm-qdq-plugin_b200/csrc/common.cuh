@@ -1,0 +1,116 @@
+// Shared helpers for the sm_100a kernels behind include/qdq_b200.h.
+//
+// Everything here is device-side bit manipulation or thin inline-PTX wrappers
+// around conversion instructions that exist on sm_100a:
+//   cvt.rn.satfinite.e2m1x2.f32   (two fp32 -> packed E2M1 pair, RNE, saturate at 6)
+//   cvt.rn.f16x2.e2m1x2           (packed E2M1 pair -> two exact fp16)
+//   cvt.rn.satfinite.e4m3x2.f32   (two fp32 -> packed E4M3 pair, RNE)
+//   cvt.rn.f16x2.e4m3x2           (packed E4M3 pair -> two exact fp16)
+// No math-library routine is re-implemented here.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "qdq_b200.h"
+
+namespace qdqb200 {
+
+// ---------------------------------------------------------------------------
+// host-side error plumbing (one message per calling thread)
+// ---------------------------------------------------------------------------
+void set_error(const char* fmt, ...);
+int fail(int status, const char* fmt, ...);
+int check_launch(const char* what);
+int device_sm_count();  // SM count of the current device (cached)
+
+// ---------------------------------------------------------------------------
+// device-side conversion helpers
+// ---------------------------------------------------------------------------
+
+// Packs RNE-to-E2M1 codes of (lo, hi) into one byte: lo -> bits 0..3, hi -> bits 4..7.
+__device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .b8 t;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\t"
+      "cvt.u32.u8 %0, t;\n\t}"
+      : "=r"(out)
+      : "f"(hi), "f"(lo));
+  return out;
+}
+
+// Expands one packed E2M1 byte into an fp16x2 word (bits 0..3 -> low half).
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .b8 t;\n\t"
+      "cvt.u8.u32 t, %1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+      : "=r"(out)
+      : "r"(byte));
+  return out;
+}
+
+// RNE fp32 -> E4M3 (saturating) -> back to fp32, exactly.
+__device__ __forceinline__ float round_e4m3(float v) {
+  uint32_t h2;
+  asm volatile(
+      "{\n\t.reg .b16 t;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 t, %1, %1;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, t;\n\t}"
+      : "=r"(h2)
+      : "f"(v));
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
+}
+
+// RNE fp32 -> E4M3 byte (saturating).
+__device__ __forceinline__ uint32_t e4m3_byte(float v) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .b16 t;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 t, %1, %1;\n\t"
+      "cvt.u32.u16 %0, t;\n\t}"
+      : "=r"(out)
+      : "f"(v));
+  return out & 0xFFu;
+}
+
+__device__ __forceinline__ float f16lo(uint32_t w) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xFFFFu)));
+}
+__device__ __forceinline__ float f16hi(uint32_t w) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16)));
+}
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// Two fp32 -> packed bf16x2 / f16x2 with round-to-nearest-even (subnormals kept).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t out;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(out) : "f"(hi), "f"(lo));
+  return out;
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t out;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(out) : "f"(hi), "f"(lo));
+  return out;
+}
+
+// Streaming 16-byte global load / store (data is touched exactly once).
+__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void st_stream(uint4* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+}  // namespace qdqb200

@@ -1,0 +1,567 @@
+// MXFP4 / NVFP4 activation quant-dequant for sm_100a.
+//
+// Both are single-pass HBM-bound kernels: every element is read once (2 B) and
+// written once (2 B).  A lane owns one 16-byte chunk (8 bf16/fp16); the lanes
+// of one scale group (4 for MXFP4's 32, 2 for NVFP4's 16) exchange their
+// partial |x| maxima with warp shuffles, so no shared memory or second pass is
+// needed.  E2M1 encoding uses the sm_100a `cvt.rn.satfinite.e2m1x2.f32`
+// instruction (round-to-nearest-even, saturating at 6), decoding uses
+// `cvt.rn.f16x2.e2m1x2` (exact).
+//
+// Semantics follow
+//   - MXFP4: vllm_qdq_plugin/qdq/mxfp4.py:98-156 (reference plugin), bit-exact;
+//   - NVFP4: vLLM 0.22 nvfp4_emulation_utils.py:439-478 (CPU branch), bit-exact.
+// All float arithmetic that the references round step by step is written with
+// __fmul_rn/__fadd_rn/__fdiv_rn so that no FMA contraction changes a rounding.
+#include "common.cuh"
+
+namespace qdqb200 {
+namespace {
+
+constexpr uint32_t kFull = 0xFFFFFFFFu;
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;           // 16-byte chunks in flight per lane
+constexpr float kRecip6 = 1.0f / 6.0f;  // fp32 value of vLLM's FLOAT4_E2M1_MAX_RECIPROCAL
+
+// ---------------------------------------------------------------------------
+// per-dtype pieces
+// ---------------------------------------------------------------------------
+template <int kDtype>
+struct Fmt;
+
+template <>
+struct Fmt<QDQ_DTYPE_BF16> {
+  __device__ static float lo(uint32_t w) { return bf16lo(w); }
+  __device__ static float hi(uint32_t w) { return bf16hi(w); }
+  __device__ static float one(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
+  __device__ static uint32_t pack(float a, float b) { return pack_bf16x2(a, b); }
+  __device__ static uint16_t pack1(float a) { return static_cast<uint16_t>(pack_bf16x2(a, 0.f) & 0xFFFFu); }
+  __device__ static float amax_value(uint32_t bits) { return __uint_as_float(bits << 16); }
+  // E8M0 exponent of the group scale from the group's max |x| bit pattern:
+  // round the mantissa up at 0.75 (`+0x20 & 0xFF80`, mxfp4.py:138-140), then
+  // clamp(floor(log2) + 127 - 2, 0, 254) (mxfp4.py:142-145).  A rounded max of
+  // zero, inf or NaN makes the reference's float->int32 cast of +-inf land on
+  // the lower clamp, i.e. exponent 0.
+  __device__ static int mx_exp(uint32_t amax_bits) {
+    const uint32_t r = (amax_bits + 0x20u) & 0xFF80u;
+    const int ef = static_cast<int>((r >> 7) & 0xFFu);
+    return (ef == 0 || ef == 255) ? 0 : max(ef - 2, 0);
+  }
+  // 2^(e-127) as the reference holds it in bf16 (mxfp4.py:146): always exact.
+  __device__ static float mx_scale(int e) {
+    return e ? __uint_as_float(static_cast<uint32_t>(e) << 23) : __uint_as_float(0x00400000u);
+  }
+  static constexpr bool kScaleCanBeZero = false;
+};
+
+template <>
+struct Fmt<QDQ_DTYPE_FP16> {
+  __device__ static float lo(uint32_t w) { return f16lo(w); }
+  __device__ static float hi(uint32_t w) { return f16hi(w); }
+  __device__ static float one(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+  __device__ static uint32_t pack(float a, float b) { return pack_f16x2(a, b); }
+  __device__ static uint16_t pack1(float a) { return static_cast<uint16_t>(pack_f16x2(a, 0.f) & 0xFFFFu); }
+  __device__ static float amax_value(uint32_t bits) { return __half2float(__ushort_as_half(static_cast<unsigned short>(bits))); }
+  // fp16 variant of the same rule (`+0x100 & 0xFC00`, exponent bias 15).
+  __device__ static int mx_exp(uint32_t amax_bits) {
+    const uint32_t r = (amax_bits + 0x100u) & 0xFC00u;
+    const int ef = static_cast<int>((r >> 10) & 0x1Fu);
+    return (ef == 0 || ef == 31) ? 0 : ef + 110;
+  }
+  // In fp16, 2^(e-127) underflows to 0 for e == 0 and is exact otherwise
+  // (e >= 111 for every finite non-tiny group).
+  __device__ static float mx_scale(int e) {
+    return e ? __uint_as_float(static_cast<uint32_t>(e) << 23) : 0.0f;
+  }
+  static constexpr bool kScaleCanBeZero = true;
+};
+
+// fp16 groups whose scale is 0: the reference divides by zero, turning x != 0
+// into +-inf and +-0 into a NaN whose sign on x86 is negative; the E2M1
+// simulation maps both to +-6 and the final multiply by the zero scale leaves
+// a signed zero.  Result: copysign(0, x) for x != 0, -0 for x == +-0.
+__device__ __forceinline__ uint16_t fp16_zero_scale_result(uint16_t xb) {
+  return ((xb & 0x7FFFu) == 0) ? static_cast<uint16_t>(0x8000u) : static_cast<uint16_t>(xb & 0x8000u);
+}
+__device__ __forceinline__ uint32_t fp16_zero_scale_word(uint32_t w) {
+  return static_cast<uint32_t>(fp16_zero_scale_result(static_cast<uint16_t>(w & 0xFFFFu))) |
+         (static_cast<uint32_t>(fp16_zero_scale_result(static_cast<uint16_t>(w >> 16))) << 16);
+}
+
+// E2M1 byte holding two signed zeros with the signs of an fp16x2 word.
+__device__ __forceinline__ uint32_t zero_codes_of(uint32_t w) {
+  return ((w >> 12) & 0x8u) | ((w >> 24) & 0x80u);
+}
+
+__device__ __forceinline__ uint32_t absmax8(const uint4& v) {
+  const uint32_t m = __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu),
+                              __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu));
+  return max(m & 0xFFFFu, m >> 16);
+}
+
+// ---------------------------------------------------------------------------
+// MXFP4: vectorised kernel (K % 32 == 0, 16-byte aligned rows)
+// ---------------------------------------------------------------------------
+template <int kDtype, bool kContig, bool kY, bool kCodes, bool kScales>
+__global__ void __launch_bounds__(kThreads)
+mxfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
+                 uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
+                 uint32_t cpr, uint64_t total, int64_t ldx, int64_t ldy, int64_t ldc,
+                 int64_t lds) {
+  using F = Fmt<kDtype>;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x * kUnroll;
+  for (uint64_t base = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31u)) * kUnroll;
+       base < total; base += stride) {
+    uint4 v[kUnroll];
+    uint64_t xo[kUnroll], yo[kUnroll], co[kUnroll], so[kUnroll];
+    bool ok[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const uint64_t c = base + static_cast<uint64_t>(u) * 32u + lane;
+      ok[u] = c < total;
+      if (kContig) {
+        xo[u] = c * 8u;
+        yo[u] = c * 8u;
+        co[u] = c * 4u;
+        so[u] = c >> 2;
+      } else {
+        const uint32_t row = static_cast<uint32_t>(c) / cpr;
+        const uint32_t col = static_cast<uint32_t>(c) - row * cpr;
+        xo[u] = row * static_cast<uint64_t>(ldx) + col * 8u;
+        yo[u] = row * static_cast<uint64_t>(ldy) + col * 8u;
+        co[u] = row * static_cast<uint64_t>(ldc) + col * 4u;
+        so[u] = row * static_cast<uint64_t>(lds) + (col >> 2);
+      }
+      v[u] = ok[u] ? ld_stream(reinterpret_cast<const uint4*>(x + xo[u])) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      uint32_t amax = absmax8(v[u]);
+      amax = max(amax, __shfl_xor_sync(kFull, amax, 1));
+      amax = max(amax, __shfl_xor_sync(kFull, amax, 2));
+      const int e = F::mx_exp(amax);
+      const float inv = __uint_as_float(static_cast<uint32_t>(254 - e) << 23);  // 1/scale, exact
+      const float sc = F::mx_scale(e);
+      const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      uint32_t o[4];
+      uint32_t code_word = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t byte = cvt_e2m1x2(__fmul_rn(F::lo(w[j]), inv), __fmul_rn(F::hi(w[j]), inv));
+        const uint32_t h = e2m1x2_to_f16x2(byte);
+        o[j] = F::pack(__fmul_rn(f16lo(h), sc), __fmul_rn(f16hi(h), sc));
+        if (F::kScaleCanBeZero && e == 0) {
+          o[j] = fp16_zero_scale_word(w[j]);
+          byte = zero_codes_of(o[j]);
+        }
+        code_word |= byte << (8 * j);
+      }
+      if (ok[u]) {
+        if (kY) st_stream(reinterpret_cast<uint4*>(y + yo[u]), make_uint4(o[0], o[1], o[2], o[3]));
+        if (kCodes) *reinterpret_cast<uint32_t*>(codes + co[u]) = code_word;
+        if (kScales && (lane & 3u) == 0) scales[so[u]] = static_cast<uint8_t>(e);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// MXFP4: generic kernel (any K, any alignment); one thread per 32-group.
+// A partial last group behaves as if zero-padded (mxfp4.py:117-120).
+// ---------------------------------------------------------------------------
+template <int kDtype>
+__global__ void __launch_bounds__(kThreads)
+mxfp4_generic_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
+                     uint8_t* __restrict__ codes, uint8_t* __restrict__ scales, int64_t M,
+                     int64_t K, int64_t ldx, int64_t ldy, int64_t ldc, int64_t lds) {
+  using F = Fmt<kDtype>;
+  const int64_t gpr = (K + 31) / 32;
+  const int64_t ngroups = M * gpr;
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < ngroups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = g / gpr;
+    const int64_t gi = g - r * gpr;
+    const int64_t k0 = gi * 32;
+    const int n = static_cast<int>((K - k0) < 32 ? (K - k0) : 32);
+    const uint16_t* xr = x + r * ldx + k0;
+    uint16_t* yr = y ? y + r * ldy + k0 : nullptr;
+    uint32_t amax = 0;
+    for (int i = 0; i < n; ++i) amax = max(amax, static_cast<uint32_t>(xr[i] & 0x7FFFu));
+    const int e = F::mx_exp(amax);
+    const float inv = __uint_as_float(static_cast<uint32_t>(254 - e) << 23);
+    const float sc = F::mx_scale(e);
+    for (int i = 0; i < 32; i += 2) {
+      uint32_t byte = 0;
+      if (i < n) {
+        const uint16_t x0 = xr[i];
+        const bool has1 = (i + 1) < n;
+        const uint16_t x1 = has1 ? xr[i + 1] : static_cast<uint16_t>(0);
+        byte = cvt_e2m1x2(__fmul_rn(F::one(x0), inv), __fmul_rn(F::one(x1), inv));
+        if (!has1) byte &= 0x0Fu;
+        const uint32_t h = e2m1x2_to_f16x2(byte);
+        uint16_t y0 = F::pack1(__fmul_rn(f16lo(h), sc));
+        uint16_t y1 = F::pack1(__fmul_rn(f16hi(h), sc));
+        if (F::kScaleCanBeZero && e == 0) {
+          y0 = fp16_zero_scale_result(x0);
+          y1 = fp16_zero_scale_result(x1);
+          byte = zero_codes_of(static_cast<uint32_t>(y0) | (static_cast<uint32_t>(y1) << 16));
+          if (!has1) byte &= 0x0Fu;
+        }
+        if (y) {
+          yr[i] = y0;
+          if (has1) yr[i + 1] = y1;
+        }
+      }
+      if (codes) codes[r * ldc + gi * 16 + i / 2] = static_cast<uint8_t>(byte);
+    }
+    if (scales) scales[r * lds + gi] = static_cast<uint8_t>(e);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// NVFP4 group math (nvfp4_emulation_utils.py:439-452 and :474-476)
+// ---------------------------------------------------------------------------
+struct NvGroup {
+  float out_scale;  // 1 / (scale * (1/gs))  with vLLM's zero-safe reciprocal
+  float deq;        // scale / gs
+  uint32_t sbyte;   // E4M3 byte of the block scale
+};
+
+__device__ __forceinline__ float zero_safe_recip(float t) {
+  // get_reciprocal(t) = 1 / (t + (t == 0) * 1e8)   (nvfp4_emulation_utils.py:415-418)
+  return __fdiv_rn(1.0f, __fadd_rn(t, t == 0.0f ? 1e8f : 0.0f));
+}
+
+__device__ __forceinline__ NvGroup nv_group(float vec_max, float gs, float rgs) {
+  float s = __fmul_rn(gs, __fmul_rn(vec_max, kRecip6));
+  s = fminf(fmaxf(s, -448.0f), 448.0f);
+  NvGroup g;
+  g.sbyte = e4m3_byte(s);
+  s = round_e4m3(s);
+  g.out_scale = zero_safe_recip(__fmul_rn(s, rgs));
+  g.deq = __fdiv_rn(s, gs);
+  return g;
+}
+
+// Codes of two scaled elements; cast_to_fp4 takes torch.sign(), which is +0
+// for -0, so an exactly-zero input loses its sign (nvfp4_emulation_utils.py:425-436).
+__device__ __forceinline__ uint32_t nv_codes(float a, float b) {
+  a = fminf(fmaxf(a, -6.0f), 6.0f);
+  b = fminf(fmaxf(b, -6.0f), 6.0f);
+  uint32_t byte = cvt_e2m1x2(a, b);
+  if (a == 0.0f) byte &= 0xF7u;
+  if (b == 0.0f) byte &= 0x7Fu;
+  return byte;
+}
+
+template <int kDtype, bool kContig, bool kY, bool kCodes, bool kScales>
+__global__ void __launch_bounds__(kThreads)
+nvfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
+                 uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
+                 const float* __restrict__ gsp, uint32_t cpr, uint64_t total, int64_t ldx,
+                 int64_t ldy, int64_t ldc, int64_t lds) {
+  using F = Fmt<kDtype>;
+  const float gs = __ldg(gsp);
+  const float rgs = zero_safe_recip(gs);
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x * kUnroll;
+  for (uint64_t base = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31u)) * kUnroll;
+       base < total; base += stride) {
+    uint4 v[kUnroll];
+    uint64_t xo[kUnroll], yo[kUnroll], co[kUnroll], so[kUnroll];
+    bool ok[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const uint64_t c = base + static_cast<uint64_t>(u) * 32u + lane;
+      ok[u] = c < total;
+      if (kContig) {
+        xo[u] = c * 8u;
+        yo[u] = c * 8u;
+        co[u] = c * 4u;
+        so[u] = c >> 1;
+      } else {
+        const uint32_t row = static_cast<uint32_t>(c) / cpr;
+        const uint32_t col = static_cast<uint32_t>(c) - row * cpr;
+        xo[u] = row * static_cast<uint64_t>(ldx) + col * 8u;
+        yo[u] = row * static_cast<uint64_t>(ldy) + col * 8u;
+        co[u] = row * static_cast<uint64_t>(ldc) + col * 4u;
+        so[u] = row * static_cast<uint64_t>(lds) + (col >> 1);
+      }
+      v[u] = ok[u] ? ld_stream(reinterpret_cast<const uint4*>(x + xo[u])) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      uint32_t amax = absmax8(v[u]);
+      amax = max(amax, __shfl_xor_sync(kFull, amax, 1));
+      const NvGroup g = nv_group(F::amax_value(amax), gs, rgs);
+      const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      uint32_t o[4];
+      uint32_t code_word = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t byte =
+            nv_codes(__fmul_rn(F::lo(w[j]), g.out_scale), __fmul_rn(F::hi(w[j]), g.out_scale));
+        code_word |= byte << (8 * j);
+        const uint32_t h = e2m1x2_to_f16x2(byte);
+        o[j] = F::pack(__fmul_rn(f16lo(h), g.deq), __fmul_rn(f16hi(h), g.deq));
+      }
+      if (ok[u]) {
+        if (kY) st_stream(reinterpret_cast<uint4*>(y + yo[u]), make_uint4(o[0], o[1], o[2], o[3]));
+        if (kCodes) *reinterpret_cast<uint32_t*>(codes + co[u]) = code_word;
+        if (kScales && (lane & 1u) == 0) scales[so[u]] = static_cast<uint8_t>(g.sbyte);
+      }
+    }
+  }
+}
+
+// NVFP4 generic kernel: one thread per 16-group (K % 16 == 0, any alignment).
+template <int kDtype>
+__global__ void __launch_bounds__(kThreads)
+nvfp4_generic_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
+                     uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
+                     const float* __restrict__ gsp, int64_t M, int64_t K, int64_t ldx,
+                     int64_t ldy, int64_t ldc, int64_t lds) {
+  using F = Fmt<kDtype>;
+  const float gs = __ldg(gsp);
+  const float rgs = zero_safe_recip(gs);
+  const int64_t gpr = K / 16;
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < M * gpr;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = g / gpr;
+    const int64_t gi = g - r * gpr;
+    const uint16_t* xr = x + r * ldx + gi * 16;
+    uint16_t* yr = y ? y + r * ldy + gi * 16 : nullptr;
+    uint32_t amax = 0;
+    for (int i = 0; i < 16; ++i) amax = max(amax, static_cast<uint32_t>(xr[i] & 0x7FFFu));
+    const NvGroup ng = nv_group(F::amax_value(amax), gs, rgs);
+    for (int i = 0; i < 16; i += 2) {
+      const uint32_t byte = nv_codes(__fmul_rn(F::one(xr[i]), ng.out_scale),
+                                     __fmul_rn(F::one(xr[i + 1]), ng.out_scale));
+      const uint32_t h = e2m1x2_to_f16x2(byte);
+      if (yr) {
+        yr[i] = F::pack1(__fmul_rn(f16lo(h), ng.deq));
+        yr[i + 1] = F::pack1(__fmul_rn(f16hi(h), ng.deq));
+      }
+      if (codes) codes[r * ldc + gi * 8 + i / 2] = static_cast<uint8_t>(byte);
+    }
+    if (scales) scales[r * lds + gi] = static_cast<uint8_t>(ng.sbyte);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// global amax -> gs = 2688 / amax   (one pass; last block finalises)
+// ws[0] = running max of |x| bit patterns, ws[1] = finished-block ticket.
+// ---------------------------------------------------------------------------
+template <int kDtype, bool kVec>
+__global__ void __launch_bounds__(kThreads)
+amax_gs_kernel(const uint16_t* __restrict__ x, int64_t M, int64_t K, int64_t ldx,
+               uint32_t* __restrict__ ws, float* __restrict__ gs_out) {
+  using F = Fmt<kDtype>;
+  uint32_t m = 0;
+  if (kVec) {
+    const uint32_t cpr = static_cast<uint32_t>(K / 8);
+    const uint64_t total = static_cast<uint64_t>(M) * cpr;
+    for (uint64_t c = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < total;
+         c += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+      const uint64_t row = c / cpr;
+      const uint64_t col = c - row * cpr;
+      m = max(m, absmax8(ld_stream(reinterpret_cast<const uint4*>(x + row * ldx + col * 8))));
+    }
+  } else {
+    const int64_t total = M * K;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      const int64_t row = i / K;
+      m = max(m, static_cast<uint32_t>(x[row * ldx + (i - row * K)] & 0x7FFFu));
+    }
+  }
+  m = __reduce_max_sync(kFull, m);
+  __shared__ uint32_t warp_max[kThreads / 32];
+  __shared__ bool last;
+  if ((threadIdx.x & 31u) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    uint32_t b = threadIdx.x < (kThreads / 32) ? warp_max[threadIdx.x] : 0u;
+    b = __reduce_max_sync(kFull, b);
+    if (threadIdx.x == 0) {
+      atomicMax(&ws[0], b);
+      __threadfence();
+      last = atomicAdd(&ws[1], 1u) == gridDim.x - 1;
+    }
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t bits = atomicOr(&ws[0], 0u);
+    *gs_out = __fdiv_rn(2688.0f, F::amax_value(bits));
+    ws[0] = 0;
+    ws[1] = 0;
+  }
+}
+
+int grid_for(uint64_t work_items, int per_block) {
+  const uint64_t need = (work_items + per_block - 1) / per_block;
+  const uint64_t cap = static_cast<uint64_t>(device_sm_count()) * 8u;
+  return static_cast<int>(need < 1 ? 1 : (need < cap ? need : cap));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+
+// Output sets the vectorised kernels are instantiated for; any other mix of
+// (y, codes, scales) goes through the generic kernel.
+enum OutSet { kOutY = 0, kOutAll = 1, kOutCodes = 2, kOutOther = 3 };
+
+OutSet out_set(const void* y, const void* codes, const void* scales) {
+  if (y && !codes && !scales) return kOutY;
+  if (y && codes && scales) return kOutAll;
+  if (!y && codes && scales) return kOutCodes;
+  return kOutOther;
+}
+
+template <int kDtype, bool kContig, typename... Args>
+void dispatch_mx_vec(OutSet o, int grid, cudaStream_t s, Args... args) {
+  if (o == kOutY) mxfp4_vec_kernel<kDtype, kContig, true, false, false><<<grid, kThreads, 0, s>>>(args...);
+  else if (o == kOutAll) mxfp4_vec_kernel<kDtype, kContig, true, true, true><<<grid, kThreads, 0, s>>>(args...);
+  else mxfp4_vec_kernel<kDtype, kContig, false, true, true><<<grid, kThreads, 0, s>>>(args...);
+}
+
+template <int kDtype, bool kContig, typename... Args>
+void dispatch_nv_vec(OutSet o, int grid, cudaStream_t s, Args... args) {
+  if (o == kOutY) nvfp4_vec_kernel<kDtype, kContig, true, false, false><<<grid, kThreads, 0, s>>>(args...);
+  else if (o == kOutAll) nvfp4_vec_kernel<kDtype, kContig, true, true, true><<<grid, kThreads, 0, s>>>(args...);
+  else nvfp4_vec_kernel<kDtype, kContig, false, true, true><<<grid, kThreads, 0, s>>>(args...);
+}
+
+int check_common(const void* x, const void* y, const void* codes, int64_t M, int64_t K,
+                 int64_t ldx, int64_t ldy, int dtype, const char* who) {
+  if (M < 0 || K < 0) return fail(QDQ_ERR_INVALID_ARG, "%s: negative shape [%lld, %lld]", who, (long long)M, (long long)K);
+  if (dtype != QDQ_DTYPE_BF16 && dtype != QDQ_DTYPE_FP16)
+    return fail(QDQ_ERR_INVALID_ARG, "%s: dtype must be bf16 (0) or fp16 (1), got %d", who, dtype);
+  if (M == 0 || K == 0) return QDQ_OK;
+  if (x == nullptr) return fail(QDQ_ERR_INVALID_ARG, "%s: null input pointer", who);
+  if (y == nullptr && codes == nullptr) return fail(QDQ_ERR_INVALID_ARG, "%s: neither y nor codes requested", who);
+  if (ldx < K || (y != nullptr && ldy < K)) return fail(QDQ_ERR_INVALID_ARG, "%s: row stride smaller than K", who);
+  if (x == y && ldx != ldy) return fail(QDQ_ERR_INVALID_ARG, "%s: in-place call needs ldx == ldy", who);
+  return QDQ_OK;
+}
+
+}  // namespace
+}  // namespace qdqb200
+
+using namespace qdqb200;
+
+extern "C" int qdq_mxfp4(const void* x, void* y, void* codes, void* scales, int64_t M, int64_t K,
+                         int64_t ldx, int64_t ldy, int dtype, int group_size, void* stream) {
+  if (int st = check_common(x, y, codes, M, K, ldx, ldy, dtype, "qdq_mxfp4")) return st;
+  if (group_size != 32)
+    return fail(QDQ_ERR_UNSUPPORTED, "qdq_mxfp4: group_size must be 32 (got %d)", group_size);
+  if (M == 0 || K == 0) return QDQ_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t Kp = (K + 31) / 32 * 32;
+  const int64_t ldc = Kp / 2, lds = Kp / 32;
+  auto* xp = static_cast<const uint16_t*>(x);
+  auto* yp = static_cast<uint16_t*>(y);
+  auto* cp = static_cast<uint8_t*>(codes);
+  auto* sp = static_cast<uint8_t*>(scales);
+  const uint64_t cpr = static_cast<uint64_t>(K / 8);
+  const uint64_t total = static_cast<uint64_t>(M) * cpr;
+  const OutSet o = out_set(y, codes, scales);
+  if (y == nullptr) ldy = K;
+  const bool vec = (K % 32 == 0) && aligned16(x) && (y == nullptr || aligned16(y)) && (ldx % 8 == 0) &&
+                   (ldy % 8 == 0) && (codes == nullptr || aligned4(codes)) && o != kOutOther;
+  const bool contig = (ldx == K) && (ldy == K);
+  if (vec && (contig || total < (1ull << 32))) {
+    const int grid = grid_for(total, kThreads * kUnroll);
+    if (dtype == QDQ_DTYPE_BF16) {
+      if (contig) dispatch_mx_vec<QDQ_DTYPE_BF16, true>(o, grid, s, xp, yp, cp, sp, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
+      else dispatch_mx_vec<QDQ_DTYPE_BF16, false>(o, grid, s, xp, yp, cp, sp, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
+    } else {
+      if (contig) dispatch_mx_vec<QDQ_DTYPE_FP16, true>(o, grid, s, xp, yp, cp, sp, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
+      else dispatch_mx_vec<QDQ_DTYPE_FP16, false>(o, grid, s, xp, yp, cp, sp, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
+    }
+  } else {
+    const uint64_t ngroups = static_cast<uint64_t>(M) * static_cast<uint64_t>((K + 31) / 32);
+    const int grid = grid_for(ngroups, kThreads);
+    if (dtype == QDQ_DTYPE_BF16)
+      mxfp4_generic_kernel<QDQ_DTYPE_BF16><<<grid, kThreads, 0, s>>>(xp, yp, cp, sp, M, K, ldx, ldy, ldc, lds);
+    else
+      mxfp4_generic_kernel<QDQ_DTYPE_FP16><<<grid, kThreads, 0, s>>>(xp, yp, cp, sp, M, K, ldx, ldy, ldc, lds);
+  }
+  return check_launch("qdq_mxfp4");
+}
+
+extern "C" int qdq_nvfp4(const void* x, void* y, void* codes, void* scales, const float* global_scale,
+                         int64_t M, int64_t K, int64_t ldx, int64_t ldy, int dtype, void* stream) {
+  if (int st = check_common(x, y, codes, M, K, ldx, ldy, dtype, "qdq_nvfp4")) return st;
+  if (K % 16 != 0) return fail(QDQ_ERR_INVALID_ARG, "qdq_nvfp4: K=%lld is not a multiple of 16", (long long)K);
+  if (M == 0 || K == 0) return QDQ_OK;
+  if (global_scale == nullptr) return fail(QDQ_ERR_INVALID_ARG, "qdq_nvfp4: null global_scale");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t ldc = K / 2, lds = K / 16;
+  auto* xp = static_cast<const uint16_t*>(x);
+  auto* yp = static_cast<uint16_t*>(y);
+  auto* cp = static_cast<uint8_t*>(codes);
+  auto* sp = static_cast<uint8_t*>(scales);
+  const uint64_t cpr = static_cast<uint64_t>(K / 8);
+  const uint64_t total = static_cast<uint64_t>(M) * cpr;
+  const OutSet o = out_set(y, codes, scales);
+  if (y == nullptr) ldy = K;
+  const bool vec = aligned16(x) && (y == nullptr || aligned16(y)) && (ldx % 8 == 0) && (ldy % 8 == 0) &&
+                   (codes == nullptr || aligned4(codes)) && o != kOutOther;
+  const bool contig = (ldx == K) && (ldy == K);
+  if (vec && (contig || total < (1ull << 32))) {
+    const int grid = grid_for(total, kThreads * kUnroll);
+    if (dtype == QDQ_DTYPE_BF16) {
+      if (contig) dispatch_nv_vec<QDQ_DTYPE_BF16, true>(o, grid, s, xp, yp, cp, sp, global_scale, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
+      else dispatch_nv_vec<QDQ_DTYPE_BF16, false>(o, grid, s, xp, yp, cp, sp, global_scale, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
+    } else {
+      if (contig) dispatch_nv_vec<QDQ_DTYPE_FP16, true>(o, grid, s, xp, yp, cp, sp, global_scale, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
+      else dispatch_nv_vec<QDQ_DTYPE_FP16, false>(o, grid, s, xp, yp, cp, sp, global_scale, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
+    }
+  } else {
+    const uint64_t ngroups = static_cast<uint64_t>(M) * static_cast<uint64_t>(K / 16);
+    const int grid = grid_for(ngroups, kThreads);
+    if (dtype == QDQ_DTYPE_BF16)
+      nvfp4_generic_kernel<QDQ_DTYPE_BF16><<<grid, kThreads, 0, s>>>(xp, yp, cp, sp, global_scale, M, K, ldx, ldy, ldc, lds);
+    else
+      nvfp4_generic_kernel<QDQ_DTYPE_FP16><<<grid, kThreads, 0, s>>>(xp, yp, cp, sp, global_scale, M, K, ldx, ldy, ldc, lds);
+  }
+  return check_launch("qdq_nvfp4");
+}
+
+namespace qdqb200 {
+// Shared by the public entry below and by any caller that owns its scratch.
+int launch_global_scale(const void* x, float* gs_out, uint32_t* ws, int64_t M, int64_t K,
+                        int64_t ldx, int dtype, cudaStream_t s) {
+  if (cudaMemsetAsync(ws, 0, 2 * sizeof(uint32_t), s) != cudaSuccess)
+    return fail(QDQ_ERR_CUDA, "qdq_nvfp4_global_scale: clearing workspace failed: %s",
+                cudaGetErrorString(cudaGetLastError()));
+  auto* xp = static_cast<const uint16_t*>(x);
+  const bool vec = aligned16(x) && (K % 8 == 0) && (ldx % 8 == 0);
+  const uint64_t work = vec ? static_cast<uint64_t>(M) * (K / 8) : static_cast<uint64_t>(M) * K;
+  const int grid = grid_for(work, kThreads * 4);
+  if (dtype == QDQ_DTYPE_BF16) {
+    if (vec) amax_gs_kernel<QDQ_DTYPE_BF16, true><<<grid, kThreads, 0, s>>>(xp, M, K, ldx, ws, gs_out);
+    else amax_gs_kernel<QDQ_DTYPE_BF16, false><<<grid, kThreads, 0, s>>>(xp, M, K, ldx, ws, gs_out);
+  } else {
+    if (vec) amax_gs_kernel<QDQ_DTYPE_FP16, true><<<grid, kThreads, 0, s>>>(xp, M, K, ldx, ws, gs_out);
+    else amax_gs_kernel<QDQ_DTYPE_FP16, false><<<grid, kThreads, 0, s>>>(xp, M, K, ldx, ws, gs_out);
+  }
+  return check_launch("qdq_nvfp4_global_scale");
+}
+}  // namespace qdqb200
+
+extern "C" int qdq_nvfp4_global_scale(const void* x, float* global_scale_out, void* workspace,
+                                      int64_t M, int64_t K, int64_t ldx, int dtype, void* stream) {
+  if (M <= 0 || K <= 0) return fail(QDQ_ERR_INVALID_ARG, "qdq_nvfp4_global_scale: empty tensor has no amax");
+  if (dtype != QDQ_DTYPE_BF16 && dtype != QDQ_DTYPE_FP16)
+    return fail(QDQ_ERR_INVALID_ARG, "qdq_nvfp4_global_scale: bad dtype %d", dtype);
+  if (!x || !global_scale_out || !workspace)
+    return fail(QDQ_ERR_INVALID_ARG, "qdq_nvfp4_global_scale: null pointer");
+  if (ldx < K) return fail(QDQ_ERR_INVALID_ARG, "qdq_nvfp4_global_scale: ldx < K");
+  if (!aligned4(workspace)) return fail(QDQ_ERR_ALIGNMENT, "qdq_nvfp4_global_scale: workspace not 4-byte aligned");
+  return launch_global_scale(x, global_scale_out, static_cast<uint32_t*>(workspace), M, K, ldx, dtype,
+                             static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,98 @@
+# SPDX-License-Identifier: Apache-2.0
+"""ctypes binding of `libqdq_b200.so` and the torch.library ops built on it.
+
+The C ABI (include/qdq_b200.h) takes raw device pointers, element strides and
+a `cudaStream_t`; this module passes `tensor.data_ptr()` and torch's current
+stream, so the kernels are stream-ordered with the caller's other work and no
+host synchronisation happens.  There is no CPU fallback: a CPU tensor or a
+missing library raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _build
+
+_LOCK = threading.Lock()
+_LIB: ctypes.CDLL | None = None
+
+DTYPE_CODE = {torch.bfloat16: 0, torch.float16: 1}
+
+_c_void_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_f32 = ctypes.c_float
+
+# name -> argtypes (restype is always c_int status unless listed in _RESTYPES)
+_SIGNATURES: dict[str, list] = {
+    "qdq_mxfp4": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64,
+                  _int, _int, _c_void_p],
+    "qdq_nvfp4": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64,
+                  _i64, _int, _c_void_p],
+    "qdq_nvfp4_global_scale": [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _int,
+                               _c_void_p],
+    "qdq_last_error": [],
+    "qdq_abi_version": [],
+}
+_RESTYPES = {"qdq_last_error": ctypes.c_char_p}
+
+
+def lib() -> ctypes.CDLL:
+    """Load (building first if missing or stale) the sm_100a library."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is None:
+            path = _build.build_native()
+            handle = ctypes.CDLL(str(path))
+            for name, argtypes in _SIGNATURES.items():
+                fn = getattr(handle, name, None)
+                if fn is None:
+                    continue
+                fn.argtypes = argtypes
+                fn.restype = _RESTYPES.get(name, ctypes.c_int)
+            _LIB = handle
+    return _LIB
+
+
+def library_path() -> str:
+    return str(_build.LIB_PATH)
+
+
+class NativeError(RuntimeError):
+    """A C-ABI entry point returned a non-zero qdq_status_t."""
+
+    def __init__(self, fn: str, status: int, message: str):
+        super().__init__(f"{fn} failed with status {status}: {message}")
+        self.status = status
+
+
+def check(fn: str, status: int) -> None:
+    if status != 0:
+        msg = lib().qdq_last_error()
+        raise NativeError(fn, status, msg.decode() if msg else "")
+
+
+def call(fn: str, *args) -> None:
+    check(fn, getattr(lib(), fn)(*args))
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError(
+                "vllm_qdq_plugin (B200) kernels need CUDA tensors on an sm_100 GPU; "
+                f"got a tensor on {t.device} (there is no CPU fallback)")
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
