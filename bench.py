@@ -71,12 +71,27 @@ def global_scale_of(x: torch.Tensor) -> torch.Tensor:
     return (torch.tensor(2688.0, dtype=torch.float32) / amax).reshape(1)
 
 
+def c3_inputs(rows: int = 4096, n: int = 14336, k: int = 4096):
+    """Config 3: A ~ N(0,1) bf16 [M, K] (seed 2); W MXFP4 [N, K]: uniform random
+    E2M1 nibbles, E8M0 exponents uniform in [-10, -4] per 32-group (seed 3)."""
+    import numpy as np
+    g = torch.Generator().manual_seed(2)
+    a = torch.randn(rows, k, generator=g).to(torch.bfloat16)
+    rng = np.random.default_rng(3)
+    codes = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+    scales = (127 + rng.integers(-10, -3, size=(n, k // 32))).astype(np.uint8)
+    return a, torch.from_numpy(codes), torch.from_numpy(scales)
+
+
 WORKLOADS = {
     "nvfp4_qdq": dict(config="BASELINE config 2: NVFP4 QDQ bf16 [16384, 8192], group 16, "
                              "E4M3 block scales, fp32 gs = 2688/amax",
                       rows=16384, cols=8192, make=c2_input),
     "mxfp4_qdq": dict(config="BASELINE config 1: MXFP4 QDQ bf16 [8192, 4096], group 32, E8M0",
                       rows=8192, cols=4096, make=c1_input),
+    "mxfp4_linear": dict(config="BASELINE config 3: MXFP4 QDQ fused into a tcgen05 FP4 GEMM, "
+                                "A bf16 [M=4096, K=4096], W MXFP4 [N=14336, K=4096], out bf16",
+                         rows=4096, cols=4096, make=None),
 }
 
 # ---------------------------------------------------------------------------
@@ -169,29 +184,43 @@ def run_reference(args) -> None:
 
     wl = WORKLOADS[args.workload]
     x = wl["make"]()
-    xb = x.view(torch.int16).numpy().view("uint16")
     cores = os.cpu_count() or 1
-    if args.workload == "nvfp4_qdq":
-        gs = float(global_scale_of(x)[0])
-        fn = lambda: oq.nvfp4_qdq(xb, gs, nthreads=cores)  # noqa: E731
-    else:
-        fn = lambda: oq.mxfp4_qdq(xb, nthreads=cores)  # noqa: E731
+
+    def runner(rows: int):
+        xb = x[:rows].view(torch.int16).numpy().view("uint16")
+        if args.workload == "nvfp4_qdq":
+            gs = float(global_scale_of(x)[0])
+            return lambda: oq.nvfp4_qdq(xb, gs, nthreads=cores)
+        return lambda: oq.mxfp4_qdq(xb, nthreads=cores)
+
+    # Each step is a bounded sample of rows, sized so that warm-up + timed
+    # steps take about two minutes of host time in total.
+    probe_rows = min(1024, x.shape[0])
+    probe = runner(probe_rows)
+    probe()
+    t0 = time.perf_counter()
+    probe()
+    per_row = (time.perf_counter() - t0) / probe_rows
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    rows = int(max(64, min(x.shape[0], budget / max(per_row, 1e-9))))
+    fn = runner(rows)
     for _ in range(args.warmup):
         fn()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         fn()
     dt = (time.perf_counter() - t0) / args.steps
-    gbs = x.numel() * BYTES_PER_ELT / dt / 1e9
+    gbs = rows * x.shape[1] * BYTES_PER_ELT / dt / 1e9
     line = {
         "impl": "reference", "metric": "QDQ HBM GB/s", "value": round(gbs, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, BASELINE shapes)",
+        "ms_per_step": round(dt * 1e3 * x.shape[0] / rows, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, BASELINE shapes)",
         "config": {"workload": wl["config"], "rows": wl["rows"], "cols": wl["cols"]},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": f"full [{wl['rows']}, {wl['cols']}] tensor per step, "
-                                   "C restatement of the reference algorithm, OpenMP"},
+                         "sample": f"first {rows} of {wl['rows']} rows (x {wl['cols']} cols) per "
+                                   "step; C restatement of the reference algorithm, OpenMP"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -249,7 +278,9 @@ def run_ours(args) -> None:
     from vllm_qdq_plugin.qdq import mxfp4_qdq, nvfp4_qdq
 
     wl = WORKLOADS[args.workload]
-    x_cpu = wl["make"]()
+    if args.workload == "mxfp4_linear":
+        return run_gemm(args, wl, world, rank, dev, dist)
+    x_cpu = wl["make"](rows=args.rows) if args.rows else wl["make"]()
     M, K = x_cpu.shape
     x = x_cpu.to(dev)
     y = torch.empty_like(x)
@@ -368,6 +399,119 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def measured_peak_fp4() -> tuple[float, str]:
+    """Dense FP4 tensor peak: MEASURED_PEAKS.json has the cuBLAS bf16 figure; the
+    sm_100 dense FP4 rate is 4x the bf16 rate (9 vs 2.25 PFLOP/s nominal)."""
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        return 4.0 * float(json.loads(p.read_text())["bf16_tflops"]), \
+            "measured bf16 x 4 (MEASURED_PEAKS.json bf16_tflops, nominal fp4:bf16 = 4)"
+    except Exception:
+        return 4.0 * 1590.0, "fallback bf16 1.59 PF x 4"
+
+
+def run_gemm(args, wl, world, rank, dev, dist) -> None:
+    from vllm_qdq_plugin import _native
+    from vllm_qdq_plugin.gemm import mxfp4_linear, prepare_mxfp4_weight
+
+    m = args.rows or wl["rows"]
+    a_cpu, codes, scales = c3_inputs(rows=m)
+    n, k = codes.shape[0], codes.shape[1] * 2
+    a = a_cpu.to(dev)
+    w = prepare_mxfp4_weight(codes.to(dev), scales.to(dev))
+    lib = _native.lib()
+    ws = torch.empty((lib.fp4_linear_workspace_bytes(m, k),), dtype=torch.uint8, device=dev)
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    # an L2 flush buffer (> 126 MB L2) written between timed steps
+    flush = torch.empty((256 << 20,), dtype=torch.uint8, device=dev)
+    launches = [0]
+
+    def step():
+        _native.check("fp4_linear_mxf4", lib.fp4_linear_mxf4(
+            a.data_ptr(), k, 0, w.codes.data_ptr(), w.sf_tiled.data_ptr(), None, out.data_ptr(),
+            m, n, k, k // 2, n, ws.data_ptr(), ws.numel(), sp))
+        launches[0] += 3  # quantise, scale tiling, GEMM
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))).start() if rank == 0 else None
+    time.sleep(0.3 if sampler else 0)
+    barrier()
+    launches[0] = 0
+    steps = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    t_wall0 = time.time()
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    barrier()
+    t_wall1 = time.time()
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in ev)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if sampler:
+        sampler.stop()
+    ms_step = ms / steps
+    flop = 2.0 * m * n * k
+    value = world * flop / (ms_step * 1e-3) / 1e12
+
+    # end to end through the public API with pinned host buffers
+    a_host = a_cpu.pin_memory()
+    out_host = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        out_host.copy_(mxfp4_linear(a_host.to(dev, non_blocking=True), w), non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = max(1, min(steps, 20))
+    e0.record(stream)
+    for _ in range(n_e2e):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e = world * flop / (e0.elapsed_time(e1) / n_e2e * 1e-3) / 1e12
+    if rank == 0:
+        peak, src = measured_peak_fp4()
+        line = {
+            "metric": "FP4 GEMM TFLOPS", "value": round(value, 1), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "e2m1 x e2m1 (E8M0 scales), fp32 accumulate, bf16 out",
+            "data": "synthetic (seeded, BASELINE config-3 distributions)",
+            "config": {"workload": wl["config"], "M": m, "N": n, "K": k,
+                       "l2": "256 MB buffer written between timed steps (L2 flush)"},
+            "e2e": {"value": round(e2e, 1), "unit": "TFLOP/s", "h2d_bytes_per_step": m * k * 2,
+                    "d2h_bytes_per_step": m * n * 2,
+                    "path": "vllm_qdq_plugin.gemm.mxfp4_linear on pinned host buffers"},
+            "gpu_launches": launches[0],
+            "roofline": {"bound": "tensor", "achieved": round(flop / (ms_step * 1e-3) / 1e12, 1),
+                         "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(flop / (ms_step * 1e-3) / 1e12 / peak, 4),
+                         "peak_source": src, "traffic": ncu_traffic("mxfp4_linear")},
+            "clocks": sampler.summary(t_wall0, t_wall1) if sampler else None,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -376,6 +520,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="nvfp4_qdq")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="override the row count (small cases for profiling only)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

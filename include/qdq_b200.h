@@ -86,6 +86,73 @@ int qdq_nvfp4_global_scale(const void* x, float* global_scale_out,
                            void* workspace, int64_t M, int64_t K, int64_t ldx,
                            int dtype, void* stream);
 
+/*
+ * Device status word of the library on the current device: 0, or the first
+ * failure a kernel recorded, as (qdq_status_t << 16) | site.  Kernels record
+ * QDQ_ERR_TIMEOUT there when a bounded wait gives up (they then release their
+ * tensor memory and exit instead of hanging).  Synchronises the device.
+ * clear != 0 resets the word to 0.
+ */
+int qdq_device_status(int* out, int clear);
+
+/*
+ * Failure-path self-test (no counterpart in the reference): launches one CTA
+ * that waits on an mbarrier nothing arrives at.  The bounded wait gives up
+ * after timeout_ns (<= 1e10) and records (QDQ_ERR_TIMEOUT << 16) | 0x7E57 in
+ * the status word read by qdq_device_status(); the context stays usable.
+ */
+int qdq_selftest_bounded_wait(int64_t timeout_ns, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Block-scaled FP4 GEMM (tcgen05 kind::mxf4) — replaces "MXFP4 QDQ of the
+ * activation + Marlin bf16 x dequantised-FP4 GEMM" for MXFP4 Marlin layers:
+ *   reference  vllm_qdq_plugin/patch.py:29-92 (_patch_marlin_gemm._patched)
+ *              -> vllm/_custom_ops.py:1277 marlin_gemm
+ *              (caller vllm/.../marlin_utils_fp4.py:149-202 apply_fp4_marlin_linear)
+ * ------------------------------------------------------------------------- */
+
+/*
+ * Bytes of a scale-factor matrix in the tcgen05 tiled layout for `rows` rows
+ * and K elements per row (E8M0, one scale per 32): rows padded to 128 and
+ * scales per row padded to a multiple of 8, grouped into 512-byte chunks
+ * (128 rows x 4 scales); chunk (rb, kc) starts at (rb * kchunks + kc) * 512
+ * and holds the scale of (row r, scale k) at (r%32)*16 + ((r/32)%4)*4 + k%4.
+ */
+int64_t qdq_sf_tiled_bytes(int64_t rows, int64_t k);
+
+/* Row-major scales [rows, ceil(k/block)] (row stride ld bytes) -> tiled
+ * layout above; padding bytes are written as 0.  block must be 32. */
+int qdq_sf_tile(const void* sf, void* sf_tiled, int64_t rows, int64_t k, int64_t ld, int block,
+                void* stream);
+
+/*
+ * C[M, N] (out_dtype bf16/fp16, row stride ldc elements) = A . W^T (+ bias[N], out_dtype),
+ * fp32 accumulation.  A: E2M1 codes [M, K/2] (row stride lda_bytes), W: E2M1
+ * codes [N, K/2] (row stride ldw_bytes), packed two per byte with element 2j
+ * in the low nibble (the layout qdq_mxfp4 emits); a_sf_tiled / w_sf_tiled:
+ * E8M0 scales in the tiled layout, 16-byte aligned.  K % 32 == 0; code
+ * buffers and row strides 16-byte aligned (TMA).  bias may be NULL.
+ */
+int fp4_gemm_mxf4(const void* a_codes, const void* a_sf_tiled, const void* w_codes,
+                  const void* w_sf_tiled, const void* bias, void* c, int64_t M, int64_t N,
+                  int64_t K, int64_t lda_bytes, int64_t ldw_bytes, int64_t ldc, int out_dtype,
+                  void* stream);
+
+/* Workspace bytes fp4_linear_mxf4 needs for an [M, K] activation. */
+int64_t fp4_linear_workspace_bytes(int64_t M, int64_t K);
+
+/*
+ * Fused linear for MXFP4 layers: a [M, K] bf16/fp16 activation (row stride
+ * lda elements) is quantised exactly as mxfp4_qdq does (qdq_mxfp4 codes +
+ * scales, into `workspace`), then multiplied with the MXFP4 weight as in
+ * fp4_gemm_mxf4; c and bias have the activation's dtype.  Output equals marlin_gemm(mxfp4_qdq(a), W) up to fp32
+ * summation order.
+ */
+int fp4_linear_mxf4(const void* a, int64_t lda, int dtype, const void* w_codes,
+                    const void* w_sf_tiled, const void* bias, void* c, int64_t M, int64_t N,
+                    int64_t K, int64_t ldw_bytes, int64_t ldc, void* workspace,
+                    int64_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -1,0 +1,60 @@
+"""CPU oracle of "MXFP4 QDQ + Marlin GEMM" (the reference's dense FP4 linear).
+
+TEST INFRASTRUCTURE ONLY (tests/, smoke(), bench.py baselines).
+
+The reference path is `mxfp4_qdq(a)` (src/vllm_qdq_plugin/patch.py:57) followed
+by vLLM's `marlin_gemm` (vllm/_custom_ops.py:1277), which multiplies the bf16
+activation by the dequantised MXFP4 weight (E2M1 value x 2^(e8m0-127)) with
+fp32 accumulation and rounds to the activation dtype.  Marlin itself is a
+compiled kernel that is not restated here; its products are exact, so the
+oracle forms them exactly (float64) and the tests allow bf16 output rounding
+plus an fp32-accumulation bound.  The E2M1 table and E8M0 power-of-two scale
+follow the reference's own dequantiser
+(src/vllm_qdq_plugin/sage3_attn/sage3/mxfp4_hw_kernel.py:31-35, :64-70, :119-139).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import qdq as oq
+
+E2M1 = np.array([0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6], np.float64)
+
+
+def dequant_mxfp4(codes: np.ndarray, scales: np.ndarray, block: int = 32) -> np.ndarray:
+    """codes uint8 [R, K/2] (element 2j in the low nibble), scales uint8 E8M0 [R, K/block]."""
+    lo = E2M1[codes & 0xF]
+    hi = E2M1[codes >> 4]
+    vals = np.stack([lo, hi], axis=-1).reshape(codes.shape[0], -1)
+    sc = np.exp2(scales.astype(np.float64) - 127.0)
+    return vals * np.repeat(sc, block, axis=1)[:, : vals.shape[1]]
+
+
+def bf16_bits_to_f64(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+
+
+def qdq_linear_exact(a_bits: np.ndarray, w_codes: np.ndarray, w_scales: np.ndarray,
+                     bias: np.ndarray | None = None, fp16: bool = False):
+    """Exact (float64) mxfp4_qdq(a) @ dequant(W)^T (+ bias) and the per-output sum
+    of |products| (bound for fp32-accumulation error)."""
+    aq = oq.mxfp4_qdq(a_bits, fp16=fp16)
+    if fp16:
+        a = aq.view(np.float16).astype(np.float64)
+    else:
+        a = bf16_bits_to_f64(aq)
+    w = dequant_mxfp4(w_codes, w_scales)
+    out = a @ w.T
+    absum = np.abs(a) @ np.abs(w).T
+    if bias is not None:
+        out = out + bias.astype(np.float64)[None, :]
+    return out, absum
+
+
+def random_mxfp4_weight(n: int, k: int, seed: int, exp_lo: int = -10, exp_hi: int = -4):
+    """Config-3 weights: uniform random E2M1 nibbles, E8M0 exponents in [exp_lo, exp_hi]."""
+    rng = np.random.default_rng(seed)
+    codes = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+    scales = (127 + rng.integers(exp_lo, exp_hi + 1, size=(n, k // 32))).astype(np.uint8)
+    return codes, scales

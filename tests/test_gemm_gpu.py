@@ -1,0 +1,126 @@
+"""GPU parity of the tcgen05 block-scaled MXFP4 GEMM (through the C ABI).
+
+Reference semantics: mxfp4_qdq(a) then Marlin's bf16 x dequantised-MXFP4 GEMM
+with fp32 accumulation (src/vllm_qdq_plugin/patch.py:57 + vllm/_custom_ops.py:1277).
+Every product is exact in both, so the tolerance is the output rounding
+(2^-8 relative, bf16) plus an fp32-accumulation bound of 2^-16 x sum|a_k w_k|.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import gemm as og
+from oracle import qdq as oq
+
+pytestmark = pytest.mark.gpu
+
+REL = 2.0 ** -8
+ACC = 2.0 ** -16
+
+
+def _check(out: torch.Tensor, exact: np.ndarray, absum: np.ndarray, what: str):
+    got = out.float().cpu().numpy().astype(np.float64)
+    err = np.abs(got - exact)
+    bound = REL * np.abs(exact) + ACC * absum + 1e-30
+    bad = err > bound
+    if bad.any():
+        i = np.argwhere(bad)[0]
+        raise AssertionError(f"{what}: {bad.sum()} of {bad.size} outside tolerance; first {tuple(i)} "
+                             f"got {got[tuple(i)]} want {exact[tuple(i)]} bound {bound[tuple(i)]}")
+
+
+def _inputs(m, n, k, seed, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(m, k, generator=g).to(dtype)
+    codes, scales = og.random_mxfp4_weight(n, k, seed + 1)
+    return a, codes, scales
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 256), (256, 512, 1024), (100, 300, 512),
+                                   (1, 256, 4096), (16, 512, 4096), (333, 768, 2048),
+                                   (129, 257, 288)])
+def test_fused_linear_matches_qdq_marlin_oracle(cuda_device, m, n, k):
+    from vllm_qdq_plugin.gemm import mxfp4_linear, prepare_mxfp4_weight
+    a, codes, scales = _inputs(m, n, k, seed=m * 31 + n + k)
+    w = prepare_mxfp4_weight(torch.from_numpy(codes).to(cuda_device),
+                             torch.from_numpy(scales).to(cuda_device))
+    out = mxfp4_linear(a.to(cuda_device), w)
+    assert out.dtype == torch.bfloat16 and out.shape == (m, n)
+    abits = a.view(torch.int16).numpy().view(np.uint16)
+    exact, absum = og.qdq_linear_exact(abits, codes, scales)
+    _check(out, exact, absum, f"linear {m}x{n}x{k}")
+
+
+def test_fp16_activation_and_bias(cuda_device):
+    from vllm_qdq_plugin.gemm import mxfp4_linear, prepare_mxfp4_weight
+    m, n, k = 200, 512, 1024
+    a, codes, scales = _inputs(m, n, k, seed=3, dtype=torch.float16)
+    bias = torch.randn(n, generator=torch.Generator().manual_seed(4)).to(torch.float16)
+    w = prepare_mxfp4_weight(torch.from_numpy(codes).to(cuda_device),
+                             torch.from_numpy(scales).to(cuda_device))
+    out = mxfp4_linear(a.to(cuda_device), w, bias.to(cuda_device))
+    assert out.dtype == torch.float16
+    abits = a.view(torch.int16).numpy().view(np.uint16)
+    exact, absum = og.qdq_linear_exact(abits, codes, scales, bias.float().numpy(), fp16=True)
+    _check(out, exact, absum + np.abs(bias.float().numpy())[None, :], "fp16 + bias")
+
+
+def test_codes_path_equals_fused_path(cuda_device):
+    from vllm_qdq_plugin.gemm import mxfp4_gemm_codes, mxfp4_linear, prepare_mxfp4_weight
+    from vllm_qdq_plugin.qdq import mxfp4_quantize
+    m, n, k = 256, 1024, 2048
+    a, codes, scales = _inputs(m, n, k, seed=11)
+    w = prepare_mxfp4_weight(torch.from_numpy(codes).to(cuda_device),
+                             torch.from_numpy(scales).to(cuda_device))
+    ad = a.to(cuda_device)
+    ac, asf = mxfp4_quantize(ad)
+    assert torch.equal(mxfp4_gemm_codes(ac, asf, w), mxfp4_linear(ad, w))
+
+
+def test_config3_full_size_rows_and_row_independence(cuda_device):
+    """M=4096, N=14336, K=4096; a row sample is checked against
+    the oracle, and every row must equal the same row computed alone (M=1)."""
+    from vllm_qdq_plugin.gemm import mxfp4_linear, prepare_mxfp4_weight
+    m, n, k = 4096, 14336, 4096
+    g = torch.Generator().manual_seed(2)
+    a = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    codes, scales = og.random_mxfp4_weight(n, k, seed=3)
+    w = prepare_mxfp4_weight(torch.from_numpy(codes).to(cuda_device),
+                             torch.from_numpy(scales).to(cuda_device))
+    ad = a.to(cuda_device)
+    out = mxfp4_linear(ad, w)
+    rows = np.array([0, 1, 127, 128, 2047, 4000, 4095])
+    abits = a[rows].contiguous().view(torch.int16).numpy().view(np.uint16)
+    exact, absum = og.qdq_linear_exact(abits, codes, scales)
+    _check(out[rows], exact, absum, "config 3 rows")
+    for r in (0, 4095):
+        single = mxfp4_linear(ad[r:r + 1], w)
+        assert torch.equal(single[0], out[r])
+    from vllm_qdq_plugin import _native
+    assert _native.device_status() == 0
+
+
+def test_marlin_hook_routes_captured_layers(cuda_device):
+    import types
+    from vllm_qdq_plugin import gemm, patch
+    m, n, k = 64, 256, 512
+    a, codes, scales = _inputs(m, n, k, seed=21)
+    marlin_weight = torch.zeros(8, dtype=torch.int32, device=cuda_device)  # stands for the repacked weight
+    w = gemm.prepare_mxfp4_weight(torch.from_numpy(codes).to(cuda_device),
+                                  torch.from_numpy(scales).to(cuda_device))
+    gemm.register_marlin_weight(marlin_weight, w)
+    st = types.SimpleNamespace(float4_e2m1f=object(), float8_e4m3fn=object())
+    ops = types.SimpleNamespace(marlin_gemm=lambda *args: (_ for _ in ()).throw(AssertionError("Marlin called")))
+    from vllm_qdq_plugin.qdq import mxfp4_qdq
+    patch._patch_marlin_gemm(ops, st, mxfp4_qdq, None, lambda *t: None)
+    import os
+    from unittest import mock
+    with mock.patch.dict(os.environ, {"VLLM_QDQ_FUSED_GEMM": "1"}):
+        out = ops.marlin_gemm(a.to(cuda_device), None, marlin_weight, None, torch.empty(1), None, None,
+                              None, None, None, torch.empty(1), st.float4_e2m1f, m, n, k)
+    abits = a.view(torch.int16).numpy().view(np.uint16)
+    exact, absum = og.qdq_linear_exact(abits, codes, scales)
+    _check(out, exact, absum, "hook")

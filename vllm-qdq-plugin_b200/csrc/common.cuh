@@ -25,6 +25,9 @@ void set_error(const char* fmt, ...);
 int fail(int status, const char* fmt, ...);
 int check_launch(const char* what);
 int device_sm_count();  // SM count of the current device (cached)
+// Device address of the library's status word on the current device (kernels
+// record bounded-wait timeouts there); nullptr + error message on failure.
+int* device_status_ptr();
 
 // ---------------------------------------------------------------------------
 // device-side conversion helpers
@@ -33,7 +36,7 @@ int device_sm_count();  // SM count of the current device (cached)
 // Packs RNE-to-E2M1 codes of (lo, hi) into one byte: lo -> bits 0..3, hi -> bits 4..7.
 __device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
   uint32_t out;
-  asm volatile(
+  asm(
       "{\n\t.reg .b8 t;\n\t"
       "cvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\t"
       "cvt.u32.u8 %0, t;\n\t}"
@@ -45,7 +48,7 @@ __device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
 // Expands one packed E2M1 byte into an fp16x2 word (bits 0..3 -> low half).
 __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
   uint32_t out;
-  asm volatile(
+  asm(
       "{\n\t.reg .b8 t;\n\t"
       "cvt.u8.u32 t, %1;\n\t"
       "cvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
@@ -57,7 +60,7 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
 // RNE fp32 -> E4M3 (saturating) -> back to fp32, exactly.
 __device__ __forceinline__ float round_e4m3(float v) {
   uint32_t h2;
-  asm volatile(
+  asm(
       "{\n\t.reg .b16 t;\n\t"
       "cvt.rn.satfinite.e4m3x2.f32 t, %1, %1;\n\t"
       "cvt.rn.f16x2.e4m3x2 %0, t;\n\t}"
@@ -69,7 +72,7 @@ __device__ __forceinline__ float round_e4m3(float v) {
 // RNE fp32 -> E4M3 byte (saturating).
 __device__ __forceinline__ uint32_t e4m3_byte(float v) {
   uint32_t out;
-  asm volatile(
+  asm(
       "{\n\t.reg .b16 t;\n\t"
       "cvt.rn.satfinite.e4m3x2.f32 t, %1, %1;\n\t"
       "cvt.u32.u16 %0, t;\n\t}"
@@ -97,6 +100,32 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   uint32_t out;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(out) : "f"(hi), "f"(lo));
   return out;
+}
+
+// Packed fp32 pair arithmetic (sm_100 f32x2 instructions): each lane is an
+// ordinary IEEE round-to-nearest-even operation, subnormals kept.
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 unpack_f32x2(uint64_t r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ float2 mul_f32x2(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack_f32x2(a.x, a.y)), "l"(pack_f32x2(b.x, b.y)));
+  return unpack_f32x2(d);
+}
+// a*b rounded to fp32, then + 0.0: the add turns a -0 product (exact zero or
+// an underflow) into +0 and leaves every other value unchanged.
+__device__ __forceinline__ float2 mul_f32x2_pos0(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack_f32x2(a.x, a.y)), "l"(pack_f32x2(b.x, b.y)));
+  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(d) : "l"(0ull));
+  return unpack_f32x2(d);
 }
 
 // Streaming 16-byte global load / store (data is touched exactly once).

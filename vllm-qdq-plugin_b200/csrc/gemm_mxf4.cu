@@ -1,0 +1,390 @@
+// Block-scaled MXFP4 GEMM on the sm_100a tensor cores:
+//   C[M, N] (bf16) = A[M, K] . W[N, K]^T (+ bias[N]),  fp32 accumulation,
+// where A and W are E2M1 codes (two per byte, element 2j in the low nibble)
+// with one E8M0 scale per 32 consecutive K elements.
+//
+// This replaces "MXFP4 QDQ of the activation, then Marlin's bf16 x
+// dequantised-FP4 GEMM" (reference: src/vllm_qdq_plugin/patch.py:51-57 +
+// vllm/_custom_ops.py:1277 marlin_gemm): because QDQ'd activations are exactly
+// MXFP4-representable, the activation can be fed to kind::mxf4 MMAs as codes
+// + scales, and every product is the same exact value Marlin forms.
+//
+// Kernel structure (one 128 x 256 output tile per CTA, 4 warps):
+//   warp 0 / one lane   TMA producer: A and W code tiles (128-byte swizzle)
+//                       and their scale-factor chunks (bulk copies) into a
+//                       4-stage shared-memory ring
+//   warp 1 / one lane   MMA issuer: tcgen05.cp scale factors smem -> TMEM,
+//                       4 x tcgen05.mma.kind::mxf4 (K = 64 each) per stage,
+//                       tcgen05.commit frees the stage
+//   warps 0-3           epilogue: TMEM accumulator -> registers -> bf16 -> global
+//
+// Scale factors use the tcgen05 "tiled" layout in global memory (see
+// qdq_sf_tile): rows are grouped by 128 and K-scales by 4 into 512-byte
+// chunks, chunk (rb, kc) at ((rb * kchunks) + kc) * 512, byte
+// (r % 32) * 16 + ((r / 32) % 4) * 4 + (ks % 4).  kchunks is even (the K-scale
+// count is padded to a multiple of 8), rows are padded to a multiple of 128.
+#include <cstring>
+
+#include "sm100.cuh"
+
+namespace qdqb200 {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;             // rows of A per tile (UMMA M)
+constexpr int BN = 256;             // rows of W per tile (UMMA N)
+constexpr int BK = 256;             // K elements per stage
+constexpr int BKB = BK / 2;         // bytes per row per stage (128: one swizzle row)
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BKB;   // 16 KB
+constexpr int B_BYTES = BN * BKB;   // 32 KB
+constexpr int SFA_BYTES = 2 * 512;  // 128 rows x 8 scales
+constexpr int SFB_BYTES = 4 * 512;  // 256 rows x 8 scales
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+constexpr int TMEM_COLS = 512;
+constexpr int ACC_COL = 0;          // 256 fp32 columns
+constexpr int SFA_COL = 256;        // 8 columns (2 K-chunks x 4)
+constexpr int SFB_COL = 272;        // 16 columns (2 K-chunks x 2 row blocks x 4)
+constexpr int THREADS = 128;
+constexpr uint32_t IDESC = idesc_mxf4(BM, BN, true);
+
+struct __align__(8) Barriers {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + sizeof(Barriers);
+
+// Output element type: bf16 (kF16 = false) or fp16; bias has the same type.
+template <bool kF16>
+struct OutT {
+  using T = __nv_bfloat16;
+  __device__ static float load(const T* p) { return __bfloat162float(*p); }
+  __device__ static uint32_t pack(float a, float b) { return pack_bf16x2(a, b); }
+  __device__ static T one(float a) { return __float2bfloat16_rn(a); }
+};
+template <>
+struct OutT<true> {
+  using T = __half;
+  __device__ static float load(const T* p) { return __half2float(*p); }
+  __device__ static uint32_t pack(float a, float b) { return pack_f16x2(a, b); }
+  __device__ static T one(float a) { return __float2half_rn(a); }
+};
+
+template <bool kF16>
+__global__ void __launch_bounds__(THREADS, 1)
+mxf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                 const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb,
+                 const void* __restrict__ bias_v, void* __restrict__ C_v, int M, int N,
+                 int K, int64_t ldc, int kchunks, int* status) {
+  using O = OutT<kF16>;
+  using T = typename O::T;
+  const T* bias = static_cast<const T*>(bias_v);
+  T* C = static_cast<T*>(C_v);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + STAGES * STAGE_BYTES);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_blk = blockIdx.y;
+  const int n_blk = blockIdx.x;
+  const int num_kt = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    bars->abort = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 0) {
+    tmem_alloc(&bars->tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0 && elect_one()) {
+    // ---------------- producer
+    int issued = 0;
+    for (int kt = 0; kt < num_kt; ++kt) {
+      const int s = kt % STAGES;
+      if (!mbar_wait(&bars->empty[s], ((kt / STAGES) & 1) ^ 1, status, 0x101)) {
+        bars->abort = 1;
+        break;
+      }
+      if (*(volatile int*)&bars->abort) break;
+      uint8_t* st = smem + s * STAGE_BYTES;
+      const bool second_rb = (n_blk * 2 + 1) * 128 < N;
+      mbar_arrive_expect_tx(&bars->full[s], A_BYTES + B_BYTES + SFA_BYTES + (second_rb ? 2048 : 1024));
+      tma_load_2d(st, &tmap_a, kt * BKB, m_blk * BM, &bars->full[s]);
+      tma_load_2d(st + A_BYTES, &tmap_b, kt * BKB, n_blk * BN, &bars->full[s]);
+      bulk_load(st + A_BYTES + B_BYTES, sfa + (static_cast<int64_t>(m_blk) * kchunks + 2 * kt) * 512,
+                1024, &bars->full[s]);
+      bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES,
+                sfb + (static_cast<int64_t>(2 * n_blk) * kchunks + 2 * kt) * 512, 1024, &bars->full[s]);
+      if (second_rb)
+        bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES + 1024,
+                  sfb + (static_cast<int64_t>(2 * n_blk + 1) * kchunks + 2 * kt) * 512, 1024,
+                  &bars->full[s]);
+      ++issued;
+    }
+    // Drain: every issued copy has landed before the CTA may exit.
+    for (int kt = (issued > STAGES ? issued - STAGES : 0); kt < issued; ++kt)
+      mbar_wait(&bars->full[kt % STAGES], (kt / STAGES) & 1, status, 0x102);
+  } else if (warp == 1 && elect_one()) {
+    // ---------------- MMA issuer
+    for (int kt = 0; kt < num_kt; ++kt) {
+      const int s = kt % STAGES;
+      if (!mbar_wait(&bars->full[s], (kt / STAGES) & 1, status, 0x201)) {
+        bars->abort = 1;
+        break;
+      }
+      if (*(volatile int*)&bars->abort) break;
+      tc_fence_after();
+      uint8_t* st = smem + s * STAGE_BYTES;
+      const uint8_t* sa = st + A_BYTES + B_BYTES;
+      const uint8_t* sb = sa + SFA_BYTES;
+      // scale factors: chunk j (K-scales 4j..4j+3 of this stage) of each 128-row block
+      tmem_cp_sf(tmem + SFA_COL + 0, smem_desc_sf(sa));
+      tmem_cp_sf(tmem + SFA_COL + 4, smem_desc_sf(sa + 512));
+      tmem_cp_sf(tmem + SFB_COL + 0, smem_desc_sf(sb));             // rows 0-127,   j = 0
+      tmem_cp_sf(tmem + SFB_COL + 8, smem_desc_sf(sb + 512));       // rows 0-127,   j = 1
+      tmem_cp_sf(tmem + SFB_COL + 4, smem_desc_sf(sb + 1024));      // rows 128-255, j = 0
+      tmem_cp_sf(tmem + SFB_COL + 12, smem_desc_sf(sb + 1536));     // rows 128-255, j = 1
+      const uint64_t da = smem_desc_sw128(st);
+      const uint64_t db = smem_desc_sw128(st + A_BYTES);
+#pragma unroll
+      for (int kk = 0; kk < BK / 64; ++kk) {
+        const uint32_t j = kk >> 1, sf_id = (kk & 1) * 2;
+        const uint32_t sfa_addr = (tmem + SFA_COL + 4 * j) | (sf_id << 30);
+        const uint32_t sfb_addr = (tmem + SFB_COL + 8 * j) | (sf_id << 30);
+        // K step of 64 E2M1 = 32 bytes inside the 128-byte swizzled row
+        mma_mxf4(tmem + ACC_COL, da + ((kk * 32) >> 4), db + ((kk * 32) >> 4),
+                 idesc_with_sf_ids(IDESC, sf_id, sf_id), sfa_addr, sfb_addr, (kt | kk) != 0);
+      }
+      tc_commit(&bars->empty[s]);
+    }
+    tc_commit(&bars->acc_full);  // also on abort: the epilogue waits for issued MMAs
+  }
+  __syncwarp();
+
+  // ---------------- epilogue (all 4 warps): TMEM lanes 32w..32w+31 = tile rows
+  const bool acc_ok = mbar_wait(&bars->acc_full, 0, status, 0x301);
+  tc_fence_after();
+  const bool do_store = acc_ok && !*(volatile int*)&bars->abort && num_kt > 0;
+  const int row = m_blk * BM + warp * 32 + lane;
+  const int n0 = n_blk * BN;
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    uint32_t r[32];
+    tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + ACC_COL + c0, r);
+    tmem_ld_wait();
+    if (!do_store || row >= M) continue;
+    T* crow = C + static_cast<int64_t>(row) * ldc + n0 + c0;
+    const int ncols = min(32, N - n0 - c0);
+    if (ncols <= 0) continue;
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    if (bias != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < ncols) v[i] += O::load(bias + n0 + c0 + i);
+    }
+    if (ncols == 32 && (reinterpret_cast<uintptr_t>(crow) & 15) == 0) {
+      uint4* dst = reinterpret_cast<uint4*>(crow);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        dst[q] = make_uint4(O::pack(v[8 * q + 0], v[8 * q + 1]), O::pack(v[8 * q + 2], v[8 * q + 3]),
+                            O::pack(v[8 * q + 4], v[8 * q + 5]), O::pack(v[8 * q + 6], v[8 * q + 7]));
+    } else {
+      for (int i = 0; i < ncols; ++i) crow[i] = O::one(v[i]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// Row-major E8M0/E4M3 scales [rows, ks] (row stride ld) -> tiled layout
+// (rows padded to 128, ks padded to a multiple of 8, pad bytes = pad_value).
+__global__ void sf_tile_kernel(const uint8_t* __restrict__ sf, uint8_t* __restrict__ out, int rows, int ks,
+                               int64_t ld, int rows_p, int ks_p, uint8_t pad_value) {
+  const int64_t total = static_cast<int64_t>(rows_p) * ks_p;
+  const int kchunks = ks_p / 4;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / ks_p);
+    const int k = static_cast<int>(i - static_cast<int64_t>(r) * ks_p);
+    const uint8_t v = (r < rows && k < ks) ? sf[static_cast<int64_t>(r) * ld + k] : pad_value;
+    const int64_t off = (static_cast<int64_t>(r / 128) * kchunks + k / 4) * 512 + (r % 32) * 16 +
+                        ((r / 32) % 4) * 4 + (k % 4);
+    out[off] = v;
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// host helpers
+// ---------------------------------------------------------------------------
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                    CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                    CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  }
+  return fn;
+}
+
+int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes, uint64_t ld_bytes,
+                    uint32_t box_bytes, uint32_t box_rows, bool swizzle128) {
+  PFN_encodeTiled fn = encode_fn();
+  if (fn == nullptr) return fail(QDQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld_bytes & 15))
+    return fail(QDQ_ERR_ALIGNMENT, "TMA operand needs 16-byte aligned base and row stride");
+  const cuuint64_t dims[2] = {row_bytes, rows};
+  const cuuint64_t strides[1] = {ld_bytes};
+  const cuuint32_t box[2] = {box_bytes, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(QDQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return QDQ_OK;
+}
+
+}  // namespace qdqb200
+
+using namespace qdqb200;
+
+extern "C" int64_t qdq_sf_tiled_bytes(int64_t rows, int64_t k) {
+  if (rows <= 0 || k <= 0) return 0;
+  const int64_t rows_p = (rows + 127) / 128 * 128;
+  const int64_t ks_p = ((k + 31) / 32 + 7) / 8 * 8;
+  return rows_p * ks_p;
+}
+
+extern "C" int qdq_sf_tile(const void* sf, void* sf_tiled, int64_t rows, int64_t k, int64_t ld, int block,
+                           void* stream) {
+  if (rows < 0 || k < 0) return fail(QDQ_ERR_INVALID_ARG, "qdq_sf_tile: negative shape");
+  if (block != 32) return fail(QDQ_ERR_UNSUPPORTED, "qdq_sf_tile: block must be 32 (MXFP4)");
+  if (rows == 0 || k == 0) return QDQ_OK;
+  if (!sf || !sf_tiled) return fail(QDQ_ERR_INVALID_ARG, "qdq_sf_tile: null pointer");
+  const int64_t ks = (k + block - 1) / block;
+  if (ld < ks) return fail(QDQ_ERR_INVALID_ARG, "qdq_sf_tile: ld < number of scales per row");
+  const int rows_p = static_cast<int>((rows + 127) / 128 * 128);
+  const int ks_p = static_cast<int>((ks + 7) / 8 * 8);
+  const int64_t total = static_cast<int64_t>(rows_p) * ks_p;
+  const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
+  sf_tile_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(sf), static_cast<uint8_t*>(sf_tiled), static_cast<int>(rows),
+      static_cast<int>(ks), ld, rows_p, ks_p, 0);
+  return check_launch("qdq_sf_tile");
+}
+
+extern "C" int fp4_gemm_mxf4(const void* a_codes, const void* a_sf_tiled, const void* w_codes,
+                             const void* w_sf_tiled, const void* bias, void* c, int64_t M, int64_t N,
+                             int64_t K, int64_t lda_bytes, int64_t ldw_bytes, int64_t ldc, int out_dtype,
+                             void* stream) {
+  if (out_dtype != QDQ_DTYPE_BF16 && out_dtype != QDQ_DTYPE_FP16)
+    return fail(QDQ_ERR_INVALID_ARG, "fp4_gemm_mxf4: out_dtype must be bf16 (0) or fp16 (1)");
+  if (M < 0 || N < 0 || K < 0) return fail(QDQ_ERR_INVALID_ARG, "fp4_gemm_mxf4: negative shape");
+  if (M == 0 || N == 0) return QDQ_OK;
+  if (!a_codes || !a_sf_tiled || !w_codes || !w_sf_tiled || !c)
+    return fail(QDQ_ERR_INVALID_ARG, "fp4_gemm_mxf4: null pointer");
+  if (K == 0) return fail(QDQ_ERR_UNSUPPORTED, "fp4_gemm_mxf4: K == 0");
+  if (K % 32 != 0) return fail(QDQ_ERR_UNSUPPORTED, "fp4_gemm_mxf4: K=%lld must be a multiple of 32", (long long)K);
+  if (M > (1ll << 30) || N > (1ll << 30) || K > (1ll << 30))
+    return fail(QDQ_ERR_UNSUPPORTED, "fp4_gemm_mxf4: dimension too large");
+  if (lda_bytes < K / 2 || ldw_bytes < K / 2 || ldc < N)
+    return fail(QDQ_ERR_INVALID_ARG, "fp4_gemm_mxf4: leading dimension too small");
+  if ((reinterpret_cast<uintptr_t>(a_sf_tiled) & 15) || (reinterpret_cast<uintptr_t>(w_sf_tiled) & 15))
+    return fail(QDQ_ERR_ALIGNMENT, "fp4_gemm_mxf4: scale-factor buffers must be 16-byte aligned");
+  int* status = device_status_ptr();
+  if (status == nullptr) return QDQ_ERR_CUDA;
+  CUtensorMap ta, tb;
+  if (int st = make_tmap_u8_2d(&ta, a_codes, M, K / 2, lda_bytes, BKB, BM, true)) return st;
+  if (int st = make_tmap_u8_2d(&tb, w_codes, N, K / 2, ldw_bytes, BKB, BN, true)) return st;
+  static bool attr_set[2][64] = {{false}};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const void* fn = out_dtype == QDQ_DTYPE_FP16 ? reinterpret_cast<const void*>(&mxf4_gemm_kernel<true>)
+                                               : reinterpret_cast<const void*>(&mxf4_gemm_kernel<false>);
+  if (dev >= 0 && dev < 64 && !attr_set[out_dtype][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(SMEM_BYTES));
+    if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_gemm_mxf4: smem attribute: %s", cudaGetErrorString(e));
+    attr_set[out_dtype][dev] = true;
+  }
+  const int kchunks = static_cast<int>(((K / 32) + 7) / 8 * 8 / 4);
+  dim3 grid(static_cast<unsigned>((N + BN - 1) / BN), static_cast<unsigned>((M + BM - 1) / BM));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto* sfa = static_cast<const uint8_t*>(a_sf_tiled);
+  auto* sfb = static_cast<const uint8_t*>(w_sf_tiled);
+  if (out_dtype == QDQ_DTYPE_FP16)
+    mxf4_gemm_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, sfa, sfb, bias, c, static_cast<int>(M),
+                                                            static_cast<int>(N), static_cast<int>(K), ldc,
+                                                            kchunks, status);
+  else
+    mxf4_gemm_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, sfa, sfb, bias, c, static_cast<int>(M),
+                                                             static_cast<int>(N), static_cast<int>(K), ldc,
+                                                             kchunks, status);
+  return check_launch("fp4_gemm_mxf4");
+}
+
+// ---------------------------------------------------------------------------
+// Fused linear: bf16/fp16 activation -> MXFP4 codes + tiled scales (exactly
+// the reference's mxfp4_qdq quantisation) -> block-scaled GEMM.  Scratch for
+// the activation codes comes from the caller's workspace.
+// ---------------------------------------------------------------------------
+extern "C" int64_t fp4_linear_workspace_bytes(int64_t M, int64_t K) {
+  if (M <= 0 || K <= 0) return 0;
+  const int64_t kp = (K + 31) / 32 * 32;
+  auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
+  return up(M * kp / 2) + up(M * kp / 32) + up(qdq_sf_tiled_bytes(M, K));
+}
+
+extern "C" int fp4_linear_mxf4(const void* a, int64_t lda, int dtype, const void* w_codes,
+                               const void* w_sf_tiled, const void* bias, void* c, int64_t M, int64_t N,
+                               int64_t K, int64_t ldw_bytes, int64_t ldc, void* workspace,
+                               int64_t workspace_bytes, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(QDQ_ERR_INVALID_ARG, "fp4_linear_mxf4: negative shape");
+  if (M == 0 || N == 0) return QDQ_OK;
+  if (K % 32 != 0) return fail(QDQ_ERR_UNSUPPORTED, "fp4_linear_mxf4: K=%lld must be a multiple of 32", (long long)K);
+  if (workspace == nullptr || workspace_bytes < fp4_linear_workspace_bytes(M, K))
+    return fail(QDQ_ERR_INVALID_ARG, "fp4_linear_mxf4: workspace smaller than fp4_linear_workspace_bytes()");
+  auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint8_t* a_codes = ws;
+  uint8_t* a_sf = a_codes + up(M * K / 2);
+  uint8_t* a_sf_t = a_sf + up(M * K / 32);
+  if (int st = qdq_mxfp4(a, nullptr, a_codes, a_sf, M, K, lda, K, dtype, 32, stream)) return st;
+  if (int st = qdq_sf_tile(a_sf, a_sf_t, M, K, K / 32, 32, stream)) return st;
+  return fp4_gemm_mxf4(a_codes, a_sf_t, w_codes, w_sf_tiled, bias, c, M, N, K, K / 2, ldw_bytes, ldc, dtype,
+                       stream);
+}

@@ -148,9 +148,11 @@ mxfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
       uint32_t code_word = 0;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        uint32_t byte = cvt_e2m1x2(__fmul_rn(F::lo(w[j]), inv), __fmul_rn(F::hi(w[j]), inv));
+        const float2 v = mul_f32x2(make_float2(F::lo(w[j]), F::hi(w[j])), make_float2(inv, inv));
+        uint32_t byte = cvt_e2m1x2(v.x, v.y);
         const uint32_t h = e2m1x2_to_f16x2(byte);
-        o[j] = F::pack(__fmul_rn(f16lo(h), sc), __fmul_rn(f16hi(h), sc));
+        const float2 d = mul_f32x2(make_float2(f16lo(h), f16hi(h)), make_float2(sc, sc));
+        o[j] = F::pack(d.x, d.y);
         if (F::kScaleCanBeZero && e == 0) {
           o[j] = fp16_zero_scale_word(w[j]);
           byte = zero_codes_of(o[j]);
@@ -244,15 +246,14 @@ __device__ __forceinline__ NvGroup nv_group(float vec_max, float gs, float rgs) 
   return g;
 }
 
-// Codes of two scaled elements; cast_to_fp4 takes torch.sign(), which is +0
-// for -0, so an exactly-zero input loses its sign (nvfp4_emulation_utils.py:425-436).
-__device__ __forceinline__ uint32_t nv_codes(float a, float b) {
-  a = fminf(fmaxf(a, -6.0f), 6.0f);
-  b = fminf(fmaxf(b, -6.0f), 6.0f);
-  uint32_t byte = cvt_e2m1x2(a, b);
-  if (a == 0.0f) byte &= 0xF7u;
-  if (b == 0.0f) byte &= 0x7Fu;
-  return byte;
+// Codes of two elements x*out_scale.  The reference clamps to +-6 and rounds
+// to nearest-even (nvfp4_emulation_utils.py:450-451, :425-436): the
+// satfinite E2M1 conversion does both.  cast_to_fp4 multiplies by
+// torch.sign(), which is +0 for a -0 product, so zero products are made +0
+// before encoding (the +0.0 add in mul_f32x2_pos0).
+__device__ __forceinline__ uint32_t nv_codes(float xa, float xb, float out_scale) {
+  const float2 p = mul_f32x2_pos0(make_float2(xa, xb), make_float2(out_scale, out_scale));
+  return cvt_e2m1x2(p.x, p.y);
 }
 
 template <int kDtype, bool kContig, bool kY, bool kCodes, bool kScales>
@@ -300,11 +301,11 @@ nvfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
       uint32_t code_word = 0;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint32_t byte =
-            nv_codes(__fmul_rn(F::lo(w[j]), g.out_scale), __fmul_rn(F::hi(w[j]), g.out_scale));
+        const uint32_t byte = nv_codes(F::lo(w[j]), F::hi(w[j]), g.out_scale);
         code_word |= byte << (8 * j);
         const uint32_t h = e2m1x2_to_f16x2(byte);
-        o[j] = F::pack(__fmul_rn(f16lo(h), g.deq), __fmul_rn(f16hi(h), g.deq));
+        const float2 d = mul_f32x2(make_float2(f16lo(h), f16hi(h)), make_float2(g.deq, g.deq));
+        o[j] = F::pack(d.x, d.y);
       }
       if (ok[u]) {
         if (kY) st_stream(reinterpret_cast<uint4*>(y + yo[u]), make_uint4(o[0], o[1], o[2], o[3]));
@@ -336,8 +337,7 @@ nvfp4_generic_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
     for (int i = 0; i < 16; ++i) amax = max(amax, static_cast<uint32_t>(xr[i] & 0x7FFFu));
     const NvGroup ng = nv_group(F::amax_value(amax), gs, rgs);
     for (int i = 0; i < 16; i += 2) {
-      const uint32_t byte = nv_codes(__fmul_rn(F::one(xr[i]), ng.out_scale),
-                                     __fmul_rn(F::one(xr[i + 1]), ng.out_scale));
+      const uint32_t byte = nv_codes(F::one(xr[i]), F::one(xr[i + 1]), ng.out_scale);
       const uint32_t h = e2m1x2_to_f16x2(byte);
       if (yr) {
         yr[i] = F::pack1(__fmul_rn(f16lo(h), ng.deq));

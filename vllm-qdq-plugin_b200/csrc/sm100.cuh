@@ -1,0 +1,240 @@
+// Thin inline-PTX layer for the sm_100a features the GEMM and attention
+// kernels use: mbarriers with bounded waits, TMA (no multicast), bulk copies,
+// TMEM allocation, tcgen05.mma block-scaled FP4, tcgen05.cp, tcgen05.ld.
+//
+// Every wait is bounded: after kWaitNs of wall time a wait gives up, records
+// QDQ_ERR_TIMEOUT in the device status word and returns false, so a kernel
+// can release its TMEM and exit instead of hanging the GPU.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace qdqb200 {
+namespace sm100 {
+
+// Bounded waits give up after kWaitNs nanoseconds of %globaltimer time.
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
+
+// Kernels receive a pointer to the library's device status word (see
+// device_status_ptr()); the first failure is kept: (status << 16) | where.
+__device__ __forceinline__ void record_timeout(int* status, int where) {
+  atomicCAS(status, 0, (QDQ_ERR_TIMEOUT << 16) | (where & 0xFFFF));
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for the phase with the given parity to complete: polls
+// try_wait and gives up after `timeout_ns` of wall time, recording
+// QDQ_ERR_TIMEOUT and the call site in the status word.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int where,
+                                          uint64_t timeout_ns = kWaitNs) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - t0 > timeout_ns) {
+      record_timeout(status, where);
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- TMA / bulk
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t x,
+                                            int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int32_t x,
+                                            int32_t y, int32_t z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+// Contiguous global -> shared copy (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---------------------------------------------------------------- TMEM
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Arrive on `bar` once every tcgen05 op this thread issued so far completes.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// ---------------------------------------------------------------- descriptors
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows of 128 B,
+// 8-row core groups 1024 B apart (SBO), version 1, layout type 2.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* smem) {
+  const uint64_t addr = smem_u32(smem);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;             // start address
+  d |= static_cast<uint64_t>(1) << 16;       // LBO (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;  // SBO
+  d |= static_cast<uint64_t>(1) << 46;       // descriptor version (sm100)
+  d |= static_cast<uint64_t>(2) << 61;       // SWIZZLE_128B
+  return d;
+}
+// Descriptor of a contiguous 32-row x 16-byte block (no swizzle) for tcgen05.cp.
+__device__ __forceinline__ uint64_t smem_desc_sf(const void* smem) {
+  const uint64_t addr = smem_u32(smem);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;
+  d |= static_cast<uint64_t>(0) << 16;         // LBO unused (single core matrix along K)
+  d |= static_cast<uint64_t>(128 >> 4) << 32;  // SBO: 8 rows x 16 B
+  d |= static_cast<uint64_t>(1) << 46;
+  return d;
+}
+
+// Instruction descriptor of tcgen05.mma.kind::mxf4 (E2M1 x E2M1, UE8M0
+// scales) and kind::mxf4nvf4 with block16 (UE4M3 scales when e8m0 == false).
+__host__ __device__ constexpr uint32_t idesc_mxf4(uint32_t M, uint32_t N, bool e8m0 = true) {
+  return (1u << 7)                    // A format E2M1
+         | (1u << 10)                 // B format E2M1
+         | ((N >> 3) << 17)           // N
+         | ((e8m0 ? 1u : 0u) << 23)   // scale format
+         | ((M >> 4) << 24);          // M
+}
+__device__ __forceinline__ uint32_t idesc_with_sf_ids(uint32_t idesc, uint32_t sfa_id, uint32_t sfb_id) {
+  return idesc | (sfb_id << 4) | (sfa_id << 29);
+}
+
+// D(tmem) (+)= A(smem) x B(smem)^T with per-32 (mxf4) E8M0 block scales from TMEM.
+__device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+// Same with per-16 block scales (kind::mxf4nvf4, block16).
+__device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// 32 lanes x 128 bits of shared memory -> TMEM, replicated into the four
+// 32-lane quadrants (the scale-factor layout the block-scaled MMA reads).
+__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Each thread of a warp reads 32 consecutive 32-bit columns of its lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+}  // namespace sm100
+
+// Host: build a 2-D TMA descriptor for a row-major uint8 matrix (rows x
+// row_bytes, stride ld_bytes) with a (box_bytes x box_rows) box and 128-byte
+// swizzle.  Returns QDQ_OK or an error status (message set).
+int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes,
+                    uint64_t ld_bytes, uint32_t box_bytes, uint32_t box_rows, bool swizzle128);
+
+}  // namespace qdqb200

@@ -37,8 +37,18 @@ _SIGNATURES: dict[str, list] = {
                                _c_void_p],
     "qdq_last_error": [],
     "qdq_abi_version": [],
+    "qdq_device_status": [ctypes.POINTER(ctypes.c_int), _int],
+    "qdq_selftest_bounded_wait": [_i64, _c_void_p],
+    "qdq_sf_tiled_bytes": [_i64, _i64],
+    "qdq_sf_tile": [_c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p],
+    "fp4_gemm_mxf4": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64,
+                      _i64, _i64, _i64, _i64, _int, _c_void_p],
+    "fp4_linear_workspace_bytes": [_i64, _i64],
+    "fp4_linear_mxf4": [_c_void_p, _i64, _int, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64,
+                        _i64, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p],
 }
-_RESTYPES = {"qdq_last_error": ctypes.c_char_p}
+_RESTYPES = {"qdq_last_error": ctypes.c_char_p, "qdq_sf_tiled_bytes": ctypes.c_int64,
+             "fp4_linear_workspace_bytes": ctypes.c_int64}
 
 
 def lib() -> ctypes.CDLL:
@@ -80,6 +90,13 @@ def check(fn: str, status: int) -> None:
 
 def call(fn: str, *args) -> None:
     check(fn, getattr(lib(), fn)(*args))
+
+
+def device_status(clear: bool = True) -> int:
+    """The library's device status word (0 = ok; else (status << 16) | site)."""
+    out = ctypes.c_int(0)
+    call("qdq_device_status", ctypes.byref(out), int(clear))
+    return out.value
 
 
 def require_cuda(*tensors: torch.Tensor) -> None:

@@ -1,0 +1,192 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Fused MXFP4 linear: activation quantisation + tcgen05 block-scaled FP4 GEMM.
+
+The reference simulates W4A4 by running `mxfp4_qdq` on the activation and
+then vLLM's Marlin kernel (bf16 activation x dequantised FP4 weight)
+(reference: src/vllm_qdq_plugin/patch.py:51-57; vllm/_custom_ops.py:1277).
+A QDQ'd activation is exactly representable in MXFP4, so the same product is
+computed here with FP4 tensor-core MMAs on codes + E8M0 scales
+(`fp4_gemm_mxf4` / `fp4_linear_mxf4` in include/qdq_b200.h).
+
+Marlin layers carry Marlin-repacked weights that this kernel cannot read, so
+with VLLM_QDQ_FUSED_GEMM=1 `capture_marlin_weights()` records each MXFP4
+layer's raw weight codes / scales / bias when vLLM prepares it for Marlin
+(vllm/model_executor/layers/quantization/utils/marlin_utils_fp4.py:205
+prepare_fp4_layer_for_marlin) and keys them by the repacked weight, which the
+patched `marlin_gemm` receives as `b_q_weight`.  Layers without a captured
+weight keep the reference path (QDQ + Marlin).
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import functools
+import threading
+
+import torch
+
+from . import _native
+from ._log import init_logger
+from .qdq.mxfp4 import mxfp4_quantize
+
+logger = init_logger(__name__)
+
+
+@dataclasses.dataclass
+class Mxfp4Weight:
+    """An MXFP4 weight [N, K] in the layout the tcgen05 GEMM reads."""
+
+    codes: torch.Tensor     # uint8 [N, K/2], element 2j in the low nibble
+    sf_tiled: torch.Tensor  # uint8, tiled E8M0 scales (qdq_sf_tile layout)
+    n: int
+    k: int
+    bias: torch.Tensor | None = None
+
+    @property
+    def device(self) -> torch.device:
+        return self.codes.device
+
+
+def _tile_scales(scales: torch.Tensor, rows: int, k: int) -> torch.Tensor:
+    lib = _native.lib()
+    nbytes = lib.qdq_sf_tiled_bytes(rows, k)
+    out = torch.empty((nbytes,), dtype=torch.uint8, device=scales.device)
+    _native.call("qdq_sf_tile", scales.data_ptr(), out.data_ptr(), rows, k, scales.stride(0), 32,
+                 _native.stream_ptr(scales.device))
+    return out
+
+
+def prepare_mxfp4_weight(codes: torch.Tensor, scales: torch.Tensor,
+                         bias: torch.Tensor | None = None) -> Mxfp4Weight:
+    """codes uint8 [N, K/2] (packed E2M1), scales uint8 [N, K/32] (E8M0)."""
+    _native.require_cuda(codes, scales)
+    assert codes.dtype == torch.uint8 and scales.dtype == torch.uint8
+    n, kh = codes.shape
+    k = kh * 2
+    assert k % 32 == 0 and scales.shape == (n, k // 32), (codes.shape, scales.shape)
+    codes = codes.contiguous()
+    scales = scales.contiguous()
+    return Mxfp4Weight(codes=codes, sf_tiled=_tile_scales(scales, n, k), n=n, k=k, bias=bias)
+
+
+@torch.library.custom_op("qdq_b200::mxfp4_gemm_codes", mutates_args=())
+def _gemm_codes_op(a_codes: torch.Tensor, a_sf_tiled: torch.Tensor, w_codes: torch.Tensor,
+                   w_sf_tiled: torch.Tensor, bias: torch.Tensor | None, out_fp16: bool) -> torch.Tensor:
+    _native.require_cuda(a_codes, w_codes)
+    m, n, k = a_codes.shape[0], w_codes.shape[0], w_codes.shape[1] * 2
+    out = torch.empty((m, n), dtype=torch.float16 if out_fp16 else torch.bfloat16,
+                      device=a_codes.device)
+    _native.call("fp4_gemm_mxf4", a_codes.data_ptr(), a_sf_tiled.data_ptr(), w_codes.data_ptr(),
+                 w_sf_tiled.data_ptr(), _native.ptr(bias), out.data_ptr(), m, n, k,
+                 a_codes.stride(0), w_codes.stride(0), n, int(out_fp16),
+                 _native.stream_ptr(a_codes.device))
+    return out
+
+
+@_gemm_codes_op.register_fake
+def _(a_codes, a_sf_tiled, w_codes, w_sf_tiled, bias, out_fp16):
+    return a_codes.new_empty((a_codes.shape[0], w_codes.shape[0]),
+                             dtype=torch.float16 if out_fp16 else torch.bfloat16)
+
+
+@torch.library.custom_op("qdq_b200::mxfp4_linear", mutates_args=())
+def _linear_op(a: torch.Tensor, w_codes: torch.Tensor, w_sf_tiled: torch.Tensor,
+               bias: torch.Tensor | None) -> torch.Tensor:
+    _native.require_cuda(a, w_codes, w_sf_tiled)
+    a = a if a.stride(-1) == 1 else a.contiguous()
+    m, k = a.shape
+    n = w_codes.shape[0]
+    lib = _native.lib()
+    ws = torch.empty((lib.fp4_linear_workspace_bytes(m, k),), dtype=torch.uint8, device=a.device)
+    out = torch.empty((m, n), dtype=a.dtype, device=a.device)
+    _native.call("fp4_linear_mxf4", a.data_ptr(), a.stride(0) if m > 1 else k,
+                 _native.DTYPE_CODE[a.dtype], w_codes.data_ptr(), w_sf_tiled.data_ptr(),
+                 _native.ptr(bias), out.data_ptr(), m, n, k, w_codes.stride(0), n, ws.data_ptr(),
+                 ws.numel(), _native.stream_ptr(a.device))
+    return out
+
+
+@_linear_op.register_fake
+def _(a, w_codes, w_sf_tiled, bias):
+    return a.new_empty((a.shape[0], w_codes.shape[0]))
+
+
+def mxfp4_linear(a: torch.Tensor, weight: Mxfp4Weight, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M, N] = mxfp4_qdq(a) @ dequant(weight)^T (+ bias), fp32 accumulation.
+
+    a: [M, K] bf16/fp16 CUDA tensor, K % 32 == 0.  Output dtype = a.dtype.
+    """
+    assert a.dim() == 2 and a.dtype in (torch.bfloat16, torch.float16)
+    assert a.shape[1] == weight.k, (a.shape, weight.k)
+    if bias is None:
+        bias = weight.bias
+    if bias is not None:
+        bias = bias.to(a.dtype).contiguous()
+    return torch.ops.qdq_b200.mxfp4_linear(a, weight.codes, weight.sf_tiled, bias)
+
+
+def mxfp4_gemm_codes(a_codes: torch.Tensor, a_scales: torch.Tensor, weight: Mxfp4Weight,
+                     bias: torch.Tensor | None = None, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """GEMM on pre-quantised activation codes [M, K/2] + row-major E8M0 scales [M, K/32]."""
+    m = a_codes.shape[0]
+    a_sf = _tile_scales(a_scales.contiguous(), m, weight.k)
+    return torch.ops.qdq_b200.mxfp4_gemm_codes(a_codes.contiguous(), a_sf, weight.codes,
+                                               weight.sf_tiled, bias, out_dtype == torch.float16)
+
+
+# ---------------------------------------------------------------------------
+# Marlin-layer capture (VLLM_QDQ_FUSED_GEMM=1)
+# ---------------------------------------------------------------------------
+_REGISTRY: dict[int, Mxfp4Weight] = {}
+_REG_LOCK = threading.Lock()
+
+
+def register_marlin_weight(marlin_weight: torch.Tensor, weight: Mxfp4Weight) -> None:
+    with _REG_LOCK:
+        _REGISTRY[marlin_weight.data_ptr()] = weight
+
+
+def lookup_marlin_weight(marlin_weight: torch.Tensor) -> Mxfp4Weight | None:
+    return _REGISTRY.get(marlin_weight.data_ptr())
+
+
+def fused_marlin_replacement(a, c, b_q_weight, b_bias, size_m, size_n, size_k):
+    """Run the fused FP4 linear for a captured layer; None means "not captured"."""
+    w = lookup_marlin_weight(b_q_weight)
+    if w is None or a.shape[1] != w.k or w.n != size_n or size_k != w.k:
+        return None
+    out = mxfp4_linear(a, w, w.bias if b_bias is not None else None)
+    if c is not None:
+        c.copy_(out)
+        return c
+    return out
+
+
+def capture_marlin_weights() -> bool:
+    """Wrap vLLM's prepare_fp4_layer_for_marlin to keep the raw MXFP4 weights."""
+    try:
+        from vllm.model_executor.layers.quantization.utils import marlin_utils_fp4 as mu
+    except ImportError:
+        return False
+    original = mu.prepare_fp4_layer_for_marlin
+    if getattr(original, "_qdq_b200_capture", False):
+        return True
+
+    @functools.wraps(original)
+    def prepare_fp4_layer_for_marlin(layer, input_dtype=None):
+        raw = None
+        if not hasattr(layer, "weight_global_scale") and (input_dtype is None or input_dtype.itemsize != 1):
+            bias = getattr(layer, "bias", None)
+            raw = (layer.weight.data, layer.weight_scale.data,
+                   None if bias is None else bias.data.clone())
+        result = original(layer, input_dtype)
+        if raw is not None and raw[0].is_cuda:
+            codes, scales, bias = raw
+            register_marlin_weight(layer.weight, prepare_mxfp4_weight(
+                codes.view(torch.uint8), scales.view(torch.uint8), bias))
+        return result
+
+    prepare_fp4_layer_for_marlin._qdq_b200_capture = True
+    mu.prepare_fp4_layer_for_marlin = prepare_fp4_layer_for_marlin
+    logger.warning("vllm-qdq-plugin: capturing raw MXFP4 weights for the fused FP4 GEMM")
+    return True
