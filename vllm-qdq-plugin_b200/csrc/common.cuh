@@ -119,15 +119,6 @@ __device__ __forceinline__ float2 mul_f32x2(float2 a, float2 b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack_f32x2(a.x, a.y)), "l"(pack_f32x2(b.x, b.y)));
   return unpack_f32x2(d);
 }
-// a*b rounded to fp32, then + 0.0: the add turns a -0 product (exact zero or
-// an underflow) into +0 and leaves every other value unchanged.
-__device__ __forceinline__ float2 mul_f32x2_pos0(float2 a, float2 b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack_f32x2(a.x, a.y)), "l"(pack_f32x2(b.x, b.y)));
-  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(d) : "l"(0ull));
-  return unpack_f32x2(d);
-}
-
 // Streaming 16-byte global load / store (data is touched exactly once).
 __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
   uint4 v;

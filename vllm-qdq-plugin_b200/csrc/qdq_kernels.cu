@@ -249,11 +249,14 @@ __device__ __forceinline__ NvGroup nv_group(float vec_max, float gs, float rgs) 
 // Codes of two elements x*out_scale.  The reference clamps to +-6 and rounds
 // to nearest-even (nvfp4_emulation_utils.py:450-451, :425-436): the
 // satfinite E2M1 conversion does both.  cast_to_fp4 multiplies by
-// torch.sign(), which is +0 for a -0 product, so zero products are made +0
-// before encoding (the +0.0 add in mul_f32x2_pos0).
+// torch.sign(), which is +0 for a -0 product (x == -0, or an underflow), so a
+// zero product is encoded as +0.
 __device__ __forceinline__ uint32_t nv_codes(float xa, float xb, float out_scale) {
-  const float2 p = mul_f32x2_pos0(make_float2(xa, xb), make_float2(out_scale, out_scale));
-  return cvt_e2m1x2(p.x, p.y);
+  const float2 p = mul_f32x2(make_float2(xa, xb), make_float2(out_scale, out_scale));
+  uint32_t byte = cvt_e2m1x2(p.x, p.y);
+  if (p.x == 0.0f) byte &= 0xF7u;
+  if (p.y == 0.0f) byte &= 0x7Fu;
+  return byte;
 }
 
 template <int kDtype, bool kContig, bool kY, bool kCodes, bool kScales>
