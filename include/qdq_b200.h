@@ -153,6 +153,23 @@ int fp4_linear_mxf4(const void* a, int64_t lda, int dtype, const void* w_codes,
                     int64_t K, int64_t ldw_bytes, int64_t ldc, void* workspace,
                     int64_t workspace_bytes, void* stream);
 
+/*
+ * fp4_linear_mxf4 for callers that cannot allocate device memory (no
+ * counterpart in the reference: its QDQ and Marlin paths allocate through
+ * torch).  Same arguments and result as fp4_linear_mxf4 minus the workspace:
+ * the activation codes go to a static 32 MiB scratch array in the library's
+ * device memory (fp4_linear_noalloc_scratch_bytes()), held by every GPU that
+ * loads the library until exit.  Calls needing more scratch than that
+ * (fp4_linear_workspace_bytes(M, K) > 32 MiB) fail with QDQ_ERR_INVALID_ARG.
+ * All calls on a device share the array: calls that overlap on the GPU race.
+ * The first call on a device looks up the array's address; make it before any
+ * stream capture.  Allocates nothing (no cudaMalloc/cudaFree).
+ */
+int64_t fp4_linear_noalloc_scratch_bytes(void);
+int fp4_linear_mxf4_noalloc(const void* a, int64_t lda, int dtype, const void* w_codes,
+                            const void* w_sf_tiled, const void* bias, void* c, int64_t M, int64_t N,
+                            int64_t K, int64_t ldw_bytes, int64_t ldc, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif
