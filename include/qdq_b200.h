@@ -153,6 +153,37 @@ int fp4_linear_mxf4(const void* a, int64_t lda, int dtype, const void* w_codes,
                     int64_t K, int64_t ldw_bytes, int64_t ldc, void* workspace,
                     int64_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Sage3 FP4 attention — replaces the SAGE_ATTN backend's attention:
+ *   reference  vllm_qdq_plugin/sage3_attn/impl.py:91-137 (_forward_sage3)
+ *              -> sage3/api.py:89-387 (_run_attention: qk_smoothing,
+ *              quantize_to_mxfp4, mxfp4_flash_attention / tiled_online_attention)
+ * ------------------------------------------------------------------------- */
+
+/* Workspace bytes sage3_fp4_attn needs (0 for an unsupported shape). */
+int64_t sage3_attn_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t D);
+
+/*
+ * O = softmax(Q K^T * sm_scale) V with FP4 tensor-core MMAs (self-attention,
+ * Q/K/V/O of the same [B, L, H, D] shape, D = 128, bf16).
+ *   strides: 12 element strides, for q, k, v, o in turn: (batch, token, head);
+ *            the head-dim stride must be 1.  NHD tensors [B, L, H, D] and HND
+ *            tensors [B, H, L, D] are both expressed this way.
+ *   quant_format: 0 = MXFP4 (E2M1 + E8M0 per 32; the reference mxfp4_hw
+ *            semantics), 1 = NVFP4 (E2M1 + E4M3 per 16).
+ *   acc_mode: 0 = fp32, 1 = a reduced-precision PV accumulator of the
+ *            reference (accepted; this kernel accumulates in fp32 either way).
+ *   causal: non-zero for a causal mask (query i sees keys <= i).
+ *   smoothing: non-zero for the reference's qk_smoothing (K centring,
+ *            per-128-token Q means and the delta_s correction).
+ *   workspace: >= sage3_attn_workspace_bytes() device bytes.
+ * Keys beyond L are masked (the reference attends to its zero padding).
+ */
+int sage3_fp4_attn(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t L,
+                   int64_t H, int64_t D, const int64_t* strides, float sm_scale,
+                   int quant_format, int acc_mode, int causal, int smoothing, int dtype,
+                   void* workspace, int64_t workspace_bytes, void* stream);
+
 /*
  * fp4_linear_mxf4 for callers that cannot allocate device memory (no
  * counterpart in the reference: its QDQ and Marlin paths allocate through

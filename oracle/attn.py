@@ -1,0 +1,161 @@
+"""CPU oracle of the Sage3 MXFP4 attention (the reference's mxfp4_hw path).
+
+TEST INFRASTRUCTURE ONLY (tests/, smoke(), bench.py baselines).
+
+Restates, in numpy (float64 accumulation):
+  - qk_smoothing (src/vllm_qdq_plugin/sage3_attn/sage3/transforms.py:47-95)
+    applied before padding, as the mxfp4_hw branch does (sage3/api.py:161-182),
+    with every bf16 op rounded to bf16;
+  - quantize_to_mxfp4 of q_s, k_c (along D) and V (along the sequence)
+    (sage3/mxfp4_hw_kernel.py:73-116) via the C oracle, pinned to the
+    reference's own outputs by tests/golden/mxfp4_hw_quant.npz;
+  - the flash loop of _mxfp4_attn_fwd_inner (mxfp4_hw_kernel.py:205-282):
+    S = deq(Q) deq(K)^T + delta_s, base-2 online softmax with
+    qk_scale = sm_scale * log2(e), l += sum of the unquantised p, P quantised
+    per 32 keys with E8M0 scale 2^ceil(log2(max p / 6)) and round-to-nearest-even
+    E2M1, O += deq(P) deq(V), O / l.
+The quantised P depends on the running max at each key tile, so the tile
+width is a parameter: the sm_100a kernel uses 128, the reference kernel 64.
+Keys beyond L are masked (mask_padding=True) or, as in the reference,
+attended as zero keys (mask_padding=False).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import qdq as oq
+
+E2M1 = np.array([0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6], np.float64)
+LOG2E = 1.4426950408889634
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """Round float values to bf16 (nearest even), returned as float32."""
+    x = np.asarray(x, np.float32)
+    b = x.view(np.uint32).astype(np.uint64)
+    b = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
+    return b.astype(np.uint32).view(np.float32)
+
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def _deq(codes: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    lo = E2M1[codes & 0xF]
+    hi = E2M1[codes >> 4]
+    vals = np.stack([lo, hi], axis=-1).reshape(*codes.shape[:-1], codes.shape[-1] * 2)
+    sc = np.exp2(scales.astype(np.float64) - 127.0)
+    return vals * np.repeat(sc, 32, axis=-1)
+
+
+def _rne_e2m1(v: np.ndarray) -> np.ndarray:
+    a = np.minimum(np.abs(v), 6.0)
+    q = np.where(a <= 0.25, 0.0, np.where(a < 0.75, 0.5, np.where(a <= 1.25, 1.0,
+        np.where(a < 1.75, 1.5, np.where(a <= 2.5, 2.0, np.where(a < 3.5, 3.0,
+        np.where(a <= 5.0, 4.0, 6.0)))))))
+    return np.copysign(q, v)
+
+
+def _ceil_log2(r: np.ndarray) -> np.ndarray:
+    m, e = np.frexp(r)  # r = m * 2^e, m in [0.5, 1)
+    out = np.where(m == 0.5, e - 1, e).astype(np.int64)
+    return np.where(r == 0, -127, out)
+
+
+def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True):
+    """q, k, v: float32 [L, D] holding bf16 values for one (batch, head).
+    Returns (qd, kd, vd, ds): dequantised Q [Lp, D], K [Lp, D], V [Lp, D] (from
+    V^T codes) and delta_s [G, Lp] (zeros without smoothing)."""
+    L, D = q.shape
+    Lp = (L + 127) // 128 * 128
+    G = Lp // 128
+    if smoothing:
+        kmean = bf16_round(k.astype(np.float64).mean(axis=0))
+        kc = bf16_round(k - kmean)
+        qpad = np.zeros((Lp, D), np.float32)
+        qpad[:L] = q
+        qmeans = bf16_round(qpad.reshape(G, 128, D).astype(np.float64).mean(axis=1))
+        qs = bf16_round(q - np.repeat(qmeans, 128, axis=0)[:L])
+        ds = bf16_round(qmeans.astype(np.float64) @ kc.astype(np.float64).T)  # [G, L]
+    else:
+        kc, qs = k, q
+        ds = np.zeros((G, L), np.float32)
+    pad = lambda a: np.concatenate([a, np.zeros((Lp - L, D), np.float32)])  # noqa: E731
+    qcodes, qsc = oq.mxfp4_hw_quant(pad(qs))
+    kcodes, ksc = oq.mxfp4_hw_quant(pad(kc))
+    vcodes, vsc = oq.mxfp4_hw_quant(np.ascontiguousarray(pad(v).T))  # [D, Lp/2], [D, Lp/32]
+    dsp = np.zeros((G, Lp), np.float64)
+    dsp[:, :L] = ds
+    return _deq(qcodes, qsc), _deq(kcodes, ksc), _deq(vcodes, vsc).T, dsp
+
+
+def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: bool = False,
+          mask_padding: bool = True) -> np.ndarray:
+    """The mxfp4_hw flash loop on dequantised operands; returns O [L, D] float64."""
+    Lp, D = qd.shape
+    n_keys = L if mask_padding else Lp
+    qk_scale = sm_scale * LOG2E
+    rows = np.arange(Lp)
+    m = np.full(Lp, -np.inf)
+    l = np.zeros(Lp)
+    acc = np.zeros((Lp, D))
+    group = np.repeat(np.arange(Lp // 128), 128)
+    for n0 in range(0, n_keys, block_n):
+        n1 = min(n0 + block_n, Lp)
+        s = qd @ kd[n0:n1].T + ds[group, n0:n1]
+        keys = np.arange(n0, n1)
+        valid = np.broadcast_to(keys[None, :] < n_keys, s.shape)
+        if causal:
+            valid = valid & (keys[None, :] <= rows[:, None])
+        s = np.where(valid, s, -np.inf)
+        m_new = np.maximum(m, s.max(axis=1) * qk_scale)
+        alpha = np.where(np.isneginf(m), 0.0, np.exp2(m - m_new))
+        p = np.where(valid, np.exp2(s * qk_scale - m_new[:, None]), 0.0)
+        l = l * alpha + p.sum(axis=1)
+        acc = acc * alpha[:, None]
+        w = n1 - n0
+        pg = p.reshape(Lp, w // 32, 32)
+        e = np.clip(_ceil_log2(pg.max(axis=2) / 6.0), -127, 127)
+        sc = np.exp2(e.astype(np.float64))[:, :, None]
+        pq = (_rne_e2m1(pg / sc) * sc).reshape(Lp, w)
+        acc = acc + pq @ vd[n0:n1]
+        m = m_new
+    return (acc / l[:, None])[:L]
+
+
+def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_scale: float,
+              block_n: int = 128, causal: bool = False, smoothing: bool = True,
+              mask_padding: bool = True) -> np.ndarray:
+    """q/k/v: uint16 bf16 bit patterns [L, H, D] (NHD with B = 1); returns O [L, H, D]."""
+    L, H, D = q_bits.shape
+    out = np.zeros((L, H, D))
+    for h in range(H):
+        q = bf16_bits_to_f32(q_bits[:, h])
+        k = bf16_bits_to_f32(k_bits[:, h])
+        v = bf16_bits_to_f32(v_bits[:, h])
+        qd, kd, vd, ds = prepass(q, k, v, smoothing)
+        out[:, h] = flash(qd, kd, vd, ds, L, sm_scale, block_n, causal, mask_padding)
+    return out
+
+
+def exact_attention(q_bits, k_bits, v_bits, sm_scale: float, causal: bool = False) -> np.ndarray:
+    """Unquantised float64 softmax attention (the accuracy reference)."""
+    L, H, D = q_bits.shape
+    out = np.zeros((L, H, D))
+    for h in range(H):
+        q = bf16_bits_to_f32(q_bits[:, h]).astype(np.float64)
+        k = bf16_bits_to_f32(k_bits[:, h]).astype(np.float64)
+        v = bf16_bits_to_f32(v_bits[:, h]).astype(np.float64)
+        s = q @ k.T * sm_scale
+        if causal:
+            s = np.where(np.arange(L)[None, :] <= np.arange(L)[:, None], s, -np.inf)
+        s = s - s.max(axis=1, keepdims=True)
+        p = np.exp(s)
+        out[:, h] = (p / p.sum(axis=1, keepdims=True)) @ v
+    return out
+
+
+def rel_l2(a: np.ndarray, b: np.ndarray) -> float:
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))

@@ -1,0 +1,96 @@
+"""GPU parity of the sm_100a Sage3 MXFP4 attention (through the C ABI).
+
+Oracle: oracle/attn.py, a numpy restatement of the reference's mxfp4_hw path
+(qk_smoothing + quantize_to_mxfp4 + the flash loop of mxfp4_hw_kernel.py) with
+the kernel's 128-key tile.  Tolerances (floating point): relative L2 error
+vs that oracle <= 2e-2 (the kernel's exp2 is the hardware approximation, so
+a few P codes sit on the other side of a rounding boundary), and the
+quantisation error vs exact float64 attention within 1.1x (+0.01) of the
+oracle's own error vs exact attention, with the reference's 64-key tiling.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attn as oa
+
+pytestmark = pytest.mark.gpu
+
+
+def _qkv(L, H, seed, k_offset=3.0, B=1):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, L, H, 128, generator=g)
+    k = torch.randn(B, L, H, 128, generator=g) + torch.randn(B, 1, H, 128, generator=g) * k_offset
+    v = torch.randn(B, L, H, 128, generator=g)
+    return q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _run(q, k, v, dev, causal=False, config="mxfp4_hw", smoothing=True):
+    from vllm_qdq_plugin.sage3_attn.sage3 import sage3_attention_nhd
+    out = sage3_attention_nhd(q.to(dev), k.to(dev), v.to(dev), config=config, is_causal=causal,
+                              per_block_mean=smoothing)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("L,H", [(128, 1), (256, 2), (300, 2), (1000, 1)])
+def test_mxfp4_attention_matches_oracle(cuda_device, L, H):
+    q, k, v = _qkv(L, H, seed=L + H)
+    sm = 1.0 / math.sqrt(128)
+    got = _run(q, k, v, cuda_device)[0]
+    qb, kb, vb = _bits(q[0]), _bits(k[0]), _bits(v[0])
+    want = oa.attention(qb, kb, vb, sm, block_n=128)
+    err = oa.rel_l2(got, want)
+    assert err < 2e-2, f"rel L2 vs oracle {err}"
+    exact = oa.exact_attention(qb, kb, vb, sm)
+    ref_err = oa.rel_l2(oa.attention(qb, kb, vb, sm, block_n=64, mask_padding=False), exact)
+    our_err = oa.rel_l2(got, exact)
+    assert our_err <= 1.1 * ref_err + 0.01, (our_err, ref_err)
+    from vllm_qdq_plugin import _native
+    assert _native.device_status() == 0
+
+
+def test_causal_and_no_smoothing(cuda_device):
+    q, k, v = _qkv(384, 1, seed=7)
+    sm = 1.0 / math.sqrt(128)
+    qb, kb, vb = _bits(q[0]), _bits(k[0]), _bits(v[0])
+    got = _run(q, k, v, cuda_device, causal=True)[0]
+    assert oa.rel_l2(got, oa.attention(qb, kb, vb, sm, causal=True)) < 2e-2
+    got = _run(q, k, v, cuda_device, smoothing=False)[0]
+    assert oa.rel_l2(got, oa.attention(qb, kb, vb, sm, smoothing=False)) < 2e-2
+
+
+def test_batch_heads_and_hnd_layout(cuda_device):
+    from vllm_qdq_plugin.sage3_attn.sage3 import sageattn3_standalone
+    q, k, v = _qkv(256, 3, seed=11, B=2)
+    nhd = _run(q, k, v, cuda_device)
+    hnd = sageattn3_standalone(q.transpose(1, 2).to(cuda_device), k.transpose(1, 2).to(cuda_device),
+                               v.transpose(1, 2).to(cuda_device), config="mxfp4_hw")
+    assert np.array_equal(hnd.transpose(1, 2).float().cpu().numpy(), nhd)
+    sm = 1.0 / math.sqrt(128)
+    for b in range(2):
+        want = oa.attention(_bits(q[b]), _bits(k[b]), _bits(v[b]), sm)
+        assert oa.rel_l2(nhd[b], want) < 2e-2
+
+
+def test_backend_impl_surface(cuda_device):
+    from vllm_qdq_plugin.sage3_attn.backend import Sage3TritonBackend
+    impl_cls = Sage3TritonBackend.get_impl_cls()
+    impl = impl_cls(num_heads=2, head_size=128, softmax_scale=1 / math.sqrt(128),
+                    backend_kwargs={"sage3_config": "mxfp4_hw"})
+    q, k, v = _qkv(200, 2, seed=5)
+    out = impl.forward_cuda(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device))
+    assert out.shape == q.shape and out.dtype == torch.bfloat16
+    # cross-attention falls back to SDPA
+    kv = _qkv(64, 2, seed=6)
+    out2 = impl.forward_cuda(q.to(cuda_device), kv[1].to(cuda_device), kv[2].to(cuda_device))
+    assert out2.shape == q.shape

@@ -1,0 +1,55 @@
+// C-ABI entry of the Sage3 FP4 attention (pre-pass + flash kernel).
+#include "attn_common.cuh"
+
+using namespace qdqb200;
+
+extern "C" int64_t sage3_attn_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t D) {
+  if (B <= 0 || L <= 0 || H <= 0 || D != 128) return 0;
+  return attn::carve(static_cast<int>(B), static_cast<int>(H), static_cast<int>(L), nullptr, nullptr);
+}
+
+extern "C" int sage3_fp4_attn(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t L,
+                              int64_t H, int64_t D, const int64_t* strides, float sm_scale, int quant_format,
+                              int acc_mode, int causal, int smoothing, int dtype, void* workspace,
+                              int64_t workspace_bytes, void* stream) {
+  if (B < 0 || L < 0 || H < 0) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: negative shape");
+  if (B == 0 || L == 0 || H == 0) return QDQ_OK;
+  if (D != 128) return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: head_dim %lld (this build supports 128)", (long long)D);
+  if (dtype != QDQ_DTYPE_BF16) return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: inputs must be bf16");
+  if (quant_format != 0)
+    return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: quant_format %d not available (0 = MXFP4)", quant_format);
+  if (acc_mode < 0 || acc_mode > 1) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: acc_mode must be 0 or 1");
+  if (!q || !k || !v || !o || !strides) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: null pointer");
+  if (!(sm_scale > 0.f)) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: sm_scale must be positive");
+  if (L > (1 << 24) || B * H > (1 << 20)) return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: problem too large");
+  for (int i = 0; i < 12; ++i)
+    if (strides[i] % 8 != 0) return fail(QDQ_ERR_ALIGNMENT, "sage3_fp4_attn: strides must be multiples of 8 elements");
+  const uintptr_t mis = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o);
+  if (mis & 15) return fail(QDQ_ERR_ALIGNMENT, "sage3_fp4_attn: q/k/v/o must be 16-byte aligned");
+  const int64_t need = sage3_attn_workspace_bytes(B, L, H, D);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: workspace smaller than sage3_attn_workspace_bytes()");
+  attn::Problem p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.o = static_cast<__nv_bfloat16*>(o);
+  p.B = static_cast<int>(B);
+  p.H = static_cast<int>(H);
+  p.L = static_cast<int>(L);
+  p.Lp = static_cast<int>((L + 127) / 128 * 128);
+  p.D = 128;
+  p.q_sb = strides[0]; p.q_sn = strides[1]; p.q_sh = strides[2];
+  p.k_sb = strides[3]; p.k_sn = strides[4]; p.k_sh = strides[5];
+  p.v_sb = strides[6]; p.v_sn = strides[7]; p.v_sh = strides[8];
+  p.o_sb = strides[9]; p.o_sn = strides[10]; p.o_sh = strides[11];
+  p.sm_scale = sm_scale;
+  p.causal = causal ? 1 : 0;
+  p.smoothing = smoothing ? 1 : 0;
+  attn::Workspace w;
+  attn::carve(p.B, p.H, p.L, static_cast<uint8_t*>(workspace), &w);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (int st = attn::launch_prepass(p, w, s)) return st;
+  return attn::launch_flash(p, w, s);
+}

@@ -1,0 +1,79 @@
+// Shared declarations of the Sage3 FP4 attention (pre-pass + flash kernel).
+#pragma once
+
+#include "sm100.cuh"
+
+namespace qdqb200 {
+namespace attn {
+
+// One attention problem: Q, K, V, O in the NHD layout [B, L, H, D] (D = 128,
+// element stride 1) with arbitrary batch / token / head strides (elements).
+struct Problem {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  __nv_bfloat16* o;
+  int B, H, L, Lp, D;
+  int64_t q_sb, q_sn, q_sh;
+  int64_t k_sb, k_sn, k_sh;
+  int64_t v_sb, v_sn, v_sh;
+  int64_t o_sb, o_sn, o_sh;
+  float sm_scale;
+  int causal;
+  int smoothing;  // per-128-token Q mean / K mean smoothing with the delta_s correction
+};
+
+// Device buffers of the pre-pass (carved out of the caller's workspace).
+struct Workspace {
+  float* ksum;            // [BH, 128]
+  __nv_bfloat16* qmean;   // [BH, G, 128]
+  uint8_t* qc;            // [BH * Lp, 64]
+  uint8_t* qsf;           // [BH * Lp / 128, 512]
+  uint8_t* kc;            // [BH * Lp, 64]
+  uint8_t* ksf;           // [BH * Lp / 128, 512]
+  uint8_t* vt;            // [BH * 128, Lp / 2]
+  uint8_t* vsf;           // [BH * Lp / 128, 512]
+  __nv_bfloat16* ds;      // [BH, G, Lp]
+};
+
+inline int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
+
+// Carve the workspace; returns total bytes needed (ws may be null to query).
+inline int64_t carve(int B, int H, int L, uint8_t* base, Workspace* w) {
+  const int64_t BH = static_cast<int64_t>(B) * H;
+  const int64_t Lp = (static_cast<int64_t>(L) + 127) / 128 * 128;
+  const int64_t G = Lp / 128;
+  int64_t off = 0;
+  auto take = [&](int64_t bytes) {
+    uint8_t* p = base ? base + off : nullptr;
+    off += align256(bytes);
+    return p;
+  };
+  uint8_t* ksum = take(BH * 128 * 4);
+  uint8_t* qmean = take(BH * G * 128 * 2);
+  uint8_t* qc = take(BH * Lp * 64);
+  uint8_t* qsf = take(BH * G * 512);
+  uint8_t* kc = take(BH * Lp * 64);
+  uint8_t* ksf = take(BH * G * 512);
+  uint8_t* vt = take(BH * 128 * Lp / 2);
+  uint8_t* vsf = take(BH * G * 512);
+  uint8_t* ds = take(BH * G * Lp * 2);
+  if (w) {
+    w->ksum = reinterpret_cast<float*>(ksum);
+    w->qmean = reinterpret_cast<__nv_bfloat16*>(qmean);
+    w->qc = qc;
+    w->qsf = qsf;
+    w->kc = kc;
+    w->ksf = ksf;
+    w->vt = vt;
+    w->vsf = vsf;
+    w->ds = reinterpret_cast<__nv_bfloat16*>(ds);
+  }
+  return off;
+}
+
+int launch_prepass(const Problem& p, const Workspace& w, cudaStream_t s);
+int launch_flash(const Problem& p, const Workspace& w, cudaStream_t s);
+
+}  // namespace attn
+}  // namespace qdqb200

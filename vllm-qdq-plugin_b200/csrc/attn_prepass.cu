@@ -1,0 +1,328 @@
+// Pre-pass of the Sage3 FP4 attention: QK smoothing + FP4 quantisation of
+// Q, K and V, and the delta_s correction, for inputs in the NHD layout
+// vllm-omni hands the backend ([B, L, H, D], reference
+// sage3_attn/impl.py:102-104 transposes these to HND; here the kernels read
+// NHD strides directly).
+//
+// Reference semantics (mxfp4_hw branch, sage3/api.py:161-206):
+//   qk_smoothing (sage3/transforms.py:47-95), applied before padding:
+//     k_c  = k - mean_L(k)                      (bf16 ops)
+//     q_m  = mean over each 128-row group of q, the last group zero-padded
+//     q_s  = q - q_m[group]
+//     delta_s[g, n] = (q_m[g] . k_c[n]) rounded to bf16 (bf16 matmul)
+//   quantize_to_mxfp4 (sage3/mxfp4_hw_kernel.py:73-116) of q_s and k_c along
+//   D and of V along the sequence, per 32-group:
+//     e = clamp(ceil(log2(max(amax, 6*2^-126) / 6)), -127, 127), byte e+127
+//     code of x / 2^e with round-half-away thresholds
+//   (ceil(log2(.)) is evaluated exactly from the float's bits).
+//
+// Outputs (workspace), with Lp = L rounded up to 128, BH = B*H, G = Lp/128:
+//   ksum   fp32 [BH, D]           per-channel sums of k (mean = bf16(ksum / L))
+//   qmean  bf16 [BH, G, D]        Q group means
+//   qc, kc uint8 [BH*Lp, D/2]     E2M1 codes (element 2j low nibble)
+//   qsf, ksf                      E8M0, one 512-byte tcgen05 scale chunk per 128 rows
+//   vt     uint8 [BH*D, Lp/2]     V transposed: row (bh, d), keys packed along the row
+//   vsf                           E8M0, chunk (bh, key tile) = 128 d-rows x 4 key groups
+//   ds     bf16 [BH, G, Lp]       delta_s
+#include "attn_common.cuh"
+
+namespace qdqb200 {
+namespace attn {
+namespace {
+
+// ---------------------------------------------------------------- helpers
+__device__ __forceinline__ float bf16_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// Exact ceil(log2(r)) for r > 0 (r finite).
+__device__ __forceinline__ int ceil_log2(float r) {
+  const uint32_t b = __float_as_uint(r);
+  const int ef = static_cast<int>((b >> 23) & 0xFF);
+  const uint32_t man = b & 0x7FFFFFu;
+  if (ef == 0) {  // subnormal: r = man * 2^-149
+    const int msb = 31 - __clz(man);
+    return (man == (1u << msb)) ? msb - 149 : msb - 148;
+  }
+  return (ef - 127) + (man != 0 ? 1 : 0);
+}
+
+// E8M0 exponent e for a group whose |x| max is amax (mxfp4_hw_kernel.py:96-100).
+__device__ __forceinline__ int mx_group_exp(float amax) {
+  const float amax_safe = fmaxf(amax, 6.0f * 1.1754943508222875e-38f);  // 6 * 2^-126
+  int e = ceil_log2(__fdiv_rn(amax_safe, 6.0f));
+  return min(max(e, -127), 127);
+}
+
+// E2M1 code of v = x / 2^e with the reference's round-half-away thresholds
+// (mxfp4_hw_kernel.py:43-61): |v| clamped to 6.
+__device__ __forceinline__ uint32_t e2m1_rna(float v) {
+  const float a = fminf(fabsf(v), 6.0f);
+  uint32_t c = (a >= 0.25f) + (a >= 0.75f) + (a >= 1.25f) + (a >= 1.75f) + (a >= 2.5f) +
+               (a >= 3.5f) + (a >= 5.0f);
+  return c | (v < 0.0f ? 8u : 0u);
+}
+
+// 2^-e as an exact float (e in [-127, 127]; 2^127 for e = -127).
+__device__ __forceinline__ float exp2_neg(int e) {
+  const int be = 127 - e;  // biased exponent of 2^-e
+  return be >= 1 ? __uint_as_float(static_cast<uint32_t>(be) << 23)
+                 : __uint_as_float(1u << (22 + be));
+}
+
+// Quantise 32 floats (one MX group): 16 code bytes into out[0..15], returns the E8M0 byte.
+__device__ __forceinline__ uint32_t mx_quant32(const float* v, uint8_t* out) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const int e = mx_group_exp(amax);
+  const float inv = exp2_neg(e);
+  uint32_t w[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) word |= e2m1_rna(v[q * 8 + i] * inv) << (4 * i);
+    w[q] = word;
+  }
+  *reinterpret_cast<uint4*>(out) = make_uint4(w[0], w[1], w[2], w[3]);
+  return static_cast<uint32_t>(e + 127);
+}
+
+__device__ __forceinline__ int64_t nhd_row(int b, int n, int h, int64_t sb, int64_t sn, int64_t sh) {
+  return b * sb + n * sn + h * sh;
+}
+
+// ---------------------------------------------------------------- K channel sums
+// grid (BH, ceil(L / 1024)), 128 threads: thread d sums k[b, n, h, d] over a chunk of keys.
+__global__ void __launch_bounds__(128) ksum_kernel(const __nv_bfloat16* __restrict__ k, int H, int L,
+                                                   int64_t sb, int64_t sn, int64_t sh,
+                                                   float* __restrict__ ksum) {
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int d = threadIdx.x;
+  const int n0 = blockIdx.y * 1024, n1 = min(L, n0 + 1024);
+  float acc = 0.f;
+  for (int n = n0; n < n1; ++n) acc += __bfloat162float(k[nhd_row(b, n, h, sb, sn, sh) + d]);
+  atomicAdd(&ksum[bh * 128 + d], acc);
+}
+
+// ---------------------------------------------------------------- Q / K quantisation
+// grid (BH, Lp/128), 256 threads.  Loads one 128-row x 128-d tile, subtracts
+// the mean (Q: the tile's own group mean, written to qmean; K: ksum / L),
+// rounds to bf16 and quantises each row along D into 4 MX groups.
+template <bool kIsQ>
+__global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __restrict__ x, int H, int L, int Lp,
+                                                       int64_t sb, int64_t sn, int64_t sh,
+                                                       const float* __restrict__ ksum, __nv_bfloat16* __restrict__ qmean,
+                                                       uint8_t* __restrict__ codes, uint8_t* __restrict__ sf,
+                                                       int smoothing) {
+  __shared__ __align__(16) __nv_bfloat16 tile[128][136];
+  __shared__ float mean[128];
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int t0 = blockIdx.y * 128;
+  for (int i = threadIdx.x; i < 128 * 16; i += 256) {  // 16-byte chunks: row i/16, chunk i%16
+    const int r = i >> 4, c = i & 15;
+    const int n = t0 + r;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (n < L) u = *reinterpret_cast<const uint4*>(x + nhd_row(b, n, h, sb, sn, sh) + c * 8);
+    *reinterpret_cast<uint4*>(&tile[r][c * 8]) = u;
+  }
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const int d = threadIdx.x;
+    float m = 0.f;
+    if (smoothing) {
+      if (kIsQ) {
+        // torch mean over the zero-padded 128-row group (transforms.py:72-80)
+        float s = 0.f;
+        for (int r = 0; r < 128; ++r) s += __bfloat162float(tile[r][d]);
+        m = bf16_round(s / 128.0f);
+        qmean[(static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 128 + d] = __float2bfloat16_rn(m);
+      } else {
+        m = bf16_round(ksum[bh * 128 + d] / static_cast<float>(L));
+      }
+    }
+    mean[d] = m;
+  }
+  __syncthreads();
+  // 512 (row, group) items, 2 per thread
+  for (int it = threadIdx.x; it < 512; it += 256) {
+    const int r = it >> 2, g = it & 3;
+    const int n = t0 + r;
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int d = g * 32 + i;
+      v[i] = (n < L) ? bf16_round(__bfloat162float(tile[r][d]) - mean[d]) : 0.f;  // padding after smoothing
+    }
+    uint8_t* crow = codes + (static_cast<int64_t>(bh) * Lp + n) * 64 + g * 16;
+    const uint32_t e = mx_quant32(v, crow);
+    sf[(static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 512 + (r % 32) * 16 + (r / 32) * 4 + g] =
+        static_cast<uint8_t>(e);
+  }
+}
+
+// ---------------------------------------------------------------- V quantisation
+// grid (BH, Lp/128), 128 threads: thread d quantises V[:, d] over the tile's
+// 128 keys in 4 groups of 32 and writes 64 code bytes of row (bh, d) of V^T.
+__global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __restrict__ v, int H, int L, int Lp,
+                                                      int64_t sb, int64_t sn, int64_t sh,
+                                                      uint8_t* __restrict__ vt, uint8_t* __restrict__ vsf) {
+  __shared__ __nv_bfloat16 tile[128][128 + 8];
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int t0 = blockIdx.y * 128;
+  for (int i = threadIdx.x; i < 128 * 16; i += 128) {
+    const int r = i >> 4, c = i & 15;
+    const int n = t0 + r;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (n < L) u = *reinterpret_cast<const uint4*>(v + nhd_row(b, n, h, sb, sn, sh) + c * 8);
+    *reinterpret_cast<uint4*>(&tile[r][c * 8]) = u;
+  }
+  __syncthreads();
+  const int d = threadIdx.x;
+  uint32_t sfw = 0;
+  uint8_t* row = vt + (static_cast<int64_t>(bh) * 128 + d) * (Lp / 2) + blockIdx.y * 64;
+#pragma unroll 1
+  for (int g = 0; g < 4; ++g) {
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(tile[g * 32 + i][d]);
+    sfw |= mx_quant32(x, row + g * 16) << (8 * g);
+  }
+  *reinterpret_cast<uint32_t*>(vsf + (static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 512 +
+                               (d % 32) * 16 + (d / 32) * 4) = sfw;
+}
+
+// ---------------------------------------------------------------- delta_s
+// ds[bh, g, n] = bf16( sum_d qmean[bh, g, d] * kc[bh, n, d] ), kc = bf16(k - mean),
+// with bf16 tensor-core MMAs (mma.sync m16n8k16, fp32 accumulation).
+// grid (BH, Lp/128), 256 threads (8 warps).  The CTA keeps its 128 keys'
+// kc (bf16) in shared memory and walks the G groups 64 at a time; each warp
+// owns a 32 (g) x 32 (n) block of the 64 x 128 output chunk.
+constexpr int DS_LD = 136;  // padded row length (bf16) -> conflict-free ldmatrix
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(sm100::smem_u32(p)));
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(256) ds_kernel(const __nv_bfloat16* __restrict__ k, int H, int L, int Lp,
+                                                 int64_t sb, int64_t sn, int64_t sh,
+                                                 const float* __restrict__ ksum,
+                                                 const __nv_bfloat16* __restrict__ qmean,
+                                                 __nv_bfloat16* __restrict__ ds) {
+  extern __shared__ __align__(16) uint8_t ds_smem[];
+  __nv_bfloat16* kcs = reinterpret_cast<__nv_bfloat16*>(ds_smem);          // [128][DS_LD]
+  __nv_bfloat16* qms = kcs + 128 * DS_LD;                                    // [64][DS_LD]
+  __shared__ float kmean[128];
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int n0 = blockIdx.y * 128;
+  const int G = Lp / 128;
+  if (threadIdx.x < 128) kmean[threadIdx.x] = bf16_round(ksum[bh * 128 + threadIdx.x] / static_cast<float>(L));
+  __syncthreads();
+  for (int i = threadIdx.x; i < 128 * 16; i += 256) {
+    const int r = i >> 4, c = i & 15;
+    const int n = n0 + r;
+    uint32_t w[4] = {0, 0, 0, 0};
+    if (n < L) {
+      const uint4 u = *reinterpret_cast<const uint4*>(k + nhd_row(b, n, h, sb, sn, sh) + c * 8);
+      const uint32_t raw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        w[j] = pack_bf16x2(bf16lo(raw[j]) - kmean[c * 8 + 2 * j], bf16hi(raw[j]) - kmean[c * 8 + 2 * j + 1]);
+    }
+    *reinterpret_cast<uint4*>(kcs + r * DS_LD + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wm = warp >> 2;        // 0..1: g rows [32 wm, 32 wm + 32)
+  const int wn = warp & 3;         // 0..3: keys [32 wn, 32 wn + 32)
+  for (int g0 = 0; g0 < G; g0 += 64) {
+    __syncthreads();  // previous chunk's qms reads are done (and kcs is ready on the first pass)
+    for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+      const int r = i >> 4, c = i & 15;
+      uint4 u = make_uint4(0, 0, 0, 0);
+      if (g0 + r < G) u = *reinterpret_cast<const uint4*>(qmean + (static_cast<int64_t>(bh) * G + g0 + r) * 128 + c * 8);
+      *reinterpret_cast<uint4*>(qms + r * DS_LD + c * 8) = u;
+    }
+    __syncthreads();
+    float acc[2][4][4] = {};
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {  // 8 x 16 = 128 = D
+      uint32_t a[2][4];
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi) {
+        const int row = wm * 32 + mi * 16 + (lane & 15);
+        const int col = kk * 16 + (lane >> 4) * 8;
+        ldsm_x4(a[mi], qms + row * DS_LD + col);
+      }
+#pragma unroll
+      for (int nj = 0; nj < 2; ++nj) {  // two pairs of n8 tiles
+        uint32_t bb[4];
+        // matrices: (n 0-7, k 0-7), (n 0-7, k 8-15), (n 8-15, k 0-7), (n 8-15, k 8-15)
+        const int nrow = wn * 32 + nj * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int col = kk * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(bb, kcs + nrow * DS_LD + col);
+#pragma unroll
+        for (int mi = 0; mi < 2; ++mi) {
+          mma_bf16_16816(acc[mi][nj * 2 + 0], a[mi], bb[0], bb[1]);
+          mma_bf16_16816(acc[mi][nj * 2 + 1], a[mi], bb[2], bb[3]);
+        }
+      }
+    }
+    // store: c fragment rows (lane/4) and (lane/4 + 8), cols 2*(lane%4) + {0,1}
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int g = g0 + wm * 32 + mi * 16 + (lane >> 2) + hh * 8;
+          const int n = n0 + wn * 32 + ni * 8 + (lane & 3) * 2;
+          if (g < G) {
+            const uint32_t pk = pack_bf16x2(acc[mi][ni][hh * 2], acc[mi][ni][hh * 2 + 1]);
+            *reinterpret_cast<uint32_t*>(ds + (static_cast<int64_t>(bh) * G + g) * Lp + n) = pk;
+          }
+        }
+  }
+}
+
+}  // namespace
+
+int launch_prepass(const Problem& p, const Workspace& w, cudaStream_t s) {
+  const int BH = p.B * p.H;
+  const int T = p.Lp / 128;
+  if (cudaMemsetAsync(w.ksum, 0, sizeof(float) * BH * 128, s) != cudaSuccess)
+    return fail(QDQ_ERR_CUDA, "sage3 prepass: memset failed");
+  if (p.smoothing) {
+    ksum_kernel<<<dim3(BH, (p.L + 1023) / 1024), 128, 0, s>>>(p.k, p.H, p.L, p.k_sb, p.k_sn, p.k_sh, w.ksum);
+  }
+  qk_quant_kernel<true><<<dim3(BH, T), 256, 0, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh, w.ksum, w.qmean,
+                                                  w.qc, w.qsf, p.smoothing);
+  qk_quant_kernel<false><<<dim3(BH, T), 256, 0, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh, w.ksum, w.qmean,
+                                                   w.kc, w.ksf, p.smoothing);
+  v_quant_kernel<<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf);
+  if (p.smoothing) {
+    const int smem = (128 + 64) * DS_LD * 2;
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr[dev]) {
+      if (cudaFuncSetAttribute(ds_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return fail(QDQ_ERR_CUDA, "sage3 prepass: smem attribute");
+      attr[dev] = true;
+    }
+    ds_kernel<<<dim3(BH, T), 256, smem, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh, w.ksum, w.qmean, w.ds);
+  }
+  return check_launch("sage3 prepass");
+}
+
+}  // namespace attn
+}  // namespace qdqb200

@@ -261,7 +261,7 @@ static PFN_encodeTiled encode_fn() {
 }
 
 int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes, uint64_t ld_bytes,
-                    uint32_t box_bytes, uint32_t box_rows, bool swizzle128) {
+                    uint32_t box_bytes, uint32_t box_rows, int swizzle_bytes) {
   PFN_encodeTiled fn = encode_fn();
   if (fn == nullptr) return fail(QDQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld_bytes & 15))
@@ -272,7 +272,9 @@ int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
   const cuuint32_t elem[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
                   CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                  : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                        : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(QDQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return QDQ_OK;
@@ -328,8 +330,8 @@ extern "C" int fp4_gemm_mxf4(const void* a_codes, const void* a_sf_tiled, const 
   int* status = device_status_ptr();
   if (status == nullptr) return QDQ_ERR_CUDA;
   CUtensorMap ta, tb;
-  if (int st = make_tmap_u8_2d(&ta, a_codes, M, K / 2, lda_bytes, BKB, BM, true)) return st;
-  if (int st = make_tmap_u8_2d(&tb, w_codes, N, K / 2, ldw_bytes, BKB, BN, true)) return st;
+  if (int st = make_tmap_u8_2d(&ta, a_codes, M, K / 2, lda_bytes, BKB, BM, 128)) return st;
+  if (int st = make_tmap_u8_2d(&tb, w_codes, N, K / 2, ldw_bytes, BKB, BN, 128)) return st;
   static bool attr_set[2][64] = {{false}};
   int dev = 0;
   cudaGetDevice(&dev);

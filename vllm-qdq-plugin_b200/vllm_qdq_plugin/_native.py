@@ -39,6 +39,10 @@ _SIGNATURES: dict[str, list] = {
     "qdq_abi_version": [],
     "qdq_device_status": [ctypes.POINTER(ctypes.c_int), _int],
     "qdq_selftest_bounded_wait": [_i64, _c_void_p],
+    "sage3_attn_workspace_bytes": [_i64, _i64, _i64, _i64],
+    "sage3_fp4_attn": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64,
+                       ctypes.POINTER(ctypes.c_int64), _f32, _int, _int, _int, _int, _int, _c_void_p,
+                       _i64, _c_void_p],
     "qdq_sf_tiled_bytes": [_i64, _i64],
     "qdq_sf_tile": [_c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p],
     "fp4_gemm_mxf4": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64,
@@ -52,7 +56,8 @@ _SIGNATURES: dict[str, list] = {
 }
 _RESTYPES = {"qdq_last_error": ctypes.c_char_p, "qdq_sf_tiled_bytes": ctypes.c_int64,
              "fp4_linear_workspace_bytes": ctypes.c_int64,
-             "fp4_linear_noalloc_scratch_bytes": ctypes.c_int64}
+             "fp4_linear_noalloc_scratch_bytes": ctypes.c_int64,
+             "sage3_attn_workspace_bytes": ctypes.c_int64}
 
 
 def lib() -> ctypes.CDLL:

@@ -1,0 +1,213 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Entry points of the sm_100a Sage3 FP4 attention.
+
+Mirrors the reference's sage3/api.py surface:
+  sageattn3_standalone(q, k, v, config, is_causal, sm_scale, per_block_mean, ...)
+  sageattn3_torch_triton_standalone(..., tensor_layout="HND", quant_format, acc_dtype)
+  scaled_dot_product_attention(query, key, value, attn_mask, dropout_p, is_causal, scale)
+  ACC_DTYPE_MAP, ATTENTION_CONFIGS
+(reference: src/vllm_qdq_plugin/sage3_attn/sage3/api.py:25-35, :394-576).
+
+Every in-scope config runs one kernel pair in libqdq_b200.so
+(`sage3_fp4_attn`, include/qdq_b200.h):
+  - a pre-pass: K channel mean, per-128-token Q means, delta_s, and FP4 codes
+    plus block scales of Q/K (along D) and V (along the sequence);
+  - a tcgen05 flash kernel: QK^T and PV on the FP4 tensor cores, with P
+    quantised in-kernel.
+Config mapping:
+  "mxfp4_hw"  MXFP4 with the reference hardware kernel's semantics
+              (sage3/mxfp4_hw_kernel.py): E8M0 per 32, l = sum of unquantised P.
+  "mxfp4"     the reference's emulated MXFP4 config (attention_kernel.py +
+              p_quant_mxfp4) runs on the same real-MXFP4 kernel; its 9-level
+              emulation grid has no hardware equivalent, so parity with it is
+              by tolerance.
+  "nvfp4"     NVFP4 (E4M3 per 16).
+The kernels read the NHD or HND strides they are given; no transposing copies.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import warnings
+from typing import Optional, Union
+
+import torch
+
+from ... import _native
+
+ACC_DTYPE_MAP = {
+    # name: (qk dot, pv dot, softmax) accumulator dtypes of the reference
+    "fp32": ("fp32", "fp32", "fp32"),
+    "fp16_pv_only": ("fp32", "fp16", "fp32"),
+    "bf16_pv_only": ("fp32", "bf16", "fp32"),
+    "fp16_qk_only": ("fp16", "fp32", "fp32"),
+    "bf16_qk_only": ("bf16", "fp32", "fp32"),
+    "fp16_both_dot": ("fp16", "fp16", "fp32"),
+    "bf16_both_dot": ("bf16", "bf16", "fp32"),
+    "fp16_full": ("fp16", "fp16", "fp16"),
+    "bf16_full": ("bf16", "bf16", "bf16"),
+}
+
+# config name -> kernel quant format (0 = MXFP4, 1 = NVFP4)
+ATTENTION_CONFIGS: dict[str, int] = {"mxfp4": 0, "mxfp4_hw": 0, "nvfp4": 1}
+
+# Names the reference registers that lie outside this build's FP4 path.
+_OTHER_REFERENCE_CONFIGS = ("mxfp4_s1", "mxfp8_s1", "nvfp4_vsmooth", "mxfp4_vsmooth", "mxfp8_hw",
+                            "mixed_mxfp8qk_mxfp4pv_hw", "mixed_mxfp4qk_mxfp8pv_hw", "int8", "fp8")
+
+_BUILT_FORMATS = (0,)  # formats with a kernel in this build
+
+
+def _get_env_bool(name: str, default: str = "0") -> bool:
+    return os.getenv(name, default).lower() in ("1", "true")
+
+
+def _resolve_config(config: str) -> int:
+    if config not in ATTENTION_CONFIGS:
+        if config in _OTHER_REFERENCE_CONFIGS:
+            raise NotImplementedError(
+                f"sage3 config '{config}' is not part of this build's FP4 attention "
+                f"(available: {list(ATTENTION_CONFIGS)})")
+        raise ValueError(f"Unknown config '{config}'. Available: {list(ATTENTION_CONFIGS.keys())}")
+    fmt = ATTENTION_CONFIGS[config]
+    if fmt not in _BUILT_FORMATS:
+        raise NotImplementedError(f"sage3 config '{config}' has no sm_100a kernel in this build yet")
+    return fmt
+
+
+@torch.library.custom_op("qdq_b200::sage3_attn", mutates_args=())
+def _sage3_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layout_nhd: bool, sm_scale: float,
+              quant_format: int, acc_mode: int, causal: bool, smoothing: bool) -> torch.Tensor:
+    _native.require_cuda(q, k, v)
+    out = torch.empty_like(q)
+    if layout_nhd:  # [B, L, H, D]
+        b_, l_, h_, d_ = q.shape
+        dims = (0, 1, 2)
+    else:           # [B, H, L, D]
+        b_, h_, l_, d_ = q.shape
+        dims = (0, 2, 1)
+    strides = []
+    for t in (q, k, v, out):
+        strides += [t.stride(dims[0]), t.stride(dims[1]), t.stride(dims[2])]
+    lib = _native.lib()
+    ws = torch.empty((lib.sage3_attn_workspace_bytes(b_, l_, h_, d_),), dtype=torch.uint8,
+                     device=q.device)
+    import ctypes
+    arr = (ctypes.c_int64 * 12)(*strides)
+    _native.call("sage3_fp4_attn", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b_, l_,
+                 h_, d_, arr, float(sm_scale), quant_format, acc_mode, int(causal), int(smoothing), 0,
+                 ws.data_ptr(), ws.numel(), _native.stream_ptr(q.device))
+    return out
+
+
+@_sage3_op.register_fake
+def _(q, k, v, layout_nhd, sm_scale, quant_format, acc_mode, causal, smoothing):
+    return torch.empty_like(q)
+
+
+def _check_inputs(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_dim: int) -> None:
+    if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError(f"q/k/v must share one 4-D shape, got {tuple(q.shape)}, "
+                         f"{tuple(k.shape)}, {tuple(v.shape)}")
+    if q.dtype != torch.bfloat16 or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise NotImplementedError(f"this build's FP4 attention takes bf16 inputs (got {q.dtype})")
+    if q.shape[-1] != 128:
+        raise NotImplementedError(f"this build's FP4 attention supports head_dim 128 (got {q.shape[-1]})")
+
+
+def sage3_attention_nhd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, config: str = "mxfp4",
+                        is_causal: bool = False, sm_scale: Optional[float] = None,
+                        per_block_mean: bool = True, acc_dtype: str = "fp32") -> torch.Tensor:
+    """Attention on NHD tensors [B, L, H, D] (the vllm-omni layout), output NHD."""
+    fmt = _resolve_config(config)
+    if acc_dtype not in ACC_DTYPE_MAP:
+        raise ValueError(f"Unknown acc_dtype '{acc_dtype}'. Available: {list(ACC_DTYPE_MAP.keys())}")
+    _check_inputs(q, k, v, 1)
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(q.shape[-1])
+    smoothing = per_block_mean and not _get_env_bool("SAGE3_DISABLE_PER_BLOCK_MEAN")
+    acc_mode = 0 if acc_dtype == "fp32" else 1
+    return torch.ops.qdq_b200.sage3_attn(q, k, v, True, float(sm_scale), fmt, acc_mode,
+                                         bool(is_causal), bool(smoothing))
+
+
+@torch.inference_mode()
+def sageattn3_standalone(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    config: Union[str, object] = "mxfp4",
+    is_causal: bool = False,
+    sm_scale: Optional[float] = None,
+    per_block_mean: bool = True,
+    tile_size_q: int = 128,
+    tile_size_k: int = 128,
+    return_lse: bool = False,
+    debug: bool = False,
+    acc_dtype: str = "fp32",
+) -> torch.Tensor:
+    """SageAttention3 FP4 attention on HND tensors [B, H, N, D] -> [B, H, N, D].
+
+    acc_dtype: every mode is accepted; the PV accumulator is fp32 in tensor
+    memory for all of them (at least as accurate as the reduced-precision
+    accumulators the reference's modes emulate).
+    """
+    name = config if isinstance(config, str) else getattr(config, "name", str(config))
+    fmt = _resolve_config(name)
+    if acc_dtype not in ACC_DTYPE_MAP:
+        raise ValueError(f"Unknown acc_dtype '{acc_dtype}'. Available: {list(ACC_DTYPE_MAP.keys())}")
+    if return_lse:
+        raise NotImplementedError("return_lse is not yet supported by the sage3 composable implementation")
+    _check_inputs(q, k, v, 2)
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(q.shape[-1])
+    smoothing = per_block_mean and not _get_env_bool("SAGE3_DISABLE_PER_BLOCK_MEAN")
+    acc_mode = 0 if acc_dtype == "fp32" else 1
+    return torch.ops.qdq_b200.sage3_attn(q, k, v, False, float(sm_scale), fmt, acc_mode,
+                                         bool(is_causal), bool(smoothing))
+
+
+@torch.inference_mode()
+def sageattn3_torch_triton_standalone(q, k, v, tensor_layout: str = "HND", is_causal: bool = False,
+                                      sm_scale: Optional[float] = None, per_block_mean: bool = True,
+                                      tile_size_q: int = 128, tile_size_k: int = 128,
+                                      return_lse: bool = False, debug: bool = False,
+                                      quant_format: str = "mxfp4", acc_dtype: str = "fp32"):
+    """Backward-compatible entry point (HND only, like the reference)."""
+    if tensor_layout != "HND":
+        raise ValueError("Only HND tensor layout is supported")
+    return sageattn3_standalone(q, k, v, config=quant_format, is_causal=is_causal, sm_scale=sm_scale,
+                                per_block_mean=per_block_mean, return_lse=return_lse,
+                                acc_dtype=acc_dtype)
+
+
+def scaled_dot_product_attention(query, key, value, attn_mask=None, dropout_p: float = 0.0,
+                                 is_causal: bool = False, scale: Optional[float] = None, **kwargs):
+    """SDPA-compatible wrapper (HND).  Same limits as the reference: no dropout,
+    no masks, identical Q/K/V shapes.  The default format comes from
+    SAGE3_QUANT_FORMAT (default 'nvfp4', as the reference's wrapper)."""
+    if not query.is_cuda:
+        raise RuntimeError("SageAttention3 requires CUDA tensors")
+    if dropout_p > 0.0:
+        warnings.warn(f"SageAttention3 doesn't support dropout_p={dropout_p}, ignoring",
+                      UserWarning, stacklevel=2)
+    if attn_mask is not None:
+        warnings.warn("SageAttention3 doesn't support arbitrary attention masks, ignoring",
+                      UserWarning, stacklevel=2)
+    B, H, N, D = query.shape
+    if key.shape != (B, H, N, D):
+        raise ValueError(f"Key shape {key.shape} doesn't match query {query.shape}. "
+                         "SageAttention3 requires identical Q/K/V shapes (no cross-attention or KV caching).")
+    if value.shape != (B, H, N, D):
+        raise ValueError(f"Value shape {value.shape} doesn't match query {query.shape}. "
+                         "SageAttention3 requires identical Q/K/V shapes (no cross-attention or KV caching).")
+    quant_format = kwargs.pop("quant_format", os.getenv("SAGE3_QUANT_FORMAT", "nvfp4").lower())
+    acc_dtype = kwargs.pop("acc_dtype", os.getenv("SAGE3_ACC_DTYPE", "fp32").lower())
+    out = sageattn3_torch_triton_standalone(query, key, value, tensor_layout="HND",
+                                            is_causal=is_causal, sm_scale=scale,
+                                            per_block_mean=not _get_env_bool("SAGE3_DISABLE_PER_BLOCK_MEAN"),
+                                            quant_format=quant_format, acc_dtype=acc_dtype)
+    if _get_env_bool("SAGE3_DEBUG") and (torch.isnan(out).any() or torch.isinf(out).any()):
+        raise RuntimeError("SageAttention3 produced NaN/Inf outputs")
+    return out
