@@ -11,15 +11,16 @@
 // Keys beyond L are masked (the reference attends to its zero padding; see
 // DESIGN.md for the size of that difference).
 //
-// CTA (6 warps):
+// CTA (10 warps):
 //   warp 0        TMA producer: K tile [128 keys x 64 B], V^T tile [128 d x 64 B]
 //                 (64-byte swizzle), their E8M0 chunks and the delta_s row slice
 //                 into a 4-stage ring; the Q tile once
 //   warp 1        MMA issuer: S[j%2] = Q K_j^T (tcgen05.mma kind::mxf4, 2 x K=64),
 //                 then O += P_{j-1} V_{j-1}; scale factors via tcgen05.cp
-//   warps 2-5     softmax, one thread per query row (TMEM lane): S -> registers,
-//                 + delta_s, row max, O rescale in TMEM when the max grows,
-//                 exp2, row sum, P -> E2M1 codes + E8M0 scales in shared memory;
+//   warps 2-9     softmax, two threads per query row (TMEM lane), 64 keys each:
+//                 S -> registers, + delta_s, row max (partner exchange through
+//                 shared memory), O rescale in TMEM when the max grows, exp2, row
+//                 sum, P -> E2M1 codes + E8M0 scales in shared memory;
 //                 epilogue O / l -> bf16 NHD
 // TMEM: S0 [0,128) S1 [128,256) O [256,384) scale factors [384,400).
 #include "attn_common.cuh"
@@ -44,8 +45,9 @@ static_assert(ST_DS + DS_BYTES <= STAGE_BYTES, "stage layout");
 constexpr int OFF_Q = 0, OFF_P = CODE_TILE, OFF_STAGE = 2 * CODE_TILE;
 constexpr int OFF_QSF = OFF_STAGE + STAGES * STAGE_BYTES;
 constexpr int OFF_PSF = OFF_QSF + SF_CHUNK;
-constexpr int OFF_BAR = OFF_PSF + SF_CHUNK;
-constexpr int THREADS = 192;
+constexpr int OFF_RED = OFF_PSF + SF_CHUNK;              // [3][2][128] floats: row max / row sum exchange
+constexpr int OFF_BAR = OFF_RED + 3 * 2 * 128 * 4;
+constexpr int THREADS = 320;                             // producer, MMA, 8 softmax warps
 constexpr int TMEM_COLS = 512;
 constexpr uint32_t T_S0 = 0, T_O = 256, T_SFQ = 384, T_SFK = 388, T_SFP = 392, T_SFV = 396;
 constexpr uint32_t IDESC = idesc_mxf4(BM, BN, true);  // also N = HD for PV
@@ -73,18 +75,6 @@ struct Params {
   int smoothing;
 };
 
-__device__ __forceinline__ int ceil_log2_pos(float r) {
-  const uint32_t b = __float_as_uint(r);
-  const int ef = static_cast<int>(b >> 23);  // r >= 0
-  const uint32_t man = b & 0x7FFFFFu;
-  if (ef == 0) {
-    if (man == 0) return -127;  // log2(0) = -inf -> clamped
-    const int msb = 31 - __clz(man);
-    return (man == (1u << msb)) ? msb - 149 : msb - 148;
-  }
-  return (ef - 127) + (man != 0 ? 1 : 0);
-}
-
 __global__ void __launch_bounds__(THREADS, 1)
 sage3_mxfp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                          const __grid_constant__ CUtensorMap map_v, const uint8_t* __restrict__ qsf,
@@ -109,9 +99,9 @@ sage3_mxfp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->s_free[i], 128);
+      mbar_init(&bars->s_free[i], 256);
     }
-    mbar_init(&bars->p_full, 128);
+    mbar_init(&bars->p_full, 256);
     mbar_init(&bars->o_done, 1);
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
@@ -213,99 +203,136 @@ sage3_mxfp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
     }
   } else {
     // ------------------------------------------------------------ softmax / epilogue
-    const int quad = warp & 3;                 // TMEM lane quadrant this warp may access
+    // 8 warps: two threads per query row, each owning 64 of the tile's 128 keys
+    // (and 64 of O's 128 columns).  Warp w reads TMEM lane quadrant w % 4.
+    const int sw = warp - 2;                   // 0..7
+    const int half = sw >> 2;                  // which 64 columns
+    const int quad = warp & 3;
     const int r = quad * 32 + lane;            // query row within the tile
+    const int c0 = half * 64;                  // first column owned
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     uint8_t* prow = smem + OFF_P + r * 64;
     const int swz = (r >> 1) & 3;              // 64-byte swizzle of this row's 16-byte chunks
+    float* red = reinterpret_cast<float*>(smem + OFF_RED);  // [2 tile parities][2 halves][128 rows]
+    const float qk = p.qk_scale;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const int s = j % STAGES, sb = j & 1;
-      ok = mbar_wait(&bars->s_full[sb], (j >> 1) & 1, status, 0x1301) &&
-           mbar_wait(&bars->kv_full[s], (j / STAGES) & 1, status, 0x1302);
+      // After a failed (timed-out) wait the thread stops waiting but keeps
+      // iterating, so every softmax warp reaches every named barrier.
+      if (ok) ok = mbar_wait(&bars->s_full[sb], (j >> 1) & 1, status, 0x1301) &&
+                   mbar_wait(&bars->kv_full[s], (j / STAGES) & 1, status, 0x1302);
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform: the TMEM loads below are .sync.aligned
-      if (!ok) break;
       tc_fence_after();
-      float x[BN];
-#pragma unroll
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t u[32];
-        tmem_ld32(tmem + lane_base + T_S0 + sb * 128 + c, u);
+      float x[64];
+      {
+        uint32_t u[32], u2[32];
+        tmem_ld32(tmem + lane_base + T_S0 + sb * 128 + c0, u);
+        tmem_ld32(tmem + lane_base + T_S0 + sb * 128 + c0 + 32, u2);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[c + i] = __uint_as_float(u[i]);
+        for (int i = 0; i < 32; ++i) {
+          x[i] = __uint_as_float(u[i]);
+          x[32 + i] = __uint_as_float(u2[i]);
+        }
       }
       tc_fence_before();
       mbar_arrive(&bars->s_free[sb]);
       const uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
       if (p.smoothing) {
-        const uint4* dsv = reinterpret_cast<const uint4*>(st + ST_DS);
+        const uint4* dsv = reinterpret_cast<const uint4*>(st + ST_DS + c0 * 2);
 #pragma unroll
-        for (int c = 0; c < BN / 8; ++c) {
+        for (int c = 0; c < 8; ++c) {
           const uint4 w = dsv[c];
           const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            x[c * 8 + 2 * i] += bf16lo(ww[i]);
-            x[c * 8 + 2 * i + 1] += bf16hi(ww[i]);
+            const float2 a = add_f32x2(make_float2(x[c * 8 + 2 * i], x[c * 8 + 2 * i + 1]),
+                                       make_float2(bf16lo(ww[i]), bf16hi(ww[i])));
+            x[c * 8 + 2 * i] = a.x;
+            x[c * 8 + 2 * i + 1] = a.y;
           }
         }
       }
       // masking: keys beyond L (last tile) and, if causal, keys after the query
-      const int key0 = j * BN;
+      const int key0 = j * BN + c0;
       const int qrow = qt * BM + r;
       const int lim = p.causal ? min(p.L - key0, qrow - key0 + 1) : p.L - key0;
-      if (lim < BN) {
+      if (lim < 64) {
 #pragma unroll
-        for (int i = 0; i < BN; ++i)
+        for (int i = 0; i < 64; ++i)
           if (i >= lim) x[i] = -INFINITY;
       }
-      float mx = -INFINITY;
+      // row max over this thread's 64 keys (8 independent chains), then with the partner
+      float mx8[8];
 #pragma unroll
-      for (int i = 0; i < BN; ++i) mx = fmaxf(mx, x[i]);
-      const float m_new = fmaxf(m_run, mx * p.qk_scale);
+      for (int a = 0; a < 8; ++a) mx8[a] = x[a];
+#pragma unroll
+      for (int i = 8; i < 64; i += 8)
+#pragma unroll
+        for (int a = 0; a < 8; ++a) mx8[a] = fmaxf(mx8[a], x[i + a]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      red[(sb * 2 + half) * 128 + r] = mx;
+      named_barrier(1, 256);
+      const float mx_row = fmaxf(mx, red[(sb * 2 + (half ^ 1)) * 128 + r]);
+      const float m_new = fmaxf(m_run, mx_row * qk);
       // PV(j-1) must be complete before O is rescaled or P is overwritten
-      if (j >= 1) ok = mbar_wait(&bars->o_done, (j - 1) & 1, status, 0x1303);
+      if (ok && j >= 1) ok = mbar_wait(&bars->o_done, (j - 1) & 1, status, 0x1303);
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
       const bool grow = (m_new > m_run) && (m_run != -INFINITY);
       const float alpha = grow ? ex2_approx(m_run - m_new) : 1.0f;
       if (__any_sync(0xffffffffu, grow)) {
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < HD; c += 32) {
+        for (int c = 0; c < 64; c += 32) {
           uint32_t u[32];
-          tmem_ld32(tmem + lane_base + T_O + c, u);
+          tmem_ld32(tmem + lane_base + T_O + c0 + c, u);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
-          tmem_st32(tmem + lane_base + T_O + c, u);
+          for (int i = 0; i < 32; i += 2) {
+            const float2 v = mul_f32x2(make_float2(__uint_as_float(u[i]), __uint_as_float(u[i + 1])),
+                                       make_float2(alpha, alpha));
+            u[i] = __float_as_uint(v.x);
+            u[i + 1] = __float_as_uint(v.y);
+          }
+          tmem_st32(tmem + lane_base + T_O + c0 + c, u);
         }
         tmem_st_wait();
       }
       l_run *= alpha;
       m_run = m_new;
-      const float mneg = -m_new;
-      float lsum = 0.f;
+      // p = exp2(x * qk_scale - m); partial row sum in 8 chains
+      const float2 qk2 = make_float2(qk, qk), mneg2 = make_float2(-m_new, -m_new);
+      float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        x[i] = ex2_approx(fmaf(x[i], p.qk_scale, mneg));
-        lsum += x[i];
+      for (int i = 0; i < 64; i += 2) {
+        const float2 t = fma_f32x2(make_float2(x[i], x[i + 1]), qk2, mneg2);
+        x[i] = ex2_approx(t.x);
+        x[i + 1] = ex2_approx(t.y);
+        ls8[(i >> 1) & 7] += x[i] + x[i + 1];
       }
-      l_run += lsum;
+      l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
       // P -> E2M1 codes (RNE) with one E8M0 scale per 32 keys
-      uint32_t sfw = 0;
+      uint32_t sfh = 0;
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        float amax = 0.f;
+      for (int g = 0; g < 2; ++g) {
+        float a8[8];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, x[g * 32 + i]);
-        int e = ceil_log2_pos(__fdiv_rn(amax, 6.0f));
-        e = min(max(e, -127), 127);
-        const int be = 127 - e;
-        const float inv = be >= 1 ? __uint_as_float(static_cast<uint32_t>(be) << 23)
-                                  : __uint_as_float(1u << (22 + be));
+        for (int a = 0; a < 8; ++a) a8[a] = x[g * 32 + a];
+#pragma unroll
+        for (int i = 8; i < 32; i += 8)
+#pragma unroll
+          for (int a = 0; a < 8; ++a) a8[a] = fmaxf(a8[a], x[g * 32 + i + a]);
+        const float amax = fmaxf(fmaxf(fmaxf(a8[0], a8[1]), fmaxf(a8[2], a8[3])),
+                                 fmaxf(fmaxf(a8[4], a8[5]), fmaxf(a8[6], a8[7])));
+        // e = clamp(ceil(log2(amax / 6)), -127, 127); 0 -> -127
+        const uint32_t rb = __float_as_uint(__fdiv_rn(amax, 6.0f));
+        const int e = min(max(static_cast<int>(rb >> 23) - 127 + ((rb & 0x7FFFFFu) != 0), -127), 127);
+        const int be = 127 - e;  // biased exponent of 2^-e, in [0, 254]
+        const float inv = __uint_as_float(be > 0 ? static_cast<uint32_t>(be) << 23 : 0x00400000u);
+        const float2 inv2 = make_float2(inv, inv);
         uint32_t w[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -313,30 +340,37 @@ sage3_mxfp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int n = g * 32 + q * 8 + 2 * i;
-            word |= cvt_e2m1x2(x[n] * inv, x[n + 1] * inv) << (8 * i);
+            const float2 sc = mul_f32x2(make_float2(x[n], x[n + 1]), inv2);
+            word |= cvt_e2m1x2(sc.x, sc.y) << (8 * i);
           }
           w[q] = word;
         }
-        *reinterpret_cast<uint4*>(prow + ((g ^ swz) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-        sfw |= static_cast<uint32_t>(e + 127) << (8 * g);
+        const int chunk = half * 2 + g;
+        *reinterpret_cast<uint4*>(prow + ((chunk ^ swz) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        sfh |= static_cast<uint32_t>(e + 127) << (8 * g);
       }
-      *reinterpret_cast<uint32_t*>(smem + OFF_PSF + (r & 31) * 16 + (r >> 5) * 4) = sfw;
+      *reinterpret_cast<uint16_t*>(smem + OFF_PSF + (r & 31) * 16 + (r >> 5) * 4 + half * 2) =
+          static_cast<uint16_t>(sfh);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->p_full);
     }
-    // ---------------- epilogue
+    // ---------------- epilogue: combine the two partial row sums, O / l -> bf16
+    red[(2 * 2 + half) * 128 + r] = l_run;
+    named_barrier(1, 256);
+    const float l_row = l_run + red[(2 * 2 + (half ^ 1)) * 128 + r];
     if (ok && nkv > 0) ok = mbar_wait(&bars->o_done, (nkv - 1) & 1, status, 0x1304);
+    ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     const int qrow = qt * BM + r;
     const bool store = ok && !*(volatile int*)&bars->abort && qrow < p.L;
-    const float inv_l = 1.0f / l_run;
+    const float inv_l = 1.0f / l_row;
     const int b = bh / p.H, h = bh % p.H;
-    __nv_bfloat16* orow = out + b * p.o_sb + static_cast<int64_t>(qrow) * p.o_sn + h * p.o_sh;
+    __nv_bfloat16* orow = out + b * p.o_sb + static_cast<int64_t>(qrow) * p.o_sn + h * p.o_sh + c0;
 #pragma unroll 1
-    for (int c = 0; c < HD; c += 32) {
+    for (int c = 0; c < 64; c += 32) {
       uint32_t u[32];
-      tmem_ld32(tmem + lane_base + T_O + c, u);
+      tmem_ld32(tmem + lane_base + T_O + c0 + c, u);
       tmem_ld_wait();
       if (store) {
         uint4* dst = reinterpret_cast<uint4*>(orow + c);

@@ -119,6 +119,19 @@ __device__ __forceinline__ float2 mul_f32x2(float2 a, float2 b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack_f32x2(a.x, a.y)), "l"(pack_f32x2(b.x, b.y)));
   return unpack_f32x2(d);
 }
+__device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack_f32x2(a.x, a.y)), "l"(pack_f32x2(b.x, b.y)));
+  return unpack_f32x2(d);
+}
+__device__ __forceinline__ float2 fma_f32x2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(pack_f32x2(a.x, a.y)), "l"(pack_f32x2(b.x, b.y)), "l"(pack_f32x2(c.x, c.y)));
+  return unpack_f32x2(d);
+}
+
 // Streaming 16-byte global load / store (data is touched exactly once).
 __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
   uint4 v;
