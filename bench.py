@@ -91,7 +91,10 @@ WORKLOADS = {
                       rows=8192, cols=4096, make=c1_input),
     "sage3_mxfp4": dict(config="BASELINE config 4: Sage3 self-attention, MXFP4, Wan-2.1-14B 720p: "
                                "B=1, H=40, L=75600, D=128, bf16 NHD, non-causal, fp32 accumulation",
-                        rows=75600, cols=128, make=None),
+                        rows=75600, cols=128, make=None, B=1, H=40, sage3="mxfp4_hw", acc="fp32"),
+    "sage3_nvfp4": dict(config="BASELINE config 5: Sage3 self-attention, NVFP4, SAGE3_ACC_DTYPE=bf16_pv_only, "
+                               "Flux-like batch: B=8, H=24, L=4608, D=128, bf16 NHD, 1% of K rows x20",
+                        rows=4608, cols=128, make=None, B=8, H=24, sage3="nvfp4", acc="bf16_pv_only"),
     "mxfp4_linear": dict(config="BASELINE config 3: MXFP4 QDQ fused into a tcgen05 FP4 GEMM, "
                                 "A bf16 [M=4096, K=4096], W MXFP4 [N=14336, K=4096], out bf16",
                          rows=4096, cols=4096, make=None),
@@ -528,16 +531,32 @@ def c4_inputs(dev, L: int = 75600, H: int = 40, seed: int = 4):
     return q, k, v
 
 
+def c5_inputs(dev, B: int = 8, L: int = 4608, H: int = 24, seed: int = 5):
+    """Config 5: Q/K/V ~ N(0,1) NHD bf16; 1% of K rows of every (b, h), chosen
+    per (b, h) with the seeded generator, scaled by 20."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn(B, L, H, 128, generator=g, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(B, L, H, 128, generator=g, device=dev)
+    pick = torch.rand(B, L, H, 1, generator=g, device=dev).argsort(dim=1) < (L // 100)
+    k = torch.where(pick, k * 20.0, k).to(torch.bfloat16)
+    v = torch.randn(B, L, H, 128, generator=g, device=dev, dtype=torch.bfloat16)
+    return q, k, v
+
+
 def run_attn(args, wl, world, rank, dev, dist) -> None:
     from vllm_qdq_plugin import _native
     from vllm_qdq_plugin.sage3_attn.impl import Sage3TritonImpl
 
     L = args.rows or wl["rows"]
-    H = 40
-    q, k, v = c4_inputs(dev, L=L, H=H)
+    B, H = wl["B"], wl["H"]
+    if args.workload == "sage3_nvfp4":
+        q, k, v = c5_inputs(dev, B=B, L=L, H=H)
+    else:
+        q, k, v = c4_inputs(dev, L=L, H=H)
+    variant = {"mxfp4_hw": 0, "nvfp4": 1, "mxfp4": 2}[wl["sage3"]]
     out = torch.empty_like(q)
     lib = _native.lib()
-    ws = torch.empty((lib.sage3_attn_workspace_bytes(1, L, H, 128),), dtype=torch.uint8, device=dev)
+    ws = torch.empty((lib.sage3_attn_workspace_bytes(B, L, H, 128),), dtype=torch.uint8, device=dev)
     import ctypes
     st = [q.stride(0), q.stride(1), q.stride(2)] * 3 + [out.stride(0), out.stride(1), out.stride(2)]
     strides = (ctypes.c_int64 * 12)(*st)
@@ -548,8 +567,8 @@ def run_attn(args, wl, world, rank, dev, dist) -> None:
 
     def step():
         _native.check("sage3_fp4_attn", lib.sage3_fp4_attn(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), 1, L, H, 128, strides, sm, 0, 0,
-            0, 1, 0, ws.data_ptr(), ws.numel(), sp))
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, L, H, 128, strides, sm, variant,
+            0 if wl["acc"] == "fp32" else 1, 0, 1, 0, ws.data_ptr(), ws.numel(), sp))
         launches[0] += 6  # k sums, Q quant, K quant, V quant, delta_s, flash
 
     def barrier():
@@ -581,11 +600,11 @@ def run_attn(args, wl, world, rank, dev, dist) -> None:
     if sampler:
         sampler.stop()
     ms_step = ms / steps
-    flop = 4.0 * H * L * L * 128
+    flop = 4.0 * B * H * L * L * 128
     value = world * flop / (ms_step * 1e-3) / 1e12
     # end to end through the backend impl with pinned host buffers
     impl = Sage3TritonImpl(num_heads=H, head_size=128, softmax_scale=sm,
-                           backend_kwargs={"sage3_config": "mxfp4_hw"})
+                           backend_kwargs={"sage3_config": wl["sage3"], "sage3_acc_dtype": wl["acc"]})
     qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
     oh = torch.empty_like(qh).pin_memory()
     n_e2e = 2
@@ -611,11 +630,12 @@ def run_attn(args, wl, world, rank, dev, dist) -> None:
             "metric": "Sage3 attention TFLOPS (4*B*H*L^2*D per call)", "value": round(value, 1),
             "unit": "TFLOP/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
             "ms_per_step": round(ms_step, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": round(261.81 / ms_step, 3) if L == 75600 else None,
+            "vs_baseline": round(261.81 / ms_step, 3) if (L == 75600 and B == 1 and H == 40) else None,
             "vs_baseline_note": "reference mxfp4_hw on 1x B200: 261.81 ms (speed-up = 261.81 / ms_per_step)",
             "dtype": "e2m1 x e2m1 (E8M0 scales), fp32 softmax/accumulate, bf16 in/out",
             "data": "synthetic (seeded, BASELINE config-4 distributions, generated on device)",
-            "config": {"workload": wl["config"], "B": 1, "H": H, "L": L, "D": 128,
+            "config": {"workload": wl["config"], "B": B, "H": H, "L": L, "D": 128, "sage3": wl["sage3"],
+                       "acc_dtype": wl["acc"],
                        "l2": "K/V/delta_s streams per head exceed L2 residency across heads"},
             "e2e": {"value": round(e2e, 1), "unit": "TFLOP/s", "h2d_bytes_per_step": 3 * q.numel() * 2,
                     "d2h_bytes_per_step": q.numel() * 2,
@@ -624,7 +644,7 @@ def run_attn(args, wl, world, rank, dev, dist) -> None:
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_source": src,
                          "traffic": ncu_traffic("sage3_mxfp4"),
-                         "softmax_floor_ms": round(H * L * L / (148 * 16 * 1.965e9) * 1e3, 2)},
+                         "softmax_floor_ms": round(B * H * L * L / (148 * 16 * 1.965e9) * 1e3, 2)},
             "clocks": sampler.summary(t_wall0, t_wall1) if sampler else None,
         }
         print(json.dumps(line), flush=True)

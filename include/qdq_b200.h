@@ -169,8 +169,15 @@ int64_t sage3_attn_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t D);
  *   strides: 12 element strides, for q, k, v, o in turn: (batch, token, head);
  *            the head-dim stride must be 1.  NHD tensors [B, L, H, D] and HND
  *            tensors [B, H, L, D] are both expressed this way.
- *   quant_format: 0 = MXFP4 (E2M1 + E8M0 per 32; the reference mxfp4_hw
- *            semantics), 1 = NVFP4 (E2M1 + E4M3 per 16).
+ *   quant_format: 0 = config "mxfp4_hw": MXFP4 (E2M1 + E8M0 per 32) with the
+ *                reference hardware kernel's P handling (l = sum of unquantised P),
+ *                mxfp4_hw_kernel.py:167-393;
+ *            1 = config "nvfp4": NVFP4 (E2M1 + E4M3 per 16) with the reference's
+ *                emulated-config P handling (P scaled by 448*6 before block
+ *                scaling, l = sum of quantised P), p_quant_kernels.py:37-99 and
+ *                attention_kernel.py:176-186;
+ *            2 = config "mxfp4": MXFP4 with the emulated-config P handling
+ *                (p_quant_kernels.py:106-150).
  *   acc_mode: 0 = fp32, 1 = a reduced-precision PV accumulator of the
  *            reference (accepted; this kernel accumulates in fp32 either way).
  *   causal: non-zero for a causal mask (query i sees keys <= i).

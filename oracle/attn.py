@@ -58,16 +58,49 @@ def _rne_e2m1(v: np.ndarray) -> np.ndarray:
     return np.copysign(q, v)
 
 
+def _rna_e2m1(v: np.ndarray) -> np.ndarray:
+    """Round-half-away onto the E2M1 grid (the reference's _float_to_e2m1_nibble
+    thresholds, mxfp4_hw_kernel.py:43-61), clamped to 6."""
+    a = np.minimum(np.abs(v), 6.0)
+    q = np.where(a < 0.25, 0.0, np.where(a < 0.75, 0.5, np.where(a < 1.25, 1.0,
+        np.where(a < 1.75, 1.5, np.where(a < 2.5, 2.0, np.where(a < 3.5, 3.0,
+        np.where(a < 5.0, 4.0, 6.0)))))))
+    return np.copysign(q, v)
+
+
+def e4m3_round(x: np.ndarray) -> np.ndarray:
+    """fp32 -> float8_e4m3fn -> fp32 for 0 <= x <= 448, round-to-nearest-even."""
+    x = np.minimum(np.asarray(x, np.float64), 448.0)
+    _, ex = np.frexp(np.maximum(x, 2.0 ** -6))  # x = m * 2^ex, m in [0.5, 1)
+    step = np.where(x < 2.0 ** -6, 2.0 ** -9, np.exp2(ex - 1 - 3.0))
+    return (np.round(x / step) * step).astype(np.float32)  # np.round: half to even
+
+
+def nv_quant_deq(x: np.ndarray) -> np.ndarray:
+    """NVFP4 of the reference's nvfp4 QuantConfig on the hardware grid, per 16
+    along the last axis: scale = e4m3(max(bf16(amax / 6), 1e-8)), codes of
+    x * (1/scale) with round-half-away, dequantised."""
+    sh = x.shape
+    xb = np.asarray(x, np.float32).reshape(*sh[:-1], sh[-1] // 16, 16)
+    amax = np.abs(xb).max(axis=-1)
+    sc = np.maximum(bf16_round(amax / np.float32(6.0)), np.float32(1e-8))
+    s = e4m3_round(sc)
+    inv = np.where(s > 0, np.float32(1.0) / np.where(s > 0, s, 1), 0).astype(np.float32)
+    q = _rna_e2m1((xb * inv[..., None]).astype(np.float32))
+    return (q * s[..., None].astype(np.float64)).reshape(sh)
+
+
 def _ceil_log2(r: np.ndarray) -> np.ndarray:
     m, e = np.frexp(r)  # r = m * 2^e, m in [0.5, 1)
     out = np.where(m == 0.5, e - 1, e).astype(np.int64)
     return np.where(r == 0, -127, out)
 
 
-def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True):
+def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True, nv: bool = False):
     """q, k, v: float32 [L, D] holding bf16 values for one (batch, head).
-    Returns (qd, kd, vd, ds): dequantised Q [Lp, D], K [Lp, D], V [Lp, D] (from
-    V^T codes) and delta_s [G, Lp] (zeros without smoothing)."""
+    Returns (qd, kd, vd, ds): dequantised Q [Lp, D], K [Lp, D], V [Lp, D]
+    (V quantised along the sequence) and delta_s [G, Lp] (zeros without
+    smoothing).  nv selects NVFP4 blocks of 16 (E4M3) instead of MXFP4."""
     L, D = q.shape
     Lp = (L + 127) // 128 * 128
     G = Lp // 128
@@ -83,17 +116,25 @@ def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True)
         kc, qs = k, q
         ds = np.zeros((G, L), np.float32)
     pad = lambda a: np.concatenate([a, np.zeros((Lp - L, D), np.float32)])  # noqa: E731
+    dsp = np.zeros((G, Lp), np.float64)
+    dsp[:, :L] = ds
+    if nv:
+        return (nv_quant_deq(pad(qs)), nv_quant_deq(pad(kc)),
+                nv_quant_deq(np.ascontiguousarray(pad(v).T)).T, dsp)
     qcodes, qsc = oq.mxfp4_hw_quant(pad(qs))
     kcodes, ksc = oq.mxfp4_hw_quant(pad(kc))
     vcodes, vsc = oq.mxfp4_hw_quant(np.ascontiguousarray(pad(v).T))  # [D, Lp/2], [D, Lp/32]
-    dsp = np.zeros((G, Lp), np.float64)
-    dsp[:, :L] = ds
     return _deq(qcodes, qsc), _deq(kcodes, ksc), _deq(vcodes, vsc).T, dsp
 
 
 def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: bool = False,
-          mask_padding: bool = True) -> np.ndarray:
-    """The mxfp4_hw flash loop on dequantised operands; returns O [L, D] float64."""
+          mask_padding: bool = True, nv: bool = False, emulated: bool = False) -> np.ndarray:
+    """The attention loop on dequantised operands; returns O [L, D] float64.
+
+    P handling: mxfp4_hw (nv=False, emulated=False): E8M0 per 32 of p, l = sum
+    of unquantised p.  Emulated configs (emulated=True): p scaled by 448*6
+    first, l = sum of the dequantised P (p_quant_kernels.py:37-150,
+    attention_kernel.py:176-186); nv=True uses E4M3 per 16."""
     Lp, D = qd.shape
     n_keys = L if mask_padding else Lp
     qk_scale = sm_scale * LOG2E
@@ -102,6 +143,7 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
     l = np.zeros(Lp)
     acc = np.zeros((Lp, D))
     group = np.repeat(np.arange(Lp // 128), 128)
+    pre = 2688.0 if emulated else 1.0
     for n0 in range(0, n_keys, block_n):
         n1 = min(n0 + block_n, Lp)
         s = qd @ kd[n0:n1].T + ds[group, n0:n1]
@@ -113,30 +155,41 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
         m_new = np.maximum(m, s.max(axis=1) * qk_scale)
         alpha = np.where(np.isneginf(m), 0.0, np.exp2(m - m_new))
         p = np.where(valid, np.exp2(s * qk_scale - m_new[:, None]), 0.0)
-        l = l * alpha + p.sum(axis=1)
         acc = acc * alpha[:, None]
         w = n1 - n0
-        pg = p.reshape(Lp, w // 32, 32)
-        e = np.clip(_ceil_log2(pg.max(axis=2) / 6.0), -127, 127)
-        sc = np.exp2(e.astype(np.float64))[:, :, None]
-        pq = (_rne_e2m1(pg / sc) * sc).reshape(Lp, w)
+        p1 = p * pre
+        if nv:
+            pg = p1.reshape(Lp, w // 16, 16)
+            sc = e4m3_round(np.maximum(pg.max(axis=2) / 6.0, 1e-8)).astype(np.float64)[:, :, None]
+            inv = np.where(sc > 0, 1.0 / np.where(sc > 0, sc, 1), 0.0)
+            pq = (_rne_e2m1(pg * inv) * sc).reshape(Lp, w)
+        else:
+            pg = p1.reshape(Lp, w // 32, 32)
+            e = np.clip(_ceil_log2(pg.max(axis=2) / 6.0), -127, 127)
+            sc = np.exp2(e.astype(np.float64))[:, :, None]
+            pq = (_rne_e2m1(pg / sc) * sc).reshape(Lp, w)
+        l = l * alpha + (pq.sum(axis=1) if emulated else p.sum(axis=1))
         acc = acc + pq @ vd[n0:n1]
         m = m_new
     return (acc / l[:, None])[:L]
 
 
+VARIANTS = {"mxfp4_hw": (False, False), "mxfp4": (False, True), "nvfp4": (True, True)}
+
+
 def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_scale: float,
               block_n: int = 128, causal: bool = False, smoothing: bool = True,
-              mask_padding: bool = True) -> np.ndarray:
+              mask_padding: bool = True, config: str = "mxfp4_hw") -> np.ndarray:
     """q/k/v: uint16 bf16 bit patterns [L, H, D] (NHD with B = 1); returns O [L, H, D]."""
+    nv, emulated = VARIANTS[config]
     L, H, D = q_bits.shape
     out = np.zeros((L, H, D))
     for h in range(H):
         q = bf16_bits_to_f32(q_bits[:, h])
         k = bf16_bits_to_f32(k_bits[:, h])
         v = bf16_bits_to_f32(v_bits[:, h])
-        qd, kd, vd, ds = prepass(q, k, v, smoothing)
-        out[:, h] = flash(qd, kd, vd, ds, L, sm_scale, block_n, causal, mask_padding)
+        qd, kd, vd, ds = prepass(q, k, v, smoothing, nv)
+        out[:, h] = flash(qd, kd, vd, ds, L, sm_scale, block_n, causal, mask_padding, nv, emulated)
     return out
 
 

@@ -59,6 +59,37 @@ def test_mxfp4_attention_matches_oracle(cuda_device, L, H):
     assert _native.device_status() == 0
 
 
+@pytest.mark.parametrize("config", ["mxfp4", "nvfp4"])
+@pytest.mark.parametrize("L,H", [(256, 2), (1000, 1)])
+def test_emulated_configs_match_oracle(cuda_device, config, L, H):
+    q, k, v = _qkv(L, H, seed=L * 3 + H)
+    sm = 1.0 / math.sqrt(128)
+    got = _run(q, k, v, cuda_device, config=config)[0]
+    qb, kb, vb = _bits(q[0]), _bits(k[0]), _bits(v[0])
+    want = oa.attention(qb, kb, vb, sm, config=config)
+    assert oa.rel_l2(got, want) < 2e-2, oa.rel_l2(got, want)
+    exact = oa.exact_attention(qb, kb, vb, sm)
+    assert oa.rel_l2(got, exact) <= 1.1 * oa.rel_l2(want, exact) + 0.01
+
+
+def test_config5_flux_shape_nvfp4(cuda_device):
+    """BASELINE config 5 distribution (1% of K rows x20) on a reduced batch."""
+    g = torch.Generator().manual_seed(5)
+    B, L, H = 1, 512, 2
+    q = torch.randn(B, L, H, 128, generator=g)
+    k = torch.randn(B, L, H, 128, generator=g)
+    rows = torch.randperm(L, generator=g)[: L // 100]
+    k[:, rows] *= 20
+    v = torch.randn(B, L, H, 128, generator=g)
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    from vllm_qdq_plugin.sage3_attn.sage3 import sage3_attention_nhd
+    got = sage3_attention_nhd(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), config="nvfp4",
+                              acc_dtype="bf16_pv_only").float().cpu().numpy()[0]
+    sm = 1.0 / math.sqrt(128)
+    want = oa.attention(_bits(q[0]), _bits(k[0]), _bits(v[0]), sm, config="nvfp4")
+    assert oa.rel_l2(got, want) < 2e-2
+
+
 def test_causal_and_no_smoothing(cuda_device):
     q, k, v = _qkv(384, 1, seed=7)
     sm = 1.0 / math.sqrt(128)

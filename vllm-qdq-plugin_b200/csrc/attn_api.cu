@@ -16,8 +16,8 @@ extern "C" int sage3_fp4_attn(const void* q, const void* k, const void* v, void*
   if (B == 0 || L == 0 || H == 0) return QDQ_OK;
   if (D != 128) return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: head_dim %lld (this build supports 128)", (long long)D);
   if (dtype != QDQ_DTYPE_BF16) return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: inputs must be bf16");
-  if (quant_format != 0)
-    return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: quant_format %d not available (0 = MXFP4)", quant_format);
+  if (quant_format < 0 || quant_format > 2)
+    return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: quant_format must be 0 (mxfp4_hw), 1 (nvfp4) or 2 (mxfp4)");
   if (acc_mode < 0 || acc_mode > 1) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: acc_mode must be 0 or 1");
   if (!q || !k || !v || !o || !strides) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: null pointer");
   if (!(sm_scale > 0.f)) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: sm_scale must be positive");
@@ -47,6 +47,8 @@ extern "C" int sage3_fp4_attn(const void* q, const void* k, const void* v, void*
   p.sm_scale = sm_scale;
   p.causal = causal ? 1 : 0;
   p.smoothing = smoothing ? 1 : 0;
+  p.nv = quant_format == 1 ? 1 : 0;
+  p.emulated = quant_format == 0 ? 0 : 1;
   attn::Workspace w;
   attn::carve(p.B, p.H, p.L, static_cast<uint8_t*>(workspace), &w);
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -21,6 +21,9 @@ struct Problem {
   float sm_scale;
   int causal;
   int smoothing;  // per-128-token Q mean / K mean smoothing with the delta_s correction
+  int nv;         // 0: MXFP4 (E8M0 per 32), 1: NVFP4 (E4M3 per 16)
+  int emulated;   // 1: the reference's emulated-config P handling (P scaled by 448*6 before
+                  //    block scaling, l = sum of quantised P); 0: its mxfp4_hw kernel's
 };
 
 // Device buffers of the pre-pass (carved out of the caller's workspace).
@@ -28,11 +31,11 @@ struct Workspace {
   float* ksum;            // [BH, 128]
   __nv_bfloat16* qmean;   // [BH, G, 128]
   uint8_t* qc;            // [BH * Lp, 64]
-  uint8_t* qsf;           // [BH * Lp / 128, 512]
+  uint8_t* qsf;           // [BH * Lp / 128, 1024]
   uint8_t* kc;            // [BH * Lp, 64]
-  uint8_t* ksf;           // [BH * Lp / 128, 512]
+  uint8_t* ksf;           // [BH * Lp / 128, 1024]
   uint8_t* vt;            // [BH * 128, Lp / 2]
-  uint8_t* vsf;           // [BH * Lp / 128, 512]
+  uint8_t* vsf;           // [BH * Lp / 128, 1024]
   __nv_bfloat16* ds;      // [BH, G, Lp]
 };
 
@@ -52,11 +55,11 @@ inline int64_t carve(int B, int H, int L, uint8_t* base, Workspace* w) {
   uint8_t* ksum = take(BH * 128 * 4);
   uint8_t* qmean = take(BH * G * 128 * 2);
   uint8_t* qc = take(BH * Lp * 64);
-  uint8_t* qsf = take(BH * G * 512);
+  uint8_t* qsf = take(BH * G * 1024);
   uint8_t* kc = take(BH * Lp * 64);
-  uint8_t* ksf = take(BH * G * 512);
+  uint8_t* ksf = take(BH * G * 1024);
   uint8_t* vt = take(BH * 128 * Lp / 2);
-  uint8_t* vsf = take(BH * G * 512);
+  uint8_t* vsf = take(BH * G * 1024);
   uint8_t* ds = take(BH * G * Lp * 2);
   if (w) {
     w->ksum = reinterpret_cast<float*>(ksum);

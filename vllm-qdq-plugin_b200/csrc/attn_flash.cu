@@ -1,5 +1,6 @@
-// Sage3 FP4 flash attention on sm_100a tensor cores (MXFP4: E2M1 data, E8M0
-// scales per 32), D = 128, one 128-row query tile per CTA.
+// Sage3 FP4 flash attention on sm_100a tensor cores, D = 128, one 128-row
+// query tile per CTA.  MXFP4 (E2M1 + E8M0 per 32, tcgen05 kind::mxf4) or
+// NVFP4 (E2M1 + E4M3 per 16, kind::mxf4nvf4 block16).
 //
 // Reference semantics: the mxfp4_hw kernel (sage3/mxfp4_hw_kernel.py:167-393)
 //   S  = dot_scaled(Q, K^T) (+ delta_s[group of the query tile, key]),
@@ -35,22 +36,23 @@ constexpr int BM = 128, BN = 128, HD = 128;
 constexpr int STAGES = 4;
 constexpr int CODE_TILE = 128 * 64;  // 8 KB: 128 rows x 128 E2M1
 constexpr int SF_CHUNK = 512;
+constexpr int SF_TILE = 1024;        // scale bytes per 128-row tile in global memory (two chunks)
 constexpr int DS_BYTES = BN * 2;
 // stage: K codes | V codes | K sf | V sf | delta_s (bf16)
-constexpr int ST_K = 0, ST_V = CODE_TILE, ST_KSF = 2 * CODE_TILE, ST_VSF = ST_KSF + SF_CHUNK,
-              ST_DS = ST_VSF + SF_CHUNK;
-constexpr int STAGE_BYTES = 18 * 1024;
+constexpr int ST_K = 0, ST_V = CODE_TILE, ST_KSF = 2 * CODE_TILE, ST_VSF = ST_KSF + SF_TILE,
+              ST_DS = ST_VSF + SF_TILE;
+constexpr int STAGE_BYTES = 19 * 1024;
 static_assert(ST_DS + DS_BYTES <= STAGE_BYTES, "stage layout");
 // CTA smem: Q codes | P codes | stages | Q sf | P sf | barriers
 constexpr int OFF_Q = 0, OFF_P = CODE_TILE, OFF_STAGE = 2 * CODE_TILE;
 constexpr int OFF_QSF = OFF_STAGE + STAGES * STAGE_BYTES;
-constexpr int OFF_PSF = OFF_QSF + SF_CHUNK;
-constexpr int OFF_RED = OFF_PSF + SF_CHUNK;              // [3][2][128] floats: row max / row sum exchange
+constexpr int OFF_PSF = OFF_QSF + SF_TILE;
+constexpr int OFF_RED = OFF_PSF + SF_TILE;              // [3][2][128] floats: row max / row sum exchange
 constexpr int OFF_BAR = OFF_RED + 3 * 2 * 128 * 4;
 constexpr int THREADS = 320;                             // producer, MMA, 8 softmax warps
 constexpr int TMEM_COLS = 512;
-constexpr uint32_t T_S0 = 0, T_O = 256, T_SFQ = 384, T_SFK = 388, T_SFP = 392, T_SFV = 396;
-constexpr uint32_t IDESC = idesc_mxf4(BM, BN, true);  // also N = HD for PV
+// scale-factor columns: 8 per operand (NVFP4: two chunks; MXFP4 uses the first 4)
+constexpr uint32_t T_S0 = 0, T_O = 256, T_SFQ = 384, T_SFK = 392, T_SFP = 400, T_SFV = 408;
 static_assert(HD == BN, "PV uses the same instruction shape as QK");
 
 struct Bars {
@@ -73,10 +75,46 @@ struct Params {
   float qk_scale;   // sm_scale * log2(e)
   int causal;
   int smoothing;
+  float p_prescale;  // 1, or 448*6 for the reference's emulated configs
+  int l_quant;       // l = sum of quantised P (emulated configs) instead of unquantised p
 };
 
+// Sum of the eight E2M1 values packed in a 32-bit word (exact in fp16).
+__device__ __forceinline__ float e2m1_word_sum(uint32_t w) {
+  __half2 acc = __floats2half2_rn(0.f, 0.f);
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const uint32_t h = e2m1x2_to_f16x2((w >> (8 * b)) & 0xFFu);
+    acc = __hadd2(acc, *reinterpret_cast<const __half2*>(&h));
+  }
+  return __low2float(acc) + __high2float(acc);
+}
+
+// Issue the two K=64 block-scaled MMAs of a 128 x 128 x 128 product.
+template <bool kNV>
+__device__ __forceinline__ void mma_k128(uint32_t d, uint64_t da, uint64_t db, uint32_t sfa, uint32_t sfb,
+                                         bool accumulate_first) {
+  constexpr uint32_t idesc = idesc_mxf4(BM, BN, !kNV);
+#pragma unroll
+  for (int kk = 0; kk < 2; ++kk) {
+    if (kNV) {  // UE4M3 per 16: MMA kk reads scale chunk kk (4 scales per row)
+      mma_nvf4(d, da + kk * 2, db + kk * 2, idesc, sfa + 4 * kk, sfb + 4 * kk, accumulate_first || kk);
+    } else {    // UE8M0 per 32: scale bytes 2kk, 2kk+1 of the chunk
+      const uint32_t sf_id = kk * 2;
+      mma_mxf4(d, da + kk * 2, db + kk * 2, idesc_with_sf_ids(idesc, sf_id, sf_id), sfa | (sf_id << 30),
+               sfb | (sf_id << 30), accumulate_first || kk);
+    }
+  }
+}
+template <bool kNV>
+__device__ __forceinline__ void cp_sf(uint32_t taddr, const uint8_t* smem_sf) {
+  tmem_cp_sf(taddr, smem_desc_sf(smem_sf));
+  if (kNV) tmem_cp_sf(taddr + 4, smem_desc_sf(smem_sf + SF_CHUNK));
+}
+
+template <bool kNV>
 __global__ void __launch_bounds__(THREADS, 1)
-sage3_mxfp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                          const __grid_constant__ CUtensorMap map_v, const uint8_t* __restrict__ qsf,
                          const uint8_t* __restrict__ ksf, const uint8_t* __restrict__ vsf,
                          const __nv_bfloat16* __restrict__ ds, __nv_bfloat16* __restrict__ out, Params p,
@@ -122,9 +160,10 @@ sage3_mxfp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one()) {
-      mbar_arrive_expect_tx(&bars->q_full, CODE_TILE + SF_CHUNK);
+      constexpr int kSfBytes = kNV ? SF_TILE : SF_CHUNK;
+      mbar_arrive_expect_tx(&bars->q_full, CODE_TILE + kSfBytes);
       tma_load_2d(smem + OFF_Q, &map_q, 0, bh * p.Lp + qt * BM, &bars->q_full);
-      bulk_load(smem + OFF_QSF, qsf + (static_cast<int64_t>(bh) * p.T + qt) * SF_CHUNK, SF_CHUNK, &bars->q_full);
+      bulk_load(smem + OFF_QSF, qsf + (static_cast<int64_t>(bh) * p.T + qt) * SF_TILE, kSfBytes, &bars->q_full);
       int issued = 0;
       for (int j = 0; j < nkv; ++j) {
         const int s = j % STAGES;
@@ -134,12 +173,12 @@ sage3_mxfp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
         }
         if (*(volatile int*)&bars->abort) break;
         uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
-        const uint32_t bytes = 2 * CODE_TILE + 2 * SF_CHUNK + (p.smoothing ? DS_BYTES : 0);
+        const uint32_t bytes = 2 * CODE_TILE + 2 * kSfBytes + (p.smoothing ? DS_BYTES : 0);
         mbar_arrive_expect_tx(&bars->kv_full[s], bytes);
         tma_load_2d(st + ST_K, &map_k, 0, bh * p.Lp + j * BN, &bars->kv_full[s]);
         tma_load_2d(st + ST_V, &map_v, j * (BN / 2), bh * HD, &bars->kv_full[s]);
-        bulk_load(st + ST_KSF, ksf + (static_cast<int64_t>(bh) * p.T + j) * SF_CHUNK, SF_CHUNK, &bars->kv_full[s]);
-        bulk_load(st + ST_VSF, vsf + (static_cast<int64_t>(bh) * p.T + j) * SF_CHUNK, SF_CHUNK, &bars->kv_full[s]);
+        bulk_load(st + ST_KSF, ksf + (static_cast<int64_t>(bh) * p.T + j) * SF_TILE, kSfBytes, &bars->kv_full[s]);
+        bulk_load(st + ST_VSF, vsf + (static_cast<int64_t>(bh) * p.T + j) * SF_TILE, kSfBytes, &bars->kv_full[s]);
         if (p.smoothing)
           bulk_load(st + ST_DS, ds + (static_cast<int64_t>(bh) * G + qt) * p.Lp + j * BN, DS_BYTES,
                     &bars->kv_full[s]);
@@ -155,7 +194,7 @@ sage3_mxfp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
       bool ok = mbar_wait(&bars->q_full, 0, status, 0x1201);
       if (ok) {
         tc_fence_after();
-        tmem_cp_sf(tmem + T_SFQ, smem_desc_sf(smem + OFF_QSF));
+        cp_sf<kNV>(tmem + T_SFQ, smem + OFF_QSF);
       }
       const uint64_t dq = smem_desc_sw64(smem + OFF_Q);
       const uint64_t dp = smem_desc_sw64(smem + OFF_P);
@@ -164,15 +203,9 @@ sage3_mxfp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
         if (!mbar_wait(&bars->p_full, t & 1, status, 0x1202)) return false;
         tc_fence_after();
         uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
-        tmem_cp_sf(tmem + T_SFP, smem_desc_sf(smem + OFF_PSF));
-        tmem_cp_sf(tmem + T_SFV, smem_desc_sf(st + ST_VSF));
-        const uint64_t dv = smem_desc_sw64(st + ST_V);
-#pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-          const uint32_t sf_id = kk * 2;
-          mma_mxf4(tmem + T_O, dp + kk * 2, dv + kk * 2, idesc_with_sf_ids(IDESC, sf_id, sf_id),
-                   (tmem + T_SFP) | (sf_id << 30), (tmem + T_SFV) | (sf_id << 30), (t | kk) != 0);
-        }
+        cp_sf<kNV>(tmem + T_SFP, smem + OFF_PSF);
+        cp_sf<kNV>(tmem + T_SFV, st + ST_VSF);
+        mma_k128<kNV>(tmem + T_O, dp, smem_desc_sw64(st + ST_V), tmem + T_SFP, tmem + T_SFV, t != 0);
         tc_commit(&bars->kv_empty[s]);
         tc_commit(&bars->o_done);
         return true;
@@ -184,14 +217,8 @@ sage3_mxfp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
         if (*(volatile int*)&bars->abort) { ok = false; break; }
         tc_fence_after();
         uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
-        tmem_cp_sf(tmem + T_SFK, smem_desc_sf(st + ST_KSF));
-        const uint64_t dk = smem_desc_sw64(st + ST_K);
-#pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-          const uint32_t sf_id = kk * 2;
-          mma_mxf4(tmem + T_S0 + sb * 128, dq + kk * 2, dk + kk * 2, idesc_with_sf_ids(IDESC, sf_id, sf_id),
-                   (tmem + T_SFQ) | (sf_id << 30), (tmem + T_SFK) | (sf_id << 30), kk != 0);
-        }
+        cp_sf<kNV>(tmem + T_SFK, st + ST_KSF);
+        mma_k128<kNV>(tmem + T_S0 + sb * 128, dq, smem_desc_sw64(st + ST_K), tmem + T_SFQ, tmem + T_SFK, false);
         tc_commit(&bars->s_full[sb]);
         if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
       }
@@ -313,44 +340,96 @@ sage3_mxfp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid
         x[i + 1] = ex2_approx(t.y);
         ls8[(i >> 1) & 7] += x[i] + x[i + 1];
       }
-      l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
-      // P -> E2M1 codes (RNE) with one E8M0 scale per 32 keys
-      uint32_t sfh = 0;
+      const float lsum_tile = ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
+      if (!p.l_quant) l_run += lsum_tile;
+      // P -> E2M1 codes (round-to-nearest-even) with per-block scales:
+      // MXFP4: E8M0 2^e per 32 keys, e = clamp(ceil(log2(max / 6)), -127, 127);
+      // NVFP4: E4M3 per 16 keys, s = e4m3(max(max / 6, 1e-8)).
+      // The emulated configs first scale p by 448*6 (it cancels in O / l).
+      float lq = 0.f;  // sum of the quantised values (emulated configs)
+      if (p.p_prescale != 1.0f) {
+        const float2 ps = make_float2(p.p_prescale, p.p_prescale);
 #pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        float a8[8];
-#pragma unroll
-        for (int a = 0; a < 8; ++a) a8[a] = x[g * 32 + a];
-#pragma unroll
-        for (int i = 8; i < 32; i += 8)
-#pragma unroll
-          for (int a = 0; a < 8; ++a) a8[a] = fmaxf(a8[a], x[g * 32 + i + a]);
-        const float amax = fmaxf(fmaxf(fmaxf(a8[0], a8[1]), fmaxf(a8[2], a8[3])),
-                                 fmaxf(fmaxf(a8[4], a8[5]), fmaxf(a8[6], a8[7])));
-        // e = clamp(ceil(log2(amax / 6)), -127, 127); 0 -> -127
-        const uint32_t rb = __float_as_uint(__fdiv_rn(amax, 6.0f));
-        const int e = min(max(static_cast<int>(rb >> 23) - 127 + ((rb & 0x7FFFFFu) != 0), -127), 127);
-        const int be = 127 - e;  // biased exponent of 2^-e, in [0, 254]
-        const float inv = __uint_as_float(be > 0 ? static_cast<uint32_t>(be) << 23 : 0x00400000u);
-        const float2 inv2 = make_float2(inv, inv);
-        uint32_t w[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t word = 0;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int n = g * 32 + q * 8 + 2 * i;
-            const float2 sc = mul_f32x2(make_float2(x[n], x[n + 1]), inv2);
-            word |= cvt_e2m1x2(sc.x, sc.y) << (8 * i);
-          }
-          w[q] = word;
+        for (int i = 0; i < 64; i += 2) {
+          const float2 v = mul_f32x2(make_float2(x[i], x[i + 1]), ps);
+          x[i] = v.x;
+          x[i + 1] = v.y;
         }
-        const int chunk = half * 2 + g;
-        *reinterpret_cast<uint4*>(prow + ((chunk ^ swz) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-        sfh |= static_cast<uint32_t>(e + 127) << (8 * g);
       }
-      *reinterpret_cast<uint16_t*>(smem + OFF_PSF + (r & 31) * 16 + (r >> 5) * 4 + half * 2) =
-          static_cast<uint16_t>(sfh);
+      if (!kNV) {
+        uint32_t sfh = 0;
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          float a8[8];
+#pragma unroll
+          for (int a = 0; a < 8; ++a) a8[a] = x[g * 32 + a];
+#pragma unroll
+          for (int i = 8; i < 32; i += 8)
+#pragma unroll
+            for (int a = 0; a < 8; ++a) a8[a] = fmaxf(a8[a], x[g * 32 + i + a]);
+          const float amax = fmaxf(fmaxf(fmaxf(a8[0], a8[1]), fmaxf(a8[2], a8[3])),
+                                   fmaxf(fmaxf(a8[4], a8[5]), fmaxf(a8[6], a8[7])));
+          const uint32_t rb = __float_as_uint(__fdiv_rn(amax, 6.0f));
+          const int e = min(max(static_cast<int>(rb >> 23) - 127 + ((rb & 0x7FFFFFu) != 0), -127), 127);
+          const int be = 127 - e;  // biased exponent of 2^-e, in [0, 254]
+          const float inv = __uint_as_float(be > 0 ? static_cast<uint32_t>(be) << 23 : 0x00400000u);
+          const float2 inv2 = make_float2(inv, inv);
+          uint32_t w[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int n = g * 32 + q * 8 + 2 * i;
+              const float2 sc = mul_f32x2(make_float2(x[n], x[n + 1]), inv2);
+              word |= cvt_e2m1x2(sc.x, sc.y) << (8 * i);
+            }
+            w[q] = word;
+          }
+          if (p.l_quant) {
+            const float sum = (e2m1_word_sum(w[0]) + e2m1_word_sum(w[1])) + (e2m1_word_sum(w[2]) + e2m1_word_sum(w[3]));
+            lq += sum * __uint_as_float(e + 127 > 0 ? static_cast<uint32_t>(e + 127) << 23 : 0x00400000u);
+          }
+          const int chunk = half * 2 + g;
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ swz) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          sfh |= static_cast<uint32_t>(e + 127) << (8 * g);
+        }
+        *reinterpret_cast<uint16_t*>(smem + OFF_PSF + (r & 31) * 16 + (r >> 5) * 4 + half * 2) =
+            static_cast<uint16_t>(sfh);
+      } else {
+        uint32_t sfw = 0;
+        uint32_t w[8];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          float a8[8];
+#pragma unroll
+          for (int a = 0; a < 8; ++a) a8[a] = fmaxf(x[g * 16 + a], x[g * 16 + 8 + a]);
+          const float amax = fmaxf(fmaxf(fmaxf(a8[0], a8[1]), fmaxf(a8[2], a8[3])),
+                                   fmaxf(fmaxf(a8[4], a8[5]), fmaxf(a8[6], a8[7])));
+          const float scl = fmaxf(__fdiv_rn(amax, 6.0f), 1e-8f);
+          const uint32_t sb8 = e4m3_byte(scl);
+          const float sv = round_e4m3(scl);
+          const float inv = sv > 0.f ? __fdiv_rn(1.0f, sv) : 0.f;
+          const float2 inv2 = make_float2(inv, inv);
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int n = g * 16 + q * 8 + 2 * i;
+              const float2 sc = mul_f32x2(make_float2(x[n], x[n + 1]), inv2);
+              word |= cvt_e2m1x2(sc.x, sc.y) << (8 * i);
+            }
+            w[g * 2 + q] = word;
+          }
+          if (p.l_quant) lq += (e2m1_word_sum(w[g * 2]) + e2m1_word_sum(w[g * 2 + 1])) * sv;
+          sfw |= sb8 << (8 * g);
+        }
+        *reinterpret_cast<uint4*>(prow + (((half * 2) ^ swz) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(prow + (((half * 2 + 1) ^ swz) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+        *reinterpret_cast<uint32_t*>(smem + OFF_PSF + half * SF_CHUNK + (r & 31) * 16 + (r >> 5) * 4) = sfw;
+      }
+      if (p.l_quant) l_run += lq;
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->p_full);
@@ -404,14 +483,15 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   if (int st = make_tmap_u8_2d(&mq, w.qc, BH * pr.Lp, 64, 64, 64, 128, 64)) return st;
   if (int st = make_tmap_u8_2d(&mk, w.kc, BH * pr.Lp, 64, 64, 64, 128, 64)) return st;
   if (int st = make_tmap_u8_2d(&mv, w.vt, BH * HD, pr.Lp / 2, pr.Lp / 2, 64, 128, 64)) return st;
-  static bool attr[64] = {false};
+  static bool attr[2][64] = {{false}};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(sage3_mxfp4_flash_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(SMEM_BYTES));
+  const void* fn = pr.nv ? reinterpret_cast<const void*>(&sage3_fp4_flash_kernel<true>)
+                         : reinterpret_cast<const void*>(&sage3_fp4_flash_kernel<false>);
+  if (dev >= 0 && dev < 64 && !attr[pr.nv][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM_BYTES));
     if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "sage3 flash: smem attribute: %s", cudaGetErrorString(e));
-    attr[dev] = true;
+    attr[pr.nv][dev] = true;
   }
   Params p;
   p.H = pr.H;
@@ -424,9 +504,15 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   p.qk_scale = pr.sm_scale * 1.4426950408889634f;
   p.causal = pr.causal;
   p.smoothing = pr.smoothing;
+  p.p_prescale = pr.emulated ? 2688.0f : 1.0f;
+  p.l_quant = pr.emulated;
   dim3 grid(static_cast<unsigned>(p.T), static_cast<unsigned>(BH));
-  sage3_mxfp4_flash_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o, p,
-                                                            status);
+  if (pr.nv)
+    sage3_fp4_flash_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o, p,
+                                                                  status);
+  else
+    sage3_fp4_flash_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o,
+                                                                   p, status);
   return check_launch("sage3 flash");
 }
 

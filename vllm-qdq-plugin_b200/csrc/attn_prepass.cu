@@ -20,9 +20,10 @@
 //   ksum   fp32 [BH, D]           per-channel sums of k (mean = bf16(ksum / L))
 //   qmean  bf16 [BH, G, D]        Q group means
 //   qc, kc uint8 [BH*Lp, D/2]     E2M1 codes (element 2j low nibble)
-//   qsf, ksf                      E8M0, one 512-byte tcgen05 scale chunk per 128 rows
+//   qsf, ksf                      block scales, 1024 bytes per 128 rows: two 512-byte tcgen05
+//                                 scale chunks (NVFP4: 8 E4M3 per row; MXFP4: 4 E8M0 in the first)
 //   vt     uint8 [BH*D, Lp/2]     V transposed: row (bh, d), keys packed along the row
-//   vsf                           E8M0, chunk (bh, key tile) = 128 d-rows x 4 key groups
+//   vsf                           1024 bytes per (bh, key tile): 128 d-rows x (4 E8M0 | 8 E4M3)
 //   ds     bf16 [BH, G, Lp]       delta_s
 #include "attn_common.cuh"
 
@@ -89,6 +90,31 @@ __device__ __forceinline__ uint32_t mx_quant32(const float* v, uint8_t* out) {
   return static_cast<uint32_t>(e + 127);
 }
 
+// Quantise 16 floats (one NVFP4 block of the reference's nvfp4 QuantConfig,
+// sage3/quantize.py:21-81 with round_to_e4m3): scale = e4m3(bf16(amax / 6)
+// clamped below at 1e-8), codes of x / scale with round-half-away thresholds
+// (the hardware E2M1 grid; the reference's emulation grid also has 0.75).
+// Writes 8 code bytes, returns the E4M3 scale byte (0 when the scale underflows).
+__device__ __forceinline__ uint32_t nv_quant16(const float* v, uint8_t* out) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const float sc = fmaxf(bf16_round(amax / 6.0f), 1e-8f);
+  const uint32_t sbyte = e4m3_byte(sc);
+  const float s = round_e4m3(sc);
+  const float inv = s > 0.f ? 1.0f / s : 0.f;
+  uint32_t w[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) word |= e2m1_rna(v[q * 8 + i] * inv) << (4 * i);
+    w[q] = word;
+  }
+  *reinterpret_cast<uint2*>(out) = make_uint2(w[0], w[1]);
+  return sbyte;
+}
+
 __device__ __forceinline__ int64_t nhd_row(int b, int n, int h, int64_t sb, int64_t sn, int64_t sh) {
   return b * sb + n * sn + h * sh;
 }
@@ -110,7 +136,7 @@ __global__ void __launch_bounds__(128) ksum_kernel(const __nv_bfloat16* __restri
 // grid (BH, Lp/128), 256 threads.  Loads one 128-row x 128-d tile, subtracts
 // the mean (Q: the tile's own group mean, written to qmean; K: ksum / L),
 // rounds to bf16 and quantises each row along D into 4 MX groups.
-template <bool kIsQ>
+template <bool kIsQ, bool kNV>
 __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __restrict__ x, int H, int L, int Lp,
                                                        int64_t sb, int64_t sn, int64_t sh,
                                                        const float* __restrict__ ksum, __nv_bfloat16* __restrict__ qmean,
@@ -145,26 +171,29 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
     mean[d] = m;
   }
   __syncthreads();
-  // 512 (row, group) items, 2 per thread
-  for (int it = threadIdx.x; it < 512; it += 256) {
-    const int r = it >> 2, g = it & 3;
+  // (row, group) items: MXFP4 4 groups of 32 per row, NVFP4 8 groups of 16.
+  // Scale chunks: 1024 bytes per 128-row tile (MXFP4 uses the first 512).
+  uint8_t* sft = sf + (static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 1024;
+  constexpr int kGroups = kNV ? 8 : 4, kGs = kNV ? 16 : 32;
+  for (int it = threadIdx.x; it < 128 * kGroups; it += 256) {
+    const int r = it / kGroups, g = it % kGroups;
     const int n = t0 + r;
-    float v[32];
+    float v[kGs];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int d = g * 32 + i;
+    for (int i = 0; i < kGs; ++i) {
+      const int d = g * kGs + i;
       v[i] = (n < L) ? bf16_round(__bfloat162float(tile[r][d]) - mean[d]) : 0.f;  // padding after smoothing
     }
-    uint8_t* crow = codes + (static_cast<int64_t>(bh) * Lp + n) * 64 + g * 16;
-    const uint32_t e = mx_quant32(v, crow);
-    sf[(static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 512 + (r % 32) * 16 + (r / 32) * 4 + g] =
-        static_cast<uint8_t>(e);
+    uint8_t* crow = codes + (static_cast<int64_t>(bh) * Lp + n) * 64 + g * (kGs / 2);
+    const uint32_t e = kNV ? nv_quant16(v, crow) : mx_quant32(v, crow);
+    sft[(g / 4) * 512 + (r % 32) * 16 + (r / 32) * 4 + (g % 4)] = static_cast<uint8_t>(e);
   }
 }
 
 // ---------------------------------------------------------------- V quantisation
 // grid (BH, Lp/128), 128 threads: thread d quantises V[:, d] over the tile's
 // 128 keys in 4 groups of 32 and writes 64 code bytes of row (bh, d) of V^T.
+template <bool kNV>
 __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __restrict__ v, int H, int L, int Lp,
                                                       int64_t sb, int64_t sn, int64_t sh,
                                                       uint8_t* __restrict__ vt, uint8_t* __restrict__ vsf) {
@@ -180,17 +209,30 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
   }
   __syncthreads();
   const int d = threadIdx.x;
-  uint32_t sfw = 0;
   uint8_t* row = vt + (static_cast<int64_t>(bh) * 128 + d) * (Lp / 2) + blockIdx.y * 64;
+  uint8_t* sft = vsf + (static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 1024 + (d % 32) * 16 + (d / 32) * 4;
+  if (kNV) {
+    uint32_t sfw[2] = {0, 0};
 #pragma unroll 1
-  for (int g = 0; g < 4; ++g) {
-    float x[32];
+    for (int g = 0; g < 8; ++g) {
+      float x[16];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(tile[g * 32 + i][d]);
-    sfw |= mx_quant32(x, row + g * 16) << (8 * g);
+      for (int i = 0; i < 16; ++i) x[i] = __bfloat162float(tile[g * 16 + i][d]);
+      sfw[g / 4] |= nv_quant16(x, row + g * 8) << (8 * (g % 4));
+    }
+    *reinterpret_cast<uint32_t*>(sft) = sfw[0];
+    *reinterpret_cast<uint32_t*>(sft + 512) = sfw[1];
+  } else {
+    uint32_t sfw = 0;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      float x[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(tile[g * 32 + i][d]);
+      sfw |= mx_quant32(x, row + g * 16) << (8 * g);
+    }
+    *reinterpret_cast<uint32_t*>(sft) = sfw;
   }
-  *reinterpret_cast<uint32_t*>(vsf + (static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 512 +
-                               (d % 32) * 16 + (d / 32) * 4) = sfw;
 }
 
 // ---------------------------------------------------------------- delta_s
@@ -304,11 +346,19 @@ int launch_prepass(const Problem& p, const Workspace& w, cudaStream_t s) {
   if (p.smoothing) {
     ksum_kernel<<<dim3(BH, (p.L + 1023) / 1024), 128, 0, s>>>(p.k, p.H, p.L, p.k_sb, p.k_sn, p.k_sh, w.ksum);
   }
-  qk_quant_kernel<true><<<dim3(BH, T), 256, 0, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh, w.ksum, w.qmean,
-                                                  w.qc, w.qsf, p.smoothing);
-  qk_quant_kernel<false><<<dim3(BH, T), 256, 0, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh, w.ksum, w.qmean,
-                                                   w.kc, w.ksf, p.smoothing);
-  v_quant_kernel<<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf);
+  if (p.nv) {
+    qk_quant_kernel<true, true><<<dim3(BH, T), 256, 0, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh, w.ksum,
+                                                          w.qmean, w.qc, w.qsf, p.smoothing);
+    qk_quant_kernel<false, true><<<dim3(BH, T), 256, 0, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh, w.ksum,
+                                                           w.qmean, w.kc, w.ksf, p.smoothing);
+    v_quant_kernel<true><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf);
+  } else {
+    qk_quant_kernel<true, false><<<dim3(BH, T), 256, 0, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh, w.ksum,
+                                                           w.qmean, w.qc, w.qsf, p.smoothing);
+    qk_quant_kernel<false, false><<<dim3(BH, T), 256, 0, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh, w.ksum,
+                                                            w.qmean, w.kc, w.ksf, p.smoothing);
+    v_quant_kernel<false><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf);
+  }
   if (p.smoothing) {
     const int smem = (128 + 64) * DS_LD * 2;
     static bool attr[64] = {false};

@@ -49,14 +49,15 @@ ACC_DTYPE_MAP = {
     "bf16_full": ("bf16", "bf16", "bf16"),
 }
 
-# config name -> kernel quant format (0 = MXFP4, 1 = NVFP4)
-ATTENTION_CONFIGS: dict[str, int] = {"mxfp4": 0, "mxfp4_hw": 0, "nvfp4": 1}
+# config name -> kernel variant of sage3_fp4_attn (include/qdq_b200.h):
+#   0 mxfp4_hw (MXFP4, hardware-kernel P handling), 1 nvfp4, 2 mxfp4 (emulated-config P handling)
+ATTENTION_CONFIGS: dict[str, int] = {"mxfp4": 2, "mxfp4_hw": 0, "nvfp4": 1}
 
 # Names the reference registers that lie outside this build's FP4 path.
 _OTHER_REFERENCE_CONFIGS = ("mxfp4_s1", "mxfp8_s1", "nvfp4_vsmooth", "mxfp4_vsmooth", "mxfp8_hw",
                             "mixed_mxfp8qk_mxfp4pv_hw", "mixed_mxfp4qk_mxfp8pv_hw", "int8", "fp8")
 
-_BUILT_FORMATS = (0,)  # formats with a kernel in this build
+_BUILT_FORMATS = (0, 1, 2)  # variants with a kernel in this build
 
 
 def _get_env_bool(name: str, default: str = "0") -> bool:
