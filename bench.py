@@ -40,6 +40,7 @@ sys.path.insert(0, str(REPO / "vllm-qdq-plugin_b200"))
 import torch  # noqa: E402
 
 BYTES_PER_ELT = 4  # 2 B read + 2 B written per bf16 element (algorithmic)
+L2_BYTES = 126 * 1000 * 1000  # B200 L2 capacity
 
 # ---------------------------------------------------------------------------
 # seeded synthetic inputs (shapes and distributions of the BASELINE configs)
@@ -290,8 +291,12 @@ def run_ours(args) -> None:
         return run_attn(args, wl, world, rank, dev, dist)
     x_cpu = wl["make"](rows=args.rows) if args.rows else wl["make"]()
     M, K = x_cpu.shape
-    x = x_cpu.to(dev)
-    y = torch.empty_like(x)
+    # Enough (x, y) pairs that each is touched again only after >= 3x the L2
+    # capacity of other traffic: every timed launch reads its input from HBM.
+    n_pairs = max(1, -(-3 * L2_BYTES // (M * K * BYTES_PER_ELT)))
+    xs = [x_cpu.to(dev) for _ in range(n_pairs)]
+    ys = [torch.empty_like(xs[0]) for _ in range(n_pairs)]
+    x = xs[0]
     gs = global_scale_of(x_cpu).to(dev)
     lib = _native.lib()
     stream = torch.cuda.current_stream(dev)
@@ -300,7 +305,8 @@ def run_ours(args) -> None:
 
     if args.workload == "nvfp4_qdq":
         def step():
-            _native.check("qdq_nvfp4", lib.qdq_nvfp4(x.data_ptr(), y.data_ptr(), None, None,
+            i = launches[0] % n_pairs
+            _native.check("qdq_nvfp4", lib.qdq_nvfp4(xs[i].data_ptr(), ys[i].data_ptr(), None, None,
                                                      gs.data_ptr(), M, K, K, K, 0, sp))
             launches[0] += 1
 
@@ -308,7 +314,8 @@ def run_ours(args) -> None:
             return nvfp4_qdq(xd, global_scale=gs)
     else:
         def step():
-            _native.check("qdq_mxfp4", lib.qdq_mxfp4(x.data_ptr(), y.data_ptr(), None, None,
+            i = launches[0] % n_pairs
+            _native.check("qdq_mxfp4", lib.qdq_mxfp4(xs[i].data_ptr(), ys[i].data_ptr(), None, None,
                                                      M, K, K, K, 0, 32, sp))
             launches[0] += 1
 
@@ -320,7 +327,7 @@ def run_ours(args) -> None:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    # ---- kernel-level throughput, inputs resident in HBM (> L2, no flush needed)
+    # ---- kernel-level throughput, inputs resident in HBM (rotated pairs, no L2 reuse)
     for _ in range(args.warmup):
         step()
     barrier()
@@ -386,7 +393,8 @@ def run_ours(args) -> None:
             "config": {"workload": wl["config"], "rows": M, "cols": K,
                        "per_rank_rows": M, "global_rows": M * world,
                        "parallelism": f"rows x{world}, no collective on the data path",
-                       "l2": "input and output (268 MB each) exceed the 126 MB L2"},
+                       "l2": (f"{n_pairs} rotating input/output pairs of {M * K * 2 / 1e6:.0f} MB each: "
+                              "no buffer is re-touched within 3x the 126 MB L2")},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * K * 2,
                     "path": f"vllm_qdq_plugin.qdq.{args.workload} on pinned host buffers"},

@@ -36,7 +36,7 @@ struct Workspace {
   uint8_t* ksf;           // [BH * Lp / 128, 1024]
   uint8_t* vt;            // [BH * 128, Lp / 2]
   uint8_t* vsf;           // [BH * Lp / 128, 1024]
-  __nv_bfloat16* ds;      // [BH, G, Lp]
+  float* ds;              // [BH, G, Lp] (bf16-rounded values, stored as fp32)
 };
 
 inline int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
@@ -60,7 +60,7 @@ inline int64_t carve(int B, int H, int L, uint8_t* base, Workspace* w) {
   uint8_t* ksf = take(BH * G * 1024);
   uint8_t* vt = take(BH * 128 * Lp / 2);
   uint8_t* vsf = take(BH * G * 1024);
-  uint8_t* ds = take(BH * G * Lp * 2);
+  uint8_t* ds = take(BH * G * Lp * 4);
   if (w) {
     w->ksum = reinterpret_cast<float*>(ksum);
     w->qmean = reinterpret_cast<__nv_bfloat16*>(qmean);
@@ -70,7 +70,7 @@ inline int64_t carve(int B, int H, int L, uint8_t* base, Workspace* w) {
     w->ksf = ksf;
     w->vt = vt;
     w->vsf = vsf;
-    w->ds = reinterpret_cast<__nv_bfloat16*>(ds);
+    w->ds = reinterpret_cast<float*>(ds);
   }
   return off;
 }

@@ -17,15 +17,16 @@
 // CTA = two 128-row query tiles (A, B) of one (batch, head) that share every
 // K/V tile, 12 warps:
 //   warps 0-3     softmax A: one thread per query row (TMEM lane): S -> registers,
-//                 + delta_s, row max, O_A rescale in TMEM when the max grows,
-//                 exp2, row sum, P -> E2M1 codes + block scales in shared
-//                 memory; epilogue O_A / l -> bf16 NHD
+//                 + delta_s, block maxima (the row max and each block's max
+//                 of p follow from them), O_A rescale in TMEM when the max
+//                 grows, exp2, row sum, P -> E2M1 codes + block scales in
+//                 shared memory; epilogue O_A / l -> bf16 NHD
 //   warps 4-7     softmax B (the same for tile B)
 //   warp 8        MMA issuer: per key tile j, S = Q_A K_j^T, then (once A has
 //                 read S) S = Q_B K_j^T, then O_A += P_A V_{j-1}, O_B += P_B V_{j-1}
 //   warp 9        TMA producer: K tile [128 keys x 64 B], V^T tile [128 d x 64 B]
 //                 (64-byte swizzle), their scale chunks and both tiles' delta_s
-//                 slices into a 4-stage ring; Q_A, Q_B once
+//                 slices (128 fp32 each) into a 4-stage ring; Q_A, Q_B once
 //   warps 10-11   idle (they complete the third warpgroup for setmaxnreg)
 // The single S buffer alternates between the two softmax warpgroups, which
 // therefore run out of phase and overlap their MUFU / FMA / ALU work.
@@ -45,17 +46,19 @@ constexpr int STAGES = 4;
 constexpr int CODE_TILE = 128 * 64;  // 8 KB: 128 rows x 128 E2M1
 constexpr int SF_CHUNK = 512;
 constexpr int SF_TILE = 1024;        // scale bytes per 128-row tile in global memory (two chunks)
-constexpr int DS_BYTES = BN * 2;
+constexpr int DS_BYTES = BN * 4;     // delta_s slice of one query tile: 128 fp32
 // stage: K codes | V codes | K sf | V sf | delta_s A | delta_s B
 constexpr int ST_K = 0, ST_V = CODE_TILE, ST_KSF = 2 * CODE_TILE, ST_VSF = ST_KSF + SF_TILE,
               ST_DS = ST_VSF + SF_TILE;
 constexpr int STAGE_BYTES = 19 * 1024;
 static_assert(ST_DS + 2 * DS_BYTES <= STAGE_BYTES, "stage layout");
-// CTA smem: Q_A | Q_B | P_A | P_B | stages | Q sf A,B | P sf A,B | barriers
-constexpr int OFF_Q = 0, OFF_P = 2 * CODE_TILE, OFF_STAGE = 4 * CODE_TILE;
+// CTA smem: Q_A | Q_B | P_A[2] | P_B[2] | stages | Q sf A,B | P sf A[2],B[2] | barriers
+// P (codes and scales) is double-buffered per query tile: key tile j writes
+// buffer j & 1 while PV(j-1) may still read the other one.
+constexpr int OFF_Q = 0, OFF_P = 2 * CODE_TILE, OFF_STAGE = 6 * CODE_TILE;
 constexpr int OFF_QSF = OFF_STAGE + STAGES * STAGE_BYTES;
 constexpr int OFF_PSF = OFF_QSF + 2 * SF_TILE;
-constexpr int OFF_BAR = OFF_PSF + 2 * SF_TILE;
+constexpr int OFF_BAR = OFF_PSF + 4 * SF_TILE;
 constexpr int THREADS = 384;
 constexpr int TMEM_COLS = 512;
 // scale-factor columns: 8 per operand (NVFP4: two chunks; MXFP4 uses the first 4)
@@ -81,19 +84,64 @@ struct Params {
   float qk_scale;   // sm_scale * log2(e)
   int causal;
   int smoothing;
-  float p_prescale;  // 1, or 448*6 for the reference's emulated configs
-  int l_quant;       // l = sum of quantised P (emulated configs) instead of unquantised p
+  float p_prescale;  // 448*6 for the reference's emulated configs (unused by kMxHw)
 };
 
-// Sum of the eight E2M1 values packed in a 32-bit word (exact in fp16).
-__device__ __forceinline__ float e2m1_word_sum(uint32_t w) {
-  __half2 acc = __floats2half2_rn(0.f, 0.f);
-#pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    const uint32_t h = e2m1x2_to_f16x2((w >> (8 * b)) & 0xFFu);
-    acc = __hadd2(acc, *reinterpret_cast<const __half2*>(&h));
-  }
-  return __low2float(acc) + __high2float(acc);
+// Softmax / P-quantisation variants of the kernel.
+enum Mode : int {
+  kMxHw = 0,   // MXFP4, the reference mxfp4_hw kernel's P handling (l = sum of unquantised p)
+  kMxEmu = 1,  // MXFP4, the emulated config's P handling (p * 448*6, l = sum of quantised P)
+  kNvEmu = 2,  // NVFP4 (E4M3 per 16), emulated-config P handling
+};
+
+// Sum of four fp16x2 words holding decoded E2M1 values (exact in fp16: the
+// values are multiples of 0.5 and at most 6, a sum of 16 of them at most 96).
+__device__ __forceinline__ __half2 hsum4(const uint32_t (&h)[4]) {
+  const __half2* v = reinterpret_cast<const __half2*>(h);
+  return __hadd2(__hadd2(v[0], v[1]), __hadd2(v[2], v[3]));
+}
+
+// Shared-memory accesses through 32-bit shared-window addresses.
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+__device__ __forceinline__ void sts64(uint32_t a, uint32_t x, uint32_t y) {
+  asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(a), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void sts32(uint32_t a, uint32_t x) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(x) : "memory");
+}
+__device__ __forceinline__ float4 lds128f(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^e as a float for e in [-127, 127] (2^-127 is the subnormal 0x00400000).
+__device__ __forceinline__ float exp2i(int e) {
+  return __uint_as_float(e + 127 > 0 ? static_cast<uint32_t>(e + 127) << 23 : 0x00400000u);
+}
+
+// E8M0 block exponent of the reference for a finite amax >= 0:
+// e = clamp(ceil(log2(q)), -127, 127) with q = amax / 6 rounded to fp32 and
+// the ceiling read from q's bits (exponent field - 127, plus 1 if the
+// mantissa is nonzero).  Without the division: for amax = M * 2^E
+// (1 <= M < 2), q = (M / 1.5) * 2^(E-2) and its rounded value has a zero
+// mantissa iff M == 1.5 or rounds up to 2^(E-2), so the ceiling is
+// E - 2 + (M > 1.5) whenever q is normal (amax exponent field >= 3).  Below
+// that q is subnormal (ceiling read as -126) or rounds to 0 (-127, amax at
+// most 3 * 2^-149).
+__device__ __forceinline__ int mx_block_exp(float amax) {
+  const uint32_t b = __float_as_uint(amax);
+  const int ex = static_cast<int>(b >> 23);
+  const int e = ex < 3 ? (b > 3u ? -126 : -127) : ex - 129 + ((b & 0x7FFFFFu) > 0x400000u);
+  return min(e, 127);
 }
 
 // The two K=64 block-scaled MMAs of a 128 x 128 x 128 product.
@@ -121,28 +169,38 @@ __device__ __forceinline__ void cp_sf(uint32_t taddr, const uint8_t* smem_sf) {
 __device__ __forceinline__ void reg_alloc_224() { asm volatile("setmaxnreg.inc.sync.aligned.u32 224;"); }
 __device__ __forceinline__ void reg_dealloc_56() { asm volatile("setmaxnreg.dec.sync.aligned.u32 56;"); }
 
-// max of v[base .. base+32) in 8 independent chains
+// max of v[0 .. 16) and of v[0 .. 32), three-input max (sm_100)
+__device__ __forceinline__ float max16(const float* v) {
+  const float a0 = fmax3(v[0], v[1], v[2]), a1 = fmax3(v[3], v[4], v[5]), a2 = fmax3(v[6], v[7], v[8]);
+  const float a3 = fmax3(v[9], v[10], v[11]), a4 = fmax3(v[12], v[13], v[14]);
+  return fmaxf(fmax3(a0, a1, a2), fmax3(a3, a4, v[15]));
+}
 __device__ __forceinline__ float max32(const float* v) {
-  float m8[8];
+  float a[10];
 #pragma unroll
-  for (int a = 0; a < 8; ++a) m8[a] = fmaxf(fmaxf(v[a], v[8 + a]), fmaxf(v[16 + a], v[24 + a]));
-  return fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+  for (int i = 0; i < 10; ++i) a[i] = fmax3(v[3 * i], v[3 * i + 1], v[3 * i + 2]);
+  const float b0 = fmax3(a[0], a[1], a[2]), b1 = fmax3(a[3], a[4], a[5]), b2 = fmax3(a[6], a[7], a[8]);
+  const float b3 = fmax3(a[9], v[30], v[31]);
+  return fmaxf(fmax3(b0, b1, b2), b3);
 }
 
 // ---------------------------------------------------------------------------
 // softmax warpgroup: one query tile, thread = row
 // ---------------------------------------------------------------------------
-template <bool kNV>
+template <int kMode>
 __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t tmem, const Params& p, int wg,
                                            int qt, int bh, int nkv, __nv_bfloat16* __restrict__ out,
                                            int* status) {
+  constexpr bool kNV = kMode == kNvEmu;
+  constexpr int NG = kNV ? 8 : 4;            // scale blocks per row of 128 keys
   const int warp = (threadIdx.x >> 5) & 3;
   const int lane = threadIdx.x & 31;
   const int r = warp * 32 + lane;            // query row in the tile = TMEM lane
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
   const uint32_t t_o = tmem + T_O + wg * 128;
-  uint8_t* prow = smem + OFF_P + wg * CODE_TILE + r * 64;
-  uint8_t* psf = smem + OFF_PSF + wg * SF_TILE;
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t prow0 = sbase + OFF_P + 2 * wg * CODE_TILE + r * 64;                   // this row of P
+  const uint32_t psf0 = sbase + OFF_PSF + 2 * wg * SF_TILE + (r & 31) * 16 + (r >> 5) * 4;  // its scale word
   const int swz = (r >> 1) & 3;              // 64-byte swizzle of this row's 16-byte chunks
   const float qk = p.qk_scale;
   const int qrow = qt * BM + r;
@@ -167,20 +225,17 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     tmem_ld_wait();
     tc_fence_before();
     mbar_arrive(&bars->s_free[wg]);
-    const uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
-    if (p.smoothing) {
-      const uint4* dsv = reinterpret_cast<const uint4*>(st + ST_DS + wg * DS_BYTES);
+    if (p.smoothing) {  // + delta_s[key]: one fp32 row shared by the whole tile (broadcast loads)
+      const uint32_t dsv = sbase + OFF_STAGE + s * STAGE_BYTES + ST_DS + wg * DS_BYTES;
 #pragma unroll
-      for (int c = 0; c < BN / 8; ++c) {
-        const uint4 w = dsv[c];
-        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 a = add_f32x2(make_float2(x[c * 8 + 2 * i], x[c * 8 + 2 * i + 1]),
-                                     make_float2(bf16lo(ww[i]), bf16hi(ww[i])));
-          x[c * 8 + 2 * i] = a.x;
-          x[c * 8 + 2 * i + 1] = a.y;
-        }
+      for (int c = 0; c < BN / 4; ++c) {
+        const float4 d = lds128f(dsv + 16 * c);
+        const float2 a = add_f32x2(make_float2(x[4 * c], x[4 * c + 1]), make_float2(d.x, d.y));
+        const float2 b = add_f32x2(make_float2(x[4 * c + 2], x[4 * c + 3]), make_float2(d.z, d.w));
+        x[4 * c] = a.x;
+        x[4 * c + 1] = a.y;
+        x[4 * c + 2] = b.x;
+        x[4 * c + 3] = b.y;
       }
     }
     // masking: keys beyond L (last tile) and, if causal, keys after the query
@@ -191,126 +246,145 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
       for (int i = 0; i < BN; ++i)
         if (i >= lim) x[i] = -INFINITY;
     }
-    const float mx = fmaxf(fmaxf(max32(x), max32(x + 32)), fmaxf(max32(x + 64), max32(x + 96)));
+    // block maxima of the scores; the row max and each block's max of p
+    // (p = exp2(x * qk - m) is monotone in x) both follow from them
+    float gm[NG];
+#pragma unroll
+    for (int g = 0; g < NG; ++g) gm[g] = kNV ? max16(x + 16 * g) : max32(x + 32 * g);
+    const float mx = kNV ? fmaxf(fmax3(gm[0], gm[1], gm[2]), fmax3(fmax3(gm[3], gm[4], gm[5]), gm[6], gm[7]))
+                         : fmaxf(fmax3(gm[0], gm[1], gm[2]), gm[3]);
     const float m_new = fmaxf(m_run, mx * qk);
-    // PV(j-1) of this tile must be complete before O is rescaled or P is overwritten
-    if (ok && j >= 1) ok = mbar_wait(&bars->o_done[wg], (j - 1) & 1, status, 0x1303);
-    ok = __all_sync(0xffffffffu, ok);
     const bool grow = (m_new > m_run) && (m_run != -INFINITY);
     const float alpha = grow ? ex2_approx(m_run - m_new) : 1.0f;
-    if (__any_sync(0xffffffffu, grow)) {
-      tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < HD; c += 32) {
-        uint32_t u[32];
-        tmem_ld32(t_o + lane_base + c, u);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float2 v = mul_f32x2(make_float2(__uint_as_float(u[i]), __uint_as_float(u[i + 1])),
-                                     make_float2(alpha, alpha));
-          u[i] = __float_as_uint(v.x);
-          u[i + 1] = __float_as_uint(v.y);
-        }
-        tmem_st32(t_o + lane_base + c, u);
-      }
-      tmem_st_wait();
-    }
     l_run *= alpha;
     m_run = m_new;
-    // p = exp2(x * qk_scale - m); row sum in 8 chains
-    const float2 qk2 = make_float2(qk, qk), mneg2 = make_float2(-m_new, -m_new);
-    float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int i = 0; i < BN; i += 2) {
-      const float2 t = fma_f32x2(make_float2(x[i], x[i + 1]), qk2, mneg2);
-      x[i] = ex2_approx(t.x);
-      x[i + 1] = ex2_approx(t.y);
-      ls8[(i >> 1) & 7] += x[i] + x[i + 1];
-    }
-    if (!p.l_quant) l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
-    // P -> E2M1 codes (round-to-nearest-even) with per-block scales:
-    // MXFP4: E8M0 2^e per 32 keys, e = clamp(ceil(log2(max / 6)), -127, 127);
-    // NVFP4: E4M3 per 16 keys, s = e4m3(max(max / 6, 1e-8)).
-    // The emulated configs first scale p by 448*6 (it cancels in O / l).
-    if (p.p_prescale != 1.0f) {
-      const float2 ps = make_float2(p.p_prescale, p.p_prescale);
-#pragma unroll
-      for (int i = 0; i < BN; i += 2) {
-        const float2 v = mul_f32x2(make_float2(x[i], x[i + 1]), ps);
-        x[i] = v.x;
-        x[i + 1] = v.y;
-      }
-    }
-    float lq = 0.f;
-    if (!kNV) {
+    // P(j) goes to buffer j & 1; PV(j-2), its previous reader, completed before
+    // p_full(j-1) was signalled (the o_done wait below, one tile earlier).
+    const uint32_t prow = prow0 + (j & 1) * CODE_TILE;
+    const uint32_t psf = psf0 + (j & 1) * SF_TILE;
+    const float2 qk2 = make_float2(qk, qk);
+    if (kMode == kMxHw) {
+      // P -> E2M1 codes (round-to-nearest-even) with E8M0 2^e per 32 keys,
+      // e = clamp(ceil(log2(max p / 6)), -127, 127).  The block scale is folded
+      // into the exponent: p * 2^-e = exp2(x * qk - m - e).  l += sum of p
+      // = sum over blocks of 2^e * sum(p * 2^-e).
       uint32_t sfw = 0;
+      float lsum = 0.f;
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
-        const float amax = max32(x + g * 32);
-        const uint32_t rb = __float_as_uint(__fdiv_rn(amax, 6.0f));
-        const int e = min(max(static_cast<int>(rb >> 23) - 127 + ((rb & 0x7FFFFFu) != 0), -127), 127);
-        const int be = 127 - e;  // biased exponent of 2^-e, in [0, 254]
-        const float inv = __uint_as_float(be > 0 ? static_cast<uint32_t>(be) << 23 : 0x00400000u);
-        const float2 inv2 = make_float2(inv, inv);
+        const int e = mx_block_exp(ex2_approx(fmaf(gm[g], qk, -m_new)));
+        const float cg = -m_new - static_cast<float>(e);
+        const float2 c2 = make_float2(cg, cg);
+        float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
         uint32_t w[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          uint32_t word = 0;
+          float v[8];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int n = g * 32 + q * 8 + 2 * i;
-            const float2 sc = mul_f32x2(make_float2(x[n], x[n + 1]), inv2);
-            word |= cvt_e2m1x2(sc.x, sc.y) << (8 * i);
+            const float2 t = fma_f32x2(make_float2(x[n], x[n + 1]), qk2, c2);
+            v[2 * i] = ex2_approx(t.x);
+            v[2 * i + 1] = ex2_approx(t.y);
+            acc[i & 1] = add_f32x2(acc[i & 1], make_float2(v[2 * i], v[2 * i + 1]));
           }
-          w[q] = word;
+          w[q] = cvt_e2m1x8(v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7]);
         }
-        if (p.l_quant) {
-          const float sum = (e2m1_word_sum(w[0]) + e2m1_word_sum(w[1])) + (e2m1_word_sum(w[2]) + e2m1_word_sum(w[3]));
-          lq += sum * __uint_as_float(e + 127 > 0 ? static_cast<uint32_t>(e + 127) << 23 : 0x00400000u);
-        }
-        *reinterpret_cast<uint4*>(prow + ((g ^ swz) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        const float2 a = add_f32x2(acc[0], acc[1]);
+        lsum = fmaf(a.x + a.y, exp2i(e), lsum);
+        sts128(prow + ((g ^ swz) << 4), w[0], w[1], w[2], w[3]);
         sfw |= static_cast<uint32_t>(e + 127) << (8 * g);
       }
-      *reinterpret_cast<uint32_t*>(psf + (r & 31) * 16 + (r >> 5) * 4) = sfw;
+      l_run += lsum;
+      sts32(psf, sfw);
     } else {
+      // Emulated configs: p = exp2(x * qk - m), scaled by 448*6 (it cancels in
+      // O / l), block-quantised; l += sum of the dequantised P.
+      //   MXFP4: E8M0 2^e per 32, e = clamp(ceil(log2(max / 6)), -127, 127);
+      //   NVFP4: E4M3 per 16, s = e4m3(max(max / 6, 1e-8)).
+      // The block max of p * 2688 is round(max p * 2688) (rounding is monotone).
+      const float2 mneg2 = make_float2(-m_new, -m_new);
+      const float2 ps2 = make_float2(p.p_prescale, p.p_prescale);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t sfw = 0;
-        uint32_t w[8];
-#pragma unroll
-        for (int g4 = 0; g4 < 4; ++g4) {
-          const int g = h * 4 + g4;
-          float a8[8];
-#pragma unroll
-          for (int a = 0; a < 8; ++a) a8[a] = fmaxf(x[g * 16 + a], x[g * 16 + 8 + a]);
-          const float amax = fmaxf(fmaxf(fmaxf(a8[0], a8[1]), fmaxf(a8[2], a8[3])),
-                                   fmaxf(fmaxf(a8[4], a8[5]), fmaxf(a8[6], a8[7])));
-          const float scl = fmaxf(__fdiv_rn(amax, 6.0f), 1e-8f);
-          const uint32_t sb8 = e4m3_byte(scl);
-          const float sv = round_e4m3(scl);
-          const float inv = sv > 0.f ? __fdiv_rn(1.0f, sv) : 0.f;
-          const float2 inv2 = make_float2(inv, inv);
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            uint32_t word = 0;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int n = g * 16 + q * 8 + 2 * i;
-              const float2 sc = mul_f32x2(make_float2(x[n], x[n + 1]), inv2);
-              word |= cvt_e2m1x2(sc.x, sc.y) << (8 * i);
-            }
-            w[g4 * 2 + q] = word;
-          }
-          if (p.l_quant) lq += (e2m1_word_sum(w[g4 * 2]) + e2m1_word_sum(w[g4 * 2 + 1])) * sv;
-          sfw |= sb8 << (8 * g4);
-        }
-        *reinterpret_cast<uint4*>(prow + (((h * 2) ^ swz) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4*>(prow + (((h * 2 + 1) ^ swz) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
-        *reinterpret_cast<uint32_t*>(psf + h * SF_CHUNK + (r & 31) * 16 + (r >> 5) * 4) = sfw;
+      for (int i = 0; i < BN; i += 2) {
+        const float2 t = fma_f32x2(make_float2(x[i], x[i + 1]), qk2, mneg2);
+        const float2 v = mul_f32x2(make_float2(ex2_approx(t.x), ex2_approx(t.y)), ps2);
+        x[i] = v.x;
+        x[i + 1] = v.y;
       }
+      float lq = 0.f;
+      uint32_t sfw[2] = {0u, 0u};
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        constexpr int GS = BN / NG;
+        const float amax = __fmul_rn(ex2_approx(fmaf(gm[g], qk, -m_new)), p.p_prescale);
+        float inv, deq;
+        uint32_t sbyte;
+        if (kNV) {
+          const float scl = fmaxf(__fdiv_rn(amax, 6.0f), 1e-8f);
+          sbyte = e4m3_byte(scl);
+          deq = round_e4m3(scl);
+          inv = deq > 0.f ? __fdiv_rn(1.0f, deq) : 0.f;
+        } else {
+          const int e = mx_block_exp(amax);
+          sbyte = static_cast<uint32_t>(e + 127);
+          deq = exp2i(e);
+          inv = exp2i(-e);
+        }
+        const float2 inv2 = make_float2(inv, inv);
+        __half2 hs = __floats2half2_rn(0.f, 0.f);
+        uint32_t w[GS / 8];
+#pragma unroll
+        for (int q = 0; q < GS / 8; ++q) {
+          float v[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int n = g * GS + q * 8 + 2 * i;
+            const float2 sc = mul_f32x2(make_float2(x[n], x[n + 1]), inv2);
+            v[2 * i] = sc.x;
+            v[2 * i + 1] = sc.y;
+          }
+          uint32_t h[4];
+          w[q] = e2m1_roundtrip8(v, h);
+          hs = __hadd2(hs, hsum4(h));
+        }
+        lq = fmaf(__low2float(hs) + __high2float(hs), deq, lq);
+        if (kNV) {
+          // 16-byte chunk g/2 of the row holds blocks 2*(g/2), 2*(g/2)+1
+          sts64(prow + (((g >> 1) ^ swz) << 4) + (g & 1) * 8, w[0], w[1]);
+          sfw[g >> 2] |= sbyte << (8 * (g & 3));
+        } else {
+          sts128(prow + ((g ^ swz) << 4), w[0], w[1], w[2], w[3]);
+          sfw[0] |= sbyte << (8 * g);
+        }
+      }
+      l_run += lq;
+      sts32(psf, sfw[0]);
+      if (kNV) sts32(psf + SF_CHUNK, sfw[1]);
     }
-    if (p.l_quant) l_run += lq;
+    // O holds PV(0 .. j-1): rescale it by alpha once PV(j-1) has completed and
+    // before PV(j) is issued (p_full).  All four column chunks in flight at once.
+    if (ok && j >= 1) ok = mbar_wait(&bars->o_done[wg], (j - 1) & 1, status, 0x1303);
+    ok = __all_sync(0xffffffffu, ok);
+    if (__any_sync(0xffffffffu, grow)) {
+      tc_fence_after();
+      uint32_t u[HD / 32][32];
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) tmem_ld32(t_o + lane_base + 32 * c, u[c]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float2 v = mul_f32x2(make_float2(__uint_as_float(u[c][i]), __uint_as_float(u[c][i + 1])),
+                                     make_float2(alpha, alpha));
+          u[c][i] = __float_as_uint(v.x);
+          u[c][i + 1] = __float_as_uint(v.y);
+        }
+        tmem_st32(t_o + lane_base + 32 * c, u[c]);
+      }
+      tmem_st_wait();
+    }
     fence_proxy_async_smem();
     tc_fence_before();
     mbar_arrive(&bars->p_full[wg]);
@@ -342,13 +416,14 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
   }
 }
 
-template <bool kNV>
+template <int kMode>
 __global__ void __launch_bounds__(THREADS, 1)
 sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                        const __grid_constant__ CUtensorMap map_v, const uint8_t* __restrict__ qsf,
                        const uint8_t* __restrict__ ksf, const uint8_t* __restrict__ vsf,
-                       const __nv_bfloat16* __restrict__ ds, __nv_bfloat16* __restrict__ out, Params p,
+                       const float* __restrict__ ds, __nv_bfloat16* __restrict__ out, Params p,
                        int* status) {
+  constexpr bool kNV = kMode == kNvEmu;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
@@ -392,7 +467,7 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
   if (warp < 8) {
     reg_alloc_224();
     const int wg = warp >> 2;
-    if (wg < nq) softmax_wg<kNV>(smem, bars, tmem, p, wg, qtA + wg, bh, nkv, out, status);
+    if (wg < nq) softmax_wg<kMode>(smem, bars, tmem, p, wg, qtA + wg, bh, nkv, out, status);
   } else {
     reg_dealloc_56();
     if (warp == 9) {
@@ -444,8 +519,9 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
             if (!mbar_wait(&bars->p_full[w], t & 1, status, 0x1202)) return false;
             tc_fence_after();
             if (w == 0) cp_sf<kNV>(tmem + T_SFV, st + ST_VSF);
-            cp_sf<kNV>(tmem + T_SFP, smem + OFF_PSF + w * SF_TILE);
-            mma_k128<kNV>(tmem + T_O + w * 128, smem_desc_sw64(smem + OFF_P + w * CODE_TILE),
+            const int pb = 2 * w + (t & 1);  // P buffer of key tile t
+            cp_sf<kNV>(tmem + T_SFP, smem + OFF_PSF + pb * SF_TILE);
+            mma_k128<kNV>(tmem + T_O + w * 128, smem_desc_sw64(smem + OFF_P + pb * CODE_TILE),
                           smem_desc_sw64(st + ST_V), tmem + T_SFP, tmem + T_SFV, t != 0);
             tc_commit(&bars->o_done[w]);
           }
@@ -499,15 +575,18 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   if (int st = make_tmap_u8_2d(&mq, w.qc, BH * pr.Lp, 64, 64, 64, 128, 64)) return st;
   if (int st = make_tmap_u8_2d(&mk, w.kc, BH * pr.Lp, 64, 64, 64, 128, 64)) return st;
   if (int st = make_tmap_u8_2d(&mv, w.vt, BH * HD, pr.Lp / 2, pr.Lp / 2, 64, 128, 64)) return st;
-  static bool attr[2][64] = {{false}};
+  const int mode = pr.nv ? kNvEmu : (pr.emulated ? kMxEmu : kMxHw);
+  const void* fns[3] = {reinterpret_cast<const void*>(&sage3_fp4_flash_kernel<kMxHw>),
+                        reinterpret_cast<const void*>(&sage3_fp4_flash_kernel<kMxEmu>),
+                        reinterpret_cast<const void*>(&sage3_fp4_flash_kernel<kNvEmu>)};
+  static bool attr[3][64] = {{false}};
   int dev = 0;
   cudaGetDevice(&dev);
-  const void* fn = pr.nv ? reinterpret_cast<const void*>(&sage3_fp4_flash_kernel<true>)
-                         : reinterpret_cast<const void*>(&sage3_fp4_flash_kernel<false>);
-  if (dev >= 0 && dev < 64 && !attr[pr.nv][dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM_BYTES));
+  if (dev >= 0 && dev < 64 && !attr[mode][dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(fns[mode], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM_BYTES));
     if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "sage3 flash: smem attribute: %s", cudaGetErrorString(e));
-    attr[pr.nv][dev] = true;
+    attr[mode][dev] = true;
   }
   Params p;
   p.H = pr.H;
@@ -521,14 +600,16 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   p.causal = pr.causal;
   p.smoothing = pr.smoothing;
   p.p_prescale = pr.emulated ? 2688.0f : 1.0f;
-  p.l_quant = pr.emulated;
   dim3 grid(static_cast<unsigned>((p.T + 1) / 2), static_cast<unsigned>(BH));
-  if (pr.nv)
-    sage3_fp4_flash_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o, p,
-                                                                  status);
+  if (mode == kMxHw)
+    sage3_fp4_flash_kernel<kMxHw><<<grid, THREADS, SMEM_BYTES, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o, p,
+                                                                   status);
+  else if (mode == kMxEmu)
+    sage3_fp4_flash_kernel<kMxEmu><<<grid, THREADS, SMEM_BYTES, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o, p,
+                                                                    status);
   else
-    sage3_fp4_flash_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o,
-                                                                   p, status);
+    sage3_fp4_flash_kernel<kNvEmu><<<grid, THREADS, SMEM_BYTES, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o, p,
+                                                                    status);
   return check_launch("sage3 flash");
 }
 

@@ -57,6 +57,41 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
   return out;
 }
 
+// Eight values (pairs v[2i], v[2i+1]) -> RNE E2M1 codes packed into one word
+// (element 2i in the low nibble of byte i), without widening each byte.
+__device__ __forceinline__ uint32_t cvt_e2m1x8(float v0, float v1, float v2, float v3, float v4, float v5,
+                                               float v6, float v7) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(out)
+      : "f"(v0), "f"(v1), "f"(v2), "f"(v3), "f"(v4), "f"(v5), "f"(v6), "f"(v7));
+  return out;
+}
+
+// Eight values -> RNE E2M1 codes (returned packed) and the same codes decoded
+// back to four exact fp16x2 words h[0..3] (pair i in h[i]).
+__device__ __forceinline__ uint32_t e2m1_roundtrip8(const float (&v)[8], uint32_t (&h)[4]) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %8, %7;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %10, %9;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %12, %11;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %4, b3;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(out), "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
+  return out;
+}
+
 // RNE fp32 -> E4M3 (saturating) -> back to fp32, exactly.
 __device__ __forceinline__ float round_e4m3(float v) {
   uint32_t h2;

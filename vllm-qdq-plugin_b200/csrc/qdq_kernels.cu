@@ -144,20 +144,28 @@ mxfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
       const float inv = __uint_as_float(static_cast<uint32_t>(254 - e) << 23);  // 1/scale, exact
       const float sc = F::mx_scale(e);
       const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-      uint32_t o[4];
-      uint32_t code_word = 0;
+      float sv[8];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float2 v = mul_f32x2(make_float2(F::lo(w[j]), F::hi(w[j])), make_float2(inv, inv));
-        uint32_t byte = cvt_e2m1x2(v.x, v.y);
-        const uint32_t h = e2m1x2_to_f16x2(byte);
-        const float2 d = mul_f32x2(make_float2(f16lo(h), f16hi(h)), make_float2(sc, sc));
+        const float2 t = mul_f32x2(make_float2(F::lo(w[j]), F::hi(w[j])), make_float2(inv, inv));
+        sv[2 * j] = t.x;
+        sv[2 * j + 1] = t.y;
+      }
+      uint32_t h[4];
+      uint32_t code_word = e2m1_roundtrip8(sv, h);
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 d = mul_f32x2(make_float2(f16lo(h[j]), f16hi(h[j])), make_float2(sc, sc));
         o[j] = F::pack(d.x, d.y);
-        if (F::kScaleCanBeZero && e == 0) {
+      }
+      if (F::kScaleCanBeZero && e == 0) {
+        code_word = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
           o[j] = fp16_zero_scale_word(w[j]);
-          byte = zero_codes_of(o[j]);
+          code_word |= zero_codes_of(o[j]) << (8 * j);
         }
-        code_word |= byte << (8 * j);
       }
       if (ok[u]) {
         if (kY) st_stream(reinterpret_cast<uint4*>(y + yo[u]), make_uint4(o[0], o[1], o[2], o[3]));
@@ -259,12 +267,34 @@ __device__ __forceinline__ uint32_t nv_codes(float xa, float xb, float out_scale
   return byte;
 }
 
+// With out_scale >= 2^-16 no nonzero bf16 or fp16 input (smallest magnitude
+// 2^-133, resp. 2^-24) has a product below the smallest fp32 subnormal
+// 2^-149, so the only zero products are those of x == +-0.
+constexpr float kNoUnderflowScale = 0x1p-16f;
+
+// x * out_scale for 8 elements, with a zero product made +0 (see nv_codes):
+// the product is formed as fma(x, out_scale, zero) with `zero` = +0.0 passed
+// in as a kernel argument (an operand the compiler cannot treat as a
+// constant), so an exact -0 product becomes -0 + +0 = +0 under RN while every
+// other product is rounded exactly once, as by a plain multiply.
+__device__ __forceinline__ void nv_scale8(const uint32_t (&w)[4], float out_scale, float zero, float (&sv)[8],
+                                          bool fp16) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float a = fp16 ? f16lo(w[j]) : bf16lo(w[j]);
+    const float b = fp16 ? f16hi(w[j]) : bf16hi(w[j]);
+    const float2 t = fma_f32x2(make_float2(a, b), make_float2(out_scale, out_scale), make_float2(zero, zero));
+    sv[2 * j] = t.x;
+    sv[2 * j + 1] = t.y;
+  }
+}
+
 template <int kDtype, bool kContig, bool kY, bool kCodes, bool kScales>
 __global__ void __launch_bounds__(kThreads)
 nvfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
                  uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
                  const float* __restrict__ gsp, uint32_t cpr, uint64_t total, int64_t ldx,
-                 int64_t ldy, int64_t ldc, int64_t lds) {
+                 int64_t ldy, int64_t ldc, int64_t lds, float zero) {
   using F = Fmt<kDtype>;
   const float gs = __ldg(gsp);
   const float rgs = zero_safe_recip(gs);
@@ -300,14 +330,25 @@ nvfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
       amax = max(amax, __shfl_xor_sync(kFull, amax, 1));
       const NvGroup g = nv_group(F::amax_value(amax), gs, rgs);
       const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      uint32_t h[4];
+      uint32_t code_word;
+      if (g.out_scale >= kNoUnderflowScale) {
+        float sv[8];
+        nv_scale8(w, g.out_scale, zero, sv, kDtype == QDQ_DTYPE_FP16);
+        code_word = e2m1_roundtrip8(sv, h);
+      } else {
+        code_word = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t byte = nv_codes(F::lo(w[j]), F::hi(w[j]), g.out_scale);
+          code_word |= byte << (8 * j);
+          h[j] = e2m1x2_to_f16x2(byte);
+        }
+      }
       uint32_t o[4];
-      uint32_t code_word = 0;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint32_t byte = nv_codes(F::lo(w[j]), F::hi(w[j]), g.out_scale);
-        code_word |= byte << (8 * j);
-        const uint32_t h = e2m1x2_to_f16x2(byte);
-        const float2 d = mul_f32x2(make_float2(f16lo(h), f16hi(h)), make_float2(g.deq, g.deq));
+        const float2 d = mul_f32x2(make_float2(f16lo(h[j]), f16hi(h[j])), make_float2(g.deq, g.deq));
         o[j] = F::pack(d.x, d.y);
       }
       if (ok[u]) {
@@ -517,11 +558,11 @@ extern "C" int qdq_nvfp4(const void* x, void* y, void* codes, void* scales, cons
   if (vec && (contig || total < (1ull << 32))) {
     const int grid = grid_for(total, kThreads * kUnroll);
     if (dtype == QDQ_DTYPE_BF16) {
-      if (contig) dispatch_nv_vec<QDQ_DTYPE_BF16, true>(o, grid, s, xp, yp, cp, sp, global_scale, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
-      else dispatch_nv_vec<QDQ_DTYPE_BF16, false>(o, grid, s, xp, yp, cp, sp, global_scale, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
+      if (contig) dispatch_nv_vec<QDQ_DTYPE_BF16, true>(o, grid, s, xp, yp, cp, sp, global_scale, (uint32_t)cpr, total, ldx, ldy, ldc, lds, 0.0f);
+      else dispatch_nv_vec<QDQ_DTYPE_BF16, false>(o, grid, s, xp, yp, cp, sp, global_scale, (uint32_t)cpr, total, ldx, ldy, ldc, lds, 0.0f);
     } else {
-      if (contig) dispatch_nv_vec<QDQ_DTYPE_FP16, true>(o, grid, s, xp, yp, cp, sp, global_scale, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
-      else dispatch_nv_vec<QDQ_DTYPE_FP16, false>(o, grid, s, xp, yp, cp, sp, global_scale, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
+      if (contig) dispatch_nv_vec<QDQ_DTYPE_FP16, true>(o, grid, s, xp, yp, cp, sp, global_scale, (uint32_t)cpr, total, ldx, ldy, ldc, lds, 0.0f);
+      else dispatch_nv_vec<QDQ_DTYPE_FP16, false>(o, grid, s, xp, yp, cp, sp, global_scale, (uint32_t)cpr, total, ldx, ldy, ldc, lds, 0.0f);
     }
   } else {
     const uint64_t ngroups = static_cast<uint64_t>(M) * static_cast<uint64_t>(K / 16);
