@@ -176,12 +176,20 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
 
 VARIANTS = {"mxfp4_hw": (False, False), "mxfp4": (False, True), "nvfp4": (True, True)}
 
+# Key tile of the reference's online softmax per config: the mxfp4_hw kernel
+# launches with BLOCK_N = 64 (sage3/mxfp4_hw_kernel.py:437); the emulated
+# configs' attention kernel requires tile_size_k = 128 (attention_kernel.py:249-253).
+REF_BLOCK_N = {"mxfp4_hw": 64, "mxfp4": 128, "nvfp4": 128}
+
 
 def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_scale: float,
-              block_n: int = 128, causal: bool = False, smoothing: bool = True,
+              block_n: int | None = None, causal: bool = False, smoothing: bool = True,
               mask_padding: bool = True, config: str = "mxfp4_hw") -> np.ndarray:
-    """q/k/v: uint16 bf16 bit patterns [L, H, D] (NHD with B = 1); returns O [L, H, D]."""
+    """q/k/v: uint16 bf16 bit patterns [L, H, D] (NHD with B = 1); returns O [L, H, D].
+    block_n defaults to the reference's key tile for the config (REF_BLOCK_N)."""
     nv, emulated = VARIANTS[config]
+    if block_n is None:
+        block_n = REF_BLOCK_N[config]
     L, H, D = q_bits.shape
     out = np.zeros((L, H, D))
     for h in range(H):
