@@ -9,14 +9,21 @@
 // MXFP4-representable, the activation can be fed to kind::mxf4 MMAs as codes
 // + scales, and every product is the same exact value Marlin forms.
 //
-// Kernel structure (one 128 x 256 output tile per CTA, 4 warps):
+// Kernel structure: persistent, one CTA per SM walking 128 x 256 output
+// tiles (tile t: m block t % num_m, n block t / num_m, so the CTAs in flight
+// share W tiles in L2), 10 warps:
 //   warp 0 / one lane   TMA producer: A and W code tiles (128-byte swizzle)
 //                       and their scale-factor chunks (bulk copies) into a
-//                       4-stage shared-memory ring
-//   warp 1 / one lane   MMA issuer: tcgen05.cp scale factors smem -> TMEM,
-//                       4 x tcgen05.mma.kind::mxf4 (K = 64 each) per stage,
-//                       tcgen05.commit frees the stage
-//   warps 0-3           epilogue: TMEM accumulator -> registers -> bf16 -> global
+//                       4-stage shared-memory ring; it runs ahead across tiles
+//   warp 1 / one lane   MMA issuer: waits until the epilogue has drained the
+//                       TMEM accumulator, then per stage tcgen05.cp scale
+//                       factors smem -> TMEM and 4 x tcgen05.mma.kind::mxf4
+//                       (K = 64 each); tcgen05.commit frees the stage and,
+//                       after the last stage, hands the tile to the epilogue
+//   warps 2-9           epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 and
+//                       columns 128 ((w - 2) / 4) .. +127 into registers, frees
+//                       the accumulator (the next tile's MMAs start), then adds
+//                       the bias, converts and stores while they run
 //
 // Scale factors use the tcgen05 "tiled" layout in global memory (see
 // qdq_sf_tile): rows are grouped by 128 and K-scales by 4 into 512-byte
@@ -46,13 +53,16 @@ constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;          // 256 fp32 columns
 constexpr int SFA_COL = 256;        // 8 columns (2 K-chunks x 4)
 constexpr int SFB_COL = 272;        // 16 columns (2 K-chunks x 2 row blocks x 4)
-constexpr int THREADS = 128;
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 32 * (2 + EPI_WARPS);
 constexpr uint32_t IDESC = idesc_mxf4(BM, BN, true);
 
 struct __align__(8) Barriers {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
-  uint64_t acc_full;
+  uint64_t acc_full;    // MMA -> epilogue: the tile's accumulator is complete
+  uint64_t acc_empty;   // epilogue -> MMA: the accumulator has been read out
+  uint64_t drain;
   uint32_t tmem_base;
   int abort;
 };
@@ -90,8 +100,9 @@ mxf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   Barriers* bars = reinterpret_cast<Barriers*>(smem + STAGES * STAGE_BYTES);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m_blk = blockIdx.y;
-  const int n_blk = blockIdx.x;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
   const int num_kt = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -100,6 +111,8 @@ mxf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       mbar_init(&bars->empty[s], 1);
     }
     mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, 32 * EPI_WARPS);
+    mbar_init(&bars->drain, 1);
     bars->abort = 0;
     fence_barrier_init();
     prefetch_tmap(&tmap_a);
@@ -114,102 +127,131 @@ mxf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 0 && elect_one()) {
+  if (warp == 0) {
     // ---------------- producer
-    int issued = 0;
-    for (int kt = 0; kt < num_kt; ++kt) {
-      const int s = kt % STAGES;
-      if (!mbar_wait(&bars->empty[s], ((kt / STAGES) & 1) ^ 1, status, 0x101)) {
-        bars->abort = 1;
-        break;
+    if (elect_one()) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int m_blk = tile % num_m, n_blk = tile / num_m;
+        const bool second_rb = (n_blk * 2 + 1) * 128 < N;
+        for (int kt = 0; kt < num_kt; ++kt, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&bars->empty[s], ((it / STAGES) & 1) ^ 1, status, 0x101)) {
+            bars->abort = 1;
+            ok = false;
+            break;
+          }
+          if (*(volatile int*)&bars->abort) { ok = false; break; }
+          uint8_t* st = smem + s * STAGE_BYTES;
+          mbar_arrive_expect_tx(&bars->full[s], A_BYTES + B_BYTES + SFA_BYTES + (second_rb ? 2048 : 1024));
+          tma_load_2d(st, &tmap_a, kt * BKB, m_blk * BM, &bars->full[s]);
+          tma_load_2d(st + A_BYTES, &tmap_b, kt * BKB, n_blk * BN, &bars->full[s]);
+          bulk_load(st + A_BYTES + B_BYTES, sfa + (static_cast<int64_t>(m_blk) * kchunks + 2 * kt) * 512,
+                    1024, &bars->full[s]);
+          bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES,
+                    sfb + (static_cast<int64_t>(2 * n_blk) * kchunks + 2 * kt) * 512, 1024, &bars->full[s]);
+          if (second_rb)
+            bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES + 1024,
+                      sfb + (static_cast<int64_t>(2 * n_blk + 1) * kchunks + 2 * kt) * 512, 1024,
+                      &bars->full[s]);
+        }
       }
-      if (*(volatile int*)&bars->abort) break;
-      uint8_t* st = smem + s * STAGE_BYTES;
-      const bool second_rb = (n_blk * 2 + 1) * 128 < N;
-      mbar_arrive_expect_tx(&bars->full[s], A_BYTES + B_BYTES + SFA_BYTES + (second_rb ? 2048 : 1024));
-      tma_load_2d(st, &tmap_a, kt * BKB, m_blk * BM, &bars->full[s]);
-      tma_load_2d(st + A_BYTES, &tmap_b, kt * BKB, n_blk * BN, &bars->full[s]);
-      bulk_load(st + A_BYTES + B_BYTES, sfa + (static_cast<int64_t>(m_blk) * kchunks + 2 * kt) * 512,
-                1024, &bars->full[s]);
-      bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES,
-                sfb + (static_cast<int64_t>(2 * n_blk) * kchunks + 2 * kt) * 512, 1024, &bars->full[s]);
-      if (second_rb)
-        bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES + 1024,
-                  sfb + (static_cast<int64_t>(2 * n_blk + 1) * kchunks + 2 * kt) * 512, 1024,
-                  &bars->full[s]);
-      ++issued;
+      // Drain: every issued copy has landed before the CTA may exit.
+      for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+        mbar_wait(&bars->full[j % STAGES], (j / STAGES) & 1, status, 0x102);
     }
-    // Drain: every issued copy has landed before the CTA may exit.
-    for (int kt = (issued > STAGES ? issued - STAGES : 0); kt < issued; ++kt)
-      mbar_wait(&bars->full[kt % STAGES], (kt / STAGES) & 1, status, 0x102);
-  } else if (warp == 1 && elect_one()) {
+  } else if (warp == 1) {
     // ---------------- MMA issuer
-    for (int kt = 0; kt < num_kt; ++kt) {
-      const int s = kt % STAGES;
-      if (!mbar_wait(&bars->full[s], (kt / STAGES) & 1, status, 0x201)) {
-        bars->abort = 1;
-        break;
+    if (elect_one()) {
+      int it = 0, i = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++i) {
+        // the epilogue has read the previous tile's accumulator out of TMEM
+        if (i > 0 && !mbar_wait(&bars->acc_empty, (i - 1) & 1, status, 0x202)) { ok = false; break; }
+        tc_fence_after();
+        for (int kt = 0; kt < num_kt; ++kt, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&bars->full[s], (it / STAGES) & 1, status, 0x201)) { ok = false; break; }
+          if (*(volatile int*)&bars->abort) { ok = false; break; }
+          tc_fence_after();
+          uint8_t* st = smem + s * STAGE_BYTES;
+          const uint8_t* sa = st + A_BYTES + B_BYTES;
+          const uint8_t* sb = sa + SFA_BYTES;
+          // scale factors: chunk j (K-scales 4j..4j+3 of this stage) of each 128-row block
+          tmem_cp_sf(tmem + SFA_COL + 0, smem_desc_sf(sa));
+          tmem_cp_sf(tmem + SFA_COL + 4, smem_desc_sf(sa + 512));
+          tmem_cp_sf(tmem + SFB_COL + 0, smem_desc_sf(sb));             // rows 0-127,   j = 0
+          tmem_cp_sf(tmem + SFB_COL + 8, smem_desc_sf(sb + 512));       // rows 0-127,   j = 1
+          tmem_cp_sf(tmem + SFB_COL + 4, smem_desc_sf(sb + 1024));      // rows 128-255, j = 0
+          tmem_cp_sf(tmem + SFB_COL + 12, smem_desc_sf(sb + 1536));     // rows 128-255, j = 1
+          const uint64_t da = smem_desc_sw128(st);
+          const uint64_t db = smem_desc_sw128(st + A_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 64; ++kk) {
+            const uint32_t j = kk >> 1, sf_id = (kk & 1) * 2;
+            const uint32_t sfa_addr = (tmem + SFA_COL + 4 * j) | (sf_id << 30);
+            const uint32_t sfb_addr = (tmem + SFB_COL + 8 * j) | (sf_id << 30);
+            // K step of 64 E2M1 = 32 bytes inside the 128-byte swizzled row
+            mma_mxf4(tmem + ACC_COL, da + ((kk * 32) >> 4), db + ((kk * 32) >> 4),
+                     idesc_with_sf_ids(IDESC, sf_id, sf_id), sfa_addr, sfb_addr, (kt | kk) != 0);
+          }
+          tc_commit(&bars->empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&bars->acc_full);
       }
-      if (*(volatile int*)&bars->abort) break;
+      if (!ok) bars->abort = 1;
+      // every issued tcgen05 op has completed before TMEM is released
+      tc_commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, status, 0x203);
+    }
+  } else {
+    // ---------------- epilogue: TMEM lanes 32 (warp % 4).. = tile rows, columns 128 h ..
+    const int q = warp & 3, h = (warp - 2) >> 2;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ACC_COL + h * 128;
+    bool ok = true;
+    int i = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
+      const int m_blk = tile % num_m, n_blk = tile / num_m;
+      if (ok) ok = mbar_wait(&bars->acc_full, i & 1, status, 0x301);
+      ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
       tc_fence_after();
-      uint8_t* st = smem + s * STAGE_BYTES;
-      const uint8_t* sa = st + A_BYTES + B_BYTES;
-      const uint8_t* sb = sa + SFA_BYTES;
-      // scale factors: chunk j (K-scales 4j..4j+3 of this stage) of each 128-row block
-      tmem_cp_sf(tmem + SFA_COL + 0, smem_desc_sf(sa));
-      tmem_cp_sf(tmem + SFA_COL + 4, smem_desc_sf(sa + 512));
-      tmem_cp_sf(tmem + SFB_COL + 0, smem_desc_sf(sb));             // rows 0-127,   j = 0
-      tmem_cp_sf(tmem + SFB_COL + 8, smem_desc_sf(sb + 512));       // rows 0-127,   j = 1
-      tmem_cp_sf(tmem + SFB_COL + 4, smem_desc_sf(sb + 1024));      // rows 128-255, j = 0
-      tmem_cp_sf(tmem + SFB_COL + 12, smem_desc_sf(sb + 1536));     // rows 128-255, j = 1
-      const uint64_t da = smem_desc_sw128(st);
-      const uint64_t db = smem_desc_sw128(st + A_BYTES);
+      uint32_t r[4][32];
 #pragma unroll
-      for (int kk = 0; kk < BK / 64; ++kk) {
-        const uint32_t j = kk >> 1, sf_id = (kk & 1) * 2;
-        const uint32_t sfa_addr = (tmem + SFA_COL + 4 * j) | (sf_id << 30);
-        const uint32_t sfb_addr = (tmem + SFB_COL + 8 * j) | (sf_id << 30);
-        // K step of 64 E2M1 = 32 bytes inside the 128-byte swizzled row
-        mma_mxf4(tmem + ACC_COL, da + ((kk * 32) >> 4), db + ((kk * 32) >> 4),
-                 idesc_with_sf_ids(IDESC, sf_id, sf_id), sfa_addr, sfb_addr, (kt | kk) != 0);
+      for (int c = 0; c < 4; ++c) tmem_ld32(taddr + 32 * c, r[c]);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&bars->acc_empty);  // the next tile's MMAs may overwrite the accumulator
+      if (!ok || *(volatile int*)&bars->abort || num_kt == 0) continue;
+      const int row = m_blk * BM + q * 32 + lane;
+      if (row >= M) continue;
+      const int n0 = n_blk * BN + h * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int ncols = min(32, N - n0 - 32 * c);
+        if (ncols <= 0) continue;
+        T* crow = C + static_cast<int64_t>(row) * ldc + n0 + 32 * c;
+        float v[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[c][e]);
+        if (bias != nullptr) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (e < ncols) v[e] += O::load(bias + n0 + 32 * c + e);
+        }
+        if (ncols == 32 && (reinterpret_cast<uintptr_t>(crow) & 15) == 0) {
+          uint4* dst = reinterpret_cast<uint4*>(crow);
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4)
+            dst[w4] = make_uint4(O::pack(v[8 * w4 + 0], v[8 * w4 + 1]), O::pack(v[8 * w4 + 2], v[8 * w4 + 3]),
+                                 O::pack(v[8 * w4 + 4], v[8 * w4 + 5]), O::pack(v[8 * w4 + 6], v[8 * w4 + 7]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (e < ncols) crow[e] = O::one(v[e]);
+        }
       }
-      tc_commit(&bars->empty[s]);
-    }
-    tc_commit(&bars->acc_full);  // also on abort: the epilogue waits for issued MMAs
-  }
-  __syncwarp();
-
-  // ---------------- epilogue (all 4 warps): TMEM lanes 32w..32w+31 = tile rows
-  const bool acc_ok = mbar_wait(&bars->acc_full, 0, status, 0x301);
-  tc_fence_after();
-  const bool do_store = acc_ok && !*(volatile int*)&bars->abort && num_kt > 0;
-  const int row = m_blk * BM + warp * 32 + lane;
-  const int n0 = n_blk * BN;
-#pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 32) {
-    uint32_t r[32];
-    tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + ACC_COL + c0, r);
-    tmem_ld_wait();
-    if (!do_store || row >= M) continue;
-    T* crow = C + static_cast<int64_t>(row) * ldc + n0 + c0;
-    const int ncols = min(32, N - n0 - c0);
-    if (ncols <= 0) continue;
-    float v[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-    if (bias != nullptr) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (i < ncols) v[i] += O::load(bias + n0 + c0 + i);
-    }
-    if (ncols == 32 && (reinterpret_cast<uintptr_t>(crow) & 15) == 0) {
-      uint4* dst = reinterpret_cast<uint4*>(crow);
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        dst[q] = make_uint4(O::pack(v[8 * q + 0], v[8 * q + 1]), O::pack(v[8 * q + 2], v[8 * q + 3]),
-                            O::pack(v[8 * q + 4], v[8 * q + 5]), O::pack(v[8 * q + 6], v[8 * q + 7]));
-    } else {
-      for (int i = 0; i < ncols; ++i) crow[i] = O::one(v[i]);
     }
   }
 
@@ -344,7 +386,9 @@ extern "C" int fp4_gemm_mxf4(const void* a_codes, const void* a_sf_tiled, const 
     attr_set[out_dtype][dev] = true;
   }
   const int kchunks = static_cast<int>(((K / 32) + 7) / 8 * 8 / 4);
-  dim3 grid(static_cast<unsigned>((N + BN - 1) / BN), static_cast<unsigned>((M + BM - 1) / BM));
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int sms = device_sm_count();
+  dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, sms > 0 ? sms : 148)));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto* sfa = static_cast<const uint8_t*>(a_sf_tiled);
   auto* sfb = static_cast<const uint8_t*>(w_sf_tiled);
