@@ -435,45 +435,60 @@ def run_gemm(args, wl, world, rank, dev, dist) -> None:
     n, k = codes.shape[0], codes.shape[1] * 2
     a = a_cpu.to(dev)
     w = prepare_mxfp4_weight(codes.to(dev), scales.to(dev))
+    # Rotating weight copies: a step reads its W again only after >= 3x the
+    # 126 MB L2 of other weights has streamed through, so every step reads W
+    # from HBM (the decode case) without an L2 flush inside the step stream.
+    w_bytes = w.codes.numel() + w.sf_tiled.numel()
+    n_w = max(1, -(-3 * L2_BYTES // w_bytes))
+    ws_list = [w] + [prepare_mxfp4_weight(codes.to(dev), scales.to(dev)) for _ in range(n_w - 1)]
     lib = _native.lib()
     ws = torch.empty((lib.fp4_linear_workspace_bytes(m, k),), dtype=torch.uint8, device=dev)
     out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev)
-    sp = stream.cuda_stream
-    # an L2 flush buffer (> 126 MB L2) written between timed steps
-    flush = torch.empty((256 << 20,), dtype=torch.uint8, device=dev)
     launches = [0]
+    per_call = 1 if m <= 64 else 3  # one fused launch for M <= 64, else quantise + scale tiling + GEMM
 
-    def step():
+    def step(i=0, sp=None):
+        wi = ws_list[i % n_w]
         _native.check("fp4_linear_mxf4", lib.fp4_linear_mxf4(
-            a.data_ptr(), k, 0, w.codes.data_ptr(), w.sf_tiled.data_ptr(), None, out.data_ptr(),
-            m, n, k, k // 2, n, ws.data_ptr(), ws.numel(), sp))
-        launches[0] += 3  # quantise, scale tiling, GEMM
+            a.data_ptr(), k, 0, wi.codes.data_ptr(), wi.sf_tiled.data_ptr(), None, out.data_ptr(),
+            m, n, k, k // 2, n, ws.data_ptr(), ws.numel(),
+            sp if sp is not None else torch.cuda.current_stream(dev).cuda_stream))
+        launches[0] += per_call
 
     def barrier():
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    for _ in range(args.warmup):
-        step()
+    for i in range(args.warmup):
+        step(i)
+    barrier()
+    # The timed steps are captured once in a CUDA graph (as vLLM runs decode),
+    # so host launch overhead stays out of the device time; W rotates per step.
+    steps = args.steps
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(graph, stream=cap):
+            for i in range(steps):
+                step(i, cap.cuda_stream)
+    stream.wait_stream(cap)
+    graph.replay()  # warm replay (first replay uploads the graph)
     barrier()
     sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))).start() if rank == 0 else None
     time.sleep(0.3 if sampler else 0)
     barrier()
-    launches[0] = 0
-    steps = args.steps
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(steps)]
+    launches[0] = steps * per_call
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_wall0 = time.time()
-    for i in range(steps):
-        flush.zero_()
-        ev[i][0].record(stream)
-        step()
-        ev[i][1].record(stream)
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
     barrier()
     t_wall1 = time.time()
-    ms = sum(e0.elapsed_time(e1) for e0, e1 in ev)
+    ms = e0.elapsed_time(e1)
     if dist is not None:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -511,7 +526,8 @@ def run_gemm(args, wl, world, rank, dev, dist) -> None:
             "vs_baseline": None, "dtype": "e2m1 x e2m1 (E8M0 scales), fp32 accumulate, bf16 out",
             "data": "synthetic (seeded, BASELINE config-3 distributions)",
             "config": {"workload": wl["config"], "M": m, "N": n, "K": k,
-                       "l2": "256 MB buffer written between timed steps (L2 flush)"},
+                       "l2": (f"{n_w} rotating weight copies ({w_bytes / 1e6:.0f} MB each): a step re-reads "
+                              "its W only after >= 3x the 126 MB L2; steps replayed from one CUDA graph")},
             "e2e": {"value": round(e2e, 1), "unit": "TFLOP/s", "h2d_bytes_per_step": m * k * 2,
                     "d2h_bytes_per_step": m * n * 2,
                     "path": "vllm_qdq_plugin.gemm.mxfp4_linear on pinned host buffers"},

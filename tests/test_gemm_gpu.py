@@ -54,6 +54,47 @@ def test_fused_linear_matches_qdq_marlin_oracle(cuda_device, m, n, k):
     _check(out, exact, absum, f"linear {m}x{n}x{k}")
 
 
+@pytest.mark.parametrize("m,n,k", [(1, 14336, 4096), (3, 300, 4128), (17, 512, 1024), (33, 640, 512),
+                                   (64, 1024, 2048)])
+def test_decode_path_matches_oracle(cuda_device, m, n, k):
+    """M <= 64 runs the one-launch kernel that quantises the activation inside
+    the GEMM producer (swap-AB tcgen05 MMAs, W rows on the M side)."""
+    from vllm_qdq_plugin.gemm import mxfp4_linear, prepare_mxfp4_weight
+    a, codes, scales = _inputs(m, n, k, seed=m * 7 + n + k)
+    w = prepare_mxfp4_weight(torch.from_numpy(codes).to(cuda_device),
+                             torch.from_numpy(scales).to(cuda_device))
+    out = mxfp4_linear(a.to(cuda_device), w)
+    abits = a.view(torch.int16).numpy().view(np.uint16)
+    exact, absum = og.qdq_linear_exact(abits, codes, scales)
+    _check(out, exact, absum, f"decode {m}x{n}x{k}")
+    from vllm_qdq_plugin import _native
+    assert _native.device_status() == 0
+
+
+def test_decode_path_fp16_bias_and_codes_path(cuda_device):
+    """fp16 activation with bias on the decode path, and agreement with the
+    three-launch path (QDQ codes -> tiled scales -> GEMM) within the fp32
+    accumulation bound."""
+    from vllm_qdq_plugin.gemm import mxfp4_gemm_codes, mxfp4_linear, prepare_mxfp4_weight
+    from vllm_qdq_plugin.qdq import mxfp4_quantize
+    m, n, k = 5, 384, 1024
+    a, codes, scales = _inputs(m, n, k, seed=9, dtype=torch.float16)
+    bias = torch.randn(n, generator=torch.Generator().manual_seed(10)).to(torch.float16)
+    w = prepare_mxfp4_weight(torch.from_numpy(codes).to(cuda_device),
+                             torch.from_numpy(scales).to(cuda_device))
+    out = mxfp4_linear(a.to(cuda_device), w, bias.to(cuda_device))
+    abits = a.view(torch.int16).numpy().view(np.uint16)
+    exact, absum = og.qdq_linear_exact(abits, codes, scales, bias.float().numpy(), fp16=True)
+    _check(out, exact, absum + np.abs(bias.float().numpy())[None, :], "decode fp16 + bias")
+    ab, _, _ = _inputs(m, n, k, seed=9)
+    ad = ab.to(cuda_device)
+    ac, asf = mxfp4_quantize(ad)
+    ref = mxfp4_gemm_codes(ac, asf, w).float().cpu().numpy().astype(np.float64)
+    exact_b, absum_b = og.qdq_linear_exact(ab.view(torch.int16).numpy().view(np.uint16), codes, scales)
+    got = mxfp4_linear(ad, w).float().cpu().numpy().astype(np.float64)
+    assert (np.abs(got - ref) <= 2 * (REL * np.abs(exact_b) + ACC * absum_b) + 1e-30).all()
+
+
 def test_fp16_activation_and_bias(cuda_device):
     from vllm_qdq_plugin.gemm import mxfp4_linear, prepare_mxfp4_weight
     m, n, k = 200, 512, 1024

@@ -25,6 +25,11 @@ void set_error(const char* fmt, ...);
 int fail(int status, const char* fmt, ...);
 int check_launch(const char* what);
 int device_sm_count();  // SM count of the current device (cached)
+// Fused small-M MXFP4 linear (gemm_decode.cu): activation quantisation inside
+// the GEMM producer, one launch; M in [1, 64], 16-byte aligned activation rows.
+int fp4_linear_decode(const void* a, int64_t lda, int dtype, const void* w_codes, const void* w_sf_tiled,
+                      const void* bias, void* c, int64_t M, int64_t N, int64_t K, int64_t ldw_bytes,
+                      int64_t ldc, void* stream);
 // Device address of the library's status word on the current device (kernels
 // record bounded-wait timeouts there); nullptr + error message on failure.
 int* device_status_ptr();

@@ -1,0 +1,288 @@
+// Fused MXFP4 linear for small M (decode and small batches), one launch:
+//   C[M, N] = mxfp4(A)[M, K] . W[N, K]^T (+ bias[N]),  fp32 accumulation,
+// with A bf16/fp16 and W E2M1 codes + E8M0 scales in the tiled layout of
+// qdq_sf_tile.  The activation is quantised inside the GEMM's producer with
+// the same group rule as the QDQ kernel (mx_quant.cuh), so the products are
+// those of the reference's mxfp4_qdq(A) against W (reference:
+// src/vllm_qdq_plugin/patch.py:51-57 + vllm/_custom_ops.py:1277 marlin_gemm).
+//
+// "Swap AB": the tcgen05 MMA's M side is 128 rows of W and its N side the
+// activation rows, padded to NA = 16, 32 or 64.  One CTA per 128 rows of W
+// streams that slice of W once (N / 128 CTAs: 112 for N = 14336), so the
+// kernel is bound by HBM reading W, not by the tensor pipe.
+//
+// CTA, 6 warps:
+//   warp 0 / one lane   TMA producer: W code tile [128 rows x 128 B] (128-byte
+//                       swizzle), its scale chunks and the raw [NA, 256]
+//                       bf16/fp16 slice of A into a ring of 3-7 stages
+//   warp 1 / one lane   MMA issuer: per stage 4 x tcgen05.mma.kind::mxf4
+//                       (M = 128, N = NA, K = 64), commit frees the stage
+//   warps 2-5           activation quantiser (the stage's raw A slice in
+//                       shared memory -> E2M1 codes in the swizzled operand
+//                       layout + E8M0 scales in the scale-chunk layout), then
+//                       the epilogue (TMEM lanes = W rows, columns = activation rows)
+#include "mx_quant.cuh"
+#include "sm100.cuh"
+
+namespace qdqb200 {
+namespace {
+
+using namespace sm100;
+
+constexpr int DBM = 128;                 // W rows per CTA (UMMA M)
+constexpr int DBK = 256;                 // K elements per stage
+constexpr int DBKB = DBK / 2;            // code bytes per row per stage (one 128-byte swizzle row)
+constexpr int NA_MAX = 64;               // activation rows per launch (UMMA N)
+constexpr int W_TILE = DBM * DBKB;       // 16 KB
+constexpr int SF_STAGE = 1024;           // two 512-byte scale chunks (8 scales per row)
+constexpr int D_THREADS = 192;
+constexpr int D_TMEM_COLS = 128;
+constexpr uint32_t T_ACC = 0, T_SFW = 64, T_SFA = 72;
+
+// Stage layout for NA activation rows: W codes | A codes | W scales | A scales | raw A.
+template <int kNA>
+struct DLayout {
+  static constexpr int A_TILE = kNA * DBKB;
+  static constexpr int RAW = kNA * DBK * 2;
+  static constexpr int ST_W = 0, ST_A = W_TILE, ST_SFW = W_TILE + A_TILE, ST_SFA = ST_SFW + SF_STAGE,
+                       ST_RAW = ST_SFA + SF_STAGE;
+  static constexpr int STAGE = (ST_RAW + RAW + 1023) / 1024 * 1024;
+  static constexpr int STAGES = kNA == 16 ? 7 : (kNA == 32 ? 5 : 3);
+};
+
+struct __align__(8) DBars {
+  uint64_t raw[8];     // W, its scales and the raw A slice landed (1 arrival + tx)
+  uint64_t ready[8];   // the activation slice is quantised (128 arrivals)
+  uint64_t empty[8];   // the stage's MMAs completed
+  uint64_t acc_full;
+  uint32_t tmem_base;
+  int abort;
+};
+template <int kNA>
+constexpr size_t d_smem_bytes() {
+  return 1024 + static_cast<size_t>(DLayout<kNA>::STAGES) * DLayout<kNA>::STAGE + sizeof(DBars);
+}
+static_assert(d_smem_bytes<16>() <= 227 * 1024 && d_smem_bytes<32>() <= 227 * 1024 &&
+              d_smem_bytes<64>() <= 227 * 1024, "decode stages exceed shared memory");
+
+template <bool kF16>
+struct DOut {
+  using T = __nv_bfloat16;
+  __device__ static float load(const T* p) { return __bfloat162float(*p); }
+  __device__ static T one(float a) { return __float2bfloat16_rn(a); }
+};
+template <>
+struct DOut<true> {
+  using T = __half;
+  __device__ static float load(const T* p) { return __half2float(*p); }
+  __device__ static T one(float a) { return __float2half_rn(a); }
+};
+
+template <int kDtype, int kNA>
+__global__ void __launch_bounds__(D_THREADS, 1)
+mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
+                   const uint8_t* __restrict__ sfw, const void* __restrict__ bias_v, void* __restrict__ c_v,
+                   int M, int N, int K, int64_t ldc, int kchunks, int* status) {
+  using Lay = DLayout<kNA>;
+  constexpr int S = Lay::STAGES;
+  constexpr bool kF16 = kDtype == QDQ_DTYPE_FP16;
+  using O = DOut<kF16>;
+  using T = typename O::T;
+  const T* bias = static_cast<const T*>(bias_v);
+  T* C = static_cast<T*>(c_v);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DBars* bars = reinterpret_cast<DBars*>(smem + S * Lay::STAGE);
+  const int warp = threadIdx.x >> 5;
+  const int n_blk = blockIdx.x;
+  const int num_kt = (K + DBK - 1) / DBK;
+
+  // Activation rows >= M and their scales stay zero for the whole launch.
+  constexpr int kZero = (Lay::A_TILE + 2 * SF_STAGE) / 16;  // A codes + both scale chunks
+  for (int i = threadIdx.x; i < S * kZero; i += D_THREADS) {
+    const int s = i / kZero, o = (i % kZero) * 16;
+    if (o < Lay::A_TILE || o >= Lay::A_TILE + SF_STAGE)  // skip the W scales (loaded every stage)
+      *reinterpret_cast<uint4*>(smem + s * Lay::STAGE + Lay::ST_A + o) = make_uint4(0, 0, 0, 0);
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&bars->raw[s], 1);
+      mbar_init(&bars->ready[s], 128);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    bars->abort = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmap_w);
+    prefetch_tmap(&tmap_a);
+  }
+  if (warp == 0) {
+    tmem_alloc(&bars->tmem_base, D_TMEM_COLS);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();  // the zeroed operand bytes are read by the tensor core
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    // ---------------- producer: W, its scales, raw A
+    if (elect_one()) {
+      int issued = 0;
+      for (int kt = 0; kt < num_kt; ++kt) {
+        const int s = kt % S;
+        if (!mbar_wait(&bars->empty[s], ((kt / S) & 1) ^ 1, status, 0x401)) {
+          bars->abort = 1;
+          break;
+        }
+        if (*(volatile int*)&bars->abort) break;
+        uint8_t* st = smem + s * Lay::STAGE;
+        mbar_arrive_expect_tx(&bars->raw[s], W_TILE + SF_STAGE + Lay::RAW);
+        tma_load_2d(st + Lay::ST_W, &tmap_w, kt * DBKB, n_blk * DBM, &bars->raw[s]);
+        bulk_load(st + Lay::ST_SFW, sfw + (static_cast<int64_t>(n_blk) * kchunks + 2 * kt) * 512, SF_STAGE,
+                  &bars->raw[s]);
+        tma_load_2d(st + Lay::ST_RAW, &tmap_a, kt * DBK, 0, &bars->raw[s]);
+        ++issued;
+      }
+      for (int kt = (issued > S ? issued - S : 0); kt < issued; ++kt)
+        mbar_wait(&bars->raw[kt % S], (kt / S) & 1, status, 0x402);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_mxf4(DBM, kNA, true);
+      bool ok = true;
+      for (int kt = 0; kt < num_kt; ++kt) {
+        const int s = kt % S;
+        if (!mbar_wait(&bars->ready[s], (kt / S) & 1, status, 0x403)) { ok = false; break; }
+        if (*(volatile int*)&bars->abort) { ok = false; break; }
+        tc_fence_after();
+        uint8_t* st = smem + s * Lay::STAGE;
+        tmem_cp_sf(tmem + T_SFW + 0, smem_desc_sf(st + Lay::ST_SFW));        // W rows, scales 0-3 of the stage
+        tmem_cp_sf(tmem + T_SFW + 4, smem_desc_sf(st + Lay::ST_SFW + 512));  // scales 4-7
+        tmem_cp_sf(tmem + T_SFA + 0, smem_desc_sf(st + Lay::ST_SFA));        // activation rows
+        tmem_cp_sf(tmem + T_SFA + 4, smem_desc_sf(st + Lay::ST_SFA + 512));
+        const uint64_t dw = smem_desc_sw128(st + Lay::ST_W);
+        const uint64_t da = smem_desc_sw128(st + Lay::ST_A);
+#pragma unroll
+        for (int kk = 0; kk < DBK / 64; ++kk) {
+          const uint32_t j = kk >> 1, sf_id = (kk & 1) * 2;
+          mma_mxf4(tmem + T_ACC, dw + ((kk * 32) >> 4), da + ((kk * 32) >> 4),
+                   idesc_with_sf_ids(idesc, sf_id, sf_id), (tmem + T_SFW + 4 * j) | (sf_id << 30),
+                   (tmem + T_SFA + 4 * j) | (sf_id << 30), (kt | kk) != 0);
+        }
+        tc_commit(&bars->empty[s]);
+      }
+      if (!ok) bars->abort = 1;
+      tc_commit(&bars->acc_full);  // also on abort: the epilogue waits for the issued MMAs
+    }
+  } else {
+    // ---------------- activation quantiser (128 threads), then epilogue
+    const int tq = threadIdx.x - 64;
+    const int lane = threadIdx.x & 31;
+    bool ok = true;
+    for (int kt = 0; kt < num_kt; ++kt) {
+      const int s = kt % S;
+      if (ok) ok = mbar_wait(&bars->raw[s], (kt / S) & 1, status, 0x404);
+      uint8_t* st = smem + s * Lay::STAGE;
+      // groups (row m, 32-block g) of this stage's [M, 256] slice; columns past K read as zero
+      for (int it = tq; it < M * (DBK / 32); it += 128) {
+        const int m = it >> 3, g = it & 7;
+        const uint4* src = reinterpret_cast<const uint4*>(st + Lay::ST_RAW + m * (DBK * 2) + g * 64);
+        uint4 v[4] = {src[0], src[1], src[2], src[3]};
+        uint32_t code[4];
+        const int e = mx_group_codes<kDtype>(v, code);
+        // 128-byte swizzle: 16-byte chunk g of row m sits at chunk g ^ (m % 8)
+        *reinterpret_cast<uint4*>(st + Lay::ST_A + m * DBKB + ((g ^ (m & 7)) << 4)) =
+            make_uint4(code[0], code[1], code[2], code[3]);
+        st[Lay::ST_SFA + (g >> 2) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4 + (g & 3)] =
+            static_cast<uint8_t>(e);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->ready[s]);
+    }
+    // epilogue: warp w reads TMEM lanes 32 (w % 4).. (W rows), columns = activation rows
+    if (ok) ok = mbar_wait(&bars->acc_full, 0, status, 0x405);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    const int q = warp & 3;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + T_ACC;
+    constexpr int NC = kNA > 32 ? 2 : 1;
+    uint32_t r[NC][32];
+#pragma unroll
+    for (int h = 0; h < NC; ++h) tmem_ld32(taddr + 32 * h, r[h]);
+    tmem_ld_wait();
+    const int n = n_blk * DBM + q * 32 + lane;
+    if (ok && !*(volatile int*)&bars->abort && n < N) {
+      const float b = bias != nullptr ? O::load(bias + n) : 0.f;
+#pragma unroll
+      for (int h = 0; h < NC; ++h)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int m = 32 * h + i;
+          if (m < M) C[static_cast<int64_t>(m) * ldc + n] = O::one(__uint_as_float(r[h][i]) + b);
+        }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, D_TMEM_COLS);
+  }
+}
+
+template <int kDtype, int kNA>
+int launch_decode(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* sf, const void* bias, void* c,
+                  int64_t M, int64_t N, int64_t K, int64_t ldc, int kchunks, int* status, cudaStream_t s) {
+  constexpr size_t smem = d_smem_bytes<kNA>();
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(&mxf4_decode_kernel<kDtype, kNA>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_linear_decode: smem attribute: %s", cudaGetErrorString(e));
+    attr_set[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>((N + DBM - 1) / DBM));
+  mxf4_decode_kernel<kDtype, kNA><<<grid, D_THREADS, smem, s>>>(tw, ta, sf, bias, c, static_cast<int>(M),
+                                                               static_cast<int>(N), static_cast<int>(K), ldc,
+                                                               kchunks, status);
+  return check_launch("fp4_linear_decode");
+}
+
+}  // namespace
+
+// Host entry used by fp4_linear_mxf4 for M <= 64 (declared in common.cuh).
+int fp4_linear_decode(const void* a, int64_t lda, int dtype, const void* w_codes, const void* w_sf_tiled,
+                      const void* bias, void* c, int64_t M, int64_t N, int64_t K, int64_t ldw_bytes,
+                      int64_t ldc, void* stream) {
+  if (M < 1 || M > NA_MAX) return fail(QDQ_ERR_INVALID_ARG, "fp4_linear_decode: M must be in [1, 64]");
+  if ((reinterpret_cast<uintptr_t>(a) & 15) || ((lda * 2) & 15))
+    return fail(QDQ_ERR_ALIGNMENT, "fp4_linear_decode: activation rows must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(w_sf_tiled) & 15)
+    return fail(QDQ_ERR_ALIGNMENT, "fp4_linear_decode: scale-factor buffer must be 16-byte aligned");
+  int* status = device_status_ptr();
+  if (status == nullptr) return QDQ_ERR_CUDA;
+  const int na = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+  CUtensorMap tw, ta;
+  if (int st = make_tmap_u8_2d(&tw, w_codes, N, K / 2, ldw_bytes, DBKB, DBM, 128)) return st;
+  if (int st = make_tmap_u16_2d(&ta, a, M, K, lda * 2, DBK, na)) return st;
+  const int kchunks = static_cast<int>(((K / 32) + 7) / 8 * 8 / 4);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto* sf = static_cast<const uint8_t*>(w_sf_tiled);
+  const bool f16 = dtype == QDQ_DTYPE_FP16;
+  if (na == 16)
+    return f16 ? launch_decode<QDQ_DTYPE_FP16, 16>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, status, s)
+               : launch_decode<QDQ_DTYPE_BF16, 16>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, status, s);
+  if (na == 32)
+    return f16 ? launch_decode<QDQ_DTYPE_FP16, 32>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, status, s)
+               : launch_decode<QDQ_DTYPE_BF16, 32>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, status, s);
+  return f16 ? launch_decode<QDQ_DTYPE_FP16, 64>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, status, s)
+             : launch_decode<QDQ_DTYPE_BF16, 64>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, status, s);
+}
+
+}  // namespace qdqb200

@@ -322,6 +322,23 @@ int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
   return QDQ_OK;
 }
 
+int make_tmap_u16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld_bytes,
+                     uint32_t box_cols, uint32_t box_rows) {
+  PFN_encodeTiled fn = encode_fn();
+  if (fn == nullptr) return fail(QDQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld_bytes & 15))
+    return fail(QDQ_ERR_ALIGNMENT, "TMA operand needs 16-byte aligned base and row stride");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld_bytes};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(QDQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return QDQ_OK;
+}
+
 }  // namespace qdqb200
 
 using namespace qdqb200;
@@ -424,6 +441,11 @@ extern "C" int fp4_linear_mxf4(const void* a, int64_t lda, int dtype, const void
   if (K % 32 != 0) return fail(QDQ_ERR_UNSUPPORTED, "fp4_linear_mxf4: K=%lld must be a multiple of 32", (long long)K);
   if (workspace == nullptr || workspace_bytes < fp4_linear_workspace_bytes(M, K))
     return fail(QDQ_ERR_INVALID_ARG, "fp4_linear_mxf4: workspace smaller than fp4_linear_workspace_bytes()");
+  // Small M: one launch that quantises the activation inside the GEMM producer.
+  if (M <= 64 && (dtype == QDQ_DTYPE_BF16 || dtype == QDQ_DTYPE_FP16) &&
+      (reinterpret_cast<uintptr_t>(a) & 15) == 0 && ((lda * 2) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(w_sf_tiled) & 15) == 0 && lda >= K && ldc >= N && ldw_bytes >= K / 2)
+    return fp4_linear_decode(a, lda, dtype, w_codes, w_sf_tiled, bias, c, M, N, K, ldw_bytes, ldc, stream);
   auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint8_t* a_codes = ws;

@@ -13,7 +13,7 @@
 //   - NVFP4: vLLM 0.22 nvfp4_emulation_utils.py:439-478 (CPU branch), bit-exact.
 // All float arithmetic that the references round step by step is written with
 // __fmul_rn/__fadd_rn/__fdiv_rn so that no FMA contraction changes a rounding.
-#include "common.cuh"
+#include "mx_quant.cuh"
 
 namespace qdqb200 {
 namespace {
@@ -22,82 +22,6 @@ constexpr uint32_t kFull = 0xFFFFFFFFu;
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;           // 16-byte chunks in flight per lane
 constexpr float kRecip6 = 1.0f / 6.0f;  // fp32 value of vLLM's FLOAT4_E2M1_MAX_RECIPROCAL
-
-// ---------------------------------------------------------------------------
-// per-dtype pieces
-// ---------------------------------------------------------------------------
-template <int kDtype>
-struct Fmt;
-
-template <>
-struct Fmt<QDQ_DTYPE_BF16> {
-  __device__ static float lo(uint32_t w) { return bf16lo(w); }
-  __device__ static float hi(uint32_t w) { return bf16hi(w); }
-  __device__ static float one(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
-  __device__ static uint32_t pack(float a, float b) { return pack_bf16x2(a, b); }
-  __device__ static uint16_t pack1(float a) { return static_cast<uint16_t>(pack_bf16x2(a, 0.f) & 0xFFFFu); }
-  __device__ static float amax_value(uint32_t bits) { return __uint_as_float(bits << 16); }
-  // E8M0 exponent of the group scale from the group's max |x| bit pattern:
-  // round the mantissa up at 0.75 (`+0x20 & 0xFF80`, mxfp4.py:138-140), then
-  // clamp(floor(log2) + 127 - 2, 0, 254) (mxfp4.py:142-145).  A rounded max of
-  // zero, inf or NaN makes the reference's float->int32 cast of +-inf land on
-  // the lower clamp, i.e. exponent 0.
-  __device__ static int mx_exp(uint32_t amax_bits) {
-    const uint32_t r = (amax_bits + 0x20u) & 0xFF80u;
-    const int ef = static_cast<int>((r >> 7) & 0xFFu);
-    return (ef == 0 || ef == 255) ? 0 : max(ef - 2, 0);
-  }
-  // 2^(e-127) as the reference holds it in bf16 (mxfp4.py:146): always exact.
-  __device__ static float mx_scale(int e) {
-    return e ? __uint_as_float(static_cast<uint32_t>(e) << 23) : __uint_as_float(0x00400000u);
-  }
-  static constexpr bool kScaleCanBeZero = false;
-};
-
-template <>
-struct Fmt<QDQ_DTYPE_FP16> {
-  __device__ static float lo(uint32_t w) { return f16lo(w); }
-  __device__ static float hi(uint32_t w) { return f16hi(w); }
-  __device__ static float one(uint16_t b) { return __half2float(__ushort_as_half(b)); }
-  __device__ static uint32_t pack(float a, float b) { return pack_f16x2(a, b); }
-  __device__ static uint16_t pack1(float a) { return static_cast<uint16_t>(pack_f16x2(a, 0.f) & 0xFFFFu); }
-  __device__ static float amax_value(uint32_t bits) { return __half2float(__ushort_as_half(static_cast<unsigned short>(bits))); }
-  // fp16 variant of the same rule (`+0x100 & 0xFC00`, exponent bias 15).
-  __device__ static int mx_exp(uint32_t amax_bits) {
-    const uint32_t r = (amax_bits + 0x100u) & 0xFC00u;
-    const int ef = static_cast<int>((r >> 10) & 0x1Fu);
-    return (ef == 0 || ef == 31) ? 0 : ef + 110;
-  }
-  // In fp16, 2^(e-127) underflows to 0 for e == 0 and is exact otherwise
-  // (e >= 111 for every finite non-tiny group).
-  __device__ static float mx_scale(int e) {
-    return e ? __uint_as_float(static_cast<uint32_t>(e) << 23) : 0.0f;
-  }
-  static constexpr bool kScaleCanBeZero = true;
-};
-
-// fp16 groups whose scale is 0: the reference divides by zero, turning x != 0
-// into +-inf and +-0 into a NaN whose sign on x86 is negative; the E2M1
-// simulation maps both to +-6 and the final multiply by the zero scale leaves
-// a signed zero.  Result: copysign(0, x) for x != 0, -0 for x == +-0.
-__device__ __forceinline__ uint16_t fp16_zero_scale_result(uint16_t xb) {
-  return ((xb & 0x7FFFu) == 0) ? static_cast<uint16_t>(0x8000u) : static_cast<uint16_t>(xb & 0x8000u);
-}
-__device__ __forceinline__ uint32_t fp16_zero_scale_word(uint32_t w) {
-  return static_cast<uint32_t>(fp16_zero_scale_result(static_cast<uint16_t>(w & 0xFFFFu))) |
-         (static_cast<uint32_t>(fp16_zero_scale_result(static_cast<uint16_t>(w >> 16))) << 16);
-}
-
-// E2M1 byte holding two signed zeros with the signs of an fp16x2 word.
-__device__ __forceinline__ uint32_t zero_codes_of(uint32_t w) {
-  return ((w >> 12) & 0x8u) | ((w >> 24) & 0x80u);
-}
-
-__device__ __forceinline__ uint32_t absmax8(const uint4& v) {
-  const uint32_t m = __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu),
-                              __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu));
-  return max(m & 0xFFFFu, m >> 16);
-}
 
 // ---------------------------------------------------------------------------
 // MXFP4: vectorised kernel (K % 32 == 0, 16-byte aligned rows)

@@ -277,5 +277,10 @@ __device__ __forceinline__ bool elect_one() {
 // swizzle (0 = none, 64 or 128 bytes).  Returns QDQ_OK or an error status.
 int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes,
                     uint64_t ld_bytes, uint32_t box_bytes, uint32_t box_rows, int swizzle_bytes);
+// The same for a row-major 16-bit matrix (rows x cols elements, row stride
+// ld_bytes), box of box_cols x box_rows elements, no swizzle; out-of-range
+// elements read as zero.
+int make_tmap_u16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld_bytes,
+                     uint32_t box_cols, uint32_t box_rows);
 
 }  // namespace qdqb200
