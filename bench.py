@@ -90,6 +90,9 @@ WORKLOADS = {
                       rows=16384, cols=8192, make=c2_input),
     "mxfp4_qdq": dict(config="BASELINE config 1: MXFP4 QDQ bf16 [8192, 4096], group 32, E8M0",
                       rows=8192, cols=4096, make=c1_input),
+    "mxfp8_qdq": dict(config="MXFP8 QDQ (float8_e4m3fn Marlin layers) on the config-1 input: bf16 "
+                             "[8192, 4096], group 32, E8M0 scales, E4M3 elements",
+                      rows=8192, cols=4096, make=c1_input),
     "sage3_mxfp4": dict(config="BASELINE config 4: Sage3 self-attention, MXFP4, Wan-2.1-14B 720p: "
                                "B=1, H=40, L=75600, D=128, bf16 NHD, non-causal, fp32 accumulation",
                         rows=75600, cols=128, make=None, B=1, H=40, sage3="mxfp4_hw", acc="fp32"),
@@ -198,6 +201,8 @@ def run_reference(args) -> None:
         if args.workload == "nvfp4_qdq":
             gs = float(global_scale_of(x)[0])
             return lambda: oq.nvfp4_qdq(xb, gs, nthreads=cores)
+        if args.workload == "mxfp8_qdq":
+            return lambda: oq.mxfp8_qdq(xb, nthreads=cores)
         return lambda: oq.mxfp4_qdq(xb, nthreads=cores)
 
     # Each step is a bounded sample of rows, sized so that warm-up + timed
@@ -244,6 +249,8 @@ def cpu_baseline(workload: str, x: torch.Tensor, budget_s: float = 15.0) -> dict
     if workload == "nvfp4_qdq":
         gs = float(global_scale_of(x)[0])
         fn = lambda: oq.nvfp4_qdq(xb, gs, nthreads=cores)  # noqa: E731
+    elif workload == "mxfp8_qdq":
+        fn = lambda: oq.mxfp8_qdq(xb, nthreads=cores)  # noqa: E731
     else:
         fn = lambda: oq.mxfp4_qdq(xb, nthreads=cores)  # noqa: E731
     fn()
@@ -282,7 +289,7 @@ def run_ours(args) -> None:
                                 device_id=dev)
 
     from vllm_qdq_plugin import _native
-    from vllm_qdq_plugin.qdq import mxfp4_qdq, nvfp4_qdq
+    from vllm_qdq_plugin.qdq import mxfp4_qdq, mxfp8_qdq, nvfp4_qdq
 
     wl = WORKLOADS[args.workload]
     if args.workload == "mxfp4_linear":
@@ -312,6 +319,15 @@ def run_ours(args) -> None:
 
         def api_call(xd):
             return nvfp4_qdq(xd, global_scale=gs)
+    elif args.workload == "mxfp8_qdq":
+        def step():
+            i = launches[0] % n_pairs
+            _native.check("qdq_mxfp8", lib.qdq_mxfp8(xs[i].data_ptr(), ys[i].data_ptr(), None, None,
+                                                     M, K, K, K, 0, 32, sp))
+            launches[0] += 1
+
+        def api_call(xd):
+            return mxfp8_qdq(xd)
     else:
         def step():
             i = launches[0] % n_pairs

@@ -62,6 +62,24 @@ int qdq_mxfp4(const void* x, void* y, void* codes, void* scales, int64_t M,
               void* stream);
 
 /*
+ * MXFP8 quant-dequant: E4M3 (float8_e4m3fn) elements, one E8M0 scale per 32
+ * elements.  Replaces the reference's MXFP8 QDQ in front of float8_e4m3fn
+ * Marlin GEMMs, vllm_qdq_plugin/qdq/mxfp8.py:73-125 (called at
+ * vllm_qdq_plugin/patch.py:61-67 and :150-152), bit-exact: scale =
+ * 2^(clamp(floor(log2 max(amax, FLT_MIN)) + 119, 0, 254) - 127), elements
+ * rounded to nearest-even onto E4M3 with saturation at 448 and the
+ * reference's subnormal clamp at 7 * 2^-9, zero quotients as +0.
+ *
+ *   x, y, ldx, ldy, dtype as qdq_mxfp4 (y may be NULL when `codes` is given)
+ *   codes  optional [M, Kp] uint8 E4M3 bytes, Kp = round_up(K, 32), zero padded
+ *   scales optional [M, Kp/32] uint8 E8M0 exponents (NULL = skip)
+ * group_size must be 32 (patch.py:67, :152).
+ */
+int qdq_mxfp8(const void* x, void* y, void* codes, void* scales, int64_t M,
+              int64_t K, int64_t ldx, int64_t ldy, int dtype, int group_size,
+              void* stream);
+
+/*
  * NVFP4 quant-dequant with a given per-tensor global scale: E2M1 elements,
  * one E4M3 scale per 16 elements, fp32 global scale `gs` read from device
  * memory (`global_scale`, 1 float).  Bit-exact with the CPU branch of

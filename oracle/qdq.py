@@ -50,6 +50,8 @@ def lib():
                 h.oracle_round_e4m3.restype = f32
                 h.oracle_mxfp4_hw_quant.argtypes = [vp, vp, vp, i64, i64, i32]
                 h.oracle_mxfp4_hw_quant.restype = None
+                h.oracle_mxfp8_qdq.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, i32, i32]
+                h.oracle_mxfp8_qdq.restype = None
                 h.oracle_max_threads.argtypes = []
                 h.oracle_max_threads.restype = i32
                 _lib = h
@@ -69,6 +71,18 @@ def mxfp4_qdq(x: np.ndarray, *, fp16: bool = False, codes: bool = False, nthread
     c = np.empty((m, kp // 2), np.uint8) if codes else None
     s = np.empty((m, kp // 32), np.uint8) if codes else None
     lib().oracle_mxfp4_qdq(_p(x), _p(y), _p(c), _p(s), m, k, k, k, int(fp16), nthreads)
+    return (y, c, s) if codes else y
+
+
+def mxfp8_qdq(x: np.ndarray, *, fp16: bool = False, codes: bool = False, group_size: int = 32,
+              nthreads: int = 0):
+    """x: uint16 [M, K] bit patterns -> y (uint16 [M, K]) [, E4M3 codes [M, K], E8M0 scales]."""
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    m, k = x.shape
+    y = np.empty_like(x)
+    c = np.empty((m, k), np.uint8) if codes else None
+    s = np.empty((m, (k + group_size - 1) // group_size), np.uint8) if codes else None
+    lib().oracle_mxfp8_qdq(_p(x), _p(y), _p(c), _p(s), m, k, k, k, int(fp16), group_size, nthreads)
     return (y, c, s) if codes else y
 
 

@@ -14,6 +14,8 @@
  *                           CPU branch (:467-478)
  *   oracle_mxfp4_hw_quant   vllm_qdq_plugin/sage3_attn/sage3/mxfp4_hw_kernel.py:43-116
  *                           (quantize_to_mxfp4 / _float_to_e2m1_nibble)
+ *   oracle_mxfp8_qdq        vllm_qdq_plugin/qdq/mxfp8.py:73-125 (+ _round_half_to_even
+ *                           :24-37, _quantize_to_e4m3fn_no_fp8_dtype :40-70)
  * Pinned against fixtures produced by importing the reference itself
  * (tests/golden/make_golden.py).
  *
@@ -325,6 +327,106 @@ void oracle_mxfp4_hw_quant(const float* x, uint8_t* codes, uint8_t* scales, int6
         }
         codes[r * (K / 2) + g * 16 + i / 2] = (uint8_t)(nib[0] | (nib[1] << 4));
       }
+    }
+  }
+}
+
+/* ------------------------------------------------------------------ */
+/* MXFP8 QDQ (vllm_qdq_plugin/qdq/mxfp8.py)                             */
+/* ------------------------------------------------------------------ */
+
+/* _round_half_to_even (mxfp8.py:24-37): floor, then +1 above one half or, on
+ * an exact half, when the floor is odd.  fp32 throughout. */
+static float rhte(float x) {
+  const float f = floorf(x);
+  const float frac = x - f;
+  const int tie = frac == 0.5f;
+  const int up = frac > 0.5f;
+  const int odd = fmodf(f, 2.0f) != 0.0f;
+  return f + (float)(up | (tie & odd));
+}
+
+static inline float clampf(float v, float lo, float hi) {  /* torch.clamp: NaN stays NaN */
+  if (isnan(v)) return v;
+  return v < lo ? lo : (v > hi ? hi : v);
+}
+
+/* _quantize_to_e4m3fn_no_fp8_dtype (mxfp8.py:40-70), fp32 in and out. */
+static float e4m3_sim(float x) {
+  const float sign = x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : (isnan(x) ? x : 0.0f));   /* torch.sign */
+  const float ax = clampf(fabsf(x), 0.0f, 448.0f);
+  const float sub_step = 0x1p-9f, min_normal = 0x1p-6f;
+  float sub_q = rhte(ax / sub_step) * sub_step;
+  sub_q = clampf(sub_q, 0.0f, 7.0f * sub_step);                         /* :57 */
+  const float safe = isnan(ax) ? ax : (ax < min_normal ? min_normal : ax);
+  float e = floorf(log2f(safe));
+  e = clampf(e, -6.0f, 8.0f);
+  const float step = exp2f(e - 3.0f);
+  float norm_q = rhte(ax / step) * step;
+  norm_q = clampf(norm_q, min_normal, 448.0f);                          /* :66 */
+  const float q = ax < min_normal ? sub_q : norm_q;
+  return q * sign;
+}
+
+/* E4M3 byte of a value e4m3_sim returns (finite, |v| <= 448, on the grid). */
+static uint8_t e4m3_byte_exact(float q) {
+  const uint8_t sgn = signbit(q) ? 0x80 : 0;
+  const float a = fabsf(q);
+  if (a == 0.0f) return sgn;
+  if (a < 0x1p-6f) return (uint8_t)(sgn | (uint8_t)(a * 512.0f));
+  const int e = ilogbf(a);
+  const int m = (int)(a / ldexpf(1.0f, e - 3)) - 8;
+  return (uint8_t)(sgn | ((e + 7) << 3) | m);
+}
+
+/* One group of n <= gs elements (a partial last group is zero-padded). */
+static void mxfp8_group(const uint16_t* x, uint16_t* y, int n, int gs, int is_fp16, uint8_t* codes,
+                        uint8_t* scale_out) {
+  /* block max in the input dtype, then fp32, clamped below at FLT_MIN (:104-105) */
+  float bm = 0.0f;
+  int has_nan = 0;
+  for (int i = 0; i < n; ++i) {
+    const float a = fabsf(h_to_f32(x[i], is_fp16));
+    if (isnan(a)) has_nan = 1;
+    if (a > bm) bm = a;
+  }
+  (void)gs;
+  if (has_nan) bm = NAN;                                 /* torch.max propagates NaN */
+  if (!(bm >= 0x1p-126f) && !isnan(bm)) bm = 0x1p-126f;  /* clamp(min=finfo(float32).tiny) */
+  /* 127 + floor(log2(bm)).to(int32) - 8, clamped to [0, 254] (:107-112); the
+   * float->int32 cast of +-inf / NaN is x86's INT_MIN */
+  const int32_t fl = x86_f32_to_i32(floorf(log2f(bm)));
+  int64_t se = 127 + (int64_t)fl - 8;
+  if (se < 0) se = 0;
+  if (se > 254) se = 254;
+  const float scale = ldexpf(1.0f, (int)se - 127);       /* 2.0 ** (scale_exp - 127) */
+  for (int i = 0; i < n; ++i) {
+    const float xs = h_to_f32(x[i], is_fp16) / scale;    /* :117 */
+    const float q = e4m3_sim(xs);                         /* :118 */
+    y[i] = f32_to_h(q * scale, is_fp16);                  /* :119 */
+    if (codes) codes[i] = isnan(q) ? 0x7F : e4m3_byte_exact(q);
+  }
+  if (scale_out) *scale_out = (uint8_t)se;
+}
+
+/*
+ * x, y: [M, K] 16-bit patterns with row strides ldx/ldy; group gs (32 in the
+ * plugin's calls).  codes (optional): [M, K] E4M3 bytes; scales (optional):
+ * [M, ceil(K/gs)] E8M0 bytes.
+ */
+void oracle_mxfp8_qdq(const uint16_t* x, uint16_t* y, uint8_t* codes, uint8_t* scales, int64_t M,
+                      int64_t K, int64_t ldx, int64_t ldy, int is_fp16, int gs, int nthreads) {
+  const int64_t gpr = (K + gs - 1) / gs;
+#ifdef _OPENMP
+  if (nthreads > 0) omp_set_num_threads(nthreads);
+#pragma omp parallel for schedule(static) if (nthreads != 1)
+#endif
+  for (int64_t r = 0; r < M; ++r) {
+    for (int64_t g = 0; g < gpr; ++g) {
+      const int64_t k0 = g * gs;
+      const int n = (int)((K - k0) < gs ? (K - k0) : gs);
+      mxfp8_group(x + r * ldx + k0, y + r * ldy + k0, n, gs, is_fp16, codes ? codes + r * K + k0 : 0,
+                  scales ? scales + r * gpr + g : 0);
     }
   }
 }

@@ -15,6 +15,10 @@ Each fixture is a compressed .npz of inputs and the reference's own outputs:
                                     several global scales, and a config-2 slice.
   mxfp4_hw_quant.npz                reference quantize_to_mxfp4 (sage3/mxfp4_hw_kernel.py:73)
                                     codes and E8M0 bytes for Q/K-like and V-like rows.
+  mxfp8_bf16.npz / mxfp8_fp16.npz   reference mxfp8_qdq (src/vllm_qdq_plugin/qdq/mxfp8.py:73)
+                                    on every finite 16-bit pattern in natural 32-groups, on
+                                    context groups reaching 20 binades below their max (into
+                                    E4M3's subnormal range), on a config-1 slice and on odd K.
 The reference is imported from its checkout; nothing from it is copied here.
 """
 
@@ -46,6 +50,14 @@ def load_reference(ref_root: Path):
     return mx.mxfp4_qdq, nv.ref_nvfp4_quant_dequant, mxfp4_hw_kernel.quantize_to_mxfp4
 
 
+def load_reference_mxfp8(ref_root: Path):
+    spec = importlib.util.spec_from_file_location(
+        "ref_mxfp8", ref_root / "src/vllm_qdq_plugin/qdq/mxfp8.py")
+    m8 = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m8)
+    return m8.mxfp8_qdq
+
+
 def finite_patterns(fp16: bool) -> np.ndarray:
     p = np.arange(65536, dtype=np.uint32).astype(np.uint16)
     if fp16:
@@ -60,9 +72,9 @@ def group_rows(vals: np.ndarray, g: int) -> np.ndarray:
     return np.concatenate([vals, np.zeros(pad, np.uint16)]).reshape(-1, g)
 
 
-def context_rows(fp16: bool, g: int, rng: np.random.Generator) -> np.ndarray:
+def context_rows(fp16: bool, g: int, rng: np.random.Generator, binades: int = 10) -> np.ndarray:
     """Groups whose largest element is a chosen 'context' value and whose other
-    elements sweep every pattern within 10 binades below it."""
+    elements sweep every pattern within `binades` binades below it."""
     mbits = 10 if fp16 else 7
     if fp16:
         ctx = [0x0001, 0x00FF, 0x02FF, 0x0300, 0x03FF, 0x0400, 0x3C00, 0x3E00, 0x3EFF, 0x3F00,
@@ -73,7 +85,7 @@ def context_rows(fp16: bool, g: int, rng: np.random.Generator) -> np.ndarray:
     rows = []
     for c in ctx:
         ef = c >> mbits
-        lo = max(0, ef - 10) << mbits
+        lo = max(0, ef - binades) << mbits
         cand = np.arange(lo, c + 1, dtype=np.uint32).astype(np.uint16)
         cand = np.concatenate([cand, cand | 0x8000]).astype(np.uint16)
         rng.shuffle(cand)
@@ -96,7 +108,11 @@ def bits_of(t: torch.Tensor) -> np.ndarray:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", choices=["all", "mxfp8"], default="all")
     args = ap.parse_args()
+    write_mxfp8(Path(args.reference))
+    if args.only == "mxfp8":
+        return
     mxfp4_qdq, nvfp4_qdq, quantize_to_mxfp4 = load_reference(Path(args.reference))
     rng = np.random.default_rng(1234)
 
@@ -153,6 +169,27 @@ def main():
         out[f"{name}_scales"] = scales.numpy()
     np.savez_compressed(HERE / "mxfp4_hw_quant.npz", **out)
     print("wrote mxfp4_hw_quant.npz")
+
+
+def write_mxfp8(ref_root: Path):
+    mxfp8_qdq = load_reference_mxfp8(ref_root)
+    rng = np.random.default_rng(808)
+    for fp16 in (False, True):
+        tag = "fp16" if fp16 else "bf16"
+        dt = torch.float16 if fp16 else torch.bfloat16
+        sets = {
+            "natural": group_rows(finite_patterns(fp16), 32),
+            "context": context_rows(fp16, 32, rng, binades=20),
+            "c1_slice": bits_of(c1_input()[:16].to(dt)),
+        }
+        g_odd = torch.Generator().manual_seed(8)
+        sets["odd_k"] = bits_of((torch.randn(7, 100, generator=g_odd) * 3).to(dt))
+        out = {}
+        for name, xb in sets.items():
+            out[f"{name}_x"] = xb
+            out[f"{name}_y"] = bits_of(mxfp8_qdq(as_t(xb, fp16), group_size=32))
+        np.savez_compressed(HERE / f"mxfp8_{tag}.npz", **out)
+        print(f"wrote mxfp8_{tag}.npz")
 
 
 if __name__ == "__main__":

@@ -1,8 +1,9 @@
 """CPU: the C oracle is pinned to the reference's own outputs.
 
 The fixtures in tests/golden/ were produced by running the reference
-(tests/golden/make_golden.py): the plugin's mxfp4_qdq, vLLM 0.22's
-ref_nvfp4_quant_dequant (CPU branch) and the plugin's quantize_to_mxfp4.
+(tests/golden/make_golden.py): the plugin's mxfp4_qdq and mxfp8_qdq, vLLM
+0.22's ref_nvfp4_quant_dequant (CPU branch) and the plugin's
+quantize_to_mxfp4.
 """
 
 from __future__ import annotations
@@ -20,6 +21,14 @@ from oracle import qdq as oq
 def test_mxfp4_oracle_matches_reference(tag, subset):
     d = golden(f"mxfp4_{tag}.npz")
     y = oq.mxfp4_qdq(d[f"{subset}_x"], fp16=(tag == "fp16"))
+    np.testing.assert_array_equal(y, d[f"{subset}_y"])
+
+
+@pytest.mark.parametrize("tag", ["bf16", "fp16"])
+@pytest.mark.parametrize("subset", ["natural", "context", "c1_slice", "odd_k"])
+def test_mxfp8_oracle_matches_reference(tag, subset):
+    d = golden(f"mxfp8_{tag}.npz")
+    y = oq.mxfp8_qdq(d[f"{subset}_x"], fp16=(tag == "fp16"))
     np.testing.assert_array_equal(y, d[f"{subset}_y"])
 
 

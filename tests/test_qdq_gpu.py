@@ -1,4 +1,4 @@
-"""GPU parity of the MXFP4 / NVFP4 QDQ kernels (through the C ABI).
+"""GPU parity of the MXFP4 / NVFP4 / MXFP8 QDQ kernels (through the C ABI).
 
 Bar: bit-exact against (a) the reference's own outputs in tests/golden/ and
 (b) the pinned C oracle at larger, random, strided and odd shapes, including
@@ -123,6 +123,72 @@ def test_empty_and_special_values(cuda_device):
     gs = torch.tensor([2.5], device=cuda_device)
     assert_bits_equal(bits(nvfp4_qdq(x, global_scale=gs)), oq.nvfp4_qdq(bits(x), 2.5),
                       "specials nvfp4")
+
+
+# ------------------------------------------------------------------ MXFP8
+@pytest.mark.parametrize("tag", ["bf16", "fp16"])
+@pytest.mark.parametrize("subset", ["natural", "context", "c1_slice", "odd_k"])
+def test_mxfp8_kernel_matches_reference_golden(cuda_device, tag, subset):
+    from vllm_qdq_plugin.qdq import mxfp8_qdq
+    d = golden(f"mxfp8_{tag}.npz")
+    y = mxfp8_qdq(to_dev(d[f"{subset}_x"], tag, cuda_device))
+    assert_bits_equal(bits(y), d[f"{subset}_y"], f"mxfp8 {tag} {subset}")
+
+
+@pytest.mark.parametrize("tag", ["bf16", "fp16"])
+@pytest.mark.parametrize("shape", [(1, 32), (3, 64), (257, 4096), (33, 96), (5, 100), (2, 7),
+                                   (129, 1056)])
+def test_mxfp8_kernel_matches_oracle(cuda_device, tag, shape):
+    from vllm_qdq_plugin.qdq import mxfp8_qdq, mxfp8_quantize
+    x = _random(*shape, DT[tag], seed=shape[0] * 13 + shape[1], dev=cuda_device)
+    want, wcodes, wscales = oq.mxfp8_qdq(bits(x), fp16=(tag == "fp16"), codes=True)
+    assert_bits_equal(bits(mxfp8_qdq(x)), want, f"mxfp8 {tag} {shape}")
+    codes, scales = mxfp8_quantize(x)
+    k = shape[1]
+    np.testing.assert_array_equal(codes.cpu().numpy()[:, :k], wcodes)
+    assert not codes.cpu().numpy()[:, k:].any()  # zero padding up to a multiple of 32
+    np.testing.assert_array_equal(scales.cpu().numpy(), wscales)
+
+
+def test_mxfp8_specials_strides_and_underflow(cuda_device):
+    """Zeros of both signs, inf, the largest values, E4M3's subnormal range and
+    bf16 groups whose max is so large that small elements underflow to zero
+    when divided by the scale (they come out +0, as torch.sign(-0) is 0)."""
+    from vllm_qdq_plugin.qdq import mxfp8_qdq
+    x = torch.zeros(6, 64, dtype=torch.bfloat16)
+    x[1] = -0.0
+    x[2, 5] = float("inf")
+    x[2, 6] = -3.0
+    x[3, :32] = torch.finfo(torch.bfloat16).max
+    x[4, 0] = 2.0 ** 100
+    x[4, 1:32] = -torch.exp2(-torch.arange(100, 131).float())
+    x[4, 32] = -(2.0 ** 40)
+    x[4, 33:64] = torch.exp2(-torch.arange(100, 131).float()) * torch.tensor(
+        [(-1) ** i for i in range(31)]).float()
+    x[5] = torch.linspace(-1, 1, 64) * 2.0 ** -8
+    x[5, 0] = 1.0
+    xd = x.to(cuda_device)
+    assert_bits_equal(bits(mxfp8_qdq(xd)), oq.mxfp8_qdq(bits(x)), "mxfp8 specials")
+    base = _random(64, 4096 + 64, torch.bfloat16, seed=15, dev=cuda_device)
+    for view in (base[:, :4096], base[:, 8:8 + 4096 - 32], base[1:, 3:3 + 1000]):
+        assert_bits_equal(bits(mxfp8_qdq(view)), oq.mxfp8_qdq(bits(view)), f"mxfp8 view {tuple(view.stride())}")
+    assert mxfp8_qdq(torch.empty(0, 64, dtype=torch.float16, device=cuda_device)).shape == (0, 64)
+
+
+def test_mxfp8_config1_shape_bit_exact_and_idempotent(cuda_device):
+    from bench import c1_input
+    from vllm_qdq_plugin.qdq import mxfp8_qdq
+    x = c1_input()
+    y = mxfp8_qdq(x.to(cuda_device))
+    want = oq.mxfp8_qdq(bits(x))
+    assert_bits_equal(bits(y), want, "mxfp8 config-1 shape")
+    # A second pass keeps every value (they are on the E4M3 grid of the same
+    # scales) but, like the reference, turns the -0 of tiny negative inputs
+    # into +0 (torch.sign(-0) is 0): equal as floats, and bit-exact with the
+    # oracle's second pass.
+    y2 = mxfp8_qdq(y)
+    assert torch.equal(y2.float(), y.float())
+    assert_bits_equal(bits(y2), oq.mxfp8_qdq(want), "mxfp8 second pass")
 
 
 # ------------------------------------------------------------------ full size

@@ -368,6 +368,161 @@ amax_gs_kernel(const uint16_t* __restrict__ x, int64_t M, int64_t K, int64_t ldx
   }
 }
 
+// ---------------------------------------------------------------------------
+// MXFP8: E4M3 elements, E8M0 scale per 32 (vllm_qdq_plugin/qdq/mxfp8.py:73-125),
+// bit-exact.
+// ---------------------------------------------------------------------------
+// Scale exponent 127 + floor(log2(max(amax, FLT_MIN))) - 8, clamped to
+// [0, 254] (mxfp8.py:104-112).  For a bf16/fp16 maximum, floor(log2) is the
+// fp32 exponent field (their mantissas are too short for log2 to round up to
+// the next integer); a zero or sub-FLT_MIN maximum sits at FLT_MIN (-126);
+// inf / NaN give 0, the x86 float->int32 cast of +-inf / NaN.
+template <int kDtype>
+__device__ __forceinline__ int mx8_exp(uint32_t amax_bits) {
+  const uint32_t b = __float_as_uint(Fmt<kDtype>::amax_value(amax_bits));
+  const int ef = static_cast<int>(b >> 23);
+  if (ef == 255) return 0;
+  return min(max((ef == 0 ? -126 : ef - 127) + 119, 0), 254);
+}
+__device__ __forceinline__ float pow2f(int e) {  // 2^e, e in [-127, 127]
+  return __uint_as_float(e > -127 ? static_cast<uint32_t>(e + 127) << 23 : 0x00400000u);
+}
+// The reference's E4M3 grid (mxfp8.py:40-70) is round-to-nearest-even with
+// saturation at 448, except that its subnormal branch is clamped to 7 * 2^-9
+// (:57): magnitudes in [7.5, 8) * 2^-9 give 7 * 2^-9 where RNE gives 2^-6.
+// Lowering [7, 8) * 2^-9 to 7 * 2^-9 before the hardware conversion
+// reproduces that.
+__device__ __forceinline__ float mx8_sub_clamp(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return ((u & 0x7FFFFFFFu) - 0x3C600000u < 0x00200000u) ? __uint_as_float((u & 0x80000000u) | 0x3C600000u) : v;
+}
+// Two values -> E4M3 pair (a in the low byte) and its exact fp16x2 decode.
+__device__ __forceinline__ uint32_t e4m3x2_roundtrip(float a, float b, uint32_t& h) {
+  uint32_t out;
+  asm("{\n\t.reg .b16 t;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 t, %3, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, t;\n\t"
+      "cvt.u32.u16 %0, t;\n\t}"
+      : "=r"(out), "=r"(h)
+      : "f"(a), "f"(b));
+  return out;
+}
+// x / scale for a pair.  torch.sign makes a zero quotient +0 (mxfp8.py:46,
+// :70): with fma(x, inv, zero), zero = +0.0 a kernel argument, an exact -0
+// becomes +0.  That covers every zero quotient while no nonzero input can
+// underflow: inv >= 2^-16 (scale exponent <= 143), always so for fp16.
+// Above it, zero quotients are cleared by comparison.
+__device__ __forceinline__ float2 mx8_scaled(float a, float b, float inv, float zero, bool fast) {
+  if (fast) return fma_f32x2(make_float2(a, b), make_float2(inv, inv), make_float2(zero, zero));
+  float2 t = mul_f32x2(make_float2(a, b), make_float2(inv, inv));
+  if (t.x == 0.0f) t.x = 0.0f;
+  if (t.y == 0.0f) t.y = 0.0f;
+  return t;
+}
+
+template <int kDtype, bool kContig, bool kY, bool kCodes, bool kScales>
+__global__ void __launch_bounds__(kThreads)
+mxfp8_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
+                 uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
+                 uint32_t cpr, uint64_t total, int64_t ldx, int64_t ldy, int64_t ldc,
+                 int64_t lds, float zero) {
+  using F = Fmt<kDtype>;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x * kUnroll;
+  for (uint64_t base = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31u)) * kUnroll;
+       base < total; base += stride) {
+    uint4 v[kUnroll];
+    uint64_t xo[kUnroll], yo[kUnroll], co[kUnroll], so[kUnroll];
+    bool ok[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const uint64_t c = base + static_cast<uint64_t>(u) * 32u + lane;
+      ok[u] = c < total;
+      if (kContig) {
+        xo[u] = c * 8u;
+        yo[u] = c * 8u;
+        co[u] = c * 8u;
+        so[u] = c >> 2;
+      } else {
+        const uint32_t row = static_cast<uint32_t>(c) / cpr;
+        const uint32_t col = static_cast<uint32_t>(c) - row * cpr;
+        xo[u] = row * static_cast<uint64_t>(ldx) + col * 8u;
+        yo[u] = row * static_cast<uint64_t>(ldy) + col * 8u;
+        co[u] = row * static_cast<uint64_t>(ldc) + col * 8u;
+        so[u] = row * static_cast<uint64_t>(lds) + (col >> 2);
+      }
+      v[u] = ok[u] ? ld_stream(reinterpret_cast<const uint4*>(x + xo[u])) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      uint32_t amax = absmax8(v[u]);
+      amax = max(amax, __shfl_xor_sync(kFull, amax, 1));
+      amax = max(amax, __shfl_xor_sync(kFull, amax, 2));
+      const int e = mx8_exp<kDtype>(amax);
+      const float inv = pow2f(127 - e), sc = pow2f(e - 127);
+      const bool fast = e <= 143;
+      const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      uint32_t o[4], cw[2] = {0u, 0u};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 t = mx8_scaled(F::lo(w[j]), F::hi(w[j]), inv, zero, fast);
+        uint32_t h;
+        const uint32_t pair = e4m3x2_roundtrip(mx8_sub_clamp(t.x), mx8_sub_clamp(t.y), h);
+        cw[j >> 1] |= pair << (16 * (j & 1));
+        const float2 d = mul_f32x2(make_float2(f16lo(h), f16hi(h)), make_float2(sc, sc));
+        o[j] = F::pack(d.x, d.y);
+      }
+      if (ok[u]) {
+        if (kY) st_stream(reinterpret_cast<uint4*>(y + yo[u]), make_uint4(o[0], o[1], o[2], o[3]));
+        if (kCodes) *reinterpret_cast<uint2*>(codes + co[u]) = make_uint2(cw[0], cw[1]);
+        if (kScales && (lane & 3u) == 0) scales[so[u]] = static_cast<uint8_t>(e);
+      }
+    }
+  }
+}
+
+// Any K, any alignment: one thread per 32-group (a partial last group is
+// zero-padded, mxfp8.py:97-100).
+template <int kDtype>
+__global__ void __launch_bounds__(kThreads)
+mxfp8_generic_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y, uint8_t* __restrict__ codes,
+                     uint8_t* __restrict__ scales, int64_t M, int64_t K, int64_t ldx, int64_t ldy,
+                     int64_t ldc, int64_t lds, float zero) {
+  using F = Fmt<kDtype>;
+  const int64_t gpr = (K + 31) / 32;
+  const int64_t ngroups = M * gpr;
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < ngroups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = g / gpr;
+    const int64_t gi = g - r * gpr;
+    const int64_t k0 = gi * 32;
+    const int n = static_cast<int>((K - k0) < 32 ? (K - k0) : 32);
+    const uint16_t* xr = x + r * ldx + k0;
+    uint32_t amax = 0;
+    for (int i = 0; i < n; ++i) amax = max(amax, static_cast<uint32_t>(xr[i] & 0x7FFFu));
+    const int e = mx8_exp<kDtype>(amax);
+    const float inv = pow2f(127 - e), sc = pow2f(e - 127);
+    const bool fast = e <= 143;
+    for (int i = 0; i < n; i += 2) {
+      const bool has1 = (i + 1) < n;
+      const float2 t = mx8_scaled(F::one(xr[i]), has1 ? F::one(xr[i + 1]) : 0.0f, inv, zero, fast);
+      uint32_t h;
+      const uint32_t pair = e4m3x2_roundtrip(mx8_sub_clamp(t.x), mx8_sub_clamp(t.y), h);
+      if (y) {
+        y[r * ldy + k0 + i] = F::pack1(__fmul_rn(f16lo(h), sc));
+        if (has1) y[r * ldy + k0 + i + 1] = F::pack1(__fmul_rn(f16hi(h), sc));
+      }
+      if (codes) {
+        codes[r * ldc + k0 + i] = static_cast<uint8_t>(pair & 0xFFu);
+        if (has1) codes[r * ldc + k0 + i + 1] = static_cast<uint8_t>(pair >> 8);
+      }
+    }
+    if (codes)
+      for (int i = n; i < 32; ++i) codes[r * ldc + k0 + i] = 0;  // zero padding
+    if (scales) scales[r * lds + gi] = static_cast<uint8_t>(e);
+  }
+}
+
 int grid_for(uint64_t work_items, int per_block) {
   const uint64_t need = (work_items + per_block - 1) / per_block;
   const uint64_t cap = static_cast<uint64_t>(device_sm_count()) * 8u;
@@ -400,6 +555,13 @@ void dispatch_nv_vec(OutSet o, int grid, cudaStream_t s, Args... args) {
   if (o == kOutY) nvfp4_vec_kernel<kDtype, kContig, true, false, false><<<grid, kThreads, 0, s>>>(args...);
   else if (o == kOutAll) nvfp4_vec_kernel<kDtype, kContig, true, true, true><<<grid, kThreads, 0, s>>>(args...);
   else nvfp4_vec_kernel<kDtype, kContig, false, true, true><<<grid, kThreads, 0, s>>>(args...);
+}
+
+template <int kDtype, bool kContig, typename... Args>
+void dispatch_mx8_vec(OutSet o, int grid, cudaStream_t s, Args... args) {
+  if (o == kOutY) mxfp8_vec_kernel<kDtype, kContig, true, false, false><<<grid, kThreads, 0, s>>>(args...);
+  else if (o == kOutAll) mxfp8_vec_kernel<kDtype, kContig, true, true, true><<<grid, kThreads, 0, s>>>(args...);
+  else mxfp8_vec_kernel<kDtype, kContig, false, true, true><<<grid, kThreads, 0, s>>>(args...);
 }
 
 int check_common(const void* x, const void* y, const void* codes, int64_t M, int64_t K,
@@ -458,6 +620,47 @@ extern "C" int qdq_mxfp4(const void* x, void* y, void* codes, void* scales, int6
       mxfp4_generic_kernel<QDQ_DTYPE_FP16><<<grid, kThreads, 0, s>>>(xp, yp, cp, sp, M, K, ldx, ldy, ldc, lds);
   }
   return check_launch("qdq_mxfp4");
+}
+
+extern "C" int qdq_mxfp8(const void* x, void* y, void* codes, void* scales, int64_t M, int64_t K,
+                         int64_t ldx, int64_t ldy, int dtype, int group_size, void* stream) {
+  if (int st = check_common(x, y, codes, M, K, ldx, ldy, dtype, "qdq_mxfp8")) return st;
+  if (group_size != 32)
+    return fail(QDQ_ERR_UNSUPPORTED, "qdq_mxfp8: group_size must be 32 (got %d)", group_size);
+  if (M == 0 || K == 0) return QDQ_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t Kp = (K + 31) / 32 * 32;
+  const int64_t ldc = Kp, lds = Kp / 32;
+  auto* xp = static_cast<const uint16_t*>(x);
+  auto* yp = static_cast<uint16_t*>(y);
+  auto* cp = static_cast<uint8_t*>(codes);
+  auto* sp = static_cast<uint8_t*>(scales);
+  const uint64_t cpr = static_cast<uint64_t>(K / 8);
+  const uint64_t total = static_cast<uint64_t>(M) * cpr;
+  const OutSet o = out_set(y, codes, scales);
+  if (y == nullptr) ldy = K;
+  const bool vec = (K % 32 == 0) && aligned16(x) && (y == nullptr || aligned16(y)) && (ldx % 8 == 0) &&
+                   (ldy % 8 == 0) && (codes == nullptr || (reinterpret_cast<uintptr_t>(codes) & 7u) == 0) &&
+                   o != kOutOther;
+  const bool contig = (ldx == K) && (ldy == K);
+  if (vec && (contig || total < (1ull << 32))) {
+    const int grid = grid_for(total, kThreads * kUnroll);
+    if (dtype == QDQ_DTYPE_BF16) {
+      if (contig) dispatch_mx8_vec<QDQ_DTYPE_BF16, true>(o, grid, s, xp, yp, cp, sp, (uint32_t)cpr, total, ldx, ldy, ldc, lds, 0.0f);
+      else dispatch_mx8_vec<QDQ_DTYPE_BF16, false>(o, grid, s, xp, yp, cp, sp, (uint32_t)cpr, total, ldx, ldy, ldc, lds, 0.0f);
+    } else {
+      if (contig) dispatch_mx8_vec<QDQ_DTYPE_FP16, true>(o, grid, s, xp, yp, cp, sp, (uint32_t)cpr, total, ldx, ldy, ldc, lds, 0.0f);
+      else dispatch_mx8_vec<QDQ_DTYPE_FP16, false>(o, grid, s, xp, yp, cp, sp, (uint32_t)cpr, total, ldx, ldy, ldc, lds, 0.0f);
+    }
+  } else {
+    const uint64_t ngroups = static_cast<uint64_t>(M) * static_cast<uint64_t>((K + 31) / 32);
+    const int grid = grid_for(ngroups, kThreads);
+    if (dtype == QDQ_DTYPE_BF16)
+      mxfp8_generic_kernel<QDQ_DTYPE_BF16><<<grid, kThreads, 0, s>>>(xp, yp, cp, sp, M, K, ldx, ldy, ldc, lds, 0.0f);
+    else
+      mxfp8_generic_kernel<QDQ_DTYPE_FP16><<<grid, kThreads, 0, s>>>(xp, yp, cp, sp, M, K, ldx, ldy, ldc, lds, 0.0f);
+  }
+  return check_launch("qdq_mxfp8");
 }
 
 extern "C" int qdq_nvfp4(const void* x, void* y, void* codes, void* scales, const float* global_scale,

@@ -31,6 +31,8 @@ _f32 = ctypes.c_float
 _SIGNATURES: dict[str, list] = {
     "qdq_mxfp4": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64,
                   _int, _int, _c_void_p],
+    "qdq_mxfp8": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64,
+                  _int, _int, _c_void_p],
     "qdq_nvfp4": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64,
                   _i64, _int, _c_void_p],
     "qdq_nvfp4_global_scale": [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _int,

@@ -6,8 +6,8 @@ Mirrors the reference's `vllm_qdq_plugin.qdq` package
 """
 
 from .mxfp4 import mxfp4_qdq, mxfp4_quantize
-from .mxfp8 import mxfp8_qdq
+from .mxfp8 import mxfp8_qdq, mxfp8_quantize
 from .nvfp4 import nvfp4_global_scale, nvfp4_qdq, nvfp4_quantize
 
-__all__ = ["mxfp4_qdq", "mxfp8_qdq", "nvfp4_qdq", "mxfp4_quantize", "nvfp4_quantize",
+__all__ = ["mxfp4_qdq", "mxfp8_qdq", "nvfp4_qdq", "mxfp4_quantize", "mxfp8_quantize", "nvfp4_quantize",
            "nvfp4_global_scale"]
