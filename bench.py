@@ -193,6 +193,8 @@ def run_reference(args) -> None:
     from oracle import qdq as oq  # CPU restatement of the reference (test/baseline only)
 
     wl = WORKLOADS[args.workload]
+    if args.workload == "mxfp4_linear" or args.workload.startswith("sage3"):
+        return run_reference_compute(args, wl)
     x = wl["make"]()
     cores = os.cpu_count() or 1
 
@@ -239,6 +241,34 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_reference_compute(args, wl) -> None:
+    """Reference arm for the GEMM / attention workloads: the reference's CPU
+    emulation of the same call, each step a bounded sample (see the samplers)."""
+    per_step = max(3.0, 100.0 / max(1, args.steps + args.warmup))
+    if args.workload == "mxfp4_linear":
+        m = args.rows or wl["rows"]
+        cb = cpu_gemm_sample(m, budget_s=per_step * args.steps)
+        metric = "FP4 GEMM TFLOPS"
+        config = {"workload": wl["config"], "M": m, "N": 14336, "K": 4096}
+        ms = 2.0 * m * 14336 * 4096 / (cb["value"] * 1e12) * 1e3
+    else:
+        L = args.rows or wl["rows"]
+        cb = cpu_attn_sample(wl, L, budget_s=per_step * args.steps)
+        metric = "Sage3 attention TFLOPS (4*B*H*L^2*D per call)"
+        config = {"workload": wl["config"], "B": wl["B"], "H": wl["H"], "L": L, "D": 128,
+                  "sage3": wl["sage3"], "acc_dtype": wl["acc"]}
+        ms = 4.0 * wl["B"] * wl["H"] * L * L * 128 / (cb["value"] * 1e12) * 1e3
+    line = {
+        "impl": "reference", "metric": metric, "value": cb["value"], "unit": cb["unit"],
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 emulation of the FP4 path", "data": "synthetic (seeded, BASELINE shapes)",
+        "config": config, "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def cpu_baseline(workload: str, x: torch.Tensor, budget_s: float = 15.0) -> dict:
     """Reported baseline: the oracle (C restatement of the reference) on host cores."""
     sys.path.insert(0, str(REPO))
@@ -265,6 +295,80 @@ def cpu_baseline(workload: str, x: torch.Tensor, budget_s: float = 15.0) -> dict
             "cores": cores, "kind": "port",
             "sample": f"{n} full passes over the [{x.shape[0]}, {x.shape[1]}] input "
                       "(C restatement of the reference algorithm, OpenMP)"}
+
+
+def cpu_gemm_sample(m: int, budget_s: float = 15.0, max_rows: int = 256) -> dict:
+    """The reference's CPU emulation of the fused linear (mxfp4_qdq of the
+    activation, then an fp32 matmul with the dequantised MXFP4 weight) on a
+    sample of activation rows, all host threads; W is dequantised once
+    beforehand (weight preparation)."""
+    sys.path.insert(0, str(REPO))
+    from oracle import gemm as og
+    from oracle import qdq as oq  # test/baseline infrastructure only
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    rows = min(m, max_rows)
+    a, codes, scales = c3_inputs(rows=rows)
+    n, k = codes.shape[0], codes.shape[1] * 2
+    w = torch.from_numpy(og.dequant_mxfp4(codes.numpy(), scales.numpy()).astype("float32"))
+    ab = a.view(torch.int16).numpy().view("uint16")
+
+    def fn():
+        aq = oq.mxfp4_qdq(ab, nthreads=cores)
+        at = torch.from_numpy(aq.astype("int16")).view(torch.bfloat16).float()
+        return (at @ w.t()).to(torch.bfloat16)
+
+    fn()
+    it, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        it += 1
+        if time.perf_counter() - t0 > budget_s or it >= 200:
+            break
+    dt = (time.perf_counter() - t0) / it
+    return {"value": round(2.0 * rows * n * k / dt / 1e12, 4), "unit": "TFLOP/s", "cores": cores,
+            "kind": "port",
+            "sample": f"{rows} of {m} activation rows x W [{n}, {k}] per pass, {it} passes: C restatement "
+                      "of mxfp4_qdq + torch fp32 matmul with the dequantised weight (W dequantised once)"}
+
+
+def cpu_attn_sample(wl: dict, L: int, budget_s: float = 20.0) -> dict:
+    """The reference's Sage3 path restated on the CPU (oracle/attn.py) for one
+    (batch, head): its pre-pass over all L tokens, and the flash loop for as many
+    128-row query tiles as fit the budget; the per-head time is extrapolated as
+    pre-pass + (query tiles) x (time per tile)."""
+    sys.path.insert(0, str(REPO))
+    from oracle import attn as oa  # test/baseline infrastructure only
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    if wl["sage3"] == "nvfp4":
+        q, k, v = c5_inputs(torch.device("cpu"), B=1, L=L, H=1)
+    else:
+        q, k, v = c4_inputs(torch.device("cpu"), L=L, H=1)
+    f = lambda t: t[0, :, 0].float().numpy()  # noqa: E731
+    nv, emulated = oa.VARIANTS[wl["sage3"]]
+    block_n = oa.REF_BLOCK_N[wl["sage3"]]
+    sm = 1.0 / math.sqrt(128)
+    t0 = time.perf_counter()
+    qd, kd, vd, ds = oa.prepass(f(q), f(k), f(v), True, nv)
+    t_pre = time.perf_counter() - t0
+    tiles = (L + 127) // 128
+    done, t0 = 0, time.perf_counter()
+    while done < tiles:
+        oa.flash(qd, kd, vd, ds, L, sm, block_n=block_n, nv=nv, emulated=emulated,
+                 q_rows=slice(128 * done, 128 * done + 128))
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    t_tile = (time.perf_counter() - t0) / done
+    per_head = t_pre + tiles * t_tile
+    return {"value": round(4.0 * L * L * 128 / per_head / 1e12, 6), "unit": "TFLOP/s", "cores": cores,
+            "kind": "port",
+            "sample": f"one (batch, head) at L={L}: pre-pass {t_pre:.2f} s + {done} of {tiles} query tiles "
+                      f"timed ({t_tile:.3f} s each), per-head time extrapolated to all tiles; numpy/C "
+                      f"restatement of the reference's {wl['sage3']} path"}
 
 
 # ---------------------------------------------------------------------------
@@ -554,6 +658,8 @@ def run_gemm(args, wl, world, rank, dev, dist) -> None:
                          "peak_source": src, "traffic": ncu_traffic("mxfp4_linear")},
             "clocks": sampler.summary(t_wall0, t_wall1) if sampler else None,
         }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_gemm_sample(m)
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
@@ -687,6 +793,8 @@ def run_attn(args, wl, world, rank, dev, dist) -> None:
                          "softmax_floor_ms": round(B * H * L * L / (148 * 16 * 1.965e9) * 1e3, 2)},
             "clocks": sampler.summary(t_wall0, t_wall1) if sampler else None,
         }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_attn_sample(wl, L)
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()

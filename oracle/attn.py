@@ -128,21 +128,25 @@ def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True,
 
 
 def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: bool = False,
-          mask_padding: bool = True, nv: bool = False, emulated: bool = False) -> np.ndarray:
-    """The attention loop on dequantised operands; returns O [L, D] float64.
+          mask_padding: bool = True, nv: bool = False, emulated: bool = False,
+          q_rows: slice | None = None) -> np.ndarray:
+    """The attention loop on dequantised operands; returns O [L, D] float64
+    (or the rows q_rows of it, for timing a slice of the query tiles).
 
     P handling: mxfp4_hw (nv=False, emulated=False): E8M0 per 32 of p, l = sum
     of unquantised p.  Emulated configs (emulated=True): p scaled by 448*6
     first, l = sum of the dequantised P (p_quant_kernels.py:37-150,
     attention_kernel.py:176-186); nv=True uses E4M3 per 16."""
-    Lp, D = qd.shape
+    Lp, D = kd.shape
     n_keys = L if mask_padding else Lp
     qk_scale = sm_scale * LOG2E
-    rows = np.arange(Lp)
-    m = np.full(Lp, -np.inf)
-    l = np.zeros(Lp)
-    acc = np.zeros((Lp, D))
-    group = np.repeat(np.arange(Lp // 128), 128)
+    rows = np.arange(Lp)[q_rows] if q_rows is not None else np.arange(Lp)
+    qd = qd[rows]
+    nq = len(rows)
+    m = np.full(nq, -np.inf)
+    l = np.zeros(nq)
+    acc = np.zeros((nq, D))
+    group = rows // 128
     pre = 2688.0 if emulated else 1.0
     for n0 in range(0, n_keys, block_n):
         n1 = min(n0 + block_n, Lp)
@@ -159,19 +163,19 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
         w = n1 - n0
         p1 = p * pre
         if nv:
-            pg = p1.reshape(Lp, w // 16, 16)
+            pg = p1.reshape(nq, w // 16, 16)
             sc = e4m3_round(np.maximum(pg.max(axis=2) / 6.0, 1e-8)).astype(np.float64)[:, :, None]
             inv = np.where(sc > 0, 1.0 / np.where(sc > 0, sc, 1), 0.0)
-            pq = (_rne_e2m1(pg * inv) * sc).reshape(Lp, w)
+            pq = (_rne_e2m1(pg * inv) * sc).reshape(nq, w)
         else:
-            pg = p1.reshape(Lp, w // 32, 32)
+            pg = p1.reshape(nq, w // 32, 32)
             e = np.clip(_ceil_log2(pg.max(axis=2) / 6.0), -127, 127)
             sc = np.exp2(e.astype(np.float64))[:, :, None]
-            pq = (_rne_e2m1(pg / sc) * sc).reshape(Lp, w)
+            pq = (_rne_e2m1(pg / sc) * sc).reshape(nq, w)
         l = l * alpha + (pq.sum(axis=1) if emulated else p.sum(axis=1))
         acc = acc + pq @ vd[n0:n1]
         m = m_new
-    return (acc / l[:, None])[:L]
+    return (acc / l[:, None])[rows < L]
 
 
 VARIANTS = {"mxfp4_hw": (False, False), "mxfp4": (False, True), "nvfp4": (True, True)}
