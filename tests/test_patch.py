@@ -152,3 +152,51 @@ def test_register_is_gated_on_vllm_qdq():
             mock.patch.object(P, "apply_patches", side_effect=lambda: called.append(1)):
         vllm_qdq_plugin.register()
     assert called == [1]
+
+
+def test_nvfp4_activation_knob_on_nvfp4_layers():
+    """VLLM_QDQ_NVFP4_ACT=1 (this build only): float4_e2m1f layers that carry a
+    global scale (vLLM's NVFP4 Marlin layers) get NVFP4 QDQ; MXFP4 layers and
+    the knob's default keep the reference's MXFP4 QDQ."""
+    st = _scalar_types()
+    seen = []
+    ops = types.SimpleNamespace(marlin_gemm=lambda *a, **k: a[0],
+                                moe_wna16_marlin_gemm=lambda *a, **k: a[0])
+
+    def fake_nv(x, group_size=16, global_scale=None):
+        seen.append(("nv", group_size))
+        return x * 5
+
+    def mx(x, group_size=32):
+        seen.append(("mx", group_size))
+        return x * 2
+
+    gs = torch.ones(1)
+    a = torch.ones((4, 64), dtype=torch.bfloat16)
+
+    def dense(global_scale):
+        return ops.marlin_gemm(a, None, torch.empty(1), None, torch.empty(1), None, global_scale, None,
+                               None, None, torch.empty(1), st.float4_e2m1f, 4, 8, 64)
+
+    def moe(global_scale):
+        return ops.moe_wna16_marlin_gemm(
+            a, None, torch.empty(1), None, torch.empty(1), None, global_scale, None, None, None,
+            torch.empty(1), torch.empty(1, dtype=torch.int32), torch.empty(1, dtype=torch.int32),
+            torch.empty(1, dtype=torch.int32), torch.empty((1, 1)), 16, 1, False, st.float4_e2m1f,
+            4, 8, 64, True, False, False, False)
+
+    P._patch_marlin_gemm(ops, st, mx, _raise, lambda *t: None)
+    P._patch_moe_marlin_gemm(ops, st, mx, _raise, lambda *t: None)
+    with mock.patch("vllm_qdq_plugin.qdq.nvfp4.nvfp4_qdq", fake_nv):
+        with mock.patch.dict(os.environ, {"VLLM_QDQ_NVFP4_ACT": "1", "VLLM_MARLIN_MOE_QDQ_MODE": "0"}):
+            assert torch.equal(dense(gs), a * 5)
+            assert torch.equal(dense(None), a * 2)
+            assert torch.equal(moe(gs), a * 5)
+            assert torch.equal(moe(None), a * 2)
+        with mock.patch.dict(os.environ, {"VLLM_QDQ_NVFP4_ACT": "0", "VLLM_MARLIN_MOE_QDQ_MODE": "0"}):
+            assert torch.equal(dense(gs), a * 2)
+            assert torch.equal(moe(gs), a * 2)
+        with mock.patch.dict(os.environ, {"VLLM_QDQ_NVFP4_ACT": "1",
+                                          "VLLM_MARLIN_MOE_QDQ_MODE": "FORCE_MXFP4"}):
+            assert torch.equal(moe(gs), a * 2)  # FORCE_MXFP4 keeps precedence, as in the reference
+    assert seen == [("nv", 16), ("mx", 32), ("nv", 16), ("mx", 32), ("mx", 32), ("mx", 32), ("mx", 32)]

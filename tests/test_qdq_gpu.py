@@ -224,3 +224,24 @@ def test_ops_trace_under_torch_compile(cuda_device):
     eager = f(a, gs)
     compiled = torch.compile(f, fullgraph=True)(a, gs)
     assert torch.equal(eager.view(torch.int16), compiled.view(torch.int16))
+
+
+def test_nvfp4_activation_knob_end_to_end(cuda_device):
+    """VLLM_QDQ_NVFP4_ACT=1 on an NVFP4 Marlin layer: the activation reaching the
+    (stand-in) Marlin kernel is exactly nvfp4_qdq(a) with a's own global scale."""
+    import os
+    import types
+    from unittest import mock
+
+    from vllm_qdq_plugin import patch as P
+    from vllm_qdq_plugin.qdq import mxfp4_qdq, nvfp4_qdq
+    st = types.SimpleNamespace(float4_e2m1f=object(), float8_e4m3fn=object())
+    ops = types.SimpleNamespace(marlin_gemm=lambda *a, **k: a[0])
+    P._patch_marlin_gemm(ops, st, mxfp4_qdq, None, lambda *t: None)
+    a = _random(64, 4096, torch.bfloat16, seed=77, dev=cuda_device)
+    with mock.patch.dict(os.environ, {"VLLM_QDQ_NVFP4_ACT": "1"}):
+        got = ops.marlin_gemm(a, None, None, None, None, None, torch.ones(1, device=cuda_device), None,
+                              None, None, None, st.float4_e2m1f, 64, 8, 4096)
+    assert_bits_equal(bits(got), bits(nvfp4_qdq(a)), "NVFP4 activation knob")
+    gs = oq.nvfp4_global_scale(bits(a))
+    assert_bits_equal(bits(got), oq.nvfp4_qdq(bits(a), gs), "NVFP4 activation knob vs oracle")

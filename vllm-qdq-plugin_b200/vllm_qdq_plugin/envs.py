@@ -80,6 +80,12 @@ environment_variables: dict[str, Callable[[], Any]] = {
     # MXFP4 weights were captured (see vllm_qdq_plugin.gemm); "0" keeps the
     # reference behaviour (QDQ then the original Marlin kernel).
     "VLLM_QDQ_FUSED_GEMM": _flag("VLLM_QDQ_FUSED_GEMM"),
+    # B200 build: on NVFP4 Marlin layers (float4_e2m1f weights with a global
+    # scale, which vLLM passes only for NVFP4: marlin_utils_fp4.py
+    # apply_fp4_marlin_linear), quantise the activation as NVFP4 (group 16,
+    # E4M3 block scales, per-tensor gs = 448*6/amax) instead of the reference's
+    # MXFP4 QDQ.  "0" keeps the reference behaviour.
+    "VLLM_QDQ_NVFP4_ACT": _flag("VLLM_QDQ_NVFP4_ACT"),
 }
 
 

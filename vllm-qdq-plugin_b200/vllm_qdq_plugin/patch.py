@@ -32,11 +32,24 @@ logger = init_logger(__name__)
 _QDQ_DTYPES = (torch.float16, torch.bfloat16)
 
 
+def _fp4_act_qdq(a: torch.Tensor, global_scale, mxfp4_qdq) -> torch.Tensor:
+    """Activation QDQ in front of an FP4 (float4_e2m1f) Marlin GEMM: the
+    reference's MXFP4 QDQ, or, with VLLM_QDQ_NVFP4_ACT=1 on an NVFP4 layer
+    (global_scale given), NVFP4 QDQ with the activation's own global scale."""
+    if (envs.VLLM_QDQ_NVFP4_ACT and global_scale is not None and a.dtype in _QDQ_DTYPES
+            and a.shape[-1] % 16 == 0):
+        from .qdq.nvfp4 import nvfp4_qdq
+        return nvfp4_qdq(a, group_size=16)
+    return mxfp4_qdq(a, group_size=32)
+
+
 def _patch_marlin_gemm(ops, scalar_types, mxfp4_qdq, mxfp8_qdq, trace_qdq):
     """Wrap ops.marlin_gemm so 2-D fp16/bf16 activations are QDQ'd first.
 
     Routing (reference patch.py:51-67): b_q_type float4_e2m1f -> MXFP4 QDQ
     (group 32); float8_e4m3fn -> MXFP8 QDQ; anything else passes through.
+    With VLLM_QDQ_NVFP4_ACT=1 (this build only), float4_e2m1f layers that
+    carry a global scale, i.e. NVFP4 Marlin layers, get NVFP4 QDQ instead.
     """
     original = ops.marlin_gemm
 
@@ -69,7 +82,7 @@ def _patch_marlin_gemm(ops, scalar_types, mxfp4_qdq, mxfp8_qdq, trace_qdq):
                 out = fused_marlin_replacement(a, c, b_q_weight, b_bias, size_m, size_n, size_k)
                 if out is not None:
                     return out
-            a = mxfp4_qdq(a, group_size=32)
+            a = _fp4_act_qdq(a, global_scale, mxfp4_qdq)
         elif qdq_ok and b_q_type == scalar_types.float8_e4m3fn:
             trace_qdq("marlin_gemm", a.shape, a.dtype)
             a = mxfp8_qdq(a, group_size=32)
@@ -125,9 +138,12 @@ def _patch_moe_marlin_gemm(ops, scalar_types, mxfp4_qdq, mxfp8_qdq, trace_qdq):
         blocks_per_sm: int = -1,
     ) -> torch.Tensor:
         if input.dim() == 2:
-            if envs.VLLM_MARLIN_MOE_QDQ_MODE == "FORCE_MXFP4" or b_q_type == scalar_types.float4_e2m1f:
+            if envs.VLLM_MARLIN_MOE_QDQ_MODE == "FORCE_MXFP4":
                 trace_qdq("moe_wna16_marlin_gemm", input.shape, input.dtype)
                 input = mxfp4_qdq(input, group_size=32)
+            elif b_q_type == scalar_types.float4_e2m1f:
+                trace_qdq("moe_wna16_marlin_gemm", input.shape, input.dtype)
+                input = _fp4_act_qdq(input, global_scale, mxfp4_qdq)
             elif b_q_type == scalar_types.float8_e4m3fn:
                 trace_qdq("moe_wna16_marlin_gemm", input.shape, input.dtype)
                 input = mxfp8_qdq(input, group_size=32)
