@@ -99,6 +99,9 @@ WORKLOADS = {
     "sage3_nvfp4": dict(config="BASELINE config 5: Sage3 self-attention, NVFP4, SAGE3_ACC_DTYPE=bf16_pv_only, "
                                "Flux-like batch: B=8, H=24, L=4608, D=128, bf16 NHD, 1% of K rows x20",
                         rows=4608, cols=128, make=None, B=8, H=24, sage3="nvfp4", acc="bf16_pv_only"),
+    "mxfp4_moe": dict(config="Grouped MXFP4 MoE GEMM (QDQ + moe_wna16_marlin_gemm replaced), gpt-oss-120b "
+                             "w13 shape: 4096 tokens, 128 experts, top-4, K=2880, N=5760, block 64, "
+                             "uniform routing", rows=4096, cols=2880, make=None, E=128, N=5760, top_k=4),
     "mxfp4_linear": dict(config="BASELINE config 3: MXFP4 QDQ fused into a tcgen05 FP4 GEMM, "
                                 "A bf16 [M=4096, K=4096], W MXFP4 [N=14336, K=4096], out bf16",
                          rows=4096, cols=4096, make=None),
@@ -193,7 +196,7 @@ def run_reference(args) -> None:
     from oracle import qdq as oq  # CPU restatement of the reference (test/baseline only)
 
     wl = WORKLOADS[args.workload]
-    if args.workload == "mxfp4_linear" or args.workload.startswith("sage3"):
+    if args.workload in ("mxfp4_linear", "mxfp4_moe") or args.workload.startswith("sage3"):
         return run_reference_compute(args, wl)
     x = wl["make"]()
     cores = os.cpu_count() or 1
@@ -245,7 +248,14 @@ def run_reference_compute(args, wl) -> None:
     """Reference arm for the GEMM / attention workloads: the reference's CPU
     emulation of the same call, each step a bounded sample (see the samplers)."""
     per_step = max(3.0, 100.0 / max(1, args.steps + args.warmup))
-    if args.workload == "mxfp4_linear":
+    if args.workload == "mxfp4_moe":
+        m = args.rows or wl["rows"]
+        cb = cpu_moe_sample(wl, m, budget_s=per_step * args.steps)
+        metric = "FP4 MoE GEMM TFLOPS (2 x routed slots x N x K)"
+        config = {"workload": wl["config"], "tokens": m, "experts": wl["E"], "top_k": wl["top_k"],
+                  "N": wl["N"], "K": wl["cols"]}
+        ms = 2.0 * m * wl["top_k"] * wl["N"] * wl["cols"] / (cb["value"] * 1e12) * 1e3
+    elif args.workload == "mxfp4_linear":
         m = args.rows or wl["rows"]
         cb = cpu_gemm_sample(m, budget_s=per_step * args.steps)
         metric = "FP4 GEMM TFLOPS"
@@ -398,6 +408,8 @@ def run_ours(args) -> None:
     wl = WORKLOADS[args.workload]
     if args.workload == "mxfp4_linear":
         return run_gemm(args, wl, world, rank, dev, dist)
+    if args.workload == "mxfp4_moe":
+        return run_moe(args, wl, world, rank, dev, dist)
     if args.workload.startswith("sage3"):
         return run_attn(args, wl, world, rank, dev, dist)
     x_cpu = wl["make"](rows=args.rows) if args.rows else wl["make"]()
@@ -687,6 +699,171 @@ def c5_inputs(dev, B: int = 8, L: int = 4608, H: int = 24, seed: int = 5):
     k = torch.where(pick, k * 20.0, k).to(torch.bfloat16)
     v = torch.randn(B, L, H, 128, generator=g, device=dev, dtype=torch.bfloat16)
     return q, k, v
+
+
+def moe_inputs(m: int, e: int, top_k: int, n: int, k: int, seed: int = 6):
+    """Synthetic MoE layer: A ~ N(0,1) bf16 [m, k]; per-expert MXFP4 weights with
+    uniform nibbles and E8M0 exponents in [-10, -4]; each token routed to top_k
+    distinct experts uniformly; routing weights U(0, 1); block size 64 (16 when
+    fewer than 32 slots per expert on average)."""
+    import numpy as np
+    sys.path.insert(0, str(REPO))
+    from oracle import gemm as og  # moe_align: vLLM's moe_align_block_size layout
+    rng = np.random.default_rng(seed)
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    codes = torch.from_numpy(rng.integers(0, 256, size=(e, n, k // 2), dtype=np.uint8))
+    scales = torch.from_numpy((127 + rng.integers(-10, -3, size=(e, n, k // 32))).astype(np.uint8))
+    topk_ids = np.argsort(rng.random((m, e)), axis=1)[:, :top_k]
+    bs = 64 if m * top_k >= 32 * e else 16
+    sid, eid, ntp = og.moe_align(topk_ids, e, bs)
+    topk_w = torch.from_numpy(rng.random((m, top_k)).astype(np.float32))
+    return a, codes, scales, torch.from_numpy(sid), torch.from_numpy(eid), torch.from_numpy(ntp), topk_w, bs
+
+
+def cpu_moe_sample(wl: dict, m: int, budget_s: float = 15.0) -> dict:
+    """The reference's CPU emulation of the MoE layer (mxfp4_qdq of the gathered
+    tokens, fp32 matmul with each dequantised expert) on a sample of experts,
+    all host threads; extrapolated to every routed slot."""
+    import numpy as np
+    sys.path.insert(0, str(REPO))
+    from oracle import gemm as og
+    from oracle import qdq as oq  # test/baseline infrastructure only
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    e, n, k, top_k = wl["E"], wl["N"], wl["cols"], wl["top_k"]
+    a, codes, scales, sid, eid, ntp, topk_w, bs = moe_inputs(m, e, top_k, n, k)
+    sid, eid = sid.numpy(), eid.numpy()
+    ab = a.view(torch.int16).numpy().view("uint16")
+    done_slots, t0, ex = 0, time.perf_counter(), 0
+    while ex < e:
+        blocks = np.nonzero(eid == ex)[0]
+        slots = np.concatenate([sid[b * bs:(b + 1) * bs] for b in blocks]) if len(blocks) else np.array([])
+        slots = slots[slots < m * top_k]
+        if len(slots):
+            w = torch.from_numpy(og.dequant_mxfp4(codes[ex].numpy(), scales[ex].numpy()).astype("float32"))
+            aq = oq.mxfp4_qdq(np.ascontiguousarray(ab[slots // top_k]), nthreads=cores)
+            at = torch.from_numpy(aq.astype("int16")).view(torch.bfloat16).float()
+            (at @ w.t()).to(torch.bfloat16)
+            done_slots += len(slots)
+        ex += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(2.0 * done_slots * n * k / dt / 1e12, 4), "unit": "TFLOP/s", "cores": cores,
+            "kind": "port",
+            "sample": f"{ex} of {e} experts ({done_slots} of {m * top_k} routed slots), each: C restatement of "
+                      "mxfp4_qdq on the gathered tokens + dequantisation of the expert + torch fp32 matmul"}
+
+
+def run_moe(args, wl, world, rank, dev, dist) -> None:
+    from vllm_qdq_plugin import _native
+    from vllm_qdq_plugin.gemm import mxfp4_moe_linear, prepare_mxfp4_moe_weight
+
+    m = args.rows or wl["rows"]
+    e, n, k, top_k = wl["E"], wl["N"], wl["cols"], wl["top_k"]
+    a_cpu, codes, scales, sid, eid, ntp, topk_w, bs = moe_inputs(m, e, top_k, n, k)
+    a, sidd, eidd, ntpd, twd = (t.to(dev) for t in (a_cpu, sid, eid, ntp, topk_w.reshape(-1)))
+    w = prepare_mxfp4_moe_weight(codes.to(dev), scales.to(dev))
+    out = torch.empty((m * top_k, n), dtype=torch.bfloat16, device=dev)
+    lib = _native.lib()
+    stream = torch.cuda.current_stream(dev)
+    slots = int((sid < m * top_k).sum())
+
+    def step(sp=None):
+        _native.check("fp4_moe_mxf4", lib.fp4_moe_mxf4(
+            a.data_ptr(), k, 0, w.codes.data_ptr(), w.sf_tiled.data_ptr(), e, sidd.data_ptr(), eidd.data_ptr(),
+            ntpd.data_ptr(), twd.data_ptr(), sidd.numel(), bs, top_k, 1, out.data_ptr(), n, m, n, k,
+            sp if sp is not None else torch.cuda.current_stream(dev).cuda_stream))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    steps = max(1, min(args.steps, 200))
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(graph, stream=cap):
+            for _ in range(steps):
+                step(cap.cuda_stream)
+    stream.wait_stream(cap)
+    graph.replay()
+    barrier()
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))).start() if rank == 0 else None
+    time.sleep(0.3 if sampler else 0)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    barrier()
+    t_wall1 = time.time()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if sampler:
+        sampler.stop()
+    ms_step = ms / steps
+    flop = 2.0 * slots * n * k
+    value = world * flop / (ms_step * 1e-3) / 1e12
+    # end to end through the torch op with pinned host buffers (activation and routing in, output out)
+    hosts = [t.pin_memory() for t in (a_cpu, sid, eid, ntp, topk_w.reshape(-1))]
+    out_host = torch.empty((m * top_k, n), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        ad, sd, ed, nd, td = (t.to(dev, non_blocking=True) for t in hosts)
+        out_host.copy_(mxfp4_moe_linear(ad, w, sd, ed, nd, td, bs, top_k, True), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = 5
+    a0.record(stream)
+    for _ in range(n_e2e):
+        e2e_step()
+    a1.record(stream)
+    barrier()
+    e2e = world * flop / (a0.elapsed_time(a1) / n_e2e * 1e-3) / 1e12
+    if rank == 0:
+        peak, src = measured_peak_fp4()
+        achieved = flop / (ms_step * 1e-3) / 1e12
+        w_bytes = w.codes.numel() + w.sf_tiled.numel()
+        line = {
+            "metric": "FP4 MoE GEMM TFLOPS (2 x routed slots x N x K)", "value": round(value, 1),
+            "unit": "TFLOP/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "e2m1 x e2m1 (E8M0 scales), fp32 accumulate, bf16 out",
+            "data": "synthetic (seeded routing and weights)",
+            "config": {"workload": wl["config"], "tokens": m, "experts": e, "top_k": top_k, "N": n, "K": k,
+                       "block": bs, "routed_slots": slots,
+                       "l2": f"{w_bytes / 1e9:.2f} GB of expert weights exceed the 126 MB L2; steps replayed "
+                             "from one CUDA graph"},
+            "e2e": {"value": round(e2e, 1), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in hosts),
+                    "d2h_bytes_per_step": out_host.numel() * 2,
+                    "path": "vllm_qdq_plugin.gemm.mxfp4_moe_linear on pinned host buffers"},
+            "gpu_launches": steps,
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "peak_source": src,
+                         "traffic": None, "hbm_floor_ms": round(w_bytes / (measured_peak_hbm()[0] * 1e9) * 1e3, 4)},
+            "clocks": sampler.summary(t_wall0, t_wall1) if sampler else None,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_moe_sample(wl, m)
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
 
 
 def run_attn(args, wl, world, rank, dev, dist) -> None:

@@ -226,6 +226,32 @@ int fp4_linear_mxf4_noalloc(const void* a, int64_t lda, int dtype, const void* w
                             const void* w_sf_tiled, const void* bias, void* c, int64_t M, int64_t N,
                             int64_t K, int64_t ldw_bytes, int64_t ldc, void* stream);
 
+/*
+ * Grouped MXFP4 MoE GEMM.  Replaces "MXFP4 QDQ of the activation, then vLLM's
+ * moe_wna16_marlin_gemm" for MXFP4 experts (reference:
+ * vllm_qdq_plugin/patch.py:139-152 + vllm/_custom_ops.py:2469, as called from
+ * vllm/model_executor/layers/fused_moe/experts/marlin_moe.py).  For every block
+ * b < num_tokens_post_padded / moe_block_size whose expert e = expert_ids[b]
+ * lies in [0, num_experts), and every slot s = sorted_token_ids[b *
+ * moe_block_size + i] < size_m * top_k:
+ *   C[s, :] = mxfp4_qdq(A[s / top_k, :]) . W_e^T   (x topk_weights[s] if mul_topk_weights)
+ * with fp32 accumulation; rows of C no slot names are not written.
+ *   a            [size_m, K] bf16/fp16 (dtype), row stride lda elements, 16-byte aligned rows
+ *   w_codes      [num_experts, N, K/2] packed E2M1 (element 2j in the low nibble), contiguous
+ *   w_sf_tiled   num_experts blocks of qdq_sf_tiled_bytes(N, K) bytes: each expert's E8M0
+ *                scales in the tiled layout of qdq_sf_tile
+ *   sorted_token_ids [num_sorted], expert_ids [num_sorted / moe_block_size],
+ *   num_tokens_post_padded [1]: int32 device arrays (vLLM's moe_align_block_size output)
+ *   topk_weights [size_m * top_k] fp32 (read only when mul_topk_weights)
+ *   c            [size_m * top_k, N], dtype of a, row stride ldc
+ * moe_block_size in [1, 64]; K % 32 == 0.
+ */
+int fp4_moe_mxf4(const void* a, int64_t lda, int dtype, const void* w_codes, const void* w_sf_tiled,
+                 int64_t num_experts, const int32_t* sorted_token_ids, const int32_t* expert_ids,
+                 const int32_t* num_tokens_post_padded, const float* topk_weights, int64_t num_sorted,
+                 int moe_block_size, int top_k, int mul_topk_weights, void* c, int64_t ldc,
+                 int64_t size_m, int64_t N, int64_t K, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

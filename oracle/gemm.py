@@ -58,3 +58,47 @@ def random_mxfp4_weight(n: int, k: int, seed: int, exp_lo: int = -10, exp_hi: in
     codes = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
     scales = (127 + rng.integers(exp_lo, exp_hi + 1, size=(n, k // 32))).astype(np.uint8)
     return codes, scales
+
+
+def moe_align(topk_ids: np.ndarray, num_experts: int, block: int):
+    """vLLM's moe_align_block_size layout (vllm/model_executor/layers/fused_moe/
+    moe_align_block_size.py): the M*top_k token slots (slot = token * top_k + j)
+    grouped by expert in slot order, each expert's run padded to a multiple of
+    `block` with the sentinel M*top_k.  Returns int32 sorted_token_ids,
+    expert_ids (one per block) and num_tokens_post_padded [1]."""
+    m, top_k = topk_ids.shape
+    flat = topk_ids.reshape(-1)
+    sorted_ids, experts = [], []
+    for e in range(num_experts):
+        slots = np.nonzero(flat == e)[0]
+        if len(slots) == 0:
+            continue
+        pad = (-len(slots)) % block
+        sorted_ids.extend(slots.tolist() + [m * top_k] * pad)
+        experts.extend([e] * ((len(slots) + pad) // block))
+    return (np.array(sorted_ids, np.int32), np.array(experts, np.int32),
+            np.array([len(sorted_ids)], np.int32))
+
+
+def moe_linear_exact(a_bits: np.ndarray, w_codes: np.ndarray, w_scales: np.ndarray,
+                     sorted_ids: np.ndarray, expert_ids: np.ndarray, num_post_padded: int, block: int,
+                     top_k: int, topk_weights: np.ndarray | None = None, fp16: bool = False):
+    """Exact (float64) grouped MoE linear, the reference's "mxfp4_qdq(input),
+    then moe_wna16_marlin_gemm" (src/vllm_qdq_plugin/patch.py:139-152): for each
+    routed slot s of a block with expert e, out[s] = mxfp4_qdq(a[s // top_k]) .
+    dequant(W_e)^T (x topk_weights[s]).  Returns {slot: (row, absum row)}."""
+    m = a_bits.shape[0]
+    rows = {}
+    for b in range(num_post_padded // block):
+        e = int(expert_ids[b])
+        if e < 0:
+            continue
+        slots = [int(s) for s in sorted_ids[b * block:(b + 1) * block] if 0 <= s < m * top_k]
+        if not slots:
+            continue
+        tok = np.array([s // top_k for s in slots])
+        out, absum = qdq_linear_exact(a_bits[tok], w_codes[e], w_scales[e], fp16=fp16)
+        for i, s in enumerate(slots):
+            wgt = 1.0 if topk_weights is None else float(np.float32(topk_weights[s]))
+            rows[s] = (out[i] * wgt, absum[i] * abs(wgt))
+    return rows

@@ -165,3 +165,102 @@ def test_marlin_hook_routes_captured_layers(cuda_device):
     abits = a.view(torch.int16).numpy().view(np.uint16)
     exact, absum = og.qdq_linear_exact(abits, codes, scales)
     _check(out, exact, absum, "hook")
+
+
+# ------------------------------------------------------------------ grouped MoE GEMM
+def _moe_case(m, e, top_k, bs, n, k, seed, dtype=torch.bfloat16):
+    rng = np.random.default_rng(seed)
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(m, k, generator=g).to(dtype)
+    ws = [og.random_mxfp4_weight(n, k, seed * 31 + i) for i in range(e)]
+    codes = np.stack([c for c, _ in ws])
+    scales = np.stack([s for _, s in ws])
+    topk_ids = np.stack([rng.permutation(e)[:top_k] for _ in range(m)])  # distinct experts per token
+    sorted_ids, expert_ids, ntp = og.moe_align(topk_ids, e, bs)
+    topk_w = rng.random((m, top_k)).astype(np.float32)
+    return a, codes, scales, sorted_ids, expert_ids, ntp, topk_w
+
+
+@pytest.mark.parametrize("m,e,top_k,bs,n,k,mul", [(5, 4, 2, 16, 256, 512, False),
+                                                  (37, 8, 2, 16, 384, 1024, True),
+                                                  (64, 16, 4, 32, 200, 2048, True),
+                                                  (3, 4, 1, 64, 128, 288, False),
+                                                  (100, 8, 8, 8, 256, 512, True)])
+def test_moe_grouped_gemm_matches_oracle(cuda_device, m, e, top_k, bs, n, k, mul):
+    """Grouped MXFP4 MoE GEMM (the reference's mxfp4_qdq + moe_wna16_marlin_gemm)
+    on vLLM's moe_align_block_size layout: every routed slot's row against the
+    exact oracle, with the fused GEMM's tolerance."""
+    from vllm_qdq_plugin.gemm import mxfp4_moe_linear, prepare_mxfp4_moe_weight
+    a, codes, scales, sid, eid, ntp, topk_w = _moe_case(m, e, top_k, bs, n, k, seed=m + e + bs)
+    dev = cuda_device
+    w = prepare_mxfp4_moe_weight(torch.from_numpy(codes).to(dev), torch.from_numpy(scales).to(dev))
+    out = mxfp4_moe_linear(a.to(dev), w, torch.from_numpy(sid).to(dev), torch.from_numpy(eid).to(dev),
+                           torch.from_numpy(ntp).to(dev), torch.from_numpy(topk_w).to(dev), bs, top_k, mul)
+    rows = og.moe_linear_exact(a.view(torch.int16).numpy().view(np.uint16), codes, scales, sid, eid,
+                               int(ntp[0]), bs, top_k, topk_w.reshape(-1) if mul else None)
+    assert len(rows) == m * top_k
+    got = out.float().cpu().numpy()
+    slots = np.array(sorted(rows))
+    exact = np.stack([rows[s][0] for s in slots])
+    absum = np.stack([rows[s][1] for s in slots])
+    _check(torch.from_numpy(got[slots]), exact, absum, f"moe m={m} e={e} top_k={top_k} bs={bs}")
+    from vllm_qdq_plugin import _native
+    assert _native.device_status() == 0
+
+
+def test_moe_skips_foreign_experts_and_padding_blocks(cuda_device):
+    """Blocks whose expert id is -1 (not on this rank) and blocks past
+    num_tokens_post_padded leave their rows untouched; fp16 activations."""
+    from vllm_qdq_plugin.gemm import mxfp4_moe_linear, prepare_mxfp4_moe_weight
+    m, e, top_k, bs, n, k = 24, 4, 2, 16, 256, 512
+    a, codes, scales, sid, eid, ntp, topk_w = _moe_case(m, e, top_k, bs, n, k, seed=5, dtype=torch.float16)
+    eid = eid.copy()
+    eid[1] = -1
+    sid_ext = np.concatenate([sid, np.arange(bs, dtype=np.int32)])  # a trailing block beyond ntp
+    eid_ext = np.concatenate([eid, np.array([0], np.int32)])
+    dev = cuda_device
+    w = prepare_mxfp4_moe_weight(torch.from_numpy(codes).to(dev), torch.from_numpy(scales).to(dev))
+    out = torch.full((m * top_k, n), 7.0, dtype=torch.float16, device=dev)
+    mxfp4_moe_linear(a.to(dev), w, torch.from_numpy(sid_ext).to(dev), torch.from_numpy(eid_ext).to(dev),
+                     torch.from_numpy(ntp).to(dev), None, bs, top_k, False, out=out)
+    rows = og.moe_linear_exact(a.view(torch.int16).numpy().view(np.uint16), codes, scales, sid, eid,
+                               int(ntp[0]), bs, top_k, fp16=True)
+    got = out.float().cpu().numpy()
+    skipped = [int(s) for s in sid[bs:2 * bs] if s < m * top_k]
+    for s in range(m * top_k):
+        if s in rows:
+            _check(torch.from_numpy(got[s:s + 1]), rows[s][0][None], rows[s][1][None], f"slot {s}")
+        else:
+            assert s in skipped and (got[s] == 7.0).all(), s
+
+
+def test_moe_marlin_hook_routes_captured_layers(cuda_device):
+    """VLLM_QDQ_FUSED_GEMM=1: the patched moe_wna16_marlin_gemm runs the grouped
+    FP4 GEMM for a captured MXFP4 MoE weight instead of QDQ + Marlin."""
+    import os
+    import types
+    from unittest import mock
+
+    from vllm_qdq_plugin import gemm, patch
+    from vllm_qdq_plugin.qdq import mxfp4_qdq
+    m, e, top_k, bs, n, k = 16, 4, 2, 16, 256, 512
+    a, codes, scales, sid, eid, ntp, topk_w = _moe_case(m, e, top_k, bs, n, k, seed=9)
+    dev = cuda_device
+    marlin_w = torch.zeros(8, dtype=torch.int32, device=dev)  # stands for the repacked expert weights
+    gemm.register_marlin_moe_weight(marlin_w, gemm.prepare_mxfp4_moe_weight(
+        torch.from_numpy(codes).to(dev), torch.from_numpy(scales).to(dev)))
+    st = types.SimpleNamespace(float4_e2m1f=object(), float8_e4m3fn=object())
+    ops = types.SimpleNamespace(
+        moe_wna16_marlin_gemm=lambda *args: (_ for _ in ()).throw(AssertionError("Marlin called")))
+    patch._patch_moe_marlin_gemm(ops, st, mxfp4_qdq, None, lambda *t: None)
+    tw = torch.from_numpy(topk_w).to(dev)
+    with mock.patch.dict(os.environ, {"VLLM_QDQ_FUSED_GEMM": "1"}):
+        out = ops.moe_wna16_marlin_gemm(
+            a.to(dev), None, marlin_w, None, torch.empty(1), None, None, None, None, None, torch.empty(1),
+            torch.from_numpy(sid).to(dev), torch.from_numpy(eid).to(dev), torch.from_numpy(ntp).to(dev),
+            tw, bs, top_k, True, st.float4_e2m1f, m, n, k, True, False, True, False)
+    rows = og.moe_linear_exact(a.view(torch.int16).numpy().view(np.uint16), codes, scales, sid, eid,
+                               int(ntp[0]), bs, top_k, topk_w.reshape(-1))
+    slots = np.array(sorted(rows))
+    _check(out[torch.from_numpy(slots).to(dev)], np.stack([rows[s][0] for s in slots]),
+           np.stack([rows[s][1] for s in slots]), "moe hook")

@@ -254,6 +254,226 @@ int launch_decode(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* s
   return check_launch("fp4_linear_decode");
 }
 
+// ---------------------------------------------------------------------------
+// Grouped MXFP4 MoE GEMM (replaces moe_wna16_marlin_gemm for MXFP4 experts)
+// ---------------------------------------------------------------------------
+// One CTA per (sorted block b, 128 rows of the block's expert W): the block's
+// token slots (moe_block_size <= 64, all routed to expert_ids[b]) are gathered,
+// quantised to MXFP4 in the producer and multiplied against W_e with the same
+// swap-AB MMAs as the decode kernel.  Stage: W codes | A codes | W scales | A scales.
+template <int kNA>
+struct MLayout {
+  static constexpr int A_TILE = kNA * DBKB;
+  static constexpr int ST_W = 0, ST_A = W_TILE, ST_SFW = W_TILE + A_TILE, ST_SFA = ST_SFW + SF_STAGE;
+  static constexpr int STAGE = (ST_SFA + SF_STAGE + 1023) / 1024 * 1024;
+  static constexpr int STAGES = 6;
+};
+struct __align__(8) MBars {
+  uint64_t full[6];    // W bytes landed (1 arrival + tx) + the gathered slice quantised (128 arrivals)
+  uint64_t empty[6];   // the stage's MMAs completed
+  uint64_t acc_full;
+  uint32_t tmem_base;
+  int abort;
+  int32_t slot[64];    // the block's token slots (-1: padding)
+};
+template <int kNA>
+constexpr size_t m_smem_bytes() {
+  return 1024 + static_cast<size_t>(MLayout<kNA>::STAGES) * MLayout<kNA>::STAGE + sizeof(MBars);
+}
+
+template <int kDtype, int kNA>
+__global__ void __launch_bounds__(D_THREADS, 1)
+mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __restrict__ a, int64_t lda,
+                const uint8_t* __restrict__ sfw, int64_t sf_per_expert, const int32_t* __restrict__ sorted_ids,
+                const int32_t* __restrict__ expert_ids, const int32_t* __restrict__ num_post_padded,
+                const float* __restrict__ topk_w, int mul_topk, int top_k, int bs, int num_experts,
+                void* __restrict__ c_v, int64_t ldc, int size_m, int N, int K, int kchunks, int* status) {
+  using Lay = MLayout<kNA>;
+  constexpr int S = Lay::STAGES;
+  constexpr bool kF16 = kDtype == QDQ_DTYPE_FP16;
+  using O = DOut<kF16>;
+  using T = typename O::T;
+  T* C = static_cast<T*>(c_v);
+  const int blk = blockIdx.y, n_tile = blockIdx.x;
+  // blocks past the padded token count, or of experts not on this rank, do nothing
+  if (blk * bs >= __ldg(num_post_padded)) return;
+  const int e = __ldg(expert_ids + blk);
+  if (e < 0 || e >= num_experts) return;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  MBars* bars = reinterpret_cast<MBars*>(smem + S * Lay::STAGE);
+  const int warp = threadIdx.x >> 5;
+  const int num_kt = (K + DBK - 1) / DBK;
+  const int n_slots = size_m * top_k;
+
+  constexpr int kZero = (Lay::A_TILE + 2 * SF_STAGE) / 16;
+  for (int i = threadIdx.x; i < S * kZero; i += D_THREADS) {
+    const int st = i / kZero, o = (i % kZero) * 16;
+    if (o < Lay::A_TILE || o >= Lay::A_TILE + SF_STAGE)
+      *reinterpret_cast<uint4*>(smem + st * Lay::STAGE + Lay::ST_A + o) = make_uint4(0, 0, 0, 0);
+  }
+  if (threadIdx.x < 64) {
+    const int s = threadIdx.x < bs ? __ldg(sorted_ids + blk * bs + threadIdx.x) : -1;
+    bars->slot[threadIdx.x] = (s >= 0 && s < n_slots) ? s : -1;
+  }
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < S; ++st) {
+      mbar_init(&bars->full[st], 1 + 128);
+      mbar_init(&bars->empty[st], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    bars->abort = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmap_w);
+  }
+  if (warp == 0) {
+    tmem_alloc(&bars->tmem_base, D_TMEM_COLS);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const int64_t w_row0 = static_cast<int64_t>(e) * N + static_cast<int64_t>(n_tile) * DBM;
+
+  if (warp == 0) {
+    // ---------------- W_e producer
+    if (elect_one()) {
+      int issued = 0;
+      for (int kt = 0; kt < num_kt; ++kt) {
+        const int st = kt % S;
+        if (!mbar_wait(&bars->empty[st], ((kt / S) & 1) ^ 1, status, 0x501)) {
+          bars->abort = 1;
+          break;
+        }
+        if (*(volatile int*)&bars->abort) break;
+        uint8_t* sp = smem + st * Lay::STAGE;
+        mbar_arrive_expect_tx(&bars->full[st], W_TILE + SF_STAGE);
+        tma_load_2d(sp + Lay::ST_W, &tmap_w, kt * DBKB, static_cast<int32_t>(w_row0), &bars->full[st]);
+        bulk_load(sp + Lay::ST_SFW,
+                  sfw + e * sf_per_expert + (static_cast<int64_t>(n_tile) * kchunks + 2 * kt) * 512, SF_STAGE,
+                  &bars->full[st]);
+        ++issued;
+      }
+      for (int kt = (issued > S ? issued - S : 0); kt < issued; ++kt)
+        mbar_wait(&bars->full[kt % S], (kt / S) & 1, status, 0x502);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_mxf4(DBM, kNA, true);
+      bool ok = true;
+      for (int kt = 0; kt < num_kt; ++kt) {
+        const int st = kt % S;
+        if (!mbar_wait(&bars->full[st], (kt / S) & 1, status, 0x503)) { ok = false; break; }
+        if (*(volatile int*)&bars->abort) { ok = false; break; }
+        tc_fence_after();
+        uint8_t* sp = smem + st * Lay::STAGE;
+        tmem_cp_sf(tmem + T_SFW + 0, smem_desc_sf(sp + Lay::ST_SFW));
+        tmem_cp_sf(tmem + T_SFW + 4, smem_desc_sf(sp + Lay::ST_SFW + 512));
+        tmem_cp_sf(tmem + T_SFA + 0, smem_desc_sf(sp + Lay::ST_SFA));
+        tmem_cp_sf(tmem + T_SFA + 4, smem_desc_sf(sp + Lay::ST_SFA + 512));
+        const uint64_t dw = smem_desc_sw128(sp + Lay::ST_W);
+        const uint64_t da = smem_desc_sw128(sp + Lay::ST_A);
+#pragma unroll
+        for (int kk = 0; kk < DBK / 64; ++kk) {
+          const uint32_t j = kk >> 1, sf_id = (kk & 1) * 2;
+          mma_mxf4(tmem + T_ACC, dw + ((kk * 32) >> 4), da + ((kk * 32) >> 4),
+                   idesc_with_sf_ids(idesc, sf_id, sf_id), (tmem + T_SFW + 4 * j) | (sf_id << 30),
+                   (tmem + T_SFA + 4 * j) | (sf_id << 30), (kt | kk) != 0);
+        }
+        tc_commit(&bars->empty[st]);
+      }
+      if (!ok) bars->abort = 1;
+      tc_commit(&bars->acc_full);
+    }
+  } else {
+    // ---------------- gather + quantise the block's token rows, then the epilogue
+    const int tq = threadIdx.x - 64;
+    const int lane = threadIdx.x & 31;
+    bool ok = true;
+    for (int kt = 0; kt < num_kt; ++kt) {
+      const int st = kt % S;
+      if (ok) ok = mbar_wait(&bars->empty[st], ((kt / S) & 1) ^ 1, status, 0x504);
+      uint8_t* sp = smem + st * Lay::STAGE;
+      for (int it = tq; it < bs * (DBK / 32); it += 128) {
+        const int i = it >> 3, g = it & 7;
+        const int s = bars->slot[i];
+        if (s < 0) continue;  // padding slot: its row stays zero
+        const int k0 = kt * DBK + g * 32;
+        const uint16_t* src = a + static_cast<int64_t>(s / top_k) * lda + k0;
+        uint4 v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          v[q] = (k0 + 8 * q < K) ? *reinterpret_cast<const uint4*>(src + 8 * q) : make_uint4(0, 0, 0, 0);
+        uint32_t code[4];
+        const int ex = mx_group_codes<kDtype>(v, code);
+        *reinterpret_cast<uint4*>(sp + Lay::ST_A + i * DBKB + ((g ^ (i & 7)) << 4)) =
+            make_uint4(code[0], code[1], code[2], code[3]);
+        sp[Lay::ST_SFA + (g >> 2) * 512 + (i & 31) * 16 + ((i >> 5) & 3) * 4 + (g & 3)] = static_cast<uint8_t>(ex);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->full[st]);
+    }
+    // epilogue: TMEM lanes = W rows, columns = the block's slots
+    if (ok) ok = mbar_wait(&bars->acc_full, 0, status, 0x505);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    const int q = warp & 3;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + T_ACC;
+    constexpr int NC = kNA > 32 ? 2 : 1;
+    uint32_t r[NC][32];
+#pragma unroll
+    for (int h = 0; h < NC; ++h) tmem_ld32(taddr + 32 * h, r[h]);
+    tmem_ld_wait();
+    const int n = n_tile * DBM + q * 32 + lane;
+    if (ok && !*(volatile int*)&bars->abort && n < N) {
+#pragma unroll
+      for (int h = 0; h < NC; ++h)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int slot_i = 32 * h + i;
+          if (slot_i >= bs) continue;
+          const int s = bars->slot[slot_i];
+          if (s < 0) continue;
+          float v = __uint_as_float(r[h][i]);
+          if (mul_topk) v *= __ldg(topk_w + s);
+          C[static_cast<int64_t>(s) * ldc + n] = O::one(v);
+        }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, D_TMEM_COLS);
+  }
+}
+
+template <int kDtype, int kNA>
+int launch_moe(const CUtensorMap& tw, const uint16_t* a, int64_t lda, const uint8_t* sf, int64_t sf_per_expert,
+               const int32_t* sorted_ids, const int32_t* expert_ids, const int32_t* npp, const float* topk_w,
+               int mul, int top_k, int bs, int num_experts, int64_t num_blocks, void* c, int64_t ldc, int64_t size_m,
+               int64_t N, int64_t K, int kchunks, int* status, cudaStream_t s) {
+  constexpr size_t smem = m_smem_bytes<kNA>();
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(&mxf4_moe_kernel<kDtype, kNA>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_moe_mxf4: smem attribute: %s", cudaGetErrorString(e));
+    attr_set[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>((N + DBM - 1) / DBM), static_cast<unsigned>(num_blocks));
+  mxf4_moe_kernel<kDtype, kNA><<<grid, D_THREADS, smem, s>>>(
+      tw, a, lda, sf, sf_per_expert, sorted_ids, expert_ids, npp, topk_w, mul, top_k, bs, num_experts, c, ldc,
+      static_cast<int>(size_m), static_cast<int>(N), static_cast<int>(K), kchunks, status);
+  return check_launch("fp4_moe_mxf4");
+}
+
 }  // namespace
 
 // Host entry used by fp4_linear_mxf4 for M <= 64 (declared in common.cuh).
@@ -286,3 +506,55 @@ int fp4_linear_decode(const void* a, int64_t lda, int dtype, const void* w_codes
 }
 
 }  // namespace qdqb200
+
+using namespace qdqb200;
+
+extern "C" int fp4_moe_mxf4(const void* a, int64_t lda, int dtype, const void* w_codes, const void* w_sf_tiled,
+                            int64_t num_experts, const int32_t* sorted_token_ids, const int32_t* expert_ids,
+                            const int32_t* num_tokens_post_padded, const float* topk_weights, int64_t num_sorted,
+                            int moe_block_size, int top_k, int mul_topk_weights, void* c, int64_t ldc,
+                            int64_t size_m, int64_t N, int64_t K, void* stream) {
+  if (dtype != QDQ_DTYPE_BF16 && dtype != QDQ_DTYPE_FP16)
+    return fail(QDQ_ERR_INVALID_ARG, "fp4_moe_mxf4: dtype must be bf16 (0) or fp16 (1)");
+  if (size_m < 0 || N < 0 || K < 0 || num_sorted < 0 || num_experts < 0)
+    return fail(QDQ_ERR_INVALID_ARG, "fp4_moe_mxf4: negative size");
+  if (moe_block_size < 1 || moe_block_size > NA_MAX)
+    return fail(QDQ_ERR_UNSUPPORTED, "fp4_moe_mxf4: moe_block_size must be in [1, 64] (got %d)", moe_block_size);
+  if (top_k < 1) return fail(QDQ_ERR_INVALID_ARG, "fp4_moe_mxf4: top_k must be >= 1");
+  if (size_m == 0 || N == 0 || num_sorted == 0 || num_experts == 0) return QDQ_OK;
+  if (K == 0 || K % 32 != 0)
+    return fail(QDQ_ERR_UNSUPPORTED, "fp4_moe_mxf4: K=%lld must be a positive multiple of 32", (long long)K);
+  if (!a || !w_codes || !w_sf_tiled || !sorted_token_ids || !expert_ids || !num_tokens_post_padded || !c ||
+      (mul_topk_weights && !topk_weights))
+    return fail(QDQ_ERR_INVALID_ARG, "fp4_moe_mxf4: null pointer");
+  if (lda < K || ldc < N) return fail(QDQ_ERR_INVALID_ARG, "fp4_moe_mxf4: leading dimension too small");
+  if ((reinterpret_cast<uintptr_t>(a) & 15) || ((lda * 2) & 15) || (reinterpret_cast<uintptr_t>(w_sf_tiled) & 15))
+    return fail(QDQ_ERR_ALIGNMENT, "fp4_moe_mxf4: activation rows and scale buffer must be 16-byte aligned");
+  if (num_experts * N > (1ll << 31) || size_m * top_k > (1ll << 31))
+    return fail(QDQ_ERR_UNSUPPORTED, "fp4_moe_mxf4: too many rows");
+  int* status = device_status_ptr();
+  if (status == nullptr) return QDQ_ERR_CUDA;
+  CUtensorMap tw;
+  if (int st = make_tmap_u8_2d(&tw, w_codes, num_experts * N, K / 2, K / 2, DBKB, DBM, 128)) return st;
+  const int64_t num_blocks = num_sorted / moe_block_size;
+  const int64_t sf_per_expert = qdq_sf_tiled_bytes(N, K);
+  const int kchunks = static_cast<int>(((K / 32) + 7) / 8 * 8 / 4);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto* ap = static_cast<const uint16_t*>(a);
+  auto* sf = static_cast<const uint8_t*>(w_sf_tiled);
+  const int na = moe_block_size <= 16 ? 16 : (moe_block_size <= 32 ? 32 : 64);
+  const int E = static_cast<int>(num_experts);
+#define QDQ_MOE_LAUNCH(DT, NA)                                                                                 \
+  return launch_moe<DT, NA>(tw, ap, lda, sf, sf_per_expert, sorted_token_ids, expert_ids, num_tokens_post_padded, \
+                            topk_weights, mul_topk_weights, top_k, moe_block_size, E, num_blocks, c, ldc, size_m, N, \
+                            K, kchunks, status, s)
+  if (dtype == QDQ_DTYPE_FP16) {
+    if (na == 16) QDQ_MOE_LAUNCH(QDQ_DTYPE_FP16, 16);
+    if (na == 32) QDQ_MOE_LAUNCH(QDQ_DTYPE_FP16, 32);
+    QDQ_MOE_LAUNCH(QDQ_DTYPE_FP16, 64);
+  }
+  if (na == 16) QDQ_MOE_LAUNCH(QDQ_DTYPE_BF16, 16);
+  if (na == 32) QDQ_MOE_LAUNCH(QDQ_DTYPE_BF16, 32);
+  QDQ_MOE_LAUNCH(QDQ_DTYPE_BF16, 64);
+#undef QDQ_MOE_LAUNCH
+}

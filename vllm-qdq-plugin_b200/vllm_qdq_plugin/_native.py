@@ -45,6 +45,8 @@ _SIGNATURES: dict[str, list] = {
     "sage3_fp4_attn": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64,
                        ctypes.POINTER(ctypes.c_int64), _f32, _int, _int, _int, _int, _int, _c_void_p,
                        _i64, _c_void_p],
+    "fp4_moe_mxf4": [_c_void_p, _i64, _int, _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p,
+                     _c_void_p, _i64, _int, _int, _int, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p],
     "qdq_sf_tiled_bytes": [_i64, _i64],
     "qdq_sf_tile": [_c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p],
     "fp4_gemm_mxf4": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64,

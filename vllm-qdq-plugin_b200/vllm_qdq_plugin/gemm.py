@@ -190,3 +190,144 @@ def capture_marlin_weights() -> bool:
     mu.prepare_fp4_layer_for_marlin = prepare_fp4_layer_for_marlin
     logger.warning("vllm-qdq-plugin: capturing raw MXFP4 weights for the fused FP4 GEMM")
     return True
+
+
+# ---------------------------------------------------------------------------
+# Grouped MXFP4 MoE GEMM (replaces QDQ + moe_wna16_marlin_gemm for MXFP4 experts)
+# ---------------------------------------------------------------------------
+@dataclasses.dataclass
+class Mxfp4MoeWeight:
+    """MXFP4 expert weights [E, N, K] in the layout the grouped tcgen05 GEMM reads."""
+
+    codes: torch.Tensor     # uint8 [E, N, K/2], element 2j in the low nibble
+    sf_tiled: torch.Tensor  # uint8 [E * qdq_sf_tiled_bytes(N, K)], per-expert tiled E8M0 scales
+    e: int
+    n: int
+    k: int
+
+
+def prepare_mxfp4_moe_weight(codes: torch.Tensor, scales: torch.Tensor) -> Mxfp4MoeWeight:
+    """codes uint8 [E, N, K/2] (packed E2M1), scales uint8 [E, N, K/32] (E8M0)."""
+    _native.require_cuda(codes, scales)
+    codes = codes.view(torch.uint8).contiguous()
+    scales = scales.view(torch.uint8).contiguous()
+    e, n, kh = codes.shape
+    k = kh * 2
+    assert k % 32 == 0 and scales.shape == (e, n, k // 32), (codes.shape, scales.shape)
+    per = _native.lib().qdq_sf_tiled_bytes(n, k)
+    sf = torch.empty((e * per,), dtype=torch.uint8, device=codes.device)
+    sp = _native.stream_ptr(codes.device)
+    for i in range(e):
+        _native.call("qdq_sf_tile", scales[i].data_ptr(), sf[i * per:].data_ptr(), n, k, scales.stride(1), 32, sp)
+    return Mxfp4MoeWeight(codes=codes, sf_tiled=sf, e=e, n=n, k=k)
+
+
+@torch.library.custom_op("qdq_b200::mxfp4_moe_linear", mutates_args=("out",))
+def _moe_op(a: torch.Tensor, w_codes: torch.Tensor, w_sf_tiled: torch.Tensor, sorted_token_ids: torch.Tensor,
+            expert_ids: torch.Tensor, num_tokens_post_padded: torch.Tensor, topk_weights: torch.Tensor | None,
+            moe_block_size: int, top_k: int, mul_topk_weights: bool, out: torch.Tensor) -> None:
+    _native.require_cuda(a, w_codes, w_sf_tiled, sorted_token_ids, expert_ids, num_tokens_post_padded, out)
+    a = a if a.stride(-1) == 1 else a.contiguous()
+    e, n, kh = w_codes.shape
+    _native.call("fp4_moe_mxf4", a.data_ptr(), a.stride(0) if a.shape[0] > 1 else a.shape[1],
+                 _native.DTYPE_CODE[a.dtype], w_codes.data_ptr(), w_sf_tiled.data_ptr(), e,
+                 sorted_token_ids.data_ptr(), expert_ids.data_ptr(), num_tokens_post_padded.data_ptr(),
+                 _native.ptr(topk_weights), sorted_token_ids.numel(), moe_block_size, top_k,
+                 int(mul_topk_weights), out.data_ptr(), out.stride(0), a.shape[0], n, kh * 2,
+                 _native.stream_ptr(a.device))
+
+
+@_moe_op.register_fake
+def _(a, w_codes, w_sf_tiled, sorted_token_ids, expert_ids, num_tokens_post_padded, topk_weights,
+      moe_block_size, top_k, mul_topk_weights, out):
+    return None
+
+
+def mxfp4_moe_linear(a: torch.Tensor, weight: Mxfp4MoeWeight, sorted_token_ids: torch.Tensor,
+                     expert_ids: torch.Tensor, num_tokens_post_padded: torch.Tensor,
+                     topk_weights: torch.Tensor | None, moe_block_size: int, top_k: int,
+                     mul_topk_weights: bool, out: torch.Tensor | None = None) -> torch.Tensor:
+    """For every routed slot s (vLLM's moe_align_block_size layout):
+    out[s] = mxfp4_qdq(a[s // top_k]) @ dequant(W[expert of s's block])^T (x topk_weights[s]).
+
+    a: [M, K] bf16/fp16; out: [M * top_k, N] (allocated when None; rows of
+    slots that are not routed keep their contents)."""
+    assert a.dim() == 2 and a.dtype in (torch.bfloat16, torch.float16) and a.shape[1] == weight.k
+    assert sorted_token_ids.dtype == torch.int32 and expert_ids.dtype == torch.int32
+    if out is None:
+        out = torch.empty((a.shape[0] * top_k, weight.n), dtype=a.dtype, device=a.device)
+    tw = topk_weights.reshape(-1).float().contiguous() if topk_weights is not None else None
+    torch.ops.qdq_b200.mxfp4_moe_linear(a, weight.codes, weight.sf_tiled, sorted_token_ids, expert_ids,
+                                        num_tokens_post_padded, tw, moe_block_size, top_k,
+                                        bool(mul_topk_weights), out)
+    return out
+
+
+_MOE_REGISTRY: dict[int, Mxfp4MoeWeight] = {}
+
+
+def register_marlin_moe_weight(marlin_weight: torch.Tensor, weight: Mxfp4MoeWeight) -> None:
+    with _REG_LOCK:
+        _MOE_REGISTRY[marlin_weight.data_ptr()] = weight
+
+
+def fused_moe_marlin_replacement(input, output, b_qweight, b_bias, a_scales, global_scale, sorted_token_ids,
+                                 expert_ids, num_tokens_past_padded, topk_weights, moe_block_size, top_k,
+                                 mul_topk_weights, size_m, size_n, size_k):
+    """The grouped FP4 GEMM for a captured MXFP4 MoE layer; None means "keep
+    the reference path" (not captured, bias, NVFP4 global scale, 8-bit input)."""
+    w = _MOE_REGISTRY.get(b_qweight.data_ptr())
+    if (w is None or b_bias is not None or a_scales is not None or global_scale is not None
+            or input.dim() != 2 or input.dtype not in (torch.bfloat16, torch.float16)
+            or tuple(input.shape) != (size_m, size_k) or w.n != size_n or w.k != size_k
+            or not 1 <= moe_block_size <= 64 or sorted_token_ids.dtype != torch.int32
+            or expert_ids.dtype != torch.int32):
+        return None
+    return mxfp4_moe_linear(input, w, sorted_token_ids, expert_ids, num_tokens_past_padded, topk_weights,
+                            moe_block_size, top_k, mul_topk_weights, output)
+
+
+def capture_moe_weights() -> bool:
+    """Wrap vLLM's MXFP4 MoE Marlin preparation (in-place and pure variants,
+    marlin_utils_fp4.py prepare_moe_fp4_layer_for_marlin /
+    prepare_moe_mxfp4_layer_for_marlin) to keep each layer's raw expert weights."""
+    try:
+        from vllm.model_executor.layers.quantization.utils import marlin_utils_fp4 as mu
+    except ImportError:
+        return False
+
+    def keep(marlin_w13, marlin_w2, w13, w13_scale, w2, w2_scale):
+        if w13.is_cuda:
+            register_marlin_moe_weight(marlin_w13, prepare_mxfp4_moe_weight(w13, w13_scale))
+            register_marlin_moe_weight(marlin_w2, prepare_mxfp4_moe_weight(w2, w2_scale))
+
+    original = getattr(mu, "prepare_moe_fp4_layer_for_marlin", None)
+    if original is not None and not getattr(original, "_qdq_b200_capture", False):
+        @functools.wraps(original)
+        def prepare_moe_fp4_layer_for_marlin(layer, input_dtype=None):
+            raw = None
+            if not hasattr(layer, "w13_weight_scale_2") and (input_dtype is None or input_dtype.itemsize != 1):
+                raw = (layer.w13_weight.data, layer.w13_weight_scale.data, layer.w2_weight.data,
+                       layer.w2_weight_scale.data)
+            result = original(layer, input_dtype)
+            if raw is not None:
+                keep(layer.w13_weight, layer.w2_weight, *raw)
+            return result
+
+        prepare_moe_fp4_layer_for_marlin._qdq_b200_capture = True
+        mu.prepare_moe_fp4_layer_for_marlin = prepare_moe_fp4_layer_for_marlin
+
+    pure = getattr(mu, "prepare_moe_mxfp4_layer_for_marlin", None)
+    if pure is not None and not getattr(pure, "_qdq_b200_capture", False):
+        @functools.wraps(pure)
+        def prepare_moe_mxfp4_layer_for_marlin(layer, w13, w2, w13_scale, w2_scale, w13_bias, w2_bias):
+            result = pure(layer, w13, w2, w13_scale, w2_scale, w13_bias, w2_bias)
+            input_dtype = mu.get_marlin_input_dtype()
+            if input_dtype is None or input_dtype.itemsize != 1:
+                keep(result[0], result[1], w13, w13_scale, w2, w2_scale)
+            return result
+
+        prepare_moe_mxfp4_layer_for_marlin._qdq_b200_capture = True
+        mu.prepare_moe_mxfp4_layer_for_marlin = prepare_moe_mxfp4_layer_for_marlin
+    logger.warning("vllm-qdq-plugin: capturing raw MXFP4 MoE weights for the grouped FP4 GEMM")
+    return True

@@ -103,6 +103,8 @@ def _patch_moe_marlin_gemm(ops, scalar_types, mxfp4_qdq, mxfp8_qdq, trace_qdq):
       b_q_type float4_e2m1f and 2-D -> MXFP4 QDQ;
       b_q_type float8_e4m3fn and 2-D -> MXFP8 QDQ.
     No activation dtype check on this path, as in the reference.
+    With VLLM_QDQ_FUSED_GEMM=1, MXFP4 experts whose raw weights were captured
+    (vllm_qdq_plugin.gemm.capture_moe_weights) run the grouped FP4 GEMM instead.
     """
     original = ops.moe_wna16_marlin_gemm
 
@@ -137,6 +139,16 @@ def _patch_moe_marlin_gemm(ops, scalar_types, mxfp4_qdq, mxfp8_qdq, trace_qdq):
         thread_n: int = -1,
         blocks_per_sm: int = -1,
     ) -> torch.Tensor:
+        if (envs.VLLM_QDQ_FUSED_GEMM and input.dim() == 2 and b_q_type == scalar_types.float4_e2m1f
+                and global_scale is None):
+            from .gemm import fused_moe_marlin_replacement
+            out = fused_moe_marlin_replacement(
+                input, output, b_qweight, b_bias, a_scales, global_scale, sorted_token_ids, expert_ids,
+                num_tokens_past_padded, topk_weights, moe_block_size, top_k, mul_topk_weights, size_m,
+                size_n, size_k)
+            if out is not None:
+                trace_qdq("moe_wna16_marlin_gemm", input.shape, input.dtype)
+                return out
         if input.dim() == 2:
             if envs.VLLM_MARLIN_MOE_QDQ_MODE == "FORCE_MXFP4":
                 trace_qdq("moe_wna16_marlin_gemm", input.shape, input.dtype)
@@ -221,6 +233,17 @@ def apply_patches():
     from .trace import trace_qdq
 
     _patch_mla_kv_b_proj_dtype()
+    if envs.VLLM_QDQ_FUSED_GEMM:
+        from . import gemm
+        from vllm.model_executor.layers.quantization.utils import marlin_utils_fp4 as mu
+        before = {name: getattr(mu, name, None) for name in
+                  ("prepare_fp4_layer_for_marlin", "prepare_moe_fp4_layer_for_marlin",
+                   "prepare_moe_mxfp4_layer_for_marlin")}
+        gemm.capture_marlin_weights()
+        gemm.capture_moe_weights()
+        # modules that imported a preparation function by name keep the original
+        _rebind_direct_imports([(name, orig, getattr(mu, name)) for name, orig in before.items()
+                                if orig is not None and getattr(mu, name) is not orig])
     patches = [
         _patch_marlin_gemm(ops, scalar_types, mxfp4_qdq, mxfp8_qdq, trace_qdq),
         _patch_moe_marlin_gemm(ops, scalar_types, mxfp4_qdq, mxfp8_qdq, trace_qdq),
