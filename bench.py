@@ -770,12 +770,13 @@ def run_moe(args, wl, world, rank, dev, dist) -> None:
     lib = _native.lib()
     stream = torch.cuda.current_stream(dev)
     slots = int((sid < m * top_k).sum())
+    ws = torch.empty((lib.fp4_moe_workspace_bytes(sidd.numel(), bs, k),), dtype=torch.uint8, device=dev)
 
     def step(sp=None):
         _native.check("fp4_moe_mxf4", lib.fp4_moe_mxf4(
             a.data_ptr(), k, 0, w.codes.data_ptr(), w.sf_tiled.data_ptr(), e, sidd.data_ptr(), eidd.data_ptr(),
             ntpd.data_ptr(), twd.data_ptr(), sidd.numel(), bs, top_k, 1, out.data_ptr(), n, m, n, k,
-            sp if sp is not None else torch.cuda.current_stream(dev).cuda_stream))
+            ws.data_ptr(), ws.numel(), sp if sp is not None else torch.cuda.current_stream(dev).cuda_stream))
 
     def barrier():
         if dist is not None:
@@ -853,7 +854,7 @@ def run_moe(args, wl, world, rank, dev, dist) -> None:
                     "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in hosts),
                     "d2h_bytes_per_step": out_host.numel() * 2,
                     "path": "vllm_qdq_plugin.gemm.mxfp4_moe_linear on pinned host buffers"},
-            "gpu_launches": steps,
+            "gpu_launches": 2 * steps,  # gather-quantise + grouped GEMM
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4), "peak_source": src,
                          "traffic": None, "hbm_floor_ms": round(w_bytes / (measured_peak_hbm()[0] * 1e9) * 1e3, 4)},

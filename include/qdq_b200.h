@@ -244,13 +244,18 @@ int fp4_linear_mxf4_noalloc(const void* a, int64_t lda, int dtype, const void* w
  *   num_tokens_post_padded [1]: int32 device arrays (vLLM's moe_align_block_size output)
  *   topk_weights [size_m * top_k] fp32 (read only when mul_topk_weights)
  *   c            [size_m * top_k, N], dtype of a, row stride ldc
+ *   workspace    device scratch of fp4_moe_workspace_bytes(num_sorted, moe_block_size, K)
+ *                bytes, 256-byte aligned: the routed activation rows quantised once, in
+ *                sorted order
  * moe_block_size in [1, 64]; K % 32 == 0.
  */
+int64_t fp4_moe_workspace_bytes(int64_t num_sorted, int moe_block_size, int64_t K);
 int fp4_moe_mxf4(const void* a, int64_t lda, int dtype, const void* w_codes, const void* w_sf_tiled,
                  int64_t num_experts, const int32_t* sorted_token_ids, const int32_t* expert_ids,
                  const int32_t* num_tokens_post_padded, const float* topk_weights, int64_t num_sorted,
                  int moe_block_size, int top_k, int mul_topk_weights, void* c, int64_t ldc,
-                 int64_t size_m, int64_t N, int64_t K, void* stream);
+                 int64_t size_m, int64_t N, int64_t K, void* workspace, int64_t workspace_bytes,
+                 void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

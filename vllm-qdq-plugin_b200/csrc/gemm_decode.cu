@@ -257,10 +257,40 @@ int launch_decode(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* s
 // ---------------------------------------------------------------------------
 // Grouped MXFP4 MoE GEMM (replaces moe_wna16_marlin_gemm for MXFP4 experts)
 // ---------------------------------------------------------------------------
-// One CTA per (sorted block b, 128 rows of the block's expert W): the block's
-// token slots (moe_block_size <= 64, all routed to expert_ids[b]) are gathered,
-// quantised to MXFP4 in the producer and multiplied against W_e with the same
-// swap-AB MMAs as the decode kernel.  Stage: W codes | A codes | W scales | A scales.
+// Pre-pass: the activation rows in sorted-slot order (vLLM's
+// moe_align_block_size layout), quantised to MXFP4 once: codes [num_sorted,
+// K/2] and, per block of moe_block_size slots, the E8M0 scales in the tiled
+// layout (rows 0..bs-1 of one 128-row chunk set).  Padding slots are zero.
+// Then one CTA per (sorted block, 128 rows of the block's expert W) streams
+// W_e and the block's codes by TMA and runs the swap-AB MMAs of the decode
+// kernel.  Stage: W codes | A codes | W scales | A scales.
+template <int kDtype>
+__global__ void __launch_bounds__(256)
+moe_gather_quant_kernel(const uint16_t* __restrict__ a, int64_t lda, const int32_t* __restrict__ sorted_ids,
+                        const int32_t* __restrict__ num_post_padded, int64_t num_sorted, int bs, int top_k,
+                        int n_slots, int K, int kchunks, uint8_t* __restrict__ codes, uint8_t* __restrict__ sf) {
+  const int gpr = K / 32;
+  const int64_t total = num_sorted * gpr;
+  const int npp = __ldg(num_post_padded);
+  for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < total;
+       it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t p = it / gpr;
+    const int g = static_cast<int>(it - p * gpr);
+    const int s = p < npp ? __ldg(sorted_ids + p) : -1;
+    uint32_t code[4] = {0u, 0u, 0u, 0u};
+    int e = 0;
+    if (s >= 0 && s < n_slots) {
+      const uint4* src = reinterpret_cast<const uint4*>(a + static_cast<int64_t>(s / top_k) * lda + g * 32);
+      uint4 v[4] = {src[0], src[1], src[2], src[3]};
+      e = mx_group_codes<kDtype>(v, code);
+    }
+    *reinterpret_cast<uint4*>(codes + p * (K / 2) + g * 16) = make_uint4(code[0], code[1], code[2], code[3]);
+    const int64_t b = p / bs;
+    const int r = static_cast<int>(p - b * bs);
+    sf[(b * kchunks + g / 4) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (g & 3)] = static_cast<uint8_t>(e);
+  }
+}
+
 template <int kNA>
 struct MLayout {
   static constexpr int A_TILE = kNA * DBKB;
@@ -269,7 +299,7 @@ struct MLayout {
   static constexpr int STAGES = 6;
 };
 struct __align__(8) MBars {
-  uint64_t full[6];    // W bytes landed (1 arrival + tx) + the gathered slice quantised (128 arrivals)
+  uint64_t full[6];    // W, the block's codes and both scale chunks landed (1 arrival + tx)
   uint64_t empty[6];   // the stage's MMAs completed
   uint64_t acc_full;
   uint32_t tmem_base;
@@ -283,11 +313,12 @@ constexpr size_t m_smem_bytes() {
 
 template <int kDtype, int kNA>
 __global__ void __launch_bounds__(D_THREADS, 1)
-mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __restrict__ a, int64_t lda,
-                const uint8_t* __restrict__ sfw, int64_t sf_per_expert, const int32_t* __restrict__ sorted_ids,
-                const int32_t* __restrict__ expert_ids, const int32_t* __restrict__ num_post_padded,
-                const float* __restrict__ topk_w, int mul_topk, int top_k, int bs, int num_experts,
-                void* __restrict__ c_v, int64_t ldc, int size_m, int N, int K, int kchunks, int* status) {
+mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
+                const uint8_t* __restrict__ sfw, int64_t sf_per_expert, const uint8_t* __restrict__ sfa,
+                const int32_t* __restrict__ sorted_ids, const int32_t* __restrict__ expert_ids,
+                const int32_t* __restrict__ num_post_padded, const float* __restrict__ topk_w, int mul_topk,
+                int top_k, int bs, int num_experts, void* __restrict__ c_v, int64_t ldc, int size_m, int N, int K,
+                int kchunks, int* status) {
   using Lay = MLayout<kNA>;
   constexpr int S = Lay::STAGES;
   constexpr bool kF16 = kDtype == QDQ_DTYPE_FP16;
@@ -306,31 +337,25 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __re
   const int num_kt = (K + DBK - 1) / DBK;
   const int n_slots = size_m * top_k;
 
-  constexpr int kZero = (Lay::A_TILE + 2 * SF_STAGE) / 16;
-  for (int i = threadIdx.x; i < S * kZero; i += D_THREADS) {
-    const int st = i / kZero, o = (i % kZero) * 16;
-    if (o < Lay::A_TILE || o >= Lay::A_TILE + SF_STAGE)
-      *reinterpret_cast<uint4*>(smem + st * Lay::STAGE + Lay::ST_A + o) = make_uint4(0, 0, 0, 0);
-  }
   if (threadIdx.x < 64) {
     const int s = threadIdx.x < bs ? __ldg(sorted_ids + blk * bs + threadIdx.x) : -1;
     bars->slot[threadIdx.x] = (s >= 0 && s < n_slots) ? s : -1;
   }
   if (threadIdx.x == 0) {
     for (int st = 0; st < S; ++st) {
-      mbar_init(&bars->full[st], 1 + 128);
+      mbar_init(&bars->full[st], 1);
       mbar_init(&bars->empty[st], 1);
     }
     mbar_init(&bars->acc_full, 1);
     bars->abort = 0;
     fence_barrier_init();
     prefetch_tmap(&tmap_w);
+    prefetch_tmap(&tmap_a);
   }
   if (warp == 0) {
     tmem_alloc(&bars->tmem_base, D_TMEM_COLS);
     tmem_relinquish();
   }
-  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -338,7 +363,7 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __re
   const int64_t w_row0 = static_cast<int64_t>(e) * N + static_cast<int64_t>(n_tile) * DBM;
 
   if (warp == 0) {
-    // ---------------- W_e producer
+    // ---------------- producer: W_e tile, the block's codes, both scale chunks
     if (elect_one()) {
       int issued = 0;
       for (int kt = 0; kt < num_kt; ++kt) {
@@ -349,10 +374,13 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __re
         }
         if (*(volatile int*)&bars->abort) break;
         uint8_t* sp = smem + st * Lay::STAGE;
-        mbar_arrive_expect_tx(&bars->full[st], W_TILE + SF_STAGE);
+        mbar_arrive_expect_tx(&bars->full[st], W_TILE + Lay::A_TILE + 2 * SF_STAGE);
         tma_load_2d(sp + Lay::ST_W, &tmap_w, kt * DBKB, static_cast<int32_t>(w_row0), &bars->full[st]);
+        tma_load_2d(sp + Lay::ST_A, &tmap_a, kt * DBKB, blk * bs, &bars->full[st]);
         bulk_load(sp + Lay::ST_SFW,
                   sfw + e * sf_per_expert + (static_cast<int64_t>(n_tile) * kchunks + 2 * kt) * 512, SF_STAGE,
+                  &bars->full[st]);
+        bulk_load(sp + Lay::ST_SFA, sfa + (static_cast<int64_t>(blk) * kchunks + 2 * kt) * 512, SF_STAGE,
                   &bars->full[st]);
         ++issued;
       }
@@ -389,35 +417,9 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __re
       tc_commit(&bars->acc_full);
     }
   } else {
-    // ---------------- gather + quantise the block's token rows, then the epilogue
-    const int tq = threadIdx.x - 64;
+    // ---------------- epilogue: TMEM lanes = W rows, columns = the block's slots
     const int lane = threadIdx.x & 31;
-    bool ok = true;
-    for (int kt = 0; kt < num_kt; ++kt) {
-      const int st = kt % S;
-      if (ok) ok = mbar_wait(&bars->empty[st], ((kt / S) & 1) ^ 1, status, 0x504);
-      uint8_t* sp = smem + st * Lay::STAGE;
-      for (int it = tq; it < bs * (DBK / 32); it += 128) {
-        const int i = it >> 3, g = it & 7;
-        const int s = bars->slot[i];
-        if (s < 0) continue;  // padding slot: its row stays zero
-        const int k0 = kt * DBK + g * 32;
-        const uint16_t* src = a + static_cast<int64_t>(s / top_k) * lda + k0;
-        uint4 v[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          v[q] = (k0 + 8 * q < K) ? *reinterpret_cast<const uint4*>(src + 8 * q) : make_uint4(0, 0, 0, 0);
-        uint32_t code[4];
-        const int ex = mx_group_codes<kDtype>(v, code);
-        *reinterpret_cast<uint4*>(sp + Lay::ST_A + i * DBKB + ((g ^ (i & 7)) << 4)) =
-            make_uint4(code[0], code[1], code[2], code[3]);
-        sp[Lay::ST_SFA + (g >> 2) * 512 + (i & 31) * 16 + ((i >> 5) & 3) * 4 + (g & 3)] = static_cast<uint8_t>(ex);
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&bars->full[st]);
-    }
-    // epilogue: TMEM lanes = W rows, columns = the block's slots
-    if (ok) ok = mbar_wait(&bars->acc_full, 0, status, 0x505);
+    bool ok = mbar_wait(&bars->acc_full, 0, status, 0x505);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     const int q = warp & 3;
@@ -453,10 +455,10 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const uint16_t* __re
 }
 
 template <int kDtype, int kNA>
-int launch_moe(const CUtensorMap& tw, const uint16_t* a, int64_t lda, const uint8_t* sf, int64_t sf_per_expert,
-               const int32_t* sorted_ids, const int32_t* expert_ids, const int32_t* npp, const float* topk_w,
-               int mul, int top_k, int bs, int num_experts, int64_t num_blocks, void* c, int64_t ldc, int64_t size_m,
-               int64_t N, int64_t K, int kchunks, int* status, cudaStream_t s) {
+int launch_moe(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* sf, int64_t sf_per_expert,
+               const uint8_t* sfa, const int32_t* sorted_ids, const int32_t* expert_ids, const int32_t* npp,
+               const float* topk_w, int mul, int top_k, int bs, int num_experts, int64_t num_blocks, void* c,
+               int64_t ldc, int64_t size_m, int64_t N, int64_t K, int kchunks, int* status, cudaStream_t s) {
   constexpr size_t smem = m_smem_bytes<kNA>();
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -469,7 +471,7 @@ int launch_moe(const CUtensorMap& tw, const uint16_t* a, int64_t lda, const uint
   }
   dim3 grid(static_cast<unsigned>((N + DBM - 1) / DBM), static_cast<unsigned>(num_blocks));
   mxf4_moe_kernel<kDtype, kNA><<<grid, D_THREADS, smem, s>>>(
-      tw, a, lda, sf, sf_per_expert, sorted_ids, expert_ids, npp, topk_w, mul, top_k, bs, num_experts, c, ldc,
+      tw, ta, sf, sf_per_expert, sfa, sorted_ids, expert_ids, npp, topk_w, mul, top_k, bs, num_experts, c, ldc,
       static_cast<int>(size_m), static_cast<int>(N), static_cast<int>(K), kchunks, status);
   return check_launch("fp4_moe_mxf4");
 }
@@ -509,11 +511,21 @@ int fp4_linear_decode(const void* a, int64_t lda, int dtype, const void* w_codes
 
 using namespace qdqb200;
 
+static int64_t moe_kchunks(int64_t K) { return ((K / 32) + 7) / 8 * 8 / 4; }
+
+extern "C" int64_t fp4_moe_workspace_bytes(int64_t num_sorted, int moe_block_size, int64_t K) {
+  if (num_sorted <= 0 || moe_block_size <= 0 || K <= 0) return 0;
+  auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
+  const int64_t blocks = (num_sorted + moe_block_size - 1) / moe_block_size;
+  return up(num_sorted * ((K + 31) / 32 * 16)) + up(blocks * moe_kchunks(K) * 512);
+}
+
 extern "C" int fp4_moe_mxf4(const void* a, int64_t lda, int dtype, const void* w_codes, const void* w_sf_tiled,
                             int64_t num_experts, const int32_t* sorted_token_ids, const int32_t* expert_ids,
                             const int32_t* num_tokens_post_padded, const float* topk_weights, int64_t num_sorted,
                             int moe_block_size, int top_k, int mul_topk_weights, void* c, int64_t ldc,
-                            int64_t size_m, int64_t N, int64_t K, void* stream) {
+                            int64_t size_m, int64_t N, int64_t K, void* workspace, int64_t workspace_bytes,
+                            void* stream) {
   if (dtype != QDQ_DTYPE_BF16 && dtype != QDQ_DTYPE_FP16)
     return fail(QDQ_ERR_INVALID_ARG, "fp4_moe_mxf4: dtype must be bf16 (0) or fp16 (1)");
   if (size_m < 0 || N < 0 || K < 0 || num_sorted < 0 || num_experts < 0)
@@ -530,22 +542,45 @@ extern "C" int fp4_moe_mxf4(const void* a, int64_t lda, int dtype, const void* w
   if (lda < K || ldc < N) return fail(QDQ_ERR_INVALID_ARG, "fp4_moe_mxf4: leading dimension too small");
   if ((reinterpret_cast<uintptr_t>(a) & 15) || ((lda * 2) & 15) || (reinterpret_cast<uintptr_t>(w_sf_tiled) & 15))
     return fail(QDQ_ERR_ALIGNMENT, "fp4_moe_mxf4: activation rows and scale buffer must be 16-byte aligned");
-  if (num_experts * N > (1ll << 31) || size_m * top_k > (1ll << 31))
+  if (num_experts * N > (1ll << 31) || size_m * top_k > (1ll << 31) || num_sorted > (1ll << 31))
     return fail(QDQ_ERR_UNSUPPORTED, "fp4_moe_mxf4: too many rows");
+  if (workspace == nullptr || workspace_bytes < fp4_moe_workspace_bytes(num_sorted, moe_block_size, K) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return fail(QDQ_ERR_INVALID_ARG, "fp4_moe_mxf4: workspace missing, unaligned or smaller than "
+                                     "fp4_moe_workspace_bytes()");
   int* status = device_status_ptr();
   if (status == nullptr) return QDQ_ERR_CUDA;
-  CUtensorMap tw;
-  if (int st = make_tmap_u8_2d(&tw, w_codes, num_experts * N, K / 2, K / 2, DBKB, DBM, 128)) return st;
+  const int kchunks = static_cast<int>(moe_kchunks(K));
   const int64_t num_blocks = num_sorted / moe_block_size;
-  const int64_t sf_per_expert = qdq_sf_tiled_bytes(N, K);
-  const int kchunks = static_cast<int>(((K / 32) + 7) / 8 * 8 / 4);
+  auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
+  uint8_t* a_codes = static_cast<uint8_t*>(workspace);
+  uint8_t* a_sf = a_codes + up(num_sorted * (K / 2));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto* ap = static_cast<const uint16_t*>(a);
-  auto* sf = static_cast<const uint8_t*>(w_sf_tiled);
+  // 1) gather + quantise the routed rows in sorted order (zero at padding)
+  {
+    const int64_t items = num_sorted * (K / 32);
+    const int grid = static_cast<int>(std::min<int64_t>((items + 255) / 256, static_cast<int64_t>(device_sm_count()) * 8));
+    if (dtype == QDQ_DTYPE_FP16)
+      moe_gather_quant_kernel<QDQ_DTYPE_FP16><<<grid, 256, 0, s>>>(
+          ap, lda, sorted_token_ids, num_tokens_post_padded, num_sorted, moe_block_size, top_k,
+          static_cast<int>(size_m * top_k), static_cast<int>(K), kchunks, a_codes, a_sf);
+    else
+      moe_gather_quant_kernel<QDQ_DTYPE_BF16><<<grid, 256, 0, s>>>(
+          ap, lda, sorted_token_ids, num_tokens_post_padded, num_sorted, moe_block_size, top_k,
+          static_cast<int>(size_m * top_k), static_cast<int>(K), kchunks, a_codes, a_sf);
+    if (int st = check_launch("fp4_moe_mxf4 (gather)")) return st;
+  }
+  // 2) grouped GEMM
   const int na = moe_block_size <= 16 ? 16 : (moe_block_size <= 32 ? 32 : 64);
+  CUtensorMap tw, ta;
+  if (int st = make_tmap_u8_2d(&tw, w_codes, num_experts * N, K / 2, K / 2, DBKB, DBM, 128)) return st;
+  if (int st = make_tmap_u8_2d(&ta, a_codes, num_sorted, K / 2, K / 2, DBKB, na, 128)) return st;
+  const int64_t sf_per_expert = qdq_sf_tiled_bytes(N, K);
+  auto* sf = static_cast<const uint8_t*>(w_sf_tiled);
   const int E = static_cast<int>(num_experts);
-#define QDQ_MOE_LAUNCH(DT, NA)                                                                                 \
-  return launch_moe<DT, NA>(tw, ap, lda, sf, sf_per_expert, sorted_token_ids, expert_ids, num_tokens_post_padded, \
+#define QDQ_MOE_LAUNCH(DT, NA)                                                                                  \
+  return launch_moe<DT, NA>(tw, ta, sf, sf_per_expert, a_sf, sorted_token_ids, expert_ids, num_tokens_post_padded, \
                             topk_weights, mul_topk_weights, top_k, moe_block_size, E, num_blocks, c, ldc, size_m, N, \
                             K, kchunks, status, s)
   if (dtype == QDQ_DTYPE_FP16) {

@@ -46,7 +46,9 @@ _SIGNATURES: dict[str, list] = {
                        ctypes.POINTER(ctypes.c_int64), _f32, _int, _int, _int, _int, _int, _c_void_p,
                        _i64, _c_void_p],
     "fp4_moe_mxf4": [_c_void_p, _i64, _int, _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p,
-                     _c_void_p, _i64, _int, _int, _int, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p],
+                     _c_void_p, _i64, _int, _int, _int, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _i64,
+                     _c_void_p],
+    "fp4_moe_workspace_bytes": [_i64, _int, _i64],
     "qdq_sf_tiled_bytes": [_i64, _i64],
     "qdq_sf_tile": [_c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p],
     "fp4_gemm_mxf4": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64,
@@ -61,7 +63,8 @@ _SIGNATURES: dict[str, list] = {
 _RESTYPES = {"qdq_last_error": ctypes.c_char_p, "qdq_sf_tiled_bytes": ctypes.c_int64,
              "fp4_linear_workspace_bytes": ctypes.c_int64,
              "fp4_linear_noalloc_scratch_bytes": ctypes.c_int64,
-             "sage3_attn_workspace_bytes": ctypes.c_int64}
+             "sage3_attn_workspace_bytes": ctypes.c_int64,
+             "fp4_moe_workspace_bytes": ctypes.c_int64}
 
 
 def lib() -> ctypes.CDLL:

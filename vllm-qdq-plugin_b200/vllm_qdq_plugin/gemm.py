@@ -229,12 +229,15 @@ def _moe_op(a: torch.Tensor, w_codes: torch.Tensor, w_sf_tiled: torch.Tensor, so
     _native.require_cuda(a, w_codes, w_sf_tiled, sorted_token_ids, expert_ids, num_tokens_post_padded, out)
     a = a if a.stride(-1) == 1 else a.contiguous()
     e, n, kh = w_codes.shape
+    lib = _native.lib()
+    ws = torch.empty((lib.fp4_moe_workspace_bytes(sorted_token_ids.numel(), moe_block_size, kh * 2),),
+                     dtype=torch.uint8, device=a.device)
     _native.call("fp4_moe_mxf4", a.data_ptr(), a.stride(0) if a.shape[0] > 1 else a.shape[1],
                  _native.DTYPE_CODE[a.dtype], w_codes.data_ptr(), w_sf_tiled.data_ptr(), e,
                  sorted_token_ids.data_ptr(), expert_ids.data_ptr(), num_tokens_post_padded.data_ptr(),
                  _native.ptr(topk_weights), sorted_token_ids.numel(), moe_block_size, top_k,
                  int(mul_topk_weights), out.data_ptr(), out.stride(0), a.shape[0], n, kh * 2,
-                 _native.stream_ptr(a.device))
+                 ws.data_ptr(), ws.numel(), _native.stream_ptr(a.device))
 
 
 @_moe_op.register_fake
