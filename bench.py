@@ -837,9 +837,16 @@ def run_moe(args, wl, world, rank, dev, dist) -> None:
     barrier()
     e2e = world * flop / (a0.elapsed_time(a1) / n_e2e * 1e-3) / 1e12
     if rank == 0:
-        peak, src = measured_peak_fp4()
-        achieved = flop / (ms_step * 1e-3) / 1e12
+        peak, src = measured_peak_hbm()
+        fp4_peak, _ = measured_peak_fp4()
         w_bytes = w.codes.numel() + w.sf_tiled.numel()
+        # Algorithmic bytes of one step: the codes and scales of every expert
+        # that owns a live block, the activation rows read once, and the routed
+        # output rows written once (the sorted-order workspace stays in L2).
+        live = eidd[: (int(ntpd.item()) + bs - 1) // bs]
+        hit = int(torch.unique(live[(live >= 0) & (live < e)]).numel())
+        alg_bytes = hit * (w_bytes // e) + m * k * 2 + slots * n * 2
+        achieved = alg_bytes / (ms_step * 1e-3) / 1e9
         line = {
             "metric": "FP4 MoE GEMM TFLOPS (2 x routed slots x N x K)", "value": round(value, 1),
             "unit": "TFLOP/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
@@ -855,9 +862,13 @@ def run_moe(args, wl, world, rank, dev, dist) -> None:
                     "d2h_bytes_per_step": out_host.numel() * 2,
                     "path": "vllm_qdq_plugin.gemm.mxfp4_moe_linear on pinned host buffers"},
             "gpu_launches": 2 * steps,  # gather-quantise + grouped GEMM
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": src,
-                         "traffic": None, "hbm_floor_ms": round(w_bytes / (measured_peak_hbm()[0] * 1e9) * 1e3, 4)},
+                         "traffic": ncu_traffic(f"mxfp4_moe_{m}"),
+                         "algorithmic_bytes": alg_bytes, "experts_hit": hit,
+                         "hbm_floor_ms": round(alg_bytes / (peak * 1e9) * 1e3, 4),
+                         "tensor_frac": round(flop / (ms_step * 1e-3) / 1e12 / fp4_peak, 4),
+                         "kernels": "moe_gather_quant_kernel + mxf4_moe_kernel (one C-ABI call)"},
             "clocks": sampler.summary(t_wall0, t_wall1) if sampler else None,
         }
         if world == 1 and not args.no_cpu_baseline:

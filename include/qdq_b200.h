@@ -246,7 +246,7 @@ int fp4_linear_mxf4_noalloc(const void* a, int64_t lda, int dtype, const void* w
  *   c            [size_m * top_k, N], dtype of a, row stride ldc
  *   workspace    device scratch of fp4_moe_workspace_bytes(num_sorted, moe_block_size, K)
  *                bytes, 256-byte aligned: the routed activation rows quantised once, in
- *                sorted order
+ *                sorted order, and the table of same-expert block runs the GEMM walks
  * moe_block_size in [1, 64]; K % 32 == 0.
  */
 int64_t fp4_moe_workspace_bytes(int64_t num_sorted, int moe_block_size, int64_t K);

@@ -257,21 +257,99 @@ int launch_decode(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* s
 // ---------------------------------------------------------------------------
 // Grouped MXFP4 MoE GEMM (replaces moe_wna16_marlin_gemm for MXFP4 experts)
 // ---------------------------------------------------------------------------
-// Pre-pass: the activation rows in sorted-slot order (vLLM's
-// moe_align_block_size layout), quantised to MXFP4 once: codes [num_sorted,
-// K/2] and, per block of moe_block_size slots, the E8M0 scales in the tiled
-// layout (rows 0..bs-1 of one 128-row chunk set).  Padding slots are zero.
-// Then one CTA per (sorted block, 128 rows of the block's expert W) streams
-// W_e and the block's codes by TMA and runs the swap-AB MMAs of the decode
-// kernel.  Stage: W codes | A codes | W scales | A scales.
+// Pre-pass (moe_gather_quant_kernel): the activation rows in sorted-slot
+// order (vLLM's moe_align_block_size layout), quantised to MXFP4 once: codes
+// [num_sorted, K/2] and, per block of moe_block_size slots, the E8M0 scales in
+// the tiled layout (rows 0..bs-1 of one 128-row chunk set).  Padding slots are
+// zero.  Its first CTA also cuts the live blocks into segments: runs of at
+// most MOE_SEG_MAX consecutive blocks that name the same local expert.
+//
+// Then the grouped GEMM walks (segment, 128 rows of the expert's W) items: a
+// stage holds one W tile and the codes of each block of the segment, so W is
+// read once per segment instead of once per block; each block is its own
+// swap-AB MMA (M = 128 W rows, N = bs slots) with its own scale chunk.
+// Stage: W codes | A codes x 3 | W scales | A scales x 3.
+constexpr int MOE_SEG_MAX = 3;
+
+// Segment table in the workspace: [0] = count, [1 + i] = first block << 2 | blocks.
+__device__ void moe_segments(const int32_t* __restrict__ expert_ids, int nlive, int num_experts,
+                             int32_t* __restrict__ seg_tab) {
+  __shared__ int s_max[8], s_sum[8];
+  __shared__ int s_carry_rs, s_carry_cnt;
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  if (t == 0) {
+    s_carry_rs = -1;
+    s_carry_cnt = 0;
+  }
+  __syncthreads();
+  for (int base = 0; base < nlive; base += 256) {
+    const int b = base + t;
+    const int e = b < nlive ? __ldg(expert_ids + b) : -1;
+    const bool valid = b < nlive && e >= 0 && e < num_experts;
+    const int ep = (b > 0 && b <= nlive) ? __ldg(expert_ids + b - 1) : -1;
+    const bool start_run = valid && (b == 0 || ep != e);
+    // inclusive max-scan of run starts: the first block of b's run
+    int v = start_run ? b : -1;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, v, off);
+      if (lane >= off) v = max(v, o);
+    }
+    if (lane == 31) s_max[wid] = v;
+    __syncthreads();
+    if (wid == 0) {
+      int w = lane < 8 ? s_max[lane] : -1;
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, w, off);
+        if (lane >= off) w = max(w, o);
+      }
+      if (lane < 8) s_max[lane] = w;
+    }
+    __syncthreads();
+    v = max(v, wid > 0 ? s_max[wid - 1] : -1);
+    v = max(v, s_carry_rs);
+    const bool seg_start = valid && ((b - v) % MOE_SEG_MAX) == 0;
+    // exclusive sum-scan of segment starts
+    const unsigned bal = __ballot_sync(0xffffffffu, seg_start);
+    if (lane == 0) s_sum[wid] = __popc(bal);
+    __syncthreads();
+    int before = s_carry_cnt + __popc(bal & ((1u << lane) - 1u));
+    for (int w = 0; w < wid; ++w) before += s_sum[w];
+    if (seg_start) {
+      int nb = 1;
+      if (b + 1 < nlive && __ldg(expert_ids + b + 1) == e) {
+        ++nb;
+        if (MOE_SEG_MAX > 2 && b + 2 < nlive && __ldg(expert_ids + b + 2) == e) ++nb;
+      }
+      seg_tab[1 + before] = (b << 2) | nb;
+    }
+    __syncthreads();
+    if (t == 255) {
+      s_carry_rs = v;
+      int tot = 0;
+      for (int w = 0; w < 8; ++w) tot += s_sum[w];
+      s_carry_cnt += tot;
+    }
+    __syncthreads();
+  }
+  if (t == 0) seg_tab[0] = s_carry_cnt;
+}
+
 template <int kDtype>
 __global__ void __launch_bounds__(256)
 moe_gather_quant_kernel(const uint16_t* __restrict__ a, int64_t lda, const int32_t* __restrict__ sorted_ids,
-                        const int32_t* __restrict__ num_post_padded, int64_t num_sorted, int bs, int top_k,
-                        int n_slots, int K, int kchunks, uint8_t* __restrict__ codes, uint8_t* __restrict__ sf) {
+                        const int32_t* __restrict__ expert_ids, const int32_t* __restrict__ num_post_padded,
+                        int64_t num_sorted, int bs, int top_k, int n_slots, int num_experts, int K, int kchunks,
+                        uint8_t* __restrict__ codes, uint8_t* __restrict__ sf, int32_t* __restrict__ seg_tab) {
   const int gpr = K / 32;
   const int64_t total = num_sorted * gpr;
   const int npp = __ldg(num_post_padded);
+  if (blockIdx.x == 0) {
+    const int64_t nb = num_sorted / bs;
+    const int64_t live = npp <= 0 ? 0 : (static_cast<int64_t>(npp) + bs - 1) / bs;
+    moe_segments(expert_ids, static_cast<int>(live < nb ? live : nb), num_experts, seg_tab);
+  }
   for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < total;
        it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t p = it / gpr;
@@ -293,156 +371,228 @@ moe_gather_quant_kernel(const uint16_t* __restrict__ a, int64_t lda, const int32
 
 template <int kNA>
 struct MLayout {
-  static constexpr int A_TILE = kNA * DBKB;
-  static constexpr int ST_W = 0, ST_A = W_TILE, ST_SFW = W_TILE + A_TILE, ST_SFA = ST_SFW + SF_STAGE;
-  static constexpr int STAGE = (ST_SFA + SF_STAGE + 1023) / 1024 * 1024;
-  static constexpr int STAGES = 6;
+  static constexpr int A_TILE = kNA * DBKB;  // one block's codes per stage
+  static constexpr int ST_W = 0, ST_A = W_TILE, ST_SFW = ST_A + MOE_SEG_MAX * A_TILE, ST_SFA = ST_SFW + SF_STAGE;
+  static constexpr int STAGE = (ST_SFA + MOE_SEG_MAX * SF_STAGE + 1023) / 1024 * 1024;
+  static constexpr int STAGES = kNA == 64 ? 5 : (kNA == 32 ? 7 : 8);
 };
 struct __align__(8) MBars {
-  uint64_t full[6];    // W, the block's codes and both scale chunks landed (1 arrival + tx)
-  uint64_t empty[6];   // the stage's MMAs completed
-  uint64_t acc_full;
+  uint64_t full[8];       // W, the segment's codes and the scale chunks landed (1 arrival + tx)
+  uint64_t empty[8];      // the stage's MMAs completed
+  uint64_t acc_full[2];   // MMA -> epilogue, per accumulator buffer
+  uint64_t acc_empty[2];  // epilogue -> MMA (128 arrivals)
+  uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  int32_t slot[64];    // the block's token slots (-1: padding)
 };
 template <int kNA>
 constexpr size_t m_smem_bytes() {
   return 1024 + static_cast<size_t>(MLayout<kNA>::STAGES) * MLayout<kNA>::STAGE + sizeof(MBars);
 }
+static_assert(m_smem_bytes<16>() <= 227 * 1024 && m_smem_bytes<32>() <= 227 * 1024 &&
+              m_smem_bytes<64>() <= 227 * 1024, "MoE stages exceed shared memory");
+// TMEM of the MoE kernel: two accumulators of MOE_SEG_MAX x 64 columns, the
+// W scales (8 columns) and MOE_SEG_MAX x 8 columns of block scales.
+constexpr uint32_t M_ACC = 0, M_ACC_STRIDE = 64 * MOE_SEG_MAX, M_SFW = 2 * M_ACC_STRIDE, M_SFA = M_SFW + 8,
+                   M_TMEM_COLS = 512;
+static_assert(M_SFA + 8 * MOE_SEG_MAX <= M_TMEM_COLS, "MoE TMEM columns");
 
+// Persistent: CTA c takes work items c, c + gridDim.x, ...; item i is segment
+// i % nseg against 128-row W tile i / nseg, so the CTAs in flight cover
+// consecutive segments of one W tile row range.  The stage ring runs across
+// items and the accumulator is double-buffered, so an item's epilogue overlaps
+// the next item's MMAs.
 template <int kDtype, int kNA>
 __global__ void __launch_bounds__(D_THREADS, 1)
 mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
                 const uint8_t* __restrict__ sfw, int64_t sf_per_expert, const uint8_t* __restrict__ sfa,
-                const int32_t* __restrict__ sorted_ids, const int32_t* __restrict__ expert_ids,
-                const int32_t* __restrict__ num_post_padded, const float* __restrict__ topk_w, int mul_topk,
-                int top_k, int bs, int num_experts, void* __restrict__ c_v, int64_t ldc, int size_m, int N, int K,
-                int kchunks, int* status) {
+                const int32_t* __restrict__ seg_tab, const int32_t* __restrict__ sorted_ids,
+                const int32_t* __restrict__ expert_ids, const float* __restrict__ topk_w, int mul_topk, int top_k,
+                int bs, int num_blocks, int num_experts, void* __restrict__ c_v, int64_t ldc, int size_m, int N, int K, int kchunks, int* status) {
   using Lay = MLayout<kNA>;
   constexpr int S = Lay::STAGES;
   constexpr bool kF16 = kDtype == QDQ_DTYPE_FP16;
   using O = DOut<kF16>;
   using T = typename O::T;
   T* C = static_cast<T*>(c_v);
-  const int blk = blockIdx.y, n_tile = blockIdx.x;
-  // blocks past the padded token count, or of experts not on this rank, do nothing
-  if (blk * bs >= __ldg(num_post_padded)) return;
-  const int e = __ldg(expert_ids + blk);
-  if (e < 0 || e >= num_experts) return;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   MBars* bars = reinterpret_cast<MBars*>(smem + S * Lay::STAGE);
   const int warp = threadIdx.x >> 5;
   const int num_kt = (K + DBK - 1) / DBK;
   const int n_slots = size_m * top_k;
+  const int nseg = min(max(seg_tab[0], 0), num_blocks);
+  const int num_items = nseg * ((N + DBM - 1) / DBM);
+  // A segment entry every role decodes alike; a malformed one is skipped.
+  auto seg_of = [&](int item, int& blk0, int& nb, int& e) -> bool {
+    const int seg = seg_tab[1 + item % nseg];
+    blk0 = seg >> 2;
+    nb = seg & 3;
+    if (blk0 < 0 || nb < 1 || blk0 + nb > num_blocks) return false;
+    e = __ldg(expert_ids + blk0);
+    return e >= 0 && e < num_experts;
+  };
 
-  if (threadIdx.x < 64) {
-    const int s = threadIdx.x < bs ? __ldg(sorted_ids + blk * bs + threadIdx.x) : -1;
-    bars->slot[threadIdx.x] = (s >= 0 && s < n_slots) ? s : -1;
-  }
   if (threadIdx.x == 0) {
     for (int st = 0; st < S; ++st) {
       mbar_init(&bars->full[st], 1);
       mbar_init(&bars->empty[st], 1);
     }
-    mbar_init(&bars->acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->acc_full[i], 1);
+      mbar_init(&bars->acc_empty[i], 128);
+    }
+    mbar_init(&bars->drain, 1);
     bars->abort = 0;
     fence_barrier_init();
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_a);
   }
   if (warp == 0) {
-    tmem_alloc(&bars->tmem_base, D_TMEM_COLS);
+    tmem_alloc(&bars->tmem_base, M_TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const int64_t w_row0 = static_cast<int64_t>(e) * N + static_cast<int64_t>(n_tile) * DBM;
 
   if (warp == 0) {
-    // ---------------- producer: W_e tile, the block's codes, both scale chunks
+    // ---------------- producer: W_e tile, the segment's codes and scale chunks
     if (elect_one()) {
-      int issued = 0;
-      for (int kt = 0; kt < num_kt; ++kt) {
-        const int st = kt % S;
-        if (!mbar_wait(&bars->empty[st], ((kt / S) & 1) ^ 1, status, 0x501)) {
-          bars->abort = 1;
-          break;
+      int it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < num_items; item += gridDim.x) {
+        int blk0, nb, e;
+        if (!seg_of(item, blk0, nb, e)) continue;
+        const int n_tile = item / nseg;
+        const int64_t w_row0 = static_cast<int64_t>(e) * N + static_cast<int64_t>(n_tile) * DBM;
+        const uint8_t* sfw_e = sfw + e * sf_per_expert + static_cast<int64_t>(n_tile) * kchunks * 512;
+        for (int kt = 0; kt < num_kt; ++kt, ++it) {
+          const int st = it % S;
+          if (!mbar_wait(&bars->empty[st], ((it / S) & 1) ^ 1, status, 0x501)) {
+            bars->abort = 1;
+            ok = false;
+            break;
+          }
+          if (*(volatile int*)&bars->abort) { ok = false; break; }
+          uint8_t* sp = smem + st * Lay::STAGE;
+          mbar_arrive_expect_tx(&bars->full[st], W_TILE + SF_STAGE + nb * (Lay::A_TILE + SF_STAGE));
+          tma_load_2d(sp + Lay::ST_W, &tmap_w, kt * DBKB, static_cast<int32_t>(w_row0), &bars->full[st]);
+          bulk_load(sp + Lay::ST_SFW, sfw_e + 2 * kt * 512, SF_STAGE, &bars->full[st]);
+          for (int i = 0; i < nb; ++i) {
+            tma_load_2d(sp + Lay::ST_A + i * Lay::A_TILE, &tmap_a, kt * DBKB, (blk0 + i) * bs, &bars->full[st]);
+            bulk_load(sp + Lay::ST_SFA + i * SF_STAGE,
+                      sfa + (static_cast<int64_t>(blk0 + i) * kchunks + 2 * kt) * 512, SF_STAGE, &bars->full[st]);
+          }
         }
-        if (*(volatile int*)&bars->abort) break;
-        uint8_t* sp = smem + st * Lay::STAGE;
-        mbar_arrive_expect_tx(&bars->full[st], W_TILE + Lay::A_TILE + 2 * SF_STAGE);
-        tma_load_2d(sp + Lay::ST_W, &tmap_w, kt * DBKB, static_cast<int32_t>(w_row0), &bars->full[st]);
-        tma_load_2d(sp + Lay::ST_A, &tmap_a, kt * DBKB, blk * bs, &bars->full[st]);
-        bulk_load(sp + Lay::ST_SFW,
-                  sfw + e * sf_per_expert + (static_cast<int64_t>(n_tile) * kchunks + 2 * kt) * 512, SF_STAGE,
-                  &bars->full[st]);
-        bulk_load(sp + Lay::ST_SFA, sfa + (static_cast<int64_t>(blk) * kchunks + 2 * kt) * 512, SF_STAGE,
-                  &bars->full[st]);
-        ++issued;
       }
-      for (int kt = (issued > S ? issued - S : 0); kt < issued; ++kt)
-        mbar_wait(&bars->full[kt % S], (kt / S) & 1, status, 0x502);
+      for (int j = (it > S ? it - S : 0); j < it; ++j)
+        mbar_wait(&bars->full[j % S], (j / S) & 1, status, 0x502);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (elect_one()) {
       constexpr uint32_t idesc = idesc_mxf4(DBM, kNA, true);
+      int it = 0, j = 0;
       bool ok = true;
-      for (int kt = 0; kt < num_kt; ++kt) {
-        const int st = kt % S;
-        if (!mbar_wait(&bars->full[st], (kt / S) & 1, status, 0x503)) { ok = false; break; }
-        if (*(volatile int*)&bars->abort) { ok = false; break; }
+      for (int item = blockIdx.x; ok && item < num_items; item += gridDim.x) {
+        int blk0, nb, e;
+        if (!seg_of(item, blk0, nb, e)) continue;
+        const int buf = j & 1;
+        // the epilogue has read this buffer's previous item out of TMEM
+        if (!mbar_wait(&bars->acc_empty[buf], ((j >> 1) & 1) ^ 1, status, 0x506)) { ok = false; break; }
         tc_fence_after();
-        uint8_t* sp = smem + st * Lay::STAGE;
-        tmem_cp_sf(tmem + T_SFW + 0, smem_desc_sf(sp + Lay::ST_SFW));
-        tmem_cp_sf(tmem + T_SFW + 4, smem_desc_sf(sp + Lay::ST_SFW + 512));
-        tmem_cp_sf(tmem + T_SFA + 0, smem_desc_sf(sp + Lay::ST_SFA));
-        tmem_cp_sf(tmem + T_SFA + 4, smem_desc_sf(sp + Lay::ST_SFA + 512));
-        const uint64_t dw = smem_desc_sw128(sp + Lay::ST_W);
-        const uint64_t da = smem_desc_sw128(sp + Lay::ST_A);
+        const uint32_t acc = tmem + M_ACC + M_ACC_STRIDE * buf;
+        for (int kt = 0; kt < num_kt; ++kt, ++it) {
+          const int st = it % S;
+          if (!mbar_wait(&bars->full[st], (it / S) & 1, status, 0x503)) { ok = false; break; }
+          if (*(volatile int*)&bars->abort) { ok = false; break; }
+          tc_fence_after();
+          uint8_t* sp = smem + st * Lay::STAGE;
+          tmem_cp_sf(tmem + M_SFW + 0, smem_desc_sf(sp + Lay::ST_SFW));
+          tmem_cp_sf(tmem + M_SFW + 4, smem_desc_sf(sp + Lay::ST_SFW + 512));
+          for (int i = 0; i < nb; ++i) {
+            tmem_cp_sf(tmem + M_SFA + 8 * i + 0, smem_desc_sf(sp + Lay::ST_SFA + i * SF_STAGE));
+            tmem_cp_sf(tmem + M_SFA + 8 * i + 4, smem_desc_sf(sp + Lay::ST_SFA + i * SF_STAGE + 512));
+          }
+          const uint64_t dw = smem_desc_sw128(sp + Lay::ST_W);
 #pragma unroll
-        for (int kk = 0; kk < DBK / 64; ++kk) {
-          const uint32_t j = kk >> 1, sf_id = (kk & 1) * 2;
-          mma_mxf4(tmem + T_ACC, dw + ((kk * 32) >> 4), da + ((kk * 32) >> 4),
-                   idesc_with_sf_ids(idesc, sf_id, sf_id), (tmem + T_SFW + 4 * j) | (sf_id << 30),
-                   (tmem + T_SFA + 4 * j) | (sf_id << 30), (kt | kk) != 0);
+          for (int kk = 0; kk < DBK / 64; ++kk) {
+            const uint32_t jj = kk >> 1, sf_id = (kk & 1) * 2;
+            for (int i = 0; i < nb; ++i) {
+              const uint64_t da = smem_desc_sw128(sp + Lay::ST_A + i * Lay::A_TILE);
+              mma_mxf4(acc + 64 * i, dw + ((kk * 32) >> 4), da + ((kk * 32) >> 4),
+                       idesc_with_sf_ids(idesc, sf_id, sf_id), (tmem + M_SFW + 4 * jj) | (sf_id << 30),
+                       (tmem + M_SFA + 8 * i + 4 * jj) | (sf_id << 30), (kt | kk) != 0);
+            }
+          }
+          tc_commit(&bars->empty[st]);
         }
-        tc_commit(&bars->empty[st]);
+        if (!ok) break;
+        tc_commit(&bars->acc_full[buf]);
+        ++j;
       }
       if (!ok) bars->abort = 1;
-      tc_commit(&bars->acc_full);
+      tc_commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, status, 0x507);
     }
   } else {
-    // ---------------- epilogue: TMEM lanes = W rows, columns = the block's slots
+    // ---------------- epilogue: TMEM lanes = W rows, columns = the blocks' slots
     const int lane = threadIdx.x & 31;
-    bool ok = mbar_wait(&bars->acc_full, 0, status, 0x505);
-    ok = __all_sync(0xffffffffu, ok);
-    tc_fence_after();
     const int q = warp & 3;
-    const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + T_ACC;
     constexpr int NC = kNA > 32 ? 2 : 1;
-    uint32_t r[NC][32];
+    bool ok = true;
+    int j = 0;
+    for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
+      int blk0, nb, e;
+      if (!seg_of(item, blk0, nb, e)) continue;
+      const int n_tile = item / nseg;
+      // Routing of the segment, fetched while the MMAs run: lane l holds
+      // slot 32*h + l of block i (-1 for padding) and its routing weight.
+      int slot[MOE_SEG_MAX][NC];
+      float wt[MOE_SEG_MAX][NC];
 #pragma unroll
-    for (int h = 0; h < NC; ++h) tmem_ld32(taddr + 32 * h, r[h]);
-    tmem_ld_wait();
-    const int n = n_tile * DBM + q * 32 + lane;
-    if (ok && !*(volatile int*)&bars->abort && n < N) {
+      for (int i = 0; i < MOE_SEG_MAX; ++i)
 #pragma unroll
-      for (int h = 0; h < NC; ++h)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int slot_i = 32 * h + i;
-          if (slot_i >= bs) continue;
-          const int s = bars->slot[slot_i];
-          if (s < 0) continue;
-          float v = __uint_as_float(r[h][i]);
-          if (mul_topk) v *= __ldg(topk_w + s);
-          C[static_cast<int64_t>(s) * ldc + n] = O::one(v);
+        for (int h = 0; h < NC; ++h) {
+          const int si = 32 * h + lane;
+          int s = (i < nb && si < bs) ? __ldg(sorted_ids + static_cast<int64_t>(blk0 + i) * bs + si) : -1;
+          if (s >= n_slots) s = -1;
+          slot[i][h] = s;
+          wt[i][h] = (mul_topk && s >= 0) ? __ldg(topk_w + s) : 1.0f;
         }
+      const int buf = j & 1;
+      if (ok) ok = mbar_wait(&bars->acc_full[buf], (j >> 1) & 1, status, 0x505);
+      ok = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + M_ACC + M_ACC_STRIDE * buf;
+      const int n = n_tile * DBM + q * 32 + lane;
+      const bool in_n = n < N;
+      // warp-uniform: every lane takes part in the shuffles below
+      const bool store = __all_sync(0xffffffffu, ok && !*(volatile int*)&bars->abort);
+#pragma unroll
+      for (int i = 0; i < MOE_SEG_MAX; ++i) {
+        if (i >= nb) break;
+        uint32_t r[NC][32];
+#pragma unroll
+        for (int h = 0; h < NC; ++h) tmem_ld32(taddr + 64 * i + 32 * h, r[h]);
+        tmem_ld_wait();
+        if (i == nb - 1) {
+          tc_fence_before();
+          mbar_arrive(&bars->acc_empty[buf]);  // the next item on this buffer may start
+        }
+        if (!store) continue;
+#pragma unroll
+        for (int h = 0; h < NC; ++h)
+#pragma unroll
+          for (int l = 0; l < 32; ++l) {
+            const int s = __shfl_sync(0xffffffffu, slot[i][h], l);
+            const float w = __shfl_sync(0xffffffffu, wt[i][h], l);
+            if (s >= 0 && in_n) C[static_cast<int64_t>(s) * ldc + n] = O::one(__uint_as_float(r[h][l]) * w);
+          }
+      }
+      ++j;
     }
   }
 
@@ -450,15 +600,16 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, D_TMEM_COLS);
+    tmem_dealloc(tmem, M_TMEM_COLS);
   }
 }
 
 template <int kDtype, int kNA>
 int launch_moe(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* sf, int64_t sf_per_expert,
-               const uint8_t* sfa, const int32_t* sorted_ids, const int32_t* expert_ids, const int32_t* npp,
-               const float* topk_w, int mul, int top_k, int bs, int num_experts, int64_t num_blocks, void* c,
-               int64_t ldc, int64_t size_m, int64_t N, int64_t K, int kchunks, int* status, cudaStream_t s) {
+               const uint8_t* sfa, const int32_t* seg_tab, const int32_t* sorted_ids, const int32_t* expert_ids,
+               const float* topk_w, int mul, int top_k, int bs, int64_t num_blocks, int num_experts, void* c,
+               int64_t ldc,
+               int64_t size_m, int64_t N, int64_t K, int kchunks, int* status, cudaStream_t s) {
   constexpr size_t smem = m_smem_bytes<kNA>();
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -469,9 +620,13 @@ int launch_moe(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* sf, 
     if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_moe_mxf4: smem attribute: %s", cudaGetErrorString(e));
     attr_set[dev] = true;
   }
-  dim3 grid(static_cast<unsigned>((N + DBM - 1) / DBM), static_cast<unsigned>(num_blocks));
+  // at most one segment per block; the kernel reads the actual count
+  const int64_t items = num_blocks * ((N + DBM - 1) / DBM);
+  const int sms = device_sm_count();
+  dim3 grid(static_cast<unsigned>(std::min<int64_t>(items, sms > 0 ? sms : 148)));
   mxf4_moe_kernel<kDtype, kNA><<<grid, D_THREADS, smem, s>>>(
-      tw, ta, sf, sf_per_expert, sfa, sorted_ids, expert_ids, npp, topk_w, mul, top_k, bs, num_experts, c, ldc,
+      tw, ta, sf, sf_per_expert, sfa, seg_tab, sorted_ids, expert_ids, topk_w, mul, top_k, bs,
+      static_cast<int>(num_blocks), num_experts, c, ldc,
       static_cast<int>(size_m), static_cast<int>(N), static_cast<int>(K), kchunks, status);
   return check_launch("fp4_moe_mxf4");
 }
@@ -517,7 +672,7 @@ extern "C" int64_t fp4_moe_workspace_bytes(int64_t num_sorted, int moe_block_siz
   if (num_sorted <= 0 || moe_block_size <= 0 || K <= 0) return 0;
   auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
   const int64_t blocks = (num_sorted + moe_block_size - 1) / moe_block_size;
-  return up(num_sorted * ((K + 31) / 32 * 16)) + up(blocks * moe_kchunks(K) * 512);
+  return up(num_sorted * ((K + 31) / 32 * 16)) + up(blocks * moe_kchunks(K) * 512) + up(4 * (blocks + 1));
 }
 
 extern "C" int fp4_moe_mxf4(const void* a, int64_t lda, int dtype, const void* w_codes, const void* w_sf_tiled,
@@ -552,9 +707,12 @@ extern "C" int fp4_moe_mxf4(const void* a, int64_t lda, int dtype, const void* w
   if (status == nullptr) return QDQ_ERR_CUDA;
   const int kchunks = static_cast<int>(moe_kchunks(K));
   const int64_t num_blocks = num_sorted / moe_block_size;
+  if (num_blocks == 0) return QDQ_OK;
   auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
   uint8_t* a_codes = static_cast<uint8_t*>(workspace);
   uint8_t* a_sf = a_codes + up(num_sorted * (K / 2));
+  const int64_t sf_blocks = (num_sorted + moe_block_size - 1) / moe_block_size;  // the gather writes a tail block
+  int32_t* seg_tab = reinterpret_cast<int32_t*>(a_sf + up(sf_blocks * kchunks * 512));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto* ap = static_cast<const uint16_t*>(a);
   // 1) gather + quantise the routed rows in sorted order (zero at padding)
@@ -563,12 +721,14 @@ extern "C" int fp4_moe_mxf4(const void* a, int64_t lda, int dtype, const void* w
     const int grid = static_cast<int>(std::min<int64_t>((items + 255) / 256, static_cast<int64_t>(device_sm_count()) * 8));
     if (dtype == QDQ_DTYPE_FP16)
       moe_gather_quant_kernel<QDQ_DTYPE_FP16><<<grid, 256, 0, s>>>(
-          ap, lda, sorted_token_ids, num_tokens_post_padded, num_sorted, moe_block_size, top_k,
-          static_cast<int>(size_m * top_k), static_cast<int>(K), kchunks, a_codes, a_sf);
+          ap, lda, sorted_token_ids, expert_ids, num_tokens_post_padded, num_sorted, moe_block_size, top_k,
+          static_cast<int>(size_m * top_k), static_cast<int>(num_experts), static_cast<int>(K), kchunks, a_codes,
+          a_sf, seg_tab);
     else
       moe_gather_quant_kernel<QDQ_DTYPE_BF16><<<grid, 256, 0, s>>>(
-          ap, lda, sorted_token_ids, num_tokens_post_padded, num_sorted, moe_block_size, top_k,
-          static_cast<int>(size_m * top_k), static_cast<int>(K), kchunks, a_codes, a_sf);
+          ap, lda, sorted_token_ids, expert_ids, num_tokens_post_padded, num_sorted, moe_block_size, top_k,
+          static_cast<int>(size_m * top_k), static_cast<int>(num_experts), static_cast<int>(K), kchunks, a_codes,
+          a_sf, seg_tab);
     if (int st = check_launch("fp4_moe_mxf4 (gather)")) return st;
   }
   // 2) grouped GEMM
@@ -578,11 +738,11 @@ extern "C" int fp4_moe_mxf4(const void* a, int64_t lda, int dtype, const void* w
   if (int st = make_tmap_u8_2d(&ta, a_codes, num_sorted, K / 2, K / 2, DBKB, na, 128)) return st;
   const int64_t sf_per_expert = qdq_sf_tiled_bytes(N, K);
   auto* sf = static_cast<const uint8_t*>(w_sf_tiled);
-  const int E = static_cast<int>(num_experts);
 #define QDQ_MOE_LAUNCH(DT, NA)                                                                                  \
-  return launch_moe<DT, NA>(tw, ta, sf, sf_per_expert, a_sf, sorted_token_ids, expert_ids, num_tokens_post_padded, \
-                            topk_weights, mul_topk_weights, top_k, moe_block_size, E, num_blocks, c, ldc, size_m, N, \
-                            K, kchunks, status, s)
+  return launch_moe<DT, NA>(tw, ta, sf, sf_per_expert, a_sf, seg_tab, sorted_token_ids, expert_ids, topk_weights, \
+                            mul_topk_weights, top_k, moe_block_size, num_blocks, static_cast<int>(num_experts), c, \
+                            ldc, size_m, N, K, kchunks,                                                          \
+                            status, s)
   if (dtype == QDQ_DTYPE_FP16) {
     if (na == 16) QDQ_MOE_LAUNCH(QDQ_DTYPE_FP16, 16);
     if (na == 32) QDQ_MOE_LAUNCH(QDQ_DTYPE_FP16, 32);
