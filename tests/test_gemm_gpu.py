@@ -187,13 +187,17 @@ def _moe_case(m, e, top_k, bs, n, k, seed, dtype=torch.bfloat16):
                                                   (3, 4, 1, 64, 128, 288, False),
                                                   (100, 8, 8, 8, 256, 512, True),
                                                   (300, 6, 2, 64, 384, 1024, True),
-                                                  (2048, 4, 2, 8, 128, 256, False)])
+                                                  (2048, 4, 2, 8, 128, 256, False),
+                                                  (512, 4, 2, 64, 320, 512, True),
+                                                  (150, 4, 2, 48, 256, 512, False)])
 def test_moe_grouped_gemm_matches_oracle(cuda_device, m, e, top_k, bs, n, k, mul):
     """Grouped MXFP4 MoE GEMM (the reference's mxfp4_qdq + moe_wna16_marlin_gemm)
     on vLLM's moe_align_block_size layout: every routed slot's row against the
     exact oracle, with the fused GEMM's tolerance.  The cases cover one block
-    per expert, runs of 2 and 13 blocks (cut into segments of at most 3), and
-    a 1024-block layout whose runs cross the segment scan's 256-block chunks."""
+    per expert, runs of 2 and 13 blocks (cut into segments of at most 3), a
+    1024-block layout whose runs cross the segment scan's 256-block chunks,
+    three-block segments of 64 rows (one MMA with N = 192), and a block size
+    (48) below the kernel's 64-row block tile."""
     from vllm_qdq_plugin.gemm import mxfp4_moe_linear, prepare_mxfp4_moe_weight
     a, codes, scales, sid, eid, ntp, topk_w = _moe_case(m, e, top_k, bs, n, k, seed=m + e + bs)
     dev = cuda_device

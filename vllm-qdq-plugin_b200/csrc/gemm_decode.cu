@@ -265,10 +265,15 @@ int launch_decode(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* s
 // most MOE_SEG_MAX consecutive blocks that name the same local expert.
 //
 // Then the grouped GEMM walks (segment, 128 rows of the expert's W) items: a
-// stage holds one W tile and the codes of each block of the segment, so W is
-// read once per segment instead of once per block; each block is its own
-// swap-AB MMA (M = 128 W rows, N = bs slots) with its own scale chunk.
-// Stage: W codes | A codes x 3 | W scales | A scales x 3.
+// stage holds one W tile and the codes of the segment's blocks (NA rows each,
+// back to back), and ONE swap-AB MMA per K step covers the whole segment
+// (M = 128 W rows, N = NA x blocks <= 192), so W is read from shared memory
+// once per segment.  The MMA's B-side scales for a segment starting at block
+// b are the scale chunk of block b, which the pre-pass fills with the rows of
+// blocks b, b+1, b+2 at their segment rows NA*i + r (rows 128-191 of a
+// three-block NA = 64 segment come from block b+2's chunk): every segment,
+// wherever it starts, finds its scales in 4-column TMEM copies.
+// Stage: W codes | A codes x 3 | W scales | A scales (rows 0-127, 128-255).
 constexpr int MOE_SEG_MAX = 3;
 
 // Segment table in the workspace: [0] = count, [1 + i] = first block << 2 | blocks.
@@ -340,8 +345,9 @@ template <int kDtype>
 __global__ void __launch_bounds__(256)
 moe_gather_quant_kernel(const uint16_t* __restrict__ a, int64_t lda, const int32_t* __restrict__ sorted_ids,
                         const int32_t* __restrict__ expert_ids, const int32_t* __restrict__ num_post_padded,
-                        int64_t num_sorted, int bs, int top_k, int n_slots, int num_experts, int K, int kchunks,
-                        uint8_t* __restrict__ codes, uint8_t* __restrict__ sf, int32_t* __restrict__ seg_tab) {
+                        int64_t num_sorted, int bs, int na, int top_k, int n_slots, int num_experts, int K,
+                        int kchunks, uint8_t* __restrict__ codes, uint8_t* __restrict__ sf,
+                        int32_t* __restrict__ seg_tab) {
   const int gpr = K / 32;
   const int64_t total = num_sorted * gpr;
   const int npp = __ldg(num_post_padded);
@@ -365,7 +371,13 @@ moe_gather_quant_kernel(const uint16_t* __restrict__ a, int64_t lda, const int32
     *reinterpret_cast<uint4*>(codes + p * (K / 2) + g * 16) = make_uint4(code[0], code[1], code[2], code[3]);
     const int64_t b = p / bs;
     const int r = static_cast<int>(p - b * bs);
-    sf[(b * kchunks + g / 4) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (g & 3)] = static_cast<uint8_t>(e);
+    // row r of block b sits at segment row na*i + r of the chunk of block b - i
+#pragma unroll
+    for (int i = 0; i < MOE_SEG_MAX; ++i) {
+      const int row = i * na + r;
+      if (row >= 128 || b < i) break;
+      sf[((b - i) * kchunks + g / 4) * 512 + (row & 31) * 16 + (row >> 5) * 4 + (g & 3)] = static_cast<uint8_t>(e);
+    }
   }
 }
 
@@ -373,14 +385,14 @@ template <int kNA>
 struct MLayout {
   static constexpr int A_TILE = kNA * DBKB;  // one block's codes per stage
   static constexpr int ST_W = 0, ST_A = W_TILE, ST_SFW = ST_A + MOE_SEG_MAX * A_TILE, ST_SFA = ST_SFW + SF_STAGE;
-  static constexpr int STAGE = (ST_SFA + MOE_SEG_MAX * SF_STAGE + 1023) / 1024 * 1024;
+  static constexpr int STAGE = (ST_SFA + 2 * SF_STAGE + 1023) / 1024 * 1024;
   static constexpr int STAGES = kNA == 64 ? 5 : (kNA == 32 ? 7 : 8);
 };
 struct __align__(8) MBars {
   uint64_t full[8];       // W, the segment's codes and the scale chunks landed (1 arrival + tx)
   uint64_t empty[8];      // the stage's MMAs completed
   uint64_t acc_full[2];   // MMA -> epilogue, per accumulator buffer
-  uint64_t acc_empty[2];  // epilogue -> MMA (128 arrivals)
+  uint64_t acc_empty[2];  // epilogue -> MMA (256 arrivals)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -392,10 +404,13 @@ constexpr size_t m_smem_bytes() {
 static_assert(m_smem_bytes<16>() <= 227 * 1024 && m_smem_bytes<32>() <= 227 * 1024 &&
               m_smem_bytes<64>() <= 227 * 1024, "MoE stages exceed shared memory");
 // TMEM of the MoE kernel: two accumulators of MOE_SEG_MAX x 64 columns, the
-// W scales (8 columns) and MOE_SEG_MAX x 8 columns of block scales.
+// W scales (4 columns per K chunk) and the segment scales (8 columns per K
+// chunk: rows 0-127, then 128-255).
 constexpr uint32_t M_ACC = 0, M_ACC_STRIDE = 64 * MOE_SEG_MAX, M_SFW = 2 * M_ACC_STRIDE, M_SFA = M_SFW + 8,
                    M_TMEM_COLS = 512;
-static_assert(M_SFA + 8 * MOE_SEG_MAX <= M_TMEM_COLS, "MoE TMEM columns");
+static_assert(M_SFA + 16 <= M_TMEM_COLS, "MoE TMEM columns");
+constexpr int M_EPI_WARPS = 8;
+constexpr int M_THREADS = 32 * (2 + M_EPI_WARPS);
 
 // Persistent: CTA c takes work items c, c + gridDim.x, ...; item i is segment
 // i % nseg against 128-row W tile i / nseg, so the CTAs in flight cover
@@ -403,7 +418,7 @@ static_assert(M_SFA + 8 * MOE_SEG_MAX <= M_TMEM_COLS, "MoE TMEM columns");
 // items and the accumulator is double-buffered, so an item's epilogue overlaps
 // the next item's MMAs.
 template <int kDtype, int kNA>
-__global__ void __launch_bounds__(D_THREADS, 1)
+__global__ void __launch_bounds__(M_THREADS, 1)
 mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
                 const uint8_t* __restrict__ sfw, int64_t sf_per_expert, const uint8_t* __restrict__ sfa,
                 const int32_t* __restrict__ seg_tab, const int32_t* __restrict__ sorted_ids,
@@ -440,7 +455,7 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->acc_full[i], 1);
-      mbar_init(&bars->acc_empty[i], 128);
+      mbar_init(&bars->acc_empty[i], 32 * M_EPI_WARPS);
     }
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
@@ -477,14 +492,18 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
           }
           if (*(volatile int*)&bars->abort) { ok = false; break; }
           uint8_t* sp = smem + st * Lay::STAGE;
-          mbar_arrive_expect_tx(&bars->full[st], W_TILE + SF_STAGE + nb * (Lay::A_TILE + SF_STAGE));
+          const bool wide = kNA * nb > 128;
+          mbar_arrive_expect_tx(&bars->full[st],
+                                W_TILE + nb * Lay::A_TILE + (wide ? 3 : 2) * SF_STAGE);
           tma_load_2d(sp + Lay::ST_W, &tmap_w, kt * DBKB, static_cast<int32_t>(w_row0), &bars->full[st]);
           bulk_load(sp + Lay::ST_SFW, sfw_e + 2 * kt * 512, SF_STAGE, &bars->full[st]);
-          for (int i = 0; i < nb; ++i) {
+          for (int i = 0; i < nb; ++i)
             tma_load_2d(sp + Lay::ST_A + i * Lay::A_TILE, &tmap_a, kt * DBKB, (blk0 + i) * bs, &bars->full[st]);
-            bulk_load(sp + Lay::ST_SFA + i * SF_STAGE,
-                      sfa + (static_cast<int64_t>(blk0 + i) * kchunks + 2 * kt) * 512, SF_STAGE, &bars->full[st]);
-          }
+          bulk_load(sp + Lay::ST_SFA, sfa + (static_cast<int64_t>(blk0) * kchunks + 2 * kt) * 512, SF_STAGE,
+                    &bars->full[st]);
+          if (wide)  // segment rows 128-191: block blk0 + 2's chunk
+            bulk_load(sp + Lay::ST_SFA + SF_STAGE, sfa + (static_cast<int64_t>(blk0 + 2) * kchunks + 2 * kt) * 512,
+                      SF_STAGE, &bars->full[st]);
         }
       }
       for (int j = (it > S ? it - S : 0); j < it; ++j)
@@ -493,12 +512,13 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (elect_one()) {
-      constexpr uint32_t idesc = idesc_mxf4(DBM, kNA, true);
       int it = 0, j = 0;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < num_items; item += gridDim.x) {
         int blk0, nb, e;
         if (!seg_of(item, blk0, nb, e)) continue;
+        const uint32_t idesc = idesc_mxf4(DBM, kNA * nb, true);  // N = the segment's rows
+        const bool wide = kNA * nb > 128;
         const int buf = j & 1;
         // the epilogue has read this buffer's previous item out of TMEM
         if (!mbar_wait(&bars->acc_empty[buf], ((j >> 1) & 1) ^ 1, status, 0x506)) { ok = false; break; }
@@ -512,20 +532,20 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
           uint8_t* sp = smem + st * Lay::STAGE;
           tmem_cp_sf(tmem + M_SFW + 0, smem_desc_sf(sp + Lay::ST_SFW));
           tmem_cp_sf(tmem + M_SFW + 4, smem_desc_sf(sp + Lay::ST_SFW + 512));
-          for (int i = 0; i < nb; ++i) {
-            tmem_cp_sf(tmem + M_SFA + 8 * i + 0, smem_desc_sf(sp + Lay::ST_SFA + i * SF_STAGE));
-            tmem_cp_sf(tmem + M_SFA + 8 * i + 4, smem_desc_sf(sp + Lay::ST_SFA + i * SF_STAGE + 512));
+          tmem_cp_sf(tmem + M_SFA + 0, smem_desc_sf(sp + Lay::ST_SFA));        // K chunk 0, rows 0-127
+          tmem_cp_sf(tmem + M_SFA + 8, smem_desc_sf(sp + Lay::ST_SFA + 512));  // K chunk 1, rows 0-127
+          if (wide) {
+            tmem_cp_sf(tmem + M_SFA + 4, smem_desc_sf(sp + Lay::ST_SFA + 1024));   // K chunk 0, rows 128-191
+            tmem_cp_sf(tmem + M_SFA + 12, smem_desc_sf(sp + Lay::ST_SFA + 1536));  // K chunk 1
           }
           const uint64_t dw = smem_desc_sw128(sp + Lay::ST_W);
+          const uint64_t da = smem_desc_sw128(sp + Lay::ST_A);
 #pragma unroll
           for (int kk = 0; kk < DBK / 64; ++kk) {
             const uint32_t jj = kk >> 1, sf_id = (kk & 1) * 2;
-            for (int i = 0; i < nb; ++i) {
-              const uint64_t da = smem_desc_sw128(sp + Lay::ST_A + i * Lay::A_TILE);
-              mma_mxf4(acc + 64 * i, dw + ((kk * 32) >> 4), da + ((kk * 32) >> 4),
-                       idesc_with_sf_ids(idesc, sf_id, sf_id), (tmem + M_SFW + 4 * jj) | (sf_id << 30),
-                       (tmem + M_SFA + 8 * i + 4 * jj) | (sf_id << 30), (kt | kk) != 0);
-            }
+            mma_mxf4(acc, dw + ((kk * 32) >> 4), da + ((kk * 32) >> 4), idesc_with_sf_ids(idesc, sf_id, sf_id),
+                     (tmem + M_SFW + 4 * jj) | (sf_id << 30), (tmem + M_SFA + 8 * jj) | (sf_id << 30),
+                     (kt | kk) != 0);
           }
           tc_commit(&bars->empty[st]);
         }
@@ -538,30 +558,33 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
       mbar_wait(&bars->drain, 0, status, 0x507);
     }
   } else {
-    // ---------------- epilogue: TMEM lanes = W rows, columns = the blocks' slots
+    // ---------------- epilogue: TMEM lanes = W rows, columns = the segment's slots
+    // Eight warps: warp w reads TMEM lanes 32 (w % 4).. and the 32-column
+    // chunks c = half, half + 2, half + 4 of the segment's NA * nb columns.
     const int lane = threadIdx.x & 31;
     const int q = warp & 3;
-    constexpr int NC = kNA > 32 ? 2 : 1;
+    const int half = (warp - 2) >> 2;
+    constexpr int CH = (64 * MOE_SEG_MAX / 32 + 1) / 2;  // chunks per warp at most
     bool ok = true;
     int j = 0;
     for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
       int blk0, nb, e;
       if (!seg_of(item, blk0, nb, e)) continue;
       const int n_tile = item / nseg;
-      // Routing of the segment, fetched while the MMAs run: lane l holds
-      // slot 32*h + l of block i (-1 for padding) and its routing weight.
-      int slot[MOE_SEG_MAX][NC];
-      float wt[MOE_SEG_MAX][NC];
+      const int nchunks = (kNA * nb + 31) / 32;
+      // Routing of this warp's columns, fetched while the MMAs run: lane l
+      // holds the slot of column 32 c + l (-1 for padding) and its weight.
+      int slot[CH];
+      float wt[CH];
 #pragma unroll
-      for (int i = 0; i < MOE_SEG_MAX; ++i)
-#pragma unroll
-        for (int h = 0; h < NC; ++h) {
-          const int si = 32 * h + lane;
-          int s = (i < nb && si < bs) ? __ldg(sorted_ids + static_cast<int64_t>(blk0 + i) * bs + si) : -1;
-          if (s >= n_slots) s = -1;
-          slot[i][h] = s;
-          wt[i][h] = (mul_topk && s >= 0) ? __ldg(topk_w + s) : 1.0f;
-        }
+      for (int t = 0; t < CH; ++t) {
+        const int col = 32 * (half + 2 * t) + lane;
+        const int i = col / kNA, r = col % kNA;
+        int s = (i < nb && r < bs) ? __ldg(sorted_ids + static_cast<int64_t>(blk0 + i) * bs + r) : -1;
+        if (s >= n_slots) s = -1;
+        slot[t] = s;
+        wt[t] = (mul_topk && s >= 0) ? __ldg(topk_w + s) : 1.0f;
+      }
       const int buf = j & 1;
       if (ok) ok = mbar_wait(&bars->acc_full[buf], (j >> 1) & 1, status, 0x505);
       ok = __all_sync(0xffffffffu, ok);
@@ -571,26 +594,28 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
       const bool in_n = n < N;
       // warp-uniform: every lane takes part in the shuffles below
       const bool store = __all_sync(0xffffffffu, ok && !*(volatile int*)&bars->abort);
+      if (half >= nchunks) {
+        tc_fence_before();
+        mbar_arrive(&bars->acc_empty[buf]);
+      }
 #pragma unroll
-      for (int i = 0; i < MOE_SEG_MAX; ++i) {
-        if (i >= nb) break;
-        uint32_t r[NC][32];
-#pragma unroll
-        for (int h = 0; h < NC; ++h) tmem_ld32(taddr + 64 * i + 32 * h, r[h]);
+      for (int t = 0; t < CH; ++t) {
+        const int c = half + 2 * t;
+        if (c >= nchunks) break;
+        uint32_t r[32];
+        tmem_ld32(taddr + 32 * c, r);
         tmem_ld_wait();
-        if (i == nb - 1) {
+        if (c + 2 >= nchunks) {  // this warp's last chunk of the item
           tc_fence_before();
           mbar_arrive(&bars->acc_empty[buf]);  // the next item on this buffer may start
         }
         if (!store) continue;
 #pragma unroll
-        for (int h = 0; h < NC; ++h)
-#pragma unroll
-          for (int l = 0; l < 32; ++l) {
-            const int s = __shfl_sync(0xffffffffu, slot[i][h], l);
-            const float w = __shfl_sync(0xffffffffu, wt[i][h], l);
-            if (s >= 0 && in_n) C[static_cast<int64_t>(s) * ldc + n] = O::one(__uint_as_float(r[h][l]) * w);
-          }
+        for (int l = 0; l < 32; ++l) {
+          const int s = __shfl_sync(0xffffffffu, slot[t], l);
+          const float w = __shfl_sync(0xffffffffu, wt[t], l);
+          if (s >= 0 && in_n) C[static_cast<int64_t>(s) * ldc + n] = O::one(__uint_as_float(r[l]) * w);
+        }
       }
       ++j;
     }
@@ -624,7 +649,7 @@ int launch_moe(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* sf, 
   const int64_t items = num_blocks * ((N + DBM - 1) / DBM);
   const int sms = device_sm_count();
   dim3 grid(static_cast<unsigned>(std::min<int64_t>(items, sms > 0 ? sms : 148)));
-  mxf4_moe_kernel<kDtype, kNA><<<grid, D_THREADS, smem, s>>>(
+  mxf4_moe_kernel<kDtype, kNA><<<grid, M_THREADS, smem, s>>>(
       tw, ta, sf, sf_per_expert, sfa, seg_tab, sorted_ids, expert_ids, topk_w, mul, top_k, bs,
       static_cast<int>(num_blocks), num_experts, c, ldc,
       static_cast<int>(size_m), static_cast<int>(N), static_cast<int>(K), kchunks, status);
@@ -715,24 +740,24 @@ extern "C" int fp4_moe_mxf4(const void* a, int64_t lda, int dtype, const void* w
   int32_t* seg_tab = reinterpret_cast<int32_t*>(a_sf + up(sf_blocks * kchunks * 512));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto* ap = static_cast<const uint16_t*>(a);
+  const int na = moe_block_size <= 16 ? 16 : (moe_block_size <= 32 ? 32 : 64);  // the GEMM's rows per block
   // 1) gather + quantise the routed rows in sorted order (zero at padding)
   {
     const int64_t items = num_sorted * (K / 32);
     const int grid = static_cast<int>(std::min<int64_t>((items + 255) / 256, static_cast<int64_t>(device_sm_count()) * 8));
     if (dtype == QDQ_DTYPE_FP16)
       moe_gather_quant_kernel<QDQ_DTYPE_FP16><<<grid, 256, 0, s>>>(
-          ap, lda, sorted_token_ids, expert_ids, num_tokens_post_padded, num_sorted, moe_block_size, top_k,
+          ap, lda, sorted_token_ids, expert_ids, num_tokens_post_padded, num_sorted, moe_block_size, na, top_k,
           static_cast<int>(size_m * top_k), static_cast<int>(num_experts), static_cast<int>(K), kchunks, a_codes,
           a_sf, seg_tab);
     else
       moe_gather_quant_kernel<QDQ_DTYPE_BF16><<<grid, 256, 0, s>>>(
-          ap, lda, sorted_token_ids, expert_ids, num_tokens_post_padded, num_sorted, moe_block_size, top_k,
+          ap, lda, sorted_token_ids, expert_ids, num_tokens_post_padded, num_sorted, moe_block_size, na, top_k,
           static_cast<int>(size_m * top_k), static_cast<int>(num_experts), static_cast<int>(K), kchunks, a_codes,
           a_sf, seg_tab);
     if (int st = check_launch("fp4_moe_mxf4 (gather)")) return st;
   }
   // 2) grouped GEMM
-  const int na = moe_block_size <= 16 ? 16 : (moe_block_size <= 32 ? 32 : 64);
   CUtensorMap tw, ta;
   if (int st = make_tmap_u8_2d(&tw, w_codes, num_experts * N, K / 2, K / 2, DBKB, DBM, 128)) return st;
   if (int st = make_tmap_u8_2d(&ta, a_codes, num_sorted, K / 2, K / 2, DBKB, na, 128)) return st;
