@@ -413,8 +413,9 @@ constexpr int M_EPI_WARPS = 8;
 constexpr int M_THREADS = 32 * (2 + M_EPI_WARPS);
 
 // Persistent: CTA c takes work items c, c + gridDim.x, ...; item i is segment
-// i % nseg against 128-row W tile i / nseg, so the CTAs in flight cover
-// consecutive segments of one W tile row range.  The stage ring runs across
+// i / n_tiles against 128-row W tile i % n_tiles, so the CTAs in flight cover
+// every W tile of a few consecutive segments: each W tile of an expert streams
+// from HBM once while its segments' codes stay in L2.  The stage ring runs across
 // items and the accumulator is double-buffered, so an item's epilogue overlaps
 // the next item's MMAs.
 template <int kDtype, int kNA>
@@ -437,10 +438,11 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
   const int num_kt = (K + DBK - 1) / DBK;
   const int n_slots = size_m * top_k;
   const int nseg = min(max(seg_tab[0], 0), num_blocks);
-  const int num_items = nseg * ((N + DBM - 1) / DBM);
+  const int n_tiles = (N + DBM - 1) / DBM;
+  const int num_items = nseg * n_tiles;
   // A segment entry every role decodes alike; a malformed one is skipped.
   auto seg_of = [&](int item, int& blk0, int& nb, int& e) -> bool {
-    const int seg = seg_tab[1 + item % nseg];
+    const int seg = seg_tab[1 + item / n_tiles];
     blk0 = seg >> 2;
     nb = seg & 3;
     if (blk0 < 0 || nb < 1 || blk0 + nb > num_blocks) return false;
@@ -480,7 +482,7 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
       for (int item = blockIdx.x; ok && item < num_items; item += gridDim.x) {
         int blk0, nb, e;
         if (!seg_of(item, blk0, nb, e)) continue;
-        const int n_tile = item / nseg;
+        const int n_tile = item % n_tiles;
         const int64_t w_row0 = static_cast<int64_t>(e) * N + static_cast<int64_t>(n_tile) * DBM;
         const uint8_t* sfw_e = sfw + e * sf_per_expert + static_cast<int64_t>(n_tile) * kchunks * 512;
         for (int kt = 0; kt < num_kt; ++kt, ++it) {
@@ -570,7 +572,7 @@ mxf4_moe_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
     for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
       int blk0, nb, e;
       if (!seg_of(item, blk0, nb, e)) continue;
-      const int n_tile = item / nseg;
+      const int n_tile = item % n_tiles;
       const int nchunks = (kNA * nb + 31) / 32;
       // Routing of this warp's columns, fetched while the MMAs run: lane l
       // holds the slot of column 32 c + l (-1 for padding) and its weight.
