@@ -96,6 +96,9 @@ WORKLOADS = {
     "sage3_mxfp4": dict(config="BASELINE config 4: Sage3 self-attention, MXFP4, Wan-2.1-14B 720p: "
                                "B=1, H=40, L=75600, D=128, bf16 NHD, non-causal, fp32 accumulation",
                         rows=75600, cols=128, make=None, B=1, H=40, sage3="mxfp4_hw", acc="fp32"),
+    "sage3_mxfp8": dict(config="Sage3 self-attention, mxfp8_hw (E4M3 + E8M0 per 32), on BASELINE config 4's "
+                               "shape: B=1, H=40, L=75600, D=128, bf16 NHD, non-causal, fp32 accumulation",
+                        rows=75600, cols=128, make=None, B=1, H=40, sage3="mxfp8_hw", acc="fp32"),
     "sage3_nvfp4": dict(config="BASELINE config 5: Sage3 self-attention, NVFP4, SAGE3_ACC_DTYPE=bf16_pv_only, "
                                "Flux-like batch: B=8, H=24, L=4608, D=128, bf16 NHD, 1% of K rows x20",
                         rows=4608, cols=128, make=None, B=8, H=24, sage3="nvfp4", acc="bf16_pv_only"),
@@ -358,17 +361,17 @@ def cpu_attn_sample(wl: dict, L: int, budget_s: float = 20.0) -> dict:
     else:
         q, k, v = c4_inputs(torch.device("cpu"), L=L, H=1)
     f = lambda t: t[0, :, 0].float().numpy()  # noqa: E731
-    nv, emulated = oa.VARIANTS[wl["sage3"]]
+    nv, emulated, fp8 = oa.VARIANTS[wl["sage3"]]
     block_n = oa.REF_BLOCK_N[wl["sage3"]]
     sm = 1.0 / math.sqrt(128)
     t0 = time.perf_counter()
-    qd, kd, vd, ds = oa.prepass(f(q), f(k), f(v), True, nv)
+    qd, kd, vd, ds = oa.prepass(f(q), f(k), f(v), True, nv, fp8)
     t_pre = time.perf_counter() - t0
     tiles = (L + 127) // 128
     done, t0 = 0, time.perf_counter()
     while done < tiles:
         oa.flash(qd, kd, vd, ds, L, sm, block_n=block_n, nv=nv, emulated=emulated,
-                 q_rows=slice(128 * done, 128 * done + 128))
+                 q_rows=slice(128 * done, 128 * done + 128), fp8=fp8)
         done += 1
         if time.perf_counter() - t0 > budget_s:
             break
@@ -545,6 +548,16 @@ def run_ours(args) -> None:
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def measured_peak_fp8() -> tuple[float, str]:
+    """Dense FP8 tensor peak: 2x the measured cuBLAS bf16 rate (4.5 vs 2.25 PFLOP/s nominal)."""
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        return 2.0 * float(json.loads(p.read_text())["bf16_tflops"]), \
+            "measured bf16 x 2 (MEASURED_PEAKS.json bf16_tflops, nominal fp8:bf16 = 2)"
+    except Exception:
+        return 2.0 * 1590.0, "fallback bf16 1.59 PF x 2"
 
 
 def measured_peak_fp4() -> tuple[float, str]:
@@ -888,7 +901,7 @@ def run_attn(args, wl, world, rank, dev, dist) -> None:
         q, k, v = c5_inputs(dev, B=B, L=L, H=H)
     else:
         q, k, v = c4_inputs(dev, L=L, H=H)
-    variant = {"mxfp4_hw": 0, "nvfp4": 1, "mxfp4": 2}[wl["sage3"]]
+    variant = {"mxfp4_hw": 0, "nvfp4": 1, "mxfp4": 2, "mxfp8_hw": 3}[wl["sage3"]]
     out = torch.empty_like(q)
     lib = _native.lib()
     ws = torch.empty((lib.sage3_attn_workspace_bytes(B, L, H, 128),), dtype=torch.uint8, device=dev)
@@ -959,15 +972,19 @@ def run_attn(args, wl, world, rank, dev, dist) -> None:
     barrier()
     e2e = world * flop / (a0.elapsed_time(a1) / n_e2e * 1e-3) / 1e12
     if rank == 0:
-        peak, src = measured_peak_fp4()
+        fp8 = wl["sage3"] == "mxfp8_hw"
+        peak, src = measured_peak_fp8() if fp8 else measured_peak_fp4()
         achieved = flop / (ms_step * 1e-3) / 1e12
+        ref_ms = 258.42 if fp8 else 261.81  # the reference's published 1x B200 times at config 4
         line = {
             "metric": "Sage3 attention TFLOPS (4*B*H*L^2*D per call)", "value": round(value, 1),
             "unit": "TFLOP/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
             "ms_per_step": round(ms_step, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": round(261.81 / ms_step, 3) if (L == 75600 and B == 1 and H == 40) else None,
-            "vs_baseline_note": "reference mxfp4_hw on 1x B200: 261.81 ms (speed-up = 261.81 / ms_per_step)",
-            "dtype": "e2m1 x e2m1 (E8M0 scales), fp32 softmax/accumulate, bf16 in/out",
+            "vs_baseline": round(ref_ms / ms_step, 3) if (L == 75600 and B == 1 and H == 40) else None,
+            "vs_baseline_note": f"reference {wl['sage3']} on 1x B200: {ref_ms} ms "
+                                f"(speed-up = {ref_ms} / ms_per_step)",
+            "dtype": ("e4m3 x e4m3" if fp8 else "e2m1 x e2m1") + " (E8M0 scales), fp32 softmax/accumulate, "
+                     "bf16 in/out",
             "data": "synthetic (seeded, BASELINE config-4 distributions, generated on device)",
             "config": {"workload": wl["config"], "B": B, "H": H, "L": L, "D": 128, "sage3": wl["sage3"],
                        "acc_dtype": wl["acc"],
@@ -978,7 +995,7 @@ def run_attn(args, wl, world, rank, dev, dist) -> None:
             "gpu_launches": launches[0],
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_source": src,
-                         "traffic": ncu_traffic("sage3_mxfp4"),
+                         "traffic": ncu_traffic(args.workload),
                          "softmax_floor_ms": round(B * H * L * L / (148 * 16 * 1.965e9) * 1e3, 2)},
             "clocks": sampler.summary(t_wall0, t_wall1) if sampler else None,
         }

@@ -172,7 +172,7 @@ int fp4_linear_mxf4(const void* a, int64_t lda, int dtype, const void* w_codes,
                     int64_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
- * Sage3 FP4 attention — replaces the SAGE_ATTN backend's attention:
+ * Sage3 FP4 / FP8 attention — replaces the SAGE_ATTN backend's attention:
  *   reference  vllm_qdq_plugin/sage3_attn/impl.py:91-137 (_forward_sage3)
  *              -> sage3/api.py:89-387 (_run_attention: qk_smoothing,
  *              quantize_to_mxfp4, mxfp4_flash_attention / tiled_online_attention)
@@ -195,7 +195,10 @@ int64_t sage3_attn_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t D);
  *                scaling, l = sum of quantised P), p_quant_kernels.py:37-99 and
  *                attention_kernel.py:176-186;
  *            2 = config "mxfp4": MXFP4 with the emulated-config P handling
- *                (p_quant_kernels.py:106-150).
+ *                (p_quant_kernels.py:106-150);
+ *            3 = config "mxfp8_hw": MXFP8 (E4M3 + E8M0 per 32) Q/K/V and P
+ *                with the reference hardware kernel's P handling,
+ *                mxfp8_hw_kernel.py:88-389 (kind::mxf8f6f4 MMAs).
  *   acc_mode: 0 = fp32, 1 = a reduced-precision PV accumulator of the
  *            reference (accepted; this kernel accumulates in fp32 either way).
  *   causal: non-zero for a causal mask (query i sees keys <= i).

@@ -1,4 +1,4 @@
-"""CPU oracle of the Sage3 MXFP4 attention (the reference's mxfp4_hw path).
+"""CPU oracle of the Sage3 FP4 / FP8 attention (the reference's mxfp4_hw and mxfp8_hw paths).
 
 TEST INFRASTRUCTURE ONLY (tests/, smoke(), bench.py baselines).
 
@@ -18,6 +18,10 @@ The quantised P depends on the running max at each key tile, so the tile
 width is a parameter: the sm_100a kernel uses 128, the reference kernel 64.
 Keys beyond L are masked (mask_padding=True) or, as in the reference,
 attended as zero keys (mask_padding=False).
+The mxfp8_hw path (sage3/api.py:114-160, mxfp8_hw_kernel.py:37-246) is the
+same with quantize_to_mxfp8 (via the C oracle, pinned by
+tests/golden/mxfp8_hw_quant.npz) and P quantised to E4M3 with
+E8M0 2^ceil(log2(max p / 448)) per 32 keys (round-to-nearest-even).
 """
 
 from __future__ import annotations
@@ -40,6 +44,23 @@ def bf16_round(x: np.ndarray) -> np.ndarray:
 
 def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
     return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def _e4m3_table() -> np.ndarray:
+    b = np.arange(256)
+    e = (b >> 3) & 0xF
+    m = (b & 7).astype(np.float64)
+    mag = np.where(e == 0, m * 2.0 ** -9, (1 + m / 8) * np.exp2(e - 7.0))
+    mag[(b & 0x7F) == 0x7F] = np.nan
+    return np.where(b & 0x80, -mag, mag)
+
+
+E4M3 = _e4m3_table()
+
+
+def _deq8(codes: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """E4M3 bytes [..., K] with E8M0 scales per 32 -> float64."""
+    return E4M3[codes] * np.repeat(np.exp2(scales.astype(np.float64) - 127.0), 32, axis=-1)
 
 
 def _deq(codes: np.ndarray, scales: np.ndarray) -> np.ndarray:
@@ -96,11 +117,13 @@ def _ceil_log2(r: np.ndarray) -> np.ndarray:
     return np.where(r == 0, -127, out)
 
 
-def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True, nv: bool = False):
+def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True, nv: bool = False,
+            fp8: bool = False):
     """q, k, v: float32 [L, D] holding bf16 values for one (batch, head).
     Returns (qd, kd, vd, ds): dequantised Q [Lp, D], K [Lp, D], V [Lp, D]
     (V quantised along the sequence) and delta_s [G, Lp] (zeros without
-    smoothing).  nv selects NVFP4 blocks of 16 (E4M3) instead of MXFP4."""
+    smoothing).  nv selects NVFP4 blocks of 16 (E4M3) instead of MXFP4; fp8
+    selects MXFP8 (quantize_to_mxfp8)."""
     L, D = q.shape
     Lp = (L + 127) // 128 * 128
     G = Lp // 128
@@ -121,6 +144,11 @@ def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True,
     if nv:
         return (nv_quant_deq(pad(qs)), nv_quant_deq(pad(kc)),
                 nv_quant_deq(np.ascontiguousarray(pad(v).T)).T, dsp)
+    if fp8:
+        qcodes, qsc = oq.mxfp8_hw_quant(pad(qs))
+        kcodes, ksc = oq.mxfp8_hw_quant(pad(kc))
+        vcodes, vsc = oq.mxfp8_hw_quant(np.ascontiguousarray(pad(v).T))  # [D, Lp], [D, Lp/32]
+        return _deq8(qcodes, qsc), _deq8(kcodes, ksc), _deq8(vcodes, vsc).T, dsp
     qcodes, qsc = oq.mxfp4_hw_quant(pad(qs))
     kcodes, ksc = oq.mxfp4_hw_quant(pad(kc))
     vcodes, vsc = oq.mxfp4_hw_quant(np.ascontiguousarray(pad(v).T))  # [D, Lp/2], [D, Lp/32]
@@ -129,14 +157,16 @@ def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True,
 
 def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: bool = False,
           mask_padding: bool = True, nv: bool = False, emulated: bool = False,
-          q_rows: slice | None = None) -> np.ndarray:
+          q_rows: slice | None = None, fp8: bool = False) -> np.ndarray:
     """The attention loop on dequantised operands; returns O [L, D] float64
     (or the rows q_rows of it, for timing a slice of the query tiles).
 
     P handling: mxfp4_hw (nv=False, emulated=False): E8M0 per 32 of p, l = sum
     of unquantised p.  Emulated configs (emulated=True): p scaled by 448*6
     first, l = sum of the dequantised P (p_quant_kernels.py:37-150,
-    attention_kernel.py:176-186); nv=True uses E4M3 per 16."""
+    attention_kernel.py:176-186); nv=True uses E4M3 per 16.  fp8=True: the
+    mxfp8_hw kernel's P, E4M3 codes of min(p / 2^e, 448) with
+    e = clamp(ceil(log2(max p / 448)), -127, 127) per 32, l = sum of p."""
     Lp, D = kd.shape
     n_keys = L if mask_padding else Lp
     qk_scale = sm_scale * LOG2E
@@ -162,7 +192,12 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
         acc = acc * alpha[:, None]
         w = n1 - n0
         p1 = p * pre
-        if nv:
+        if fp8:
+            pg = p1.reshape(nq, w // 32, 32)
+            e = np.clip(_ceil_log2(pg.max(axis=2) / 448.0), -127, 127)
+            sc = np.exp2(e.astype(np.float64))[:, :, None]
+            pq = (e4m3_round(pg / sc).astype(np.float64) * sc).reshape(nq, w)
+        elif nv:
             pg = p1.reshape(nq, w // 16, 16)
             sc = e4m3_round(np.maximum(pg.max(axis=2) / 6.0, 1e-8)).astype(np.float64)[:, :, None]
             inv = np.where(sc > 0, 1.0 / np.where(sc > 0, sc, 1), 0.0)
@@ -178,12 +213,15 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
     return (acc / l[:, None])[rows < L]
 
 
-VARIANTS = {"mxfp4_hw": (False, False), "mxfp4": (False, True), "nvfp4": (True, True)}
+# config -> (nv, emulated, fp8)
+VARIANTS = {"mxfp4_hw": (False, False, False), "mxfp4": (False, True, False), "nvfp4": (True, True, False),
+            "mxfp8_hw": (False, False, True)}
 
 # Key tile of the reference's online softmax per config: the mxfp4_hw kernel
 # launches with BLOCK_N = 64 (sage3/mxfp4_hw_kernel.py:437); the emulated
-# configs' attention kernel requires tile_size_k = 128 (attention_kernel.py:249-253).
-REF_BLOCK_N = {"mxfp4_hw": 64, "mxfp4": 128, "nvfp4": 128}
+# configs' attention kernel requires tile_size_k = 128 (attention_kernel.py:249-253);
+# the mxfp8_hw kernel launches with BLOCK_N = 64 (sage3/mxfp8_hw_kernel.py:341).
+REF_BLOCK_N = {"mxfp4_hw": 64, "mxfp4": 128, "nvfp4": 128, "mxfp8_hw": 64}
 
 
 def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_scale: float,
@@ -191,7 +229,7 @@ def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_sca
               mask_padding: bool = True, config: str = "mxfp4_hw") -> np.ndarray:
     """q/k/v: uint16 bf16 bit patterns [L, H, D] (NHD with B = 1); returns O [L, H, D].
     block_n defaults to the reference's key tile for the config (REF_BLOCK_N)."""
-    nv, emulated = VARIANTS[config]
+    nv, emulated, fp8 = VARIANTS[config]
     if block_n is None:
         block_n = REF_BLOCK_N[config]
     L, H, D = q_bits.shape
@@ -200,8 +238,9 @@ def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_sca
         q = bf16_bits_to_f32(q_bits[:, h])
         k = bf16_bits_to_f32(k_bits[:, h])
         v = bf16_bits_to_f32(v_bits[:, h])
-        qd, kd, vd, ds = prepass(q, k, v, smoothing, nv)
-        out[:, h] = flash(qd, kd, vd, ds, L, sm_scale, block_n, causal, mask_padding, nv, emulated)
+        qd, kd, vd, ds = prepass(q, k, v, smoothing, nv, fp8)
+        out[:, h] = flash(qd, kd, vd, ds, L, sm_scale, block_n, causal, mask_padding, nv, emulated,
+                          fp8=fp8)
     return out
 
 

@@ -50,6 +50,8 @@ def lib():
                 h.oracle_round_e4m3.restype = f32
                 h.oracle_mxfp4_hw_quant.argtypes = [vp, vp, vp, i64, i64, i32]
                 h.oracle_mxfp4_hw_quant.restype = None
+                h.oracle_mxfp8_hw_quant.argtypes = [vp, vp, vp, i64, i64, i32]
+                h.oracle_mxfp8_hw_quant.restype = None
                 h.oracle_mxfp8_qdq.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, i32, i32]
                 h.oracle_mxfp8_qdq.restype = None
                 h.oracle_max_threads.argtypes = []
@@ -118,6 +120,18 @@ def mxfp4_hw_quant(x: np.ndarray, nthreads: int = 0):
     c = np.empty(x.shape[:-1] + (k // 2,), np.uint8)
     s = np.empty(x.shape[:-1] + (k // 32,), np.uint8)
     lib().oracle_mxfp4_hw_quant(_p(x), _p(c), _p(s), rows, k, nthreads)
+    return c, s
+
+
+def mxfp8_hw_quant(x: np.ndarray, nthreads: int = 0):
+    """quantize_to_mxfp8 restated: fp32 [..., K] -> (E4M3 bytes [..., K], E8M0 scales [..., K/32])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    k = x.shape[-1]
+    assert k % 32 == 0
+    rows = x.size // k
+    c = np.empty(x.shape, np.uint8)
+    s = np.empty(x.shape[:-1] + (k // 32,), np.uint8)
+    lib().oracle_mxfp8_hw_quant(_p(x), _p(c), _p(s), rows, k, nthreads)
     return c, s
 
 

@@ -14,6 +14,8 @@
  *                           CPU branch (:467-478)
  *   oracle_mxfp4_hw_quant   vllm_qdq_plugin/sage3_attn/sage3/mxfp4_hw_kernel.py:43-116
  *                           (quantize_to_mxfp4 / _float_to_e2m1_nibble)
+ *   oracle_mxfp8_hw_quant   vllm_qdq_plugin/sage3_attn/sage3/mxfp8_hw_kernel.py:37-65
+ *                           (quantize_to_mxfp8)
  *   oracle_mxfp8_qdq        vllm_qdq_plugin/qdq/mxfp8.py:73-125 (+ _round_half_to_even
  *                           :24-37, _quantize_to_e4m3fn_no_fp8_dtype :40-70)
  * Pinned against fixtures produced by importing the reference itself
@@ -327,6 +329,45 @@ void oracle_mxfp4_hw_quant(const float* x, uint8_t* codes, uint8_t* scales, int6
         }
         codes[r * (K / 2) + g * 16 + i / 2] = (uint8_t)(nib[0] | (nib[1] << 4));
       }
+    }
+  }
+}
+
+/* ------------------------------------------------------------------ */
+/* quantize_to_mxfp8 (sage3/mxfp8_hw_kernel.py:37-65): fp32 rows of length */
+/* K (K % 32 == 0) -> E4M3 bytes [rows, K] + E8M0 bytes [rows, K/32]:      */
+/*   e = ceil(log2(max(amax, 1e-12) / 448)), byte clamp(e + 127, 0, 254),  */
+/*   code = torch's float8_e4m3fn cast of x / 2^e (round-to-nearest-even). */
+/* ------------------------------------------------------------------ */
+static uint8_t e4m3_rne_byte(float x) {   /* |x| <= 448 */
+  const uint8_t sgn = signbit(x) ? 0x80 : 0;
+  const float a = fabsf(x);
+  if (a < 0x1p-6f) return (uint8_t)(sgn | (int)nearbyintf(a * 512.0f));  /* 8 -> 0x08, the min normal */
+  int e = ilogbf(a);
+  int m = (int)nearbyintf(a / ldexpf(1.0f, e - 3));                     /* 8 .. 16 */
+  if (m == 16) { m = 8; ++e; }
+  if (e > 8 || (e == 8 && m > 14)) { e = 8; m = 14; }                    /* 448 */
+  return (uint8_t)(sgn | ((e + 7) << 3) | (m - 8));
+}
+
+void oracle_mxfp8_hw_quant(const float* x, uint8_t* codes, uint8_t* scales, int64_t rows, int64_t K,
+                           int nthreads) {
+#ifdef _OPENMP
+  if (nthreads > 0) omp_set_num_threads(nthreads);
+#pragma omp parallel for schedule(static) if (nthreads != 1)
+#endif
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t g = 0; g < K / 32; ++g) {
+      const float* xg = x + r * K + g * 32;
+      float amax = 0.0f;
+      for (int i = 0; i < 32; ++i) { float a = fabsf(xg[i]); if (a > amax) amax = a; }
+      if (amax < 1e-12f) amax = 1e-12f;
+      int b = ceil_log2_exact(amax / 448.0f) + 127;
+      if (b < 0) b = 0;
+      if (b > 254) b = 254;
+      scales[r * (K / 32) + g] = (uint8_t)b;
+      const float sc = ldexpf(1.0f, b - 127);
+      for (int i = 0; i < 32; ++i) codes[r * K + g * 32 + i] = e4m3_rne_byte(xg[i] / sc);
     }
   }
 }

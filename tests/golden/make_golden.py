@@ -15,6 +15,8 @@ Each fixture is a compressed .npz of inputs and the reference's own outputs:
                                     several global scales, and a config-2 slice.
   mxfp4_hw_quant.npz                reference quantize_to_mxfp4 (sage3/mxfp4_hw_kernel.py:73)
                                     codes and E8M0 bytes for Q/K-like and V-like rows.
+  mxfp8_hw_quant.npz                reference quantize_to_mxfp8 (sage3/mxfp8_hw_kernel.py:37)
+                                    E4M3 codes and E8M0 bytes for Q/K-like and V-like rows.
   mxfp8_bf16.npz / mxfp8_fp16.npz   reference mxfp8_qdq (src/vllm_qdq_plugin/qdq/mxfp8.py:73)
                                     on every finite 16-bit pattern in natural 32-groups, on
                                     context groups reaching 20 binades below their max (into
@@ -25,6 +27,7 @@ The reference is imported from its checkout; nothing from it is copied here.
 from __future__ import annotations
 
 import argparse
+import ast
 import importlib.util
 import sys
 from pathlib import Path
@@ -56,6 +59,42 @@ def load_reference_mxfp8(ref_root: Path):
     m8 = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(m8)
     return m8.mxfp8_qdq
+
+
+def load_reference_mxfp8_hw(ref_root: Path):
+    """quantize_to_mxfp8 from the reference's mxfp8_hw_kernel.py.  Importing the
+    module asks Triton for an active GPU driver, so only the two CPU-safe
+    functions it needs are compiled from the reference file here and run."""
+    path = ref_root / "src/vllm_qdq_plugin/sage3_attn/sage3/mxfp8_hw_kernel.py"
+    tree = ast.parse(path.read_text())
+    keep = [n for n in tree.body if isinstance(n, ast.FunctionDef)
+            and n.name in ("fp8e8m0_to_float32", "quantize_to_mxfp8")]
+    assert len(keep) == 2
+    ns = {"torch": torch}
+    exec(compile(ast.Module(body=keep, type_ignores=[]), str(path), "exec"), ns)
+    return ns["quantize_to_mxfp8"]
+
+
+def write_mxfp8_hw(ref_root: Path):
+    quantize_to_mxfp8 = load_reference_mxfp8_hw(ref_root)
+    g = torch.Generator().manual_seed(98)
+    qk = (torch.randn(512, 128, generator=g) * torch.exp(torch.randn(512, 1, generator=g) * 3)
+          ).to(torch.bfloat16).float()
+    qk[7] = 0.0                                     # all-zero group: amax clamped to 1e-12
+    qk[9, :32] = torch.tensor([2.0 ** -40] * 32)    # tiny values (E4M3 subnormal / zero codes)
+    qk[11, :32] = -(2.0 ** -30)                     # tiny negatives under a large max: -0 codes
+    qk[11, 0] = -1.0
+    qk[13, 0] = 448.0                               # amax / 448 an exact power of two
+    qk[15, 0] = 450.0                               # just above: the exponent bumps
+    v = (torch.randn(128, 1024, generator=g) * 3).to(torch.bfloat16).float()
+    out = {}
+    for name, t in (("qk", qk), ("v", v)):
+        codes, scales = quantize_to_mxfp8(t)
+        out[f"{name}_x"] = t.numpy()
+        out[f"{name}_codes"] = codes.view(torch.uint8).numpy()
+        out[f"{name}_scales"] = scales.numpy()
+    np.savez_compressed(HERE / "mxfp8_hw_quant.npz", **out)
+    print("wrote mxfp8_hw_quant.npz")
 
 
 def finite_patterns(fp16: bool) -> np.ndarray:
@@ -108,8 +147,12 @@ def bits_of(t: torch.Tensor) -> np.ndarray:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=["all", "mxfp8"], default="all")
+    ap.add_argument("--only", choices=["all", "mxfp8", "mxfp8_hw"], default="all")
     args = ap.parse_args()
+    if args.only in ("all", "mxfp8_hw"):
+        write_mxfp8_hw(Path(args.reference))
+    if args.only == "mxfp8_hw":
+        return
     write_mxfp8(Path(args.reference))
     if args.only == "mxfp8":
         return

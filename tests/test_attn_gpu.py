@@ -1,4 +1,4 @@
-"""GPU parity of the sm_100a Sage3 FP4 attention (through the C ABI).
+"""GPU parity of the sm_100a Sage3 FP4 / FP8 attention (through the C ABI).
 
 Oracle: oracle/attn.py, a numpy restatement of the reference's paths
 (qk_smoothing + FP4 quantisation + the flash loop).  The kernel steps its
@@ -94,6 +94,83 @@ def test_config5_flux_shape_nvfp4(cuda_device):
     sm = 1.0 / math.sqrt(128)
     want = oa.attention(_bits(q[0]), _bits(k[0]), _bits(v[0]), sm, block_n=KERNEL_BLOCK_N, config="nvfp4")
     assert oa.rel_l2(got, want) < 2e-2
+
+
+@pytest.mark.parametrize("L,H", [(128, 1), (300, 2), (1000, 1)])
+def test_mxfp8_attention_matches_oracle(cuda_device, L, H):
+    """mxfp8_hw (E4M3 Q/K/V/P on kind::mxf8f6f4): relative L2 vs the same-tile
+    oracle <= 1e-2, and the error vs exact attention within 1.1x (+0.005) of
+    the reference-tiled oracle's."""
+    q, k, v = _qkv(L, H, seed=L + 5 * H)
+    sm = 1.0 / math.sqrt(128)
+    got = _run(q, k, v, cuda_device, config="mxfp8_hw")[0]
+    qb, kb, vb = _bits(q[0]), _bits(k[0]), _bits(v[0])
+    want = oa.attention(qb, kb, vb, sm, block_n=KERNEL_BLOCK_N, config="mxfp8_hw")
+    err = oa.rel_l2(got, want)
+    assert err < 1e-2, f"rel L2 vs oracle {err}"
+    exact = oa.exact_attention(qb, kb, vb, sm)
+    ref_err = oa.rel_l2(oa.attention(qb, kb, vb, sm, mask_padding=False, config="mxfp8_hw"), exact)
+    our_err = oa.rel_l2(got, exact)
+    assert our_err <= 1.1 * ref_err + 0.005, (our_err, ref_err)
+    # MXFP8 is far closer to exact attention than MXFP4
+    assert our_err < 0.5 * oa.rel_l2(oa.attention(qb, kb, vb, sm, block_n=KERNEL_BLOCK_N), exact)
+    from vllm_qdq_plugin import _native
+    assert _native.device_status() == 0
+
+
+def test_mxfp8_causal_and_no_smoothing(cuda_device):
+    q, k, v = _qkv(384, 1, seed=17)
+    sm = 1.0 / math.sqrt(128)
+    qb, kb, vb = _bits(q[0]), _bits(k[0]), _bits(v[0])
+    got = _run(q, k, v, cuda_device, causal=True, config="mxfp8_hw")[0]
+    want = oa.attention(qb, kb, vb, sm, block_n=KERNEL_BLOCK_N, causal=True, config="mxfp8_hw")
+    assert oa.rel_l2(got, want) < 1e-2
+    got = _run(q, k, v, cuda_device, smoothing=False, config="mxfp8_hw")[0]
+    want = oa.attention(qb, kb, vb, sm, block_n=KERNEL_BLOCK_N, smoothing=False, config="mxfp8_hw")
+    assert oa.rel_l2(got, want) < 1e-2
+
+
+def _sf_tile(buf: np.ndarray, tiles: int) -> np.ndarray:
+    """Scale bytes [tiles * 128, 4] from 1024-byte tcgen05 chunks (row r, group g
+    at (r % 32) * 16 + (r // 32) * 4 + g of the first 512 bytes)."""
+    t = buf[: tiles * 1024].reshape(tiles, 1024)[:, :512].reshape(tiles, 32, 4, 4)  # [tile, r%32, r//32, g]
+    return t.transpose(0, 2, 1, 3).reshape(tiles * 128, 4)
+
+
+def test_mxfp8_prepass_codes_bit_exact(cuda_device):
+    """The pre-pass's E4M3 codes and E8M0 scales of q_s, k_c (along D) and V
+    (along the sequence), read back from the workspace, dequantise to exactly
+    the oracle's quantize_to_mxfp8 values (smoothing included)."""
+    import ctypes
+    from vllm_qdq_plugin import _native
+    L, H = 300, 1
+    q, k, v = _qkv(L, H, seed=23)
+    dev = cuda_device
+    qd_, kd_, vd_ = (t.to(dev) for t in (q, k, v))
+    out = torch.empty_like(qd_)
+    lib = _native.lib()
+    nbytes = lib.sage3_attn_workspace_bytes(1, L, H, 128)
+    ws = torch.zeros((nbytes,), dtype=torch.uint8, device=dev)
+    st = [qd_.stride(0), qd_.stride(1), qd_.stride(2)] * 3 + [out.stride(0), out.stride(1), out.stride(2)]
+    _native.call("sage3_fp4_attn", qd_.data_ptr(), kd_.data_ptr(), vd_.data_ptr(), out.data_ptr(), 1, L, H, 128,
+                 (ctypes.c_int64 * 12)(*st), 1.0 / math.sqrt(128), 3, 0, 0, 1, 0, ws.data_ptr(), nbytes,
+                 _native.stream_ptr(dev))
+    torch.cuda.synchronize()
+    w = ws.cpu().numpy()
+    Lp, G = 384, 3
+    up = lambda n: (n + 255) // 256 * 256  # noqa: E731
+    off = up(128 * 4) + up(G * 128 * 2)
+    qc = w[off: off + Lp * 128].reshape(Lp, 128); off += up(Lp * 128)
+    qsf = _sf_tile(w[off:], G); off += up(G * 1024)
+    kc = w[off: off + Lp * 128].reshape(Lp, 128); off += up(Lp * 128)
+    ksf = _sf_tile(w[off:], G); off += up(G * 1024)
+    vt = w[off: off + 128 * Lp].reshape(128, Lp); off += up(128 * Lp)
+    vsf = _sf_tile(w[off:], G).reshape(G, 128, 4).transpose(1, 0, 2).reshape(128, G * 4)  # [d, key group]
+    qd, kd, vd, _ = oa.prepass(oa.bf16_bits_to_f32(_bits(q[0, :, 0])), oa.bf16_bits_to_f32(_bits(k[0, :, 0])),
+                               oa.bf16_bits_to_f32(_bits(v[0, :, 0])), True, False, True)
+    np.testing.assert_array_equal(oa._deq8(qc, qsf), qd)
+    np.testing.assert_array_equal(oa._deq8(kc, ksf), kd)
+    np.testing.assert_array_equal(oa._deq8(vt, vsf).T, vd)
 
 
 def test_causal_and_no_smoothing(cuda_device):

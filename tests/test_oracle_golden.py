@@ -55,6 +55,17 @@ def test_mxfp4_hw_quant_oracle_matches_reference():
         np.testing.assert_array_equal(scales, d[f"{name}_scales"])
 
 
+def test_mxfp8_hw_quant_oracle_matches_reference():
+    """quantize_to_mxfp8 (sage3/mxfp8_hw_kernel.py:37): E4M3 codes (including
+    -0 codes) and E8M0 bytes (including the 1e-12 clamp and exact powers of
+    two) equal the reference's."""
+    d = golden("mxfp8_hw_quant.npz")
+    for name in ("qk", "v"):
+        codes, scales = oq.mxfp8_hw_quant(d[f"{name}_x"])
+        np.testing.assert_array_equal(codes, d[f"{name}_codes"])
+        np.testing.assert_array_equal(scales, d[f"{name}_scales"])
+
+
 def test_e4m3_rounding_matches_torch_cast():
     # the NVFP4 block scale is torch's fp32 -> float8_e4m3fn -> fp32 cast
     g = torch.Generator().manual_seed(0)

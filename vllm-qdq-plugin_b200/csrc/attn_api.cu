@@ -1,4 +1,4 @@
-// C-ABI entry of the Sage3 FP4 attention (pre-pass + flash kernel).
+// C-ABI entry of the Sage3 FP4 / FP8 attention (pre-pass + flash kernel).
 #include "attn_common.cuh"
 
 using namespace qdqb200;
@@ -16,8 +16,9 @@ extern "C" int sage3_fp4_attn(const void* q, const void* k, const void* v, void*
   if (B == 0 || L == 0 || H == 0) return QDQ_OK;
   if (D != 128) return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: head_dim %lld (this build supports 128)", (long long)D);
   if (dtype != QDQ_DTYPE_BF16) return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: inputs must be bf16");
-  if (quant_format < 0 || quant_format > 2)
-    return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: quant_format must be 0 (mxfp4_hw), 1 (nvfp4) or 2 (mxfp4)");
+  if (quant_format < 0 || quant_format > 3)
+    return fail(QDQ_ERR_INVALID_ARG,
+                "sage3_fp4_attn: quant_format must be 0 (mxfp4_hw), 1 (nvfp4), 2 (mxfp4) or 3 (mxfp8_hw)");
   if (acc_mode < 0 || acc_mode > 1) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: acc_mode must be 0 or 1");
   if (!q || !k || !v || !o || !strides) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: null pointer");
   if (!(sm_scale > 0.f)) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: sm_scale must be positive");
@@ -48,7 +49,8 @@ extern "C" int sage3_fp4_attn(const void* q, const void* k, const void* v, void*
   p.causal = causal ? 1 : 0;
   p.smoothing = smoothing ? 1 : 0;
   p.nv = quant_format == 1 ? 1 : 0;
-  p.emulated = quant_format == 0 ? 0 : 1;
+  p.emulated = (quant_format == 1 || quant_format == 2) ? 1 : 0;
+  p.fp8 = quant_format == 3 ? 1 : 0;
   attn::Workspace w;
   attn::carve(p.B, p.H, p.L, static_cast<uint8_t*>(workspace), &w);
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -24,17 +24,18 @@ struct Problem {
   int nv;         // 0: MXFP4 (E8M0 per 32), 1: NVFP4 (E4M3 per 16)
   int emulated;   // 1: the reference's emulated-config P handling (P scaled by 448*6 before
                   //    block scaling, l = sum of quantised P); 0: its mxfp4_hw kernel's
+  int fp8;        // 1: MXFP8 (E4M3 + E8M0 per 32) operands, the reference's mxfp8_hw kernel
 };
 
 // Device buffers of the pre-pass (carved out of the caller's workspace).
 struct Workspace {
   float* ksum;            // [BH, 128]
   __nv_bfloat16* qmean;   // [BH, G, 128]
-  uint8_t* qc;            // [BH * Lp, 64]
+  uint8_t* qc;            // [BH * Lp, 64] (E2M1) or [BH * Lp, 128] (E4M3)
   uint8_t* qsf;           // [BH * Lp / 128, 1024]
-  uint8_t* kc;            // [BH * Lp, 64]
+  uint8_t* kc;            // as qc
   uint8_t* ksf;           // [BH * Lp / 128, 1024]
-  uint8_t* vt;            // [BH * 128, Lp / 2]
+  uint8_t* vt;            // [BH * 128, Lp / 2] (E2M1) or [BH * 128, Lp] (E4M3)
   uint8_t* vsf;           // [BH * Lp / 128, 1024]
   float* ds;              // [BH, G, Lp] (bf16-rounded values, stored as fp32)
 };
@@ -42,6 +43,7 @@ struct Workspace {
 inline int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 
 // Carve the workspace; returns total bytes needed (ws may be null to query).
+// The code buffers are sized for 8-bit codes, so one size serves every format.
 inline int64_t carve(int B, int H, int L, uint8_t* base, Workspace* w) {
   const int64_t BH = static_cast<int64_t>(B) * H;
   const int64_t Lp = (static_cast<int64_t>(L) + 127) / 128 * 128;
@@ -54,11 +56,11 @@ inline int64_t carve(int B, int H, int L, uint8_t* base, Workspace* w) {
   };
   uint8_t* ksum = take(BH * 128 * 4);
   uint8_t* qmean = take(BH * G * 128 * 2);
-  uint8_t* qc = take(BH * Lp * 64);
+  uint8_t* qc = take(BH * Lp * 128);
   uint8_t* qsf = take(BH * G * 1024);
-  uint8_t* kc = take(BH * Lp * 64);
+  uint8_t* kc = take(BH * Lp * 128);
   uint8_t* ksf = take(BH * G * 1024);
-  uint8_t* vt = take(BH * 128 * Lp / 2);
+  uint8_t* vt = take(BH * 128 * Lp);
   uint8_t* vsf = take(BH * G * 1024);
   uint8_t* ds = take(BH * G * Lp * 4);
   if (w) {

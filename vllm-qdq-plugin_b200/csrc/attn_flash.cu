@@ -1,6 +1,6 @@
-// Sage3 FP4 flash attention on sm_100a tensor cores, D = 128.
-// MXFP4 (E2M1 + E8M0 per 32, tcgen05 kind::mxf4) or NVFP4 (E2M1 + E4M3 per
-// 16, kind::mxf4nvf4 block16).
+// Sage3 FP4 / FP8 flash attention on sm_100a tensor cores, D = 128.
+// MXFP4 (E2M1 + E8M0 per 32, tcgen05 kind::mxf4), NVFP4 (E2M1 + E4M3 per
+// 16, kind::mxf4nvf4 block16) or MXFP8 (E4M3 + E8M0 per 32, kind::mxf8f6f4).
 //
 // Reference semantics: the mxfp4_hw kernel (sage3/mxfp4_hw_kernel.py:167-393)
 //   S  = dot_scaled(Q, K^T) (+ delta_s[group of the query tile, key]),
@@ -11,8 +11,11 @@
 //   O += dot_scaled(P, V), O / l at the end;
 // and, for the emulated configs (p_quant_kernels.py:37-150,
 // attention_kernel.py:176-186), P scaled by 448*6 before block scaling and
-// l = sum of the dequantised P.  Keys beyond L are masked (the reference
-// attends to its zero padding).
+// l = sum of the dequantised P.  The mxfp8_hw kernel
+// (sage3/mxfp8_hw_kernel.py:88-246) is the mxfp4_hw one with E4M3 operands:
+// P scale e = clamp(ceil(log2(max(p)/448)), -127, 127), codes
+// E4M3(min(p * 2^-e, 448)) round-to-nearest-even.  Keys beyond L are masked
+// (the reference attends to its zero padding).
 //
 // CTA = two 128-row query tiles (A, B) of one (batch, head) that share every
 // K/V tile, 12 warps:
@@ -25,8 +28,9 @@
 //   warp 8        MMA issuer: per key tile j, S = Q_A K_j^T, then (once A has
 //                 read S) S = Q_B K_j^T, then O_A += P_A V_{j-1}, O_B += P_B V_{j-1}
 //   warp 9        TMA producer: K tile [128 keys x 64 B], V^T tile [128 d x 64 B]
-//                 (64-byte swizzle), their scale chunks and both tiles' delta_s
-//                 slices (128 fp32 each) into a 4-stage ring; Q_A, Q_B once
+//                 (64-byte swizzle; E4M3: 128 B rows, 128-byte swizzle), their
+//                 scale chunks and both tiles' delta_s slices (128 fp32 each)
+//                 into a 4-stage ring (3 for E4M3); Q_A, Q_B once
 //   warps 10-11   idle (they complete the third warpgroup for setmaxnreg)
 // The single S buffer alternates between the two softmax warpgroups, which
 // therefore run out of phase and overlap their MUFU / FMA / ALU work.
@@ -42,23 +46,10 @@ namespace {
 using namespace sm100;
 
 constexpr int BM = 128, BN = 128, HD = 128;
-constexpr int STAGES = 4;
-constexpr int CODE_TILE = 128 * 64;  // 8 KB: 128 rows x 128 E2M1
+constexpr int MAX_STAGES = 4;
 constexpr int SF_CHUNK = 512;
 constexpr int SF_TILE = 1024;        // scale bytes per 128-row tile in global memory (two chunks)
 constexpr int DS_BYTES = BN * 4;     // delta_s slice of one query tile: 128 fp32
-// stage: K codes | V codes | K sf | V sf | delta_s A | delta_s B
-constexpr int ST_K = 0, ST_V = CODE_TILE, ST_KSF = 2 * CODE_TILE, ST_VSF = ST_KSF + SF_TILE,
-              ST_DS = ST_VSF + SF_TILE;
-constexpr int STAGE_BYTES = 19 * 1024;
-static_assert(ST_DS + 2 * DS_BYTES <= STAGE_BYTES, "stage layout");
-// CTA smem: Q_A | Q_B | P_A[2] | P_B[2] | stages | Q sf A,B | P sf A[2],B[2] | barriers
-// P (codes and scales) is double-buffered per query tile: key tile j writes
-// buffer j & 1 while PV(j-1) may still read the other one.
-constexpr int OFF_Q = 0, OFF_P = 2 * CODE_TILE, OFF_STAGE = 6 * CODE_TILE;
-constexpr int OFF_QSF = OFF_STAGE + STAGES * STAGE_BYTES;
-constexpr int OFF_PSF = OFF_QSF + 2 * SF_TILE;
-constexpr int OFF_BAR = OFF_PSF + 4 * SF_TILE;
 constexpr int THREADS = 384;
 constexpr int TMEM_COLS = 512;
 // scale-factor columns: 8 per operand (NVFP4: two chunks; MXFP4 uses the first 4)
@@ -66,8 +57,8 @@ constexpr uint32_t T_S = 0, T_O = 128, T_SFQ = 384, T_SFK = 400, T_SFP = 408, T_
 
 struct Bars {
   uint64_t q_full;
-  uint64_t kv_full[STAGES];
-  uint64_t kv_empty[STAGES];
+  uint64_t kv_full[MAX_STAGES];
+  uint64_t kv_empty[MAX_STAGES];
   uint64_t s_full[2];   // per warpgroup: S holds its tile's scores
   uint64_t s_free[2];   // per warpgroup: its scores are in registers
   uint64_t p_full[2];   // per warpgroup: its P codes / scales are in shared memory
@@ -76,7 +67,31 @@ struct Bars {
   uint32_t tmem_base;
   int abort;
 };
-constexpr size_t SMEM_BYTES = 1024 + OFF_BAR + sizeof(Bars);
+
+// Shared-memory layout for E2M1 (kF8 = false: 64-byte code rows) or E4M3
+// (128-byte rows) operands.
+// stage: K codes | V codes | K sf | V sf | delta_s A | delta_s B
+// CTA: Q_A | Q_B | P_A[2] | P_B[2] | stages | Q sf A,B | P sf A[2],B[2] | barriers
+// P (codes and scales) is double-buffered per query tile: key tile j writes
+// buffer j & 1 while PV(j-1) may still read the other one.
+template <bool kF8>
+struct FL {
+  static constexpr int ROW = kF8 ? 128 : 64;  // code bytes per 128-element row
+  static constexpr int CODE_TILE = 128 * ROW;
+  static constexpr int STAGES = kF8 ? 3 : 4;
+  static constexpr int ST_K = 0, ST_V = CODE_TILE, ST_KSF = 2 * CODE_TILE, ST_VSF = ST_KSF + SF_TILE,
+                       ST_DS = ST_VSF + SF_TILE;
+  static constexpr int STAGE_BYTES = (ST_DS + 2 * DS_BYTES + 1023) / 1024 * 1024;
+  static constexpr int OFF_Q = 0, OFF_P = 2 * CODE_TILE, OFF_STAGE = 6 * CODE_TILE;
+  static constexpr int OFF_QSF = OFF_STAGE + STAGES * STAGE_BYTES;
+  static constexpr int OFF_PSF = OFF_QSF + 2 * SF_TILE;
+  static constexpr int OFF_BAR = OFF_PSF + 4 * SF_TILE;
+  static constexpr size_t SMEM_BYTES = 1024 + OFF_BAR + sizeof(Bars);
+  static_assert(STAGES <= MAX_STAGES && SMEM_BYTES <= 227 * 1024, "flash layout");
+};
+__device__ __forceinline__ uint64_t code_desc(bool f8, const void* p) {
+  return f8 ? smem_desc_sw128(p) : smem_desc_sw64(p);
+}
 
 struct Params {
   int H, L, Lp, T;  // T = Lp / 128
@@ -92,6 +107,7 @@ enum Mode : int {
   kMxHw = 0,   // MXFP4, the reference mxfp4_hw kernel's P handling (l = sum of unquantised p)
   kMxEmu = 1,  // MXFP4, the emulated config's P handling (p * 448*6, l = sum of quantised P)
   kNvEmu = 2,  // NVFP4 (E4M3 per 16), emulated-config P handling
+  kMx8Hw = 3,  // MXFP8 (E4M3 + E8M0 per 32), the reference mxfp8_hw kernel's P handling
 };
 
 // Sum of four fp16x2 words holding decoded E2M1 values (exact in fp16: the
@@ -144,10 +160,33 @@ __device__ __forceinline__ int mx_block_exp(float amax) {
   return min(e, 127);
 }
 
-// The two K=64 block-scaled MMAs of a 128 x 128 x 128 product.
-template <bool kNV>
+// E8M0 block exponent of the mxfp8_hw kernel's P for a finite amax >= 0:
+// e = clamp(ceil(log2(amax / 448)), -127, 127).  For amax = M * 2^E
+// (1 <= M < 2) the quotient is (M / 1.75) * 2^(E-8) with a zero mantissa only
+// at M == 1.75, so the ceiling is E - 8 + (M > 1.75); amax exponent fields
+// below 8 (a quotient under 2^-127) clamp to -127, and so does amax = 0.
+__device__ __forceinline__ int mx8_block_exp(float amax) {
+  const uint32_t b = __float_as_uint(amax);
+  const int e = static_cast<int>(b >> 23) - 135 + ((b & 0x7FFFFFu) > 0x600000u ? 1 : 0);
+  return min(max(e, -127), 127);
+}
+
+// The block-scaled MMAs of a 128 x 128 x 128 product: two K=64 (E2M1) or
+// four K=32 (E4M3) instructions.
+template <int kMode>
 __device__ __forceinline__ void mma_k128(uint32_t d, uint64_t da, uint64_t db, uint32_t sfa, uint32_t sfb,
                                          bool accumulate_first) {
+  constexpr bool kNV = kMode == kNvEmu;
+  if (kMode == kMx8Hw) {
+    constexpr uint32_t idesc8 = idesc_mxf8(BM, BN);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {  // 32 E4M3 = 32 bytes per step; scale byte kk of the chunk
+      const uint32_t sf_id = kk;
+      mma_mxf8(d, da + kk * 2, db + kk * 2, idesc_with_sf_ids(idesc8, sf_id, sf_id), sfa | (sf_id << 30),
+               sfb | (sf_id << 30), accumulate_first || kk);
+    }
+    return;
+  }
   constexpr uint32_t idesc = idesc_mxf4(BM, BN, !kNV);
 #pragma unroll
   for (int kk = 0; kk < 2; ++kk) {
@@ -192,6 +231,8 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
                                            int qt, int bh, int nkv, __nv_bfloat16* __restrict__ out,
                                            int* status) {
   constexpr bool kNV = kMode == kNvEmu;
+  constexpr bool kF8 = kMode == kMx8Hw;
+  using Lay = FL<kF8>;
   constexpr int NG = kNV ? 8 : 4;            // scale blocks per row of 128 keys
   const int warp = (threadIdx.x >> 5) & 3;
   const int lane = threadIdx.x & 31;
@@ -199,19 +240,20 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
   const uint32_t t_o = tmem + T_O + wg * 128;
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t prow0 = sbase + OFF_P + 2 * wg * CODE_TILE + r * 64;                   // this row of P
-  const uint32_t psf0 = sbase + OFF_PSF + 2 * wg * SF_TILE + (r & 31) * 16 + (r >> 5) * 4;  // its scale word
-  const int swz = (r >> 1) & 3;              // 64-byte swizzle of this row's 16-byte chunks
+  const uint32_t prow0 = sbase + Lay::OFF_P + 2 * wg * Lay::CODE_TILE + r * Lay::ROW;         // this row of P
+  const uint32_t psf0 = sbase + Lay::OFF_PSF + 2 * wg * SF_TILE + (r & 31) * 16 + (r >> 5) * 4;  // its scale word
+  // swizzle of this row's 16-byte chunks: 64-byte (E2M1) or 128-byte (E4M3) pattern
+  const int swz = kF8 ? (r & 7) : ((r >> 1) & 3);
   const float qk = p.qk_scale;
   const int qrow = qt * BM + r;
   float m_run = -INFINITY, l_run = 0.f;
   bool ok = true;
   for (int j = 0; j < nkv; ++j) {
-    const int s = j % STAGES;
+    const int s = j % Lay::STAGES;
     // After a failed (timed-out) wait the thread stops waiting but keeps
     // iterating, so the other roles are never left waiting on it.
     if (ok) ok = mbar_wait(&bars->s_full[wg], j & 1, status, 0x1301) &&
-                 mbar_wait(&bars->kv_full[s], (j / STAGES) & 1, status, 0x1302);
+                 mbar_wait(&bars->kv_full[s], (j / Lay::STAGES) & 1, status, 0x1302);
     ok = __all_sync(0xffffffffu, ok);  // warp-uniform: the TMEM accesses below are .sync.aligned
     tc_fence_after();
     float x[BN];
@@ -226,7 +268,7 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     tc_fence_before();
     mbar_arrive(&bars->s_free[wg]);
     if (p.smoothing) {  // + delta_s[key]: one fp32 row shared by the whole tile (broadcast loads)
-      const uint32_t dsv = sbase + OFF_STAGE + s * STAGE_BYTES + ST_DS + wg * DS_BYTES;
+      const uint32_t dsv = sbase + Lay::OFF_STAGE + s * Lay::STAGE_BYTES + Lay::ST_DS + wg * DS_BYTES;
 #pragma unroll
       for (int c = 0; c < BN / 4; ++c) {
         const float4 d = lds128f(dsv + 16 * c);
@@ -260,10 +302,45 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     m_run = m_new;
     // P(j) goes to buffer j & 1; PV(j-2), its previous reader, completed before
     // p_full(j-1) was signalled (the o_done wait below, one tile earlier).
-    const uint32_t prow = prow0 + (j & 1) * CODE_TILE;
+    const uint32_t prow = prow0 + (j & 1) * Lay::CODE_TILE;
     const uint32_t psf = psf0 + (j & 1) * SF_TILE;
     const float2 qk2 = make_float2(qk, qk);
-    if (kMode == kMxHw) {
+    if (kMode == kMx8Hw) {
+      // P -> E4M3 codes (round-to-nearest-even, saturating at 448 as the
+      // reference's min(., 448)) with E8M0 2^e per 32 keys,
+      // e = clamp(ceil(log2(max p / 448)), -127, 127), folded into the
+      // exponent as for E2M1; l += sum of the unquantised p.
+      uint32_t sfw = 0;
+      float lsum = 0.f;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int e = mx8_block_exp(ex2_approx(fmaf(gm[g], qk, -m_new)));
+        const float cg = -m_new - static_cast<float>(e);
+        const float2 c2 = make_float2(cg, cg);
+        float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        uint32_t w[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float v[4];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int n = g * 32 + q * 4 + 2 * i;
+            const float2 t = fma_f32x2(make_float2(x[n], x[n + 1]), qk2, c2);
+            v[2 * i] = ex2_approx(t.x);
+            v[2 * i + 1] = ex2_approx(t.y);
+            acc[i] = add_f32x2(acc[i], make_float2(v[2 * i], v[2 * i + 1]));
+          }
+          w[q] = cvt_e4m3x4(v[0], v[1], v[2], v[3]);
+        }
+        const float2 a = add_f32x2(acc[0], acc[1]);
+        lsum = fmaf(a.x + a.y, exp2i(e), lsum);
+        sts128(prow + (((2 * g) ^ swz) << 4), w[0], w[1], w[2], w[3]);
+        sts128(prow + (((2 * g + 1) ^ swz) << 4), w[4], w[5], w[6], w[7]);
+        sfw |= static_cast<uint32_t>(e + 127) << (8 * g);
+      }
+      l_run += lsum;
+      sts32(psf, sfw);
+    } else if (kMode == kMxHw) {
       // P -> E2M1 codes (round-to-nearest-even) with E8M0 2^e per 32 keys,
       // e = clamp(ceil(log2(max p / 6)), -127, 127).  The block scale is folded
       // into the exponent: p * 2^-e = exp2(x * qk - m - e).  l += sum of p
@@ -424,9 +501,12 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
                        const float* __restrict__ ds, __nv_bfloat16* __restrict__ out, Params p,
                        int* status) {
   constexpr bool kNV = kMode == kNvEmu;
+  constexpr bool kF8 = kMode == kMx8Hw;
+  using Lay = FL<kF8>;
+  constexpr int STAGES = Lay::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
+  Bars* bars = reinterpret_cast<Bars*>(smem + Lay::OFF_BAR);
   const int warp = threadIdx.x >> 5;
   const int qtA = 2 * blockIdx.x;
   const int qtB = qtA + 1;
@@ -473,10 +553,10 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
     if (warp == 9) {
       // ------------------------------------------------------------ producer
       if (elect_one()) {
-        mbar_arrive_expect_tx(&bars->q_full, nq * (CODE_TILE + kSfBytes));
+        mbar_arrive_expect_tx(&bars->q_full, nq * (Lay::CODE_TILE + kSfBytes));
         for (int t = 0; t < nq; ++t) {
-          tma_load_2d(smem + OFF_Q + t * CODE_TILE, &map_q, 0, bh * p.Lp + (qtA + t) * BM, &bars->q_full);
-          bulk_load(smem + OFF_QSF + t * SF_TILE, qsf + (static_cast<int64_t>(bh) * p.T + qtA + t) * SF_TILE,
+          tma_load_2d(smem + Lay::OFF_Q + t * Lay::CODE_TILE, &map_q, 0, bh * p.Lp + (qtA + t) * BM, &bars->q_full);
+          bulk_load(smem + Lay::OFF_QSF + t * SF_TILE, qsf + (static_cast<int64_t>(bh) * p.T + qtA + t) * SF_TILE,
                     kSfBytes, &bars->q_full);
         }
         int issued = 0;
@@ -487,16 +567,18 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
             break;
           }
           if (*(volatile int*)&bars->abort) break;
-          uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
-          const uint32_t bytes = 2 * CODE_TILE + 2 * kSfBytes + (p.smoothing ? nq * DS_BYTES : 0);
+          uint8_t* st = smem + Lay::OFF_STAGE + s * Lay::STAGE_BYTES;
+          const uint32_t bytes = 2 * Lay::CODE_TILE + 2 * kSfBytes + (p.smoothing ? nq * DS_BYTES : 0);
           mbar_arrive_expect_tx(&bars->kv_full[s], bytes);
-          tma_load_2d(st + ST_K, &map_k, 0, bh * p.Lp + j * BN, &bars->kv_full[s]);
-          tma_load_2d(st + ST_V, &map_v, j * (BN / 2), bh * HD, &bars->kv_full[s]);
-          bulk_load(st + ST_KSF, ksf + (static_cast<int64_t>(bh) * p.T + j) * SF_TILE, kSfBytes, &bars->kv_full[s]);
-          bulk_load(st + ST_VSF, vsf + (static_cast<int64_t>(bh) * p.T + j) * SF_TILE, kSfBytes, &bars->kv_full[s]);
+          tma_load_2d(st + Lay::ST_K, &map_k, 0, bh * p.Lp + j * BN, &bars->kv_full[s]);
+          tma_load_2d(st + Lay::ST_V, &map_v, j * (kF8 ? BN : BN / 2), bh * HD, &bars->kv_full[s]);
+          bulk_load(st + Lay::ST_KSF, ksf + (static_cast<int64_t>(bh) * p.T + j) * SF_TILE, kSfBytes,
+                    &bars->kv_full[s]);
+          bulk_load(st + Lay::ST_VSF, vsf + (static_cast<int64_t>(bh) * p.T + j) * SF_TILE, kSfBytes,
+                    &bars->kv_full[s]);
           if (p.smoothing)
             for (int t = 0; t < nq; ++t)
-              bulk_load(st + ST_DS + t * DS_BYTES, ds + (static_cast<int64_t>(bh) * p.T + qtA + t) * p.Lp + j * BN,
+              bulk_load(st + Lay::ST_DS + t * DS_BYTES, ds + (static_cast<int64_t>(bh) * p.T + qtA + t) * p.Lp + j * BN,
                         DS_BYTES, &bars->kv_full[s]);
           ++issued;
         }
@@ -510,19 +592,19 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
         bool ok = mbar_wait(&bars->q_full, 0, status, 0x1201);
         if (ok) {
           tc_fence_after();
-          for (int t = 0; t < nq; ++t) cp_sf<kNV>(tmem + T_SFQ + t * 8, smem + OFF_QSF + t * SF_TILE);
+          for (int t = 0; t < nq; ++t) cp_sf<kNV>(tmem + T_SFQ + t * 8, smem + Lay::OFF_QSF + t * SF_TILE);
         }
         auto issue_pv = [&](int t) -> bool {
           const int s = t % STAGES;
-          uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
+          uint8_t* st = smem + Lay::OFF_STAGE + s * Lay::STAGE_BYTES;
           for (int w = 0; w < nq; ++w) {
             if (!mbar_wait(&bars->p_full[w], t & 1, status, 0x1202)) return false;
             tc_fence_after();
-            if (w == 0) cp_sf<kNV>(tmem + T_SFV, st + ST_VSF);
+            if (w == 0) cp_sf<kNV>(tmem + T_SFV, st + Lay::ST_VSF);
             const int pb = 2 * w + (t & 1);  // P buffer of key tile t
-            cp_sf<kNV>(tmem + T_SFP, smem + OFF_PSF + pb * SF_TILE);
-            mma_k128<kNV>(tmem + T_O + w * 128, smem_desc_sw64(smem + OFF_P + pb * CODE_TILE),
-                          smem_desc_sw64(st + ST_V), tmem + T_SFP, tmem + T_SFV, t != 0);
+            cp_sf<kNV>(tmem + T_SFP, smem + Lay::OFF_PSF + pb * SF_TILE);
+            mma_k128<kMode>(tmem + T_O + w * 128, code_desc(kF8, smem + Lay::OFF_P + pb * Lay::CODE_TILE),
+                            code_desc(kF8, st + Lay::ST_V), tmem + T_SFP, tmem + T_SFV, t != 0);
             tc_commit(&bars->o_done[w]);
           }
           tc_commit(&bars->kv_empty[s]);
@@ -532,7 +614,7 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
           const int s = j % STAGES;
           if (!mbar_wait(&bars->kv_full[s], (j / STAGES) & 1, status, 0x1203)) { ok = false; break; }
           if (*(volatile int*)&bars->abort) { ok = false; break; }
-          uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
+          uint8_t* st = smem + Lay::OFF_STAGE + s * Lay::STAGE_BYTES;
           for (int w = 0; w < nq && ok; ++w) {
             // S is free once the warpgroup that used it last has read its scores:
             // for A that is B (or A alone) at key tile j-1, for B it is A at key tile j.
@@ -540,9 +622,9 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
             const int prev_j = w == 0 ? j - 1 : j;
             if (prev_j >= 0 && !mbar_wait(&bars->s_free[prev], prev_j & 1, status, 0x1204)) { ok = false; break; }
             tc_fence_after();
-            if (w == 0) cp_sf<kNV>(tmem + T_SFK, st + ST_KSF);
-            mma_k128<kNV>(tmem + T_S, smem_desc_sw64(smem + OFF_Q + w * CODE_TILE), smem_desc_sw64(st + ST_K),
-                          tmem + T_SFQ + w * 8, tmem + T_SFK, false);
+            if (w == 0) cp_sf<kNV>(tmem + T_SFK, st + Lay::ST_KSF);
+            mma_k128<kMode>(tmem + T_S, code_desc(kF8, smem + Lay::OFF_Q + w * Lay::CODE_TILE),
+                            code_desc(kF8, st + Lay::ST_K), tmem + T_SFQ + w * 8, tmem + T_SFK, false);
             tc_commit(&bars->s_full[w]);
           }
           if (!ok) break;
@@ -565,6 +647,23 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
   }
 }
 
+template <int kMode>
+int launch_mode(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Workspace& w,
+                const Problem& pr, const Params& p, dim3 grid, int* status, cudaStream_t s) {
+  constexpr size_t smem = FL<kMode == kMx8Hw>::SMEM_BYTES;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(&sage3_fp4_flash_kernel<kMode>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "sage3 flash: smem attribute: %s", cudaGetErrorString(e));
+    attr[dev] = true;
+  }
+  sage3_fp4_flash_kernel<kMode><<<grid, THREADS, smem, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o, p, status);
+  return check_launch("sage3 flash");
+}
+
 }  // namespace
 
 int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
@@ -572,21 +671,14 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   if (status == nullptr) return QDQ_ERR_CUDA;
   const int64_t BH = static_cast<int64_t>(pr.B) * pr.H;
   CUtensorMap mq, mk, mv;
-  if (int st = make_tmap_u8_2d(&mq, w.qc, BH * pr.Lp, 64, 64, 64, 128, 64)) return st;
-  if (int st = make_tmap_u8_2d(&mk, w.kc, BH * pr.Lp, 64, 64, 64, 128, 64)) return st;
-  if (int st = make_tmap_u8_2d(&mv, w.vt, BH * HD, pr.Lp / 2, pr.Lp / 2, 64, 128, 64)) return st;
-  const int mode = pr.nv ? kNvEmu : (pr.emulated ? kMxEmu : kMxHw);
-  const void* fns[3] = {reinterpret_cast<const void*>(&sage3_fp4_flash_kernel<kMxHw>),
-                        reinterpret_cast<const void*>(&sage3_fp4_flash_kernel<kMxEmu>),
-                        reinterpret_cast<const void*>(&sage3_fp4_flash_kernel<kNvEmu>)};
-  static bool attr[3][64] = {{false}};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr[mode][dev]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(fns[mode], cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM_BYTES));
-    if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "sage3 flash: smem attribute: %s", cudaGetErrorString(e));
-    attr[mode][dev] = true;
+  if (pr.fp8) {  // E4M3 codes: 128-byte rows, 128-byte swizzle
+    if (int st = make_tmap_u8_2d(&mq, w.qc, BH * pr.Lp, 128, 128, 128, 128, 128)) return st;
+    if (int st = make_tmap_u8_2d(&mk, w.kc, BH * pr.Lp, 128, 128, 128, 128, 128)) return st;
+    if (int st = make_tmap_u8_2d(&mv, w.vt, BH * HD, pr.Lp, pr.Lp, 128, 128, 128)) return st;
+  } else {
+    if (int st = make_tmap_u8_2d(&mq, w.qc, BH * pr.Lp, 64, 64, 64, 128, 64)) return st;
+    if (int st = make_tmap_u8_2d(&mk, w.kc, BH * pr.Lp, 64, 64, 64, 128, 64)) return st;
+    if (int st = make_tmap_u8_2d(&mv, w.vt, BH * HD, pr.Lp / 2, pr.Lp / 2, 64, 128, 64)) return st;
   }
   Params p;
   p.H = pr.H;
@@ -601,16 +693,10 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   p.smoothing = pr.smoothing;
   p.p_prescale = pr.emulated ? 2688.0f : 1.0f;
   dim3 grid(static_cast<unsigned>((p.T + 1) / 2), static_cast<unsigned>(BH));
-  if (mode == kMxHw)
-    sage3_fp4_flash_kernel<kMxHw><<<grid, THREADS, SMEM_BYTES, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o, p,
-                                                                   status);
-  else if (mode == kMxEmu)
-    sage3_fp4_flash_kernel<kMxEmu><<<grid, THREADS, SMEM_BYTES, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o, p,
-                                                                    status);
-  else
-    sage3_fp4_flash_kernel<kNvEmu><<<grid, THREADS, SMEM_BYTES, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o, p,
-                                                                    status);
-  return check_launch("sage3 flash");
+  if (pr.fp8) return launch_mode<kMx8Hw>(mq, mk, mv, w, pr, p, grid, status, s);
+  if (pr.nv) return launch_mode<kNvEmu>(mq, mk, mv, w, pr, p, grid, status, s);
+  if (pr.emulated) return launch_mode<kMxEmu>(mq, mk, mv, w, pr, p, grid, status, s);
+  return launch_mode<kMxHw>(mq, mk, mv, w, pr, p, grid, status, s);
 }
 
 }  // namespace attn

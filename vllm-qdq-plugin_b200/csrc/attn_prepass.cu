@@ -15,14 +15,19 @@
 //     e = clamp(ceil(log2(max(amax, 6*2^-126) / 6)), -127, 127), byte e+127
 //     code of x / 2^e with round-half-away thresholds
 //   (ceil(log2(.)) is evaluated exactly from the float's bits).
+//   mxfp8_hw (sage3/api.py:114-160) quantises the same q_s, k_c and V with
+//   quantize_to_mxfp8 (sage3/mxfp8_hw_kernel.py:37-65):
+//     e = ceil(log2(max(amax, 1e-12) / 448)), byte clamp(e + 127, 0, 254),
+//     code = E4M3 of x / 2^e, round-to-nearest-even (torch's float8_e4m3fn cast).
 //
 // Outputs (workspace), with Lp = L rounded up to 128, BH = B*H, G = Lp/128:
 //   ksum   fp32 [BH, D]           per-channel sums of k (mean = bf16(ksum / L))
 //   qmean  bf16 [BH, G, D]        Q group means
-//   qc, kc uint8 [BH*Lp, D/2]     E2M1 codes (element 2j low nibble)
+//   qc, kc uint8 [BH*Lp, D/2]     E2M1 codes (element 2j low nibble), or [BH*Lp, D] E4M3
 //   qsf, ksf                      block scales, 1024 bytes per 128 rows: two 512-byte tcgen05
 //                                 scale chunks (NVFP4: 8 E4M3 per row; MXFP4: 4 E8M0 in the first)
 //   vt     uint8 [BH*D, Lp/2]     V transposed: row (bh, d), keys packed along the row
+//                                 ([BH*D, Lp] for E4M3)
 //   vsf                           1024 bytes per (bh, key tile): 128 d-rows x (4 E8M0 | 8 E4M3)
 //   ds     fp32 [BH, G, Lp]       delta_s, rounded to bf16 (the reference's dtype)
 #include "attn_common.cuh"
@@ -90,6 +95,34 @@ __device__ __forceinline__ uint32_t mx_quant32(const float* v, uint8_t* out) {
   return static_cast<uint32_t>(e + 127);
 }
 
+// E8M0 exponent of quantize_to_mxfp8 for a group whose |x| max is amax:
+// e = ceil(log2(a / 448)) with a = max(amax, 1e-12).  For a = M * 2^E
+// (1 <= M < 2) the fp32 quotient is (M / 1.75) * 2^(E-8), normal for every
+// a >= 1e-12, and has a zero mantissa only when M == 1.75 (M just below 1.75
+// rounds to 1 - 2^-24, not 1), so the ceiling is E - 8 + (M > 1.75).
+__device__ __forceinline__ int mx8_group_exp(float amax) {
+  const uint32_t b = __float_as_uint(fmaxf(amax, 1e-12f));
+  return static_cast<int>(b >> 23) - 135 + ((b & 0x7FFFFFu) > 0x600000u ? 1 : 0);
+}
+
+// Quantise 32 floats (one MXFP8 group): 32 E4M3 bytes into out[0..31]
+// (16-byte aligned), returns the E8M0 byte.  x * 2^-e equals the
+// reference's x / 2^e exactly (a power-of-two scale, both rounded once).
+__device__ __forceinline__ uint32_t mx8_quant32(const float* v, uint8_t* out) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const int e = mx8_group_exp(amax);
+  const float inv = exp2_neg(e);
+  uint32_t w[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    w[q] = cvt_e4m3x4(v[4 * q] * inv, v[4 * q + 1] * inv, v[4 * q + 2] * inv, v[4 * q + 3] * inv);
+  reinterpret_cast<uint4*>(out)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  reinterpret_cast<uint4*>(out)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  return static_cast<uint32_t>(min(max(e + 127, 0), 254));
+}
+
 // Quantise 16 floats (one NVFP4 block of the reference's nvfp4 QuantConfig,
 // sage3/quantize.py:21-81 with round_to_e4m3): scale = e4m3(bf16(amax / 6)
 // clamped below at 1e-8), codes of x / scale with round-half-away thresholds
@@ -136,7 +169,7 @@ __global__ void __launch_bounds__(128) ksum_kernel(const __nv_bfloat16* __restri
 // grid (BH, Lp/128), 256 threads.  Loads one 128-row x 128-d tile, subtracts
 // the mean (Q: the tile's own group mean, written to qmean; K: ksum / L),
 // rounds to bf16 and quantises each row along D into 4 MX groups.
-template <bool kIsQ, bool kNV>
+template <bool kIsQ, bool kNV, bool kF8 = false>
 __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __restrict__ x, int H, int L, int Lp,
                                                        int64_t sb, int64_t sn, int64_t sh,
                                                        const float* __restrict__ ksum, __nv_bfloat16* __restrict__ qmean,
@@ -184,16 +217,18 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
       const int d = g * kGs + i;
       v[i] = (n < L) ? bf16_round(__bfloat162float(tile[r][d]) - mean[d]) : 0.f;  // padding after smoothing
     }
-    uint8_t* crow = codes + (static_cast<int64_t>(bh) * Lp + n) * 64 + g * (kGs / 2);
-    const uint32_t e = kNV ? nv_quant16(v, crow) : mx_quant32(v, crow);
+    uint8_t* crow = kF8 ? codes + (static_cast<int64_t>(bh) * Lp + n) * 128 + g * 32
+                        : codes + (static_cast<int64_t>(bh) * Lp + n) * 64 + g * (kGs / 2);
+    const uint32_t e = kF8 ? mx8_quant32(v, crow) : (kNV ? nv_quant16(v, crow) : mx_quant32(v, crow));
     sft[(g / 4) * 512 + (r % 32) * 16 + (r / 32) * 4 + (g % 4)] = static_cast<uint8_t>(e);
   }
 }
 
 // ---------------------------------------------------------------- V quantisation
 // grid (BH, Lp/128), 128 threads: thread d quantises V[:, d] over the tile's
-// 128 keys in 4 groups of 32 and writes 64 code bytes of row (bh, d) of V^T.
-template <bool kNV>
+// 128 keys in 4 groups of 32 and writes 64 (E2M1) or 128 (E4M3) code bytes of
+// row (bh, d) of V^T.
+template <bool kNV, bool kF8 = false>
 __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __restrict__ v, int H, int L, int Lp,
                                                       int64_t sb, int64_t sn, int64_t sh,
                                                       uint8_t* __restrict__ vt, uint8_t* __restrict__ vsf) {
@@ -209,7 +244,8 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
   }
   __syncthreads();
   const int d = threadIdx.x;
-  uint8_t* row = vt + (static_cast<int64_t>(bh) * 128 + d) * (Lp / 2) + blockIdx.y * 64;
+  uint8_t* row = kF8 ? vt + (static_cast<int64_t>(bh) * 128 + d) * Lp + blockIdx.y * 128
+                     : vt + (static_cast<int64_t>(bh) * 128 + d) * (Lp / 2) + blockIdx.y * 64;
   uint8_t* sft = vsf + (static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 1024 + (d % 32) * 16 + (d / 32) * 4;
   if (kNV) {
     uint32_t sfw[2] = {0, 0};
@@ -229,7 +265,7 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
       float x[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(tile[g * 32 + i][d]);
-      sfw |= mx_quant32(x, row + g * 16) << (8 * g);
+      sfw |= (kF8 ? mx8_quant32(x, row + g * 32) : mx_quant32(x, row + g * 16)) << (8 * g);
     }
     *reinterpret_cast<uint32_t*>(sft) = sfw;
   }
@@ -348,7 +384,14 @@ int launch_prepass(const Problem& p, const Workspace& w, cudaStream_t s) {
   if (p.smoothing) {
     ksum_kernel<<<dim3(BH, (p.L + 1023) / 1024), 128, 0, s>>>(p.k, p.H, p.L, p.k_sb, p.k_sn, p.k_sh, w.ksum);
   }
-  if (p.nv) {
+  if (p.fp8) {
+    qk_quant_kernel<true, false, true><<<dim3(BH, T), 256, 0, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh,
+                                                                 w.ksum, w.qmean, w.qc, w.qsf, p.smoothing);
+    qk_quant_kernel<false, false, true><<<dim3(BH, T), 256, 0, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh,
+                                                                  w.ksum, w.qmean, w.kc, w.ksf, p.smoothing);
+    v_quant_kernel<false, true><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt,
+                                                          w.vsf);
+  } else if (p.nv) {
     qk_quant_kernel<true, true><<<dim3(BH, T), 256, 0, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh, w.ksum,
                                                           w.qmean, w.qc, w.qsf, p.smoothing);
     qk_quant_kernel<false, true><<<dim3(BH, T), 256, 0, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh, w.ksum,

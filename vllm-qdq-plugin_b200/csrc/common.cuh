@@ -109,6 +109,20 @@ __device__ __forceinline__ float round_e4m3(float v) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
 }
 
+// Four fp32 -> four E4M3 bytes, v0 in the low byte (RNE, saturating to
+// +-448).  cvt's first source goes to the high byte of each pair.
+__device__ __forceinline__ uint32_t cvt_e4m3x4(float v0, float v1, float v2, float v3) {
+  uint32_t r;
+  asm(
+      "{\n\t.reg .b16 lo, hi;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n\t"
+      "mov.b32 %0, {lo, hi};\n\t}"
+      : "=r"(r)
+      : "f"(v0), "f"(v1), "f"(v2), "f"(v3));
+  return r;
+}
+
 // RNE fp32 -> E4M3 byte (saturating).
 __device__ __forceinline__ uint32_t e4m3_byte(float v) {
   uint32_t out;

@@ -167,6 +167,11 @@ __host__ __device__ constexpr uint32_t idesc_mxf4(uint32_t M, uint32_t N, bool e
          | ((e8m0 ? 1u : 0u) << 23)   // scale format
          | ((M >> 4) << 24);          // M
 }
+// Instruction descriptor of kind::mxf8f6f4 with E4M3 A and B (format code 0),
+// UE8M0 scales per 32 (bit 23), K = 32 per MMA, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_mxf8(uint32_t M, uint32_t N) {
+  return ((N >> 3) << 17) | (1u << 23) | ((M >> 4) << 24);
+}
 __device__ __forceinline__ uint32_t idesc_with_sf_ids(uint32_t idesc, uint32_t sfa_id, uint32_t sfb_id) {
   return idesc | (sfb_id << 4) | (sfa_id << 29);
 }
@@ -179,6 +184,19 @@ __device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t a_desc, uint6
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+// D(tmem) (+)= A(smem) x B(smem)^T, E4M3 operands with per-32 E8M0 scales
+// from TMEM (kind::mxf8f6f4, K = 32).
+__device__ __forceinline__ void mma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
           d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
       : "memory");

@@ -1,5 +1,5 @@
 # SPDX-License-Identifier: Apache-2.0
-"""Entry points of the sm_100a Sage3 FP4 attention.
+"""Entry points of the sm_100a Sage3 FP4 / FP8 attention.
 
 Mirrors the reference's sage3/api.py surface:
   sageattn3_standalone(q, k, v, config, is_causal, sm_scale, per_block_mean, ...)
@@ -22,6 +22,9 @@ Config mapping:
               emulation grid has no hardware equivalent, so parity with it is
               by tolerance.
   "nvfp4"     NVFP4 (E4M3 per 16).
+  "mxfp8_hw"  MXFP8 (E4M3 + E8M0 per 32) Q/K/V and P with the reference
+              hardware kernel's semantics (sage3/mxfp8_hw_kernel.py,
+              quantize_to_mxfp8), on kind::mxf8f6f4 tensor-core MMAs.
 The kernels read the NHD or HND strides they are given; no transposing copies.
 """
 
@@ -50,14 +53,15 @@ ACC_DTYPE_MAP = {
 }
 
 # config name -> kernel variant of sage3_fp4_attn (include/qdq_b200.h):
-#   0 mxfp4_hw (MXFP4, hardware-kernel P handling), 1 nvfp4, 2 mxfp4 (emulated-config P handling)
-ATTENTION_CONFIGS: dict[str, int] = {"mxfp4": 2, "mxfp4_hw": 0, "nvfp4": 1}
+#   0 mxfp4_hw (MXFP4, hardware-kernel P handling), 1 nvfp4, 2 mxfp4 (emulated-config P handling),
+#   3 mxfp8_hw (MXFP8, hardware-kernel P handling)
+ATTENTION_CONFIGS: dict[str, int] = {"mxfp4": 2, "mxfp4_hw": 0, "nvfp4": 1, "mxfp8_hw": 3}
 
-# Names the reference registers that lie outside this build's FP4 path.
-_OTHER_REFERENCE_CONFIGS = ("mxfp4_s1", "mxfp8_s1", "nvfp4_vsmooth", "mxfp4_vsmooth", "mxfp8_hw",
+# Names the reference registers that lie outside this build's attention kernels.
+_OTHER_REFERENCE_CONFIGS = ("mxfp4_s1", "mxfp8_s1", "nvfp4_vsmooth", "mxfp4_vsmooth",
                             "mixed_mxfp8qk_mxfp4pv_hw", "mixed_mxfp4qk_mxfp8pv_hw", "int8", "fp8")
 
-_BUILT_FORMATS = (0, 1, 2)  # variants with a kernel in this build
+_BUILT_FORMATS = (0, 1, 2, 3)  # variants with a kernel in this build
 
 
 def _get_env_bool(name: str, default: str = "0") -> bool:
