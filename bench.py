@@ -680,7 +680,8 @@ def run_gemm(args, wl, world, rank, dev, dist) -> None:
             "roofline": {"bound": "tensor", "achieved": round(flop / (ms_step * 1e-3) / 1e12, 1),
                          "peak": peak, "unit": "TFLOP/s",
                          "frac": round(flop / (ms_step * 1e-3) / 1e12 / peak, 4),
-                         "peak_source": src, "traffic": ncu_traffic("mxfp4_linear")},
+                         "peak_source": src,
+                         "traffic": ncu_traffic("mxfp4_linear" if m == 4096 else f"mxfp4_linear_{m}")},
             "clocks": sampler.summary(t_wall0, t_wall1) if sampler else None,
         }
         if world == 1 and not args.no_cpu_baseline:
