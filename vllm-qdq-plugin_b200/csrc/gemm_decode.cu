@@ -11,16 +11,19 @@
 // streams that slice of W once (N / 128 CTAs: 112 for N = 14336), so the
 // kernel is bound by HBM reading W, not by the tensor pipe.
 //
-// CTA, 6 warps:
+// CTA, 10 warps:
 //   warp 0 / one lane   TMA producer: W code tile [128 rows x 128 B] (128-byte
 //                       swizzle), its scale chunks and the raw [NA, 256]
 //                       bf16/fp16 slice of A into a ring of 3-7 stages
 //   warp 1 / one lane   MMA issuer: per stage 4 x tcgen05.mma.kind::mxf4
 //                       (M = 128, N = NA, K = 64), commit frees the stage
-//   warps 2-5           activation quantiser (the stage's raw A slice in
-//                       shared memory -> E2M1 codes in the swizzled operand
-//                       layout + E8M0 scales in the scale-chunk layout), then
-//                       the epilogue (TMEM lanes = W rows, columns = activation rows)
+//   warps 2-9           activation quantiser in 1, 2 or 4 teams (decode_teams),
+//                       team t taking the stages of ring slots s = t (mod
+//                       teams), so several stages are quantised at once (each
+//                       slot's barrier phases are observed in order by one team) (the stage's raw A slice in shared
+//                       memory -> E2M1 codes in the swizzled operand layout +
+//                       E8M0 scales in the scale-chunk layout); then the
+//                       epilogue (TMEM lanes = W rows, columns = activation rows)
 #include "mx_quant.cuh"
 #include "sm100.cuh"
 
@@ -35,7 +38,12 @@ constexpr int DBKB = DBK / 2;            // code bytes per row per stage (one 12
 constexpr int NA_MAX = 64;               // activation rows per launch (UMMA N)
 constexpr int W_TILE = DBM * DBKB;       // 16 KB
 constexpr int SF_STAGE = 1024;           // two 512-byte scale chunks (8 scales per row)
-constexpr int D_THREADS = 192;
+constexpr int D_QUANT_THREADS = 256;                 // 8 quantiser / epilogue warps
+constexpr int D_THREADS = 64 + D_QUANT_THREADS;      // + producer and MMA warps
+// Quantiser teams (one stage each in flight) for M activation rows: few rows
+// make a stage's quantisation latency-bound, so more stages run at once;
+// many rows make it throughput-bound, so more threads share one stage.
+__host__ __device__ constexpr int decode_teams(int M) { return M <= 16 ? 4 : (M <= 32 ? 2 : 1); }
 constexpr int D_TMEM_COLS = 128;
 constexpr uint32_t T_ACC = 0, T_SFW = 64, T_SFA = 72;
 
@@ -52,11 +60,12 @@ struct DLayout {
 
 struct __align__(8) DBars {
   uint64_t raw[8];     // W, its scales and the raw A slice landed (1 arrival + tx)
-  uint64_t ready[8];   // the activation slice is quantised (128 arrivals)
+  uint64_t ready[8];   // the activation slice is quantised (one team's arrivals)
   uint64_t empty[8];   // the stage's MMAs completed
   uint64_t acc_full;
   uint32_t tmem_base;
   int abort;
+  int preissued;       // stages whose loads thread 0 issued before the CTA-wide sync
 };
 template <int kNA>
 constexpr size_t d_smem_bytes() {
@@ -97,17 +106,20 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
   const int n_blk = blockIdx.x;
   const int num_kt = (K + DBK - 1) / DBK;
 
-  // Activation rows >= M and their scales stay zero for the whole launch.
-  constexpr int kZero = (Lay::A_TILE + 2 * SF_STAGE) / 16;  // A codes + both scale chunks
-  for (int i = threadIdx.x; i < S * kZero; i += D_THREADS) {
-    const int s = i / kZero, o = (i % kZero) * 16;
-    if (o < Lay::A_TILE || o >= Lay::A_TILE + SF_STAGE)  // skip the W scales (loaded every stage)
-      *reinterpret_cast<uint4*>(smem + s * Lay::STAGE + Lay::ST_A + o) = make_uint4(0, 0, 0, 0);
-  }
+  // One stage's loads: the W tile, its scales and the raw A slice.
+  auto issue_stage = [&](int kt) {
+    const int s = kt % S;
+    uint8_t* st = smem + s * Lay::STAGE;
+    mbar_arrive_expect_tx(&bars->raw[s], W_TILE + SF_STAGE + Lay::RAW);
+    tma_load_2d(st + Lay::ST_W, &tmap_w, kt * DBKB, n_blk * DBM, &bars->raw[s]);
+    bulk_load(st + Lay::ST_SFW, sfw + (static_cast<int64_t>(n_blk) * kchunks + 2 * kt) * 512, SF_STAGE,
+              &bars->raw[s]);
+    tma_load_2d(st + Lay::ST_RAW, &tmap_a, kt * DBK, 0, &bars->raw[s]);
+  };
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&bars->raw[s], 1);
-      mbar_init(&bars->ready[s], 128);
+      mbar_init(&bars->ready[s], D_QUANT_THREADS / decode_teams(M));
       mbar_init(&bars->empty[s], 1);
     }
     mbar_init(&bars->acc_full, 1);
@@ -115,6 +127,19 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
     fence_barrier_init();
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_a);
+    // The first ring of loads needs neither TMEM nor the cleared tiles, so it
+    // starts before them: the HBM latency overlaps the rest of the prologue.
+    const int pre = min(S, num_kt);
+    for (int kt = 0; kt < pre; ++kt) issue_stage(kt);
+    bars->preissued = pre;
+  }
+  // Activation rows >= M and their scales stay zero for the whole launch
+  // (disjoint from the W, W-scale and raw-A bytes the loads above write).
+  constexpr int kZero = (Lay::A_TILE + 2 * SF_STAGE) / 16;  // A codes + both scale chunks
+  for (int i = threadIdx.x; i < S * kZero; i += D_THREADS) {
+    const int s = i / kZero, o = (i % kZero) * 16;
+    if (o < Lay::A_TILE || o >= Lay::A_TILE + SF_STAGE)  // skip the W scales (loaded every stage)
+      *reinterpret_cast<uint4*>(smem + s * Lay::STAGE + Lay::ST_A + o) = make_uint4(0, 0, 0, 0);
   }
   if (warp == 0) {
     tmem_alloc(&bars->tmem_base, D_TMEM_COLS);
@@ -129,20 +154,15 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
   if (warp == 0) {
     // ---------------- producer: W, its scales, raw A
     if (elect_one()) {
-      int issued = 0;
-      for (int kt = 0; kt < num_kt; ++kt) {
+      int issued = bars->preissued;
+      for (int kt = issued; kt < num_kt; ++kt) {
         const int s = kt % S;
         if (!mbar_wait(&bars->empty[s], ((kt / S) & 1) ^ 1, status, 0x401)) {
           bars->abort = 1;
           break;
         }
         if (*(volatile int*)&bars->abort) break;
-        uint8_t* st = smem + s * Lay::STAGE;
-        mbar_arrive_expect_tx(&bars->raw[s], W_TILE + SF_STAGE + Lay::RAW);
-        tma_load_2d(st + Lay::ST_W, &tmap_w, kt * DBKB, n_blk * DBM, &bars->raw[s]);
-        bulk_load(st + Lay::ST_SFW, sfw + (static_cast<int64_t>(n_blk) * kchunks + 2 * kt) * 512, SF_STAGE,
-                  &bars->raw[s]);
-        tma_load_2d(st + Lay::ST_RAW, &tmap_a, kt * DBK, 0, &bars->raw[s]);
+        issue_stage(kt);
         ++issued;
       }
       for (int kt = (issued > S ? issued - S : 0); kt < issued; ++kt)
@@ -178,16 +198,22 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
       tc_commit(&bars->acc_full);  // also on abort: the epilogue waits for the issued MMAs
     }
   } else {
-    // ---------------- activation quantiser (128 threads), then epilogue
-    const int tq = threadIdx.x - 64;
+    // ---------------- activation quantiser (teams), then epilogue
+    const int teams = decode_teams(M);
+    const int team_threads = D_QUANT_THREADS / teams;
+    const int team = (threadIdx.x - 64) / team_threads;
+    const int tq = (threadIdx.x - 64) % team_threads;
     const int lane = threadIdx.x & 31;
     bool ok = true;
     for (int kt = 0; kt < num_kt; ++kt) {
       const int s = kt % S;
+      // A parity wait can only tell the current phase from the previous one,
+      // so every stage of a slot goes to the same team, in order.
+      if (s % teams != team) continue;
       if (ok) ok = mbar_wait(&bars->raw[s], (kt / S) & 1, status, 0x404);
       uint8_t* st = smem + s * Lay::STAGE;
       // groups (row m, 32-block g) of this stage's [M, 256] slice; columns past K read as zero
-      for (int it = tq; it < M * (DBK / 32); it += 128) {
+      for (int it = tq; it < M * (DBK / 32); it += team_threads) {
         const int m = it >> 3, g = it & 7;
         const uint4* src = reinterpret_cast<const uint4*>(st + Lay::ST_RAW + m * (DBK * 2) + g * 64);
         uint4 v[4] = {src[0], src[1], src[2], src[3]};
@@ -202,27 +228,28 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
       fence_proxy_async_smem();
       mbar_arrive(&bars->ready[s]);
     }
-    // epilogue: warp w reads TMEM lanes 32 (w % 4).. (W rows), columns = activation rows
+    // epilogue: warp w reads TMEM lanes 32 (w % 4).. (W rows); warps 2-5 take
+    // the activation-row columns [0, 32), warps 6-9 [32, 64)
     if (ok) ok = mbar_wait(&bars->acc_full, 0, status, 0x405);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     const int q = warp & 3;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + T_ACC;
     constexpr int NC = kNA > 32 ? 2 : 1;
-    uint32_t r[NC][32];
-#pragma unroll
-    for (int h = 0; h < NC; ++h) tmem_ld32(taddr + 32 * h, r[h]);
-    tmem_ld_wait();
-    const int n = n_blk * DBM + q * 32 + lane;
-    if (ok && !*(volatile int*)&bars->abort && n < N) {
-      const float b = bias != nullptr ? O::load(bias + n) : 0.f;
-#pragma unroll
-      for (int h = 0; h < NC; ++h)
+    const int half = (warp - 2) >> 2;
+    if (half < NC && 32 * half < M) {
+      uint32_t r[32];
+      tmem_ld32(taddr + 32 * half, r);
+      tmem_ld_wait();
+      const int n = n_blk * DBM + q * 32 + lane;
+      if (ok && !*(volatile int*)&bars->abort && n < N) {
+        const float b = bias != nullptr ? O::load(bias + n) : 0.f;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int m = 32 * h + i;
-          if (m < M) C[static_cast<int64_t>(m) * ldc + n] = O::one(__uint_as_float(r[h][i]) + b);
+          const int m = 32 * half + i;
+          if (m < M) C[static_cast<int64_t>(m) * ldc + n] = O::one(__uint_as_float(r[i]) + b);
         }
+      }
     }
   }
 
