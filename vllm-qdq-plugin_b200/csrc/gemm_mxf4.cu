@@ -263,6 +263,222 @@ mxf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs computes 256 x 256 tiles with
+// tcgen05.mma.cta_group::2 (M = 256: CTA r holds A rows [128 r, 128 r + 128)
+// and W rows [128 r, 128 r + 128) of the tile, and its TMEM the accumulator
+// of its 128 rows over all 256 columns).  Per SM and K stage this streams
+// 32 KB of codes instead of 48 KB, so the ring holds 6 stages.
+//   rank 0 and 1, warp 0   TMA producer of the CTA's own halves and scale
+//                          chunks (W scales for all 256 columns, which each
+//                          CTA's MMA half reads), completing on the leader's
+//                          full barrier
+//   rank 0, warp 1         MMA issuer for the pair; commits arrive on both
+//                          CTAs' barriers
+//   warps 2-9              epilogue of the CTA's 128 rows
+// Scale chunks arrive by TMA (2-D maps of 512-byte rows) so that they, too,
+// complete on the leader's barrier.
+// ---------------------------------------------------------------------------
+constexpr int P_STAGES = 6;
+constexpr int P_A = 128 * BKB;      // 16 KB: the CTA's 128 A rows
+constexpr int P_B = 128 * BKB;      // 16 KB: the CTA's 128 W rows
+constexpr int P_SFA = 2 * 512;      // the CTA's 128 rows x 8 scales
+constexpr int P_SFB = 4 * 512;      // all 256 W rows x 8 scales
+constexpr int P_STAGE = P_A + P_B + P_SFA + P_SFB;  // 35 KB
+constexpr int P_TX = 2 * P_STAGE;   // bytes both CTAs land on the leader's barrier per stage
+constexpr uint32_t P_IDESC = idesc_mxf4(256, BN, true);
+
+struct __align__(8) PairBars {
+  uint64_t full[P_STAGES];   // leader: both CTAs' stage bytes landed
+  uint64_t empty[P_STAGES];  // each CTA: the pair's MMAs on the stage completed
+  uint64_t acc_full;         // each CTA: its accumulator half is complete
+  uint64_t acc_empty;        // leader: both CTAs' epilogues read their halves (512 arrivals)
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr size_t P_SMEM_BYTES = 1024 + P_STAGES * P_STAGE + sizeof(PairBars);
+static_assert(P_SMEM_BYTES <= 227 * 1024, "pair GEMM shared memory");
+
+template <bool kF16>
+__global__ void __launch_bounds__(THREADS, 1)
+mxf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                      const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
+                      const void* __restrict__ bias_v, void* __restrict__ C_v, int M, int N, int K, int64_t ldc,
+                      int kchunks, int* status) {
+  using O = OutT<kF16>;
+  using T = typename O::T;
+  const T* bias = static_cast<const T*>(bias_v);
+  T* C = static_cast<T*>(C_v);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  PairBars* bars = reinterpret_cast<PairBars*>(smem + P_STAGES * P_STAGE);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+  const int num_m = (M + 255) / 256;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kt = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, 2 * 32 * EPI_WARPS);
+    mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+    prefetch_tmap(&tmap_sfa);
+    prefetch_tmap(&tmap_sfb);
+  }
+  if (warp == 0) {
+    tmem_alloc_pair(&bars->tmem_base, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers are initialised and the TMEM is allocated
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    // ---------------- producer (both CTAs): own halves, landing on the leader's barrier
+    if (elect_one()) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < num_tiles; tile += num_pairs) {
+        const int m_blk = tile % num_m, n_blk = tile / num_m;
+        const int a_row = m_blk * 256 + static_cast<int>(rank) * 128;
+        const int b_row = n_blk * BN + static_cast<int>(rank) * 128;
+        for (int kt = 0; kt < num_kt; ++kt, ++it) {
+          const int s = it % P_STAGES;
+          if (!mbar_wait(&bars->empty[s], ((it / P_STAGES) & 1) ^ 1, status, 0x111)) {
+            bars->abort = 1;
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * P_STAGE;
+          const uint32_t full0 = cluster_addr(&bars->full[s], 0);
+          if (rank == 0) mbar_arrive_expect_tx(&bars->full[s], P_TX);
+          tma_load_2d_pair(st, &tmap_a, kt * BKB, a_row, full0);
+          tma_load_2d_pair(st + P_A, &tmap_b, kt * BKB, b_row, full0);
+          tma_load_2d_pair(st + P_A + P_B, &tmap_sfa, 0, (m_blk * 2 + static_cast<int>(rank)) * kchunks + 2 * kt,
+                           full0);
+          tma_load_2d_pair(st + P_A + P_B + P_SFA, &tmap_sfb, 0, (n_blk * 2) * kchunks + 2 * kt, full0);
+          tma_load_2d_pair(st + P_A + P_B + P_SFA + 1024, &tmap_sfb, 0, (n_blk * 2 + 1) * kchunks + 2 * kt, full0);
+        }
+      }
+      // The leader's MMA waits on every stage either CTA issued; its final
+      // full waits (below) cover the pair's copies still in flight.
+      if (rank == 0)
+        for (int j = (it > P_STAGES ? it - P_STAGES : 0); j < it; ++j)
+          mbar_wait(&bars->full[j % P_STAGES], (j / P_STAGES) & 1, status, 0x112);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader)
+    if (rank == 0 && elect_one()) {
+      int it = 0, i = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < num_tiles; tile += num_pairs, ++i) {
+        // both CTAs' epilogues have read the previous tile's accumulator
+        if (i > 0 && !mbar_wait(&bars->acc_empty, (i - 1) & 1, status, 0x212)) { ok = false; break; }
+        tc_fence_after();
+        for (int kt = 0; kt < num_kt; ++kt, ++it) {
+          const int s = it % P_STAGES;
+          if (!mbar_wait(&bars->full[s], (it / P_STAGES) & 1, status, 0x211)) { ok = false; break; }
+          tc_fence_after();
+          uint8_t* st = smem + s * P_STAGE;
+          const uint8_t* sa = st + P_A + P_B;
+          const uint8_t* sb = sa + P_SFA;
+          tmem_cp_sf_pair(tmem + SFA_COL + 0, smem_desc_sf(sa));
+          tmem_cp_sf_pair(tmem + SFA_COL + 4, smem_desc_sf(sa + 512));
+          tmem_cp_sf_pair(tmem + SFB_COL + 0, smem_desc_sf(sb));          // W rows 0-127,   j = 0
+          tmem_cp_sf_pair(tmem + SFB_COL + 8, smem_desc_sf(sb + 512));    // W rows 0-127,   j = 1
+          tmem_cp_sf_pair(tmem + SFB_COL + 4, smem_desc_sf(sb + 1024));   // W rows 128-255, j = 0
+          tmem_cp_sf_pair(tmem + SFB_COL + 12, smem_desc_sf(sb + 1536));  // W rows 128-255, j = 1
+          const uint64_t da = smem_desc_sw128(st);
+          const uint64_t db = smem_desc_sw128(st + P_A);
+#pragma unroll
+          for (int kk = 0; kk < BK / 64; ++kk) {
+            const uint32_t j = kk >> 1, sf_id = (kk & 1) * 2;
+            mma_mxf4_pair(tmem + ACC_COL, da + ((kk * 32) >> 4), db + ((kk * 32) >> 4),
+                          idesc_with_sf_ids(P_IDESC, sf_id, sf_id), (tmem + SFA_COL + 4 * j) | (sf_id << 30),
+                          (tmem + SFB_COL + 8 * j) | (sf_id << 30), (kt | kk) != 0);
+          }
+          tc_commit_pair(&bars->empty[s]);
+        }
+        if (!ok) break;
+        tc_commit_pair(&bars->acc_full);
+      }
+      if (!ok) bars->abort = 1;
+      tc_commit_pair_local(&bars->drain);  // tracks the pair's tcgen05 ops
+      mbar_wait(&bars->drain, 0, status, 0x213);
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): TMEM lanes = the CTA's 128 tile rows
+    const int q = warp & 3, h = (warp - 2) >> 2;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ACC_COL + h * 128;
+    const uint32_t acc_empty0 = cluster_addr(&bars->acc_empty, 0);
+    bool ok = true;
+    int i = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++i) {
+      const int m_blk = tile % num_m, n_blk = tile / num_m;
+      if (ok) ok = mbar_wait(&bars->acc_full, i & 1, status, 0x311);
+      ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
+      tc_fence_after();
+      uint32_t r[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(taddr + 32 * c, r[c]);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive_cluster(acc_empty0);  // the pair's next MMAs may overwrite the accumulator
+      if (!ok || *(volatile int*)&bars->abort) continue;
+      const int row = m_blk * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+      if (row >= M) continue;
+      const int n0 = n_blk * BN + h * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int ncols = min(32, N - n0 - 32 * c);
+        if (ncols <= 0) continue;
+        T* crow = C + static_cast<int64_t>(row) * ldc + n0 + 32 * c;
+        float v[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[c][e]);
+        if (bias != nullptr) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (e < ncols) v[e] += O::load(bias + n0 + 32 * c + e);
+        }
+        if (ncols == 32 && (reinterpret_cast<uintptr_t>(crow) & 15) == 0) {
+          uint4* dst = reinterpret_cast<uint4*>(crow);
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4)
+            dst[w4] = make_uint4(O::pack(v[8 * w4 + 0], v[8 * w4 + 1]), O::pack(v[8 * w4 + 2], v[8 * w4 + 3]),
+                                 O::pack(v[8 * w4 + 4], v[8 * w4 + 5]), O::pack(v[8 * w4 + 6], v[8 * w4 + 7]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (e < ncols) crow[e] = O::one(v[e]);
+        }
+      }
+    }
+  }
+
+  // Neither CTA releases the pair's TMEM or exits while the other may still
+  // arrive on its barriers or read its shared memory.
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, TMEM_COLS);
+  }
+}
+
 // Row-major E8M0/E4M3 scales [rows, ks] (row stride ld) -> tiled layout
 // (rows padded to 128, ks padded to a multiple of 8, pad bytes = pad_value).
 __global__ void sf_tile_kernel(const uint8_t* __restrict__ sf, uint8_t* __restrict__ out, int rows, int ks,
@@ -339,6 +555,23 @@ int make_tmap_u16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
   return QDQ_OK;
 }
 
+int make_tmap_u32_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld_bytes,
+                     uint32_t box_cols, uint32_t box_rows) {
+  PFN_encodeTiled fn = encode_fn();
+  if (fn == nullptr) return fail(QDQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld_bytes & 15))
+    return fail(QDQ_ERR_ALIGNMENT, "TMA operand needs 16-byte aligned base and row stride");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld_bytes};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(QDQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return QDQ_OK;
+}
+
 }  // namespace qdqb200
 
 using namespace qdqb200;
@@ -388,6 +621,51 @@ extern "C" int fp4_gemm_mxf4(const void* a_codes, const void* a_sf_tiled, const 
     return fail(QDQ_ERR_ALIGNMENT, "fp4_gemm_mxf4: scale-factor buffers must be 16-byte aligned");
   int* status = device_status_ptr();
   if (status == nullptr) return QDQ_ERR_CUDA;
+  const int kchunks = static_cast<int>(((K / 32) + 7) / 8 * 8 / 4);
+  const int sms = device_sm_count();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Two or more 128-row blocks of A: CTA pairs on 256 x 256 tiles.
+  if (M > BM && sms >= 2) {
+    CUtensorMap ta, tb, tsa, tsb;
+    if (int st = make_tmap_u8_2d(&ta, a_codes, M, K / 2, lda_bytes, BKB, 128, 128)) return st;
+    if (int st = make_tmap_u8_2d(&tb, w_codes, N, K / 2, ldw_bytes, BKB, 128, 128)) return st;
+    if (int st = make_tmap_u32_2d(&tsa, a_sf_tiled, (M + 127) / 128 * kchunks, 128, 512, 128, 2)) return st;
+    if (int st = make_tmap_u32_2d(&tsb, w_sf_tiled, (N + 127) / 128 * kchunks, 128, 512, 128, 2)) return st;
+    static bool pair_attr[2][64] = {{false}};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const void* pfn = out_dtype == QDQ_DTYPE_FP16 ? reinterpret_cast<const void*>(&mxf4_gemm_pair_kernel<true>)
+                                                  : reinterpret_cast<const void*>(&mxf4_gemm_pair_kernel<false>);
+    if (dev >= 0 && dev < 64 && !pair_attr[out_dtype][dev]) {
+      cudaError_t e = cudaFuncSetAttribute(pfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(P_SMEM_BYTES));
+      if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_gemm_mxf4: smem attribute: %s", cudaGetErrorString(e));
+      pair_attr[out_dtype][dev] = true;
+    }
+    const int64_t tiles = ((M + 255) / 256) * ((N + BN - 1) / BN);
+    const int64_t pairs = std::min<int64_t>(tiles, sms / 2);
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const int m_ = static_cast<int>(M), n_ = static_cast<int>(N), k_ = static_cast<int>(K);
+    cudaError_t e = out_dtype == QDQ_DTYPE_FP16
+                        ? cudaLaunchKernelEx(&cfg, mxf4_gemm_pair_kernel<true>, ta, tb, tsa, tsb, bias, c, m_, n_, k_,
+                                             ldc, kchunks, status)
+                        : cudaLaunchKernelEx(&cfg, mxf4_gemm_pair_kernel<false>, ta, tb, tsa, tsb, bias, c, m_, n_,
+                                             k_, ldc, kchunks, status);
+    if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_gemm_mxf4: pair launch: %s", cudaGetErrorString(e));
+    return check_launch("fp4_gemm_mxf4");
+  }
   CUtensorMap ta, tb;
   if (int st = make_tmap_u8_2d(&ta, a_codes, M, K / 2, lda_bytes, BKB, BM, 128)) return st;
   if (int st = make_tmap_u8_2d(&tb, w_codes, N, K / 2, ldw_bytes, BKB, BN, 128)) return st;
@@ -402,11 +680,8 @@ extern "C" int fp4_gemm_mxf4(const void* a_codes, const void* a_sf_tiled, const 
     if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_gemm_mxf4: smem attribute: %s", cudaGetErrorString(e));
     attr_set[out_dtype][dev] = true;
   }
-  const int kchunks = static_cast<int>(((K / 32) + 7) / 8 * 8 / 4);
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int sms = device_sm_count();
   dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, sms > 0 ? sms : 148)));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto* sfa = static_cast<const uint8_t*>(a_sf_tiled);
   auto* sfb = static_cast<const uint8_t*>(w_sf_tiled);
   if (out_dtype == QDQ_DTYPE_FP16)
