@@ -591,7 +591,9 @@ def run_gemm(args, wl, world, rank, dev, dist) -> None:
     out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev)
     launches = [0]
-    per_call = 1 if m <= 64 else 3  # one fused launch for M <= 64, else quantise + scale tiling + GEMM
+    # one fused launch for M <= 64; else quantise (scales written in the GEMM's tiled
+    # layout when K % 256 == 0, otherwise + a scale-tiling launch) and the GEMM
+    per_call = 1 if m <= 64 else (2 if k % 256 == 0 else 3)
 
     def step(i=0, sp=None):
         wi = ws_list[i % n_w]

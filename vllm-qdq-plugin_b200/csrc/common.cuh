@@ -27,6 +27,9 @@ int check_launch(const char* what);
 int device_sm_count();  // SM count of the current device (cached)
 // Fused small-M MXFP4 linear (gemm_decode.cu): activation quantisation inside
 // the GEMM producer, one launch; M in [1, 64], 16-byte aligned activation rows.
+// MXFP4 codes + E8M0 scales in the GEMM's tiled layout in one pass (K % 256 == 0).
+int qdq_mxfp4_codes_tiled(const void* x, void* codes, void* sf_tiled, int64_t M, int64_t K, int64_t ldx,
+                          int dtype, void* stream);
 int fp4_linear_decode(const void* a, int64_t lda, int dtype, const void* w_codes, const void* w_sf_tiled,
                       const void* bias, void* c, int64_t M, int64_t N, int64_t K, int64_t ldw_bytes,
                       int64_t ldc, void* stream);

@@ -726,8 +726,14 @@ extern "C" int fp4_linear_mxf4(const void* a, int64_t lda, int dtype, const void
   uint8_t* a_codes = ws;
   uint8_t* a_sf = a_codes + up(M * K / 2);
   uint8_t* a_sf_t = a_sf + up(M * K / 32);
-  if (int st = qdq_mxfp4(a, nullptr, a_codes, a_sf, M, K, lda, K, dtype, 32, stream)) return st;
-  if (int st = qdq_sf_tile(a_sf, a_sf_t, M, K, K / 32, 32, stream)) return st;
+  if (K % 256 == 0 && (dtype == QDQ_DTYPE_BF16 || dtype == QDQ_DTYPE_FP16) &&
+      (reinterpret_cast<uintptr_t>(a) & 15) == 0 && lda % 8 == 0) {
+    // one pass: codes and tiled scales (no padded K chunk to clear)
+    if (int st = qdq_mxfp4_codes_tiled(a, a_codes, a_sf_t, M, K, lda, dtype, stream)) return st;
+  } else {
+    if (int st = qdq_mxfp4(a, nullptr, a_codes, a_sf, M, K, lda, K, dtype, 32, stream)) return st;
+    if (int st = qdq_sf_tile(a_sf, a_sf_t, M, K, K / 32, 32, stream)) return st;
+  }
   return fp4_gemm_mxf4(a_codes, a_sf_t, w_codes, w_sf_tiled, bias, c, M, N, K, K / 2, ldw_bytes, ldc, dtype,
                        stream);
 }

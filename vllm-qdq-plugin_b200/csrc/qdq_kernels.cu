@@ -26,7 +26,9 @@ constexpr float kRecip6 = 1.0f / 6.0f;  // fp32 value of vLLM's FLOAT4_E2M1_MAX_
 // ---------------------------------------------------------------------------
 // MXFP4: vectorised kernel (K % 32 == 0, 16-byte aligned rows)
 // ---------------------------------------------------------------------------
-template <int kDtype, bool kContig, bool kY, bool kCodes, bool kScales>
+// kTiledSF: the E8M0 bytes go straight to the block-scaled GEMM's tiled
+// scale layout (qdq_sf_tile; `lds` then holds its K-chunk count).
+template <int kDtype, bool kContig, bool kY, bool kCodes, bool kScales, bool kTiledSF = false>
 __global__ void __launch_bounds__(kThreads)
 mxfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
                  uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
@@ -56,6 +58,12 @@ mxfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
         yo[u] = row * static_cast<uint64_t>(ldy) + col * 8u;
         co[u] = row * static_cast<uint64_t>(ldc) + col * 4u;
         so[u] = row * static_cast<uint64_t>(lds) + (col >> 2);
+      }
+      if (kTiledSF) {
+        const uint32_t row = static_cast<uint32_t>(c / cpr);
+        const uint32_t gi = static_cast<uint32_t>(c - static_cast<uint64_t>(row) * cpr) >> 2;
+        so[u] = (static_cast<uint64_t>(row >> 7) * static_cast<uint64_t>(lds) + (gi >> 2)) * 512u +
+                (row & 31u) * 16u + ((row >> 5) & 3u) * 4u + (gi & 3u);
       }
       v[u] = ok[u] ? ld_stream(reinterpret_cast<const uint4*>(x + xo[u])) : make_uint4(0, 0, 0, 0);
     }
@@ -621,6 +629,42 @@ extern "C" int qdq_mxfp4(const void* x, void* y, void* codes, void* scales, int6
   }
   return check_launch("qdq_mxfp4");
 }
+
+namespace qdqb200 {
+// MXFP4 codes [M, K/2] (row stride K/2) and E8M0 scales written directly in
+// the GEMM's tiled layout (qdq_sf_tile), one pass.  K % 256 == 0 (no padded
+// K chunk), 16-byte aligned rows; scale bytes of pad rows (>= M) are left as
+// they are: the GEMM multiplies them only with the zero codes TMA fills in.
+int qdq_mxfp4_codes_tiled(const void* x, void* codes, void* sf_tiled, int64_t M, int64_t K, int64_t ldx,
+                          int dtype, void* stream) {
+  if (M <= 0 || K <= 0) return QDQ_OK;
+  if (K % 256 != 0 || !aligned16(x) || ldx % 8 != 0 || !aligned4(codes))
+    return fail(QDQ_ERR_UNSUPPORTED, "qdq_mxfp4_codes_tiled: K %% 256 and 16-byte aligned rows required");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint64_t cpr = static_cast<uint64_t>(K / 8);
+  const uint64_t total = static_cast<uint64_t>(M) * cpr;
+  if (total >= (1ull << 32) && ldx != K)
+    return fail(QDQ_ERR_UNSUPPORTED, "qdq_mxfp4_codes_tiled: too many elements for a strided input");
+  const int64_t kchunks = K / 128;
+  const int grid = grid_for(total, kThreads * kUnroll);
+  auto* xp = static_cast<const uint16_t*>(x);
+  auto* cp = static_cast<uint8_t*>(codes);
+  auto* sp = static_cast<uint8_t*>(sf_tiled);
+  const bool contig = ldx == K;
+#define QDQ_TILED(DT, CONTIG)                                                                        \
+  mxfp4_vec_kernel<DT, CONTIG, false, true, true, true><<<grid, kThreads, 0, s>>>(                   \
+      xp, nullptr, cp, sp, static_cast<uint32_t>(cpr), total, ldx, K, K / 2, kchunks)
+  if (dtype == QDQ_DTYPE_BF16) {
+    if (contig) QDQ_TILED(QDQ_DTYPE_BF16, true);
+    else QDQ_TILED(QDQ_DTYPE_BF16, false);
+  } else {
+    if (contig) QDQ_TILED(QDQ_DTYPE_FP16, true);
+    else QDQ_TILED(QDQ_DTYPE_FP16, false);
+  }
+#undef QDQ_TILED
+  return check_launch("qdq_mxfp4_codes_tiled");
+}
+}  // namespace qdqb200
 
 extern "C" int qdq_mxfp8(const void* x, void* y, void* codes, void* scales, int64_t M, int64_t K,
                          int64_t ldx, int64_t ldy, int dtype, int group_size, void* stream) {
