@@ -361,17 +361,18 @@ def cpu_attn_sample(wl: dict, L: int, budget_s: float = 20.0) -> dict:
     else:
         q, k, v = c4_inputs(torch.device("cpu"), L=L, H=1)
     f = lambda t: t[0, :, 0].float().numpy()  # noqa: E731
-    nv, emulated, fp8 = oa.VARIANTS[wl["sage3"]]
+    qk_fmt, pv_fmt, emulated, pre, vsmooth, qk_smooth = oa.CONFIGS[wl["sage3"]]
+    nv, fp8 = pv_fmt == "nv4", pv_fmt == "mx8"
     block_n = oa.REF_BLOCK_N[wl["sage3"]]
     sm = 1.0 / math.sqrt(128)
     t0 = time.perf_counter()
-    qd, kd, vd, ds = oa.prepass(f(q), f(k), f(v), True, nv, fp8)
+    qd, kd, vd, ds = oa.prepass(f(q), f(k), f(v), qk_smooth, qk_fmt=qk_fmt, pv_fmt=pv_fmt, vsmooth=vsmooth)
     t_pre = time.perf_counter() - t0
     tiles = (L + 127) // 128
     done, t0 = 0, time.perf_counter()
     while done < tiles:
         oa.flash(qd, kd, vd, ds, L, sm, block_n=block_n, nv=nv, emulated=emulated,
-                 q_rows=slice(128 * done, 128 * done + 128), fp8=fp8)
+                 q_rows=slice(128 * done, 128 * done + 128), fp8=fp8, pre=pre)
         done += 1
         if time.perf_counter() - t0 > budget_s:
             break

@@ -198,12 +198,22 @@ int64_t sage3_attn_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t D);
  *                (p_quant_kernels.py:106-150);
  *            3 = config "mxfp8_hw": MXFP8 (E4M3 + E8M0 per 32) Q/K/V and P
  *                with the reference hardware kernel's P handling,
- *                mxfp8_hw_kernel.py:88-389 (kind::mxf8f6f4 MMAs).
+ *                mxfp8_hw_kernel.py:88-389 (kind::mxf8f6f4 MMAs);
+ *            4 = "mxfp4_s1": MXFP4, emulated P without the 448*6 prescale
+ *                (p_quant_kernels.py:158-195);
+ *            5 = "mxfp8_s1": MXFP8 Q/K/V, emulated single-level MXFP8 P
+ *                (p_quant_kernels.py:238-275);
+ *            6 = "mixed_fp8qk_fp4pv": MXFP8 Q/K, MXFP4 P/V (single-level P);
+ *            7 = "mixed_fp4qk_fp8pv": MXFP4 Q/K, MXFP8 P/V (single-level P);
+ *            8 = "mixed_mxfp8qk_mxfp4pv_hw", 9 = "mixed_mxfp4qk_mxfp8pv_hw":
+ *                the mixed hardware kernels (hardware P handling).
  *   acc_mode: 0 = fp32, 1 = a reduced-precision PV accumulator of the
  *            reference (accepted; this kernel accumulates in fp32 either way).
  *   causal: non-zero for a causal mask (query i sees keys <= i).
- *   smoothing: non-zero for the reference's qk_smoothing (K centring,
- *            per-128-token Q means and the delta_s correction).
+ *   smoothing: bit 0 for the reference's qk_smoothing (K centring,
+ *            per-128-token Q means and the delta_s correction); bit 1 for its
+ *            v_smoothing (V centred over the sequence before quantisation,
+ *            the mean added back to the output: the "_vs" / "_vsmooth" configs).
  *   workspace: >= sage3_attn_workspace_bytes() device bytes.
  * Keys beyond L are masked (the reference attends to its zero padding).
  */

@@ -117,13 +117,29 @@ def _ceil_log2(r: np.ndarray) -> np.ndarray:
     return np.where(r == 0, -127, out)
 
 
+def _quant_deq(x: np.ndarray, fmt: str) -> np.ndarray:
+    """Dequantised x [rows, K] in operand format fmt, blocks along K:
+    "mx4" quantize_to_mxfp4, "nv4" NVFP4 per 16, "mx8" quantize_to_mxfp8."""
+    if fmt == "nv4":
+        return nv_quant_deq(x)
+    if fmt == "mx8":
+        return _deq8(*oq.mxfp8_hw_quant(x))
+    return _deq(*oq.mxfp4_hw_quant(x))
+
+
 def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True, nv: bool = False,
-            fp8: bool = False):
+            fp8: bool = False, qk_fmt: str | None = None, pv_fmt: str | None = None, vsmooth: bool = False):
     """q, k, v: float32 [L, D] holding bf16 values for one (batch, head).
     Returns (qd, kd, vd, ds): dequantised Q [Lp, D], K [Lp, D], V [Lp, D]
     (V quantised along the sequence) and delta_s [G, Lp] (zeros without
     smoothing).  nv selects NVFP4 blocks of 16 (E4M3) instead of MXFP4; fp8
-    selects MXFP8 (quantize_to_mxfp8)."""
+    selects MXFP8 (quantize_to_mxfp8); qk_fmt / pv_fmt ("mx4", "nv4", "mx8")
+    set the two operand formats separately.  vsmooth (transforms.py
+    v_smoothing) quantises bf16(v - bf16(mean_L(v))); the mean is then the
+    caller's to add to the output (see vmean())."""
+    default = "nv4" if nv else ("mx8" if fp8 else "mx4")
+    qk_fmt = qk_fmt or default
+    pv_fmt = pv_fmt or default
     L, D = q.shape
     Lp = (L + 127) // 128 * 128
     G = Lp // 128
@@ -141,23 +157,20 @@ def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True,
     pad = lambda a: np.concatenate([a, np.zeros((Lp - L, D), np.float32)])  # noqa: E731
     dsp = np.zeros((G, Lp), np.float64)
     dsp[:, :L] = ds
-    if nv:
-        return (nv_quant_deq(pad(qs)), nv_quant_deq(pad(kc)),
-                nv_quant_deq(np.ascontiguousarray(pad(v).T)).T, dsp)
-    if fp8:
-        qcodes, qsc = oq.mxfp8_hw_quant(pad(qs))
-        kcodes, ksc = oq.mxfp8_hw_quant(pad(kc))
-        vcodes, vsc = oq.mxfp8_hw_quant(np.ascontiguousarray(pad(v).T))  # [D, Lp], [D, Lp/32]
-        return _deq8(qcodes, qsc), _deq8(kcodes, ksc), _deq8(vcodes, vsc).T, dsp
-    qcodes, qsc = oq.mxfp4_hw_quant(pad(qs))
-    kcodes, ksc = oq.mxfp4_hw_quant(pad(kc))
-    vcodes, vsc = oq.mxfp4_hw_quant(np.ascontiguousarray(pad(v).T))  # [D, Lp/2], [D, Lp/32]
-    return _deq(qcodes, qsc), _deq(kcodes, ksc), _deq(vcodes, vsc).T, dsp
+    if vsmooth:
+        v = bf16_round(v - vmean(v))
+    return (_quant_deq(pad(qs), qk_fmt), _quant_deq(pad(kc), qk_fmt),
+            _quant_deq(np.ascontiguousarray(pad(v).T), pv_fmt).T, dsp)
+
+
+def vmean(v: np.ndarray) -> np.ndarray:
+    """bf16(mean over the sequence of v) [D] (transforms.py v_smoothing)."""
+    return bf16_round(v.astype(np.float64).mean(axis=0))
 
 
 def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: bool = False,
           mask_padding: bool = True, nv: bool = False, emulated: bool = False,
-          q_rows: slice | None = None, fp8: bool = False) -> np.ndarray:
+          q_rows: slice | None = None, fp8: bool = False, pre: float | None = None) -> np.ndarray:
     """The attention loop on dequantised operands; returns O [L, D] float64
     (or the rows q_rows of it, for timing a slice of the query tiles).
 
@@ -166,7 +179,11 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
     first, l = sum of the dequantised P (p_quant_kernels.py:37-150,
     attention_kernel.py:176-186); nv=True uses E4M3 per 16.  fp8=True: the
     mxfp8_hw kernel's P, E4M3 codes of min(p / 2^e, 448) with
-    e = clamp(ceil(log2(max p / 448)), -127, 127) per 32, l = sum of p."""
+    e = clamp(ceil(log2(max p / 448)), -127, 127) per 32, l = sum of p; with
+    emulated=True the single-level emulated MXFP8 P (p_quant_mxfp8_s1): the
+    same codes, l = sum of the dequantised P.  pre: the emulated prescale
+    (448*6 by default, 1 for the single-level _s1 configs).  The emulated E8M0
+    scales take the reference's max(., 1e-8) before the ceiling."""
     Lp, D = kd.shape
     n_keys = L if mask_padding else Lp
     qk_scale = sm_scale * LOG2E
@@ -177,7 +194,8 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
     l = np.zeros(nq)
     acc = np.zeros((nq, D))
     group = rows // 128
-    pre = 2688.0 if emulated else 1.0
+    if pre is None or not emulated:
+        pre = 2688.0 if emulated else 1.0
     for n0 in range(0, n_keys, block_n):
         n1 = min(n0 + block_n, Lp)
         s = qd @ kd[n0:n1].T + ds[group, n0:n1]
@@ -195,6 +213,8 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
         if fp8:
             pg = p1.reshape(nq, w // 32, 32)
             e = np.clip(_ceil_log2(pg.max(axis=2) / 448.0), -127, 127)
+            if emulated:
+                e = np.maximum(e, -26)  # ceil(log2(1e-8))
             sc = np.exp2(e.astype(np.float64))[:, :, None]
             pq = (e4m3_round(pg / sc).astype(np.float64) * sc).reshape(nq, w)
         elif nv:
@@ -205,6 +225,8 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
         else:
             pg = p1.reshape(nq, w // 32, 32)
             e = np.clip(_ceil_log2(pg.max(axis=2) / 6.0), -127, 127)
+            if emulated:
+                e = np.maximum(e, -26)  # ceil(log2(1e-8))
             sc = np.exp2(e.astype(np.float64))[:, :, None]
             pq = (_rne_e2m1(pg / sc) * sc).reshape(nq, w)
         l = l * alpha + (pq.sum(axis=1) if emulated else p.sum(axis=1))
@@ -213,15 +235,31 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
     return (acc / l[:, None])[rows < L]
 
 
-# config -> (nv, emulated, fp8)
-VARIANTS = {"mxfp4_hw": (False, False, False), "mxfp4": (False, True, False), "nvfp4": (True, True, False),
-            "mxfp8_hw": (False, False, True)}
+# config -> (Q/K format, P/V format, emulated P, prescale, V smoothing, QK smoothing)
+# (reference: sage3/quant_config.py:161-330 and the hardware branches of sage3/api.py)
+CONFIGS = {
+    "mxfp4_hw": ("mx4", "mx4", False, 1.0, False, True),
+    "mxfp4": ("mx4", "mx4", True, 2688.0, False, True),
+    "mxfp4_s1_2level": ("mx4", "mx4", True, 2688.0, False, True),
+    "nvfp4": ("nv4", "nv4", True, 2688.0, False, True),
+    "mxfp8_hw": ("mx8", "mx8", False, 1.0, False, True),
+    "mxfp4_s1": ("mx4", "mx4", True, 1.0, False, True),
+    "mxfp8_s1": ("mx8", "mx8", True, 1.0, False, True),
+    "mixed_fp8qk_fp4pv": ("mx8", "mx4", True, 1.0, False, True),
+    "mixed_fp4qk_fp8pv": ("mx4", "mx8", True, 1.0, False, True),
+    "mixed_mxfp8qk_mxfp4pv_hw": ("mx8", "mx4", False, 1.0, False, False),
+    "mixed_mxfp4qk_mxfp8pv_hw": ("mx4", "mx8", False, 1.0, False, False),
+    "mxfp4_s1_vsmooth": ("mx4", "mx4", True, 1.0, True, True),
+    "mixed_fp8qk_fp4pv_vs": ("mx8", "mx4", True, 1.0, True, True),
+    "mixed_fp4qk_fp8pv_vs": ("mx4", "mx8", True, 1.0, True, True),
+}
 
 # Key tile of the reference's online softmax per config: the mxfp4_hw kernel
 # launches with BLOCK_N = 64 (sage3/mxfp4_hw_kernel.py:437); the emulated
 # configs' attention kernel requires tile_size_k = 128 (attention_kernel.py:249-253);
-# the mxfp8_hw kernel launches with BLOCK_N = 64 (sage3/mxfp8_hw_kernel.py:341).
-REF_BLOCK_N = {"mxfp4_hw": 64, "mxfp4": 128, "nvfp4": 128, "mxfp8_hw": 64}
+# the mxfp8_hw and mixed hardware kernels launch with BLOCK_N = 64
+# (sage3/mxfp8_hw_kernel.py:341 and the mixed kernels' launchers).
+REF_BLOCK_N = {name: (128 if cfg[2] else 64) for name, cfg in CONFIGS.items()}
 
 
 def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_scale: float,
@@ -229,7 +267,8 @@ def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_sca
               mask_padding: bool = True, config: str = "mxfp4_hw") -> np.ndarray:
     """q/k/v: uint16 bf16 bit patterns [L, H, D] (NHD with B = 1); returns O [L, H, D].
     block_n defaults to the reference's key tile for the config (REF_BLOCK_N)."""
-    nv, emulated, fp8 = VARIANTS[config]
+    qk_fmt, pv_fmt, emulated, pre, vsmooth, qk_smooth = CONFIGS[config]
+    smoothing = smoothing and qk_smooth
     if block_n is None:
         block_n = REF_BLOCK_N[config]
     L, H, D = q_bits.shape
@@ -238,9 +277,11 @@ def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_sca
         q = bf16_bits_to_f32(q_bits[:, h])
         k = bf16_bits_to_f32(k_bits[:, h])
         v = bf16_bits_to_f32(v_bits[:, h])
-        qd, kd, vd, ds = prepass(q, k, v, smoothing, nv, fp8)
-        out[:, h] = flash(qd, kd, vd, ds, L, sm_scale, block_n, causal, mask_padding, nv, emulated,
-                          fp8=fp8)
+        qd, kd, vd, ds = prepass(q, k, v, smoothing, qk_fmt=qk_fmt, pv_fmt=pv_fmt, vsmooth=vsmooth)
+        out[:, h] = flash(qd, kd, vd, ds, L, sm_scale, block_n, causal, mask_padding, pv_fmt == "nv4", emulated,
+                          fp8=pv_fmt == "mx8", pre=pre)
+        if vsmooth:
+            out[:, h] += vmean(v)
     return out
 
 

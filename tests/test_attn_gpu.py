@@ -28,11 +28,13 @@ pytestmark = pytest.mark.gpu
 KERNEL_BLOCK_N = 128  # keys per online-softmax step of the flash kernel
 
 
-def _qkv(L, H, seed, k_offset=3.0, B=1):
+def _qkv(L, H, seed, k_offset=3.0, B=1, v_offset=0.0):
     g = torch.Generator().manual_seed(seed)
     q = torch.randn(B, L, H, 128, generator=g)
     k = torch.randn(B, L, H, 128, generator=g) + torch.randn(B, 1, H, 128, generator=g) * k_offset
     v = torch.randn(B, L, H, 128, generator=g)
+    if v_offset:
+        v = v + torch.randn(B, 1, H, 128, generator=g) * v_offset
     return q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
 
 
@@ -76,6 +78,85 @@ def test_emulated_configs_match_oracle(cuda_device, config, L, H):
     assert oa.rel_l2(got, want) < 2e-2, oa.rel_l2(got, want)
     exact = oa.exact_attention(qb, kb, vb, sm)
     assert oa.rel_l2(got, exact) <= 1.1 * oa.rel_l2(want, exact) + 0.01
+
+
+SINGLE_LEVEL_AND_MIXED = ["mxfp4_s1", "mxfp8_s1", "mixed_fp8qk_fp4pv", "mixed_fp4qk_fp8pv",
+                          "mixed_mxfp8qk_mxfp4pv_hw", "mixed_mxfp4qk_mxfp8pv_hw", "mxfp4_s1_vsmooth",
+                          "mixed_fp8qk_fp4pv_vs", "mixed_fp4qk_fp8pv_vs", "mxfp4_s1_2level"]
+
+
+@pytest.mark.parametrize("config", SINGLE_LEVEL_AND_MIXED)
+@pytest.mark.parametrize("L,H,causal", [(256, 2, False), (1000, 1, False), (300, 1, True)])
+def test_single_level_and_mixed_configs_match_oracle(cuda_device, config, L, H, causal):
+    """Single-level (_s1), mixed-format and V-smoothed configs: relative L2 vs
+    the same-tile oracle <= 2e-2 and the error vs exact attention within 1.1x
+    (+0.01) of the oracle's.  V carries a per-channel offset so that V
+    smoothing changes the quantised operand."""
+    q, k, v = _qkv(L, H, seed=L * 7 + H + len(config), v_offset=2.0)
+    sm = 1.0 / math.sqrt(128)
+    got = _run(q, k, v, cuda_device, causal=causal, config=config)[0]
+    qb, kb, vb = _bits(q[0]), _bits(k[0]), _bits(v[0])
+    want = oa.attention(qb, kb, vb, sm, block_n=KERNEL_BLOCK_N, causal=causal, config=config)
+    err = oa.rel_l2(got, want)
+    assert err < 2e-2, f"rel L2 vs oracle {err}"
+    exact = oa.exact_attention(qb, kb, vb, sm, causal=causal)
+    assert oa.rel_l2(got, exact) <= 1.1 * oa.rel_l2(want, exact) + 0.01
+    from vllm_qdq_plugin import _native
+    assert _native.device_status() == 0
+
+
+def test_v_smoothing_reduces_error(cuda_device):
+    """With a large per-channel V offset, subtracting the V mean before the FP4
+    quantisation (mxfp4_s1_vsmooth) gives a smaller error than mxfp4_s1."""
+    q, k, v = _qkv(512, 2, seed=31, v_offset=8.0)
+    sm = 1.0 / math.sqrt(128)
+    qb, kb, vb = _bits(q[0]), _bits(k[0]), _bits(v[0])
+    exact = oa.exact_attention(qb, kb, vb, sm)
+    plain = oa.rel_l2(_run(q, k, v, cuda_device, config="mxfp4_s1")[0], exact)
+    smooth = oa.rel_l2(_run(q, k, v, cuda_device, config="mxfp4_s1_vsmooth")[0], exact)
+    assert smooth < 0.8 * plain, (smooth, plain)
+
+
+@pytest.mark.parametrize("config", ["mixed_fp8qk_fp4pv", "mixed_mxfp4qk_mxfp8pv_hw", "mxfp4_s1_vsmooth"])
+def test_new_config_prepass_codes_bit_exact(cuda_device, config):
+    """The pre-pass codes and scales of q_s, k_c and V (mean-subtracted for the
+    V-smoothed configs), read back from the workspace, dequantise to exactly
+    the oracle's values in each operand format."""
+    import ctypes
+    from vllm_qdq_plugin import _native
+    from vllm_qdq_plugin.sage3_attn.sage3 import api
+    qk_fmt, pv_fmt, _, _, vsmooth, qk_smooth = oa.CONFIGS[config]
+    L, H = 300, 1
+    q, k, v = _qkv(L, H, seed=29, v_offset=2.0)
+    dev = cuda_device
+    qd_, kd_, vd_ = (t.to(dev) for t in (q, k, v))
+    out = torch.empty_like(qd_)
+    lib = _native.lib()
+    nbytes = lib.sage3_attn_workspace_bytes(1, L, H, 128)
+    ws = torch.zeros((nbytes,), dtype=torch.uint8, device=dev)
+    st = [qd_.stride(0), qd_.stride(1), qd_.stride(2)] * 3 + [out.stride(0), out.stride(1), out.stride(2)]
+    _native.call("sage3_fp4_attn", qd_.data_ptr(), kd_.data_ptr(), vd_.data_ptr(), out.data_ptr(), 1, L, H, 128,
+                 (ctypes.c_int64 * 12)(*st), 1.0 / math.sqrt(128), api.ATTENTION_CONFIGS[config], 0, 0,
+                 api._smoothing_flags(config, True), 0, ws.data_ptr(), nbytes, _native.stream_ptr(dev))
+    torch.cuda.synchronize()
+    w = ws.cpu().numpy()
+    Lp, G = 384, 3
+    up = lambda n: (n + 255) // 256 * 256  # noqa: E731
+    row = lambda fmt: 128 if fmt == "mx8" else 64  # noqa: E731
+    deq = lambda fmt, c, s: oa._deq8(c, s) if fmt == "mx8" else oa._deq(c, s)  # noqa: E731
+    off = up(128 * 4) + up(G * 128 * 2)
+    qc = w[off: off + Lp * row(qk_fmt)].reshape(Lp, row(qk_fmt)); off += up(Lp * 128)
+    qsf = _sf_tile(w[off:], G); off += up(G * 1024)
+    kc = w[off: off + Lp * row(qk_fmt)].reshape(Lp, row(qk_fmt)); off += up(Lp * 128)
+    ksf = _sf_tile(w[off:], G); off += up(G * 1024)
+    vrow = Lp if pv_fmt == "mx8" else Lp // 2
+    vt = w[off: off + 128 * vrow].reshape(128, vrow); off += up(128 * Lp)
+    vsf = _sf_tile(w[off:], G).reshape(G, 128, 4).transpose(1, 0, 2).reshape(128, G * 4)
+    f = lambda t: oa.bf16_bits_to_f32(_bits(t[0, :, 0]))  # noqa: E731
+    qd, kd, vd, _ = oa.prepass(f(q), f(k), f(v), qk_smooth, qk_fmt=qk_fmt, pv_fmt=pv_fmt, vsmooth=vsmooth)
+    np.testing.assert_array_equal(deq(qk_fmt, qc, qsf), qd)
+    np.testing.assert_array_equal(deq(qk_fmt, kc, ksf), kd)
+    np.testing.assert_array_equal(deq(pv_fmt, vt, vsf).T, vd)
 
 
 def test_config5_flux_shape_nvfp4(cuda_device):

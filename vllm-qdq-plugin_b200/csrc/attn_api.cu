@@ -16,9 +16,24 @@ extern "C" int sage3_fp4_attn(const void* q, const void* k, const void* v, void*
   if (B == 0 || L == 0 || H == 0) return QDQ_OK;
   if (D != 128) return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: head_dim %lld (this build supports 128)", (long long)D);
   if (dtype != QDQ_DTYPE_BF16) return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: inputs must be bf16");
-  if (quant_format < 0 || quant_format > 3)
-    return fail(QDQ_ERR_INVALID_ARG,
-                "sage3_fp4_attn: quant_format must be 0 (mxfp4_hw), 1 (nvfp4), 2 (mxfp4) or 3 (mxfp8_hw)");
+  // quant_format -> (Q/K format, P/V format, emulated P, P prescale); see include/qdq_b200.h
+  struct Variant { int qk, pv, emu; float pre; };
+  static const Variant kVariants[] = {
+      {attn::F_MX4, attn::F_MX4, 0, 1.f},      // 0 mxfp4_hw
+      {attn::F_NV4, attn::F_NV4, 1, 2688.f},   // 1 nvfp4
+      {attn::F_MX4, attn::F_MX4, 1, 2688.f},   // 2 mxfp4 (= mxfp4_s1_2level)
+      {attn::F_MX8, attn::F_MX8, 0, 1.f},      // 3 mxfp8_hw
+      {attn::F_MX4, attn::F_MX4, 1, 1.f},      // 4 mxfp4_s1
+      {attn::F_MX8, attn::F_MX8, 1, 1.f},      // 5 mxfp8_s1
+      {attn::F_MX8, attn::F_MX4, 1, 1.f},      // 6 mixed_fp8qk_fp4pv
+      {attn::F_MX4, attn::F_MX8, 1, 1.f},      // 7 mixed_fp4qk_fp8pv
+      {attn::F_MX8, attn::F_MX4, 0, 1.f},      // 8 mixed_mxfp8qk_mxfp4pv_hw
+      {attn::F_MX4, attn::F_MX8, 0, 1.f},      // 9 mixed_mxfp4qk_mxfp8pv_hw
+  };
+  if (quant_format < 0 || quant_format > 9)
+    return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: quant_format must be in [0, 9] (got %d)", quant_format);
+  if (smoothing < 0 || smoothing > 3)
+    return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: smoothing must be in [0, 3] (bit 0 QK, bit 1 V)");
   if (acc_mode < 0 || acc_mode > 1) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: acc_mode must be 0 or 1");
   if (!q || !k || !v || !o || !strides) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: null pointer");
   if (!(sm_scale > 0.f)) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: sm_scale must be positive");
@@ -47,10 +62,13 @@ extern "C" int sage3_fp4_attn(const void* q, const void* k, const void* v, void*
   p.o_sb = strides[9]; p.o_sn = strides[10]; p.o_sh = strides[11];
   p.sm_scale = sm_scale;
   p.causal = causal ? 1 : 0;
-  p.smoothing = smoothing ? 1 : 0;
-  p.nv = quant_format == 1 ? 1 : 0;
-  p.emulated = (quant_format == 1 || quant_format == 2) ? 1 : 0;
-  p.fp8 = quant_format == 3 ? 1 : 0;
+  const Variant& var = kVariants[quant_format];
+  p.smoothing = smoothing & 1;
+  p.vsmooth = (smoothing >> 1) & 1;
+  p.qk_fmt = var.qk;
+  p.pv_fmt = var.pv;
+  p.emulated = var.emu;
+  p.p_prescale = var.pre;
   attn::Workspace w;
   attn::carve(p.B, p.H, p.L, static_cast<uint8_t*>(workspace), &w);
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -6,6 +6,13 @@
 namespace qdqb200 {
 namespace attn {
 
+// Operand formats of the two products.
+enum Fmt : int {
+  F_MX4 = 0,  // E2M1 + E8M0 per 32 (kind::mxf4), 64-byte code rows
+  F_NV4 = 1,  // E2M1 + E4M3 per 16 (kind::mxf4nvf4 block16), 64-byte code rows
+  F_MX8 = 2,  // E4M3 + E8M0 per 32 (kind::mxf8f6f4), 128-byte code rows
+};
+
 // One attention problem: Q, K, V, O in the NHD layout [B, L, H, D] (D = 128,
 // element stride 1) with arbitrary batch / token / head strides (elements).
 struct Problem {
@@ -20,11 +27,13 @@ struct Problem {
   int64_t o_sb, o_sn, o_sh;
   float sm_scale;
   int causal;
-  int smoothing;  // per-128-token Q mean / K mean smoothing with the delta_s correction
-  int nv;         // 0: MXFP4 (E8M0 per 32), 1: NVFP4 (E4M3 per 16)
-  int emulated;   // 1: the reference's emulated-config P handling (P scaled by 448*6 before
-                  //    block scaling, l = sum of quantised P); 0: its mxfp4_hw kernel's
-  int fp8;        // 1: MXFP8 (E4M3 + E8M0 per 32) operands, the reference's mxfp8_hw kernel
+  int smoothing;    // per-128-token Q mean / K mean smoothing with the delta_s correction
+  int vsmooth;      // V mean subtracted before quantisation, added back to the output
+  int qk_fmt;       // Fmt of Q and K
+  int pv_fmt;       // Fmt of P and V
+  int emulated;     // 1: the reference's emulated-config P handling (P times p_prescale before
+                    //    block scaling, l = sum of quantised P); 0: its hardware kernels'
+  float p_prescale; // 448*6 (two-level emulated configs) or 1
 };
 
 // Device buffers of the pre-pass (carved out of the caller's workspace).
@@ -38,6 +47,8 @@ struct Workspace {
   uint8_t* vt;            // [BH * 128, Lp / 2] (E2M1) or [BH * 128, Lp] (E4M3)
   uint8_t* vsf;           // [BH * Lp / 128, 1024]
   float* ds;              // [BH, G, Lp] (bf16-rounded values, stored as fp32)
+  float* vsum;            // [BH, 128] per-channel sums of v (V smoothing)
+  float* vmean;           // [BH, 128] bf16(vsum / L), stored as fp32
 };
 
 inline int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
@@ -63,6 +74,8 @@ inline int64_t carve(int B, int H, int L, uint8_t* base, Workspace* w) {
   uint8_t* vt = take(BH * 128 * Lp);
   uint8_t* vsf = take(BH * G * 1024);
   uint8_t* ds = take(BH * G * Lp * 4);
+  uint8_t* vsum = take(BH * 128 * 4);
+  uint8_t* vmean = take(BH * 128 * 4);
   if (w) {
     w->ksum = reinterpret_cast<float*>(ksum);
     w->qmean = reinterpret_cast<__nv_bfloat16*>(qmean);
@@ -73,6 +86,8 @@ inline int64_t carve(int B, int H, int L, uint8_t* base, Workspace* w) {
     w->vt = vt;
     w->vsf = vsf;
     w->ds = reinterpret_cast<float*>(ds);
+    w->vsum = reinterpret_cast<float*>(vsum);
+    w->vmean = reinterpret_cast<float*>(vmean);
   }
   return off;
 }

@@ -68,27 +68,32 @@ struct Bars {
   int abort;
 };
 
-// Shared-memory layout for E2M1 (kF8 = false: 64-byte code rows) or E4M3
-// (128-byte rows) operands.
+// Shared-memory layout for Q/K rows of QKR bytes and P/V rows of PVR bytes
+// (64 for E2M1, 128 for E4M3).
 // stage: K codes | V codes | K sf | V sf | delta_s A | delta_s B
 // CTA: Q_A | Q_B | P_A[2] | P_B[2] | stages | Q sf A,B | P sf A[2],B[2] | barriers
 // P (codes and scales) is double-buffered per query tile: key tile j writes
 // buffer j & 1 while PV(j-1) may still read the other one.
-template <bool kF8>
+template <int QKR, int PVR>
 struct FL {
-  static constexpr int ROW = kF8 ? 128 : 64;  // code bytes per 128-element row
-  static constexpr int CODE_TILE = 128 * ROW;
-  static constexpr int STAGES = kF8 ? 3 : 4;
-  static constexpr int ST_K = 0, ST_V = CODE_TILE, ST_KSF = 2 * CODE_TILE, ST_VSF = ST_KSF + SF_TILE,
+  static constexpr int QK_TILE = 128 * QKR;   // a Q or K tile
+  static constexpr int PV_TILE = 128 * PVR;   // a P or V^T tile
+  static constexpr int ST_K = 0, ST_V = QK_TILE, ST_KSF = QK_TILE + PV_TILE, ST_VSF = ST_KSF + SF_TILE,
                        ST_DS = ST_VSF + SF_TILE;
   static constexpr int STAGE_BYTES = (ST_DS + 2 * DS_BYTES + 1023) / 1024 * 1024;
-  static constexpr int OFF_Q = 0, OFF_P = 2 * CODE_TILE, OFF_STAGE = 6 * CODE_TILE;
+  static constexpr int OFF_Q = 0, OFF_P = 2 * QK_TILE, OFF_STAGE = 2 * QK_TILE + 4 * PV_TILE;
+  static constexpr int FIXED = 1024 + OFF_STAGE + 6 * SF_TILE + static_cast<int>(sizeof(Bars));
+  static constexpr int STAGES = (227 * 1024 - FIXED) / STAGE_BYTES < MAX_STAGES
+                                    ? (227 * 1024 - FIXED) / STAGE_BYTES : MAX_STAGES;
   static constexpr int OFF_QSF = OFF_STAGE + STAGES * STAGE_BYTES;
   static constexpr int OFF_PSF = OFF_QSF + 2 * SF_TILE;
   static constexpr int OFF_BAR = OFF_PSF + 4 * SF_TILE;
   static constexpr size_t SMEM_BYTES = 1024 + OFF_BAR + sizeof(Bars);
-  static_assert(STAGES <= MAX_STAGES && SMEM_BYTES <= 227 * 1024, "flash layout");
+  static_assert(STAGES >= 2 && SMEM_BYTES <= 227 * 1024, "flash layout");
 };
+__host__ __device__ constexpr int fmt_row(int f) { return f == F_MX8 ? 128 : 64; }
+template <int kQK, int kPV>
+using FLay = FL<fmt_row(kQK), fmt_row(kPV)>;
 __device__ __forceinline__ uint64_t code_desc(bool f8, const void* p) {
   return f8 ? smem_desc_sw128(p) : smem_desc_sw64(p);
 }
@@ -99,16 +104,18 @@ struct Params {
   float qk_scale;   // sm_scale * log2(e)
   int causal;
   int smoothing;
-  float p_prescale;  // 448*6 for the reference's emulated configs (unused by kMxHw)
+  float p_prescale;      // emulated-config P prescale: 448*6 (two-level) or 1 (single-level _s1)
+  int vsmooth;           // the V mean was subtracted before quantisation: add it back to O / l
+  const float* vmean;    // [BH, 128] the V means (bf16 values), when vsmooth
 };
 
-// Softmax / P-quantisation variants of the kernel.
-enum Mode : int {
-  kMxHw = 0,   // MXFP4, the reference mxfp4_hw kernel's P handling (l = sum of unquantised p)
-  kMxEmu = 1,  // MXFP4, the emulated config's P handling (p * 448*6, l = sum of quantised P)
-  kNvEmu = 2,  // NVFP4 (E4M3 per 16), emulated-config P handling
-  kMx8Hw = 3,  // MXFP8 (E4M3 + E8M0 per 32), the reference mxfp8_hw kernel's P handling
-};
+// Kernel variants are <Q/K format, P/V format, emulated P handling>:
+//   hardware-kernel P (kEmu = false): P quantised per 32 keys with E8M0
+//     2^ceil(log2(max p / fmt_max)), l = sum of the unquantised p
+//     (mxfp4_hw_kernel.py / mxfp8_hw_kernel.py and the mixed _hw kernels);
+//   emulated-config P (kEmu = true): p times a prescale (448*6 for the
+//     two-level configs, 1 for the single-level _s1 ones), block-quantised,
+//     l = sum of the dequantised P (p_quant_kernels.py, attention_kernel.py).
 
 // Sum of four fp16x2 words holding decoded E2M1 values (exact in fp16: the
 // values are multiples of 0.5 and at most 6, a sum of 16 of them at most 96).
@@ -173,11 +180,11 @@ __device__ __forceinline__ int mx8_block_exp(float amax) {
 
 // The block-scaled MMAs of a 128 x 128 x 128 product: two K=64 (E2M1) or
 // four K=32 (E4M3) instructions.
-template <int kMode>
+template <int kFmt>
 __device__ __forceinline__ void mma_k128(uint32_t d, uint64_t da, uint64_t db, uint32_t sfa, uint32_t sfb,
                                          bool accumulate_first) {
-  constexpr bool kNV = kMode == kNvEmu;
-  if (kMode == kMx8Hw) {
+  constexpr bool kNV = kFmt == F_NV4;
+  if (kFmt == F_MX8) {
     constexpr uint32_t idesc8 = idesc_mxf8(BM, BN);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {  // 32 E4M3 = 32 bytes per step; scale byte kk of the chunk
@@ -226,13 +233,25 @@ __device__ __forceinline__ float max32(const float* v) {
 // ---------------------------------------------------------------------------
 // softmax warpgroup: one query tile, thread = row
 // ---------------------------------------------------------------------------
-template <int kMode>
+// Sum of four E4M3 bytes (exact in fp32).
+__device__ __forceinline__ float e4m3x4_sum(uint32_t w) {
+  uint32_t h0, h1;
+  asm("{\n\t.reg .b16 lo, hi;\n\t"
+      "mov.b32 {lo, hi}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, lo;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
+      : "=r"(h0), "=r"(h1)
+      : "r"(w));
+  return (f16lo(h0) + f16hi(h0)) + (f16lo(h1) + f16hi(h1));
+}
+
+template <int kQK, int kPV, bool kEmu>
 __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t tmem, const Params& p, int wg,
                                            int qt, int bh, int nkv, __nv_bfloat16* __restrict__ out,
                                            int* status) {
-  constexpr bool kNV = kMode == kNvEmu;
-  constexpr bool kF8 = kMode == kMx8Hw;
-  using Lay = FL<kF8>;
+  constexpr bool kNV = kPV == F_NV4;
+  constexpr bool kP8 = kPV == F_MX8;
+  using Lay = FLay<kQK, kPV>;
   constexpr int NG = kNV ? 8 : 4;            // scale blocks per row of 128 keys
   const int warp = (threadIdx.x >> 5) & 3;
   const int lane = threadIdx.x & 31;
@@ -240,10 +259,10 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
   const uint32_t t_o = tmem + T_O + wg * 128;
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t prow0 = sbase + Lay::OFF_P + 2 * wg * Lay::CODE_TILE + r * Lay::ROW;         // this row of P
+  const uint32_t prow0 = sbase + Lay::OFF_P + 2 * wg * Lay::PV_TILE + r * fmt_row(kPV);      // this row of P
   const uint32_t psf0 = sbase + Lay::OFF_PSF + 2 * wg * SF_TILE + (r & 31) * 16 + (r >> 5) * 4;  // its scale word
   // swizzle of this row's 16-byte chunks: 64-byte (E2M1) or 128-byte (E4M3) pattern
-  const int swz = kF8 ? (r & 7) : ((r >> 1) & 3);
+  const int swz = kP8 ? (r & 7) : ((r >> 1) & 3);
   const float qk = p.qk_scale;
   const int qrow = qt * BM + r;
   float m_run = -INFINITY, l_run = 0.f;
@@ -302,10 +321,10 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     m_run = m_new;
     // P(j) goes to buffer j & 1; PV(j-2), its previous reader, completed before
     // p_full(j-1) was signalled (the o_done wait below, one tile earlier).
-    const uint32_t prow = prow0 + (j & 1) * Lay::CODE_TILE;
+    const uint32_t prow = prow0 + (j & 1) * Lay::PV_TILE;
     const uint32_t psf = psf0 + (j & 1) * SF_TILE;
     const float2 qk2 = make_float2(qk, qk);
-    if (kMode == kMx8Hw) {
+    if (!kEmu && kP8) {
       // P -> E4M3 codes (round-to-nearest-even, saturating at 448 as the
       // reference's min(., 448)) with E8M0 2^e per 32 keys,
       // e = clamp(ceil(log2(max p / 448)), -127, 127), folded into the
@@ -340,7 +359,7 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
       }
       l_run += lsum;
       sts32(psf, sfw);
-    } else if (kMode == kMxHw) {
+    } else if (!kEmu) {
       // P -> E2M1 codes (round-to-nearest-even) with E8M0 2^e per 32 keys,
       // e = clamp(ceil(log2(max p / 6)), -127, 127).  The block scale is folded
       // into the exponent: p * 2^-e = exp2(x * qk - m - e).  l += sum of p
@@ -374,9 +393,47 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
       }
       l_run += lsum;
       sts32(psf, sfw);
+    } else if (kP8) {
+      // Emulated single-level MXFP8 P (p_quant_mxfp8_s1): E8M0 2^e per 32 keys,
+      // e = clamp(ceil(log2(max(max p / 448, 1e-8))), -127, 127), E4M3 codes
+      // of p * 2^-e (the fp8 cast, round-to-nearest-even); l += sum of the
+      // dequantised P.
+      const float2 mneg2 = make_float2(-m_new, -m_new);
+      uint32_t sfw = 0;
+      float lq = 0.f;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const float amax = __fmul_rn(ex2_approx(fmaf(gm[g], qk, -m_new)), p.p_prescale);
+        const int e = max(mx8_block_exp(amax), -26);  // ceil(log2(1e-8)) = -26
+        const float2 inv2 = make_float2(exp2i(-e), exp2i(-e));
+        const float2 ps2 = make_float2(p.p_prescale, p.p_prescale);
+        uint32_t w[8];
+        float gsum = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float v[4];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int n = g * 32 + q * 4 + 2 * i;
+            const float2 t = fma_f32x2(make_float2(x[n], x[n + 1]), qk2, mneg2);
+            const float2 pv = mul_f32x2(mul_f32x2(make_float2(ex2_approx(t.x), ex2_approx(t.y)), ps2), inv2);
+            v[2 * i] = pv.x;
+            v[2 * i + 1] = pv.y;
+          }
+          w[q] = cvt_e4m3x4(v[0], v[1], v[2], v[3]);
+          gsum += e4m3x4_sum(w[q]);
+        }
+        lq = fmaf(gsum, exp2i(e), lq);
+        sts128(prow + (((2 * g) ^ swz) << 4), w[0], w[1], w[2], w[3]);
+        sts128(prow + (((2 * g + 1) ^ swz) << 4), w[4], w[5], w[6], w[7]);
+        sfw |= static_cast<uint32_t>(e + 127) << (8 * g);
+      }
+      l_run += lq;
+      sts32(psf, sfw);
     } else {
-      // Emulated configs: p = exp2(x * qk - m), scaled by 448*6 (it cancels in
-      // O / l), block-quantised; l += sum of the dequantised P.
+      // Emulated configs: p = exp2(x * qk - m), times the prescale (448*6 for
+      // the two-level configs, which cancels in O / l; 1 for the single-level
+      // _s1 ones), block-quantised; l += sum of the dequantised P.
       //   MXFP4: E8M0 2^e per 32, e = clamp(ceil(log2(max / 6)), -127, 127);
       //   NVFP4: E4M3 per 16, s = e4m3(max(max / 6, 1e-8)).
       // The block max of p * 2688 is round(max p * 2688) (rounding is monotone).
@@ -403,7 +460,7 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
           deq = round_e4m3(scl);
           inv = deq > 0.f ? __fdiv_rn(1.0f, deq) : 0.f;
         } else {
-          const int e = mx_block_exp(amax);
+          const int e = max(mx_block_exp(amax), -26);  // the scale's max(., 1e-8): ceil(log2(1e-8)) = -26
           sbyte = static_cast<uint32_t>(e + 127);
           deq = exp2i(e);
           inv = exp2i(-e);
@@ -480,29 +537,45 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     tmem_ld32(t_o + lane_base + c, u);
     tmem_ld_wait();
     if (store) {
+      float add[32];
+      if (p.vsmooth) {  // softmax rows sum to 1: O + v_mean is the attention of the uncentred V
+        const float4* vm = reinterpret_cast<const float4*>(p.vmean + static_cast<int64_t>(bh) * HD + c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 t = __ldg(vm + i);
+          add[4 * i] = t.x;
+          add[4 * i + 1] = t.y;
+          add[4 * i + 2] = t.z;
+          add[4 * i + 3] = t.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) add[i] = 0.f;
+      }
       uint4* dst = reinterpret_cast<uint4*>(orow + c);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         uint32_t w[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          w[i] = pack_bf16x2(__uint_as_float(u[q * 8 + 2 * i]) * inv_l, __uint_as_float(u[q * 8 + 2 * i + 1]) * inv_l);
+          w[i] = pack_bf16x2(fmaf(__uint_as_float(u[q * 8 + 2 * i]), inv_l, add[q * 8 + 2 * i]),
+                             fmaf(__uint_as_float(u[q * 8 + 2 * i + 1]), inv_l, add[q * 8 + 2 * i + 1]));
         dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
   }
 }
 
-template <int kMode>
+template <int kQK, int kPV, bool kEmu>
 __global__ void __launch_bounds__(THREADS, 1)
 sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                        const __grid_constant__ CUtensorMap map_v, const uint8_t* __restrict__ qsf,
                        const uint8_t* __restrict__ ksf, const uint8_t* __restrict__ vsf,
                        const float* __restrict__ ds, __nv_bfloat16* __restrict__ out, Params p,
                        int* status) {
-  constexpr bool kNV = kMode == kNvEmu;
-  constexpr bool kF8 = kMode == kMx8Hw;
-  using Lay = FL<kF8>;
+  constexpr bool kNVq = kQK == F_NV4, kNVp = kPV == F_NV4;   // two scale chunks per tile
+  constexpr bool kQ8 = kQK == F_MX8, kP8 = kPV == F_MX8;     // 128-byte code rows
+  using Lay = FLay<kQK, kPV>;
   constexpr int STAGES = Lay::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -514,7 +587,7 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
   const int nq = hasB ? 2 : 1;
   const int bh = blockIdx.y;
   const int nkv = p.causal ? qtA + nq : p.T;  // causal: keys up to the last query row of the CTA
-  constexpr int kSfBytes = kNV ? SF_TILE : SF_CHUNK;
+  constexpr int kSfQK = kNVq ? SF_TILE : SF_CHUNK, kSfPV = kNVp ? SF_TILE : SF_CHUNK;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
@@ -547,17 +620,17 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
   if (warp < 8) {
     reg_alloc_224();
     const int wg = warp >> 2;
-    if (wg < nq) softmax_wg<kMode>(smem, bars, tmem, p, wg, qtA + wg, bh, nkv, out, status);
+    if (wg < nq) softmax_wg<kQK, kPV, kEmu>(smem, bars, tmem, p, wg, qtA + wg, bh, nkv, out, status);
   } else {
     reg_dealloc_56();
     if (warp == 9) {
       // ------------------------------------------------------------ producer
       if (elect_one()) {
-        mbar_arrive_expect_tx(&bars->q_full, nq * (Lay::CODE_TILE + kSfBytes));
+        mbar_arrive_expect_tx(&bars->q_full, nq * (Lay::QK_TILE + kSfQK));
         for (int t = 0; t < nq; ++t) {
-          tma_load_2d(smem + Lay::OFF_Q + t * Lay::CODE_TILE, &map_q, 0, bh * p.Lp + (qtA + t) * BM, &bars->q_full);
+          tma_load_2d(smem + Lay::OFF_Q + t * Lay::QK_TILE, &map_q, 0, bh * p.Lp + (qtA + t) * BM, &bars->q_full);
           bulk_load(smem + Lay::OFF_QSF + t * SF_TILE, qsf + (static_cast<int64_t>(bh) * p.T + qtA + t) * SF_TILE,
-                    kSfBytes, &bars->q_full);
+                    kSfQK, &bars->q_full);
         }
         int issued = 0;
         for (int j = 0; j < nkv; ++j) {
@@ -568,13 +641,13 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
           }
           if (*(volatile int*)&bars->abort) break;
           uint8_t* st = smem + Lay::OFF_STAGE + s * Lay::STAGE_BYTES;
-          const uint32_t bytes = 2 * Lay::CODE_TILE + 2 * kSfBytes + (p.smoothing ? nq * DS_BYTES : 0);
+          const uint32_t bytes = Lay::QK_TILE + Lay::PV_TILE + kSfQK + kSfPV + (p.smoothing ? nq * DS_BYTES : 0);
           mbar_arrive_expect_tx(&bars->kv_full[s], bytes);
           tma_load_2d(st + Lay::ST_K, &map_k, 0, bh * p.Lp + j * BN, &bars->kv_full[s]);
-          tma_load_2d(st + Lay::ST_V, &map_v, j * (kF8 ? BN : BN / 2), bh * HD, &bars->kv_full[s]);
-          bulk_load(st + Lay::ST_KSF, ksf + (static_cast<int64_t>(bh) * p.T + j) * SF_TILE, kSfBytes,
+          tma_load_2d(st + Lay::ST_V, &map_v, j * (kP8 ? BN : BN / 2), bh * HD, &bars->kv_full[s]);
+          bulk_load(st + Lay::ST_KSF, ksf + (static_cast<int64_t>(bh) * p.T + j) * SF_TILE, kSfQK,
                     &bars->kv_full[s]);
-          bulk_load(st + Lay::ST_VSF, vsf + (static_cast<int64_t>(bh) * p.T + j) * SF_TILE, kSfBytes,
+          bulk_load(st + Lay::ST_VSF, vsf + (static_cast<int64_t>(bh) * p.T + j) * SF_TILE, kSfPV,
                     &bars->kv_full[s]);
           if (p.smoothing)
             for (int t = 0; t < nq; ++t)
@@ -592,7 +665,7 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
         bool ok = mbar_wait(&bars->q_full, 0, status, 0x1201);
         if (ok) {
           tc_fence_after();
-          for (int t = 0; t < nq; ++t) cp_sf<kNV>(tmem + T_SFQ + t * 8, smem + Lay::OFF_QSF + t * SF_TILE);
+          for (int t = 0; t < nq; ++t) cp_sf<kNVq>(tmem + T_SFQ + t * 8, smem + Lay::OFF_QSF + t * SF_TILE);
         }
         auto issue_pv = [&](int t) -> bool {
           const int s = t % STAGES;
@@ -600,11 +673,11 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
           for (int w = 0; w < nq; ++w) {
             if (!mbar_wait(&bars->p_full[w], t & 1, status, 0x1202)) return false;
             tc_fence_after();
-            if (w == 0) cp_sf<kNV>(tmem + T_SFV, st + Lay::ST_VSF);
+            if (w == 0) cp_sf<kNVp>(tmem + T_SFV, st + Lay::ST_VSF);
             const int pb = 2 * w + (t & 1);  // P buffer of key tile t
-            cp_sf<kNV>(tmem + T_SFP, smem + Lay::OFF_PSF + pb * SF_TILE);
-            mma_k128<kMode>(tmem + T_O + w * 128, code_desc(kF8, smem + Lay::OFF_P + pb * Lay::CODE_TILE),
-                            code_desc(kF8, st + Lay::ST_V), tmem + T_SFP, tmem + T_SFV, t != 0);
+            cp_sf<kNVp>(tmem + T_SFP, smem + Lay::OFF_PSF + pb * SF_TILE);
+            mma_k128<kPV>(tmem + T_O + w * 128, code_desc(kP8, smem + Lay::OFF_P + pb * Lay::PV_TILE),
+                          code_desc(kP8, st + Lay::ST_V), tmem + T_SFP, tmem + T_SFV, t != 0);
             tc_commit(&bars->o_done[w]);
           }
           tc_commit(&bars->kv_empty[s]);
@@ -622,9 +695,9 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
             const int prev_j = w == 0 ? j - 1 : j;
             if (prev_j >= 0 && !mbar_wait(&bars->s_free[prev], prev_j & 1, status, 0x1204)) { ok = false; break; }
             tc_fence_after();
-            if (w == 0) cp_sf<kNV>(tmem + T_SFK, st + Lay::ST_KSF);
-            mma_k128<kMode>(tmem + T_S, code_desc(kF8, smem + Lay::OFF_Q + w * Lay::CODE_TILE),
-                            code_desc(kF8, st + Lay::ST_K), tmem + T_SFQ + w * 8, tmem + T_SFK, false);
+            if (w == 0) cp_sf<kNVq>(tmem + T_SFK, st + Lay::ST_KSF);
+            mma_k128<kQK>(tmem + T_S, code_desc(kQ8, smem + Lay::OFF_Q + w * Lay::QK_TILE),
+                          code_desc(kQ8, st + Lay::ST_K), tmem + T_SFQ + w * 8, tmem + T_SFK, false);
             tc_commit(&bars->s_full[w]);
           }
           if (!ok) break;
@@ -647,21 +720,27 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
   }
 }
 
-template <int kMode>
+template <int kQK, int kPV, bool kEmu>
 int launch_mode(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Workspace& w,
                 const Problem& pr, const Params& p, dim3 grid, int* status, cudaStream_t s) {
-  constexpr size_t smem = FL<kMode == kMx8Hw>::SMEM_BYTES;
+  constexpr size_t smem = FLay<kQK, kPV>::SMEM_BYTES;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(&sage3_fp4_flash_kernel<kMode>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    cudaError_t e = cudaFuncSetAttribute(&sage3_fp4_flash_kernel<kQK, kPV, kEmu>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "sage3 flash: smem attribute: %s", cudaGetErrorString(e));
     attr[dev] = true;
   }
-  sage3_fp4_flash_kernel<kMode><<<grid, THREADS, smem, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o, p, status);
+  sage3_fp4_flash_kernel<kQK, kPV, kEmu><<<grid, THREADS, smem, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o,
+                                                                     p, status);
   return check_launch("sage3 flash");
+}
+
+int code_map(CUtensorMap* map, const uint8_t* base, int64_t rows, int64_t row_bytes, bool f8) {
+  // E2M1 rows of 64 bytes (64-byte swizzle) or E4M3 rows of 128 (128-byte swizzle); 128-row boxes
+  return make_tmap_u8_2d(map, base, rows, row_bytes, row_bytes, f8 ? 128 : 64, 128, f8 ? 128 : 64);
 }
 
 }  // namespace
@@ -670,16 +749,11 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   int* status = device_status_ptr();
   if (status == nullptr) return QDQ_ERR_CUDA;
   const int64_t BH = static_cast<int64_t>(pr.B) * pr.H;
+  const bool q8 = pr.qk_fmt == F_MX8, p8 = pr.pv_fmt == F_MX8;
   CUtensorMap mq, mk, mv;
-  if (pr.fp8) {  // E4M3 codes: 128-byte rows, 128-byte swizzle
-    if (int st = make_tmap_u8_2d(&mq, w.qc, BH * pr.Lp, 128, 128, 128, 128, 128)) return st;
-    if (int st = make_tmap_u8_2d(&mk, w.kc, BH * pr.Lp, 128, 128, 128, 128, 128)) return st;
-    if (int st = make_tmap_u8_2d(&mv, w.vt, BH * HD, pr.Lp, pr.Lp, 128, 128, 128)) return st;
-  } else {
-    if (int st = make_tmap_u8_2d(&mq, w.qc, BH * pr.Lp, 64, 64, 64, 128, 64)) return st;
-    if (int st = make_tmap_u8_2d(&mk, w.kc, BH * pr.Lp, 64, 64, 64, 128, 64)) return st;
-    if (int st = make_tmap_u8_2d(&mv, w.vt, BH * HD, pr.Lp / 2, pr.Lp / 2, 64, 128, 64)) return st;
-  }
+  if (int st = code_map(&mq, w.qc, BH * pr.Lp, q8 ? 128 : 64, q8)) return st;
+  if (int st = code_map(&mk, w.kc, BH * pr.Lp, q8 ? 128 : 64, q8)) return st;
+  if (int st = code_map(&mv, w.vt, BH * HD, p8 ? pr.Lp : pr.Lp / 2, p8)) return st;
   Params p;
   p.H = pr.H;
   p.L = pr.L;
@@ -691,12 +765,25 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   p.qk_scale = pr.sm_scale * 1.4426950408889634f;
   p.causal = pr.causal;
   p.smoothing = pr.smoothing;
-  p.p_prescale = pr.emulated ? 2688.0f : 1.0f;
+  p.p_prescale = pr.p_prescale;
+  p.vsmooth = pr.vsmooth;
+  p.vmean = w.vmean;
   dim3 grid(static_cast<unsigned>((p.T + 1) / 2), static_cast<unsigned>(BH));
-  if (pr.fp8) return launch_mode<kMx8Hw>(mq, mk, mv, w, pr, p, grid, status, s);
-  if (pr.nv) return launch_mode<kNvEmu>(mq, mk, mv, w, pr, p, grid, status, s);
-  if (pr.emulated) return launch_mode<kMxEmu>(mq, mk, mv, w, pr, p, grid, status, s);
-  return launch_mode<kMxHw>(mq, mk, mv, w, pr, p, grid, status, s);
+#define QDQ_FLASH(QK, PV, EMU)                                                             \
+  if (pr.qk_fmt == QK && pr.pv_fmt == PV && (pr.emulated != 0) == EMU)                     \
+    return launch_mode<QK, PV, EMU>(mq, mk, mv, w, pr, p, grid, status, s);
+  QDQ_FLASH(F_MX4, F_MX4, false)   // mxfp4_hw
+  QDQ_FLASH(F_MX4, F_MX4, true)    // mxfp4, mxfp4_s1 (+ vsmooth)
+  QDQ_FLASH(F_NV4, F_NV4, true)    // nvfp4
+  QDQ_FLASH(F_MX8, F_MX8, false)   // mxfp8_hw
+  QDQ_FLASH(F_MX8, F_MX8, true)    // mxfp8_s1
+  QDQ_FLASH(F_MX8, F_MX4, true)    // mixed_fp8qk_fp4pv (+ _vs)
+  QDQ_FLASH(F_MX4, F_MX8, true)    // mixed_fp4qk_fp8pv (+ _vs)
+  QDQ_FLASH(F_MX8, F_MX4, false)   // mixed_mxfp8qk_mxfp4pv_hw
+  QDQ_FLASH(F_MX4, F_MX8, false)   // mixed_mxfp4qk_mxfp8pv_hw
+#undef QDQ_FLASH
+  return fail(QDQ_ERR_UNSUPPORTED, "sage3 flash: no kernel for formats (%d, %d, emulated %d)", pr.qk_fmt, pr.pv_fmt,
+              pr.emulated);
 }
 
 }  // namespace attn

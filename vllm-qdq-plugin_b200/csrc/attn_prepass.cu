@@ -231,7 +231,8 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
 template <bool kNV, bool kF8 = false>
 __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __restrict__ v, int H, int L, int Lp,
                                                       int64_t sb, int64_t sn, int64_t sh,
-                                                      uint8_t* __restrict__ vt, uint8_t* __restrict__ vsf) {
+                                                      uint8_t* __restrict__ vt, uint8_t* __restrict__ vsf,
+                                                      const float* __restrict__ vsum, float* __restrict__ vmean) {
   __shared__ __nv_bfloat16 tile[128][128 + 8];
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
   const int t0 = blockIdx.y * 128;
@@ -244,6 +245,15 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
   }
   __syncthreads();
   const int d = threadIdx.x;
+  // V smoothing (transforms.py v_smoothing): quantise bf16(v - mean_L(v)); the
+  // flash epilogue adds the mean back.  Padding rows stay zero.
+  float vm = 0.f;
+  if (vsum != nullptr) {
+    vm = bf16_round(vsum[bh * 128 + d] / static_cast<float>(L));
+    if (blockIdx.y == 0) vmean[bh * 128 + d] = vm;
+    for (int r = 0; r < 128 && t0 + r < L; ++r)
+      tile[r][d] = __float2bfloat16_rn(__bfloat162float(tile[r][d]) - vm);
+  }
   uint8_t* row = kF8 ? vt + (static_cast<int64_t>(bh) * 128 + d) * Lp + blockIdx.y * 128
                      : vt + (static_cast<int64_t>(bh) * 128 + d) * (Lp / 2) + blockIdx.y * 64;
   uint8_t* sft = vsf + (static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 1024 + (d % 32) * 16 + (d / 32) * 4;
@@ -384,26 +394,32 @@ int launch_prepass(const Problem& p, const Workspace& w, cudaStream_t s) {
   if (p.smoothing) {
     ksum_kernel<<<dim3(BH, (p.L + 1023) / 1024), 128, 0, s>>>(p.k, p.H, p.L, p.k_sb, p.k_sn, p.k_sh, w.ksum);
   }
-  if (p.fp8) {
-    qk_quant_kernel<true, false, true><<<dim3(BH, T), 256, 0, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh,
-                                                                 w.ksum, w.qmean, w.qc, w.qsf, p.smoothing);
-    qk_quant_kernel<false, false, true><<<dim3(BH, T), 256, 0, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh,
-                                                                  w.ksum, w.qmean, w.kc, w.ksf, p.smoothing);
-    v_quant_kernel<false, true><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt,
-                                                          w.vsf);
-  } else if (p.nv) {
-    qk_quant_kernel<true, true><<<dim3(BH, T), 256, 0, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh, w.ksum,
-                                                          w.qmean, w.qc, w.qsf, p.smoothing);
-    qk_quant_kernel<false, true><<<dim3(BH, T), 256, 0, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh, w.ksum,
-                                                           w.qmean, w.kc, w.ksf, p.smoothing);
-    v_quant_kernel<true><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf);
-  } else {
-    qk_quant_kernel<true, false><<<dim3(BH, T), 256, 0, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh, w.ksum,
-                                                           w.qmean, w.qc, w.qsf, p.smoothing);
-    qk_quant_kernel<false, false><<<dim3(BH, T), 256, 0, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh, w.ksum,
-                                                            w.qmean, w.kc, w.ksf, p.smoothing);
-    v_quant_kernel<false><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf);
+  if (p.vsmooth) {
+    if (cudaMemsetAsync(w.vsum, 0, sizeof(float) * BH * 128, s) != cudaSuccess)
+      return fail(QDQ_ERR_CUDA, "sage3 prepass: memset failed");
+    ksum_kernel<<<dim3(BH, (p.L + 1023) / 1024), 128, 0, s>>>(p.v, p.H, p.L, p.v_sb, p.v_sn, p.v_sh, w.vsum);
   }
+  // Q and K in the Q/K format
+#define QDQ_QK(NV, F8)                                                                                        \
+  qk_quant_kernel<true, NV, F8><<<dim3(BH, T), 256, 0, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh, w.ksum, \
+                                                            w.qmean, w.qc, w.qsf, p.smoothing);                \
+  qk_quant_kernel<false, NV, F8><<<dim3(BH, T), 256, 0, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh,       \
+                                                             w.ksum, w.qmean, w.kc, w.ksf, p.smoothing)
+  if (p.qk_fmt == F_MX8) { QDQ_QK(false, true); }
+  else if (p.qk_fmt == F_NV4) { QDQ_QK(true, false); }
+  else { QDQ_QK(false, false); }
+#undef QDQ_QK
+  // V^T in the P/V format
+  const float* vs = p.vsmooth ? w.vsum : nullptr;
+  if (p.pv_fmt == F_MX8)
+    v_quant_kernel<false, true><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf,
+                                                           vs, w.vmean);
+  else if (p.pv_fmt == F_NV4)
+    v_quant_kernel<true><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf, vs,
+                                                    w.vmean);
+  else
+    v_quant_kernel<false><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf, vs,
+                                                     w.vmean);
   if (p.smoothing) {
     const int smem = (128 + 64) * DS_LD * 2;
     static bool attr[64] = {false};

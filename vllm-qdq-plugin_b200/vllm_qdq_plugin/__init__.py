@@ -52,9 +52,23 @@ def register_omni_sage3_triton():
     return _register_sage_attn_slot(SAGE3_BACKEND_PATH, "sage3 (sm_100a FP4)", "VLLM_SAGE3_TRITON")
 
 
+def _maybe_install_route(route_file: str) -> None:
+    """Per-(layer, step) attention routing from SAGE3_ROUTE_FILE (reference
+    __init__.py:110-127); a bad route file or a missing vllm-omni logs and
+    leaves routing off instead of stopping the worker."""
+    if not route_file:
+        return
+    try:
+        from .sage3_attn.routing import patch_attention
+        patch_attention.install(route_file)
+    except Exception as e:  # noqa: BLE001 - startup must continue
+        logger.warning("vllm-qdq-plugin: failed to install sage3 attention routing from %s (%s) — "
+                       "continuing without routing", route_file, e)
+
+
 def _not_in_this_build(what: str, flag: str) -> None:
-    # SpargeAttn, the external SageAttention3 CuTe kernel and the per-(layer,
-    # step) route table are outside the FP4 hot path this build replaces.
+    # SpargeAttn and the external SageAttention3 CuTe kernel are outside the
+    # attention this build replaces.
     logger.warning("vllm-qdq-plugin (B200 build): %s=1 requests %s, which this build does "
                    "not provide; the SAGE_ATTN slot is left unchanged", flag, what)
 
@@ -73,8 +87,7 @@ def register_omni():
         _not_in_this_build("the SpargeAttn backend", "VLLM_SPARGE_ATTN")
     elif envs.VLLM_SAGE3_TRITON:
         register_omni_sage3_triton()
-        if envs.SAGE3_ROUTE_FILE:
-            _not_in_this_build("per-(layer, step) attention routing", "SAGE3_ROUTE_FILE")
+        _maybe_install_route(envs.SAGE3_ROUTE_FILE)
     elif envs.VLLM_SAGE3_CUTE:
         _not_in_this_build("the external SageAttention3 CuTe kernel", "VLLM_SAGE3_CUTE")
     else:

@@ -25,6 +25,15 @@ Config mapping:
   "mxfp8_hw"  MXFP8 (E4M3 + E8M0 per 32) Q/K/V and P with the reference
               hardware kernel's semantics (sage3/mxfp8_hw_kernel.py,
               quantize_to_mxfp8), on kind::mxf8f6f4 tensor-core MMAs.
+  "mxfp4_s1", "mxfp8_s1"   the single-level emulated configs (P without the
+              448*6 prescale); "mxfp4_s1_2level" is "mxfp4".
+  "mixed_fp8qk_fp4pv", "mixed_fp4qk_fp8pv"   Q/K in one format, P/V in the
+              other (emulated P of the P/V format); "*_vs" / "_vsmooth" add
+              V smoothing (the V mean is subtracted before quantisation and
+              added back to the output).
+  "mixed_mxfp8qk_mxfp4pv_hw", "mixed_mxfp4qk_mxfp8pv_hw"   the mixed hardware
+              kernels (hardware P handling, no QK smoothing).
+  "mxfp4_s1_e4m3" (E4M3 scales per 32) has no kernel in this build.
 The kernels read the NHD or HND strides they are given; no transposing copies.
 """
 
@@ -52,16 +61,32 @@ ACC_DTYPE_MAP = {
     "bf16_full": ("bf16", "bf16", "bf16"),
 }
 
-# config name -> kernel variant of sage3_fp4_attn (include/qdq_b200.h):
-#   0 mxfp4_hw (MXFP4, hardware-kernel P handling), 1 nvfp4, 2 mxfp4 (emulated-config P handling),
-#   3 mxfp8_hw (MXFP8, hardware-kernel P handling)
-ATTENTION_CONFIGS: dict[str, int] = {"mxfp4": 2, "mxfp4_hw": 0, "nvfp4": 1, "mxfp8_hw": 3}
+# config name -> quant_format of sage3_fp4_attn (include/qdq_b200.h):
+#   0 mxfp4_hw, 1 nvfp4, 2 mxfp4 (two-level emulated P), 3 mxfp8_hw, 4 mxfp4_s1,
+#   5 mxfp8_s1, 6 mixed_fp8qk_fp4pv, 7 mixed_fp4qk_fp8pv, 8 mixed_mxfp8qk_mxfp4pv_hw,
+#   9 mixed_mxfp4qk_mxfp8pv_hw
+# (reference: sage3/quant_config.py:161-330 and the hardware branches of sage3/api.py).
+ATTENTION_CONFIGS: dict[str, int] = {
+    "mxfp4_hw": 0, "nvfp4": 1, "mxfp4": 2, "mxfp4_s1_2level": 2, "mxfp8_hw": 3,
+    "mxfp4_s1": 4, "mxfp8_s1": 5, "mixed_fp8qk_fp4pv": 6, "mixed_fp4qk_fp8pv": 7,
+    "mixed_mxfp8qk_mxfp4pv_hw": 8, "mixed_mxfp4qk_mxfp8pv_hw": 9,
+    "mxfp4_s1_vsmooth": 4, "mixed_fp8qk_fp4pv_vs": 6, "mixed_fp4qk_fp8pv_vs": 7,
+}
+# V smoothing (transforms.py v_smoothing: V mean subtracted before quantisation,
+# added back to the output).
+_VSMOOTH_CONFIGS = {"mxfp4_s1_vsmooth", "mixed_fp8qk_fp4pv_vs", "mixed_fp4qk_fp8pv_vs"}
+# The mixed hardware kernels run without QK smoothing (sage3/api.py:209-291).
+_NO_QK_SMOOTHING = {"mixed_mxfp8qk_mxfp4pv_hw", "mixed_mxfp4qk_mxfp8pv_hw"}
 
-# Names the reference registers that lie outside this build's attention kernels.
-_OTHER_REFERENCE_CONFIGS = ("mxfp4_s1", "mxfp8_s1", "nvfp4_vsmooth", "mxfp4_vsmooth",
-                            "mixed_mxfp8qk_mxfp4pv_hw", "mixed_mxfp4qk_mxfp8pv_hw", "int8", "fp8")
+# Every config name the reference registers (sage3/quant_config.py).
+REFERENCE_CONFIG_NAMES = (
+    "nvfp4", "mxfp4", "mxfp4_s1", "mxfp8_s1", "mxfp4_s1_2level", "mxfp4_s1_e4m3",
+    "mixed_fp8qk_fp4pv", "mixed_fp4qk_fp8pv", "mxfp4_s1_vsmooth", "mixed_fp8qk_fp4pv_vs",
+    "mixed_fp4qk_fp8pv_vs", "mxfp8_hw", "mxfp4_hw", "mixed_mxfp8qk_mxfp4pv_hw", "mixed_mxfp4qk_mxfp8pv_hw")
+# Names the reference registers that this build has no kernel for.
+_OTHER_REFERENCE_CONFIGS = tuple(n for n in REFERENCE_CONFIG_NAMES if n not in ATTENTION_CONFIGS)
 
-_BUILT_FORMATS = (0, 1, 2, 3)  # variants with a kernel in this build
+_BUILT_FORMATS = tuple(range(10))  # variants with a kernel in this build
 
 
 def _get_env_bool(name: str, default: str = "0") -> bool:
@@ -81,9 +106,15 @@ def _resolve_config(config: str) -> int:
     return fmt
 
 
+def _smoothing_flags(config: str, per_block_mean: bool) -> int:
+    """sage3_fp4_attn's `smoothing`: bit 0 QK smoothing, bit 1 V smoothing."""
+    qk = per_block_mean and not _get_env_bool("SAGE3_DISABLE_PER_BLOCK_MEAN") and config not in _NO_QK_SMOOTHING
+    return int(qk) | (2 if config in _VSMOOTH_CONFIGS else 0)
+
+
 @torch.library.custom_op("qdq_b200::sage3_attn", mutates_args=())
 def _sage3_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layout_nhd: bool, sm_scale: float,
-              quant_format: int, acc_mode: int, causal: bool, smoothing: bool) -> torch.Tensor:
+              quant_format: int, acc_mode: int, causal: bool, smoothing: int) -> torch.Tensor:
     _native.require_cuda(q, k, v)
     out = torch.empty_like(q)
     if layout_nhd:  # [B, L, H, D]
@@ -131,10 +162,10 @@ def sage3_attention_nhd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, confi
     _check_inputs(q, k, v, 1)
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(q.shape[-1])
-    smoothing = per_block_mean and not _get_env_bool("SAGE3_DISABLE_PER_BLOCK_MEAN")
+    smoothing = _smoothing_flags(config, per_block_mean)
     acc_mode = 0 if acc_dtype == "fp32" else 1
     return torch.ops.qdq_b200.sage3_attn(q, k, v, True, float(sm_scale), fmt, acc_mode,
-                                         bool(is_causal), bool(smoothing))
+                                         bool(is_causal), int(smoothing))
 
 
 @torch.inference_mode()
@@ -167,10 +198,10 @@ def sageattn3_standalone(
     _check_inputs(q, k, v, 2)
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(q.shape[-1])
-    smoothing = per_block_mean and not _get_env_bool("SAGE3_DISABLE_PER_BLOCK_MEAN")
+    smoothing = _smoothing_flags(name, per_block_mean)
     acc_mode = 0 if acc_dtype == "fp32" else 1
     return torch.ops.qdq_b200.sage3_attn(q, k, v, False, float(sm_scale), fmt, acc_mode,
-                                         bool(is_causal), bool(smoothing))
+                                         bool(is_causal), int(smoothing))
 
 
 @torch.inference_mode()
