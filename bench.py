@@ -372,7 +372,7 @@ def cpu_attn_sample(wl: dict, L: int, budget_s: float = 20.0) -> dict:
     done, t0 = 0, time.perf_counter()
     while done < tiles:
         oa.flash(qd, kd, vd, ds, L, sm, block_n=block_n, nv=nv, emulated=emulated,
-                 q_rows=slice(128 * done, 128 * done + 128), fp8=fp8, pre=pre)
+                 q_rows=slice(128 * done, 128 * done + 128), fp8=fp8, pre=pre, e4s32=pv_fmt == "nv4b32")
         done += 1
         if time.perf_counter() - t0 > budget_s:
             break

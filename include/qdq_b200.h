@@ -206,7 +206,10 @@ int64_t sage3_attn_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t D);
  *            6 = "mixed_fp8qk_fp4pv": MXFP8 Q/K, MXFP4 P/V (single-level P);
  *            7 = "mixed_fp4qk_fp8pv": MXFP4 Q/K, MXFP8 P/V (single-level P);
  *            8 = "mixed_mxfp8qk_mxfp4pv_hw", 9 = "mixed_mxfp4qk_mxfp8pv_hw":
- *                the mixed hardware kernels (hardware P handling).
+ *                the mixed hardware kernels (hardware P handling);
+ *           10 = "mxfp4_s1_e4m3": E2M1 with an E4M3 scale per 32 for Q/K/V
+ *                (quant_config.py:246-263) and single-level P with E4M3
+ *                scales per 32, at least 2^-9 (p_quant_kernels.py:197-232).
  *   acc_mode: 0 = fp32, 1 = a reduced-precision PV accumulator of the
  *            reference (accepted; this kernel accumulates in fp32 either way).
  *   causal: non-zero for a causal mask (query i sees keys <= i).

@@ -97,12 +97,13 @@ def e4m3_round(x: np.ndarray) -> np.ndarray:
     return (np.round(x / step) * step).astype(np.float32)  # np.round: half to even
 
 
-def nv_quant_deq(x: np.ndarray) -> np.ndarray:
+def nv_quant_deq(x: np.ndarray, block: int = 16) -> np.ndarray:
     """NVFP4 of the reference's nvfp4 QuantConfig on the hardware grid, per 16
     along the last axis: scale = e4m3(max(bf16(amax / 6), 1e-8)), codes of
-    x * (1/scale) with round-half-away, dequantised."""
+    x * (1/scale) with round-half-away, dequantised.  block=32 gives the
+    mxfp4_s1_e4m3 QuantConfig (quant_config.py:246-255), the same steps per 32."""
     sh = x.shape
-    xb = np.asarray(x, np.float32).reshape(*sh[:-1], sh[-1] // 16, 16)
+    xb = np.asarray(x, np.float32).reshape(*sh[:-1], sh[-1] // block, block)
     amax = np.abs(xb).max(axis=-1)
     sc = np.maximum(bf16_round(amax / np.float32(6.0)), np.float32(1e-8))
     s = e4m3_round(sc)
@@ -119,9 +120,12 @@ def _ceil_log2(r: np.ndarray) -> np.ndarray:
 
 def _quant_deq(x: np.ndarray, fmt: str) -> np.ndarray:
     """Dequantised x [rows, K] in operand format fmt, blocks along K:
-    "mx4" quantize_to_mxfp4, "nv4" NVFP4 per 16, "mx8" quantize_to_mxfp8."""
+    "mx4" quantize_to_mxfp4, "nv4" NVFP4 per 16, "mx8" quantize_to_mxfp8,
+    "nv4b32" E2M1 with an E4M3 scale per 32."""
     if fmt == "nv4":
         return nv_quant_deq(x)
+    if fmt == "nv4b32":
+        return nv_quant_deq(x, 32)
     if fmt == "mx8":
         return _deq8(*oq.mxfp8_hw_quant(x))
     return _deq(*oq.mxfp4_hw_quant(x))
@@ -170,7 +174,8 @@ def vmean(v: np.ndarray) -> np.ndarray:
 
 def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: bool = False,
           mask_padding: bool = True, nv: bool = False, emulated: bool = False,
-          q_rows: slice | None = None, fp8: bool = False, pre: float | None = None) -> np.ndarray:
+          q_rows: slice | None = None, fp8: bool = False, pre: float | None = None,
+          e4s32: bool = False) -> np.ndarray:
     """The attention loop on dequantised operands; returns O [L, D] float64
     (or the rows q_rows of it, for timing a slice of the query tiles).
 
@@ -183,7 +188,9 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
     emulated=True the single-level emulated MXFP8 P (p_quant_mxfp8_s1): the
     same codes, l = sum of the dequantised P.  pre: the emulated prescale
     (448*6 by default, 1 for the single-level _s1 configs).  The emulated E8M0
-    scales take the reference's max(., 1e-8) before the ceiling."""
+    scales take the reference's max(., 1e-8) before the ceiling.  e4s32=True:
+    p_quant_mxfp4_s1_e4m3 (p_quant_kernels.py:197-232), E2M1 with the scale
+    max(e4m3(max(b / 6, 1e-8)), 2^-9) per 32."""
     Lp, D = kd.shape
     n_keys = L if mask_padding else Lp
     qk_scale = sm_scale * LOG2E
@@ -217,6 +224,11 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
                 e = np.maximum(e, -26)  # ceil(log2(1e-8))
             sc = np.exp2(e.astype(np.float64))[:, :, None]
             pq = (e4m3_round(pg / sc).astype(np.float64) * sc).reshape(nq, w)
+        elif e4s32:
+            pg = p1.reshape(nq, w // 32, 32)
+            sc = np.maximum(e4m3_round(np.maximum(pg.max(axis=2) / 6.0, 1e-8)), 2.0 ** -9)
+            sc = sc.astype(np.float64)[:, :, None]
+            pq = (_rne_e2m1(pg * (1.0 / sc)) * sc).reshape(nq, w)
         elif nv:
             pg = p1.reshape(nq, w // 16, 16)
             sc = e4m3_round(np.maximum(pg.max(axis=2) / 6.0, 1e-8)).astype(np.float64)[:, :, None]
@@ -252,6 +264,7 @@ CONFIGS = {
     "mxfp4_s1_vsmooth": ("mx4", "mx4", True, 1.0, True, True),
     "mixed_fp8qk_fp4pv_vs": ("mx8", "mx4", True, 1.0, True, True),
     "mixed_fp4qk_fp8pv_vs": ("mx4", "mx8", True, 1.0, True, True),
+    "mxfp4_s1_e4m3": ("nv4b32", "nv4b32", True, 1.0, False, True),
 }
 
 # Key tile of the reference's online softmax per config: the mxfp4_hw kernel
@@ -279,7 +292,7 @@ def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_sca
         v = bf16_bits_to_f32(v_bits[:, h])
         qd, kd, vd, ds = prepass(q, k, v, smoothing, qk_fmt=qk_fmt, pv_fmt=pv_fmt, vsmooth=vsmooth)
         out[:, h] = flash(qd, kd, vd, ds, L, sm_scale, block_n, causal, mask_padding, pv_fmt == "nv4", emulated,
-                          fp8=pv_fmt == "mx8", pre=pre)
+                          fp8=pv_fmt == "mx8", pre=pre, e4s32=pv_fmt == "nv4b32")
         if vsmooth:
             out[:, h] += vmean(v)
     return out

@@ -82,7 +82,7 @@ def test_emulated_configs_match_oracle(cuda_device, config, L, H):
 
 SINGLE_LEVEL_AND_MIXED = ["mxfp4_s1", "mxfp8_s1", "mixed_fp8qk_fp4pv", "mixed_fp4qk_fp8pv",
                           "mixed_mxfp8qk_mxfp4pv_hw", "mixed_mxfp4qk_mxfp8pv_hw", "mxfp4_s1_vsmooth",
-                          "mixed_fp8qk_fp4pv_vs", "mixed_fp4qk_fp8pv_vs", "mxfp4_s1_2level"]
+                          "mixed_fp8qk_fp4pv_vs", "mixed_fp4qk_fp8pv_vs", "mxfp4_s1_2level", "mxfp4_s1_e4m3"]
 
 
 @pytest.mark.parametrize("config", SINGLE_LEVEL_AND_MIXED)
@@ -117,7 +117,8 @@ def test_v_smoothing_reduces_error(cuda_device):
     assert smooth < 0.8 * plain, (smooth, plain)
 
 
-@pytest.mark.parametrize("config", ["mixed_fp8qk_fp4pv", "mixed_mxfp4qk_mxfp8pv_hw", "mxfp4_s1_vsmooth"])
+@pytest.mark.parametrize("config", ["mixed_fp8qk_fp4pv", "mixed_mxfp4qk_mxfp8pv_hw", "mxfp4_s1_vsmooth",
+                                    "mxfp4_s1_e4m3"])
 def test_new_config_prepass_codes_bit_exact(cuda_device, config):
     """The pre-pass codes and scales of q_s, k_c and V (mean-subtracted for the
     V-smoothed configs), read back from the workspace, dequantise to exactly
@@ -143,15 +144,31 @@ def test_new_config_prepass_codes_bit_exact(cuda_device, config):
     Lp, G = 384, 3
     up = lambda n: (n + 255) // 256 * 256  # noqa: E731
     row = lambda fmt: 128 if fmt == "mx8" else 64  # noqa: E731
-    deq = lambda fmt, c, s: oa._deq8(c, s) if fmt == "mx8" else oa._deq(c, s)  # noqa: E731
+
+    def deq(fmt, c, sc):
+        if fmt == "mx8":
+            return oa._deq8(c, sc)
+        if fmt == "nv4b32":  # E2M1 codes, E4M3 scale bytes per 32
+            vals = np.stack([oa.E2M1[c & 0xF], oa.E2M1[c >> 4]], axis=-1).reshape(c.shape[0], -1)
+            return vals * np.repeat(oa.E4M3[sc], 32, axis=-1)
+        return oa._deq(c, sc)
+
+    def sf(buf):
+        if qk_fmt != "nv4b32" and pv_fmt != "nv4b32":
+            return _sf_tile(buf, G)
+        # 8 slots of 16 per row in two chunks; each per-32 scale fills two adjacent slots
+        both = np.concatenate([_sf_tile(buf, G), _sf_tile(buf[512:], G)], axis=1)
+        np.testing.assert_array_equal(both[:, 0::2], both[:, 1::2])
+        return both[:, 0::2]
+
     off = up(128 * 4) + up(G * 128 * 2)
     qc = w[off: off + Lp * row(qk_fmt)].reshape(Lp, row(qk_fmt)); off += up(Lp * 128)
-    qsf = _sf_tile(w[off:], G); off += up(G * 1024)
+    qsf = sf(w[off:]); off += up(G * 1024)
     kc = w[off: off + Lp * row(qk_fmt)].reshape(Lp, row(qk_fmt)); off += up(Lp * 128)
-    ksf = _sf_tile(w[off:], G); off += up(G * 1024)
+    ksf = sf(w[off:]); off += up(G * 1024)
     vrow = Lp if pv_fmt == "mx8" else Lp // 2
     vt = w[off: off + 128 * vrow].reshape(128, vrow); off += up(128 * Lp)
-    vsf = _sf_tile(w[off:], G).reshape(G, 128, 4).transpose(1, 0, 2).reshape(128, G * 4)
+    vsf = sf(w[off:]).reshape(G, 128, 4).transpose(1, 0, 2).reshape(128, G * 4)
     f = lambda t: oa.bf16_bits_to_f32(_bits(t[0, :, 0]))  # noqa: E731
     qd, kd, vd, _ = oa.prepass(f(q), f(k), f(v), qk_smooth, qk_fmt=qk_fmt, pv_fmt=pv_fmt, vsmooth=vsmooth)
     np.testing.assert_array_equal(deq(qk_fmt, qc, qsf), qd)

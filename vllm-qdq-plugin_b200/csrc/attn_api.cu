@@ -29,9 +29,10 @@ extern "C" int sage3_fp4_attn(const void* q, const void* k, const void* v, void*
       {attn::F_MX4, attn::F_MX8, 1, 1.f},      // 7 mixed_fp4qk_fp8pv
       {attn::F_MX8, attn::F_MX4, 0, 1.f},      // 8 mixed_mxfp8qk_mxfp4pv_hw
       {attn::F_MX4, attn::F_MX8, 0, 1.f},      // 9 mixed_mxfp4qk_mxfp8pv_hw
+      {attn::F_NV4B32, attn::F_NV4B32, 1, 1.f},  // 10 mxfp4_s1_e4m3
   };
-  if (quant_format < 0 || quant_format > 9)
-    return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: quant_format must be in [0, 9] (got %d)", quant_format);
+  if (quant_format < 0 || quant_format > 10)
+    return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: quant_format must be in [0, 10] (got %d)", quant_format);
   if (smoothing < 0 || smoothing > 3)
     return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: smoothing must be in [0, 3] (bit 0 QK, bit 1 V)");
   if (acc_mode < 0 || acc_mode > 1) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: acc_mode must be 0 or 1");

@@ -11,7 +11,12 @@ enum Fmt : int {
   F_MX4 = 0,  // E2M1 + E8M0 per 32 (kind::mxf4), 64-byte code rows
   F_NV4 = 1,  // E2M1 + E4M3 per 16 (kind::mxf4nvf4 block16), 64-byte code rows
   F_MX8 = 2,  // E4M3 + E8M0 per 32 (kind::mxf8f6f4), 128-byte code rows
+  F_NV4B32 = 3,  // E2M1 + E4M3 per 32: run as block16 (kind::mxf4nvf4) with each
+                 // scale in both of its 16-element slots, 64-byte code rows
 };
+
+// Formats whose MMA is kind::mxf4nvf4.block16 (two 512-byte scale chunks per 128 K).
+__host__ __device__ constexpr bool fmt_block16(int f) { return f == F_NV4 || f == F_NV4B32; }
 
 // One attention problem: Q, K, V, O in the NHD layout [B, L, H, D] (D = 128,
 // element stride 1) with arbitrary batch / token / head strides (elements).

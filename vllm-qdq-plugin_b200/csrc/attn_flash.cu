@@ -116,6 +116,9 @@ struct Params {
 //   emulated-config P (kEmu = true): p times a prescale (448*6 for the
 //     two-level configs, 1 for the single-level _s1 ones), block-quantised,
 //     l = sum of the dequantised P (p_quant_kernels.py, attention_kernel.py).
+// F_NV4B32 (mxfp4_s1_e4m3) runs on the block16 MMA with each per-32 E4M3
+// scale in both of its 16-element slots, which multiplies every element by
+// the same scale as one per-32 slot would.
 
 // Sum of four fp16x2 words holding decoded E2M1 values (exact in fp16: the
 // values are multiples of 0.5 and at most 6, a sum of 16 of them at most 96).
@@ -183,7 +186,7 @@ __device__ __forceinline__ int mx8_block_exp(float amax) {
 template <int kFmt>
 __device__ __forceinline__ void mma_k128(uint32_t d, uint64_t da, uint64_t db, uint32_t sfa, uint32_t sfb,
                                          bool accumulate_first) {
-  constexpr bool kNV = kFmt == F_NV4;
+  constexpr bool kNV = fmt_block16(kFmt);
   if (kFmt == F_MX8) {
     constexpr uint32_t idesc8 = idesc_mxf8(BM, BN);
 #pragma unroll
@@ -197,7 +200,7 @@ __device__ __forceinline__ void mma_k128(uint32_t d, uint64_t da, uint64_t db, u
   constexpr uint32_t idesc = idesc_mxf4(BM, BN, !kNV);
 #pragma unroll
   for (int kk = 0; kk < 2; ++kk) {
-    if (kNV) {  // UE4M3 per 16: MMA kk reads scale chunk kk (4 scales per row)
+    if (kNV) {  // UE4M3 per 16 (F_NV4B32: each scale twice): MMA kk reads scale chunk kk
       mma_nvf4(d, da + kk * 2, db + kk * 2, idesc, sfa + 4 * kk, sfb + 4 * kk, accumulate_first || kk);
     } else {    // UE8M0 per 32: scale bytes 2kk, 2kk+1 of the chunk
       const uint32_t sf_id = kk * 2;
@@ -251,6 +254,7 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
                                            int* status) {
   constexpr bool kNV = kPV == F_NV4;
   constexpr bool kP8 = kPV == F_MX8;
+  constexpr bool kE4S32 = kPV == F_NV4B32;   // E4M3 scale per 32 keys
   using Lay = FLay<kQK, kPV>;
   constexpr int NG = kNV ? 8 : 4;            // scale blocks per row of 128 keys
   const int warp = (threadIdx.x >> 5) & 3;
@@ -459,6 +463,13 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
           sbyte = e4m3_byte(scl);
           deq = round_e4m3(scl);
           inv = deq > 0.f ? __fdiv_rn(1.0f, deq) : 0.f;
+        } else if (kE4S32) {
+          // p_quant_mxfp4_s1_e4m3: max(e4m3(max(b / 6, 1e-8)), 2^-9), the
+          // smallest E4M3 subnormal (byte 1)
+          const float scl = fmaxf(__fdiv_rn(amax, 6.0f), 1e-8f);
+          sbyte = max(e4m3_byte(scl), 1u);
+          deq = fmaxf(round_e4m3(scl), 1.953125e-3f);
+          inv = __fdiv_rn(1.0f, deq);
         } else {
           const int e = max(mx_block_exp(amax), -26);  // the scale's max(., 1e-8): ceil(log2(1e-8)) = -26
           sbyte = static_cast<uint32_t>(e + 127);
@@ -487,6 +498,10 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
           // 16-byte chunk g/2 of the row holds blocks 2*(g/2), 2*(g/2)+1
           sts64(prow + (((g >> 1) ^ swz) << 4) + (g & 1) * 8, w[0], w[1]);
           sfw[g >> 2] |= sbyte << (8 * (g & 3));
+        } else if (kE4S32) {
+          // block g fills 16-element scale slots 2g and 2g+1
+          sts128(prow + ((g ^ swz) << 4), w[0], w[1], w[2], w[3]);
+          sfw[g >> 1] |= (sbyte * 0x101u) << (16 * (g & 1));
         } else {
           sts128(prow + ((g ^ swz) << 4), w[0], w[1], w[2], w[3]);
           sfw[0] |= sbyte << (8 * g);
@@ -494,7 +509,7 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
       }
       l_run += lq;
       sts32(psf, sfw[0]);
-      if (kNV) sts32(psf + SF_CHUNK, sfw[1]);
+      if (kNV || kE4S32) sts32(psf + SF_CHUNK, sfw[1]);
     }
     // O holds PV(0 .. j-1): rescale it by alpha once PV(j-1) has completed and
     // before PV(j) is issued (p_full).  All four column chunks in flight at once.
@@ -573,7 +588,7 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
                        const uint8_t* __restrict__ ksf, const uint8_t* __restrict__ vsf,
                        const float* __restrict__ ds, __nv_bfloat16* __restrict__ out, Params p,
                        int* status) {
-  constexpr bool kNVq = kQK == F_NV4, kNVp = kPV == F_NV4;   // two scale chunks per tile
+  constexpr bool kNVq = fmt_block16(kQK), kNVp = fmt_block16(kPV);   // two scale chunks per tile
   constexpr bool kQ8 = kQK == F_MX8, kP8 = kPV == F_MX8;     // 128-byte code rows
   using Lay = FLay<kQK, kPV>;
   constexpr int STAGES = Lay::STAGES;
@@ -781,6 +796,7 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   QDQ_FLASH(F_MX4, F_MX8, true)    // mixed_fp4qk_fp8pv (+ _vs)
   QDQ_FLASH(F_MX8, F_MX4, false)   // mixed_mxfp8qk_mxfp4pv_hw
   QDQ_FLASH(F_MX4, F_MX8, false)   // mixed_mxfp4qk_mxfp8pv_hw
+  QDQ_FLASH(F_NV4B32, F_NV4B32, true)  // mxfp4_s1_e4m3
 #undef QDQ_FLASH
   return fail(QDQ_ERR_UNSUPPORTED, "sage3 flash: no kernel for formats (%d, %d, emulated %d)", pr.qk_fmt, pr.pv_fmt,
               pr.emulated);

@@ -25,7 +25,8 @@
 //   qmean  bf16 [BH, G, D]        Q group means
 //   qc, kc uint8 [BH*Lp, D/2]     E2M1 codes (element 2j low nibble), or [BH*Lp, D] E4M3
 //   qsf, ksf                      block scales, 1024 bytes per 128 rows: two 512-byte tcgen05
-//                                 scale chunks (NVFP4: 8 E4M3 per row; MXFP4: 4 E8M0 in the first)
+//                                 scale chunks (NVFP4: 8 E4M3 per row; MXFP4: 4 E8M0 in the first;
+//                                 E4M3 per 32: 4 scales, each in two adjacent 16-element slots)
 //   vt     uint8 [BH*D, Lp/2]     V transposed: row (bh, d), keys packed along the row
 //                                 ([BH*D, Lp] for E4M3)
 //   vsf                           1024 bytes per (bh, key tile): 128 d-rows x (4 E8M0 | 8 E4M3)
@@ -148,6 +149,30 @@ __device__ __forceinline__ uint32_t nv_quant16(const float* v, uint8_t* out) {
   return sbyte;
 }
 
+// Quantise 32 floats with one E4M3 scale (the reference's mxfp4_s1_e4m3
+// QuantConfig, sage3/quant_config.py:246-255 through quantize.py:21-81): the
+// nv_quant16 steps over a block of 32.  Writes 16 code bytes, returns the
+// E4M3 scale byte.
+__device__ __forceinline__ uint32_t nv_quant32(const float* v, uint8_t* out) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const float sc = fmaxf(bf16_round(amax / 6.0f), 1e-8f);
+  const uint32_t sbyte = e4m3_byte(sc);
+  const float s = round_e4m3(sc);
+  const float inv = s > 0.f ? 1.0f / s : 0.f;
+  uint32_t w[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) word |= e2m1_rna(v[q * 8 + i] * inv) << (4 * i);
+    w[q] = word;
+  }
+  *reinterpret_cast<uint4*>(out) = make_uint4(w[0], w[1], w[2], w[3]);
+  return sbyte;
+}
+
 __device__ __forceinline__ int64_t nhd_row(int b, int n, int h, int64_t sb, int64_t sn, int64_t sh) {
   return b * sb + n * sn + h * sh;
 }
@@ -168,8 +193,8 @@ __global__ void __launch_bounds__(128) ksum_kernel(const __nv_bfloat16* __restri
 // ---------------------------------------------------------------- Q / K quantisation
 // grid (BH, Lp/128), 256 threads.  Loads one 128-row x 128-d tile, subtracts
 // the mean (Q: the tile's own group mean, written to qmean; K: ksum / L),
-// rounds to bf16 and quantises each row along D into 4 MX groups.
-template <bool kIsQ, bool kNV, bool kF8 = false>
+// rounds to bf16 and quantises each row along D in format kFmt.
+template <bool kIsQ, int kFmt>
 __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __restrict__ x, int H, int L, int Lp,
                                                        int64_t sb, int64_t sn, int64_t sh,
                                                        const float* __restrict__ ksum, __nv_bfloat16* __restrict__ qmean,
@@ -204,9 +229,11 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
     mean[d] = m;
   }
   __syncthreads();
-  // (row, group) items: MXFP4 4 groups of 32 per row, NVFP4 8 groups of 16.
-  // Scale chunks: 1024 bytes per 128-row tile (MXFP4 uses the first 512).
+  // (row, group) items: 4 groups of 32 per row, NVFP4 8 groups of 16.
+  // Scale chunks: 1024 bytes per 128-row tile (the E8M0 formats use the first
+  // 512; F_NV4B32 writes each scale into both 16-element slots of its group).
   uint8_t* sft = sf + (static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 1024;
+  constexpr bool kNV = kFmt == F_NV4, kF8 = kFmt == F_MX8;
   constexpr int kGroups = kNV ? 8 : 4, kGs = kNV ? 16 : 32;
   for (int it = threadIdx.x; it < 128 * kGroups; it += 256) {
     const int r = it / kGroups, g = it % kGroups;
@@ -219,16 +246,22 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
     }
     uint8_t* crow = kF8 ? codes + (static_cast<int64_t>(bh) * Lp + n) * 128 + g * 32
                         : codes + (static_cast<int64_t>(bh) * Lp + n) * 64 + g * (kGs / 2);
-    const uint32_t e = kF8 ? mx8_quant32(v, crow) : (kNV ? nv_quant16(v, crow) : mx_quant32(v, crow));
-    sft[(g / 4) * 512 + (r % 32) * 16 + (r / 32) * 4 + (g % 4)] = static_cast<uint8_t>(e);
+    if (kFmt == F_NV4B32) {
+      const uint32_t e = nv_quant32(v, crow);
+      *reinterpret_cast<uint16_t*>(sft + (g / 2) * 512 + (r % 32) * 16 + (r / 32) * 4 + 2 * (g % 2)) =
+          static_cast<uint16_t>(e * 0x101u);
+    } else {
+      const uint32_t e = kF8 ? mx8_quant32(v, crow) : (kNV ? nv_quant16(v, crow) : mx_quant32(v, crow));
+      sft[(g / 4) * 512 + (r % 32) * 16 + (r / 32) * 4 + (g % 4)] = static_cast<uint8_t>(e);
+    }
   }
 }
 
 // ---------------------------------------------------------------- V quantisation
 // grid (BH, Lp/128), 128 threads: thread d quantises V[:, d] over the tile's
-// 128 keys in 4 groups of 32 and writes 64 (E2M1) or 128 (E4M3) code bytes of
-// row (bh, d) of V^T.
-template <bool kNV, bool kF8 = false>
+// 128 keys in groups of 32 (NVFP4: 16) in format kFmt and writes 64 (E2M1)
+// or 128 (E4M3) code bytes of row (bh, d) of V^T.
+template <int kFmt>
 __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __restrict__ v, int H, int L, int Lp,
                                                       int64_t sb, int64_t sn, int64_t sh,
                                                       uint8_t* __restrict__ vt, uint8_t* __restrict__ vsf,
@@ -245,6 +278,7 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
   }
   __syncthreads();
   const int d = threadIdx.x;
+  constexpr bool kF8 = kFmt == F_MX8;
   // V smoothing (transforms.py v_smoothing): quantise bf16(v - mean_L(v)); the
   // flash epilogue adds the mean back.  Padding rows stay zero.
   float vm = 0.f;
@@ -257,7 +291,18 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
   uint8_t* row = kF8 ? vt + (static_cast<int64_t>(bh) * 128 + d) * Lp + blockIdx.y * 128
                      : vt + (static_cast<int64_t>(bh) * 128 + d) * (Lp / 2) + blockIdx.y * 64;
   uint8_t* sft = vsf + (static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 1024 + (d % 32) * 16 + (d / 32) * 4;
-  if (kNV) {
+  if (kFmt == F_NV4B32) {
+    uint32_t sfw[2] = {0, 0};
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      float x[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(tile[g * 32 + i][d]);
+      sfw[g / 2] |= (nv_quant32(x, row + g * 16) * 0x101u) << (16 * (g % 2));
+    }
+    *reinterpret_cast<uint32_t*>(sft) = sfw[0];
+    *reinterpret_cast<uint32_t*>(sft + 512) = sfw[1];
+  } else if (kFmt == F_NV4) {
     uint32_t sfw[2] = {0, 0};
 #pragma unroll 1
     for (int g = 0; g < 8; ++g) {
@@ -400,26 +445,30 @@ int launch_prepass(const Problem& p, const Workspace& w, cudaStream_t s) {
     ksum_kernel<<<dim3(BH, (p.L + 1023) / 1024), 128, 0, s>>>(p.v, p.H, p.L, p.v_sb, p.v_sn, p.v_sh, w.vsum);
   }
   // Q and K in the Q/K format
-#define QDQ_QK(NV, F8)                                                                                        \
-  qk_quant_kernel<true, NV, F8><<<dim3(BH, T), 256, 0, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh, w.ksum, \
-                                                            w.qmean, w.qc, w.qsf, p.smoothing);                \
-  qk_quant_kernel<false, NV, F8><<<dim3(BH, T), 256, 0, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh,       \
-                                                             w.ksum, w.qmean, w.kc, w.ksf, p.smoothing)
-  if (p.qk_fmt == F_MX8) { QDQ_QK(false, true); }
-  else if (p.qk_fmt == F_NV4) { QDQ_QK(true, false); }
-  else { QDQ_QK(false, false); }
+#define QDQ_QK(FMT)                                                                                          \
+  qk_quant_kernel<true, FMT><<<dim3(BH, T), 256, 0, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh, w.ksum,     \
+                                                         w.qmean, w.qc, w.qsf, p.smoothing);                    \
+  qk_quant_kernel<false, FMT><<<dim3(BH, T), 256, 0, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh, w.ksum,    \
+                                                          w.qmean, w.kc, w.ksf, p.smoothing)
+  switch (p.qk_fmt) {
+    case F_MX8: QDQ_QK(F_MX8); break;
+    case F_NV4: QDQ_QK(F_NV4); break;
+    case F_NV4B32: QDQ_QK(F_NV4B32); break;
+    default: QDQ_QK(F_MX4); break;
+  }
 #undef QDQ_QK
   // V^T in the P/V format
   const float* vs = p.vsmooth ? w.vsum : nullptr;
-  if (p.pv_fmt == F_MX8)
-    v_quant_kernel<false, true><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf,
-                                                           vs, w.vmean);
-  else if (p.pv_fmt == F_NV4)
-    v_quant_kernel<true><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf, vs,
-                                                    w.vmean);
-  else
-    v_quant_kernel<false><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf, vs,
-                                                     w.vmean);
+#define QDQ_V(FMT)                                                                                           \
+  v_quant_kernel<FMT><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf, vs, \
+                                                  w.vmean)
+  switch (p.pv_fmt) {
+    case F_MX8: QDQ_V(F_MX8); break;
+    case F_NV4: QDQ_V(F_NV4); break;
+    case F_NV4B32: QDQ_V(F_NV4B32); break;
+    default: QDQ_V(F_MX4); break;
+  }
+#undef QDQ_V
   if (p.smoothing) {
     const int smem = (128 + 64) * DS_LD * 2;
     static bool attr[64] = {false};

@@ -33,7 +33,9 @@ Config mapping:
               added back to the output).
   "mixed_mxfp8qk_mxfp4pv_hw", "mixed_mxfp4qk_mxfp8pv_hw"   the mixed hardware
               kernels (hardware P handling, no QK smoothing).
-  "mxfp4_s1_e4m3" (E4M3 scales per 32) has no kernel in this build.
+  "mxfp4_s1_e4m3"  E2M1 with E4M3 scales per 32 (Q/K/V and single-level
+              P), run on the NVFP4 block16 MMA with each scale in both of its
+              16-element slots.
 The kernels read the NHD or HND strides they are given; no transposing copies.
 """
 
@@ -70,7 +72,7 @@ ATTENTION_CONFIGS: dict[str, int] = {
     "mxfp4_hw": 0, "nvfp4": 1, "mxfp4": 2, "mxfp4_s1_2level": 2, "mxfp8_hw": 3,
     "mxfp4_s1": 4, "mxfp8_s1": 5, "mixed_fp8qk_fp4pv": 6, "mixed_fp4qk_fp8pv": 7,
     "mixed_mxfp8qk_mxfp4pv_hw": 8, "mixed_mxfp4qk_mxfp8pv_hw": 9,
-    "mxfp4_s1_vsmooth": 4, "mixed_fp8qk_fp4pv_vs": 6, "mixed_fp4qk_fp8pv_vs": 7,
+    "mxfp4_s1_vsmooth": 4, "mixed_fp8qk_fp4pv_vs": 6, "mixed_fp4qk_fp8pv_vs": 7, "mxfp4_s1_e4m3": 10,
 }
 # V smoothing (transforms.py v_smoothing: V mean subtracted before quantisation,
 # added back to the output).
@@ -86,7 +88,7 @@ REFERENCE_CONFIG_NAMES = (
 # Names the reference registers that this build has no kernel for.
 _OTHER_REFERENCE_CONFIGS = tuple(n for n in REFERENCE_CONFIG_NAMES if n not in ATTENTION_CONFIGS)
 
-_BUILT_FORMATS = tuple(range(10))  # variants with a kernel in this build
+_BUILT_FORMATS = tuple(range(11))  # variants with a kernel in this build
 
 
 def _get_env_bool(name: str, default: str = "0") -> bool:
