@@ -51,7 +51,7 @@ struct Workspace {
   uint8_t* ksf;           // [BH * Lp / 128, 1024]
   uint8_t* vt;            // [BH * 128, Lp / 2] (E2M1) or [BH * 128, Lp] (E4M3)
   uint8_t* vsf;           // [BH * Lp / 128, 1024]
-  float* ds;              // [BH, G, Lp] (bf16-rounded values, stored as fp32)
+  __nv_bfloat16* ds;      // [BH, G, Lp]
   float* vsum;            // [BH, 128] per-channel sums of v (V smoothing)
   float* vmean;           // [BH, 128] bf16(vsum / L), stored as fp32
 };
@@ -78,7 +78,7 @@ inline int64_t carve(int B, int H, int L, uint8_t* base, Workspace* w) {
   uint8_t* ksf = take(BH * G * 1024);
   uint8_t* vt = take(BH * 128 * Lp);
   uint8_t* vsf = take(BH * G * 1024);
-  uint8_t* ds = take(BH * G * Lp * 4);
+  uint8_t* ds = take(BH * G * Lp * 2);
   uint8_t* vsum = take(BH * 128 * 4);
   uint8_t* vmean = take(BH * 128 * 4);
   if (w) {
@@ -90,7 +90,7 @@ inline int64_t carve(int B, int H, int L, uint8_t* base, Workspace* w) {
     w->ksf = ksf;
     w->vt = vt;
     w->vsf = vsf;
-    w->ds = reinterpret_cast<float*>(ds);
+    w->ds = reinterpret_cast<__nv_bfloat16*>(ds);
     w->vsum = reinterpret_cast<float*>(vsum);
     w->vmean = reinterpret_cast<float*>(vmean);
   }

@@ -20,20 +20,30 @@
 // CTA = two 128-row query tiles (A, B) of one (batch, head) that share every
 // K/V tile, 12 warps:
 //   warps 0-3     softmax A: one thread per query row (TMEM lane): S -> registers,
-//                 + delta_s, block maxima (the row max and each block's max
+//                 block maxima (the row max and each block's max
 //                 of p follow from them), O_A rescale in TMEM when the max
 //                 grows, exp2, row sum, P -> E2M1 codes + block scales in
 //                 shared memory; epilogue O_A / l -> bf16 NHD
 //   warps 4-7     softmax B (the same for tile B)
-//   warp 8        MMA issuer: per key tile j, S = Q_A K_j^T, then (once A has
-//                 read S) S = Q_B K_j^T, then O_A += P_A V_{j-1}, O_B += P_B V_{j-1}
+//   warp 8        MMA issuer: per key tile j, S = delta_s_A + Q_A K_j^T, then
+//                 (once A has read S) S = delta_s_B + Q_B K_j^T, then
+//                 O_A += P_A V_{j-1}, O_B += P_B V_{j-1}
 //   warp 9        TMA producer: K tile [128 keys x 64 B], V^T tile [128 d x 64 B]
 //                 (64-byte swizzle; E4M3: 128 B rows, 128-byte swizzle), their
-//                 scale chunks and both tiles' delta_s slices (128 fp32 each)
-//                 into a 4-stage ring (3 for E4M3); Q_A, Q_B once
+//                 scale chunks and the two tiles' delta_s rows (bf16) into a
+//                 4-stage ring (3 for E4M3); Q_A, Q_B once
 //   warps 10-11   idle (they complete the third warpgroup for setmaxnreg)
 // The single S buffer alternates between the two softmax warpgroups, which
 // therefore run out of phase and overlap their MUFU / FMA / ALU work.
+// delta_s on the tensor core: with QK smoothing, S starts as one bf16 MMA
+// (kind::f16, K = 16) of a constant "ones" operand by the stage's delta_s tile,
+// and the block-scaled QK MMAs accumulate onto it.  A_t (128 x 16, K-major, no
+// swizzle) is 1 in column t and 0 elsewhere; B (128 keys x 16, MN-major,
+// 128-byte swizzle) holds delta_s of query group qtA in K-row 0 and of qtA + 1
+// in K-row 1 (one 2-row TMA box per 64 keys), rows 2-15 zero, so
+// A_t x B^T = delta_s of tile t broadcast over its 128 query rows.  The
+// reference adds delta_s to the fp32 scores after the QK product; here it is
+// the accumulator's initial value, the same sum in another order.
 // Registers: softmax warpgroups 224 per thread, the rest 56 (setmaxnreg;
 // 2 x 128 x 224 + 128 x 56 = 384 x 168, the launch allocation).
 // TMEM: S [0,128) O_A [128,256) O_B [256,384), scale factors [384,432).
@@ -49,7 +59,11 @@ constexpr int BM = 128, BN = 128, HD = 128;
 constexpr int MAX_STAGES = 4;
 constexpr int SF_CHUNK = 512;
 constexpr int SF_TILE = 1024;        // scale bytes per 128-row tile in global memory (two chunks)
-constexpr int DS_BYTES = BN * 4;     // delta_s slice of one query tile: 128 fp32
+constexpr int DS_TILE = 2048;        // delta_s MMA operand: two 1 KB 128-byte-swizzle atoms of 64 keys
+constexpr int DS_TX = 2 * 2 * 64 * 2;  // bytes the two 64-key x 2-row delta_s boxes bring per stage
+constexpr int ONES_TILE = 2048;      // "ones" MMA operand of one query tile: 128 rows x 16 B
+constexpr int ZERO_TILE = 2048;      // zero K-rows 8-15 of both delta_s MMA operands
+constexpr uint32_t IDESC_DS = idesc_bf16(BM, BN, true);
 constexpr int THREADS = 384;
 constexpr int TMEM_COLS = 512;
 // scale-factor columns: 8 per operand (NVFP4: two chunks; MXFP4 uses the first 4)
@@ -70,8 +84,8 @@ struct Bars {
 
 // Shared-memory layout for Q/K rows of QKR bytes and P/V rows of PVR bytes
 // (64 for E2M1, 128 for E4M3).
-// stage: K codes | V codes | K sf | V sf | delta_s A | delta_s B
-// CTA: Q_A | Q_B | P_A[2] | P_B[2] | stages | Q sf A,B | P sf A[2],B[2] | barriers
+// stage: K codes | V codes | K sf | V sf | delta_s tile
+// CTA: Q_A | Q_B | P_A[2] | P_B[2] | stages | Q sf A,B | P sf A[2],B[2] | ones A,B | zeros | barriers
 // P (codes and scales) is double-buffered per query tile: key tile j writes
 // buffer j & 1 while PV(j-1) may still read the other one.
 template <int QKR, int PVR>
@@ -80,16 +94,22 @@ struct FL {
   static constexpr int PV_TILE = 128 * PVR;   // a P or V^T tile
   static constexpr int ST_K = 0, ST_V = QK_TILE, ST_KSF = QK_TILE + PV_TILE, ST_VSF = ST_KSF + SF_TILE,
                        ST_DS = ST_VSF + SF_TILE;
-  static constexpr int STAGE_BYTES = (ST_DS + 2 * DS_BYTES + 1023) / 1024 * 1024;
+  static constexpr int STAGE_BYTES = (ST_DS + DS_TILE + 1023) / 1024 * 1024;
   static constexpr int OFF_Q = 0, OFF_P = 2 * QK_TILE, OFF_STAGE = 2 * QK_TILE + 4 * PV_TILE;
-  static constexpr int FIXED = 1024 + OFF_STAGE + 6 * SF_TILE + static_cast<int>(sizeof(Bars));
+  static constexpr int FIXED =
+      1024 + OFF_STAGE + 6 * SF_TILE + 2 * ONES_TILE + ZERO_TILE + static_cast<int>(sizeof(Bars));
   static constexpr int STAGES = (227 * 1024 - FIXED) / STAGE_BYTES < MAX_STAGES
                                     ? (227 * 1024 - FIXED) / STAGE_BYTES : MAX_STAGES;
   static constexpr int OFF_QSF = OFF_STAGE + STAGES * STAGE_BYTES;
   static constexpr int OFF_PSF = OFF_QSF + 2 * SF_TILE;
-  static constexpr int OFF_BAR = OFF_PSF + 4 * SF_TILE;
+  static constexpr int OFF_ONES = OFF_PSF + 4 * SF_TILE;
+  static constexpr int OFF_ZERO = OFF_ONES + 2 * ONES_TILE;  // above every tile whose descriptor points here
+  static constexpr int OFF_BAR = OFF_ZERO + ZERO_TILE;
   static constexpr size_t SMEM_BYTES = 1024 + OFF_BAR + sizeof(Bars);
   static_assert(STAGES >= 2 && SMEM_BYTES <= 227 * 1024, "flash layout");
+  static_assert(ST_DS % 1024 == 0 && STAGE_BYTES % 1024 == 0 && OFF_STAGE % 1024 == 0 && OFF_ZERO % 1024 == 0,
+                "128-byte-swizzle atoms of the delta_s operands must be 1024-byte aligned");
+  static_assert(OFF_ZERO - OFF_STAGE < (1 << 18), "descriptor byte offsets are 14-bit multiples of 16");
 };
 __host__ __device__ constexpr int fmt_row(int f) { return f == F_MX8 ? 128 : 64; }
 template <int kQK, int kPV>
@@ -136,11 +156,6 @@ __device__ __forceinline__ void sts64(uint32_t a, uint32_t x, uint32_t y) {
 }
 __device__ __forceinline__ void sts32(uint32_t a, uint32_t x) {
   asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(x) : "memory");
-}
-__device__ __forceinline__ float4 lds128f(uint32_t a) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a) : "memory");
-  return v;
 }
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -272,11 +287,9 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
   float m_run = -INFINITY, l_run = 0.f;
   bool ok = true;
   for (int j = 0; j < nkv; ++j) {
-    const int s = j % Lay::STAGES;
     // After a failed (timed-out) wait the thread stops waiting but keeps
     // iterating, so the other roles are never left waiting on it.
-    if (ok) ok = mbar_wait(&bars->s_full[wg], j & 1, status, 0x1301) &&
-                 mbar_wait(&bars->kv_full[s], (j / Lay::STAGES) & 1, status, 0x1302);
+    if (ok) ok = mbar_wait(&bars->s_full[wg], j & 1, status, 0x1301);
     ok = __all_sync(0xffffffffu, ok);  // warp-uniform: the TMEM accesses below are .sync.aligned
     tc_fence_after();
     float x[BN];
@@ -290,19 +303,6 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     tmem_ld_wait();
     tc_fence_before();
     mbar_arrive(&bars->s_free[wg]);
-    if (p.smoothing) {  // + delta_s[key]: one fp32 row shared by the whole tile (broadcast loads)
-      const uint32_t dsv = sbase + Lay::OFF_STAGE + s * Lay::STAGE_BYTES + Lay::ST_DS + wg * DS_BYTES;
-#pragma unroll
-      for (int c = 0; c < BN / 4; ++c) {
-        const float4 d = lds128f(dsv + 16 * c);
-        const float2 a = add_f32x2(make_float2(x[4 * c], x[4 * c + 1]), make_float2(d.x, d.y));
-        const float2 b = add_f32x2(make_float2(x[4 * c + 2], x[4 * c + 3]), make_float2(d.z, d.w));
-        x[4 * c] = a.x;
-        x[4 * c + 1] = a.y;
-        x[4 * c + 2] = b.x;
-        x[4 * c + 3] = b.y;
-      }
-    }
     // masking: keys beyond L (last tile) and, if causal, keys after the query
     const int key0 = j * BN;
     const int lim = p.causal ? min(p.L - key0, qrow - key0 + 1) : p.L - key0;
@@ -584,10 +584,9 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
 template <int kQK, int kPV, bool kEmu>
 __global__ void __launch_bounds__(THREADS, 1)
 sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                       const __grid_constant__ CUtensorMap map_v, const uint8_t* __restrict__ qsf,
-                       const uint8_t* __restrict__ ksf, const uint8_t* __restrict__ vsf,
-                       const float* __restrict__ ds, __nv_bfloat16* __restrict__ out, Params p,
-                       int* status) {
+                       const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_ds,
+                       const uint8_t* __restrict__ qsf, const uint8_t* __restrict__ ksf,
+                       const uint8_t* __restrict__ vsf, __nv_bfloat16* __restrict__ out, Params p, int* status) {
   constexpr bool kNVq = fmt_block16(kQK), kNVp = fmt_block16(kPV);   // two scale chunks per tile
   constexpr bool kQ8 = kQK == F_MX8, kP8 = kPV == F_MX8;     // 128-byte code rows
   using Lay = FLay<kQK, kPV>;
@@ -622,6 +621,22 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
     prefetch_tmap(&map_q);
     prefetch_tmap(&map_k);
     prefetch_tmap(&map_v);
+    if (p.smoothing) prefetch_tmap(&map_ds);
+  }
+  if (p.smoothing) {
+    // delta_s MMA operands: every stage's delta_s tile and the zero tile start
+    // at zero (the TMA writes only K-rows 0-1 of each atom); ones tile t has
+    // bf16 1.0 in column t of each 16-byte row
+    for (int s = 0; s < STAGES; ++s)
+      for (int i = threadIdx.x; i < DS_TILE / 16; i += THREADS)
+        *reinterpret_cast<uint4*>(smem + Lay::OFF_STAGE + s * Lay::STAGE_BYTES + Lay::ST_DS + 16 * i) =
+            make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < (2 * ONES_TILE + ZERO_TILE) / 16; i += THREADS) {
+      const int t = i / (ONES_TILE / 16);  // 0, 1: ones tiles; 2: zero tile
+      *reinterpret_cast<uint4*>(smem + Lay::OFF_ONES + 16 * i) =  // element t of the row = 1.0 (0x3F80)
+          make_uint4(t == 0 ? 0x00003F80u : (t == 1 ? 0x3F800000u : 0u), 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();  // visible to the TMA unit and the tensor core
   }
   if (warp == 8) {
     tmem_alloc(&bars->tmem_base, TMEM_COLS);
@@ -656,7 +671,7 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
           }
           if (*(volatile int*)&bars->abort) break;
           uint8_t* st = smem + Lay::OFF_STAGE + s * Lay::STAGE_BYTES;
-          const uint32_t bytes = Lay::QK_TILE + Lay::PV_TILE + kSfQK + kSfPV + (p.smoothing ? nq * DS_BYTES : 0);
+          const uint32_t bytes = Lay::QK_TILE + Lay::PV_TILE + kSfQK + kSfPV + (p.smoothing ? DS_TX : 0);
           mbar_arrive_expect_tx(&bars->kv_full[s], bytes);
           tma_load_2d(st + Lay::ST_K, &map_k, 0, bh * p.Lp + j * BN, &bars->kv_full[s]);
           tma_load_2d(st + Lay::ST_V, &map_v, j * (kP8 ? BN : BN / 2), bh * HD, &bars->kv_full[s]);
@@ -664,10 +679,9 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
                     &bars->kv_full[s]);
           bulk_load(st + Lay::ST_VSF, vsf + (static_cast<int64_t>(bh) * p.T + j) * SF_TILE, kSfPV,
                     &bars->kv_full[s]);
-          if (p.smoothing)
-            for (int t = 0; t < nq; ++t)
-              bulk_load(st + Lay::ST_DS + t * DS_BYTES, ds + (static_cast<int64_t>(bh) * p.T + qtA + t) * p.Lp + j * BN,
-                        DS_BYTES, &bars->kv_full[s]);
+          if (p.smoothing)  // delta_s rows qtA, qtA + 1 (zero-filled past the last row) of keys j*128 + [0, 128)
+            for (int h = 0; h < 2; ++h)
+              tma_load_2d(st + Lay::ST_DS + h * 1024, &map_ds, j * BN + h * 64, bh * p.T + qtA, &bars->kv_full[s]);
           ++issued;
         }
         mbar_wait(&bars->q_full, 0, status, 0x1102);
@@ -711,8 +725,17 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
             if (prev_j >= 0 && !mbar_wait(&bars->s_free[prev], prev_j & 1, status, 0x1204)) { ok = false; break; }
             tc_fence_after();
             if (w == 0) cp_sf<kNVq>(tmem + T_SFK, st + Lay::ST_KSF);
+            if (p.smoothing) {  // S = delta_s of this tile's query group
+              const uint32_t a_addr = smem_u32(smem + Lay::OFF_ONES + w * ONES_TILE);
+              const uint32_t b_addr = smem_u32(st + Lay::ST_DS);
+              const uint32_t z_addr = smem_u32(smem + Lay::OFF_ZERO);
+              // A: K-major, no swizzle: 8-row core matrices 128 B apart (SBO), K-rows 8-15 -> zeros (LBO)
+              // B: MN-major, 128-byte swizzle: 64-key atoms 1024 B apart (LBO), K-rows 8-15 -> zeros (SBO)
+              mma_f16(tmem + T_S, smem_desc(a_addr, z_addr - a_addr, 128, 0), smem_desc(b_addr, 1024, z_addr - b_addr, 2),
+                      IDESC_DS, 0);
+            }
             mma_k128<kQK>(tmem + T_S, code_desc(kQ8, smem + Lay::OFF_Q + w * Lay::QK_TILE),
-                          code_desc(kQ8, st + Lay::ST_K), tmem + T_SFQ + w * 8, tmem + T_SFK, false);
+                          code_desc(kQ8, st + Lay::ST_K), tmem + T_SFQ + w * 8, tmem + T_SFK, p.smoothing != 0);
             tc_commit(&bars->s_full[w]);
           }
           if (!ok) break;
@@ -736,8 +759,8 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
 }
 
 template <int kQK, int kPV, bool kEmu>
-int launch_mode(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Workspace& w,
-                const Problem& pr, const Params& p, dim3 grid, int* status, cudaStream_t s) {
+int launch_mode(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mds,
+                const Workspace& w, const Problem& pr, const Params& p, dim3 grid, int* status, cudaStream_t s) {
   constexpr size_t smem = FLay<kQK, kPV>::SMEM_BYTES;
   static bool attr[64] = {false};
   int dev = 0;
@@ -748,7 +771,7 @@ int launch_mode(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
     if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "sage3 flash: smem attribute: %s", cudaGetErrorString(e));
     attr[dev] = true;
   }
-  sage3_fp4_flash_kernel<kQK, kPV, kEmu><<<grid, THREADS, smem, s>>>(mq, mk, mv, w.qsf, w.ksf, w.vsf, w.ds, pr.o,
+  sage3_fp4_flash_kernel<kQK, kPV, kEmu><<<grid, THREADS, smem, s>>>(mq, mk, mv, mds, w.qsf, w.ksf, w.vsf, pr.o,
                                                                      p, status);
   return check_launch("sage3 flash");
 }
@@ -765,10 +788,13 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   if (status == nullptr) return QDQ_ERR_CUDA;
   const int64_t BH = static_cast<int64_t>(pr.B) * pr.H;
   const bool q8 = pr.qk_fmt == F_MX8, p8 = pr.pv_fmt == F_MX8;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mds;
   if (int st = code_map(&mq, w.qc, BH * pr.Lp, q8 ? 128 : 64, q8)) return st;
   if (int st = code_map(&mk, w.kc, BH * pr.Lp, q8 ? 128 : 64, q8)) return st;
   if (int st = code_map(&mv, w.vt, BH * HD, p8 ? pr.Lp : pr.Lp / 2, p8)) return st;
+  // delta_s [BH * G, Lp] bf16, boxes of 64 keys x 2 query groups, 128-byte swizzle
+  if (int st = make_tmap_u16_2d(&mds, w.ds, BH * (pr.Lp / 128), pr.Lp, static_cast<uint64_t>(pr.Lp) * 2, 64, 2, 128))
+    return st;
   Params p;
   p.H = pr.H;
   p.L = pr.L;
@@ -786,7 +812,7 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   dim3 grid(static_cast<unsigned>((p.T + 1) / 2), static_cast<unsigned>(BH));
 #define QDQ_FLASH(QK, PV, EMU)                                                             \
   if (pr.qk_fmt == QK && pr.pv_fmt == PV && (pr.emulated != 0) == EMU)                     \
-    return launch_mode<QK, PV, EMU>(mq, mk, mv, w, pr, p, grid, status, s);
+    return launch_mode<QK, PV, EMU>(mq, mk, mv, mds, w, pr, p, grid, status, s);
   QDQ_FLASH(F_MX4, F_MX4, false)   // mxfp4_hw
   QDQ_FLASH(F_MX4, F_MX4, true)    // mxfp4, mxfp4_s1 (+ vsmooth)
   QDQ_FLASH(F_NV4, F_NV4, true)    // nvfp4

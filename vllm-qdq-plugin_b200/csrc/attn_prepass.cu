@@ -30,7 +30,7 @@
 //   vt     uint8 [BH*D, Lp/2]     V transposed: row (bh, d), keys packed along the row
 //                                 ([BH*D, Lp] for E4M3)
 //   vsf                           1024 bytes per (bh, key tile): 128 d-rows x (4 E8M0 | 8 E4M3)
-//   ds     fp32 [BH, G, Lp]       delta_s, rounded to bf16 (the reference's dtype)
+//   ds     bf16 [BH, G, Lp]       delta_s (the reference's dtype)
 #include "attn_common.cuh"
 
 namespace qdqb200 {
@@ -328,9 +328,8 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
 
 // ---------------------------------------------------------------- delta_s
 // ds[bh, g, n] = bf16( sum_d qmean[bh, g, d] * kc[bh, n, d] ), kc = bf16(k - mean),
-// with bf16 tensor-core MMAs (mma.sync m16n8k16, fp32 accumulation); the
-// bf16-rounded values are stored as fp32 so the flash kernel adds them
-// without unpacking.
+// with bf16 tensor-core MMAs (mma.sync m16n8k16, fp32 accumulation), stored
+// as bf16 rows the flash kernel loads by TMA as an MMA operand.
 // grid (BH, Lp/128), 256 threads (8 warps).  The CTA keeps its 128 keys'
 // kc (bf16) in shared memory and walks the G groups 64 at a time; each warp
 // owns a 32 (g) x 32 (n) block of the 64 x 128 output chunk.
@@ -353,7 +352,7 @@ __global__ void __launch_bounds__(256) ds_kernel(const __nv_bfloat16* __restrict
                                                  int64_t sb, int64_t sn, int64_t sh,
                                                  const float* __restrict__ ksum,
                                                  const __nv_bfloat16* __restrict__ qmean,
-                                                 float* __restrict__ ds) {
+                                                 __nv_bfloat16* __restrict__ ds) {
   extern __shared__ __align__(16) uint8_t ds_smem[];
   __nv_bfloat16* kcs = reinterpret_cast<__nv_bfloat16*>(ds_smem);          // [128][DS_LD]
   __nv_bfloat16* qms = kcs + 128 * DS_LD;                                    // [64][DS_LD]
@@ -422,8 +421,8 @@ __global__ void __launch_bounds__(256) ds_kernel(const __nv_bfloat16* __restrict
           const int g = g0 + wm * 32 + mi * 16 + (lane >> 2) + hh * 8;
           const int n = n0 + wn * 32 + ni * 8 + (lane & 3) * 2;
           if (g < G) {
-            const float2 v = make_float2(bf16_round(acc[mi][ni][hh * 2]), bf16_round(acc[mi][ni][hh * 2 + 1]));
-            *reinterpret_cast<float2*>(ds + (static_cast<int64_t>(bh) * G + g) * Lp + n) = v;
+            *reinterpret_cast<__nv_bfloat162*>(ds + (static_cast<int64_t>(bh) * G + g) * Lp + n) =
+                __floats2bfloat162_rn(acc[mi][ni][hh * 2], acc[mi][ni][hh * 2 + 1]);
           }
         }
   }

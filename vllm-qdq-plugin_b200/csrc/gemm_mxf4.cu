@@ -539,7 +539,7 @@ int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
 }
 
 int make_tmap_u16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld_bytes,
-                     uint32_t box_cols, uint32_t box_rows) {
+                     uint32_t box_cols, uint32_t box_rows, int swizzle_bytes) {
   PFN_encodeTiled fn = encode_fn();
   if (fn == nullptr) return fail(QDQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld_bytes & 15))
@@ -549,8 +549,9 @@ int make_tmap_u16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t elem[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, elem,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(QDQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return QDQ_OK;
 }

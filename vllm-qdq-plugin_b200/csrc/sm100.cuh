@@ -201,6 +201,32 @@ __device__ __forceinline__ void mma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint6
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
       : "memory");
 }
+// D(tmem) (+)= A(smem) x B(smem)^T, 16-bit operands (kind::f16, K = 16).
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Instruction descriptor of kind::f16 with bf16 A and B, fp32 accumulation;
+// b_mn_major: B is MN-major (N contiguous) instead of K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(uint32_t M, uint32_t N, bool b_mn_major) {
+  return (1u << 4)                        // D format F32
+         | (1u << 7) | (1u << 10)         // A, B format BF16
+         | ((b_mn_major ? 1u : 0u) << 16)
+         | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+// Shared-memory matrix descriptor from its parts: leading / stride byte
+// offsets (multiples of 16) and the layout type (0 none, 2 128-byte swizzle,
+// 4 64-byte, 6 32-byte), sm100 descriptor version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(layout) << 61);
+}
 // Same with per-16 block scales (kind::mxf4nvf4, block16).
 __device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                          uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
@@ -373,10 +399,10 @@ __device__ __forceinline__ bool elect_one() {
 int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes,
                     uint64_t ld_bytes, uint32_t box_bytes, uint32_t box_rows, int swizzle_bytes);
 // The same for a row-major 16-bit matrix (rows x cols elements, row stride
-// ld_bytes), box of box_cols x box_rows elements, no swizzle; out-of-range
-// elements read as zero.
+// ld_bytes), box of box_cols x box_rows elements, no swizzle or (128) the
+// 128-byte swizzle; out-of-range elements read as zero.
 int make_tmap_u16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld_bytes,
-                     uint32_t box_cols, uint32_t box_rows);
+                     uint32_t box_cols, uint32_t box_rows, int swizzle_bytes = 0);
 // The same for 32-bit elements (used for 512-byte scale-factor chunks: 128
 // words per row).
 int make_tmap_u32_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld_bytes,
