@@ -47,6 +47,8 @@
 // Registers: softmax warpgroups 224 per thread, the rest 56 (setmaxnreg;
 // 2 x 128 x 224 + 128 x 56 = 384 x 168, the launch allocation).
 // TMEM: S [0,128) O_A [128,256) O_B [256,384), scale factors [384,432).
+#include <cmath>
+
 #include "attn_common.cuh"
 
 namespace qdqb200 {
@@ -125,6 +127,7 @@ struct Params {
   int causal;
   int smoothing;
   float p_prescale;      // emulated-config P prescale: 448*6 (two-level) or 1 (single-level _s1)
+  float p_prescale_lg2;  // log2(p_prescale)
   int vsmooth;           // the V mean was subtracted before quantisation: add it back to O / l
   const float* vmean;    // [BH, 128] the V means (bf16 values), when vsmooth
 };
@@ -162,6 +165,12 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
+}
+
+__device__ __forceinline__ float lg2_approx(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // 2^e as a float for e in [-127, 127] (2^-127 is the subnormal 0x00400000).
@@ -402,15 +411,16 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
       // e = clamp(ceil(log2(max(max p / 448, 1e-8))), -127, 127), E4M3 codes
       // of p * 2^-e (the fp8 cast, round-to-nearest-even); l += sum of the
       // dequantised P.
-      const float2 mneg2 = make_float2(-m_new, -m_new);
+      // The prescale and 2^-e are folded into the exponent:
+      // p * prescale * 2^-e = exp2(x * qk - m + log2(prescale) - e).
       uint32_t sfw = 0;
       float lq = 0.f;
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         const float amax = __fmul_rn(ex2_approx(fmaf(gm[g], qk, -m_new)), p.p_prescale);
         const int e = max(mx8_block_exp(amax), -26);  // ceil(log2(1e-8)) = -26
-        const float2 inv2 = make_float2(exp2i(-e), exp2i(-e));
-        const float2 ps2 = make_float2(p.p_prescale, p.p_prescale);
+        const float cg = p.p_prescale_lg2 - m_new - static_cast<float>(e);
+        const float2 c2 = make_float2(cg, cg);
         uint32_t w[8];
         float gsum = 0.f;
 #pragma unroll
@@ -419,10 +429,9 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
             const int n = g * 32 + q * 4 + 2 * i;
-            const float2 t = fma_f32x2(make_float2(x[n], x[n + 1]), qk2, mneg2);
-            const float2 pv = mul_f32x2(mul_f32x2(make_float2(ex2_approx(t.x), ex2_approx(t.y)), ps2), inv2);
-            v[2 * i] = pv.x;
-            v[2 * i + 1] = pv.y;
+            const float2 t = fma_f32x2(make_float2(x[n], x[n + 1]), qk2, c2);
+            v[2 * i] = ex2_approx(t.x);
+            v[2 * i + 1] = ex2_approx(t.y);
           }
           w[q] = cvt_e4m3x4(v[0], v[1], v[2], v[3]);
           gsum += e4m3x4_sum(w[q]);
@@ -439,44 +448,39 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
       // the two-level configs, which cancels in O / l; 1 for the single-level
       // _s1 ones), block-quantised; l += sum of the dequantised P.
       //   MXFP4: E8M0 2^e per 32, e = clamp(ceil(log2(max / 6)), -127, 127);
-      //   NVFP4: E4M3 per 16, s = e4m3(max(max / 6, 1e-8)).
-      // The block max of p * 2688 is round(max p * 2688) (rounding is monotone).
-      const float2 mneg2 = make_float2(-m_new, -m_new);
-      const float2 ps2 = make_float2(p.p_prescale, p.p_prescale);
-#pragma unroll
-      for (int i = 0; i < BN; i += 2) {
-        const float2 t = fma_f32x2(make_float2(x[i], x[i + 1]), qk2, mneg2);
-        const float2 v = mul_f32x2(make_float2(ex2_approx(t.x), ex2_approx(t.y)), ps2);
-        x[i] = v.x;
-        x[i + 1] = v.y;
-      }
+      //   NVFP4: E4M3 per 16, s = e4m3(max(max / 6, 1e-8));
+      //   E4M3 per 32: s = max(e4m3(max(max / 6, 1e-8)), 2^-9).
+      // The block max of p * prescale is round(max p * prescale) (rounding is
+      // monotone).  prescale / s is folded into the exponent:
+      // p * prescale / s = exp2(x * qk - m + log2(prescale) - log2(s)), log2(s)
+      // exact for the power-of-two scales and lg2.approx for the E4M3 ones
+      // (a zero E4M3 scale zeroes its block in the MMA; its codes are then
+      // taken at 2^-9).
       float lq = 0.f;
       uint32_t sfw[2] = {0u, 0u};
 #pragma unroll
       for (int g = 0; g < NG; ++g) {
         constexpr int GS = BN / NG;
         const float amax = __fmul_rn(ex2_approx(fmaf(gm[g], qk, -m_new)), p.p_prescale);
-        float inv, deq;
+        float deq, lg2s;
         uint32_t sbyte;
-        if (kNV) {
-          const float scl = fmaxf(__fdiv_rn(amax, 6.0f), 1e-8f);
+        if (kNV || kE4S32) {
+          const float scl = fmaxf(amax * (1.0f / 6.0f), 1e-8f);
           sbyte = e4m3_byte(scl);
           deq = round_e4m3(scl);
-          inv = deq > 0.f ? __fdiv_rn(1.0f, deq) : 0.f;
-        } else if (kE4S32) {
-          // p_quant_mxfp4_s1_e4m3: max(e4m3(max(b / 6, 1e-8)), 2^-9), the
-          // smallest E4M3 subnormal (byte 1)
-          const float scl = fmaxf(__fdiv_rn(amax, 6.0f), 1e-8f);
-          sbyte = max(e4m3_byte(scl), 1u);
-          deq = fmaxf(round_e4m3(scl), 1.953125e-3f);
-          inv = __fdiv_rn(1.0f, deq);
+          if (kE4S32) {  // p_quant_mxfp4_s1_e4m3 clamps at the smallest E4M3 subnormal (byte 1)
+            sbyte = max(sbyte, 1u);
+            deq = fmaxf(deq, 1.953125e-3f);
+          }
+          lg2s = lg2_approx(fmaxf(deq, 1.953125e-3f));
         } else {
           const int e = max(mx_block_exp(amax), -26);  // the scale's max(., 1e-8): ceil(log2(1e-8)) = -26
           sbyte = static_cast<uint32_t>(e + 127);
           deq = exp2i(e);
-          inv = exp2i(-e);
+          lg2s = static_cast<float>(e);
         }
-        const float2 inv2 = make_float2(inv, inv);
+        const float cg = p.p_prescale_lg2 - m_new - lg2s;
+        const float2 c2 = make_float2(cg, cg);
         __half2 hs = __floats2half2_rn(0.f, 0.f);
         uint32_t w[GS / 8];
 #pragma unroll
@@ -485,9 +489,9 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int n = g * GS + q * 8 + 2 * i;
-            const float2 sc = mul_f32x2(make_float2(x[n], x[n + 1]), inv2);
-            v[2 * i] = sc.x;
-            v[2 * i + 1] = sc.y;
+            const float2 t = fma_f32x2(make_float2(x[n], x[n + 1]), qk2, c2);
+            v[2 * i] = ex2_approx(t.x);
+            v[2 * i + 1] = ex2_approx(t.y);
           }
           uint32_t h[4];
           w[q] = e2m1_roundtrip8(v, h);
@@ -807,6 +811,7 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   p.causal = pr.causal;
   p.smoothing = pr.smoothing;
   p.p_prescale = pr.p_prescale;
+  p.p_prescale_lg2 = static_cast<float>(std::log2(static_cast<double>(pr.p_prescale)));
   p.vsmooth = pr.vsmooth;
   p.vmean = w.vmean;
   dim3 grid(static_cast<unsigned>((p.T + 1) / 2), static_cast<unsigned>(BH));
