@@ -22,6 +22,8 @@
 //
 // Outputs (workspace), with Lp = L rounded up to 128, BH = B*H, G = Lp/128:
 //   ksum   fp32 [BH, D]           per-channel sums of k (mean = bf16(ksum / L))
+//   (kernels: colsum_kernel for the K (and V) sums; the Q pass; the K pass,
+//   which also writes delta_s; the V pass)
 //   qmean  bf16 [BH, G, D]        Q group means
 //   qc, kc uint8 [BH*Lp, D/2]     E2M1 codes (element 2j low nibble), or [BH*Lp, D] E4M3
 //   qsf, ksf                      block scales, 1024 bytes per 128 rows: two 512-byte tcgen05
@@ -61,14 +63,6 @@ __device__ __forceinline__ int mx_group_exp(float amax) {
   return min(max(e, -127), 127);
 }
 
-// E2M1 code of v = x / 2^e with the reference's round-half-away thresholds
-// (mxfp4_hw_kernel.py:43-61): |v| clamped to 6.
-__device__ __forceinline__ uint32_t e2m1_rna(float v) {
-  const float a = fminf(fabsf(v), 6.0f);
-  uint32_t c = (a >= 0.25f) + (a >= 0.75f) + (a >= 1.25f) + (a >= 1.75f) + (a >= 2.5f) +
-               (a >= 3.5f) + (a >= 5.0f);
-  return c | (v < 0.0f ? 8u : 0u);
-}
 
 // 2^-e as an exact float (e in [-127, 127]; 2^127 for e = -127).
 __device__ __forceinline__ float exp2_neg(int e) {
@@ -77,24 +71,6 @@ __device__ __forceinline__ float exp2_neg(int e) {
                  : __uint_as_float(1u << (22 + be));
 }
 
-// Quantise 32 floats (one MX group): 16 code bytes into out[0..15], returns the E8M0 byte.
-__device__ __forceinline__ uint32_t mx_quant32(const float* v, uint8_t* out) {
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-  const int e = mx_group_exp(amax);
-  const float inv = exp2_neg(e);
-  uint32_t w[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint32_t word = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) word |= e2m1_rna(v[q * 8 + i] * inv) << (4 * i);
-    w[q] = word;
-  }
-  *reinterpret_cast<uint4*>(out) = make_uint4(w[0], w[1], w[2], w[3]);
-  return static_cast<uint32_t>(e + 127);
-}
 
 // E8M0 exponent of quantize_to_mxfp8 for a group whose |x| max is amax:
 // e = ceil(log2(a / 448)) with a = max(amax, 1e-12).  For a = M * 2^E
@@ -124,92 +100,181 @@ __device__ __forceinline__ uint32_t mx8_quant32(const float* v, uint8_t* out) {
   return static_cast<uint32_t>(min(max(e + 127, 0), 254));
 }
 
-// Quantise 16 floats (one NVFP4 block of the reference's nvfp4 QuantConfig,
-// sage3/quantize.py:21-81 with round_to_e4m3): scale = e4m3(bf16(amax / 6)
-// clamped below at 1e-8), codes of x / scale with round-half-away thresholds
-// (the hardware E2M1 grid; the reference's emulation grid also has 0.75).
-// Writes 8 code bytes, returns the E4M3 scale byte (0 when the scale underflows).
-__device__ __forceinline__ uint32_t nv_quant16(const float* v, uint8_t* out) {
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-  const float sc = fmaxf(bf16_round(amax / 6.0f), 1e-8f);
-  const uint32_t sbyte = e4m3_byte(sc);
-  const float s = round_e4m3(sc);
-  const float inv = s > 0.f ? 1.0f / s : 0.f;
-  uint32_t w[2];
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    uint32_t word = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) word |= e2m1_rna(v[q * 8 + i] * inv) << (4 * i);
-    w[q] = word;
-  }
-  *reinterpret_cast<uint2*>(out) = make_uint2(w[0], w[1]);
-  return sbyte;
-}
 
-// Quantise 32 floats with one E4M3 scale (the reference's mxfp4_s1_e4m3
-// QuantConfig, sage3/quant_config.py:246-255 through quantize.py:21-81): the
-// nv_quant16 steps over a block of 32.  Writes 16 code bytes, returns the
-// E4M3 scale byte.
-__device__ __forceinline__ uint32_t nv_quant32(const float* v, uint8_t* out) {
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-  const float sc = fmaxf(bf16_round(amax / 6.0f), 1e-8f);
-  const uint32_t sbyte = e4m3_byte(sc);
-  const float s = round_e4m3(sc);
-  const float inv = s > 0.f ? 1.0f / s : 0.f;
-  uint32_t w[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint32_t word = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) word |= e2m1_rna(v[q * 8 + i] * inv) << (4 * i);
-    w[q] = word;
-  }
-  *reinterpret_cast<uint4*>(out) = make_uint4(w[0], w[1], w[2], w[3]);
-  return sbyte;
-}
 
 __device__ __forceinline__ int64_t nhd_row(int b, int n, int h, int64_t sb, int64_t sn, int64_t sh) {
   return b * sb + n * sn + h * sh;
 }
 
-// ---------------------------------------------------------------- K channel sums
-// grid (BH, ceil(L / 1024)), 128 threads: thread d sums k[b, n, h, d] over a chunk of keys.
-__global__ void __launch_bounds__(128) ksum_kernel(const __nv_bfloat16* __restrict__ k, int H, int L,
-                                                   int64_t sb, int64_t sn, int64_t sh,
-                                                   float* __restrict__ ksum) {
-  const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  const int d = threadIdx.x;
-  const int n0 = blockIdx.y * 1024, n1 = min(L, n0 + 1024);
-  float acc = 0.f;
-  for (int n = n0; n < n1; ++n) acc += __bfloat162float(k[nhd_row(b, n, h, sb, sn, sh) + d]);
-  atomicAdd(&ksum[bh * 128 + d], acc);
+// E8M0 group quantisers for inputs of bf16 precision (at most 8 significant
+// bits: q_s, k_c and V are bf16 values).  x * 2^-e is then exact, and its
+// distance to a midpoint between E2M1 values (0.25, 0.75, ... 5, at most 3
+// significant bits) is zero or at least 2^-8 relative.  Scaling by
+// (1 + 2^-12), also exact, lifts the midpoints themselves just above and moves
+// nothing else across one, so the hardware's round-to-nearest-even cvt yields
+// the reference's round-half-away codes (mxfp4_hw_kernel.py:43-61).  The
+// product is formed as fma(x, inv, +0), so an input of -0 encodes as +0 like
+// the reference's sign test x < 0 (a negative product that underflows to
+// zero keeps the negative-zero code; both dequantise to 0).
+__device__ __forceinline__ uint32_t mx_quant32_bf(const float* v, uint8_t* out) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const int e = mx_group_exp(amax);
+  const float inv = exp2_neg(e) * (1.0f + 1.0f / 4096.0f);
+  float s[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) s[i] = __fmaf_rn(v[i], inv, 0.0f);
+  uint32_t w[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    w[q] = cvt_e2m1x8(s[8 * q], s[8 * q + 1], s[8 * q + 2], s[8 * q + 3], s[8 * q + 4], s[8 * q + 5],
+                      s[8 * q + 6], s[8 * q + 7]);
+  *reinterpret_cast<uint4*>(out) = make_uint4(w[0], w[1], w[2], w[3]);
+  return static_cast<uint32_t>(e + 127);
 }
 
-// ---------------------------------------------------------------- Q / K quantisation
-// grid (BH, Lp/128), 256 threads.  Loads one 128-row x 128-d tile, subtracts
-// the mean (Q: the tile's own group mean, written to qmean; K: ksum / L),
-// rounds to bf16 and quantises each row along D in format kFmt.
+// |v| rounded to the E2M1 grid with ties away from zero, for any finite v
+// (the reference's thresholds 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5, |v|
+// clamped to 6, mxfp4_hw_kernel.py:43-61): the magnitude keeps 1 mantissa bit at or
+// above 1, none in [0.5, 1), and is 0 or 0.5 below; the sign is v < 0.  The
+// result is an E2M1 value, so cvt encodes it exactly.
+__device__ __forceinline__ float e2m1_rna_value(float v) {
+  const float a = fminf(fabsf(v), 6.0f);
+  const uint32_t b = __float_as_uint(a);
+  const uint32_t sh = b >= 0x3F800000u ? 22u : 23u;
+  float q = __uint_as_float((b + (1u << (sh - 1))) & ~((1u << sh) - 1u));
+  q = a >= 0.5f ? q : (a >= 0.25f ? 0.5f : 0.0f);
+  return v < 0.0f ? -q : q;
+}
+
+// E4M3-scaled blocks (nv_quant16 / nv_quant32 semantics) with the bit-level
+// round-half-away above: KB elements, KB / 2 code bytes, returns the scale byte.
+template <int KB>
+__device__ __forceinline__ uint32_t nv_quant_fast(const float* v, uint8_t* out) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < KB; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const float sc = fmaxf(bf16_round(amax / 6.0f), 1e-8f);
+  const uint32_t sbyte = e4m3_byte(sc);
+  const float s = round_e4m3(sc);
+  const float inv = s > 0.f ? 1.0f / s : 0.f;
+  uint32_t w[KB / 8];
+#pragma unroll
+  for (int q = 0; q < KB / 8; ++q)
+    w[q] = cvt_e2m1x8(e2m1_rna_value(v[8 * q] * inv), e2m1_rna_value(v[8 * q + 1] * inv),
+                      e2m1_rna_value(v[8 * q + 2] * inv), e2m1_rna_value(v[8 * q + 3] * inv),
+                      e2m1_rna_value(v[8 * q + 4] * inv), e2m1_rna_value(v[8 * q + 5] * inv),
+                      e2m1_rna_value(v[8 * q + 6] * inv), e2m1_rna_value(v[8 * q + 7] * inv));
+  if (KB == 16) *reinterpret_cast<uint2*>(out) = make_uint2(w[0], w[1]);
+  else *reinterpret_cast<uint4*>(out) = make_uint4(w[0], w[1], w[2 % (KB / 8)], w[3 % (KB / 8)]);
+  return sbyte;
+}
+
+// One group of a row in format kFmt: codes to `crow`, the scale byte(s) to the
+// tcgen05 scale chunk(s) at sft (row r, group g of the tile).
+template <int kFmt>
+__device__ __forceinline__ void quant_group(const float* v, uint8_t* crow, uint8_t* sft, int r, int g) {
+  const int slot = (r % 32) * 16 + (r / 32) * 4;
+  if (kFmt == F_MX8) {
+    sft[slot + g] = static_cast<uint8_t>(mx8_quant32(v, crow));
+  } else if (kFmt == F_NV4) {
+    sft[(g / 4) * 512 + slot + (g % 4)] = static_cast<uint8_t>(nv_quant_fast<16>(v, crow));
+  } else if (kFmt == F_NV4B32) {
+    *reinterpret_cast<uint16_t*>(sft + (g / 2) * 512 + slot + 2 * (g % 2)) =
+        static_cast<uint16_t>(nv_quant_fast<32>(v, crow) * 0x101u);
+  } else {
+    sft[slot + g] = static_cast<uint8_t>(mx_quant32_bf(v, crow));
+  }
+}
+
+// ---------------------------------------------------------------- channel sums
+// sum[bh, d] += sum over keys of x[b, n, h, d] (K for its mean; V for V
+// smoothing).  grid (BH, ceil(L / 256)), 256 threads: thread t sums the 8
+// channels of 16-byte chunk t % 16 over rows t / 16 + 16 i of the block's 256
+// rows (16 independent loads in flight), then the 16 partial sums per channel
+// meet in shared memory.
+__global__ void __launch_bounds__(256) colsum_kernel(const __nv_bfloat16* __restrict__ x, int H, int L,
+                                                     int64_t sb, int64_t sn, int64_t sh, float* __restrict__ sum) {
+  __shared__ __align__(16) float part[16][128];
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int c = threadIdx.x & 15, r0 = threadIdx.x >> 4;
+  const int n0 = blockIdx.y * 256;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int n = n0 + r0 + 16 * i;
+    if (n < L) {
+      const uint4 u = ld_stream(reinterpret_cast<const uint4*>(x + nhd_row(b, n, h, sb, sn, sh) + c * 8));
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] += bf16lo(w[j]);
+        acc[2 * j + 1] += bf16hi(w[j]);
+      }
+    }
+  }
+  *reinterpret_cast<float4*>(&part[r0][c * 8]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  *reinterpret_cast<float4*>(&part[r0][c * 8 + 4]) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    float t = 0.f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) t += part[r][threadIdx.x];
+    atomicAdd(&sum[bh * 128 + threadIdx.x], t);
+  }
+}
+
+// ---------------------------------------------------------------- Q / K passes
+// grid (BH, Lp/128), 256 threads, one 128-row x 128-d tile per CTA:
+//   load the tile into shared memory (thread t: 16-byte chunk t % 16 of rows
+//   t / 16 + 16 i; Q also sums its columns on the way, for the group mean);
+//   the mean (Q: the tile's zero-padded group mean, written to qmean; K:
+//   bf16(ksum / L)); the centred bf16 tile in place (padding rows stay 0);
+//   each row's groups along D quantised in format kFmt.
+// K with smoothing also computes this key tile's delta_s rows for every query
+// group from the centred tile (see ds_tile), so K is read once here.
+constexpr int DS_LD = 136;  // padded row length (bf16) -> conflict-free ldmatrix
+constexpr int QK_TILE_BYTES = 128 * DS_LD * 2;
+constexpr int QK_SMEM_Q = QK_TILE_BYTES + 16 * 128 * 4;   // tile + column partial sums
+constexpr int QK_SMEM_K = QK_TILE_BYTES + 64 * DS_LD * 2;  // tile + 64 query-group means
+
+__device__ void ds_tile(const __nv_bfloat16* kcs, __nv_bfloat16* qms, const __nv_bfloat16* __restrict__ qmean,
+                        __nv_bfloat16* __restrict__ ds, int bh, int G, int Lp, int n0);
+
 template <bool kIsQ, int kFmt>
 __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __restrict__ x, int H, int L, int Lp,
                                                        int64_t sb, int64_t sn, int64_t sh,
                                                        const float* __restrict__ ksum, __nv_bfloat16* __restrict__ qmean,
                                                        uint8_t* __restrict__ codes, uint8_t* __restrict__ sf,
-                                                       int smoothing) {
-  __shared__ __align__(16) __nv_bfloat16 tile[128][136];
+                                                       int smoothing, __nv_bfloat16* __restrict__ ds) {
+  extern __shared__ __align__(16) uint8_t qk_smem[];
+  __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(qk_smem);  // [128][DS_LD]
   __shared__ float mean[128];
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
   const int t0 = blockIdx.y * 128;
-  for (int i = threadIdx.x; i < 128 * 16; i += 256) {  // 16-byte chunks: row i/16, chunk i%16
-    const int r = i >> 4, c = i & 15;
+  const int c = threadIdx.x & 15, r0 = threadIdx.x >> 4;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = r0 + 16 * i;
     const int n = t0 + r;
     uint4 u = make_uint4(0, 0, 0, 0);
-    if (n < L) u = *reinterpret_cast<const uint4*>(x + nhd_row(b, n, h, sb, sn, sh) + c * 8);
-    *reinterpret_cast<uint4*>(&tile[r][c * 8]) = u;
+    if (n < L) u = ld_stream(reinterpret_cast<const uint4*>(x + nhd_row(b, n, h, sb, sn, sh) + c * 8));
+    *reinterpret_cast<uint4*>(tile + r * DS_LD + c * 8) = u;
+    if (kIsQ) {
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] += bf16lo(w[j]);
+        acc[2 * j + 1] += bf16hi(w[j]);
+      }
+    }
+  }
+  if (kIsQ) {
+    float* part = reinterpret_cast<float*>(qk_smem + QK_TILE_BYTES);  // [16][128]
+    *reinterpret_cast<float4*>(part + r0 * 128 + c * 8) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(part + r0 * 128 + c * 8 + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
   }
   __syncthreads();
   if (threadIdx.x < 128) {
@@ -218,9 +283,11 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
     if (smoothing) {
       if (kIsQ) {
         // torch mean over the zero-padded 128-row group (transforms.py:72-80)
-        float s = 0.f;
-        for (int r = 0; r < 128; ++r) s += __bfloat162float(tile[r][d]);
-        m = bf16_round(s / 128.0f);
+        const float* part = reinterpret_cast<const float*>(qk_smem + QK_TILE_BYTES);
+        float sum = 0.f;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) sum += part[r * 128 + d];
+        m = bf16_round(sum / 128.0f);
         qmean[(static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 128 + d] = __float2bfloat16_rn(m);
       } else {
         m = bf16_round(ksum[bh * 128 + d] / static_cast<float>(L));
@@ -229,31 +296,49 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
     mean[d] = m;
   }
   __syncthreads();
+  if (smoothing) {  // centre in place: bf16(x - mean) on real rows, padding rows stay 0
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = r0 + 16 * i;
+      if (t0 + r < L) {
+        uint4* pu = reinterpret_cast<uint4*>(tile + r * DS_LD + c * 8);
+        const uint4 u = *pu;
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          o[j] = pack_bf16x2(bf16lo(w[j]) - mean[c * 8 + 2 * j], bf16hi(w[j]) - mean[c * 8 + 2 * j + 1]);
+        *pu = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    __syncthreads();
+  }
   // (row, group) items: 4 groups of 32 per row, NVFP4 8 groups of 16.
   // Scale chunks: 1024 bytes per 128-row tile (the E8M0 formats use the first
   // 512; F_NV4B32 writes each scale into both 16-element slots of its group).
   uint8_t* sft = sf + (static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 1024;
-  constexpr bool kNV = kFmt == F_NV4, kF8 = kFmt == F_MX8;
-  constexpr int kGroups = kNV ? 8 : 4, kGs = kNV ? 16 : 32;
+  constexpr int kGroups = kFmt == F_NV4 ? 8 : 4, kGs = kFmt == F_NV4 ? 16 : 32;
   for (int it = threadIdx.x; it < 128 * kGroups; it += 256) {
     const int r = it / kGroups, g = it % kGroups;
     const int n = t0 + r;
     float v[kGs];
 #pragma unroll
-    for (int i = 0; i < kGs; ++i) {
-      const int d = g * kGs + i;
-      v[i] = (n < L) ? bf16_round(__bfloat162float(tile[r][d]) - mean[d]) : 0.f;  // padding after smoothing
+    for (int q = 0; q < kGs / 8; ++q) {
+      const uint4 u = *reinterpret_cast<const uint4*>(tile + r * DS_LD + g * kGs + q * 8);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[q * 8 + 2 * j] = bf16lo(w[j]);
+        v[q * 8 + 2 * j + 1] = bf16hi(w[j]);
+      }
     }
-    uint8_t* crow = kF8 ? codes + (static_cast<int64_t>(bh) * Lp + n) * 128 + g * 32
-                        : codes + (static_cast<int64_t>(bh) * Lp + n) * 64 + g * (kGs / 2);
-    if (kFmt == F_NV4B32) {
-      const uint32_t e = nv_quant32(v, crow);
-      *reinterpret_cast<uint16_t*>(sft + (g / 2) * 512 + (r % 32) * 16 + (r / 32) * 4 + 2 * (g % 2)) =
-          static_cast<uint16_t>(e * 0x101u);
-    } else {
-      const uint32_t e = kF8 ? mx8_quant32(v, crow) : (kNV ? nv_quant16(v, crow) : mx_quant32(v, crow));
-      sft[(g / 4) * 512 + (r % 32) * 16 + (r / 32) * 4 + (g % 4)] = static_cast<uint8_t>(e);
-    }
+    uint8_t* crow = kFmt == F_MX8 ? codes + (static_cast<int64_t>(bh) * Lp + n) * 128 + g * 32
+                                  : codes + (static_cast<int64_t>(bh) * Lp + n) * 64 + g * (kGs / 2);
+    quant_group<kFmt>(v, crow, sft, r, g);
+  }
+  if (!kIsQ && smoothing) {
+    __syncthreads();  // (the tile was only read above; ds_tile reuses the rest of the buffer)
+    ds_tile(tile, reinterpret_cast<__nv_bfloat16*>(qk_smem + QK_TILE_BYTES), qmean, ds, bh, Lp / 128, Lp, t0);
   }
 }
 
@@ -273,7 +358,7 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
     const int r = i >> 4, c = i & 15;
     const int n = t0 + r;
     uint4 u = make_uint4(0, 0, 0, 0);
-    if (n < L) u = *reinterpret_cast<const uint4*>(v + nhd_row(b, n, h, sb, sn, sh) + c * 8);
+    if (n < L) u = ld_stream(reinterpret_cast<const uint4*>(v + nhd_row(b, n, h, sb, sn, sh) + c * 8));
     *reinterpret_cast<uint4*>(&tile[r][c * 8]) = u;
   }
   __syncthreads();
@@ -298,7 +383,7 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
       float x[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(tile[g * 32 + i][d]);
-      sfw[g / 2] |= (nv_quant32(x, row + g * 16) * 0x101u) << (16 * (g % 2));
+      sfw[g / 2] |= (nv_quant_fast<32>(x, row + g * 16) * 0x101u) << (16 * (g % 2));
     }
     *reinterpret_cast<uint32_t*>(sft) = sfw[0];
     *reinterpret_cast<uint32_t*>(sft + 512) = sfw[1];
@@ -309,7 +394,7 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
       float x[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) x[i] = __bfloat162float(tile[g * 16 + i][d]);
-      sfw[g / 4] |= nv_quant16(x, row + g * 8) << (8 * (g % 4));
+      sfw[g / 4] |= nv_quant_fast<16>(x, row + g * 8) << (8 * (g % 4));
     }
     *reinterpret_cast<uint32_t*>(sft) = sfw[0];
     *reinterpret_cast<uint32_t*>(sft + 512) = sfw[1];
@@ -320,7 +405,7 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
       float x[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(tile[g * 32 + i][d]);
-      sfw |= (kF8 ? mx8_quant32(x, row + g * 32) : mx_quant32(x, row + g * 16)) << (8 * g);
+      sfw |= (kF8 ? mx8_quant32(x, row + g * 32) : mx_quant32_bf(x, row + g * 16)) << (8 * g);
     }
     *reinterpret_cast<uint32_t*>(sft) = sfw;
   }
@@ -330,10 +415,10 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
 // ds[bh, g, n] = bf16( sum_d qmean[bh, g, d] * kc[bh, n, d] ), kc = bf16(k - mean),
 // with bf16 tensor-core MMAs (mma.sync m16n8k16, fp32 accumulation), stored
 // as bf16 rows the flash kernel loads by TMA as an MMA operand.
-// grid (BH, Lp/128), 256 threads (8 warps).  The CTA keeps its 128 keys'
-// kc (bf16) in shared memory and walks the G groups 64 at a time; each warp
-// owns a 32 (g) x 32 (n) block of the 64 x 128 output chunk.
-constexpr int DS_LD = 136;  // padded row length (bf16) -> conflict-free ldmatrix
+// Run by the K pass's 256 threads (8 warps) on its centred key tile kcs
+// ([128][DS_LD] bf16 in shared memory): walks the G query groups 64 at a
+// time through qms ([64][DS_LD]); each warp owns a 32 (g) x 32 (n) block of
+// the 64 x 128 output chunk.
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -348,33 +433,8 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__global__ void __launch_bounds__(256) ds_kernel(const __nv_bfloat16* __restrict__ k, int H, int L, int Lp,
-                                                 int64_t sb, int64_t sn, int64_t sh,
-                                                 const float* __restrict__ ksum,
-                                                 const __nv_bfloat16* __restrict__ qmean,
-                                                 __nv_bfloat16* __restrict__ ds) {
-  extern __shared__ __align__(16) uint8_t ds_smem[];
-  __nv_bfloat16* kcs = reinterpret_cast<__nv_bfloat16*>(ds_smem);          // [128][DS_LD]
-  __nv_bfloat16* qms = kcs + 128 * DS_LD;                                    // [64][DS_LD]
-  __shared__ float kmean[128];
-  const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  const int n0 = blockIdx.y * 128;
-  const int G = Lp / 128;
-  if (threadIdx.x < 128) kmean[threadIdx.x] = bf16_round(ksum[bh * 128 + threadIdx.x] / static_cast<float>(L));
-  __syncthreads();
-  for (int i = threadIdx.x; i < 128 * 16; i += 256) {
-    const int r = i >> 4, c = i & 15;
-    const int n = n0 + r;
-    uint32_t w[4] = {0, 0, 0, 0};
-    if (n < L) {
-      const uint4 u = *reinterpret_cast<const uint4*>(k + nhd_row(b, n, h, sb, sn, sh) + c * 8);
-      const uint32_t raw[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        w[j] = pack_bf16x2(bf16lo(raw[j]) - kmean[c * 8 + 2 * j], bf16hi(raw[j]) - kmean[c * 8 + 2 * j + 1]);
-    }
-    *reinterpret_cast<uint4*>(kcs + r * DS_LD + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
-  }
+__device__ void ds_tile(const __nv_bfloat16* kcs, __nv_bfloat16* qms, const __nv_bfloat16* __restrict__ qmean,
+                        __nv_bfloat16* __restrict__ ds, int bh, int G, int Lp, int n0) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wm = warp >> 2;        // 0..1: g rows [32 wm, 32 wm + 32)
   const int wn = warp & 3;         // 0..3: keys [32 wn, 32 wn + 32)
@@ -430,32 +490,50 @@ __global__ void __launch_bounds__(256) ds_kernel(const __nv_bfloat16* __restrict
 
 }  // namespace
 
+// The Q and K passes of format kFmt; their dynamic shared memory (above the
+// 48 KB default) is enabled once per device for this instantiation.
+template <int kFmt>
+int launch_qk(const Problem& p, const Workspace& w, cudaStream_t s) {
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(qk_quant_kernel<true, kFmt>, cudaFuncAttributeMaxDynamicSharedMemorySize, QK_SMEM_Q) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(qk_quant_kernel<false, kFmt>, cudaFuncAttributeMaxDynamicSharedMemorySize, QK_SMEM_K) !=
+            cudaSuccess)
+      return fail(QDQ_ERR_CUDA, "sage3 prepass: smem attribute");
+    attr[dev] = true;
+  }
+  const int BH = p.B * p.H, T = p.Lp / 128;
+  qk_quant_kernel<true, kFmt><<<dim3(BH, T), 256, QK_SMEM_Q, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh, w.ksum,
+                                                                 w.qmean, w.qc, w.qsf, p.smoothing, w.ds);
+  qk_quant_kernel<false, kFmt><<<dim3(BH, T), 256, QK_SMEM_K, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh,
+                                                                  w.ksum, w.qmean, w.kc, w.ksf, p.smoothing, w.ds);
+  return QDQ_OK;
+}
+
 int launch_prepass(const Problem& p, const Workspace& w, cudaStream_t s) {
   const int BH = p.B * p.H;
   const int T = p.Lp / 128;
   if (cudaMemsetAsync(w.ksum, 0, sizeof(float) * BH * 128, s) != cudaSuccess)
     return fail(QDQ_ERR_CUDA, "sage3 prepass: memset failed");
-  if (p.smoothing) {
-    ksum_kernel<<<dim3(BH, (p.L + 1023) / 1024), 128, 0, s>>>(p.k, p.H, p.L, p.k_sb, p.k_sn, p.k_sh, w.ksum);
-  }
+  if (p.smoothing)
+    colsum_kernel<<<dim3(BH, (p.L + 255) / 256), 256, 0, s>>>(p.k, p.H, p.L, p.k_sb, p.k_sn, p.k_sh, w.ksum);
   if (p.vsmooth) {
     if (cudaMemsetAsync(w.vsum, 0, sizeof(float) * BH * 128, s) != cudaSuccess)
       return fail(QDQ_ERR_CUDA, "sage3 prepass: memset failed");
-    ksum_kernel<<<dim3(BH, (p.L + 1023) / 1024), 128, 0, s>>>(p.v, p.H, p.L, p.v_sb, p.v_sn, p.v_sh, w.vsum);
+    colsum_kernel<<<dim3(BH, (p.L + 255) / 256), 256, 0, s>>>(p.v, p.H, p.L, p.v_sb, p.v_sn, p.v_sh, w.vsum);
   }
-  // Q and K in the Q/K format
-#define QDQ_QK(FMT)                                                                                          \
-  qk_quant_kernel<true, FMT><<<dim3(BH, T), 256, 0, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh, w.ksum,     \
-                                                         w.qmean, w.qc, w.qsf, p.smoothing);                    \
-  qk_quant_kernel<false, FMT><<<dim3(BH, T), 256, 0, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh, w.ksum,    \
-                                                          w.qmean, w.kc, w.ksf, p.smoothing)
+  // Q (group means first: the K pass's delta_s reads them), then K, in the Q/K format
+  int st = QDQ_OK;
   switch (p.qk_fmt) {
-    case F_MX8: QDQ_QK(F_MX8); break;
-    case F_NV4: QDQ_QK(F_NV4); break;
-    case F_NV4B32: QDQ_QK(F_NV4B32); break;
-    default: QDQ_QK(F_MX4); break;
+    case F_MX8: st = launch_qk<F_MX8>(p, w, s); break;
+    case F_NV4: st = launch_qk<F_NV4>(p, w, s); break;
+    case F_NV4B32: st = launch_qk<F_NV4B32>(p, w, s); break;
+    default: st = launch_qk<F_MX4>(p, w, s); break;
   }
-#undef QDQ_QK
+  if (st != QDQ_OK) return st;
   // V^T in the P/V format
   const float* vs = p.vsmooth ? w.vsum : nullptr;
 #define QDQ_V(FMT)                                                                                           \
@@ -468,18 +546,6 @@ int launch_prepass(const Problem& p, const Workspace& w, cudaStream_t s) {
     default: QDQ_V(F_MX4); break;
   }
 #undef QDQ_V
-  if (p.smoothing) {
-    const int smem = (128 + 64) * DS_LD * 2;
-    static bool attr[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr[dev]) {
-      if (cudaFuncSetAttribute(ds_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-        return fail(QDQ_ERR_CUDA, "sage3 prepass: smem attribute");
-      attr[dev] = true;
-    }
-    ds_kernel<<<dim3(BH, T), 256, smem, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh, w.ksum, w.qmean, w.ds);
-  }
   return check_launch("sage3 prepass");
 }
 
