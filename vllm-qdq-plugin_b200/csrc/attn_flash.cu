@@ -18,21 +18,26 @@
 // (the reference attends to its zero padding).
 //
 // CTA = two 128-row query tiles (A, B) of one (batch, head) that share every
-// K/V tile, 12 warps:
-//   warps 0-3     softmax A: one thread per query row (TMEM lane): S -> registers,
-//                 block maxima (the row max and each block's max
-//                 of p follow from them), O_A rescale in TMEM when the max
-//                 grows, exp2, row sum, P -> E2M1 codes + block scales in
-//                 shared memory; epilogue O_A / l -> bf16 NHD
-//   warps 4-7     softmax B (the same for tile B)
-//   warp 8        MMA issuer: per key tile j, S = delta_s_A + Q_A K_j^T, then
+// K/V tile, 18 warps:
+//   warps 0-7     softmax A: two threads per query row (TMEM lane), warps
+//                 0-3 on keys 0-63 of every key tile and warps 4-7 on keys
+//                 64-127 (warps w and w + 4 share TMEM lanes 32 (w % 4) ..):
+//                 S half-row -> registers, half-row block maxima and the row
+//                 max through the partner thread, O_A half-row rescale in TMEM
+//                 when the max grows, exp2, partial row sum, P -> codes +
+//                 block scales in shared memory; epilogue O_A / l -> bf16 NHD
+//   warps 8-15    softmax B (the same for tile B)
+//   warp 16       MMA issuer: per key tile j, S = delta_s_A + Q_A K_j^T, then
 //                 (once A has read S) S = delta_s_B + Q_B K_j^T, then
 //                 O_A += P_A V_{j-1}, O_B += P_B V_{j-1}
-//   warp 9        TMA producer: K tile [128 keys x 64 B], V^T tile [128 d x 64 B]
+//   warp 17       TMA producer (warps 18-19 idle): K tile [128 keys x 64 B], V^T tile [128 d x 64 B]
 //                 (64-byte swizzle; E4M3: 128 B rows, 128-byte swizzle), their
 //                 scale chunks and the two tiles' delta_s rows (bf16) into a
 //                 4-stage ring (3 for E4M3); Q_A, Q_B once
-//   warps 10-11   idle (they complete the third warpgroup for setmaxnreg)
+// Four softmax warps per SM sub-partition (instead of two with one thread
+// per row) hide the latency of the exp2 / convert / sum chains; the partner
+// threads of a row exchange their half-row maxima (and at the end their
+// partial row sums) through shared memory and a 64-arrival mbarrier.
 // The single S buffer alternates between the two softmax warpgroups, which
 // therefore run out of phase and overlap their MUFU / FMA / ALU work.
 // delta_s on the tensor core: with QK smoothing, S starts as one bf16 MMA
@@ -44,8 +49,9 @@
 // A_t x B^T = delta_s of tile t broadcast over its 128 query rows.  The
 // reference adds delta_s to the fp32 scores after the QK product; here it is
 // the accumulator's initial value, the same sum in another order.
-// Registers: softmax warpgroups 224 per thread, the rest 56 (setmaxnreg;
-// 2 x 128 x 224 + 128 x 56 = 384 x 168, the launch allocation).
+// Registers: 96 per thread at launch (640 x 96); setmaxnreg moves them to
+// 104 for the four softmax warpgroups and 64 for the fifth (MMA, producer,
+// two idle warps that complete the warpgroup): 512 x 104 + 128 x 64 = 640 x 96.
 // TMEM: S [0,128) O_A [128,256) O_B [256,384), scale factors [384,432).
 #include <cmath>
 
@@ -66,7 +72,8 @@ constexpr int DS_TX = 2 * 2 * 64 * 2;  // bytes the two 64-key x 2-row delta_s b
 constexpr int ONES_TILE = 2048;      // "ones" MMA operand of one query tile: 128 rows x 16 B
 constexpr int ZERO_TILE = 2048;      // zero K-rows 8-15 of both delta_s MMA operands
 constexpr uint32_t IDESC_DS = idesc_bf16(BM, BN, true);
-constexpr int THREADS = 384;
+constexpr int THREADS = 640;         // 16 softmax warps; the MMA, TMA producer and two idle warps
+constexpr int MMA_WARP = 16, TMA_WARP = 17;
 constexpr int TMEM_COLS = 512;
 // scale-factor columns: 8 per operand (NVFP4: two chunks; MXFP4 uses the first 4)
 constexpr uint32_t T_S = 0, T_O = 128, T_SFQ = 384, T_SFK = 400, T_SFP = 408, T_SFV = 416;
@@ -80,6 +87,8 @@ struct Bars {
   uint64_t p_full[2];   // per warpgroup: its P codes / scales are in shared memory
   uint64_t o_done[2];   // per warpgroup: its PV MMA completed
   uint64_t drain;
+  uint64_t xready[2][4];          // per (query tile, lane quadrant): the two half-row threads' exchange
+  float xslot[2][2][2][BM];       // [tile][phase & 1][half][row]: exchanged row maxima, then l
   uint32_t tmem_base;
   int abort;
 };
@@ -156,6 +165,11 @@ __device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint3
 }
 __device__ __forceinline__ void sts64(uint32_t a, uint32_t x, uint32_t y) {
   asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(a), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void reg_alloc_softmax() { asm volatile("setmaxnreg.inc.sync.aligned.u32 104;"); }
+__device__ __forceinline__ void reg_dealloc_others() { asm volatile("setmaxnreg.dec.sync.aligned.u32 64;"); }
+__device__ __forceinline__ void sts16(uint32_t a, uint32_t x) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"(static_cast<unsigned short>(x)) : "memory");
 }
 __device__ __forceinline__ void sts32(uint32_t a, uint32_t x) {
   asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(x) : "memory");
@@ -239,8 +253,6 @@ __device__ __forceinline__ void cp_sf(uint32_t taddr, const uint8_t* smem_sf) {
   if (kNV) tmem_cp_sf(taddr + 4, smem_desc_sf(smem_sf + SF_CHUNK));
 }
 
-__device__ __forceinline__ void reg_alloc_224() { asm volatile("setmaxnreg.inc.sync.aligned.u32 224;"); }
-__device__ __forceinline__ void reg_dealloc_56() { asm volatile("setmaxnreg.dec.sync.aligned.u32 56;"); }
 
 // max of v[0 .. 16) and of v[0 .. 32), three-input max (sm_100)
 __device__ __forceinline__ float max16(const float* v) {
@@ -272,20 +284,39 @@ __device__ __forceinline__ float e4m3x4_sum(uint32_t w) {
   return (f16lo(h0) + f16hi(h0)) + (f16lo(h1) + f16hi(h1));
 }
 
+// A row's value from the partner thread (same query tile and row, other half
+// of the keys): both warps write theirs into slot ph & 1 and arrive on the
+// pair's mbarrier (count 64), whose phase ph then completes.  A thread
+// cannot reach phase ph + 2, which reuses the slot, before its partner has
+// arrived for phase ph + 1, i.e. has read phase ph's value.
+__device__ __forceinline__ float pair_exchange(Bars* bars, int wg, int hf, int quad, int r, float v, int ph, bool& ok,
+                                               int* status, int site) {
+  volatile float* slot = &bars->xslot[wg][ph & 1][0][0];
+  slot[hf * BM + r] = v;
+  mbar_arrive(&bars->xready[wg][quad]);
+  if (ok) ok = mbar_wait(&bars->xready[wg][quad], ph & 1, status, site);
+  return slot[(hf ^ 1) * BM + r];
+}
+
+// One softmax thread: query row r of tile wg and keys [64 hf, 64 hf + 64) of
+// every key tile.  Warps (wg, hf = 0, quad) and (wg, hf = 1, quad) share TMEM
+// lanes 32 quad .. 32 quad + 31 (the rows) and split the 128 S / O columns.
 template <int kQK, int kPV, bool kEmu>
-__device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t tmem, const Params& p, int wg,
-                                           int qt, int bh, int nkv, __nv_bfloat16* __restrict__ out,
+__device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t tmem, const Params& p, int wg, int hf,
+                                           int quad, int qt, int bh, int nkv, __nv_bfloat16* __restrict__ out,
                                            int* status) {
   constexpr bool kNV = kPV == F_NV4;
   constexpr bool kP8 = kPV == F_MX8;
   constexpr bool kE4S32 = kPV == F_NV4B32;   // E4M3 scale per 32 keys
   using Lay = FLay<kQK, kPV>;
   constexpr int NG = kNV ? 8 : 4;            // scale blocks per row of 128 keys
-  const int warp = (threadIdx.x >> 5) & 3;
+  constexpr int NGH = NG / 2;                // of them in this thread's half
+  constexpr int HB = BN / 2;                 // keys per half
+  const int warp = quad;
   const int lane = threadIdx.x & 31;
   const int r = warp * 32 + lane;            // query row in the tile = TMEM lane
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-  const uint32_t t_o = tmem + T_O + wg * 128;
+  const uint32_t t_o = tmem + T_O + wg * 128 + hf * HB;
   const uint32_t sbase = smem_u32(smem);
   const uint32_t prow0 = sbase + Lay::OFF_P + 2 * wg * Lay::PV_TILE + r * fmt_row(kPV);      // this row of P
   const uint32_t psf0 = sbase + Lay::OFF_PSF + 2 * wg * SF_TILE + (r & 31) * 16 + (r >> 5) * 4;  // its scale word
@@ -301,11 +332,11 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     if (ok) ok = mbar_wait(&bars->s_full[wg], j & 1, status, 0x1301);
     ok = __all_sync(0xffffffffu, ok);  // warp-uniform: the TMEM accesses below are .sync.aligned
     tc_fence_after();
-    float x[BN];
+    float x[HB];
 #pragma unroll
-    for (int c = 0; c < BN; c += 32) {
+    for (int c = 0; c < HB; c += 32) {
       uint32_t u[32];
-      tmem_ld32(tmem + lane_base + T_S + c, u);
+      tmem_ld32(tmem + lane_base + T_S + hf * HB + c, u);
 #pragma unroll
       for (int i = 0; i < 32; ++i) x[c + i] = __uint_as_float(u[i]);
     }
@@ -313,20 +344,20 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     tc_fence_before();
     mbar_arrive(&bars->s_free[wg]);
     // masking: keys beyond L (last tile) and, if causal, keys after the query
-    const int key0 = j * BN;
+    const int key0 = j * BN + hf * HB;
     const int lim = p.causal ? min(p.L - key0, qrow - key0 + 1) : p.L - key0;
-    if (lim < BN) {
+    if (lim < HB) {
 #pragma unroll
-      for (int i = 0; i < BN; ++i)
+      for (int i = 0; i < HB; ++i)
         if (i >= lim) x[i] = -INFINITY;
     }
-    // block maxima of the scores; the row max and each block's max of p
-    // (p = exp2(x * qk - m) is monotone in x) both follow from them
-    float gm[NG];
+    // block maxima of the scores; the row max (with the partner's half) and
+    // each block's max of p (p = exp2(x * qk - m) is monotone in x) follow
+    float gm[NGH];
 #pragma unroll
-    for (int g = 0; g < NG; ++g) gm[g] = kNV ? max16(x + 16 * g) : max32(x + 32 * g);
-    const float mx = kNV ? fmaxf(fmax3(gm[0], gm[1], gm[2]), fmax3(fmax3(gm[3], gm[4], gm[5]), gm[6], gm[7]))
-                         : fmaxf(fmax3(gm[0], gm[1], gm[2]), gm[3]);
+    for (int g = 0; g < NGH; ++g) gm[g] = kNV ? max16(x + 16 * g) : max32(x + 32 * g);
+    const float mh = kNV ? fmaxf(fmaxf(gm[0], gm[1]), fmaxf(gm[2], gm[3])) : fmaxf(gm[0], gm[1]);
+    const float mx = fmaxf(mh, pair_exchange(bars, wg, hf, quad, r, mh, j, ok, status, 0x1305));
     const float m_new = fmaxf(m_run, mx * qk);
     const bool grow = (m_new > m_run) && (m_run != -INFINITY);
     const float alpha = grow ? ex2_approx(m_run - m_new) : 1.0f;
@@ -334,6 +365,7 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     m_run = m_new;
     // P(j) goes to buffer j & 1; PV(j-2), its previous reader, completed before
     // p_full(j-1) was signalled (the o_done wait below, one tile earlier).
+    // Block g below is this half's block g (the row's block hf * NGH + g).
     const uint32_t prow = prow0 + (j & 1) * Lay::PV_TILE;
     const uint32_t psf = psf0 + (j & 1) * SF_TILE;
     const float2 qk2 = make_float2(qk, qk);
@@ -345,7 +377,8 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
       uint32_t sfw = 0;
       float lsum = 0.f;
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
+      for (int g = 0; g < NGH; ++g) {
+        const int gg = hf * NGH + g;
         const int e = mx8_block_exp(ex2_approx(fmaf(gm[g], qk, -m_new)));
         const float cg = -m_new - static_cast<float>(e);
         const float2 c2 = make_float2(cg, cg);
@@ -366,12 +399,12 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
         }
         const float2 a = add_f32x2(acc[0], acc[1]);
         lsum = fmaf(a.x + a.y, exp2i(e), lsum);
-        sts128(prow + (((2 * g) ^ swz) << 4), w[0], w[1], w[2], w[3]);
-        sts128(prow + (((2 * g + 1) ^ swz) << 4), w[4], w[5], w[6], w[7]);
+        sts128(prow + (((2 * gg) ^ swz) << 4), w[0], w[1], w[2], w[3]);
+        sts128(prow + (((2 * gg + 1) ^ swz) << 4), w[4], w[5], w[6], w[7]);
         sfw |= static_cast<uint32_t>(e + 127) << (8 * g);
       }
       l_run += lsum;
-      sts32(psf, sfw);
+      sts16(psf + 2 * hf, sfw);
     } else if (!kEmu) {
       // P -> E2M1 codes (round-to-nearest-even) with E8M0 2^e per 32 keys,
       // e = clamp(ceil(log2(max p / 6)), -127, 127).  The block scale is folded
@@ -380,7 +413,8 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
       uint32_t sfw = 0;
       float lsum = 0.f;
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
+      for (int g = 0; g < NGH; ++g) {
+        const int gg = hf * NGH + g;
         const int e = mx_block_exp(ex2_approx(fmaf(gm[g], qk, -m_new)));
         const float cg = -m_new - static_cast<float>(e);
         const float2 c2 = make_float2(cg, cg);
@@ -401,11 +435,11 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
         }
         const float2 a = add_f32x2(acc[0], acc[1]);
         lsum = fmaf(a.x + a.y, exp2i(e), lsum);
-        sts128(prow + ((g ^ swz) << 4), w[0], w[1], w[2], w[3]);
+        sts128(prow + ((gg ^ swz) << 4), w[0], w[1], w[2], w[3]);
         sfw |= static_cast<uint32_t>(e + 127) << (8 * g);
       }
       l_run += lsum;
-      sts32(psf, sfw);
+      sts16(psf + 2 * hf, sfw);
     } else if (kP8) {
       // Emulated single-level MXFP8 P (p_quant_mxfp8_s1): E8M0 2^e per 32 keys,
       // e = clamp(ceil(log2(max(max p / 448, 1e-8))), -127, 127), E4M3 codes
@@ -416,7 +450,8 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
       uint32_t sfw = 0;
       float lq = 0.f;
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
+      for (int g = 0; g < NGH; ++g) {
+        const int gg = hf * NGH + g;
         const float amax = __fmul_rn(ex2_approx(fmaf(gm[g], qk, -m_new)), p.p_prescale);
         const int e = max(mx8_block_exp(amax), -26);  // ceil(log2(1e-8)) = -26
         const float cg = p.p_prescale_lg2 - m_new - static_cast<float>(e);
@@ -437,12 +472,12 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
           gsum += e4m3x4_sum(w[q]);
         }
         lq = fmaf(gsum, exp2i(e), lq);
-        sts128(prow + (((2 * g) ^ swz) << 4), w[0], w[1], w[2], w[3]);
-        sts128(prow + (((2 * g + 1) ^ swz) << 4), w[4], w[5], w[6], w[7]);
+        sts128(prow + (((2 * gg) ^ swz) << 4), w[0], w[1], w[2], w[3]);
+        sts128(prow + (((2 * gg + 1) ^ swz) << 4), w[4], w[5], w[6], w[7]);
         sfw |= static_cast<uint32_t>(e + 127) << (8 * g);
       }
       l_run += lq;
-      sts32(psf, sfw);
+      sts16(psf + 2 * hf, sfw);
     } else {
       // Emulated configs: p = exp2(x * qk - m), times the prescale (448*6 for
       // the two-level configs, which cancels in O / l; 1 for the single-level
@@ -457,10 +492,11 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
       // (a zero E4M3 scale zeroes its block in the MMA; its codes are then
       // taken at 2^-9).
       float lq = 0.f;
-      uint32_t sfw[2] = {0u, 0u};
+      uint32_t sfw = 0u;
 #pragma unroll
-      for (int g = 0; g < NG; ++g) {
+      for (int g = 0; g < NGH; ++g) {
         constexpr int GS = BN / NG;
+        const int gg = hf * NGH + g;
         const float amax = __fmul_rn(ex2_approx(fmaf(gm[g], qk, -m_new)), p.p_prescale);
         float deq, lg2s;
         uint32_t sbyte;
@@ -499,21 +535,21 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
         }
         lq = fmaf(__low2float(hs) + __high2float(hs), deq, lq);
         if (kNV) {
-          // 16-byte chunk g/2 of the row holds blocks 2*(g/2), 2*(g/2)+1
-          sts64(prow + (((g >> 1) ^ swz) << 4) + (g & 1) * 8, w[0], w[1]);
-          sfw[g >> 2] |= sbyte << (8 * (g & 3));
+          // 16-byte chunk gg/2 of the row holds blocks 2*(gg/2), 2*(gg/2)+1
+          sts64(prow + (((gg >> 1) ^ swz) << 4) + (gg & 1) * 8, w[0], w[1]);
+          sfw |= sbyte << (8 * g);  // scale chunk hf holds this half's 4 blocks
         } else if (kE4S32) {
-          // block g fills 16-element scale slots 2g and 2g+1
-          sts128(prow + ((g ^ swz) << 4), w[0], w[1], w[2], w[3]);
-          sfw[g >> 1] |= (sbyte * 0x101u) << (16 * (g & 1));
+          // block gg fills 16-element scale slots 2gg and 2gg+1 (chunk hf)
+          sts128(prow + ((gg ^ swz) << 4), w[0], w[1], w[2], w[3]);
+          sfw |= (sbyte * 0x101u) << (16 * g);
         } else {
-          sts128(prow + ((g ^ swz) << 4), w[0], w[1], w[2], w[3]);
-          sfw[0] |= sbyte << (8 * g);
+          sts128(prow + ((gg ^ swz) << 4), w[0], w[1], w[2], w[3]);
+          sfw |= sbyte << (8 * g);
         }
       }
       l_run += lq;
-      sts32(psf, sfw[0]);
-      if (kNV || kE4S32) sts32(psf + SF_CHUNK, sfw[1]);
+      if (kNV || kE4S32) sts32(psf + hf * SF_CHUNK, sfw);
+      else sts16(psf + 2 * hf, sfw);
     }
     // O holds PV(0 .. j-1): rescale it by alpha once PV(j-1) has completed and
     // before PV(j) is issued (p_full).  All four column chunks in flight at once.
@@ -521,12 +557,12 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     ok = __all_sync(0xffffffffu, ok);
     if (__any_sync(0xffffffffu, grow)) {
       tc_fence_after();
-      uint32_t u[HD / 32][32];
+      uint32_t u[HD / 64][32];
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) tmem_ld32(t_o + lane_base + 32 * c, u[c]);
+      for (int c = 0; c < HD / 64; ++c) tmem_ld32(t_o + lane_base + 32 * c, u[c]);
       tmem_ld_wait();
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < HD / 64; ++c) {
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           const float2 v = mul_f32x2(make_float2(__uint_as_float(u[c][i]), __uint_as_float(u[c][i + 1])),
@@ -543,22 +579,23 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     mbar_arrive(&bars->p_full[wg]);
   }
   // ---------------- epilogue: O / l -> bf16 NHD
+  const float l_row = l_run + pair_exchange(bars, wg, hf, quad, r, l_run, nkv, ok, status, 0x1306);
   if (ok && nkv > 0) ok = mbar_wait(&bars->o_done[wg], (nkv - 1) & 1, status, 0x1304);
   ok = __all_sync(0xffffffffu, ok);
   tc_fence_after();
   const bool store = ok && !*(volatile int*)&bars->abort && qrow < p.L;
-  const float inv_l = 1.0f / l_run;
+  const float inv_l = 1.0f / l_row;
   const int b = bh / p.H, h = bh % p.H;
-  __nv_bfloat16* orow = out + b * p.o_sb + static_cast<int64_t>(qrow) * p.o_sn + h * p.o_sh;
+  __nv_bfloat16* orow = out + b * p.o_sb + static_cast<int64_t>(qrow) * p.o_sn + h * p.o_sh + hf * HB;
 #pragma unroll 1
-  for (int c = 0; c < HD; c += 32) {
+  for (int c = 0; c < HB; c += 32) {
     uint32_t u[32];
     tmem_ld32(t_o + lane_base + c, u);
     tmem_ld_wait();
     if (store) {
       float add[32];
       if (p.vsmooth) {  // softmax rows sum to 1: O + v_mean is the attention of the uncentred V
-        const float4* vm = reinterpret_cast<const float4*>(p.vmean + static_cast<int64_t>(bh) * HD + c);
+        const float4* vm = reinterpret_cast<const float4*>(p.vmean + static_cast<int64_t>(bh) * HD + hf * HB + c);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float4 t = __ldg(vm + i);
@@ -615,8 +652,9 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->s_free[i], 128);
-      mbar_init(&bars->p_full[i], 128);
+      mbar_init(&bars->s_free[i], 2 * BM);
+      mbar_init(&bars->p_full[i], 2 * BM);
+      for (int q = 0; q < 4; ++q) mbar_init(&bars->xready[i][q], 64);
       mbar_init(&bars->o_done[i], 1);
     }
     mbar_init(&bars->drain, 1);
@@ -642,7 +680,7 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
     }
     fence_proxy_async_smem();  // visible to the TMA unit and the tensor core
   }
-  if (warp == 8) {
+  if (warp == MMA_WARP) {
     tmem_alloc(&bars->tmem_base, TMEM_COLS);
     tmem_relinquish();
   }
@@ -651,13 +689,14 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp < 8) {
-    reg_alloc_224();
-    const int wg = warp >> 2;
-    if (wg < nq) softmax_wg<kQK, kPV, kEmu>(smem, bars, tmem, p, wg, qtA + wg, bh, nkv, out, status);
+  if (warp < MMA_WARP) {
+    reg_alloc_softmax();
+    const int wg = warp >> 3;  // query tile
+    if (wg < nq)
+      softmax_wg<kQK, kPV, kEmu>(smem, bars, tmem, p, wg, (warp >> 2) & 1, warp & 3, qtA + wg, bh, nkv, out, status);
   } else {
-    reg_dealloc_56();
-    if (warp == 9) {
+    reg_dealloc_others();
+    if (warp == TMA_WARP) {
       // ------------------------------------------------------------ producer
       if (elect_one()) {
         mbar_arrive_expect_tx(&bars->q_full, nq * (Lay::QK_TILE + kSfQK));
@@ -692,7 +731,7 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
         for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
           mbar_wait(&bars->kv_full[j % STAGES], (j / STAGES) & 1, status, 0x1103);
       }
-    } else if (warp == 8) {
+    } else if (warp == MMA_WARP) {
       // ------------------------------------------------------------ MMA issuer
       if (elect_one()) {
         bool ok = mbar_wait(&bars->q_full, 0, status, 0x1201);
@@ -756,7 +795,7 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
