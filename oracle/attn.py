@@ -98,18 +98,22 @@ def e4m3_round(x: np.ndarray) -> np.ndarray:
 
 
 def nv_quant_deq(x: np.ndarray, block: int = 16) -> np.ndarray:
-    """NVFP4 of the reference's nvfp4 QuantConfig on the hardware grid, per 16
-    along the last axis: scale = e4m3(max(bf16(amax / 6), 1e-8)), codes of
-    x * (1/scale) with round-half-away, dequantised.  block=32 gives the
-    mxfp4_s1_e4m3 QuantConfig (quant_config.py:246-255), the same steps per 32."""
+    """NVFP4 of the reference's nvfp4 QuantConfig (quantize.py:21-81 with
+    round_to_e4m3) on the hardware grid, per 16 along the last axis:
+    scale = e4m3(max(bf16(amax / 6), 1e-8)), codes of the exact quotient
+    x / scale rounded half away from zero (the reference's own steps use a
+    bf16 quotient and a 9-level grid no FP4 hardware has; parity with them is
+    by tolerance), dequantised; a zero scale zeroes the block.  block=32 gives
+    the mxfp4_s1_e4m3 QuantConfig (quant_config.py:246-255), the same steps per
+    32."""
     sh = x.shape
     xb = np.asarray(x, np.float32).reshape(*sh[:-1], sh[-1] // block, block)
     amax = np.abs(xb).max(axis=-1)
     sc = np.maximum(bf16_round(amax / np.float32(6.0)), np.float32(1e-8))
-    s = e4m3_round(sc)
-    inv = np.where(s > 0, np.float32(1.0) / np.where(s > 0, s, 1), 0).astype(np.float32)
-    q = _rna_e2m1((xb * inv[..., None]).astype(np.float32))
-    return (q * s[..., None].astype(np.float64)).reshape(sh)
+    s = e4m3_round(sc).astype(np.float64)
+    quot = xb.astype(np.float64) / np.where(s > 0, s, 1.0)[..., None]  # correctly rounded: exact at midpoints
+    q = np.where(s[..., None] > 0, _rna_e2m1(quot), 0.0)
+    return (q * s[..., None]).reshape(sh)
 
 
 def _ceil_log2(r: np.ndarray) -> np.ndarray:

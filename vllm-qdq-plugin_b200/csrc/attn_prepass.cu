@@ -134,22 +134,18 @@ __device__ __forceinline__ uint32_t mx_quant32_bf(const float* v, uint8_t* out) 
   return static_cast<uint32_t>(e + 127);
 }
 
-// |v| rounded to the E2M1 grid with ties away from zero, for any finite v
-// (the reference's thresholds 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5, |v|
-// clamped to 6, mxfp4_hw_kernel.py:43-61): the magnitude keeps 1 mantissa bit at or
-// above 1, none in [0.5, 1), and is 0 or 0.5 below; the sign is v < 0.  The
-// result is an E2M1 value, so cvt encodes it exactly.
-__device__ __forceinline__ float e2m1_rna_value(float v) {
-  const float a = fminf(fabsf(v), 6.0f);
-  const uint32_t b = __float_as_uint(a);
-  const uint32_t sh = b >= 0x3F800000u ? 22u : 23u;
-  float q = __uint_as_float((b + (1u << (sh - 1))) & ~((1u << sh) - 1u));
-  q = a >= 0.5f ? q : (a >= 0.25f ? 0.5f : 0.0f);
-  return v < 0.0f ? -q : q;
-}
-
-// E4M3-scaled blocks (nv_quant16 / nv_quant32 semantics) with the bit-level
-// round-half-away above: KB elements, KB / 2 code bytes, returns the scale byte.
+// E4M3-scaled blocks (the reference's nvfp4 / mxfp4_s1_e4m3 QuantConfigs,
+// quantize.py:21-81 with round_to_e4m3, on the hardware E2M1 grid): scale
+// s = e4m3(max(bf16(amax / 6), 1e-8)), codes of the quotient x / s rounded
+// half away from zero.  x has bf16 precision (8 significant bits) and s at
+// most 4, so x / s is either exactly an E2M1 midpoint (a value with at most 7
+// significant bits times s) or at least 2^-9 relative away from every
+// midpoint.  x * (RN(1 / s) * (1 + 2^-12)) is within 2^-11 relative of
+// x / s * (1 + 2^-12): above a midpoint that x / s equals, on the same side
+// of every other, so the round-to-nearest-even cvt gives the round-half-away
+// code (checked exhaustively on the CPU for every bf16 x and E4M3 s).
+// fma(x, inv, +0) turns an exact -0 into +0 (the reference's sign is x < 0).
+// KB elements, KB / 2 code bytes; returns the scale byte (0: the block is 0).
 template <int KB>
 __device__ __forceinline__ uint32_t nv_quant_fast(const float* v, uint8_t* out) {
   float amax = 0.f;
@@ -158,14 +154,15 @@ __device__ __forceinline__ uint32_t nv_quant_fast(const float* v, uint8_t* out) 
   const float sc = fmaxf(bf16_round(amax / 6.0f), 1e-8f);
   const uint32_t sbyte = e4m3_byte(sc);
   const float s = round_e4m3(sc);
-  const float inv = s > 0.f ? 1.0f / s : 0.f;
+  const float inv = s > 0.f ? (1.0f / s) * (1.0f + 1.0f / 4096.0f) : 0.f;
+  float t[KB];
+#pragma unroll
+  for (int i = 0; i < KB; ++i) t[i] = __fmaf_rn(v[i], inv, 0.0f);
   uint32_t w[KB / 8];
 #pragma unroll
   for (int q = 0; q < KB / 8; ++q)
-    w[q] = cvt_e2m1x8(e2m1_rna_value(v[8 * q] * inv), e2m1_rna_value(v[8 * q + 1] * inv),
-                      e2m1_rna_value(v[8 * q + 2] * inv), e2m1_rna_value(v[8 * q + 3] * inv),
-                      e2m1_rna_value(v[8 * q + 4] * inv), e2m1_rna_value(v[8 * q + 5] * inv),
-                      e2m1_rna_value(v[8 * q + 6] * inv), e2m1_rna_value(v[8 * q + 7] * inv));
+    w[q] = cvt_e2m1x8(t[8 * q], t[8 * q + 1], t[8 * q + 2], t[8 * q + 3], t[8 * q + 4], t[8 * q + 5],
+                      t[8 * q + 6], t[8 * q + 7]);
   if (KB == 16) *reinterpret_cast<uint2*>(out) = make_uint2(w[0], w[1]);
   else *reinterpret_cast<uint4*>(out) = make_uint4(w[0], w[1], w[2 % (KB / 8)], w[3 % (KB / 8)]);
   return sbyte;
