@@ -239,6 +239,28 @@ constexpr int QK_SMEM_K = QK_TILE_BYTES + 64 * DS_LD * 2;  // tile + 64 query-gr
 __device__ void ds_tile(const __nv_bfloat16* kcs, __nv_bfloat16* qms, const __nv_bfloat16* __restrict__ qmean,
                         __nv_bfloat16* __restrict__ ds, int bh, int G, int Lp, int n0);
 
+// 16-byte global -> shared copy that bypasses registers (src_size 0: zero fill).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sm100::smem_u32(smem)), "l"(gmem),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Rows [g0, g0 + 64) of this head's query-group means -> qms ([64][DS_LD]),
+// zero past G: four 16-byte copies per thread of the 256.
+__device__ __forceinline__ void qmean_chunk_async(__nv_bfloat16* qms, const __nv_bfloat16* __restrict__ qmean, int bh,
+                                                  int G, int g0) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = threadIdx.x + 256 * k, r = i >> 4, c = i & 15;
+    const bool valid = g0 + r < G;
+    cp_async16(qms + r * DS_LD + c * 8,
+               qmean + (static_cast<int64_t>(bh) * G + (valid ? g0 + r : 0)) * 128 + c * 8, valid);
+  }
+  cp_async_commit();
+}
+
 template <bool kIsQ, int kFmt>
 __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __restrict__ x, int H, int L, int Lp,
                                                        int64_t sb, int64_t sn, int64_t sh,
@@ -251,6 +273,8 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
   const int t0 = blockIdx.y * 128;
   const int c = threadIdx.x & 15, r0 = threadIdx.x >> 4;
+  if (!kIsQ && smoothing)  // the first 64 query-group means for delta_s, fetched while K is quantised
+    qmean_chunk_async(reinterpret_cast<__nv_bfloat16*>(qk_smem + QK_TILE_BYTES), qmean, bh, Lp / 128, 0);
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -341,22 +365,39 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
 
 // ---------------------------------------------------------------- V quantisation
 // grid (BH, Lp/128), 128 threads: thread d quantises V[:, d] over the tile's
-// 128 keys in groups of 32 (NVFP4: 16) in format kFmt and writes 64 (E2M1)
-// or 128 (E4M3) code bytes of row (bh, d) of V^T.
+// 128 keys in groups of 32 (NVFP4: 16) in format kFmt into 64 (E2M1) or 128
+// (E4M3) code bytes of row (bh, d) of V^T, staged in shared memory and then
+// written row by row in 16-byte pieces (coalesced).
+constexpr int V_TILE_BYTES = 128 * (128 + 8) * 2;
+template <int kFmt>
+__host__ __device__ constexpr int v_code_ld() { return (kFmt == F_MX8 ? 128 : 64) + 16; }  // staged code row (bytes, padded)
+template <int kFmt>
+__host__ __device__ constexpr int v_smem_bytes() { return V_TILE_BYTES + 128 * v_code_ld<kFmt>(); }
+
 template <int kFmt>
 __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __restrict__ v, int H, int L, int Lp,
                                                       int64_t sb, int64_t sn, int64_t sh,
                                                       uint8_t* __restrict__ vt, uint8_t* __restrict__ vsf,
                                                       const float* __restrict__ vsum, float* __restrict__ vmean) {
-  __shared__ __nv_bfloat16 tile[128][128 + 8];
+  extern __shared__ __align__(16) uint8_t v_smem[];
+  auto tile = reinterpret_cast<__nv_bfloat16 (*)[128 + 8]>(v_smem);
+  uint8_t* cst = v_smem + V_TILE_BYTES;  // [128][v_code_ld] staged code rows
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
   const int t0 = blockIdx.y * 128;
-  for (int i = threadIdx.x; i < 128 * 16; i += 128) {
-    const int r = i >> 4, c = i & 15;
-    const int n = t0 + r;
-    uint4 u = make_uint4(0, 0, 0, 0);
-    if (n < L) u = ld_stream(reinterpret_cast<const uint4*>(v + nhd_row(b, n, h, sb, sn, sh) + c * 8));
-    *reinterpret_cast<uint4*>(&tile[r][c * 8]) = u;
+  {
+    uint4 u[16];  // all 16 loads in flight before the first shared-memory store
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int i = threadIdx.x + 128 * k, r = i >> 4, c = i & 15;
+      const int n = t0 + r;
+      u[k] = n < L ? ld_stream(reinterpret_cast<const uint4*>(v + nhd_row(b, n, h, sb, sn, sh) + c * 8))
+                   : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int i = threadIdx.x + 128 * k;
+      *reinterpret_cast<uint4*>(&tile[i >> 4][(i & 15) * 8]) = u[k];
+    }
   }
   __syncthreads();
   const int d = threadIdx.x;
@@ -370,8 +411,7 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
     for (int r = 0; r < 128 && t0 + r < L; ++r)
       tile[r][d] = __float2bfloat16_rn(__bfloat162float(tile[r][d]) - vm);
   }
-  uint8_t* row = kF8 ? vt + (static_cast<int64_t>(bh) * 128 + d) * Lp + blockIdx.y * 128
-                     : vt + (static_cast<int64_t>(bh) * 128 + d) * (Lp / 2) + blockIdx.y * 64;
+  uint8_t* row = cst + d * v_code_ld<kFmt>();
   uint8_t* sft = vsf + (static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 1024 + (d % 32) * 16 + (d / 32) * 4;
   if (kFmt == F_NV4B32) {
     uint32_t sfw[2] = {0, 0};
@@ -406,6 +446,14 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
     }
     *reinterpret_cast<uint32_t*>(sft) = sfw;
   }
+  __syncthreads();
+  constexpr int kRow = kF8 ? 128 : 64, kChunks = kRow / 16;
+  const int64_t vld = kF8 ? Lp : Lp / 2;  // V^T row length in bytes
+  for (int i = threadIdx.x; i < 128 * kChunks; i += 128) {
+    const int rr = i / kChunks, c = i % kChunks;
+    *reinterpret_cast<uint4*>(vt + (static_cast<int64_t>(bh) * 128 + rr) * vld + blockIdx.y * kRow + c * 16) =
+        *reinterpret_cast<const uint4*>(cst + rr * v_code_ld<kFmt>() + c * 16);
+  }
 }
 
 // ---------------------------------------------------------------- delta_s
@@ -437,12 +485,8 @@ __device__ void ds_tile(const __nv_bfloat16* kcs, __nv_bfloat16* qms, const __nv
   const int wn = warp & 3;         // 0..3: keys [32 wn, 32 wn + 32)
   for (int g0 = 0; g0 < G; g0 += 64) {
     __syncthreads();  // previous chunk's qms reads are done (and kcs is ready on the first pass)
-    for (int i = threadIdx.x; i < 64 * 16; i += 256) {
-      const int r = i >> 4, c = i & 15;
-      uint4 u = make_uint4(0, 0, 0, 0);
-      if (g0 + r < G) u = *reinterpret_cast<const uint4*>(qmean + (static_cast<int64_t>(bh) * G + g0 + r) * 128 + c * 8);
-      *reinterpret_cast<uint4*>(qms + r * DS_LD + c * 8) = u;
-    }
+    if (g0 > 0) qmean_chunk_async(qms, qmean, bh, G, g0);  // chunk 0 was issued at kernel start
+    cp_async_wait_all();
     __syncthreads();
     float acc[2][4][4] = {};
 #pragma unroll
@@ -510,9 +554,25 @@ int launch_qk(const Problem& p, const Workspace& w, cudaStream_t s) {
   return QDQ_OK;
 }
 
+// The V pass of format kFmt (dynamic shared memory above the 48 KB default).
+template <int kFmt>
+int launch_v(const Problem& p, const Workspace& w, const float* vs, cudaStream_t s) {
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(v_quant_kernel<kFmt>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             v_smem_bytes<kFmt>()) != cudaSuccess)
+      return fail(QDQ_ERR_CUDA, "sage3 prepass: smem attribute");
+    attr[dev] = true;
+  }
+  v_quant_kernel<kFmt><<<dim3(p.B * p.H, p.Lp / 128), 128, v_smem_bytes<kFmt>(), s>>>(
+      p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf, vs, w.vmean);
+  return QDQ_OK;
+}
+
 int launch_prepass(const Problem& p, const Workspace& w, cudaStream_t s) {
   const int BH = p.B * p.H;
-  const int T = p.Lp / 128;
   if (cudaMemsetAsync(w.ksum, 0, sizeof(float) * BH * 128, s) != cudaSuccess)
     return fail(QDQ_ERR_CUDA, "sage3 prepass: memset failed");
   if (p.smoothing)
@@ -533,16 +593,13 @@ int launch_prepass(const Problem& p, const Workspace& w, cudaStream_t s) {
   if (st != QDQ_OK) return st;
   // V^T in the P/V format
   const float* vs = p.vsmooth ? w.vsum : nullptr;
-#define QDQ_V(FMT)                                                                                           \
-  v_quant_kernel<FMT><<<dim3(BH, T), 128, 0, s>>>(p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf, vs, \
-                                                  w.vmean)
   switch (p.pv_fmt) {
-    case F_MX8: QDQ_V(F_MX8); break;
-    case F_NV4: QDQ_V(F_NV4); break;
-    case F_NV4B32: QDQ_V(F_NV4B32); break;
-    default: QDQ_V(F_MX4); break;
+    case F_MX8: st = launch_v<F_MX8>(p, w, vs, s); break;
+    case F_NV4: st = launch_v<F_NV4>(p, w, vs, s); break;
+    case F_NV4B32: st = launch_v<F_NV4B32>(p, w, vs, s); break;
+    default: st = launch_v<F_MX4>(p, w, vs, s); break;
   }
-#undef QDQ_V
+  if (st != QDQ_OK) return st;
   return check_launch("sage3 prepass");
 }
 
