@@ -152,11 +152,17 @@ struct Params {
 // scale in both of its 16-element slots, which multiplies every element by
 // the same scale as one per-32 slot would.
 
-// Sum of four fp16x2 words holding decoded E2M1 values (exact in fp16: the
-// values are multiples of 0.5 and at most 6, a sum of 16 of them at most 96).
-__device__ __forceinline__ __half2 hsum4(const uint32_t (&h)[4]) {
-  const __half2* v = reinterpret_cast<const __half2*>(h);
-  return __hadd2(__hadd2(v[0], v[1]), __hadd2(v[2], v[3]));
+// acc + the sum of 2 * value over eight non-negative E2M1 codes (one per
+// nibble of w): prmt looks each 3-bit magnitude up in {0, 1, 2, 3, 4, 6, 8,
+// 12} (twice the E2M1 values, one byte each) and dp4a adds the bytes; exact.
+__device__ __forceinline__ uint32_t e2m1x8_sum2(uint32_t w, uint32_t acc) {
+  const uint32_t lo = __byte_perm(0x03020100u, 0x0C080604u, w & 0xFFFFu);
+  const uint32_t hi = __byte_perm(0x03020100u, 0x0C080604u, w >> 16);
+  return __dp4a(hi, 0x01010101u, __dp4a(lo, 0x01010101u, acc));
+}
+// A small non-negative integer (< 2^23) as a float, without the I2F unit.
+__device__ __forceinline__ float small_u2f(uint32_t v) {
+  return __uint_as_float(0x4B000000u | v) - 8388608.0f;
 }
 
 // Shared-memory accesses through 32-bit shared-window addresses.
@@ -517,7 +523,7 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
         }
         const float cg = p.p_prescale_lg2 - m_new - lg2s;
         const float2 c2 = make_float2(cg, cg);
-        __half2 hs = __floats2half2_rn(0.f, 0.f);
+        uint32_t isum = 0;  // sum of 2 * the block's E2M1 values (p >= 0: no sign bits)
         uint32_t w[GS / 8];
 #pragma unroll
         for (int q = 0; q < GS / 8; ++q) {
@@ -529,11 +535,10 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
             v[2 * i] = ex2_approx(t.x);
             v[2 * i + 1] = ex2_approx(t.y);
           }
-          uint32_t h[4];
-          w[q] = e2m1_roundtrip8(v, h);
-          hs = __hadd2(hs, hsum4(h));
+          w[q] = cvt_e2m1x8(v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7]);
+          isum = e2m1x8_sum2(w[q], isum);
         }
-        lq = fmaf(__low2float(hs) + __high2float(hs), deq, lq);
+        lq = fmaf(small_u2f(isum), 0.5f * deq, lq);
         if (kNV) {
           // 16-byte chunk gg/2 of the row holds blocks 2*(gg/2), 2*(gg/2)+1
           sts64(prow + (((gg >> 1) ^ swz) << 4) + (gg & 1) * 8, w[0], w[1]);
