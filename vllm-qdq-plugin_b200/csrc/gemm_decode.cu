@@ -106,15 +106,23 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
   const int n_blk = blockIdx.x;
   const int num_kt = (K + DBK - 1) / DBK;
 
-  // One stage's loads: the W tile, its scales and the raw A slice.
-  auto issue_stage = [&](int kt) {
+  // One stage's loads: the W tile and its scales (weights), then the raw A
+  // slice (the activation, which the previous kernel on the stream may write).
+  auto issue_w = [&](int kt) {
     const int s = kt % S;
     uint8_t* st = smem + s * Lay::STAGE;
     mbar_arrive_expect_tx(&bars->raw[s], W_TILE + SF_STAGE + Lay::RAW);
     tma_load_2d(st + Lay::ST_W, &tmap_w, kt * DBKB, n_blk * DBM, &bars->raw[s]);
     bulk_load(st + Lay::ST_SFW, sfw + (static_cast<int64_t>(n_blk) * kchunks + 2 * kt) * 512, SF_STAGE,
               &bars->raw[s]);
-    tma_load_2d(st + Lay::ST_RAW, &tmap_a, kt * DBK, 0, &bars->raw[s]);
+  };
+  auto issue_a = [&](int kt) {
+    const int s = kt % S;
+    tma_load_2d(smem + s * Lay::STAGE + Lay::ST_RAW, &tmap_a, kt * DBK, 0, &bars->raw[s]);
+  };
+  auto issue_stage = [&](int kt) {
+    issue_w(kt);
+    issue_a(kt);
   };
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -127,12 +135,15 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
     fence_barrier_init();
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_a);
-    // The first ring of loads needs neither TMEM nor the cleared tiles, so it
-    // starts before them: the HBM latency overlaps the rest of the prologue.
+    // The first ring of weight loads needs neither TMEM nor the cleared tiles,
+    // nor the previous kernel on the stream, so it starts before all of them:
+    // the HBM latency overlaps the prologue (and, under programmatic dependent
+    // launch, the previous kernel's tail).
     const int pre = min(S, num_kt);
-    for (int kt = 0; kt < pre; ++kt) issue_stage(kt);
+    for (int kt = 0; kt < pre; ++kt) issue_w(kt);
     bars->preissued = pre;
   }
+  pdl_launch_dependents();
   // Activation rows >= M and their scales stay zero for the whole launch
   // (disjoint from the W, W-scale and raw-A bytes the loads above write).
   constexpr int kZero = (Lay::A_TILE + 2 * SF_STAGE) / 16;  // A codes + both scale chunks
@@ -145,6 +156,11 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
     tmem_alloc(&bars->tmem_base, D_TMEM_COLS);
     tmem_relinquish();
   }
+  // Everything below reads the activation or writes C: the previous kernel
+  // on the stream must have completed (programmatic dependent launch).
+  pdl_wait();
+  if (threadIdx.x == 0)
+    for (int kt = 0; kt < bars->preissued; ++kt) issue_a(kt);
   fence_proxy_async_smem();  // the zeroed operand bytes are read by the tensor core
   tc_fence_before();
   __syncthreads();
@@ -274,10 +290,23 @@ int launch_decode(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* s
     if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_linear_decode: smem attribute: %s", cudaGetErrorString(e));
     attr_set[dev] = true;
   }
-  dim3 grid(static_cast<unsigned>((N + DBM - 1) / DBM));
-  mxf4_decode_kernel<kDtype, kNA><<<grid, D_THREADS, smem, s>>>(tw, ta, sf, bias, c, static_cast<int>(M),
-                                                               static_cast<int>(N), static_cast<int>(K), ldc,
-                                                               kchunks, status);
+  // Programmatic dependent launch: the kernel streams its first weight tiles
+  // while the previous kernel on the stream finishes (griddepcontrol.wait
+  // guards every activation read and output write).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((N + DBM - 1) / DBM));
+  cfg.blockDim = dim3(D_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, mxf4_decode_kernel<kDtype, kNA>, tw, ta, sf, bias, c,
+                                           static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), ldc,
+                                           kchunks, status);
+  if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_linear_decode: launch: %s", cudaGetErrorString(e));
   return check_launch("fp4_linear_decode");
 }
 

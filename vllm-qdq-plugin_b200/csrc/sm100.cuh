@@ -371,6 +371,17 @@ __device__ __forceinline__ uint64_t smem_desc_sw64(const void* smem) {
   d |= static_cast<uint64_t>(4) << 61;  // SWIZZLE_64B
   return d;
 }
+// Programmatic dependent launch (PTX griddepcontrol).  launch_dependents lets
+// the next grid on the stream (launched with programmatic stream
+// serialization) start once every CTA of this grid has issued it or exited;
+// wait blocks the calling thread until the previous grid on the stream has
+// completed and its memory operations are visible (a no-op when the grid was
+// launched without the attribute).
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
