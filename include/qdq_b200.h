@@ -165,6 +165,13 @@ int64_t fp4_linear_workspace_bytes(int64_t M, int64_t K);
  * scales, into `workspace`), then multiplied with the MXFP4 weight as in
  * fp4_gemm_mxf4; c and bias have the activation's dtype.  Output equals marlin_gemm(mxfp4_qdq(a), W) up to fp32
  * summation order.
+ * Stream order: fp4_linear_mxf4 and fp4_gemm_mxf4 (M > 128) launch with
+ * programmatic dependent launch.  Their kernels may start while the previous
+ * kernel on the stream finishes and prefetch the weight (w_codes, w_sf_tiled)
+ * before waiting for it; the activation, workspace, bias and output are
+ * touched only after that kernel has completed.  The weight must therefore
+ * not be written by the kernel launched just before the call (as in
+ * inference, where weights are static).
  */
 int fp4_linear_mxf4(const void* a, int64_t lda, int dtype, const void* w_codes,
                     const void* w_sf_tiled, const void* bias, void* c, int64_t M, int64_t N,

@@ -344,33 +344,51 @@ mxf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
   tc_fence_before();
   cluster_sync();  // both CTAs' barriers are initialised and the TMEM is allocated
   tc_fence_after();
+  pdl_launch_dependents();
   const uint32_t tmem = bars->tmem_base;
 
   if (warp == 0) {
     // ---------------- producer (both CTAs): own halves, landing on the leader's barrier
     if (elect_one()) {
+      // A stage's weight loads (W codes and both W scale chunks) and its
+      // activation loads (codes and scales: the previous kernel on the stream
+      // writes them).
+      auto load_w = [&](int s, int n_blk, int kt) {
+        uint8_t* st = smem + s * P_STAGE;
+        const uint32_t full0 = cluster_addr(&bars->full[s], 0);
+        if (rank == 0) mbar_arrive_expect_tx(&bars->full[s], P_TX);
+        tma_load_2d_pair(st + P_A, &tmap_b, kt * BKB, n_blk * BN + static_cast<int>(rank) * 128, full0);
+        tma_load_2d_pair(st + P_A + P_B + P_SFA, &tmap_sfb, 0, (n_blk * 2) * kchunks + 2 * kt, full0);
+        tma_load_2d_pair(st + P_A + P_B + P_SFA + 1024, &tmap_sfb, 0, (n_blk * 2 + 1) * kchunks + 2 * kt, full0);
+      };
+      auto load_a = [&](int s, int m_blk, int kt) {
+        uint8_t* st = smem + s * P_STAGE;
+        const uint32_t full0 = cluster_addr(&bars->full[s], 0);
+        tma_load_2d_pair(st, &tmap_a, kt * BKB, m_blk * 256 + static_cast<int>(rank) * 128, full0);
+        tma_load_2d_pair(st + P_A + P_B, &tmap_sfa, 0, (m_blk * 2 + static_cast<int>(rank)) * kchunks + 2 * kt,
+                         full0);
+      };
+      // The first ring of the first tile's weight loads goes out before
+      // griddepcontrol.wait (programmatic dependent launch): it overlaps the
+      // tail of the kernel that produces the activation codes.
+      const int pre = pair < num_tiles ? min(P_STAGES, num_kt) : 0;
+      for (int kt = 0; kt < pre; ++kt) load_w(kt, pair / num_m, kt);
+      pdl_wait();
+      for (int kt = 0; kt < pre; ++kt) load_a(kt, pair % num_m, kt);
       int it = 0;
       bool ok = true;
       for (int tile = pair; ok && tile < num_tiles; tile += num_pairs) {
         const int m_blk = tile % num_m, n_blk = tile / num_m;
-        const int a_row = m_blk * 256 + static_cast<int>(rank) * 128;
-        const int b_row = n_blk * BN + static_cast<int>(rank) * 128;
         for (int kt = 0; kt < num_kt; ++kt, ++it) {
+          if (it < pre) continue;  // issued above
           const int s = it % P_STAGES;
           if (!mbar_wait(&bars->empty[s], ((it / P_STAGES) & 1) ^ 1, status, 0x111)) {
             bars->abort = 1;
             ok = false;
             break;
           }
-          uint8_t* st = smem + s * P_STAGE;
-          const uint32_t full0 = cluster_addr(&bars->full[s], 0);
-          if (rank == 0) mbar_arrive_expect_tx(&bars->full[s], P_TX);
-          tma_load_2d_pair(st, &tmap_a, kt * BKB, a_row, full0);
-          tma_load_2d_pair(st + P_A, &tmap_b, kt * BKB, b_row, full0);
-          tma_load_2d_pair(st + P_A + P_B, &tmap_sfa, 0, (m_blk * 2 + static_cast<int>(rank)) * kchunks + 2 * kt,
-                           full0);
-          tma_load_2d_pair(st + P_A + P_B + P_SFA, &tmap_sfb, 0, (n_blk * 2) * kchunks + 2 * kt, full0);
-          tma_load_2d_pair(st + P_A + P_B + P_SFA + 1024, &tmap_sfb, 0, (n_blk * 2 + 1) * kchunks + 2 * kt, full0);
+          load_w(s, n_blk, kt);
+          load_a(s, m_blk, kt);
         }
       }
       // The leader's MMA waits on every stage either CTA issued; its final
@@ -382,6 +400,7 @@ mxf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader)
     if (rank == 0 && elect_one()) {
+      pdl_wait();
       int it = 0, i = 0;
       bool ok = true;
       for (int tile = pair; ok && tile < num_tiles; tile += num_pairs, ++i) {
@@ -421,6 +440,7 @@ mxf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     }
   } else {
     // ---------------- epilogue (both CTAs): TMEM lanes = the CTA's 128 tile rows
+    pdl_wait();  // C and the bias belong to the stream's order
     const int q = warp & 3, h = (warp - 2) >> 2;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ACC_COL + h * 128;
     const uint32_t acc_empty0 = cluster_addr(&bars->acc_empty, 0);
@@ -651,13 +671,16 @@ extern "C" int fp4_gemm_mxf4(const void* a_codes, const void* a_sf_tiled, const 
     cfg.blockDim = dim3(THREADS);
     cfg.dynamicSmemBytes = P_SMEM_BYTES;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // programmatic dependent launch: weight prefetch overlaps the previous kernel
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     const int m_ = static_cast<int>(M), n_ = static_cast<int>(N), k_ = static_cast<int>(K);
     cudaError_t e = out_dtype == QDQ_DTYPE_FP16
                         ? cudaLaunchKernelEx(&cfg, mxf4_gemm_pair_kernel<true>, ta, tb, tsa, tsb, bias, c, m_, n_, k_,

@@ -35,6 +35,14 @@ mxfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
                  uint32_t cpr, uint64_t total, int64_t ldx, int64_t ldy, int64_t ldc,
                  int64_t lds) {
   using F = Fmt<kDtype>;
+  if (kTiledSF) {
+    // The fused linear's activation pass, launched with programmatic dependent
+    // launch: the GEMM after it may start (and prefetch its weights) at once;
+    // this pass reads the activation and overwrites the codes the previous
+    // GEMM read, so it waits for the previous kernel first.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+  }
   const uint32_t lane = threadIdx.x & 31u;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x * kUnroll;
   for (uint64_t base = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31u)) * kUnroll;
@@ -651,9 +659,22 @@ int qdq_mxfp4_codes_tiled(const void* x, void* codes, void* sf_tiled, int64_t M,
   auto* cp = static_cast<uint8_t*>(codes);
   auto* sp = static_cast<uint8_t*>(sf_tiled);
   const bool contig = ldx == K;
-#define QDQ_TILED(DT, CONTIG)                                                                        \
-  mxfp4_vec_kernel<DT, CONTIG, false, true, true, true><<<grid, kThreads, 0, s>>>(                   \
-      xp, nullptr, cp, sp, static_cast<uint32_t>(cpr), total, ldx, K, K / 2, kchunks)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see the kernel's griddepcontrol
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  uint16_t* const no_y = nullptr;
+  const int64_t ldy_ = K, ldc_ = K / 2;
+  const uint32_t cpr32 = static_cast<uint32_t>(cpr);
+  cudaError_t e = cudaSuccess;
+#define QDQ_TILED(DT, CONTIG)                                                                                 \
+  e = cudaLaunchKernelEx(&cfg, mxfp4_vec_kernel<DT, CONTIG, false, true, true, true>, xp, no_y, cp, sp, cpr32, \
+                         total, ldx, ldy_, ldc_, kchunks)
   if (dtype == QDQ_DTYPE_BF16) {
     if (contig) QDQ_TILED(QDQ_DTYPE_BF16, true);
     else QDQ_TILED(QDQ_DTYPE_BF16, false);
@@ -662,6 +683,7 @@ int qdq_mxfp4_codes_tiled(const void* x, void* codes, void* sf_tiled, int64_t M,
     else QDQ_TILED(QDQ_DTYPE_FP16, false);
   }
 #undef QDQ_TILED
+  if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "qdq_mxfp4_codes_tiled: launch: %s", cudaGetErrorString(e));
   return check_launch("qdq_mxfp4_codes_tiled");
 }
 }  // namespace qdqb200
