@@ -105,6 +105,44 @@ int qdq_nvfp4_global_scale(const void* x, float* global_scale_out,
                            int dtype, void* stream);
 
 /*
+ * Quant-dequant of an activation held in HOST memory, with the result written
+ * to host memory.  Replaces the caller-side sequence "copy x to the GPU,
+ * mxfp4_qdq / mxfp8_qdq / NVFP4 QDQ, copy the result back"
+ * (vllm_qdq_plugin/qdq/mxfp4.py:98, qdq/mxfp8.py:73 and vLLM 0.22
+ * nvfp4_emulation_utils.py:455 take device tensors).  The rows go through
+ * the GPU in blocks of `block_rows`: H2D on an internal copy stream, the QDQ
+ * kernel on `stream`, D2H on a second internal copy stream, with
+ * staging_bytes / (2 * block_rows * K * elt) blocks in flight (at most 8),
+ * so both PCIe directions and the kernel overlap.  Output is bit-identical to
+ * the device entry points on the whole tensor (group size 32 for MXFP4 and
+ * MXFP8, 16 for NVFP4, whose `global_scale` is a device float computed over
+ * the whole tensor).
+ *
+ *   x_host, y_host  [M, K] bf16/fp16 with row strides ldx, ldy; pinned
+ *                   (cudaHostAlloc / cudaHostRegister) for the copies to run
+ *                   asynchronously
+ *   staging         device buffer of at least
+ *                   qdq_host_stream_staging_bytes(block_rows, K, dtype, 1)
+ *                   bytes; with a 16-byte aligned base and block_rows * K * elt
+ *                   a multiple of 16 every block takes the vectorised kernel
+ *
+ * Stream-ordered like every entry point: the copies start after the work
+ * already on `stream`, and `stream` continues after the last copy, so the
+ * caller synchronises `stream` before reading y_host and may release
+ * `staging` in `stream`'s order.  The two copy streams are created per device
+ * on first use and kept until exit.  Allocates no device memory.
+ */
+enum { QDQ_FORMAT_MXFP4 = 0, QDQ_FORMAT_NVFP4 = 1, QDQ_FORMAT_MXFP8 = 2 };
+int qdq_host_stream(int format, const void* x_host, void* y_host,
+                    const float* global_scale, int64_t M, int64_t K,
+                    int64_t ldx, int64_t ldy, int dtype, void* staging,
+                    int64_t staging_bytes, int64_t block_rows, void* stream);
+
+/* Staging bytes for `depth` blocks of block_rows x K in flight; -1 if invalid. */
+int64_t qdq_host_stream_staging_bytes(int64_t block_rows, int64_t K, int dtype,
+                                      int depth);
+
+/*
  * Device status word of the library on the current device: 0, or the first
  * failure a kernel recorded, as (qdq_status_t << 16) | site.  Kernels record
  * QDQ_ERR_TIMEOUT there when a bounded wait gives up (they then release their

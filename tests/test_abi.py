@@ -99,3 +99,17 @@ def test_reference_assertions_are_kept():
         mxfp4_qdq(torch.zeros(2, 3, 64, dtype=torch.bfloat16))
     with pytest.raises(AssertionError, match="fp16/bf16"):
         mxfp4_qdq(torch.zeros(2, 64, dtype=torch.float32))
+
+
+def test_host_streaming_qdq_checks_its_arguments_before_touching_a_gpu():
+    import torch
+    from vllm_qdq_plugin.qdq import qdq_from_host
+    x = torch.zeros(4, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="global_scale"):
+        qdq_from_host(x, "nvfp4")
+    with pytest.raises(ValueError, match="unknown format"):
+        qdq_from_host(x, "int4")
+    with pytest.raises(AssertionError, match="fp16/bf16"):
+        qdq_from_host(x.float(), "mxfp4")
+    with pytest.raises(ValueError, match="out must be"):
+        qdq_from_host(x, "mxfp4", out=torch.zeros(4, 32, dtype=torch.bfloat16))

@@ -245,3 +245,32 @@ def test_nvfp4_activation_knob_end_to_end(cuda_device):
     assert_bits_equal(bits(got), bits(nvfp4_qdq(a)), "NVFP4 activation knob")
     gs = oq.nvfp4_global_scale(bits(a))
     assert_bits_equal(bits(got), oq.nvfp4_qdq(bits(a), gs), "NVFP4 activation knob vs oracle")
+
+
+# ------------------------------------------------------------------ host-resident input
+@pytest.mark.parametrize("fmt", ["mxfp4", "mxfp8", "nvfp4"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_streamed_host_qdq_equals_device_qdq(cuda_device, fmt, dtype):
+    """Row blocks streamed through the GPU (H2D, QDQ and D2H on three streams)
+    give the device hook's output bit for bit: ragged last block, more blocks
+    than staging slots, pinned and pageable outputs, and back-to-back calls."""
+    from vllm_qdq_plugin.qdq import mxfp4_qdq, mxfp8_qdq, nvfp4_qdq, qdq_from_host
+    g = torch.Generator().manual_seed(11)
+    x = (torch.randn(1000, 256, generator=g) * torch.exp(torch.randn(1000, 1, generator=g) * 3)).to(dtype)
+    xd = x.to(cuda_device)
+    gs = torch.tensor([2688.0], dtype=torch.float32) / x.float().abs().max()
+    if fmt == "nvfp4":
+        want = nvfp4_qdq(xd, global_scale=gs.to(cuda_device))
+    else:
+        want = (mxfp4_qdq if fmt == "mxfp4" else mxfp8_qdq)(xd)
+    want = bits(want)
+    kw = dict(global_scale=gs) if fmt == "nvfp4" else {}
+    got = qdq_from_host(x.pin_memory(), fmt, block_bytes=37 * 256 * 2, depth=3, **kw)
+    assert got.is_pinned()
+    assert_bits_equal(bits(got), want, f"{fmt} streamed, pinned out")
+    out = torch.empty_like(x)
+    qdq_from_host(x, fmt, out=out, block_bytes=300 * 256 * 2, depth=2, **kw)
+    assert_bits_equal(bits(out), want, f"{fmt} streamed, pageable")
+    again = qdq_from_host(x.pin_memory(), fmt, non_blocking=True, **kw)
+    torch.cuda.current_stream(cuda_device).synchronize()
+    assert_bits_equal(bits(again), want, f"{fmt} streamed, one block")

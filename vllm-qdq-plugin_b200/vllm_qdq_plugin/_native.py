@@ -37,6 +37,9 @@ _SIGNATURES: dict[str, list] = {
                   _i64, _int, _c_void_p],
     "qdq_nvfp4_global_scale": [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _int,
                                _c_void_p],
+    "qdq_host_stream": [_int, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _int, _c_void_p,
+                        _i64, _i64, _c_void_p],
+    "qdq_host_stream_staging_bytes": [_i64, _i64, _int, _int],
     "qdq_last_error": [],
     "qdq_abi_version": [],
     "qdq_device_status": [ctypes.POINTER(ctypes.c_int), _int],
@@ -64,7 +67,8 @@ _RESTYPES = {"qdq_last_error": ctypes.c_char_p, "qdq_sf_tiled_bytes": ctypes.c_i
              "fp4_linear_workspace_bytes": ctypes.c_int64,
              "fp4_linear_noalloc_scratch_bytes": ctypes.c_int64,
              "sage3_attn_workspace_bytes": ctypes.c_int64,
-             "fp4_moe_workspace_bytes": ctypes.c_int64}
+             "fp4_moe_workspace_bytes": ctypes.c_int64,
+             "qdq_host_stream_staging_bytes": ctypes.c_int64}
 
 
 def lib() -> ctypes.CDLL:
