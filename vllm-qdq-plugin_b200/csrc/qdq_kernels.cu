@@ -13,6 +13,8 @@
 //   - NVFP4: vLLM 0.22 nvfp4_emulation_utils.py:439-478 (CPU branch), bit-exact.
 // All float arithmetic that the references round step by step is written with
 // __fmul_rn/__fadd_rn/__fdiv_rn so that no FMA contraction changes a rounding.
+#include <algorithm>
+
 #include "mx_quant.cuh"
 
 namespace qdqb200 {
@@ -539,10 +541,16 @@ mxfp8_generic_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y, u
   }
 }
 
+// Grid of the QDQ kernels: one CTA per `per_block` work items, so the block
+// scheduler keeps every SM at full occupancy until the last wave, with the
+// grid-stride loop only as a guard for grids beyond the hardware limit.
+// Measured on B200 against a persistent grid of 8 CTAs per SM: config 2
+// 5958 -> 6572 GB/s, config 1 5675 -> 6041 GB/s (a persistent grid with
+// equal rounds per CTA was slower still, 5222 GB/s at config 1).
 int grid_for(uint64_t work_items, int per_block) {
   const uint64_t need = (work_items + per_block - 1) / per_block;
-  const uint64_t cap = static_cast<uint64_t>(device_sm_count()) * 8u;
-  return static_cast<int>(need < 1 ? 1 : (need < cap ? need : cap));
+  constexpr uint64_t kMaxGrid = 1u << 30;
+  return static_cast<int>(need < 1 ? 1 : (need < kMaxGrid ? need : kMaxGrid));
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -778,7 +786,8 @@ int launch_global_scale(const void* x, float* gs_out, uint32_t* ws, int64_t M, i
   auto* xp = static_cast<const uint16_t*>(x);
   const bool vec = aligned16(x) && (K % 8 == 0) && (ldx % 8 == 0);
   const uint64_t work = vec ? static_cast<uint64_t>(M) * (K / 8) : static_cast<uint64_t>(M) * K;
-  const int grid = grid_for(work, kThreads * 4);
+  // a persistent grid (8 CTAs per SM): one pair of atomics per CTA on ws
+  const int grid = std::min(grid_for(work, kThreads * 4), device_sm_count() * 8);
   if (dtype == QDQ_DTYPE_BF16) {
     if (vec) amax_gs_kernel<QDQ_DTYPE_BF16, true><<<grid, kThreads, 0, s>>>(xp, M, K, ldx, ws, gs_out);
     else amax_gs_kernel<QDQ_DTYPE_BF16, false><<<grid, kThreads, 0, s>>>(xp, M, K, ldx, ws, gs_out);
