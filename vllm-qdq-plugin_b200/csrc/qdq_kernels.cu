@@ -25,13 +25,19 @@ constexpr int kThreads = 256;
 constexpr int kUnroll = 4;           // 16-byte chunks in flight per lane
 constexpr float kRecip6 = 1.0f / 6.0f;  // fp32 value of vLLM's FLOAT4_E2M1_MAX_RECIPROCAL
 
+// Resident CTAs per SM asked of the y-only MXFP4 kernel: at <= 32 registers
+// 8 CTAs fit instead of 6, keeping more 16-byte loads in flight (config 1:
+// 6012-6041 -> 6177-6181 GB/s).  The same cap measured no gain for MXFP8 and
+// a 1.5% loss for NVFP4 (capped at 40), so those keep the compiler's choice.
+constexpr int kMxMinBlocks = 8;
+
 // ---------------------------------------------------------------------------
 // MXFP4: vectorised kernel (K % 32 == 0, 16-byte aligned rows)
 // ---------------------------------------------------------------------------
 // kTiledSF: the E8M0 bytes go straight to the block-scaled GEMM's tiled
 // scale layout (qdq_sf_tile; `lds` then holds its K-chunk count).
 template <int kDtype, bool kContig, bool kY, bool kCodes, bool kScales, bool kTiledSF = false>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, (kY && !kCodes && !kScales) ? kMxMinBlocks : 1)
 mxfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
                  uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
                  uint32_t cpr, uint64_t total, int64_t ldx, int64_t ldy, int64_t ldc,
