@@ -3,7 +3,7 @@
 Run inside the build container, where the reference checkout and vLLM 0.22 are
 importable (CPU only):
 
-    python tests/golden/make_golden.py [--reference /path/to/vllm-qdq-plugin]
+    python tests/golden/make_golden.py --reference /path/to/vllm-qdq-plugin
 
 Each fixture is a compressed .npz of inputs and the reference's own outputs:
   mxfp4_bf16.npz / mxfp4_fp16.npz   reference mxfp4_qdq (src/vllm_qdq_plugin/qdq/mxfp4.py:98)
@@ -146,7 +146,7 @@ def bits_of(t: torch.Tensor) -> np.ndarray:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="checkout of the reference plugin (vllm-qdq-plugin)")
     ap.add_argument("--only", choices=["all", "mxfp8", "mxfp8_hw"], default="all")
     args = ap.parse_args()
     if args.only in ("all", "mxfp8_hw"):
