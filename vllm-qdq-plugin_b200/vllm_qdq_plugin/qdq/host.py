@@ -76,8 +76,12 @@ def qdq_from_host(x: torch.Tensor, fmt: str = "mxfp4", *, global_scale: torch.Te
     if m == 0 or k == 0:
         return out
 
-    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
-                       (device if isinstance(device, int) else device.index or 0))
+    if isinstance(device, int):
+        dev = torch.device("cuda", device)
+    elif device is None or torch.device(device).index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    else:
+        dev = torch.device(device)
     dtype = _native.DTYPE_CODE[x.dtype]
     row_bytes = k * x.element_size()
     # whole rows per block, a multiple of 8 / gcd(K, 8) so that every staging
