@@ -30,6 +30,12 @@ constexpr float kRecip6 = 1.0f / 6.0f;  // fp32 value of vLLM's FLOAT4_E2M1_MAX_
 // 6012-6041 -> 6177-6181 GB/s).  The same cap measured no gain for MXFP8 and
 // a 1.5% loss for NVFP4 (capped at 40), so those keep the compiler's choice.
 constexpr int kMxMinBlocks = 8;
+// 16-byte chunks in flight per lane of the MXFP4 kernel: 2 for the y-only
+// variant under its 32-register cap (config 1: 6337 against 6210 GB/s at 4;
+// 8 spills and drops to 4139), kUnroll otherwise.
+__host__ __device__ constexpr int mx_unroll(bool y, bool codes, bool scales) {
+  return (y && !codes && !scales) ? 2 : kUnroll;
+}
 
 // ---------------------------------------------------------------------------
 // MXFP4: vectorised kernel (K % 32 == 0, 16-byte aligned rows)
@@ -37,12 +43,13 @@ constexpr int kMxMinBlocks = 8;
 // kTiledSF: the E8M0 bytes go straight to the block-scaled GEMM's tiled
 // scale layout (qdq_sf_tile; `lds` then holds its K-chunk count).
 template <int kDtype, bool kContig, bool kY, bool kCodes, bool kScales, bool kTiledSF = false>
-__global__ void __launch_bounds__(kThreads, (kY && !kCodes && !kScales) ? kMxMinBlocks : 1)
+__global__ void __launch_bounds__(kThreads, (kY && !kCodes && !kScales) ? kMxMinBlocks : 0)
 mxfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
                  uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
                  uint32_t cpr, uint64_t total, int64_t ldx, int64_t ldy, int64_t ldc,
                  int64_t lds) {
   using F = Fmt<kDtype>;
+  constexpr int kU = mx_unroll(kY, kCodes, kScales);
   if (kTiledSF) {
     // The fused linear's activation pass, launched with programmatic dependent
     // launch: the GEMM after it may start (and prefetch its weights) at once;
@@ -52,14 +59,14 @@ mxfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
     asm volatile("griddepcontrol.wait;" ::: "memory");
   }
   const uint32_t lane = threadIdx.x & 31u;
-  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x * kUnroll;
-  for (uint64_t base = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31u)) * kUnroll;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x * kU;
+  for (uint64_t base = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31u)) * kU;
        base < total; base += stride) {
-    uint4 v[kUnroll];
-    uint64_t xo[kUnroll], yo[kUnroll], co[kUnroll], so[kUnroll];
-    bool ok[kUnroll];
+    uint4 v[kU];
+    uint64_t xo[kU], yo[kU], co[kU], so[kU];
+    bool ok[kU];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const uint64_t c = base + static_cast<uint64_t>(u) * 32u + lane;
       ok[u] = c < total;
       if (kContig) {
@@ -84,7 +91,7 @@ mxfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
       v[u] = ok[u] ? ld_stream(reinterpret_cast<const uint4*>(x + xo[u])) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < kU; ++u) {
       uint32_t amax = absmax8(v[u]);
       amax = max(amax, __shfl_xor_sync(kFull, amax, 1));
       amax = max(amax, __shfl_xor_sync(kFull, amax, 2));
@@ -633,7 +640,7 @@ extern "C" int qdq_mxfp4(const void* x, void* y, void* codes, void* scales, int6
                    (ldy % 8 == 0) && (codes == nullptr || aligned4(codes)) && o != kOutOther;
   const bool contig = (ldx == K) && (ldy == K);
   if (vec && (contig || total < (1ull << 32))) {
-    const int grid = grid_for(total, kThreads * kUnroll);
+    const int grid = grid_for(total, kThreads * (o == kOutY ? mx_unroll(true, false, false) : kUnroll));
     if (dtype == QDQ_DTYPE_BF16) {
       if (contig) dispatch_mx_vec<QDQ_DTYPE_BF16, true>(o, grid, s, xp, yp, cp, sp, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
       else dispatch_mx_vec<QDQ_DTYPE_BF16, false>(o, grid, s, xp, yp, cp, sp, (uint32_t)cpr, total, ldx, ldy, ldc, lds);
