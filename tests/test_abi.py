@@ -113,3 +113,12 @@ def test_host_streaming_qdq_checks_its_arguments_before_touching_a_gpu():
         qdq_from_host(x.float(), "mxfp4")
     with pytest.raises(ValueError, match="out must be"):
         qdq_from_host(x, "mxfp4", out=torch.zeros(4, 32, dtype=torch.bfloat16))
+
+
+def test_host_stream_format_codes_match_the_header():
+    import re
+    from vllm_qdq_plugin.qdq import host
+    header = (REPO / "include" / "qdq_b200.h").read_text()
+    codes = {m.group(1).lower(): int(m.group(2))
+             for m in re.finditer(r"QDQ_FORMAT_(\w+)\s*=\s*(\d+)", header)}
+    assert codes == host._FORMATS
