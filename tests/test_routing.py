@@ -15,7 +15,7 @@ import torch
 
 from vllm_qdq_plugin.sage3_attn.impl import Sage3TritonImpl
 from vllm_qdq_plugin.sage3_attn.routing import patch_attention as P
-from vllm_qdq_plugin.sage3_attn.routing.route_table import RouteTable, _parse_ranges, allowed_configs
+from vllm_qdq_plugin.sage3_attn.routing.route_table import IntervalSet, RouteTable, route_vocabulary
 
 
 def _route(tmp_path, data, name="route.json") -> str:
@@ -30,13 +30,21 @@ def _route(tmp_path, data, name="route.json") -> str:
     ("5", {5}), ("3-3", {3}), ("", set()), (" 1 - 3 , 5 ", {1, 2, 3, 5}),
 ])
 def test_parse_ranges(spec, want):
-    assert _parse_ranges(spec) == want
+    assert IntervalSet.parse(spec) == want
+    assert all(x in IntervalSet.parse(spec) for x in want)
+    assert -1 not in IntervalSet.parse(spec) and 10**6 not in IntervalSet.parse(spec)
 
 
-@pytest.mark.parametrize("spec", ["7-3", "a-b", "1-x"])
+def test_intervals_are_sorted_and_merged():
+    assert IntervalSet.parse("12-15,0-3,4-7,9,6-8").intervals() == [(0, 9), (12, 15)]
+    assert IntervalSet.parse(7).intervals() == [(7, 7)]
+    assert None not in IntervalSet.parse("0-3")
+
+
+@pytest.mark.parametrize("spec", ["7-3", "a-b", "1-x", "-2", "1-2-3"])
 def test_parse_ranges_rejects(spec):
     with pytest.raises(ValueError):
-        _parse_ranges(spec)
+        IntervalSet.parse(spec)
 
 
 # ------------------------------------------------------------------ resolution
@@ -69,7 +77,7 @@ def test_load_rules(tmp_path):
     assert t.resolve(7, 0) == "mxfp4" and t.resolve(8, 0) is None
     assert RouteTable.from_json_file(_route(tmp_path, {"default": "sdpa", "rules": []})).resolve(0, 0) == "sdpa"
     # every config name the reference registers is a valid route target
-    assert {"mxfp4_s1_e4m3", "mixed_fp4qk_fp8pv_vs", "mxfp8_hw", "sdpa"} <= allowed_configs()
+    assert {"mxfp4_s1_e4m3", "mixed_fp4qk_fp8pv_vs", "mxfp8_hw", "sdpa"} <= route_vocabulary()
 
 
 @pytest.mark.parametrize("data", [

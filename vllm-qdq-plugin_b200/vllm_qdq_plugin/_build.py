@@ -47,18 +47,40 @@ def nvcc_path() -> str:
     raise RuntimeError("nvcc not found: cannot build libqdq_b200.so for sm_100a")
 
 
-def build_native(force: bool = False, verbose: bool = False) -> Path:
-    """Compile every csrc/*.cu into one sm_100a shared library (idempotent)."""
-    if not force and not is_stale():
-        return LIB_PATH
-    LIB_DIR.mkdir(parents=True, exist_ok=True)
-    tmp = LIB_PATH.with_name(f".{LIB_PATH.name}.{os.getpid()}.tmp")
-    cmd = [nvcc_path(), *ARCH_FLAGS, *NVCC_FLAGS, f"-I{INCLUDE_DIR}", f"-I{CSRC_DIR}",
-           "-o", str(tmp), *[str(s) for s in sources()]]
+def _run(cmd: list[str], verbose: bool) -> None:
     if verbose:
         print(" ".join(cmd))
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if proc.returncode != 0:
         raise RuntimeError(f"nvcc failed ({proc.returncode}):\n{proc.stdout}\n{proc.stderr}")
-    os.replace(tmp, LIB_PATH)
+
+
+def build_native(force: bool = False, verbose: bool = False) -> Path:
+    """Compile every csrc/*.cu into one sm_100a shared library (idempotent).
+
+    Each translation unit is compiled to an object file in parallel (one nvcc
+    per source), then nvcc links the objects into the shared library."""
+    if not force and not is_stale():
+        return LIB_PATH
+    from concurrent.futures import ThreadPoolExecutor
+
+    LIB_DIR.mkdir(parents=True, exist_ok=True)
+    obj_dir = LIB_DIR / f".obj.{os.getpid()}"
+    obj_dir.mkdir(exist_ok=True)
+    compile_flags = [f for f in NVCC_FLAGS if f != "-shared"]
+    jobs = []
+    for src in sources():
+        obj = obj_dir / (src.stem + ".o")
+        jobs.append((obj, [nvcc_path(), *ARCH_FLAGS, *compile_flags, f"-I{INCLUDE_DIR}", f"-I{CSRC_DIR}",
+                           "-c", "-o", str(obj), str(src)]))
+    try:
+        with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as pool:
+            for fut in [pool.submit(_run, cmd, verbose) for _, cmd in jobs]:
+                fut.result()
+        tmp = LIB_PATH.with_name(f".{LIB_PATH.name}.{os.getpid()}.tmp")
+        _run([nvcc_path(), *ARCH_FLAGS, "-shared", "-Xcompiler", "-fPIC", "-o", str(tmp),
+              *[str(o) for o, _ in jobs]], verbose)
+        os.replace(tmp, LIB_PATH)
+    finally:
+        shutil.rmtree(obj_dir, ignore_errors=True)
     return LIB_PATH

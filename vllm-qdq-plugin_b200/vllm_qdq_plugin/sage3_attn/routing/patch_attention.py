@@ -80,4 +80,4 @@ def install(route_file: str) -> None:
     Attention._run_local_attention = _routed_run_local_attention
     _installed = True
     logger.warning("sage3 per-(layer, step) attention routing installed from %s (default=%s, %d rule(s))",
-                   route_file, table.default, len(table.rules))
+                   route_file, table.default, len(table))
