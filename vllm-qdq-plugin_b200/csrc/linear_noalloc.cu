@@ -17,11 +17,20 @@
 //     M <= 14561 rows); larger calls are rejected with QDQ_ERR_INVALID_ARG;
 //   - all calls on a device share the one array; two calls whose kernels can
 //     overlap on the GPU (different streams without ordering) race on it;
-//   - the array keeps the last call's contents; every byte a call reads is
-//     written earlier in the same call, so nothing has to be cleared.
+//   - the array keeps the last call's contents and is never cleared.  Every
+//     activation code and every scale byte of a real row (row < M) is written
+//     earlier in the same call.  The GEMM also reads the tiled scale bytes of
+//     the pad rows that complete the last 128-row block (M <= row < 128 *
+//     ceil(M / 128)); this call does not write them, so they hold whatever an
+//     earlier call left.  Those scales only multiply the pad rows' codes,
+//     which the tensor map fills with zeros, and pad rows of the product are
+//     never stored, so they cannot reach the output.
 // The first call on each device looks up the array's device address with
 // cudaGetSymbolAddress (with that device current); make that first call
-// before any stream capture.
+// before any stream capture.  The per-device lookup is guarded by a mutex, so
+// host threads may make their first calls concurrently.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace qdqb200 {
@@ -32,6 +41,7 @@ constexpr int64_t kLinearScratchBytes = 32ll << 20;
 __device__ __align__(256) uint8_t g_linear_scratch[kLinearScratchBytes];
 
 uint8_t* linear_scratch_ptr() {
+  static std::mutex lock;
   static uint8_t* cache[64] = {nullptr};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -39,6 +49,7 @@ uint8_t* linear_scratch_ptr() {
     set_error("fp4_linear_mxf4_noalloc: cudaGetDevice failed");
     return nullptr;
   }
+  std::lock_guard<std::mutex> guard(lock);
   if (cache[dev] == nullptr) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_linear_scratch);

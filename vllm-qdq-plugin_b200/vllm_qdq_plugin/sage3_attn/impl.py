@@ -21,9 +21,16 @@ import torch.nn.functional as F
 
 from .. import envs
 from .._log import init_logger
-from .sage3.api import sage3_attention_nhd
+from .sage3.api import sage3_attention_nhd, unsupported_reason
 
 logger = init_logger(__name__)
+_WARNED: set[str] = set()
+
+
+def _warn_once(msg: str) -> None:
+    if msg not in _WARNED:
+        _WARNED.add(msg)
+        logger.warning("Sage3 FP4 attention: %s; this call runs SDPA instead", msg)
 
 try:
     from vllm_omni.diffusion.attention.backends.abstract import AttentionImpl, AttentionMetadata
@@ -55,6 +62,13 @@ class Sage3TritonImpl(AttentionImpl):
                      config_override: str | None = None) -> torch.Tensor:
         # Cross-attention (different Q and K/V lengths) goes to SDPA, as in the reference.
         if query.shape[1] != key.shape[1]:
+            return self._forward_sdpa(query, key, value)
+        # The backend advertises the reference's head sizes (32-256); the FP4
+        # kernels take the head dims and dtypes in sage3.api.SUPPORTED_*.  A call
+        # outside them runs SDPA, with one warning per (head dim, dtype).
+        why = unsupported_reason(query)
+        if why is not None:
+            _warn_once(why)
             return self._forward_sdpa(query, key, value)
         return self._forward_sage3(query, key, value, config=config_override or self._config)
 

@@ -144,14 +144,50 @@ def _(q, k, v, layout_nhd, sm_scale, quant_format, acc_mode, causal, smoothing):
     return torch.empty_like(q)
 
 
+# Head dims and input dtypes the FP4 kernels take.
+SUPPORTED_HEAD_DIMS = (128,)
+SUPPORTED_DTYPES = (torch.bfloat16,)
+
+
+def unsupported_reason(q: torch.Tensor) -> Optional[str]:
+    """Why the FP4 kernels cannot take this query tensor, or None if they can."""
+    if q.shape[-1] not in SUPPORTED_HEAD_DIMS:
+        return f"head_dim {q.shape[-1]} (kernels take {list(SUPPORTED_HEAD_DIMS)})"
+    if q.dtype not in SUPPORTED_DTYPES:
+        return f"{q.dtype} inputs (kernels take {[str(d) for d in SUPPORTED_DTYPES]})"
+    return None
+
+
 def _check_inputs(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_dim: int) -> None:
     if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
         raise ValueError(f"q/k/v must share one 4-D shape, got {tuple(q.shape)}, "
                          f"{tuple(k.shape)}, {tuple(v.shape)}")
-    if q.dtype != torch.bfloat16 or k.dtype != q.dtype or v.dtype != q.dtype:
-        raise NotImplementedError(f"this build's FP4 attention takes bf16 inputs (got {q.dtype})")
-    if q.shape[-1] != 128:
-        raise NotImplementedError(f"this build's FP4 attention supports head_dim 128 (got {q.shape[-1]})")
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError(f"q/k/v must share one dtype, got {q.dtype}, {k.dtype}, {v.dtype}")
+    why = unsupported_reason(q)
+    if why is not None:
+        raise NotImplementedError(f"this build's FP4 attention does not take {why}")
+
+
+_ACC_WARNED: set[str] = set()
+
+
+def _acc_mode(acc_dtype: str) -> int:
+    """Validate acc_dtype (the reference's ACC_DTYPE_MAP names).  The kernels
+    accumulate QK^T, the softmax and PV in fp32 for every mode; the reference's
+    reduced-precision modes (e.g. bf16_pv_only: O rescaled and accumulated in
+    bf16, attention_kernel.py:88,169,191) are not emulated, which changes the
+    output by far less than the FP4 quantisation itself.  A non-fp32 mode is
+    logged once."""
+    if acc_dtype not in ACC_DTYPE_MAP:
+        raise ValueError(f"Unknown acc_dtype '{acc_dtype}'. Available: {list(ACC_DTYPE_MAP.keys())}")
+    if acc_dtype != "fp32" and acc_dtype not in _ACC_WARNED:
+        _ACC_WARNED.add(acc_dtype)
+        from ..._log import init_logger
+        init_logger(__name__).warning(
+            "SAGE3_ACC_DTYPE=%s: this build accumulates in fp32 for every acc_dtype "
+            "(the reference's %s accumulators are not emulated)", acc_dtype, ACC_DTYPE_MAP[acc_dtype])
+    return 0 if acc_dtype == "fp32" else 1
 
 
 def sage3_attention_nhd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, config: str = "mxfp4",
@@ -159,13 +195,11 @@ def sage3_attention_nhd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, confi
                         per_block_mean: bool = True, acc_dtype: str = "fp32") -> torch.Tensor:
     """Attention on NHD tensors [B, L, H, D] (the vllm-omni layout), output NHD."""
     fmt = _resolve_config(config)
-    if acc_dtype not in ACC_DTYPE_MAP:
-        raise ValueError(f"Unknown acc_dtype '{acc_dtype}'. Available: {list(ACC_DTYPE_MAP.keys())}")
+    acc_mode = _acc_mode(acc_dtype)
     _check_inputs(q, k, v, 1)
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(q.shape[-1])
     smoothing = _smoothing_flags(config, per_block_mean)
-    acc_mode = 0 if acc_dtype == "fp32" else 1
     return torch.ops.qdq_b200.sage3_attn(q, k, v, True, float(sm_scale), fmt, acc_mode,
                                          bool(is_causal), int(smoothing))
 
@@ -193,15 +227,13 @@ def sageattn3_standalone(
     """
     name = config if isinstance(config, str) else getattr(config, "name", str(config))
     fmt = _resolve_config(name)
-    if acc_dtype not in ACC_DTYPE_MAP:
-        raise ValueError(f"Unknown acc_dtype '{acc_dtype}'. Available: {list(ACC_DTYPE_MAP.keys())}")
+    acc_mode = _acc_mode(acc_dtype)
     if return_lse:
         raise NotImplementedError("return_lse is not yet supported by the sage3 composable implementation")
     _check_inputs(q, k, v, 2)
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(q.shape[-1])
     smoothing = _smoothing_flags(name, per_block_mean)
-    acc_mode = 0 if acc_dtype == "fp32" else 1
     return torch.ops.qdq_b200.sage3_attn(q, k, v, False, float(sm_scale), fmt, acc_mode,
                                          bool(is_causal), int(smoothing))
 
