@@ -109,8 +109,10 @@ def test_patched_marlin_gemm_fused_route_equals_reference_route(cuda_device, mon
     ns = types.SimpleNamespace(marlin_gemm=ops.marlin_gemm)
     patch._patch_marlin_gemm(ns, scalar_types, mxfp4_qdq, mxfp8_qdq, lambda *t: None)
     a = torch.randn(m, k, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).to(cuda_device)
+    # the arguments vLLM's apply_fp4_marlin_linear passes (marlin_utils_fp4.py:149-202):
+    # fp32 reduction of the split-K partial sums, no atomic add at this size
     args = (a, None, layer.weight, None, layer.weight_scale, None, None, None, None, None, layer.workspace,
-            scalar_types.float4_e2m1f, m, n, k)
+            scalar_types.float4_e2m1f, m, n, k, True, False, True)
     monkeypatch.setenv("VLLM_QDQ_FUSED_GEMM", "0")
     ref = ns.marlin_gemm(*args)
     monkeypatch.setenv("VLLM_QDQ_FUSED_GEMM", "1")
