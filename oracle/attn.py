@@ -35,11 +35,12 @@ LOG2E = 1.4426950408889634
 
 
 def bf16_round(x: np.ndarray) -> np.ndarray:
-    """Round float values to bf16 (nearest even), returned as float32."""
-    x = np.asarray(x, np.float32)
-    b = x.view(np.uint32).astype(np.uint64)
-    b = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
-    return b.astype(np.uint32).view(np.float32)
+    """Round float values to bf16 (nearest even), returned as float32.  This
+    is the rounding of torch's bf16 cast, which the reference's torch code
+    applies after every bf16 operation; the cast is used here for speed."""
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32))
+    return t.to(torch.bfloat16).to(torch.float32).numpy()
 
 
 def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
@@ -299,6 +300,31 @@ def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_sca
                           fp8=pv_fmt == "mx8", pre=pre, e4s32=pv_fmt == "nv4b32")
         if vsmooth:
             out[:, h] += vmean(v)
+    return out
+
+
+def attention_rows(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_scale: float,
+                   rows: np.ndarray, config: str = "mxfp4_hw", block_n: int | None = None,
+                   mask_padding: bool = True) -> np.ndarray:
+    """attention() of one head ([L, 1, D] bit patterns) for the query rows
+    `rows` only: the pre-pass over the whole sequence, then the flash loop on
+    each 128-row query tile that holds a requested row.  Returns O [len(rows), D]."""
+    qk_fmt, pv_fmt, emulated, pre, vsmooth, qk_smooth = CONFIGS[config]
+    if block_n is None:
+        block_n = REF_BLOCK_N[config]
+    L = q_bits.shape[0]
+    q, k, v = (bf16_bits_to_f32(t[:, 0]) for t in (q_bits, k_bits, v_bits))
+    qd, kd, vd, ds = prepass(q, k, v, qk_smooth, qk_fmt=qk_fmt, pv_fmt=pv_fmt, vsmooth=vsmooth)
+    rows = np.asarray(rows)
+    out = np.zeros((len(rows), q.shape[1]))
+    for t in np.unique(rows // 128):
+        o = flash(qd, kd, vd, ds, L, sm_scale, block_n, False, mask_padding, pv_fmt == "nv4", emulated,
+                  q_rows=slice(128 * t, 128 * t + 128), fp8=pv_fmt == "mx8", pre=pre,
+                  e4s32=pv_fmt == "nv4b32")
+        sel = rows // 128 == t
+        out[sel] = o[rows[sel] - 128 * t]
+        if vsmooth:
+            out[sel] += vmean(v)
     return out
 
 

@@ -31,6 +31,9 @@ without touching the reference:
   4. downcasts: fp32 -> bf16 rounds to nearest even (the interpreter
      truncates) and fp32 -> fp8 e4m3 rounds to nearest even (the interpreter
      converts the integer value).
+The mxfp8_hw module also asks Triton's active GPU driver for its torch device
+when it is imported (mxfp8_hw_kernel.py:24); with no GPU a stand-in driver
+answers "cpu".
 
 Elementwise math (exp, exp2, log2, division) uses numpy's correctly rounded
 fp32 functions where the GPU uses approximate ones; the fp32 dots are exact
@@ -277,6 +280,15 @@ def install_interpreter_gaps() -> None:
     B.create_fp_to_fp = create_fp_to_fp
     # create_fadd, create_fmul, create_fcmp*, create_fp_trunc, ... are lambdas that
     # call self.binary_op / self.cast_impl, so they pick up the methods above.
+
+    import triton
+
+    class _CpuDriver:
+        @staticmethod
+        def get_active_torch_device():
+            return torch.device("cpu")
+
+    triton.runtime.driver.set_active(_CpuDriver())
 
 
 def _self_check() -> None:
