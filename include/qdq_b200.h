@@ -176,8 +176,13 @@ int qdq_selftest_bounded_wait(int64_t timeout_ns, void* stream);
  */
 int64_t qdq_sf_tiled_bytes(int64_t rows, int64_t k);
 
+/* Same for NVFP4's E4M3 scales, one per 16 elements: scales per row padded
+ * to a multiple of 16 (one K-256 GEMM stage), same chunk layout. */
+int64_t qdq_sf16_tiled_bytes(int64_t rows, int64_t k);
+
 /* Row-major scales [rows, ceil(k/block)] (row stride ld bytes) -> tiled
- * layout above; padding bytes are written as 0.  block must be 32. */
+ * layout above; padding bytes are written as 0.  block 32 (E8M0, sized by
+ * qdq_sf_tiled_bytes) or 16 (E4M3, sized by qdq_sf16_tiled_bytes). */
 int qdq_sf_tile(const void* sf, void* sf_tiled, int64_t rows, int64_t k, int64_t ld, int block,
                 void* stream);
 
@@ -193,6 +198,42 @@ int fp4_gemm_mxf4(const void* a_codes, const void* a_sf_tiled, const void* w_cod
                   const void* w_sf_tiled, const void* bias, void* c, int64_t M, int64_t N,
                   int64_t K, int64_t lda_bytes, int64_t ldw_bytes, int64_t ldc, int out_dtype,
                   void* stream);
+
+/*
+ * NVFP4 GEMM: C = alpha * A . W^T (+ bias), fp32 accumulation, where A and W
+ * are E2M1 codes as in fp4_gemm_mxf4 with one UE4M3 scale per 16 K elements
+ * (tiled by qdq_sf_tile with block 16) and alpha = w_global_scale /
+ * *a_global_scale.  Conventions are vLLM's NVFP4 ones: the activation
+ * dequantises as code * s / gs_a (gs_a = 2688 / amax, the `global_scale` of
+ * qdq_nvfp4; device pointer, read after the previous kernel on the stream
+ * completes), the weight as code * s * gs_w (the layer's weight_global_scale,
+ * passed by value).  Replaces, for NVFP4 Marlin layers:
+ *   vllm/.../marlin_utils_fp4.py:149-202 apply_fp4_marlin_linear with a
+ *   global_scale -> vllm/_custom_ops.py:1277 marlin_gemm.
+ */
+int fp4_gemm_nvf4(const void* a_codes, const void* a_sf_tiled, const float* a_global_scale,
+                  const void* w_codes, const void* w_sf_tiled, float w_global_scale, const void* bias,
+                  void* c, int64_t M, int64_t N, int64_t K, int64_t lda_bytes, int64_t ldw_bytes,
+                  int64_t ldc, int out_dtype, void* stream);
+
+/* Workspace bytes fp4_linear_nvf4 needs for an [M, K] activation. */
+int64_t fp4_linear_nvf4_workspace_bytes(int64_t M, int64_t K);
+
+/*
+ * Fused linear for NVFP4 layers with NVFP4 activations (the build's
+ * VLLM_QDQ_NVFP4_ACT=1 route): the activation's global scale (computed here
+ * when a_global_scale is NULL, as nvfp4_qdq does), its NVFP4 codes and E4M3
+ * scales (bit-identical to qdq_nvfp4's), then fp4_gemm_nvf4.  Equals
+ * marlin_gemm(nvfp4_qdq(a), W_nvfp4) up to the bf16 rounding nvfp4_qdq
+ * applies to each activation element and fp32 summation order.  workspace:
+ * 256-byte aligned, fp4_linear_nvf4_workspace_bytes(M, K).  K % 32 == 0.
+ * Same programmatic-dependent-launch stream order as fp4_linear_mxf4 for
+ * M > 128.
+ */
+int fp4_linear_nvf4(const void* a, int64_t lda, int dtype, const float* a_global_scale,
+                    const void* w_codes, const void* w_sf_tiled, float w_global_scale,
+                    const void* bias, void* c, int64_t M, int64_t N, int64_t K, int64_t ldw_bytes,
+                    int64_t ldc, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Workspace bytes fp4_linear_mxf4 needs for an [M, K] activation. */
 int64_t fp4_linear_workspace_bytes(int64_t M, int64_t K);

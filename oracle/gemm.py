@@ -102,3 +102,54 @@ def moe_linear_exact(a_bits: np.ndarray, w_codes: np.ndarray, w_scales: np.ndarr
             wgt = 1.0 if topk_weights is None else float(np.float32(topk_weights[s]))
             rows[s] = (out[i] * wgt, absum[i] * abs(wgt))
     return rows
+
+
+def e4m3_values(b: np.ndarray) -> np.ndarray:
+    """float64 value of E4M3 (float8_e4m3fn) bytes."""
+    b = np.asarray(b, np.uint8).astype(np.int64)
+    exp, man = (b >> 3) & 0xF, b & 7
+    mag = np.where(exp == 0, man / 8.0 * 2.0 ** -6, (1 + man / 8.0) * np.exp2(exp - 7.0))
+    mag = np.where((exp == 15) & (man == 7), np.nan, mag)
+    return np.where(b & 0x80, -mag, mag)
+
+
+def dequant_nvfp4(codes: np.ndarray, scales: np.ndarray, global_scale: float) -> np.ndarray:
+    """NVFP4 weight [R, K]: E2M1 code x E4M3 scale (per 16) x the fp32 tensor
+    scale, vLLM's convention for NVFP4 layers (marlin_utils_fp4.py
+    rand_marlin_weight_nvfp4_like: weight_ref = fp4 * global_scale * scales)."""
+    lo = E2M1[codes & 0xF]
+    hi = E2M1[codes >> 4]
+    vals = np.stack([lo, hi], axis=-1).reshape(codes.shape[0], -1)
+    return vals * np.repeat(e4m3_values(scales), 16, axis=1) * float(global_scale)
+
+
+def nvfp4_linear_exact(a_bits: np.ndarray, w_codes: np.ndarray, w_scales: np.ndarray, w_global_scale: float,
+                       fp16: bool = False, a_global_scale: float | None = None):
+    """The NVFP4 linear with NVFP4 activations, exactly (float64):
+      exact     nvfp4(a) @ W^T with the activation dequantised as code * s / gs_a
+                before any rounding (what the block16 tensor-core GEMM computes);
+      via_qdq   nvfp4_qdq(a) @ W^T, the activation rounded to bf16/fp16 first
+                (what nvfp4_qdq + Marlin computes);
+      absum     sum |a_k w_k| per output (bound for fp32-accumulation error).
+    gs_a = 2688 / amax(a) (vLLM's ref_nvfp4_quant_dequant convention) unless given."""
+    gs = oq.nvfp4_global_scale(a_bits, fp16=fp16) if a_global_scale is None else a_global_scale
+    y, codes, scales = oq.nvfp4_qdq(a_bits, gs, fp16=fp16, codes=True)
+    lo, hi = E2M1[codes & 0xF], E2M1[codes >> 4]
+    a_codes = np.stack([lo, hi], axis=-1).reshape(codes.shape[0], -1)
+    a_exact = a_codes * np.repeat(e4m3_values(scales), 16, axis=1) / np.float64(np.float32(gs))
+    a_qdq = y.view(np.float16).astype(np.float64) if fp16 else bf16_bits_to_f64(y)
+    w = dequant_nvfp4(w_codes, w_scales, w_global_scale)
+    return a_exact @ w.T, a_qdq @ w.T, np.abs(a_exact) @ np.abs(w).T
+
+
+def random_nvfp4_weight(n: int, k: int, seed: int):
+    """Uniform random E2M1 nibbles; E4M3 scales uniform over the normal range
+    [2^-6, 448] in log space (as a quantiser emits for a layer's groups), and a
+    weight tensor scale of 1/2048."""
+    rng = np.random.default_rng(seed)
+    codes = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+    exp = rng.integers(1, 16, size=(n, k // 16))
+    man = rng.integers(0, 8, size=(n, k // 16))
+    man = np.where(exp == 15, np.minimum(man, 6), man)          # 0x7F is NaN
+    scales = ((exp << 3) | man).astype(np.uint8)
+    return codes, scales, 1.0 / 2048

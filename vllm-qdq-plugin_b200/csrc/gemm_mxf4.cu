@@ -28,8 +28,18 @@
 // Scale factors use the tcgen05 "tiled" layout in global memory (see
 // qdq_sf_tile): rows are grouped by 128 and K-scales by 4 into 512-byte
 // chunks, chunk (rb, kc) at ((rb * kchunks) + kc) * 512, byte
-// (r % 32) * 16 + ((r / 32) % 4) * 4 + (ks % 4).  kchunks is even (the K-scale
-// count is padded to a multiple of 8), rows are padded to a multiple of 128.
+// (r % 32) * 16 + ((r / 32) % 4) * 4 + (ks % 4).  Rows are padded to a
+// multiple of 128 and the K-scale count to one stage's worth (8 for E8M0 per
+// 32, 16 for E4M3 per 16).
+//
+// NVFP4 variant (kNV): E2M1 codes with one UE4M3 scale per 16 K elements and
+// an fp32 tensor scale per operand, on tcgen05.mma.kind::mxf4nvf4.block16.
+// A K-256 stage then carries four scale chunks per 128-row block instead of
+// two, each MMA (K = 64) reads one whole chunk column, and the epilogue
+// multiplies the fp32 accumulator by alpha = w_global_scale / a_global_scale
+// (vLLM's conventions: the activation is dequantised as code * s / gs_a, the
+// weight as code * s * gs_w).
+#include <cmath>
 #include <cstring>
 
 #include "sm100.cuh"
@@ -46,16 +56,24 @@ constexpr int BKB = BK / 2;         // bytes per row per stage (128: one swizzle
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BKB;   // 16 KB
 constexpr int B_BYTES = BN * BKB;   // 32 KB
-constexpr int SFA_BYTES = 2 * 512;  // 128 rows x 8 scales
-constexpr int SFB_BYTES = 4 * 512;  // 256 rows x 8 scales
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;          // 256 fp32 columns
-constexpr int SFA_COL = 256;        // 8 columns (2 K-chunks x 4)
-constexpr int SFB_COL = 272;        // 16 columns (2 K-chunks x 2 row blocks x 4)
+constexpr int SFA_COL = 256;        // 8 columns (2 K-chunks x 4), NVFP4 16
+constexpr int SFB_COL = 272;        // 16 columns (2 K-chunks x 2 row blocks x 4), NVFP4 32
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
-constexpr uint32_t IDESC = idesc_mxf4(BM, BN, true);
+
+// Per-format stage geometry: 512-byte scale chunks per 128-row block and
+// stage (CPS), stage bytes, and the ring depths that fit 227 KB.
+template <bool kNV>
+struct Fmt {
+  static constexpr int CPS = kNV ? 4 : 2;
+  static constexpr int SFA = CPS * 512;        // 128 rows of A
+  static constexpr int SFB = 2 * CPS * 512;    // 256 rows of W
+  static constexpr int STAGE = BM * (BK / 2) + BN * (BK / 2) + SFA + SFB;
+  static constexpr uint32_t IDESC1 = idesc_mxf4(BM, BN, !kNV);
+  static constexpr uint32_t IDESC2 = idesc_mxf4(256, BN, !kNV);
+};
 
 struct __align__(8) Barriers {
   uint64_t full[STAGES];
@@ -67,7 +85,34 @@ struct __align__(8) Barriers {
   int abort;
 };
 
-constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + sizeof(Barriers);
+template <bool kNV>
+constexpr size_t smem_bytes() { return 1024 + STAGES * Fmt<kNV>::STAGE + sizeof(Barriers); }
+static_assert(smem_bytes<true>() <= 227 * 1024, "NVFP4 GEMM shared memory");
+
+// The 4 MMAs (K = 64 each) of one K-256 stage.  MXFP4: scale chunk j = kk / 2
+// holds the stage's K-scales 4j..4j+3, of which the MMA reads the pair sf_id.
+// NVFP4: chunk kk holds the MMA's four K-scales.  sfb: chunk j of W rows
+// 0-127 at column 8 j, of rows 128-255 at 8 j + 4.
+template <bool kNV, bool kPair>
+__device__ __forceinline__ void issue_stage(uint32_t acc, uint64_t da, uint64_t db, uint32_t sfa, uint32_t sfb,
+                                            bool first) {
+  constexpr uint32_t idesc = kPair ? Fmt<kNV>::IDESC2 : Fmt<kNV>::IDESC1;
+#pragma unroll
+  for (int kk = 0; kk < BK / 64; ++kk) {
+    const uint32_t acc_on = (!first || kk != 0) ? 1u : 0u;
+    // K step of 64 E2M1 = 32 bytes inside the 128-byte swizzled row
+    const uint64_t a = da + ((kk * 32) >> 4), b = db + ((kk * 32) >> 4);
+    if constexpr (kNV) {
+      if constexpr (kPair) mma_nvf4_pair(acc, a, b, idesc, sfa + 4 * kk, sfb + 8 * kk, acc_on);
+      else mma_nvf4(acc, a, b, idesc, sfa + 4 * kk, sfb + 8 * kk, acc_on);
+    } else {
+      const uint32_t j = kk >> 1, sf_id = (kk & 1) * 2;
+      const uint32_t id = idesc_with_sf_ids(idesc, sf_id, sf_id);
+      if constexpr (kPair) mma_mxf4_pair(acc, a, b, id, (sfa + 4 * j) | (sf_id << 30), (sfb + 8 * j) | (sf_id << 30), acc_on);
+      else mma_mxf4(acc, a, b, id, (sfa + 4 * j) | (sf_id << 30), (sfb + 8 * j) | (sf_id << 30), acc_on);
+    }
+  }
+}
 
 // Output element type: bf16 (kF16 = false) or fp16; bias has the same type.
 template <bool kF16>
@@ -85,13 +130,15 @@ struct OutT<true> {
   __device__ static T one(float a) { return __float2half_rn(a); }
 };
 
-template <bool kF16>
+template <bool kF16, bool kNV>
 __global__ void __launch_bounds__(THREADS, 1)
 mxf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                  const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb,
                  const void* __restrict__ bias_v, void* __restrict__ C_v, int M, int N,
-                 int K, int64_t ldc, int kchunks, int* status) {
+                 int K, int64_t ldc, int kchunks, const float* __restrict__ a_gs, float w_gs, int* status) {
   using O = OutT<kF16>;
+  using F = Fmt<kNV>;
+  constexpr int STAGE_BYTES = F::STAGE, SFA_BYTES = F::SFA, CPS = F::CPS;
   using T = typename O::T;
   const T* bias = static_cast<const T*>(bias_v);
   T* C = static_cast<T*>(C_v);
@@ -144,16 +191,16 @@ mxf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           }
           if (*(volatile int*)&bars->abort) { ok = false; break; }
           uint8_t* st = smem + s * STAGE_BYTES;
-          mbar_arrive_expect_tx(&bars->full[s], A_BYTES + B_BYTES + SFA_BYTES + (second_rb ? 2048 : 1024));
+          mbar_arrive_expect_tx(&bars->full[s], A_BYTES + B_BYTES + SFA_BYTES + (second_rb ? 2 : 1) * CPS * 512);
           tma_load_2d(st, &tmap_a, kt * BKB, m_blk * BM, &bars->full[s]);
           tma_load_2d(st + A_BYTES, &tmap_b, kt * BKB, n_blk * BN, &bars->full[s]);
-          bulk_load(st + A_BYTES + B_BYTES, sfa + (static_cast<int64_t>(m_blk) * kchunks + 2 * kt) * 512,
-                    1024, &bars->full[s]);
+          bulk_load(st + A_BYTES + B_BYTES, sfa + (static_cast<int64_t>(m_blk) * kchunks + CPS * kt) * 512,
+                    CPS * 512, &bars->full[s]);
           bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES,
-                    sfb + (static_cast<int64_t>(2 * n_blk) * kchunks + 2 * kt) * 512, 1024, &bars->full[s]);
+                    sfb + (static_cast<int64_t>(2 * n_blk) * kchunks + CPS * kt) * 512, CPS * 512, &bars->full[s]);
           if (second_rb)
-            bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES + 1024,
-                      sfb + (static_cast<int64_t>(2 * n_blk + 1) * kchunks + 2 * kt) * 512, 1024,
+            bulk_load(st + A_BYTES + B_BYTES + SFA_BYTES + CPS * 512,
+                      sfb + (static_cast<int64_t>(2 * n_blk + 1) * kchunks + CPS * kt) * 512, CPS * 512,
                       &bars->full[s]);
         }
       }
@@ -178,24 +225,16 @@ mxf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           uint8_t* st = smem + s * STAGE_BYTES;
           const uint8_t* sa = st + A_BYTES + B_BYTES;
           const uint8_t* sb = sa + SFA_BYTES;
-          // scale factors: chunk j (K-scales 4j..4j+3 of this stage) of each 128-row block
-          tmem_cp_sf(tmem + SFA_COL + 0, smem_desc_sf(sa));
-          tmem_cp_sf(tmem + SFA_COL + 4, smem_desc_sf(sa + 512));
-          tmem_cp_sf(tmem + SFB_COL + 0, smem_desc_sf(sb));             // rows 0-127,   j = 0
-          tmem_cp_sf(tmem + SFB_COL + 8, smem_desc_sf(sb + 512));       // rows 0-127,   j = 1
-          tmem_cp_sf(tmem + SFB_COL + 4, smem_desc_sf(sb + 1024));      // rows 128-255, j = 0
-          tmem_cp_sf(tmem + SFB_COL + 12, smem_desc_sf(sb + 1536));     // rows 128-255, j = 1
-          const uint64_t da = smem_desc_sw128(st);
-          const uint64_t db = smem_desc_sw128(st + A_BYTES);
+          // scale factors: chunk j of each 128-row block (MXFP4: K-scales
+          // 4j..4j+3 of this stage; NVFP4: the four K-scales of MMA j)
 #pragma unroll
-          for (int kk = 0; kk < BK / 64; ++kk) {
-            const uint32_t j = kk >> 1, sf_id = (kk & 1) * 2;
-            const uint32_t sfa_addr = (tmem + SFA_COL + 4 * j) | (sf_id << 30);
-            const uint32_t sfb_addr = (tmem + SFB_COL + 8 * j) | (sf_id << 30);
-            // K step of 64 E2M1 = 32 bytes inside the 128-byte swizzled row
-            mma_mxf4(tmem + ACC_COL, da + ((kk * 32) >> 4), db + ((kk * 32) >> 4),
-                     idesc_with_sf_ids(IDESC, sf_id, sf_id), sfa_addr, sfb_addr, (kt | kk) != 0);
+          for (int j = 0; j < CPS; ++j) {
+            tmem_cp_sf(tmem + SFA_COL + 4 * j, smem_desc_sf(sa + 512 * j));
+            tmem_cp_sf(tmem + SFB_COL + 8 * j, smem_desc_sf(sb + 512 * j));                // rows 0-127
+            tmem_cp_sf(tmem + SFB_COL + 8 * j + 4, smem_desc_sf(sb + CPS * 512 + 512 * j));  // rows 128-255
           }
+          issue_stage<kNV, false>(tmem + ACC_COL, smem_desc_sw128(st), smem_desc_sw128(st + A_BYTES),
+                                  tmem + SFA_COL, tmem + SFB_COL, kt == 0);
           tc_commit(&bars->empty[s]);
         }
         if (!ok) break;
@@ -210,6 +249,7 @@ mxf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     // ---------------- epilogue: TMEM lanes 32 (warp % 4).. = tile rows, columns 128 h ..
     const int q = warp & 3, h = (warp - 2) >> 2;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ACC_COL + h * 128;
+    const float alpha = kNV ? w_gs / *a_gs : 1.0f;
     bool ok = true;
     int i = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
@@ -234,7 +274,7 @@ mxf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
         T* crow = C + static_cast<int64_t>(row) * ldc + n0 + 32 * c;
         float v[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[c][e]);
+        for (int e = 0; e < 32; ++e) v[e] = kNV ? __uint_as_float(r[c][e]) * alpha : __uint_as_float(r[c][e]);
         if (bias != nullptr) {
 #pragma unroll
           for (int e = 0; e < 32; ++e)
@@ -279,34 +319,44 @@ mxf4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
 // Scale chunks arrive by TMA (2-D maps of 512-byte rows) so that they, too,
 // complete on the leader's barrier.
 // ---------------------------------------------------------------------------
-constexpr int P_STAGES = 6;
+constexpr int P_STAGES_MAX = 6;
 constexpr int P_A = 128 * BKB;      // 16 KB: the CTA's 128 A rows
 constexpr int P_B = 128 * BKB;      // 16 KB: the CTA's 128 W rows
-constexpr int P_SFA = 2 * 512;      // the CTA's 128 rows x 8 scales
-constexpr int P_SFB = 4 * 512;      // all 256 W rows x 8 scales
-constexpr int P_STAGE = P_A + P_B + P_SFA + P_SFB;  // 35 KB
-constexpr int P_TX = 2 * P_STAGE;   // bytes both CTAs land on the leader's barrier per stage
-constexpr uint32_t P_IDESC = idesc_mxf4(256, BN, true);
+// Per format: the CTA's 128 A rows' and all 256 W rows' scale chunks; MXFP4
+// stages are 35 KB (6 in the ring), NVFP4 stages 38 KB (5).
+template <bool kNV>
+struct PairFmt {
+  static constexpr int STAGES = kNV ? 5 : 6;
+  static constexpr int SFA = Fmt<kNV>::SFA;
+  static constexpr int SFB = Fmt<kNV>::SFB;
+  static constexpr int STAGE = P_A + P_B + SFA + SFB;
+  static constexpr int TX = 2 * STAGE;  // bytes both CTAs land on the leader's barrier per stage
+};
 
 struct __align__(8) PairBars {
-  uint64_t full[P_STAGES];   // leader: both CTAs' stage bytes landed
-  uint64_t empty[P_STAGES];  // each CTA: the pair's MMAs on the stage completed
-  uint64_t acc_full;         // each CTA: its accumulator half is complete
-  uint64_t acc_empty;        // leader: both CTAs' epilogues read their halves (512 arrivals)
+  uint64_t full[P_STAGES_MAX];   // leader: both CTAs' stage bytes landed
+  uint64_t empty[P_STAGES_MAX];  // each CTA: the pair's MMAs on the stage completed
+  uint64_t acc_full;             // each CTA: its accumulator half is complete
+  uint64_t acc_empty;            // leader: both CTAs' epilogues read their halves (512 arrivals)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
 };
-constexpr size_t P_SMEM_BYTES = 1024 + P_STAGES * P_STAGE + sizeof(PairBars);
-static_assert(P_SMEM_BYTES <= 227 * 1024, "pair GEMM shared memory");
+template <bool kNV>
+constexpr size_t pair_smem_bytes() { return 1024 + PairFmt<kNV>::STAGES * PairFmt<kNV>::STAGE + sizeof(PairBars); }
+static_assert(pair_smem_bytes<false>() <= 227 * 1024, "pair GEMM shared memory");
+static_assert(pair_smem_bytes<true>() <= 227 * 1024, "NVFP4 pair GEMM shared memory");
 
-template <bool kF16>
+template <bool kF16, bool kNV>
 __global__ void __launch_bounds__(THREADS, 1)
 mxf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
                       const void* __restrict__ bias_v, void* __restrict__ C_v, int M, int N, int K, int64_t ldc,
-                      int kchunks, int* status) {
+                      int kchunks, const float* __restrict__ a_gs, float w_gs, int* status) {
   using O = OutT<kF16>;
+  using PF = PairFmt<kNV>;
+  constexpr int P_STAGES = PF::STAGES, P_STAGE = PF::STAGE, P_SFA = PF::SFA, P_TX = PF::TX;
+  constexpr int CPS = Fmt<kNV>::CPS;
   using T = typename O::T;
   const T* bias = static_cast<const T*>(bias_v);
   T* C = static_cast<T*>(C_v);
@@ -358,14 +408,15 @@ mxf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         const uint32_t full0 = cluster_addr(&bars->full[s], 0);
         if (rank == 0) mbar_arrive_expect_tx(&bars->full[s], P_TX);
         tma_load_2d_pair(st + P_A, &tmap_b, kt * BKB, n_blk * BN + static_cast<int>(rank) * 128, full0);
-        tma_load_2d_pair(st + P_A + P_B + P_SFA, &tmap_sfb, 0, (n_blk * 2) * kchunks + 2 * kt, full0);
-        tma_load_2d_pair(st + P_A + P_B + P_SFA + 1024, &tmap_sfb, 0, (n_blk * 2 + 1) * kchunks + 2 * kt, full0);
+        tma_load_2d_pair(st + P_A + P_B + P_SFA, &tmap_sfb, 0, (n_blk * 2) * kchunks + CPS * kt, full0);
+        tma_load_2d_pair(st + P_A + P_B + P_SFA + CPS * 512, &tmap_sfb, 0, (n_blk * 2 + 1) * kchunks + CPS * kt,
+                         full0);
       };
       auto load_a = [&](int s, int m_blk, int kt) {
         uint8_t* st = smem + s * P_STAGE;
         const uint32_t full0 = cluster_addr(&bars->full[s], 0);
         tma_load_2d_pair(st, &tmap_a, kt * BKB, m_blk * 256 + static_cast<int>(rank) * 128, full0);
-        tma_load_2d_pair(st + P_A + P_B, &tmap_sfa, 0, (m_blk * 2 + static_cast<int>(rank)) * kchunks + 2 * kt,
+        tma_load_2d_pair(st + P_A + P_B, &tmap_sfa, 0, (m_blk * 2 + static_cast<int>(rank)) * kchunks + CPS * kt,
                          full0);
       };
       // The first ring of the first tile's weight loads goes out before
@@ -414,21 +465,14 @@ mxf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
           uint8_t* st = smem + s * P_STAGE;
           const uint8_t* sa = st + P_A + P_B;
           const uint8_t* sb = sa + P_SFA;
-          tmem_cp_sf_pair(tmem + SFA_COL + 0, smem_desc_sf(sa));
-          tmem_cp_sf_pair(tmem + SFA_COL + 4, smem_desc_sf(sa + 512));
-          tmem_cp_sf_pair(tmem + SFB_COL + 0, smem_desc_sf(sb));          // W rows 0-127,   j = 0
-          tmem_cp_sf_pair(tmem + SFB_COL + 8, smem_desc_sf(sb + 512));    // W rows 0-127,   j = 1
-          tmem_cp_sf_pair(tmem + SFB_COL + 4, smem_desc_sf(sb + 1024));   // W rows 128-255, j = 0
-          tmem_cp_sf_pair(tmem + SFB_COL + 12, smem_desc_sf(sb + 1536));  // W rows 128-255, j = 1
-          const uint64_t da = smem_desc_sw128(st);
-          const uint64_t db = smem_desc_sw128(st + P_A);
 #pragma unroll
-          for (int kk = 0; kk < BK / 64; ++kk) {
-            const uint32_t j = kk >> 1, sf_id = (kk & 1) * 2;
-            mma_mxf4_pair(tmem + ACC_COL, da + ((kk * 32) >> 4), db + ((kk * 32) >> 4),
-                          idesc_with_sf_ids(P_IDESC, sf_id, sf_id), (tmem + SFA_COL + 4 * j) | (sf_id << 30),
-                          (tmem + SFB_COL + 8 * j) | (sf_id << 30), (kt | kk) != 0);
+          for (int j = 0; j < CPS; ++j) {
+            tmem_cp_sf_pair(tmem + SFA_COL + 4 * j, smem_desc_sf(sa + 512 * j));
+            tmem_cp_sf_pair(tmem + SFB_COL + 8 * j, smem_desc_sf(sb + 512 * j));                // W rows 0-127
+            tmem_cp_sf_pair(tmem + SFB_COL + 8 * j + 4, smem_desc_sf(sb + CPS * 512 + 512 * j));  // W rows 128-255
           }
+          issue_stage<kNV, true>(tmem + ACC_COL, smem_desc_sw128(st), smem_desc_sw128(st + P_A), tmem + SFA_COL,
+                                 tmem + SFB_COL, kt == 0);
           tc_commit_pair(&bars->empty[s]);
         }
         if (!ok) break;
@@ -440,9 +484,10 @@ mxf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     }
   } else {
     // ---------------- epilogue (both CTAs): TMEM lanes = the CTA's 128 tile rows
-    pdl_wait();  // C and the bias belong to the stream's order
+    pdl_wait();  // C, the bias and the activation's global scale belong to the stream's order
     const int q = warp & 3, h = (warp - 2) >> 2;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + ACC_COL + h * 128;
+    const float alpha = kNV ? w_gs / *a_gs : 1.0f;
     const uint32_t acc_empty0 = cluster_addr(&bars->acc_empty, 0);
     bool ok = true;
     int i = 0;
@@ -468,7 +513,7 @@ mxf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         T* crow = C + static_cast<int64_t>(row) * ldc + n0 + 32 * c;
         float v[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[c][e]);
+        for (int e = 0; e < 32; ++e) v[e] = kNV ? __uint_as_float(r[c][e]) * alpha : __uint_as_float(r[c][e]);
         if (bias != nullptr) {
 #pragma unroll
           for (int e = 0; e < 32; ++e)
@@ -607,13 +652,16 @@ extern "C" int64_t qdq_sf_tiled_bytes(int64_t rows, int64_t k) {
 extern "C" int qdq_sf_tile(const void* sf, void* sf_tiled, int64_t rows, int64_t k, int64_t ld, int block,
                            void* stream) {
   if (rows < 0 || k < 0) return fail(QDQ_ERR_INVALID_ARG, "qdq_sf_tile: negative shape");
-  if (block != 32) return fail(QDQ_ERR_UNSUPPORTED, "qdq_sf_tile: block must be 32 (MXFP4)");
+  if (block != 32 && block != 16)
+    return fail(QDQ_ERR_UNSUPPORTED, "qdq_sf_tile: block must be 32 (MXFP4, E8M0) or 16 (NVFP4, E4M3)");
   if (rows == 0 || k == 0) return QDQ_OK;
   if (!sf || !sf_tiled) return fail(QDQ_ERR_INVALID_ARG, "qdq_sf_tile: null pointer");
   const int64_t ks = (k + block - 1) / block;
   if (ld < ks) return fail(QDQ_ERR_INVALID_ARG, "qdq_sf_tile: ld < number of scales per row");
   const int rows_p = static_cast<int>((rows + 127) / 128 * 128);
-  const int ks_p = static_cast<int>((ks + 7) / 8 * 8);
+  // one K-256 GEMM stage: 8 E8M0 scales per 32, or 16 E4M3 scales per 16
+  const int per_stage = 256 / block;
+  const int ks_p = static_cast<int>((ks + per_stage - 1) / per_stage * per_stage);
   const int64_t total = static_cast<int64_t>(rows_p) * ks_p;
   const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
   sf_tile_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
@@ -622,46 +670,38 @@ extern "C" int qdq_sf_tile(const void* sf, void* sf_tiled, int64_t rows, int64_t
   return check_launch("qdq_sf_tile");
 }
 
-extern "C" int fp4_gemm_mxf4(const void* a_codes, const void* a_sf_tiled, const void* w_codes,
-                             const void* w_sf_tiled, const void* bias, void* c, int64_t M, int64_t N,
-                             int64_t K, int64_t lda_bytes, int64_t ldw_bytes, int64_t ldc, int out_dtype,
-                             void* stream) {
-  if (out_dtype != QDQ_DTYPE_BF16 && out_dtype != QDQ_DTYPE_FP16)
-    return fail(QDQ_ERR_INVALID_ARG, "fp4_gemm_mxf4: out_dtype must be bf16 (0) or fp16 (1)");
-  if (M < 0 || N < 0 || K < 0) return fail(QDQ_ERR_INVALID_ARG, "fp4_gemm_mxf4: negative shape");
-  if (M == 0 || N == 0) return QDQ_OK;
-  if (!a_codes || !a_sf_tiled || !w_codes || !w_sf_tiled || !c)
-    return fail(QDQ_ERR_INVALID_ARG, "fp4_gemm_mxf4: null pointer");
-  if (K == 0) return fail(QDQ_ERR_UNSUPPORTED, "fp4_gemm_mxf4: K == 0");
-  if (K % 32 != 0) return fail(QDQ_ERR_UNSUPPORTED, "fp4_gemm_mxf4: K=%lld must be a multiple of 32", (long long)K);
-  if (M > (1ll << 30) || N > (1ll << 30) || K > (1ll << 30))
-    return fail(QDQ_ERR_UNSUPPORTED, "fp4_gemm_mxf4: dimension too large");
-  if (lda_bytes < K / 2 || ldw_bytes < K / 2 || ldc < N)
-    return fail(QDQ_ERR_INVALID_ARG, "fp4_gemm_mxf4: leading dimension too small");
-  if ((reinterpret_cast<uintptr_t>(a_sf_tiled) & 15) || (reinterpret_cast<uintptr_t>(w_sf_tiled) & 15))
-    return fail(QDQ_ERR_ALIGNMENT, "fp4_gemm_mxf4: scale-factor buffers must be 16-byte aligned");
+namespace qdqb200 {
+namespace {
+
+// One block-scaled GEMM launch: CTA pairs on 256 x 256 tiles when A has two
+// or more 128-row blocks, else one CTA per 128 x 256 tile.  kchunks = 512-byte
+// scale chunks per 128-row block (per K).
+template <bool kNV>
+int launch_gemm(const char* who, const void* a_codes, const void* a_sf_tiled, const void* w_codes,
+                const void* w_sf_tiled, const float* a_gs, float w_gs, const void* bias, void* c, int64_t M,
+                int64_t N, int64_t K, int64_t lda_bytes, int64_t ldw_bytes, int64_t ldc, int out_dtype,
+                int kchunks, cudaStream_t s) {
   int* status = device_status_ptr();
   if (status == nullptr) return QDQ_ERR_CUDA;
-  const int kchunks = static_cast<int>(((K / 32) + 7) / 8 * 8 / 4);
   const int sms = device_sm_count();
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // Two or more 128-row blocks of A: CTA pairs on 256 x 256 tiles.
+  const int of = out_dtype == QDQ_DTYPE_FP16 ? 1 : 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
   if (M > BM && sms >= 2) {
     CUtensorMap ta, tb, tsa, tsb;
+    constexpr int CPS = Fmt<kNV>::CPS;
     if (int st = make_tmap_u8_2d(&ta, a_codes, M, K / 2, lda_bytes, BKB, 128, 128)) return st;
     if (int st = make_tmap_u8_2d(&tb, w_codes, N, K / 2, ldw_bytes, BKB, 128, 128)) return st;
-    if (int st = make_tmap_u32_2d(&tsa, a_sf_tiled, (M + 127) / 128 * kchunks, 128, 512, 128, 2)) return st;
-    if (int st = make_tmap_u32_2d(&tsb, w_sf_tiled, (N + 127) / 128 * kchunks, 128, 512, 128, 2)) return st;
+    if (int st = make_tmap_u32_2d(&tsa, a_sf_tiled, (M + 127) / 128 * kchunks, 128, 512, 128, CPS)) return st;
+    if (int st = make_tmap_u32_2d(&tsb, w_sf_tiled, (N + 127) / 128 * kchunks, 128, 512, 128, CPS)) return st;
     static bool pair_attr[2][64] = {{false}};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const void* pfn = out_dtype == QDQ_DTYPE_FP16 ? reinterpret_cast<const void*>(&mxf4_gemm_pair_kernel<true>)
-                                                  : reinterpret_cast<const void*>(&mxf4_gemm_pair_kernel<false>);
-    if (dev >= 0 && dev < 64 && !pair_attr[out_dtype][dev]) {
-      cudaError_t e = cudaFuncSetAttribute(pfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(P_SMEM_BYTES));
-      if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_gemm_mxf4: smem attribute: %s", cudaGetErrorString(e));
-      pair_attr[out_dtype][dev] = true;
+    const void* pfn = of ? reinterpret_cast<const void*>(&mxf4_gemm_pair_kernel<true, kNV>)
+                         : reinterpret_cast<const void*>(&mxf4_gemm_pair_kernel<false, kNV>);
+    constexpr size_t smem = pair_smem_bytes<kNV>();
+    if (dev >= 0 && dev < 64 && !pair_attr[of][dev]) {
+      cudaError_t e = cudaFuncSetAttribute(pfn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "%s: smem attribute: %s", who, cudaGetErrorString(e));
+      pair_attr[of][dev] = true;
     }
     const int64_t tiles = ((M + 255) / 256) * ((N + BN - 1) / BN);
     const int64_t pairs = std::min<int64_t>(tiles, sms / 2);
@@ -669,7 +709,7 @@ extern "C" int fp4_gemm_mxf4(const void* a_codes, const void* a_sf_tiled, const 
     std::memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
     cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -682,41 +722,97 @@ extern "C" int fp4_gemm_mxf4(const void* a_codes, const void* a_sf_tiled, const 
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     const int m_ = static_cast<int>(M), n_ = static_cast<int>(N), k_ = static_cast<int>(K);
-    cudaError_t e = out_dtype == QDQ_DTYPE_FP16
-                        ? cudaLaunchKernelEx(&cfg, mxf4_gemm_pair_kernel<true>, ta, tb, tsa, tsb, bias, c, m_, n_, k_,
-                                             ldc, kchunks, status)
-                        : cudaLaunchKernelEx(&cfg, mxf4_gemm_pair_kernel<false>, ta, tb, tsa, tsb, bias, c, m_, n_,
-                                             k_, ldc, kchunks, status);
-    if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_gemm_mxf4: pair launch: %s", cudaGetErrorString(e));
-    return check_launch("fp4_gemm_mxf4");
+    cudaError_t e = of ? cudaLaunchKernelEx(&cfg, mxf4_gemm_pair_kernel<true, kNV>, ta, tb, tsa, tsb, bias, c, m_,
+                                            n_, k_, ldc, kchunks, a_gs, w_gs, status)
+                       : cudaLaunchKernelEx(&cfg, mxf4_gemm_pair_kernel<false, kNV>, ta, tb, tsa, tsb, bias, c, m_,
+                                            n_, k_, ldc, kchunks, a_gs, w_gs, status);
+    if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "%s: pair launch: %s", who, cudaGetErrorString(e));
+    return check_launch(who);
   }
   CUtensorMap ta, tb;
   if (int st = make_tmap_u8_2d(&ta, a_codes, M, K / 2, lda_bytes, BKB, BM, 128)) return st;
   if (int st = make_tmap_u8_2d(&tb, w_codes, N, K / 2, ldw_bytes, BKB, BN, 128)) return st;
   static bool attr_set[2][64] = {{false}};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const void* fn = out_dtype == QDQ_DTYPE_FP16 ? reinterpret_cast<const void*>(&mxf4_gemm_kernel<true>)
-                                               : reinterpret_cast<const void*>(&mxf4_gemm_kernel<false>);
-  if (dev >= 0 && dev < 64 && !attr_set[out_dtype][dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(SMEM_BYTES));
-    if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_gemm_mxf4: smem attribute: %s", cudaGetErrorString(e));
-    attr_set[out_dtype][dev] = true;
+  const void* fn = of ? reinterpret_cast<const void*>(&mxf4_gemm_kernel<true, kNV>)
+                      : reinterpret_cast<const void*>(&mxf4_gemm_kernel<false, kNV>);
+  constexpr size_t smem = smem_bytes<kNV>();
+  if (dev >= 0 && dev < 64 && !attr_set[of][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "%s: smem attribute: %s", who, cudaGetErrorString(e));
+    attr_set[of][dev] = true;
   }
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, sms > 0 ? sms : 148)));
   auto* sfa = static_cast<const uint8_t*>(a_sf_tiled);
   auto* sfb = static_cast<const uint8_t*>(w_sf_tiled);
-  if (out_dtype == QDQ_DTYPE_FP16)
-    mxf4_gemm_kernel<true><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, sfa, sfb, bias, c, static_cast<int>(M),
-                                                            static_cast<int>(N), static_cast<int>(K), ldc,
-                                                            kchunks, status);
+  const int m_ = static_cast<int>(M), n_ = static_cast<int>(N), k_ = static_cast<int>(K);
+  if (of)
+    mxf4_gemm_kernel<true, kNV><<<grid, THREADS, smem, s>>>(ta, tb, sfa, sfb, bias, c, m_, n_, k_, ldc, kchunks,
+                                                           a_gs, w_gs, status);
   else
-    mxf4_gemm_kernel<false><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, sfa, sfb, bias, c, static_cast<int>(M),
-                                                             static_cast<int>(N), static_cast<int>(K), ldc,
-                                                             kchunks, status);
-  return check_launch("fp4_gemm_mxf4");
+    mxf4_gemm_kernel<false, kNV><<<grid, THREADS, smem, s>>>(ta, tb, sfa, sfb, bias, c, m_, n_, k_, ldc, kchunks,
+                                                            a_gs, w_gs, status);
+  return check_launch(who);
+}
+
+int check_gemm_args(const char* who, const void* a_codes, const void* a_sf_tiled, const void* w_codes,
+                    const void* w_sf_tiled, const void* c, int64_t M, int64_t N, int64_t K, int64_t lda_bytes,
+                    int64_t ldw_bytes, int64_t ldc, int out_dtype) {
+  if (out_dtype != QDQ_DTYPE_BF16 && out_dtype != QDQ_DTYPE_FP16)
+    return fail(QDQ_ERR_INVALID_ARG, "%s: out_dtype must be bf16 (0) or fp16 (1)", who);
+  if (M < 0 || N < 0 || K < 0) return fail(QDQ_ERR_INVALID_ARG, "%s: negative shape", who);
+  if (M == 0 || N == 0) return QDQ_OK;
+  if (!a_codes || !a_sf_tiled || !w_codes || !w_sf_tiled || !c)
+    return fail(QDQ_ERR_INVALID_ARG, "%s: null pointer", who);
+  if (K == 0) return fail(QDQ_ERR_UNSUPPORTED, "%s: K == 0", who);
+  if (K % 32 != 0) return fail(QDQ_ERR_UNSUPPORTED, "%s: K=%lld must be a multiple of 32", who, (long long)K);
+  if (M > (1ll << 30) || N > (1ll << 30) || K > (1ll << 30))
+    return fail(QDQ_ERR_UNSUPPORTED, "%s: dimension too large", who);
+  if (lda_bytes < K / 2 || ldw_bytes < K / 2 || ldc < N)
+    return fail(QDQ_ERR_INVALID_ARG, "%s: leading dimension too small", who);
+  if ((reinterpret_cast<uintptr_t>(a_sf_tiled) & 15) || (reinterpret_cast<uintptr_t>(w_sf_tiled) & 15))
+    return fail(QDQ_ERR_ALIGNMENT, "%s: scale-factor buffers must be 16-byte aligned", who);
+  return QDQ_OK;
+}
+
+}  // namespace
+}  // namespace qdqb200
+
+extern "C" int fp4_gemm_mxf4(const void* a_codes, const void* a_sf_tiled, const void* w_codes,
+                             const void* w_sf_tiled, const void* bias, void* c, int64_t M, int64_t N,
+                             int64_t K, int64_t lda_bytes, int64_t ldw_bytes, int64_t ldc, int out_dtype,
+                             void* stream) {
+  if (int st = check_gemm_args("fp4_gemm_mxf4", a_codes, a_sf_tiled, w_codes, w_sf_tiled, c, M, N, K, lda_bytes,
+                               ldw_bytes, ldc, out_dtype))
+    return st;
+  if (M == 0 || N == 0) return QDQ_OK;
+  const int kchunks = static_cast<int>(((K / 32) + 7) / 8 * 8 / 4);
+  return launch_gemm<false>("fp4_gemm_mxf4", a_codes, a_sf_tiled, w_codes, w_sf_tiled, nullptr, 1.0f, bias, c, M,
+                            N, K, lda_bytes, ldw_bytes, ldc, out_dtype, kchunks, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int64_t qdq_sf16_tiled_bytes(int64_t rows, int64_t k) {
+  if (rows <= 0 || k <= 0) return 0;
+  const int64_t rows_p = (rows + 127) / 128 * 128;
+  const int64_t ks_p = ((k + 15) / 16 + 15) / 16 * 16;
+  return rows_p * ks_p;
+}
+
+extern "C" int fp4_gemm_nvf4(const void* a_codes, const void* a_sf_tiled, const float* a_global_scale,
+                             const void* w_codes, const void* w_sf_tiled, float w_global_scale, const void* bias,
+                             void* c, int64_t M, int64_t N, int64_t K, int64_t lda_bytes, int64_t ldw_bytes,
+                             int64_t ldc, int out_dtype, void* stream) {
+  if (int st = check_gemm_args("fp4_gemm_nvf4", a_codes, a_sf_tiled, w_codes, w_sf_tiled, c, M, N, K, lda_bytes,
+                               ldw_bytes, ldc, out_dtype))
+    return st;
+  if (M == 0 || N == 0) return QDQ_OK;
+  if (a_global_scale == nullptr) return fail(QDQ_ERR_INVALID_ARG, "fp4_gemm_nvf4: null a_global_scale");
+  if (!(w_global_scale > 0.0f) || !std::isfinite(w_global_scale))
+    return fail(QDQ_ERR_INVALID_ARG, "fp4_gemm_nvf4: w_global_scale must be finite and positive");
+  const int kchunks = static_cast<int>(((K / 16) + 15) / 16 * 16 / 4);
+  return launch_gemm<true>("fp4_gemm_nvf4", a_codes, a_sf_tiled, w_codes, w_sf_tiled, a_global_scale,
+                           w_global_scale, bias, c, M, N, K, lda_bytes, ldw_bytes, ldc, out_dtype, kchunks,
+                           static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------------------
@@ -760,4 +856,46 @@ extern "C" int fp4_linear_mxf4(const void* a, int64_t lda, int dtype, const void
   }
   return fp4_gemm_mxf4(a_codes, a_sf_t, w_codes, w_sf_tiled, bias, c, M, N, K, K / 2, ldw_bytes, ldc, dtype,
                        stream);
+}
+
+// ---------------------------------------------------------------------------
+// Fused NVFP4 linear: bf16/fp16 activation -> (global amax) -> NVFP4 codes +
+// E4M3 scales per 16 (exactly vLLM's NVFP4 quantisation, the codes of
+// nvfp4_qdq) -> tiled scales -> block16 GEMM with alpha = gs_w / gs_a.
+// ---------------------------------------------------------------------------
+extern "C" int64_t fp4_linear_nvf4_workspace_bytes(int64_t M, int64_t K) {
+  if (M <= 0 || K <= 0) return 0;
+  auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
+  return 256 + up(M * K / 2) + up(M * K / 16) + up(qdq_sf16_tiled_bytes(M, K));
+}
+
+extern "C" int fp4_linear_nvf4(const void* a, int64_t lda, int dtype, const float* a_global_scale,
+                               const void* w_codes, const void* w_sf_tiled, float w_global_scale,
+                               const void* bias, void* c, int64_t M, int64_t N, int64_t K, int64_t ldw_bytes,
+                               int64_t ldc, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(QDQ_ERR_INVALID_ARG, "fp4_linear_nvf4: negative shape");
+  if (M == 0 || N == 0) return QDQ_OK;
+  if (dtype != QDQ_DTYPE_BF16 && dtype != QDQ_DTYPE_FP16)
+    return fail(QDQ_ERR_INVALID_ARG, "fp4_linear_nvf4: dtype must be bf16 (0) or fp16 (1)");
+  if (K % 32 != 0) return fail(QDQ_ERR_UNSUPPORTED, "fp4_linear_nvf4: K=%lld must be a multiple of 32", (long long)K);
+  if (workspace == nullptr || workspace_bytes < fp4_linear_nvf4_workspace_bytes(M, K) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return fail(QDQ_ERR_INVALID_ARG,
+                "fp4_linear_nvf4: workspace must be 256-byte aligned and hold fp4_linear_nvf4_workspace_bytes()");
+  auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* gs = reinterpret_cast<float*>(ws);           // 4 bytes of gs, then 16 bytes of amax scratch
+  uint8_t* a_codes = ws + 256;
+  uint8_t* a_sf = a_codes + up(M * K / 2);
+  uint8_t* a_sf_t = a_sf + up(M * K / 16);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const float* gs_a = a_global_scale;
+  if (gs_a == nullptr) {
+    if (int st = qdq_nvfp4_global_scale(a, gs, ws + 16, M, K, lda, dtype, stream)) return st;
+    gs_a = gs;
+  }
+  if (int st = qdq_nvfp4(a, nullptr, a_codes, a_sf, gs_a, M, K, lda, K, dtype, stream)) return st;
+  if (int st = qdq_sf_tile(a_sf, a_sf_t, M, K, K / 16, 16, stream)) return st;
+  return fp4_gemm_nvf4(a_codes, a_sf_t, gs_a, w_codes, w_sf_tiled, w_global_scale, bias, c, M, N, K, K / 2,
+                       ldw_bytes, ldc, dtype, s);
 }

@@ -57,6 +57,12 @@ _SIGNATURES: dict[str, list] = {
     "fp4_gemm_mxf4": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64,
                       _i64, _i64, _i64, _i64, _int, _c_void_p],
     "fp4_linear_workspace_bytes": [_i64, _i64],
+    "qdq_sf16_tiled_bytes": [_i64, _i64],
+    "fp4_gemm_nvf4": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _f32, _c_void_p, _c_void_p,
+                      _i64, _i64, _i64, _i64, _i64, _i64, _int, _c_void_p],
+    "fp4_linear_nvf4_workspace_bytes": [_i64, _i64],
+    "fp4_linear_nvf4": [_c_void_p, _i64, _int, _c_void_p, _c_void_p, _c_void_p, _f32, _c_void_p, _c_void_p,
+                        _i64, _i64, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p],
     "fp4_linear_noalloc_scratch_bytes": [],
     "fp4_linear_mxf4_noalloc": [_c_void_p, _i64, _int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                 _i64, _i64, _i64, _i64, _i64, _c_void_p],
@@ -65,6 +71,8 @@ _SIGNATURES: dict[str, list] = {
 }
 _RESTYPES = {"qdq_last_error": ctypes.c_char_p, "qdq_sf_tiled_bytes": ctypes.c_int64,
              "fp4_linear_workspace_bytes": ctypes.c_int64,
+             "qdq_sf16_tiled_bytes": ctypes.c_int64,
+             "fp4_linear_nvf4_workspace_bytes": ctypes.c_int64,
              "fp4_linear_noalloc_scratch_bytes": ctypes.c_int64,
              "sage3_attn_workspace_bytes": ctypes.c_int64,
              "fp4_moe_workspace_bytes": ctypes.c_int64,

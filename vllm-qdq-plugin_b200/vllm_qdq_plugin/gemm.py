@@ -135,27 +135,113 @@ def mxfp4_gemm_codes(a_codes: torch.Tensor, a_scales: torch.Tensor, weight: Mxfp
 
 
 # ---------------------------------------------------------------------------
+# NVFP4 linear (E2M1 + UE4M3 per 16 + fp32 tensor scales), kind::mxf4nvf4
+# ---------------------------------------------------------------------------
+@dataclasses.dataclass
+class Nvfp4Weight:
+    """An NVFP4 weight [N, K]: codes, E4M3 scales per 16 (tiled) and the fp32
+    tensor scale that multiplies them (vLLM's `weight_global_scale`)."""
+
+    codes: torch.Tensor     # uint8 [N, K/2], element 2j in the low nibble
+    sf_tiled: torch.Tensor  # uint8, tiled E4M3 scales (qdq_sf_tile, block 16)
+    global_scale: float     # dequantised weight = code * scale * global_scale
+    n: int
+    k: int
+    bias: torch.Tensor | None = None
+
+
+def prepare_nvfp4_weight(codes: torch.Tensor, scales: torch.Tensor, global_scale: float,
+                         bias: torch.Tensor | None = None) -> Nvfp4Weight:
+    """codes uint8 [N, K/2] (packed E2M1); scales [N, K/16] E4M3 (uint8 or
+    float8_e4m3fn); global_scale: the weight's fp32 tensor scale."""
+    _native.require_cuda(codes, scales)
+    codes = codes.view(torch.uint8).contiguous()
+    scales = scales.view(torch.uint8).contiguous()
+    n, kh = codes.shape
+    k = kh * 2
+    assert k % 32 == 0 and scales.shape == (n, k // 16), (codes.shape, scales.shape)
+    lib = _native.lib()
+    sf = torch.empty((lib.qdq_sf16_tiled_bytes(n, k),), dtype=torch.uint8, device=codes.device)
+    _native.call("qdq_sf_tile", scales.data_ptr(), sf.data_ptr(), n, k, scales.stride(0), 16,
+                 _native.stream_ptr(codes.device))
+    return Nvfp4Weight(codes=codes, sf_tiled=sf, global_scale=float(global_scale), n=n, k=k, bias=bias)
+
+
+@torch.library.custom_op("qdq_b200::nvfp4_linear", mutates_args=())
+def _nvfp4_linear_op(a: torch.Tensor, w_codes: torch.Tensor, w_sf_tiled: torch.Tensor, w_global_scale: float,
+                     bias: torch.Tensor | None, a_global_scale: torch.Tensor | None) -> torch.Tensor:
+    _native.require_cuda(a, w_codes, w_sf_tiled)
+    a = a if a.stride(-1) == 1 else a.contiguous()
+    m, k = a.shape
+    n = w_codes.shape[0]
+    lib = _native.lib()
+    ws = torch.empty((lib.fp4_linear_nvf4_workspace_bytes(m, k),), dtype=torch.uint8, device=a.device)
+    out = torch.empty((m, n), dtype=a.dtype, device=a.device)
+    gs = None if a_global_scale is None else a_global_scale.reshape(-1)[:1].to(torch.float32).contiguous()
+    _native.call("fp4_linear_nvf4", a.data_ptr(), a.stride(0) if m > 1 else k, _native.DTYPE_CODE[a.dtype],
+                 _native.ptr(gs), w_codes.data_ptr(), w_sf_tiled.data_ptr(), float(w_global_scale),
+                 _native.ptr(bias), out.data_ptr(), m, n, k, w_codes.stride(0), n, ws.data_ptr(), ws.numel(),
+                 _native.stream_ptr(a.device))
+    return out
+
+
+@_nvfp4_linear_op.register_fake
+def _(a, w_codes, w_sf_tiled, w_global_scale, bias, a_global_scale):
+    return a.new_empty((a.shape[0], w_codes.shape[0]))
+
+
+def nvfp4_linear(a: torch.Tensor, weight: Nvfp4Weight, bias: torch.Tensor | None = None,
+                 a_global_scale: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M, N] = nvfp4(a) @ dequant(weight)^T (+ bias), fp32 accumulation.
+
+    The activation is quantised exactly as nvfp4_qdq does (group 16, E4M3
+    scales, gs_a = 2688 / amax(a) unless `a_global_scale` is given), and the
+    product is formed from the codes on the FP4 tensor cores, so it equals
+    nvfp4_qdq(a) @ dequant(W)^T up to nvfp4_qdq's bf16 rounding of each
+    activation element and fp32 summation order.  a: [M, K] bf16/fp16 CUDA,
+    K % 32 == 0.  Output dtype = a.dtype."""
+    assert a.dim() == 2 and a.dtype in (torch.bfloat16, torch.float16)
+    assert a.shape[1] == weight.k, (a.shape, weight.k)
+    if bias is None:
+        bias = weight.bias
+    if bias is not None:
+        bias = bias.to(a.dtype).contiguous()
+    return torch.ops.qdq_b200.nvfp4_linear(a, weight.codes, weight.sf_tiled, weight.global_scale, bias,
+                                           a_global_scale)
+
+
+# ---------------------------------------------------------------------------
 # Marlin-layer capture (VLLM_QDQ_FUSED_GEMM=1)
 # ---------------------------------------------------------------------------
-_REGISTRY: dict[int, Mxfp4Weight] = {}
+_REGISTRY: dict[int, Mxfp4Weight | Nvfp4Weight] = {}
 _REG_LOCK = threading.Lock()
 
 
-def register_marlin_weight(marlin_weight: torch.Tensor, weight: Mxfp4Weight) -> None:
+def register_marlin_weight(marlin_weight: torch.Tensor, weight: Mxfp4Weight | Nvfp4Weight) -> None:
     with _REG_LOCK:
         _REGISTRY[marlin_weight.data_ptr()] = weight
 
 
-def lookup_marlin_weight(marlin_weight: torch.Tensor) -> Mxfp4Weight | None:
+def lookup_marlin_weight(marlin_weight: torch.Tensor) -> Mxfp4Weight | Nvfp4Weight | None:
     return _REGISTRY.get(marlin_weight.data_ptr())
 
 
-def fused_marlin_replacement(a, c, b_q_weight, b_bias, size_m, size_n, size_k):
-    """Run the fused FP4 linear for a captured layer; None means "not captured"."""
+def fused_marlin_replacement(a, c, b_q_weight, b_bias, size_m, size_n, size_k, nvfp4_act: bool = False):
+    """Run the fused FP4 linear for a captured layer; None means "keep the
+    reference path" (QDQ + Marlin).  MXFP4 layers take the MXFP4 linear (the
+    reference's MXFP4 activation QDQ, fused).  NVFP4 layers take the NVFP4
+    linear only with nvfp4_act (VLLM_QDQ_NVFP4_ACT=1): the reference itself
+    applies MXFP4 QDQ to their activations, which no NVFP4 MMA can take."""
     w = lookup_marlin_weight(b_q_weight)
     if w is None or a.shape[1] != w.k or w.n != size_n or size_k != w.k:
         return None
-    out = mxfp4_linear(a, w, w.bias if b_bias is not None else None)
+    bias = w.bias if b_bias is not None else None
+    if isinstance(w, Nvfp4Weight):
+        if not nvfp4_act or a.shape[1] % 32 != 0:
+            return None
+        out = nvfp4_linear(a, w, bias)
+    else:
+        out = mxfp4_linear(a, w, bias)
     if c is not None:
         c.copy_(out)
         return c
@@ -175,20 +261,25 @@ def capture_marlin_weights() -> bool:
     @functools.wraps(original)
     def prepare_fp4_layer_for_marlin(layer, input_dtype=None):
         raw = None
-        if not hasattr(layer, "weight_global_scale") and (input_dtype is None or input_dtype.itemsize != 1):
+        if input_dtype is None or input_dtype.itemsize != 1:
             bias = getattr(layer, "bias", None)
+            gs = getattr(layer, "weight_global_scale", None)
             raw = (layer.weight.data, layer.weight_scale.data,
-                   None if bias is None else bias.data.clone())
+                   None if bias is None else bias.data.clone(),
+                   None if gs is None else float(gs.data.reshape(-1)[0].float()))
         result = original(layer, input_dtype)
         if raw is not None and raw[0].is_cuda:
-            codes, scales, bias = raw
-            register_marlin_weight(layer.weight, prepare_mxfp4_weight(
-                codes.view(torch.uint8), scales.view(torch.uint8), bias))
+            codes, scales, bias, gs = raw
+            if gs is None:   # MXFP4: E8M0 scales per 32
+                w = prepare_mxfp4_weight(codes.view(torch.uint8), scales.view(torch.uint8), bias)
+            else:            # NVFP4: E4M3 scales per 16 and the weight's tensor scale
+                w = prepare_nvfp4_weight(codes.view(torch.uint8), scales.view(torch.uint8), gs, bias)
+            register_marlin_weight(layer.weight, w)
         return result
 
     prepare_fp4_layer_for_marlin._qdq_b200_capture = True
     mu.prepare_fp4_layer_for_marlin = prepare_fp4_layer_for_marlin
-    logger.warning("vllm-qdq-plugin: capturing raw MXFP4 weights for the fused FP4 GEMM")
+    logger.warning("vllm-qdq-plugin: capturing raw MXFP4 / NVFP4 weights for the fused FP4 GEMM")
     return True
 
 

@@ -79,7 +79,8 @@ def _patch_marlin_gemm(ops, scalar_types, mxfp4_qdq, mxfp8_qdq, trace_qdq):
             trace_qdq("marlin_gemm", a.shape, a.dtype)
             if envs.VLLM_QDQ_FUSED_GEMM:
                 from .gemm import fused_marlin_replacement
-                out = fused_marlin_replacement(a, c, b_q_weight, b_bias, size_m, size_n, size_k)
+                out = fused_marlin_replacement(a, c, b_q_weight, b_bias, size_m, size_n, size_k,
+                                               nvfp4_act=bool(envs.VLLM_QDQ_NVFP4_ACT and global_scale is not None))
                 if out is not None:
                     return out
             a = _fp4_act_qdq(a, global_scale, mxfp4_qdq)
