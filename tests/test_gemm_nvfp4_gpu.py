@@ -23,6 +23,7 @@ import pytest
 import torch
 
 from oracle import gemm as og
+from oracle import qdq as oq
 
 pytestmark = pytest.mark.gpu
 
@@ -113,8 +114,10 @@ def test_nvfp4_linear_vs_nvfp4_qdq_plus_marlin(cuda_device, m):
                                      layer.workspace, n, k)
     ours = nvfp4_linear(ad, w)
     rows = min(m, 64)
+    # the activation's global scale is over all M rows, as nvfp4_qdq computes it
+    gs_a = oq.nvfp4_global_scale(a.view(torch.int16).numpy().view(np.uint16))
     exact, via_qdq, absum = og.nvfp4_linear_exact(a[:rows].view(torch.int16).numpy().view(np.uint16),
-                                                   codes, scales, gs)
+                                                   codes, scales, gs, a_global_scale=gs_a)
     # Marlin reproduces the QDQ'd product; the fused linear the unrounded one; the two agree
     assert _bad(ref[:rows], via_qdq, via_qdq, absum, ACC) == 0
     assert _bad(ours[:rows], exact, exact, absum, ACC) == 0
