@@ -163,6 +163,10 @@ WORKLOADS = {
     "mxfp4_linear": dict(config="BASELINE config 3: MXFP4 QDQ fused into a tcgen05 FP4 GEMM, "
                                 "A bf16 [M=4096, K=4096], W MXFP4 [N=14336, K=4096], out bf16",
                          rows=4096, cols=4096),
+    "nvfp4_linear": dict(config="BASELINE config 3's shape with NVFP4 weights and activations (VLLM_QDQ_NVFP4_ACT): "
+                                "A bf16 [M=4096, K=4096] -> E2M1 + E4M3 per 16 + gs = 2688/amax, W NVFP4 "
+                                "[N=14336, K=4096] (E4M3 scales per 16, tensor scale 1/2048), out bf16",
+                         rows=4096, cols=4096),
 }
 
 # ---------------------------------------------------------------------------
@@ -542,7 +546,7 @@ def run_reference(args) -> None:
     from oracle import qdq as oq  # CPU restatement of the reference (test/baseline only)
 
     wl = WORKLOADS[args.workload]
-    if args.workload in ("mxfp4_linear", "mxfp4_moe") or args.workload.startswith("sage3"):
+    if args.workload in ("mxfp4_linear", "nvfp4_linear", "mxfp4_moe") or args.workload.startswith("sage3"):
         return run_reference_compute(args, wl)
     x = wl["make"]()
     cores = os.cpu_count() or 1
@@ -601,7 +605,7 @@ def run_reference_compute(args, wl) -> None:
         config = {"workload": wl["config"], "tokens": m, "experts": wl["E"], "top_k": wl["top_k"],
                   "N": wl["N"], "K": wl["cols"]}
         ms = 2.0 * m * wl["top_k"] * wl["N"] * wl["cols"] / (cb["value"] * 1e12) * 1e3
-    elif args.workload == "mxfp4_linear":
+    elif args.workload in ("mxfp4_linear", "nvfp4_linear"):
         m = args.rows or wl["rows"]
         cb = cpu_gemm_sample(m, budget_s=per_step * args.steps)
         metric = "FP4 GEMM TFLOPS"
@@ -801,16 +805,33 @@ def vllm_nvfp4_gpu(ctx: Ctx, xs_local: torch.Tensor, gs: torch.Tensor, ours_ms: 
             "unit": "GB/s", "speedup_of_ours": round(ms / ours_ms, 2), "bit_identical_to_ours": same}
 
 
-def gemm_record(ctx: Ctx, m: int, sub: bool = False, marlin: bool = True) -> dict:
-    """Config 3's fused linear (activation MXFP4 QDQ + tcgen05 FP4 GEMM).
+def nvfp4_weight_of(codes: torch.Tensor, seed: int = 3) -> tuple[torch.Tensor, float]:
+    """E4M3 scales per 16 for config 3's codes: exponents uniform over the
+    normal E4M3 range (seeded), weight tensor scale 1/2048."""
+    import numpy as np
+    rng = np.random.default_rng(seed + 100)
+    n, k = codes.shape[0], codes.shape[1] * 2
+    exp = rng.integers(1, 16, size=(n, k // 16))
+    man = np.where(exp == 15, rng.integers(0, 7, size=(n, k // 16)), rng.integers(0, 8, size=(n, k // 16)))
+    return torch.from_numpy(((exp << 3) | man).astype(np.uint8)), 1.0 / 2048
+
+
+def gemm_record(ctx: Ctx, m: int, sub: bool = False, marlin: bool = True, nv: bool = False) -> dict:
+    """Config 3's fused linear (activation QDQ + tcgen05 FP4 GEMM): MXFP4
+    (E8M0 per 32, the reference's QDQ), or with nv=True NVFP4 weights and
+    activations (E4M3 per 16 + tensor scales, the VLLM_QDQ_NVFP4_ACT route).
     Strong scaling: M > 256 splits the activation rows; the decode shapes
     (M <= 256) split the 14336 output columns in 128-column blocks."""
     from vllm_qdq_plugin import _native
-    from vllm_qdq_plugin.gemm import mxfp4_linear, prepare_mxfp4_weight
+    from vllm_qdq_plugin.gemm import (mxfp4_linear, nvfp4_linear, prepare_mxfp4_weight,
+                                      prepare_nvfp4_weight)
 
     args = ctx.args
-    wl = WORKLOADS["mxfp4_linear"]
+    wl = WORKLOADS["nvfp4_linear" if nv else "mxfp4_linear"]
     a_full, codes_full, scales_full = c3_inputs(rows=m)
+    w_gs = 1.0
+    if nv:
+        scales_full, w_gs = nvfp4_weight_of(codes_full)
     n_full, k = codes_full.shape[0], codes_full.shape[1] * 2
     if m > 256:
         r0, r1 = ctx.share(m)
@@ -825,22 +846,35 @@ def gemm_record(ctx: Ctx, m: int, sub: bool = False, marlin: bool = True) -> dic
     codes, scales = codes_full[c0:c1].contiguous(), scales_full[c0:c1].contiguous()
     ml, n = a_cpu.shape[0], codes.shape[0]
     a = a_cpu.to(ctx.dev)
-    w = prepare_mxfp4_weight(codes.to(ctx.dev), scales.to(ctx.dev))
+
+    def prep():
+        if nv:
+            return prepare_nvfp4_weight(codes.to(ctx.dev), scales.to(ctx.dev), w_gs)
+        return prepare_mxfp4_weight(codes.to(ctx.dev), scales.to(ctx.dev))
+
+    w = prep()
     # rotating weight copies: a step reads its W again only after >= 3x the
     # 126 MB L2 of other weights has streamed through
     w_bytes = w.codes.numel() + w.sf_tiled.numel()
     n_w = max(1, -(-3 * L2_BYTES // max(1, w_bytes)))
-    ws_list = [w] + [prepare_mxfp4_weight(codes.to(ctx.dev), scales.to(ctx.dev)) for _ in range(n_w - 1)]
+    ws_list = [w] + [prep() for _ in range(n_w - 1)]
     lib = _native.lib()
-    wsp = torch.empty((lib.fp4_linear_workspace_bytes(ml, k),), dtype=torch.uint8, device=ctx.dev)
+    ws_bytes = (lib.fp4_linear_nvf4_workspace_bytes if nv else lib.fp4_linear_workspace_bytes)(ml, k)
+    wsp = torch.empty((ws_bytes,), dtype=torch.uint8, device=ctx.dev)
     out = torch.empty((ml, n), dtype=torch.bfloat16, device=ctx.dev)
-    per_call = 1 if ml <= 64 else (2 if k % 256 == 0 else 3)
+    # MXFP4: one fused launch for M <= 64, else codes (+ scale tiling when K % 256 != 0) and the GEMM;
+    # NVFP4: global amax, codes, scale tiling, GEMM
+    per_call = 4 if nv else (1 if ml <= 64 else (2 if k % 256 == 0 else 3))
 
     def step(i, sp):
         wi = ws_list[i % n_w]
-        _native.check("fp4_linear_mxf4", lib.fp4_linear_mxf4(
-            a.data_ptr(), k, 0, wi.codes.data_ptr(), wi.sf_tiled.data_ptr(), None, out.data_ptr(),
-            ml, n, k, k // 2, n, wsp.data_ptr(), wsp.numel(), sp))
+        if nv:
+            st = lib.fp4_linear_nvf4(a.data_ptr(), k, 0, None, wi.codes.data_ptr(), wi.sf_tiled.data_ptr(), w_gs,
+                                     None, out.data_ptr(), ml, n, k, k // 2, n, wsp.data_ptr(), wsp.numel(), sp)
+        else:
+            st = lib.fp4_linear_mxf4(a.data_ptr(), k, 0, wi.codes.data_ptr(), wi.sf_tiled.data_ptr(), None,
+                                     out.data_ptr(), ml, n, k, k // 2, n, wsp.data_ptr(), wsp.numel(), sp)
+        _native.check("fp4_linear_nvf4" if nv else "fp4_linear_mxf4", st)
 
     steps = args.steps
     for i in range(args.warmup):
@@ -852,21 +886,25 @@ def gemm_record(ctx: Ctx, m: int, sub: bool = False, marlin: bool = True) -> dic
     a_host = a_cpu.pin_memory()
     out_host = torch.empty((ml, n), dtype=torch.bfloat16).pin_memory()
 
+    linear = nvfp4_linear if nv else mxfp4_linear
+
     def e2e_step():
-        out_host.copy_(mxfp4_linear(a_host.to(ctx.dev, non_blocking=True), w), non_blocking=True)
+        out_host.copy_(linear(a_host.to(ctx.dev, non_blocking=True), w), non_blocking=True)
 
     for _ in range(3):
         e2e_step()
     ms_e2e = timed_host(ctx, e2e_step, max(1, min(steps, 20)))
     e2e = flop_total / (ms_e2e * 1e-3) / 1e12
 
-    ref = marlin_reference(ctx, a, codes, scales, w, ms_step, steps) if marlin else None
+    ref = marlin_reference(ctx, a, codes, scales, w, ms_step, steps, w_gs if nv else None) if marlin else None
     peak, src = measured_peak_fp4()
     rec = {
         "metric": "FP4 GEMM TFLOPS", "value": round(value, 1), "unit": "TFLOP/s",
         "n_gpus": ctx.world, "steps": steps, "warmup": args.warmup,
         "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "e2m1 x e2m1 (E8M0 scales), fp32 accumulate, bf16 out",
+        "vs_baseline": None,
+        "dtype": "e2m1 x e2m1 (" + ("UE4M3 scales per 16, fp32 tensor scales" if nv else "E8M0 scales") +
+                 "), fp32 accumulate, bf16 out",
         "data": "synthetic (seeded, BASELINE config-3 distributions)",
         "config": {"workload": wl["config"], "M": m, "N": n_full, "K": k},
         "parallelism": split + "; no collective",
@@ -874,31 +912,34 @@ def gemm_record(ctx: Ctx, m: int, sub: bool = False, marlin: bool = True) -> dic
                "only after >= 3x the 126 MB L2; steps replayed from one CUDA graph"),
         "e2e": {"value": round(e2e, 1), "unit": "TFLOP/s", "h2d_bytes_per_step": ml * k * 2,
                 "d2h_bytes_per_step": ml * n * 2,
-                "path": "vllm_qdq_plugin.gemm.mxfp4_linear on pinned host buffers (bytes per rank)"},
+                "path": f"vllm_qdq_plugin.gemm.{linear.__name__} on pinned host buffers (bytes per rank)"},
         "gpu_launches": steps * per_call,
         "roofline": linear_roofline(ml, n, k, ms_step, 2.0 * ml * n * k, peak, src),
         "clocks": clocks,
     }
     if ref:
         rec["reference_gpu"] = ref
-    if ctx.world == 1 and not args.no_cpu_baseline and not sub:
+    if ctx.world == 1 and not args.no_cpu_baseline and not sub and not nv:
         rec["cpu_baseline"] = cpu_gemm_sample(m)
     return rec
 
 
 def marlin_reference(ctx: Ctx, a: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, w,
-                     ours_ms: float, steps: int) -> dict:
+                     ours_ms: float, steps: int, w_gs: float | None = None) -> dict:
     """The path the fused linear replaces, on the same GPU and shapes: this
-    build's activation MXFP4 QDQ (bit-exact with the reference's mxfp4_qdq),
-    then vLLM's Marlin GEMM on weights prepared by vLLM itself
+    build's activation QDQ (MXFP4: bit-exact with the reference's mxfp4_qdq;
+    NVFP4, w_gs given: bit-exact with vLLM's ref_nvfp4_quant_dequant), then
+    vLLM's Marlin GEMM on weights prepared by vLLM itself
     (prepare_fp4_layer_for_marlin), with the same weight rotation."""
     try:
         from vllm.model_executor.layers.quantization.utils import marlin_utils_fp4 as mu
     except Exception as e:  # pragma: no cover
         return {"unavailable": f"vLLM import failed: {e}"}
-    from vllm_qdq_plugin.gemm import mxfp4_linear
-    from vllm_qdq_plugin.qdq import mxfp4_qdq
+    from vllm_qdq_plugin.gemm import mxfp4_linear, nvfp4_linear
+    from vllm_qdq_plugin.qdq import mxfp4_qdq, nvfp4_qdq
     n, k = codes.shape[0], codes.shape[1] * 2
+    nv = w_gs is not None
+    qdq, linear = (nvfp4_qdq, nvfp4_linear) if nv else (mxfp4_qdq, mxfp4_linear)
 
     class _Layer(torch.nn.Module):
         pass
@@ -906,7 +947,11 @@ def marlin_reference(ctx: Ctx, a: torch.Tensor, codes: torch.Tensor, scales: tor
     def layer():
         lay = _Layer()
         lay.weight = torch.nn.Parameter(codes.to(ctx.dev), requires_grad=False)
-        lay.weight_scale = torch.nn.Parameter(scales.to(ctx.dev), requires_grad=False)
+        lay.weight_scale = torch.nn.Parameter(
+            scales.to(ctx.dev).view(torch.float8_e4m3fn) if nv else scales.to(ctx.dev), requires_grad=False)
+        if nv:
+            lay.weight_global_scale = torch.nn.Parameter(torch.tensor(w_gs, dtype=torch.float32, device=ctx.dev),
+                                                         requires_grad=False)
         lay.output_size_per_partition, lay.input_size_per_partition = n, k
         lay.params_dtype, lay.bias = torch.bfloat16, None
         mu.prepare_fp4_layer_for_marlin(lay)
@@ -916,23 +961,28 @@ def marlin_reference(ctx: Ctx, a: torch.Tensor, codes: torch.Tensor, scales: tor
     w_bytes = lay0.weight.numel() * lay0.weight.element_size()
     layers = [lay0] + [layer() for _ in range(max(1, -(-3 * L2_BYTES // max(1, w_bytes))) - 1)]
 
-    def run(i, sp, qdq=True):
+    def run(i, sp, do_qdq=True):
         lay = layers[i % len(layers)]
-        aq = mxfp4_qdq(a) if qdq else a_q
-        return mu.apply_fp4_marlin_linear(aq, lay.weight, lay.weight_scale, None, lay.workspace, n, k)
+        aq = qdq(a) if do_qdq else a_q
+        return mu.apply_fp4_marlin_linear(aq, lay.weight, lay.weight_scale,
+                                          lay.weight_global_scale if nv else None, lay.workspace, n, k)
 
     ref_out = run(0, None)
-    same = bool(torch.equal(ref_out.view(torch.int16), mxfp4_linear(a, w).view(torch.int16)))
-    a_q = mxfp4_qdq(a)
+    ours_out = linear(a, w)
+    same = bool(torch.equal(ref_out.view(torch.int16), ours_out.view(torch.int16)))
+    rel = float((ours_out.float() - ref_out.float()).norm() / ref_out.float().norm())
+    a_q = qdq(a)
     for i in range(3):
         run(i, None)
     ms_both, _ = timed(ctx, lambda i, sp: run(i, sp), steps, clocks=False)
-    ms_marlin, _ = timed(ctx, lambda i, sp: run(i, sp, qdq=False), steps, clocks=False)
-    return {"impl": "mxfp4_qdq (this build's kernel, bit-exact with the reference's) + vLLM 0.22 marlin_gemm "
-                    "via apply_fp4_marlin_linear, same rows/columns, same GPU, CUDA graph",
+    ms_marlin, _ = timed(ctx, lambda i, sp: run(i, sp, do_qdq=False), steps, clocks=False)
+    return {"impl": (f"{qdq.__name__} (this build's kernel, bit-exact with the " +
+                     ("vLLM NVFP4 emulation" if nv else "reference's") + ") + vLLM 0.22 marlin_gemm "
+                     "via apply_fp4_marlin_linear, same rows/columns, same GPU, CUDA graph"),
             "ms_per_step": round(ms_both, 5), "marlin_only_ms": round(ms_marlin, 5),
             "value": round(2.0 * a.shape[0] * n * k / (ms_both * 1e-3) / 1e12, 1), "unit": "TFLOP/s (per rank)",
-            "speedup_of_ours": round(ms_both / ours_ms, 2), "bit_identical_to_ours": same}
+            "speedup_of_ours": round(ms_both / ours_ms, 2), "bit_identical_to_ours": same,
+            "rel_l2_ours_vs_reference": round(rel, 6)}
 
 
 def attn_record(ctx: Ctx, workload: str, steps: int | None = None, sub: bool = False,
@@ -1181,13 +1231,15 @@ def run_ours(args) -> None:
                 subs["config1_mxfp4_qdq"] = qdq_record(ctx, "mxfp4_qdq", sub=True)
                 subs["config3_linear_m4096"] = gemm_record(ctx, 4096, sub=True)
                 subs["config3_linear_m16"] = gemm_record(ctx, 16, sub=True)
+                subs["config3_nvfp4_linear_m4096"] = gemm_record(ctx, 4096, sub=True, nv=True)
                 subs["config4_sage3_mxfp4_hw"] = attn_record(ctx, "sage3_mxfp4", steps=2, sub=True, sdpa=True)
                 subs["config5_sage3_nvfp4"] = attn_record(ctx, "sage3_nvfp4", steps=5, sub=True)
                 if world > 1:
                     subs["config2_weak_scaling"] = qdq_record(ctx, "nvfp4_qdq", weak=True, sub=True)
             line["sub_records"] = subs
-        elif args.workload == "mxfp4_linear":
-            line = gemm_record(ctx, args.rows or WORKLOADS["mxfp4_linear"]["rows"])
+        elif args.workload in ("mxfp4_linear", "nvfp4_linear"):
+            line = gemm_record(ctx, args.rows or WORKLOADS[args.workload]["rows"],
+                               nv=args.workload == "nvfp4_linear")
         elif args.workload == "mxfp4_moe":
             line = moe_record(ctx)
         elif args.workload.startswith("sage3"):
