@@ -914,7 +914,8 @@ def gemm_record(ctx: Ctx, m: int, sub: bool = False, marlin: bool = True, nv: bo
                 "d2h_bytes_per_step": ml * n * 2,
                 "path": f"vllm_qdq_plugin.gemm.{linear.__name__} on pinned host buffers (bytes per rank)"},
         "gpu_launches": steps * per_call,
-        "roofline": linear_roofline(ml, n, k, ms_step, 2.0 * ml * n * k, peak, src),
+        "roofline": linear_roofline(ml, n, k, ms_step, 2.0 * ml * n * k, peak, src,
+                                    "nvfp4_linear" if nv else "mxfp4_linear"),
         "clocks": clocks,
     }
     if ref:
@@ -1189,15 +1190,15 @@ def moe_record(ctx: Ctx) -> dict:
     return rec
 
 
-def linear_roofline(m: int, n: int, k: int, ms_step: float, flop: float, peak_tf: float, src: str) -> dict:
+def linear_roofline(m: int, n: int, k: int, ms_step: float, flop: float, peak_tf: float, src: str,
+                    kind: str = "mxfp4_linear") -> dict:
     """The bound of one fused linear: the FP4 tensor peak or HBM, whichever
     takes longer for its algorithmic work.  Bytes = 2MK (bf16 A) + NK/2 (W
     codes) + NK/32 (W scales) + 2MN (bf16 C); the decode shapes (M <= 256)
     are HBM-bound, config 3's M = 4096 tensor-bound."""
     nbytes = 2 * m * k + n * k // 2 + n * k // 32 + 2 * m * n
     hbm, hbm_src = measured_peak_hbm()
-    traffic = ncu_traffic("mxfp4_linear" if (m, n) == (4096, 14336) else f"mxfp4_linear_{m}") \
-        if n == 14336 else None
+    traffic = ncu_traffic(kind if (m, n) == (4096, 14336) else f"{kind}_{m}") if n == 14336 else None
     if nbytes / (hbm * 1e9) > flop / (peak_tf * 1e12):
         achieved = nbytes / (ms_step * 1e-3) / 1e9
         return {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
