@@ -61,7 +61,7 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 
-# name -> (config, acc_dtype, distribution, B, H, L, query tiles (None = all))
+# name -> (config, acc_dtype, distribution, B, H, L, query tiles (None = all)[, head dim])
 CASES = {
     # config 4 (Wan-2.1): the reference's Blackwell kernel, 64-key steps
     "mxfp4_hw_L1024": ("mxfp4_hw", "fp32", "c4", 1, 2, 1024, None),
@@ -75,24 +75,34 @@ CASES = {
     # emulated MXFP4 (fp32 accumulation) and the hardware MXFP8 kernel
     "mxfp4_L1024": ("mxfp4", "fp32", "c4", 1, 2, 1024, None),
     "mxfp8_hw_L1024": ("mxfp8_hw", "fp32", "c4", 1, 2, 1024, None),
+    # head dim 64, which the reference's hardware kernels take beside 128
+    # (mxfp4_hw_kernel.py:439), and the emulated NVFP4 config at D = 64 (fp32
+    # accumulation, which the reference allows below D = 128)
+    "mxfp4_hw_D64_L1024": ("mxfp4_hw", "fp32", "c4", 1, 2, 1024, None, 64),
+    "nvfp4_D64_L1024": ("nvfp4", "fp32", "c5", 1, 2, 1024, None, 64),
 }
 
 
+def head_dim(name: str) -> int:
+    return CASES[name][7] if len(CASES[name]) > 7 else 128
+
+
 def case_inputs(name: str) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Seeded bf16 HND inputs [B, H, L, 128] of a case (CPU, deterministic).
+    """Seeded bf16 HND inputs [B, H, L, D] of a case (CPU, deterministic).
 
     c4: Q, V ~ N(0,1); K ~ N(0,1) + a per-(head, channel) offset ~ N(0, 3)
         shared by all tokens (BASELINE config 4's distribution).
     c5: Q, K, V ~ N(0,1); 1% of the K rows of every head scaled by 20
         (BASELINE config 5's distribution)."""
-    _, _, dist, B, H, L, _ = CASES[name]
+    _, _, dist, B, H, L, _ = CASES[name][:7]
+    D = head_dim(name)
     seed = int(hashlib.sha256(name.encode()).hexdigest()[:8], 16)
     g = torch.Generator().manual_seed(seed)
-    q = torch.randn(B, H, L, 128, generator=g)
-    k = torch.randn(B, H, L, 128, generator=g)
-    v = torch.randn(B, H, L, 128, generator=g)
+    q = torch.randn(B, H, L, D, generator=g)
+    k = torch.randn(B, H, L, D, generator=g)
+    v = torch.randn(B, H, L, D, generator=g)
     if dist == "c4":
-        k = k + torch.randn(B, H, 1, 128, generator=g) * 3.0
+        k = k + torch.randn(B, H, 1, D, generator=g) * 3.0
     else:
         pick = torch.rand(B, H, L, 1, generator=g).argsort(dim=2) < max(1, L // 100)
         k = torch.where(pick, k * 20.0, k)
@@ -309,8 +319,8 @@ def _self_check() -> None:
 # running the reference
 # ---------------------------------------------------------------------------
 def run_case(name: str) -> np.ndarray:
-    """The reference's output for a case, as bf16 bits [B, H, rows, 128]."""
-    config, acc, _, B, H, L, tiles = CASES[name]
+    """The reference's output for a case, as bf16 bits [B, H, rows, D]."""
+    config, acc, _, B, H, L, tiles = CASES[name][:7]
     from sage3 import api
     q, k, v = case_inputs(name)
     if tiles is None:

@@ -70,7 +70,7 @@ def test_matches_reference_outputs(cuda_device, name):
     ours = ours[:, :, rows].double()
     ref = torch.from_numpy(fx[f"{name}/out"].view(np.int16).copy()).view(torch.bfloat16)
     ref = ref.to(cuda_device).double()
-    ex = _exact(qd, kd, vd, rows, 1.0 / math.sqrt(128))
+    ex = _exact(qd, kd, vd, rows, 1.0 / math.sqrt(q.shape[-1]))
     e_ours, e_ref, dist = _rel(ours, ex), _rel(ref, ex), _rel(ours, ref)
     print(f"\n{name}: err(ours)={e_ours:.4f} err(reference)={e_ref:.4f} |ours-reference|={dist:.4f}")
     assert torch.isfinite(ours).all()

@@ -1,9 +1,9 @@
 """CPU: the SAGE_ATTN backend surface for calls the FP4 kernels do not take.
 
 The backend advertises the reference's head sizes, 32-256
-(src/vllm_qdq_plugin/sage3_attn/backend.py:18-20).  A head dim or dtype that
-the FP4 kernels do not take runs SDPA with a warning instead of failing in
-forward; the acc_dtype knob is validated and a non-fp32 mode is logged once.
+(src/vllm_qdq_plugin/sage3_attn/backend.py:18-20); the FP4 kernels take 32,
+64, 96 and 128 with bf16 inputs.  A head dim or dtype outside that runs SDPA
+with a warning instead of failing in forward; the acc_dtype knob is validated and a non-fp32 mode is logged once.
 """
 
 from __future__ import annotations
@@ -25,8 +25,8 @@ def _sdpa_nhd(q, k, v, scale):
                                           scale=scale).transpose(1, 2)
 
 
-@pytest.mark.parametrize("d,dtype", [(64, torch.bfloat16), (32, torch.bfloat16), (256, torch.bfloat16),
-                                     (128, torch.float16), (96, torch.float32)])
+@pytest.mark.parametrize("d,dtype", [(256, torch.bfloat16), (160, torch.bfloat16), (224, torch.bfloat16),
+                                     (128, torch.float16), (64, torch.float32)])
 def test_unsupported_head_dim_or_dtype_runs_sdpa(d, dtype, caplog):
     assert d in Sage3TritonBackend.get_supported_head_sizes() or dtype != torch.bfloat16
     g = torch.Generator().manual_seed(d)
@@ -42,9 +42,9 @@ def test_unsupported_head_dim_or_dtype_runs_sdpa(d, dtype, caplog):
 
 
 def test_supported_shape_is_not_rerouted():
-    q = torch.zeros(1, 8, 2, 128, dtype=torch.bfloat16)
-    assert api.unsupported_reason(q) is None
-    assert "head_dim 64" in api.unsupported_reason(torch.zeros(1, 8, 2, 64, dtype=torch.bfloat16))
+    for d in (32, 64, 96, 128):
+        assert api.unsupported_reason(torch.zeros(1, 8, 2, d, dtype=torch.bfloat16)) is None
+    assert "head_dim 256" in api.unsupported_reason(torch.zeros(1, 8, 2, 256, dtype=torch.bfloat16))
 
 
 def test_acc_dtype_validated_and_logged_once(caplog):

@@ -38,7 +38,7 @@ def _case(name):
     return q, k, v, rows, ref
 
 
-@pytest.mark.parametrize("name", ["mxfp4_hw_L1024", "mxfp8_hw_L1024", "mxfp4_hw_L75600"])
+@pytest.mark.parametrize("name", ["mxfp4_hw_L1024", "mxfp8_hw_L1024", "mxfp4_hw_D64_L1024", "mxfp4_hw_L75600"])
 def test_hardware_config_oracle_reproduces_reference(name):
     config = G.CASES[name][0]
     q, k, v, rows, ref = _case(name)
@@ -51,21 +51,21 @@ def test_hardware_config_oracle_reproduces_reference(name):
     for h in range(q.shape[1]):
         bits = [t[0, h].contiguous().view(torch.int16).numpy().view(np.uint16)[:, None, :] for t in (q, k, v)]
         if len(rows) < q.shape[2]:
-            got = oa.attention_rows(*bits, 1.0 / math.sqrt(128), rows, config=config,
+            got = oa.attention_rows(*bits, 1.0 / math.sqrt(q.shape[-1]), rows, config=config,
                                     block_n=oa.REF_BLOCK_N[config], mask_padding=False)
         else:
-            got = oa.attention(*bits, 1.0 / math.sqrt(128), config=config, block_n=oa.REF_BLOCK_N[config],
+            got = oa.attention(*bits, 1.0 / math.sqrt(q.shape[-1]), config=config, block_n=oa.REF_BLOCK_N[config],
                                mask_padding=False)[:, 0]
         assert oa.rel_l2(got, ref[0, h]) < 2.2e-3, (name, h, oa.rel_l2(got, ref[0, h]))
 
 
-@pytest.mark.parametrize("name", ["mxfp4_L1024", "nvfp4_bf16pv_L1024"])
+@pytest.mark.parametrize("name", ["mxfp4_L1024", "nvfp4_bf16pv_L1024", "nvfp4_D64_L1024"])
 def test_emulated_config_oracle_accuracy_against_reference(name):
     config = G.CASES[name][0]
     q, k, v, rows, ref = _case(name)
     for h in range(q.shape[1]):
         bits = [t[0, h].contiguous().view(torch.int16).numpy().view(np.uint16)[:, None, :] for t in (q, k, v)]
-        ex = oa.exact_attention(*bits, 1.0 / math.sqrt(128))[:, 0]
-        got = oa.attention(*bits, 1.0 / math.sqrt(128), config=config, block_n=128)[:, 0]
+        ex = oa.exact_attention(*bits, 1.0 / math.sqrt(q.shape[-1]))[:, 0]
+        got = oa.attention(*bits, 1.0 / math.sqrt(q.shape[-1]), config=config, block_n=128)[:, 0]
         e_ref, e_got = oa.rel_l2(ref[0, h], ex), oa.rel_l2(got, ex)
         assert e_got <= 1.1 * e_ref + 0.005, (name, h, e_got, e_ref)

@@ -3,8 +3,11 @@
 
 using namespace qdqb200;
 
+// Head dims the kernels take: 128, and 32 / 64 / 96 zero-extended to 128.
+static bool head_dim_ok(int64_t D) { return D == 32 || D == 64 || D == 96 || D == 128; }
+
 extern "C" int64_t sage3_attn_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t D) {
-  if (B <= 0 || L <= 0 || H <= 0 || D != 128) return 0;
+  if (B <= 0 || L <= 0 || H <= 0 || !head_dim_ok(D)) return 0;
   return attn::carve(static_cast<int>(B), static_cast<int>(H), static_cast<int>(L), nullptr, nullptr);
 }
 
@@ -14,7 +17,9 @@ extern "C" int sage3_fp4_attn(const void* q, const void* k, const void* v, void*
                               int64_t workspace_bytes, void* stream) {
   if (B < 0 || L < 0 || H < 0) return fail(QDQ_ERR_INVALID_ARG, "sage3_fp4_attn: negative shape");
   if (B == 0 || L == 0 || H == 0) return QDQ_OK;
-  if (D != 128) return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: head_dim %lld (this build supports 128)", (long long)D);
+  if (!head_dim_ok(D))
+    return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: head_dim %lld (this build supports 32, 64, 96 and 128)",
+                (long long)D);
   if (dtype != QDQ_DTYPE_BF16) return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: inputs must be bf16");
   // quant_format -> (Q/K format, P/V format, emulated P, P prescale); see include/qdq_b200.h
   struct Variant { int qk, pv, emu; float pre; };
@@ -56,7 +61,7 @@ extern "C" int sage3_fp4_attn(const void* q, const void* k, const void* v, void*
   p.H = static_cast<int>(H);
   p.L = static_cast<int>(L);
   p.Lp = static_cast<int>((L + 127) / 128 * 128);
-  p.D = 128;
+  p.D = static_cast<int>(D);
   p.q_sb = strides[0]; p.q_sn = strides[1]; p.q_sh = strides[2];
   p.k_sb = strides[3]; p.k_sn = strides[4]; p.k_sh = strides[5];
   p.v_sb = strides[6]; p.v_sn = strides[7]; p.v_sh = strides[8];

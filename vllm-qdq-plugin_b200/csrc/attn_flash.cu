@@ -131,6 +131,7 @@ __device__ __forceinline__ uint64_t code_desc(bool f8, const void* p) {
 
 struct Params {
   int H, L, Lp, T;  // T = Lp / 128
+  int D;            // head dim stored (32, 64, 96 or 128; the channels above D are zero)
   int64_t o_sb, o_sn, o_sh;
   float qk_scale;   // sm_scale * log2(e)
   int causal;
@@ -597,7 +598,7 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     uint32_t u[32];
     tmem_ld32(t_o + lane_base + c, u);
     tmem_ld_wait();
-    if (store) {
+    if (store && hf * HB + c < p.D) {
       float add[32];
       if (p.vsmooth) {  // softmax rows sum to 1: O + v_mean is the attention of the uncentred V
         const float4* vm = reinterpret_cast<const float4*>(p.vmean + static_cast<int64_t>(bh) * HD + hf * HB + c);
@@ -848,6 +849,7 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   p.L = pr.L;
   p.Lp = pr.Lp;
   p.T = pr.Lp / 128;
+  p.D = pr.D;
   p.o_sb = pr.o_sb;
   p.o_sn = pr.o_sn;
   p.o_sh = pr.o_sh;

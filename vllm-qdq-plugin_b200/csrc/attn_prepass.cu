@@ -20,6 +20,12 @@
 //     e = ceil(log2(max(amax, 1e-12) / 448)), byte clamp(e + 127, 0, 254),
 //     code = E4M3 of x / 2^e, round-to-nearest-even (torch's float8_e4m3fn cast).
 //
+// Head dims D < 128 (32, 64, 96) are zero-extended to 128 as the rows are
+// loaded: the extra channels are zero in Q, K and V, so they add nothing to
+// Q K^T, delta_s or P V, and their quantisation groups (whole groups of 32,
+// or of 16 for NVFP4) hold only zeros and leave the real groups' scales
+// alone.  The flash kernel stores only the first D output channels.
+//
 // Outputs (workspace), with Lp = L rounded up to 128, BH = B*H, G = Lp/128:
 //   ksum   fp32 [BH, D]           per-channel sums of k (mean = bf16(ksum / L))
 //   (kernels: colsum_kernel for the K (and V) sums; the Q pass; the K pass,
@@ -191,7 +197,7 @@ __device__ __forceinline__ void quant_group(const float* v, uint8_t* crow, uint8
 // channels of 16-byte chunk t % 16 over rows t / 16 + 16 i of the block's 256
 // rows (16 independent loads in flight), then the 16 partial sums per channel
 // meet in shared memory.
-__global__ void __launch_bounds__(256) colsum_kernel(const __nv_bfloat16* __restrict__ x, int H, int L,
+__global__ void __launch_bounds__(256) colsum_kernel(const __nv_bfloat16* __restrict__ x, int H, int L, int D,
                                                      int64_t sb, int64_t sn, int64_t sh, float* __restrict__ sum) {
   __shared__ __align__(16) float part[16][128];
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
@@ -201,7 +207,7 @@ __global__ void __launch_bounds__(256) colsum_kernel(const __nv_bfloat16* __rest
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const int n = n0 + r0 + 16 * i;
-    if (n < L) {
+    if (n < L && c * 8 < D) {
       const uint4 u = ld_stream(reinterpret_cast<const uint4*>(x + nhd_row(b, n, h, sb, sn, sh) + c * 8));
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -262,7 +268,7 @@ __device__ __forceinline__ void qmean_chunk_async(__nv_bfloat16* qms, const __nv
 }
 
 template <bool kIsQ, int kFmt>
-__global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __restrict__ x, int H, int L, int Lp,
+__global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __restrict__ x, int H, int L, int Lp, int D,
                                                        int64_t sb, int64_t sn, int64_t sh,
                                                        const float* __restrict__ ksum, __nv_bfloat16* __restrict__ qmean,
                                                        uint8_t* __restrict__ codes, uint8_t* __restrict__ sf,
@@ -281,7 +287,7 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
     const int r = r0 + 16 * i;
     const int n = t0 + r;
     uint4 u = make_uint4(0, 0, 0, 0);
-    if (n < L) u = ld_stream(reinterpret_cast<const uint4*>(x + nhd_row(b, n, h, sb, sn, sh) + c * 8));
+    if (n < L && c * 8 < D) u = ld_stream(reinterpret_cast<const uint4*>(x + nhd_row(b, n, h, sb, sn, sh) + c * 8));
     *reinterpret_cast<uint4*>(tile + r * DS_LD + c * 8) = u;
     if (kIsQ) {
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -375,7 +381,7 @@ template <int kFmt>
 __host__ __device__ constexpr int v_smem_bytes() { return V_TILE_BYTES + 128 * v_code_ld<kFmt>(); }
 
 template <int kFmt>
-__global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __restrict__ v, int H, int L, int Lp,
+__global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __restrict__ v, int H, int L, int Lp, int D,
                                                       int64_t sb, int64_t sn, int64_t sh,
                                                       uint8_t* __restrict__ vt, uint8_t* __restrict__ vsf,
                                                       const float* __restrict__ vsum, float* __restrict__ vmean) {
@@ -390,8 +396,8 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
     for (int k = 0; k < 16; ++k) {
       const int i = threadIdx.x + 128 * k, r = i >> 4, c = i & 15;
       const int n = t0 + r;
-      u[k] = n < L ? ld_stream(reinterpret_cast<const uint4*>(v + nhd_row(b, n, h, sb, sn, sh) + c * 8))
-                   : make_uint4(0, 0, 0, 0);
+      u[k] = (n < L && c * 8 < D) ? ld_stream(reinterpret_cast<const uint4*>(v + nhd_row(b, n, h, sb, sn, sh) + c * 8))
+                                  : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
@@ -547,9 +553,9 @@ int launch_qk(const Problem& p, const Workspace& w, cudaStream_t s) {
     attr[dev] = true;
   }
   const int BH = p.B * p.H, T = p.Lp / 128;
-  qk_quant_kernel<true, kFmt><<<dim3(BH, T), 256, QK_SMEM_Q, s>>>(p.q, p.H, p.L, p.Lp, p.q_sb, p.q_sn, p.q_sh, w.ksum,
+  qk_quant_kernel<true, kFmt><<<dim3(BH, T), 256, QK_SMEM_Q, s>>>(p.q, p.H, p.L, p.Lp, p.D, p.q_sb, p.q_sn, p.q_sh, w.ksum,
                                                                  w.qmean, w.qc, w.qsf, p.smoothing, w.ds);
-  qk_quant_kernel<false, kFmt><<<dim3(BH, T), 256, QK_SMEM_K, s>>>(p.k, p.H, p.L, p.Lp, p.k_sb, p.k_sn, p.k_sh,
+  qk_quant_kernel<false, kFmt><<<dim3(BH, T), 256, QK_SMEM_K, s>>>(p.k, p.H, p.L, p.Lp, p.D, p.k_sb, p.k_sn, p.k_sh,
                                                                   w.ksum, w.qmean, w.kc, w.ksf, p.smoothing, w.ds);
   return QDQ_OK;
 }
@@ -567,7 +573,7 @@ int launch_v(const Problem& p, const Workspace& w, const float* vs, cudaStream_t
     attr[dev] = true;
   }
   v_quant_kernel<kFmt><<<dim3(p.B * p.H, p.Lp / 128), 128, v_smem_bytes<kFmt>(), s>>>(
-      p.v, p.H, p.L, p.Lp, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf, vs, w.vmean);
+      p.v, p.H, p.L, p.Lp, p.D, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf, vs, w.vmean);
   return QDQ_OK;
 }
 
@@ -576,11 +582,11 @@ int launch_prepass(const Problem& p, const Workspace& w, cudaStream_t s) {
   if (cudaMemsetAsync(w.ksum, 0, sizeof(float) * BH * 128, s) != cudaSuccess)
     return fail(QDQ_ERR_CUDA, "sage3 prepass: memset failed");
   if (p.smoothing)
-    colsum_kernel<<<dim3(BH, (p.L + 255) / 256), 256, 0, s>>>(p.k, p.H, p.L, p.k_sb, p.k_sn, p.k_sh, w.ksum);
+    colsum_kernel<<<dim3(BH, (p.L + 255) / 256), 256, 0, s>>>(p.k, p.H, p.L, p.D, p.k_sb, p.k_sn, p.k_sh, w.ksum);
   if (p.vsmooth) {
     if (cudaMemsetAsync(w.vsum, 0, sizeof(float) * BH * 128, s) != cudaSuccess)
       return fail(QDQ_ERR_CUDA, "sage3 prepass: memset failed");
-    colsum_kernel<<<dim3(BH, (p.L + 255) / 256), 256, 0, s>>>(p.v, p.H, p.L, p.v_sb, p.v_sn, p.v_sh, w.vsum);
+    colsum_kernel<<<dim3(BH, (p.L + 255) / 256), 256, 0, s>>>(p.v, p.H, p.L, p.D, p.v_sb, p.v_sn, p.v_sh, w.vsum);
   }
   // Q (group means first: the K pass's delta_s reads them), then K, in the Q/K format
   int st = QDQ_OK;

@@ -144,8 +144,10 @@ def _(q, k, v, layout_nhd, sm_scale, quant_format, acc_mode, causal, smoothing):
     return torch.empty_like(q)
 
 
-# Head dims and input dtypes the FP4 kernels take.
-SUPPORTED_HEAD_DIMS = (128,)
+# Head dims and input dtypes the FP4 kernels take (dims below 128 are
+# zero-extended to 128 in the pre-pass; the reference's hardware kernels take
+# 64 and 128, its emulated kernel any dim).
+SUPPORTED_HEAD_DIMS = (32, 64, 96, 128)
 SUPPORTED_DTYPES = (torch.bfloat16,)
 
 
