@@ -1114,7 +1114,59 @@ def sdpa_same_gpu(ctx: Ctx, q, k, v, ours_ms: float) -> dict:
             "ms_per_step": round(sd_ms, 3), "speedup_of_ours": round(sd_ms / ours_ms, 3)}
 
 
-def moe_record(ctx: Ctx) -> dict:
+def moe_marlin_reference(ctx: Ctx, a, codes, scales, sidd, eidd, ntpd, twd, bs, top_k, ours_out,
+                         ours_ms: float, steps: int) -> dict:
+    """The path the grouped GEMM replaces, on the same GPU and routing: this
+    build's mxfp4_qdq (bit-exact with the reference's) of the tokens, then
+    vLLM's moe_wna16_marlin_gemm on expert weights prepared by vLLM itself
+    (prepare_moe_mxfp4_layer_for_marlin), timed in a CUDA graph."""
+    try:
+        import vllm._custom_ops as ops
+        from vllm.model_executor.layers.quantization.utils import marlin_utils_fp4 as mu
+        from vllm.model_executor.layers.quantization.utils.marlin_utils import marlin_make_workspace_new
+        from vllm.scalar_type import scalar_types
+    except Exception as e:  # pragma: no cover
+        return {"unavailable": f"vLLM import failed: {e}"}
+    from vllm_qdq_plugin.qdq import mxfp4_qdq
+    e, n, kh = codes.shape
+    k = kh * 2
+
+    class _Layer(torch.nn.Module):
+        pass
+
+    lay = _Layer()
+    lay.params_dtype = torch.bfloat16
+    w13 = codes.to(ctx.dev)
+    w13_s = scales.to(ctx.dev)
+    w2 = torch.zeros((e, k, n // 4), dtype=torch.uint8, device=ctx.dev)       # the down projection is not timed
+    w2_s = torch.full((e, k, n // 64), 127, dtype=torch.uint8, device=ctx.dev)
+    mw13, _mw2, mw13_s, _mw2_s, _, _ = mu.prepare_moe_mxfp4_layer_for_marlin(lay, w13, w2, w13_s, w2_s, None, None)
+    del w2, w2_s, _mw2, _mw2_s
+    workspace = marlin_make_workspace_new(ctx.dev, 4)
+    m = a.shape[0]
+    out = torch.zeros((m * top_k, n), dtype=torch.bfloat16, device=ctx.dev)
+
+    def run(i, sp):
+        ops.moe_wna16_marlin_gemm(mxfp4_qdq(a), out, mw13, None, mw13_s, None, None, None, None, None, workspace,
+                                  sidd, eidd, ntpd, twd, moe_block_size=bs, top_k=top_k, mul_topk_weights=True,
+                                  b_q_type=scalar_types.float4_e2m1f, size_m=m, size_n=n, size_k=k, is_k_full=True,
+                                  use_atomic_add=False, use_fp32_reduce=True, is_zp_float=False)
+
+    run(0, None)
+    routed = sidd[: int(ntpd.item())]
+    routed = routed[routed < m * top_k].long()
+    same = bool(torch.equal(out[routed].view(torch.int16), ours_out[routed].view(torch.int16)))
+    rel = float((ours_out[routed].float() - out[routed].float()).norm() / out[routed].float().norm())
+    for i in range(2):
+        run(i, None)
+    ms, _ = timed(ctx, run, steps, clocks=False)
+    return {"impl": "mxfp4_qdq (this build's kernel, bit-exact with the reference's) + vLLM 0.22 "
+                    "moe_wna16_marlin_gemm on vLLM-prepared experts, same routing, same GPU, CUDA graph",
+            "ms_per_step": round(ms, 5), "speedup_of_ours": round(ms / ours_ms, 2),
+            "bit_identical_to_ours": same, "rel_l2_ours_vs_reference": round(rel, 6)}
+
+
+def moe_record(ctx: Ctx, sub: bool = False) -> dict:
     """Grouped MXFP4 MoE GEMM at gpt-oss-120b's w13 shape (one replica per rank)."""
     from vllm_qdq_plugin import _native
     from vllm_qdq_plugin.gemm import mxfp4_moe_linear, prepare_mxfp4_moe_weight
@@ -1140,6 +1192,7 @@ def moe_record(ctx: Ctx) -> dict:
         step(i, torch.cuda.current_stream(ctx.dev).cuda_stream)
     steps = max(1, min(args.steps, 200))
     ms_step, clocks = timed(ctx, step, steps)
+    ref = moe_marlin_reference(ctx, a, codes, scales, sidd, eidd, ntpd, twd, bs, top_k, out, ms_step, steps)
     flop = 2.0 * slots * n * k
     value = ctx.world * flop / (ms_step * 1e-3) / 1e12
     hosts = [t.pin_memory() for t in (a_cpu, sid, eid, ntp, topk_w.reshape(-1))]
@@ -1185,7 +1238,8 @@ def moe_record(ctx: Ctx) -> dict:
                      "kernels": "moe_gather_quant_kernel + mxf4_moe_kernel (one C-ABI call)"},
         "clocks": clocks,
     }
-    if ctx.world == 1 and not args.no_cpu_baseline:
+    rec["reference_gpu"] = ref
+    if ctx.world == 1 and not args.no_cpu_baseline and not sub:
         rec["cpu_baseline"] = cpu_moe_sample(wl, m)
     return rec
 
@@ -1235,6 +1289,9 @@ def run_ours(args) -> None:
                 subs["config3_nvfp4_linear_m4096"] = gemm_record(ctx, 4096, sub=True, nv=True)
                 subs["config4_sage3_mxfp4_hw"] = attn_record(ctx, "sage3_mxfp4", steps=2, sub=True, sdpa=True)
                 subs["config5_sage3_nvfp4"] = attn_record(ctx, "sage3_nvfp4", steps=5, sub=True)
+                subs["mxfp8_qdq_config1"] = qdq_record(ctx, "mxfp8_qdq", sub=True)
+                subs["sage3_mxfp8_hw_config4_shape"] = attn_record(ctx, "sage3_mxfp8", steps=2, sub=True)
+                subs["moe_gpt_oss_w13_4096_tokens"] = moe_record(ctx, sub=True)
                 if world > 1:
                     subs["config2_weak_scaling"] = qdq_record(ctx, "nvfp4_qdq", weak=True, sub=True)
             line["sub_records"] = subs
