@@ -37,7 +37,7 @@
 // Four softmax warps per SM sub-partition (instead of two with one thread
 // per row) hide the latency of the exp2 / convert / sum chains; the partner
 // threads of a row exchange their half-row maxima (and at the end their
-// partial row sums) through shared memory and a 64-arrival mbarrier.
+// partial row sums) through shared memory and a 64-thread named barrier.
 // The single S buffer alternates between the two softmax warpgroups, which
 // therefore run out of phase and overlap their MUFU / FMA / ALU work.
 // delta_s on the tensor core: with QK smoothing, S starts as one bf16 MMA
@@ -87,7 +87,6 @@ struct Bars {
   uint64_t p_full[2];   // per warpgroup: its P codes / scales are in shared memory
   uint64_t o_done[2];   // per warpgroup: its PV MMA completed
   uint64_t drain;
-  uint64_t xready[2][4];          // per (query tile, lane quadrant): the two half-row threads' exchange
   float xslot[2][2][2][BM];       // [tile][phase & 1][half][row]: exchanged row maxima, then l
   uint32_t tmem_base;
   int abort;
@@ -292,16 +291,18 @@ __device__ __forceinline__ float e4m3x4_sum(uint32_t w) {
 }
 
 // A row's value from the partner thread (same query tile and row, other half
-// of the keys): both warps write theirs into slot ph & 1 and arrive on the
-// pair's mbarrier (count 64), whose phase ph then completes.  A thread
-// cannot reach phase ph + 2, which reuses the slot, before its partner has
-// arrived for phase ph + 1, i.e. has read phase ph's value.
-__device__ __forceinline__ float pair_exchange(Bars* bars, int wg, int hf, int quad, int r, float v, int ph, bool& ok,
-                                               int* status, int site) {
+// of the keys): both warps write theirs into slot ph & 1 and meet at the
+// pair's named barrier (1 + 4 wg + quad, 64 threads), which also orders the
+// shared-memory writes before the reads.  A thread cannot reach exchange
+// ph + 2, which reuses the slot, before its partner has passed exchange
+// ph + 1, i.e. has read exchange ph's value.  The barrier cannot be left
+// waiting: the two warps run the same nkv + 1 exchanges on every path (a
+// timed-out wait stops waiting but never leaves the loop), and warps of an
+// unused query tile skip softmax_wg together.
+__device__ __forceinline__ float pair_exchange(Bars* bars, int wg, int hf, int quad, int r, float v, int ph) {
   volatile float* slot = &bars->xslot[wg][ph & 1][0][0];
   slot[hf * BM + r] = v;
-  mbar_arrive(&bars->xready[wg][quad]);
-  if (ok) ok = mbar_wait(&bars->xready[wg][quad], ph & 1, status, site);
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + wg * 4 + quad) : "memory");
   return slot[(hf ^ 1) * BM + r];
 }
 
@@ -364,7 +365,7 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
 #pragma unroll
     for (int g = 0; g < NGH; ++g) gm[g] = kNV ? max16(x + 16 * g) : max32(x + 32 * g);
     const float mh = kNV ? fmaxf(fmaxf(gm[0], gm[1]), fmaxf(gm[2], gm[3])) : fmaxf(gm[0], gm[1]);
-    const float mx = fmaxf(mh, pair_exchange(bars, wg, hf, quad, r, mh, j, ok, status, 0x1305));
+    const float mx = fmaxf(mh, pair_exchange(bars, wg, hf, quad, r, mh, j));
     const float m_new = fmaxf(m_run, mx * qk);
     const bool grow = (m_new > m_run) && (m_run != -INFINITY);
     const float alpha = grow ? ex2_approx(m_run - m_new) : 1.0f;
@@ -585,7 +586,7 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     mbar_arrive(&bars->p_full[wg]);
   }
   // ---------------- epilogue: O / l -> bf16 NHD
-  const float l_row = l_run + pair_exchange(bars, wg, hf, quad, r, l_run, nkv, ok, status, 0x1306);
+  const float l_row = l_run + pair_exchange(bars, wg, hf, quad, r, l_run, nkv);
   if (ok && nkv > 0) ok = mbar_wait(&bars->o_done[wg], (nkv - 1) & 1, status, 0x1304);
   ok = __all_sync(0xffffffffu, ok);
   tc_fence_after();
@@ -660,7 +661,6 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->s_free[i], 2 * BM);
       mbar_init(&bars->p_full[i], 2 * BM);
-      for (int q = 0; q < 4; ++q) mbar_init(&bars->xready[i][q], 64);
       mbar_init(&bars->o_done[i], 1);
     }
     mbar_init(&bars->drain, 1);
