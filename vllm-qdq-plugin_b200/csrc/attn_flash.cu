@@ -18,7 +18,7 @@
 // (the reference attends to its zero padding).
 //
 // CTA = two 128-row query tiles (A, B) of one (batch, head) that share every
-// K/V tile, 18 warps:
+// K/V tile, 20 warps:
 //   warps 0-7     softmax A: two threads per query row (TMEM lane), warps
 //                 0-3 on keys 0-63 of every key tile and warps 4-7 on keys
 //                 64-127 (warps w and w + 4 share TMEM lanes 32 (w % 4) ..):
@@ -27,13 +27,14 @@
 //                 when the max grows, exp2, partial row sum, P -> codes +
 //                 block scales in shared memory; epilogue O_A / l -> bf16 NHD
 //   warps 8-15    softmax B (the same for tile B)
-//   warp 16       MMA issuer: per key tile j, S = delta_s_A + Q_A K_j^T, then
-//                 (once A has read S) S = delta_s_B + Q_B K_j^T, then
-//                 O_A += P_A V_{j-1}, O_B += P_B V_{j-1}
-//   warp 17       TMA producer (warps 18-19 idle): K tile [128 keys x 64 B], V^T tile [128 d x 64 B]
+//   warp 16       QK MMA issuer: per key tile j, S = delta_s_A + Q_A K_j^T, then
+//                 (once A has read S) S = delta_s_B + Q_B K_j^T
+//   warp 17       TMA producer: K tile [128 keys x 64 B], V^T tile [128 d x 64 B]
 //                 (64-byte swizzle; E4M3: 128 B rows, 128-byte swizzle), their
 //                 scale chunks and the two tiles' delta_s rows (bf16) into a
 //                 4-stage ring (3 for E4M3); Q_A, Q_B once
+//   warp 18       PV MMA issuer: O_A += P_A V_j, O_B += P_B V_j as each P tile
+//                 is complete (warp 19 idle)
 // Four softmax warps per SM sub-partition (instead of two with one thread
 // per row) hide the latency of the exp2 / convert / sum chains; the partner
 // threads of a row exchange their half-row maxima (and at the end their
@@ -50,8 +51,8 @@
 // reference adds delta_s to the fp32 scores after the QK product; here it is
 // the accumulator's initial value, the same sum in another order.
 // Registers: 96 per thread at launch (640 x 96); setmaxnreg moves them to
-// 104 for the four softmax warpgroups and 64 for the fifth (MMA, producer,
-// two idle warps that complete the warpgroup): 512 x 104 + 128 x 64 = 640 x 96.
+// 104 for the four softmax warpgroups and 64 for the fifth (the two MMA
+// issuers, the producer and an idle warp that completes the warpgroup): 512 x 104 + 128 x 64 = 640 x 96.
 // TMEM: S [0,128) O_A [128,256) O_B [256,384), scale factors [384,432).
 #include <cmath>
 
@@ -72,8 +73,8 @@ constexpr int DS_TX = 2 * 2 * 64 * 2;  // bytes the two 64-key x 2-row delta_s b
 constexpr int ONES_TILE = 2048;      // "ones" MMA operand of one query tile: 128 rows x 16 B
 constexpr int ZERO_TILE = 2048;      // zero K-rows 8-15 of both delta_s MMA operands
 constexpr uint32_t IDESC_DS = idesc_bf16(BM, BN, true);
-constexpr int THREADS = 640;         // 16 softmax warps; the MMA, TMA producer and two idle warps
-constexpr int MMA_WARP = 16, TMA_WARP = 17;
+constexpr int THREADS = 640;         // 16 softmax warps; the two MMA issuers, TMA producer and an idle warp
+constexpr int MMA_WARP = 16, TMA_WARP = 17, PV_WARP = 18;
 constexpr int TMEM_COLS = 512;
 // scale-factor columns: 8 per operand (NVFP4: two chunks; MXFP4 uses the first 4)
 constexpr uint32_t T_S = 0, T_O = 128, T_SFQ = 384, T_SFK = 400, T_SFP = 408, T_SFV = 416;
@@ -86,7 +87,7 @@ struct Bars {
   uint64_t s_free[2];   // per warpgroup: its scores are in registers
   uint64_t p_full[2];   // per warpgroup: its P codes / scales are in shared memory
   uint64_t o_done[2];   // per warpgroup: its PV MMA completed
-  uint64_t drain;
+  uint64_t drain[2];    // per MMA issuer: its last tcgen05 op completed
   float xslot[2][2][2][BM];       // [tile][phase & 1][half][row]: exchanged row maxima, then l
   uint32_t tmem_base;
   int abort;
@@ -655,7 +656,7 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
     mbar_init(&bars->q_full, 1);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&bars->kv_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->kv_empty[s], 2);  // one commit from each MMA issuer
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
@@ -663,7 +664,8 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
       mbar_init(&bars->p_full[i], 2 * BM);
       mbar_init(&bars->o_done[i], 1);
     }
-    mbar_init(&bars->drain, 1);
+    mbar_init(&bars->drain[0], 1);
+    mbar_init(&bars->drain[1], 1);
     bars->abort = 0;
     fence_barrier_init();
     prefetch_tmap(&map_q);
@@ -738,29 +740,13 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
           mbar_wait(&bars->kv_full[j % STAGES], (j / STAGES) & 1, status, 0x1103);
       }
     } else if (warp == MMA_WARP) {
-      // ------------------------------------------------------------ MMA issuer
+      // ---------------------------------------------------- QK (S) MMA issuer
       if (elect_one()) {
         bool ok = mbar_wait(&bars->q_full, 0, status, 0x1201);
         if (ok) {
           tc_fence_after();
           for (int t = 0; t < nq; ++t) cp_sf<kNVq>(tmem + T_SFQ + t * 8, smem + Lay::OFF_QSF + t * SF_TILE);
         }
-        auto issue_pv = [&](int t) -> bool {
-          const int s = t % STAGES;
-          uint8_t* st = smem + Lay::OFF_STAGE + s * Lay::STAGE_BYTES;
-          for (int w = 0; w < nq; ++w) {
-            if (!mbar_wait(&bars->p_full[w], t & 1, status, 0x1202)) return false;
-            tc_fence_after();
-            if (w == 0) cp_sf<kNVp>(tmem + T_SFV, st + Lay::ST_VSF);
-            const int pb = 2 * w + (t & 1);  // P buffer of key tile t
-            cp_sf<kNVp>(tmem + T_SFP, smem + Lay::OFF_PSF + pb * SF_TILE);
-            mma_k128<kPV>(tmem + T_O + w * 128, code_desc(kP8, smem + Lay::OFF_P + pb * Lay::PV_TILE),
-                          code_desc(kP8, st + Lay::ST_V), tmem + T_SFP, tmem + T_SFV, t != 0);
-            tc_commit(&bars->o_done[w]);
-          }
-          tc_commit(&bars->kv_empty[s]);
-          return true;
-        };
         for (int j = 0; ok && j < nkv; ++j) {
           const int s = j % STAGES;
           if (!mbar_wait(&bars->kv_full[s], (j / STAGES) & 1, status, 0x1203)) { ok = false; break; }
@@ -788,13 +774,43 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
             tc_commit(&bars->s_full[w]);
           }
           if (!ok) break;
-          if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+          tc_commit(&bars->kv_empty[s]);  // the stage's K side (K, its scales, delta_s) is read
         }
-        if (ok && nkv > 0) ok = issue_pv(nkv - 1);
         if (!ok) bars->abort = 1;
-        // every issued tcgen05 op has completed before TMEM is released
-        tc_commit(&bars->drain);
-        mbar_wait(&bars->drain, 0, status, 0x1205);
+        // every tcgen05 op this thread issued has completed before TMEM is released
+        tc_commit(&bars->drain[0]);
+        mbar_wait(&bars->drain[0], 0, status, 0x1205);
+      }
+    } else if (warp == PV_WARP) {
+      // ------------------------------------------------------ PV MMA issuer
+      // A thread of its own, so that a PV issue never delays the next S and
+      // each P tile goes to the tensor core as soon as it is complete.  Both
+      // issuers' MMAs touch disjoint TMEM (S, SFQ, SFK here; O, SFP, SFV there)
+      // and only read the stage, which kv_empty (two commits) releases.
+      if (elect_one()) {
+        bool ok = true;
+        for (int t = 0; ok && t < nkv; ++t) {
+          const int s = t % STAGES;
+          // the stage cannot be refilled before this thread's kv_empty commit for tile t
+          if (!mbar_wait(&bars->kv_full[s], (t / STAGES) & 1, status, 0x1206)) { ok = false; break; }
+          uint8_t* st = smem + Lay::OFF_STAGE + s * Lay::STAGE_BYTES;
+          for (int w = 0; w < nq; ++w) {
+            if (!mbar_wait(&bars->p_full[w], t & 1, status, 0x1202)) { ok = false; break; }
+            if (*(volatile int*)&bars->abort) { ok = false; break; }
+            tc_fence_after();
+            if (w == 0) cp_sf<kNVp>(tmem + T_SFV, st + Lay::ST_VSF);
+            const int pb = 2 * w + (t & 1);  // P buffer of key tile t
+            cp_sf<kNVp>(tmem + T_SFP, smem + Lay::OFF_PSF + pb * SF_TILE);
+            mma_k128<kPV>(tmem + T_O + w * 128, code_desc(kP8, smem + Lay::OFF_P + pb * Lay::PV_TILE),
+                          code_desc(kP8, st + Lay::ST_V), tmem + T_SFP, tmem + T_SFV, t != 0);
+            tc_commit(&bars->o_done[w]);
+          }
+          if (!ok) break;
+          tc_commit(&bars->kv_empty[s]);  // the stage's V side is read
+        }
+        if (!ok) bars->abort = 1;
+        tc_commit(&bars->drain[1]);
+        mbar_wait(&bars->drain[1], 0, status, 0x1207);
       }
     }
   }
