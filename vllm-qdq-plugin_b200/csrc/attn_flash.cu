@@ -254,10 +254,15 @@ __device__ __forceinline__ void mma_k128(uint32_t d, uint64_t da, uint64_t db, u
     }
   }
 }
+// Scale chunk(s) at shared-memory descriptor d -> TMEM (NVFP4: two chunks).
+template <bool kNV>
+__device__ __forceinline__ void cp_sf_d(uint32_t taddr, uint64_t d) {
+  tmem_cp_sf(taddr, d);
+  if (kNV) tmem_cp_sf(taddr + 4, d + (SF_CHUNK >> 4));
+}
 template <bool kNV>
 __device__ __forceinline__ void cp_sf(uint32_t taddr, const uint8_t* smem_sf) {
-  tmem_cp_sf(taddr, smem_desc_sf(smem_sf));
-  if (kNV) tmem_cp_sf(taddr + 4, smem_desc_sf(smem_sf + SF_CHUNK));
+  cp_sf_d<kNV>(taddr, smem_desc_sf(smem_sf));
 }
 
 
@@ -747,11 +752,30 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
           tc_fence_after();
           for (int t = 0; t < nq; ++t) cp_sf<kNVq>(tmem + T_SFQ + t * 8, smem + Lay::OFF_QSF + t * SF_TILE);
         }
+        // Descriptors are computed once: a shared-memory descriptor's start
+        // address counts 16-byte units (14 bits, no carry out for addresses
+        // below 256 KB), so the tile in stage s, or query tile w, is the
+        // stage-0 (tile-0) descriptor plus its byte offset / 16.  The delta_s
+        // B descriptor's SBO (bits 32-45) is the distance to the zero tile,
+        // which shrinks by the same amount as the start grows.
+        constexpr uint64_t kStage = Lay::STAGE_BYTES >> 4;
+        constexpr uint64_t kDsStep = kStage - (kStage << 32);
+        const uint64_t kd0 = code_desc(kQ8, smem + Lay::OFF_STAGE + Lay::ST_K);
+        const uint64_t ksf0 = smem_desc_sf(smem + Lay::OFF_STAGE + Lay::ST_KSF);
+        const uint64_t qd0 = code_desc(kQ8, smem + Lay::OFF_Q);
+        const uint32_t z_addr = smem_u32(smem + Lay::OFF_ZERO);
+        const uint32_t a_addr = smem_u32(smem + Lay::OFF_ONES);
+        const uint32_t b_addr = smem_u32(smem + Lay::OFF_STAGE + Lay::ST_DS);
+        // A: K-major, no swizzle: 8-row core matrices 128 B apart (SBO), K-rows 8-15 -> zeros (LBO)
+        // B: MN-major, 128-byte swizzle: 64-key atoms 1024 B apart (LBO), K-rows 8-15 -> zeros (SBO)
+        const uint64_t dsa[2] = {smem_desc(a_addr, z_addr - a_addr, 128, 0),
+                                 smem_desc(a_addr + ONES_TILE, z_addr - a_addr - ONES_TILE, 128, 0)};
+        const uint64_t dsb0 = smem_desc(b_addr, 1024, z_addr - b_addr, 2);
         for (int j = 0; ok && j < nkv; ++j) {
           const int s = j % STAGES;
           if (!mbar_wait(&bars->kv_full[s], (j / STAGES) & 1, status, 0x1203)) { ok = false; break; }
           if (*(volatile int*)&bars->abort) { ok = false; break; }
-          uint8_t* st = smem + Lay::OFF_STAGE + s * Lay::STAGE_BYTES;
+          const uint64_t su = static_cast<uint64_t>(s);
           for (int w = 0; w < nq && ok; ++w) {
             // S is free once the warpgroup that used it last has read its scores:
             // for A that is B (or A alone) at key tile j-1, for B it is A at key tile j.
@@ -759,18 +783,11 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
             const int prev_j = w == 0 ? j - 1 : j;
             if (prev_j >= 0 && !mbar_wait(&bars->s_free[prev], prev_j & 1, status, 0x1204)) { ok = false; break; }
             tc_fence_after();
-            if (w == 0) cp_sf<kNVq>(tmem + T_SFK, st + Lay::ST_KSF);
-            if (p.smoothing) {  // S = delta_s of this tile's query group
-              const uint32_t a_addr = smem_u32(smem + Lay::OFF_ONES + w * ONES_TILE);
-              const uint32_t b_addr = smem_u32(st + Lay::ST_DS);
-              const uint32_t z_addr = smem_u32(smem + Lay::OFF_ZERO);
-              // A: K-major, no swizzle: 8-row core matrices 128 B apart (SBO), K-rows 8-15 -> zeros (LBO)
-              // B: MN-major, 128-byte swizzle: 64-key atoms 1024 B apart (LBO), K-rows 8-15 -> zeros (SBO)
-              mma_f16(tmem + T_S, smem_desc(a_addr, z_addr - a_addr, 128, 0), smem_desc(b_addr, 1024, z_addr - b_addr, 2),
-                      IDESC_DS, 0);
-            }
-            mma_k128<kQK>(tmem + T_S, code_desc(kQ8, smem + Lay::OFF_Q + w * Lay::QK_TILE),
-                          code_desc(kQ8, st + Lay::ST_K), tmem + T_SFQ + w * 8, tmem + T_SFK, p.smoothing != 0);
+            if (w == 0) cp_sf_d<kNVq>(tmem + T_SFK, ksf0 + su * kStage);
+            if (p.smoothing)  // S = delta_s of this tile's query group
+              mma_f16(tmem + T_S, dsa[w], dsb0 + su * kDsStep, IDESC_DS, 0);
+            mma_k128<kQK>(tmem + T_S, qd0 + static_cast<uint64_t>(w) * (Lay::QK_TILE >> 4), kd0 + su * kStage,
+                          tmem + T_SFQ + w * 8, tmem + T_SFK, p.smoothing != 0);
             tc_commit(&bars->s_full[w]);
           }
           if (!ok) break;
@@ -789,20 +806,25 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
       // and only read the stage, which kv_empty (two commits) releases.
       if (elect_one()) {
         bool ok = true;
+        constexpr uint64_t kStage = Lay::STAGE_BYTES >> 4;
+        const uint64_t vd0 = code_desc(kP8, smem + Lay::OFF_STAGE + Lay::ST_V);
+        const uint64_t vsf0 = smem_desc_sf(smem + Lay::OFF_STAGE + Lay::ST_VSF);
+        const uint64_t pd0 = code_desc(kP8, smem + Lay::OFF_P);
+        const uint64_t psf0 = smem_desc_sf(smem + Lay::OFF_PSF);
         for (int t = 0; ok && t < nkv; ++t) {
           const int s = t % STAGES;
           // the stage cannot be refilled before this thread's kv_empty commit for tile t
           if (!mbar_wait(&bars->kv_full[s], (t / STAGES) & 1, status, 0x1206)) { ok = false; break; }
-          uint8_t* st = smem + Lay::OFF_STAGE + s * Lay::STAGE_BYTES;
+          const uint64_t so = static_cast<uint64_t>(s) * kStage;
           for (int w = 0; w < nq; ++w) {
             if (!mbar_wait(&bars->p_full[w], t & 1, status, 0x1202)) { ok = false; break; }
             if (*(volatile int*)&bars->abort) { ok = false; break; }
             tc_fence_after();
-            if (w == 0) cp_sf<kNVp>(tmem + T_SFV, st + Lay::ST_VSF);
-            const int pb = 2 * w + (t & 1);  // P buffer of key tile t
-            cp_sf<kNVp>(tmem + T_SFP, smem + Lay::OFF_PSF + pb * SF_TILE);
-            mma_k128<kPV>(tmem + T_O + w * 128, code_desc(kP8, smem + Lay::OFF_P + pb * Lay::PV_TILE),
-                          code_desc(kP8, st + Lay::ST_V), tmem + T_SFP, tmem + T_SFV, t != 0);
+            if (w == 0) cp_sf_d<kNVp>(tmem + T_SFV, vsf0 + so);
+            const uint64_t pb = static_cast<uint64_t>(2 * w + (t & 1));  // P buffer of key tile t
+            cp_sf_d<kNVp>(tmem + T_SFP, psf0 + pb * (SF_TILE >> 4));
+            mma_k128<kPV>(tmem + T_O + w * 128, pd0 + pb * (Lay::PV_TILE >> 4), vd0 + so, tmem + T_SFP, tmem + T_SFV,
+                          t != 0);
             tc_commit(&bars->o_done[w]);
           }
           if (!ok) break;
