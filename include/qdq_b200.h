@@ -269,7 +269,9 @@ int64_t sage3_attn_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t D);
 
 /*
  * O = softmax(Q K^T * sm_scale) V with FP4 tensor-core MMAs (self-attention,
- * Q/K/V/O of the same [B, L, H, D] shape, D in {32, 64, 96, 128}, bf16; the
+ * Q/K/V/O of the same [B, L, H, D] shape, D in {32, 64, 96, 128}, bf16 or fp16
+ * (dtype QDQ_DTYPE_BF16 / QDQ_DTYPE_FP16; with fp16 the smoothing rounds to
+ * fp16 and O is fp16, as the reference's torch ops on fp16 tensors); the
  * reference's hardware kernels take D in {64, 128}, mxfp4_hw_kernel.py:439).
  * Head dims below 128 are zero-extended to 128 inside the pre-pass, which
  * leaves every real quantisation group and every product unchanged.

@@ -47,6 +47,24 @@ def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
     return (bits.astype(np.uint32) << 16).view(np.float32)
 
 
+def f16_round(x: np.ndarray) -> np.ndarray:
+    """Round to fp16 (nearest even; numpy's conversion from float64 rounds
+    once), returned as float32: the reference's torch ops on fp16 inputs."""
+    return np.asarray(x, np.float64).astype(np.float16).astype(np.float32)
+
+
+def round16(x: np.ndarray, f16: bool = False) -> np.ndarray:
+    """Round to the 16-bit input dtype: fp16 if f16, else bf16."""
+    return f16_round(x) if f16 else bf16_round(x)
+
+
+def bits_to_f32(bits: np.ndarray, f16: bool = False) -> np.ndarray:
+    """uint16 bit patterns of fp16 (f16) or bf16 values -> float32."""
+    if f16:
+        return np.ascontiguousarray(bits, dtype=np.uint16).view(np.float16).astype(np.float32)
+    return bf16_bits_to_f32(bits)
+
+
 def _e4m3_table() -> np.ndarray:
     b = np.arange(256)
     e = (b >> 3) & 0xF
@@ -98,7 +116,7 @@ def e4m3_round(x: np.ndarray) -> np.ndarray:
     return (np.round(x / step) * step).astype(np.float32)  # np.round: half to even
 
 
-def nv_quant_deq(x: np.ndarray, block: int = 16) -> np.ndarray:
+def nv_quant_deq(x: np.ndarray, block: int = 16, f16: bool = False) -> np.ndarray:
     """NVFP4 of the reference's nvfp4 QuantConfig (quantize.py:21-81 with
     round_to_e4m3) on the hardware grid, per 16 along the last axis:
     scale = e4m3(max(bf16(amax / 6), 1e-8)), codes of the exact quotient
@@ -106,11 +124,11 @@ def nv_quant_deq(x: np.ndarray, block: int = 16) -> np.ndarray:
     bf16 quotient and a 9-level grid no FP4 hardware has; parity with them is
     by tolerance), dequantised; a zero scale zeroes the block.  block=32 gives
     the mxfp4_s1_e4m3 QuantConfig (quant_config.py:246-255), the same steps per
-    32."""
+    32.  With fp16 inputs (f16) the scale is rounded to fp16 instead of bf16."""
     sh = x.shape
     xb = np.asarray(x, np.float32).reshape(*sh[:-1], sh[-1] // block, block)
     amax = np.abs(xb).max(axis=-1)
-    sc = np.maximum(bf16_round(amax / np.float32(6.0)), np.float32(1e-8))
+    sc = np.maximum(round16(amax / np.float32(6.0), f16), np.float32(1e-8))
     s = e4m3_round(sc).astype(np.float64)
     quot = xb.astype(np.float64) / np.where(s > 0, s, 1.0)[..., None]  # correctly rounded: exact at midpoints
     q = np.where(s[..., None] > 0, _rna_e2m1(quot), 0.0)
@@ -123,21 +141,22 @@ def _ceil_log2(r: np.ndarray) -> np.ndarray:
     return np.where(r == 0, -127, out)
 
 
-def _quant_deq(x: np.ndarray, fmt: str) -> np.ndarray:
+def _quant_deq(x: np.ndarray, fmt: str, f16: bool = False) -> np.ndarray:
     """Dequantised x [rows, K] in operand format fmt, blocks along K:
     "mx4" quantize_to_mxfp4, "nv4" NVFP4 per 16, "mx8" quantize_to_mxfp8,
     "nv4b32" E2M1 with an E4M3 scale per 32."""
     if fmt == "nv4":
-        return nv_quant_deq(x)
+        return nv_quant_deq(x, 16, f16)
     if fmt == "nv4b32":
-        return nv_quant_deq(x, 32)
+        return nv_quant_deq(x, 32, f16)
     if fmt == "mx8":
         return _deq8(*oq.mxfp8_hw_quant(x))
     return _deq(*oq.mxfp4_hw_quant(x))
 
 
 def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True, nv: bool = False,
-            fp8: bool = False, qk_fmt: str | None = None, pv_fmt: str | None = None, vsmooth: bool = False):
+            fp8: bool = False, qk_fmt: str | None = None, pv_fmt: str | None = None, vsmooth: bool = False,
+            f16: bool = False):
     """q, k, v: float32 [L, D] holding bf16 values for one (batch, head).
     Returns (qd, kd, vd, ds): dequantised Q [Lp, D], K [Lp, D], V [Lp, D]
     (V quantised along the sequence) and delta_s [G, Lp] (zeros without
@@ -145,7 +164,8 @@ def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True,
     selects MXFP8 (quantize_to_mxfp8); qk_fmt / pv_fmt ("mx4", "nv4", "mx8")
     set the two operand formats separately.  vsmooth (transforms.py
     v_smoothing) quantises bf16(v - bf16(mean_L(v))); the mean is then the
-    caller's to add to the output (see vmean())."""
+    caller's to add to the output (see vmean()).  f16: the inputs are fp16
+    values and every rounding of the smoothing is to fp16."""
     default = "nv4" if nv else ("mx8" if fp8 else "mx4")
     qk_fmt = qk_fmt or default
     pv_fmt = pv_fmt or default
@@ -153,13 +173,13 @@ def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True,
     Lp = (L + 127) // 128 * 128
     G = Lp // 128
     if smoothing:
-        kmean = bf16_round(k.astype(np.float64).mean(axis=0))
-        kc = bf16_round(k - kmean)
+        kmean = round16(k.astype(np.float64).mean(axis=0), f16)
+        kc = round16(k - kmean, f16)
         qpad = np.zeros((Lp, D), np.float32)
         qpad[:L] = q
-        qmeans = bf16_round(qpad.reshape(G, 128, D).astype(np.float64).mean(axis=1))
-        qs = bf16_round(q - np.repeat(qmeans, 128, axis=0)[:L])
-        ds = bf16_round(qmeans.astype(np.float64) @ kc.astype(np.float64).T)  # [G, L]
+        qmeans = round16(qpad.reshape(G, 128, D).astype(np.float64).mean(axis=1), f16)
+        qs = round16(q - np.repeat(qmeans, 128, axis=0)[:L], f16)
+        ds = round16(qmeans.astype(np.float64) @ kc.astype(np.float64).T, f16)  # [G, L]
     else:
         kc, qs = k, q
         ds = np.zeros((G, L), np.float32)
@@ -167,14 +187,14 @@ def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, smoothing: bool = True,
     dsp = np.zeros((G, Lp), np.float64)
     dsp[:, :L] = ds
     if vsmooth:
-        v = bf16_round(v - vmean(v))
-    return (_quant_deq(pad(qs), qk_fmt), _quant_deq(pad(kc), qk_fmt),
-            _quant_deq(np.ascontiguousarray(pad(v).T), pv_fmt).T, dsp)
+        v = round16(v - vmean(v, f16), f16)
+    return (_quant_deq(pad(qs), qk_fmt, f16), _quant_deq(pad(kc), qk_fmt, f16),
+            _quant_deq(np.ascontiguousarray(pad(v).T), pv_fmt, f16).T, dsp)
 
 
-def vmean(v: np.ndarray) -> np.ndarray:
-    """bf16(mean over the sequence of v) [D] (transforms.py v_smoothing)."""
-    return bf16_round(v.astype(np.float64).mean(axis=0))
+def vmean(v: np.ndarray, f16: bool = False) -> np.ndarray:
+    """dtype(mean over the sequence of v) [D] (transforms.py v_smoothing)."""
+    return round16(v.astype(np.float64).mean(axis=0), f16)
 
 
 def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: bool = False,
@@ -282,9 +302,10 @@ REF_BLOCK_N = {name: (128 if cfg[2] else 64) for name, cfg in CONFIGS.items()}
 
 def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_scale: float,
               block_n: int | None = None, causal: bool = False, smoothing: bool = True,
-              mask_padding: bool = True, config: str = "mxfp4_hw") -> np.ndarray:
-    """q/k/v: uint16 bf16 bit patterns [L, H, D] (NHD with B = 1); returns O [L, H, D].
-    block_n defaults to the reference's key tile for the config (REF_BLOCK_N)."""
+              mask_padding: bool = True, config: str = "mxfp4_hw", f16: bool = False) -> np.ndarray:
+    """q/k/v: uint16 bf16 (fp16 if f16) bit patterns [L, H, D] (NHD with B = 1);
+    returns O [L, H, D].  block_n defaults to the reference's key tile for the
+    config (REF_BLOCK_N)."""
     qk_fmt, pv_fmt, emulated, pre, vsmooth, qk_smooth = CONFIGS[config]
     smoothing = smoothing and qk_smooth
     if block_n is None:
@@ -292,20 +313,20 @@ def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_sca
     L, H, D = q_bits.shape
     out = np.zeros((L, H, D))
     for h in range(H):
-        q = bf16_bits_to_f32(q_bits[:, h])
-        k = bf16_bits_to_f32(k_bits[:, h])
-        v = bf16_bits_to_f32(v_bits[:, h])
-        qd, kd, vd, ds = prepass(q, k, v, smoothing, qk_fmt=qk_fmt, pv_fmt=pv_fmt, vsmooth=vsmooth)
+        q = bits_to_f32(q_bits[:, h], f16)
+        k = bits_to_f32(k_bits[:, h], f16)
+        v = bits_to_f32(v_bits[:, h], f16)
+        qd, kd, vd, ds = prepass(q, k, v, smoothing, qk_fmt=qk_fmt, pv_fmt=pv_fmt, vsmooth=vsmooth, f16=f16)
         out[:, h] = flash(qd, kd, vd, ds, L, sm_scale, block_n, causal, mask_padding, pv_fmt == "nv4", emulated,
                           fp8=pv_fmt == "mx8", pre=pre, e4s32=pv_fmt == "nv4b32")
         if vsmooth:
-            out[:, h] += vmean(v)
+            out[:, h] += vmean(v, f16)
     return out
 
 
 def attention_rows(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_scale: float,
                    rows: np.ndarray, config: str = "mxfp4_hw", block_n: int | None = None,
-                   mask_padding: bool = True) -> np.ndarray:
+                   mask_padding: bool = True, f16: bool = False) -> np.ndarray:
     """attention() of one head ([L, 1, D] bit patterns) for the query rows
     `rows` only: the pre-pass over the whole sequence, then the flash loop on
     each 128-row query tile that holds a requested row.  Returns O [len(rows), D]."""
@@ -313,8 +334,8 @@ def attention_rows(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, s
     if block_n is None:
         block_n = REF_BLOCK_N[config]
     L = q_bits.shape[0]
-    q, k, v = (bf16_bits_to_f32(t[:, 0]) for t in (q_bits, k_bits, v_bits))
-    qd, kd, vd, ds = prepass(q, k, v, qk_smooth, qk_fmt=qk_fmt, pv_fmt=pv_fmt, vsmooth=vsmooth)
+    q, k, v = (bits_to_f32(t[:, 0], f16) for t in (q_bits, k_bits, v_bits))
+    qd, kd, vd, ds = prepass(q, k, v, qk_smooth, qk_fmt=qk_fmt, pv_fmt=pv_fmt, vsmooth=vsmooth, f16=f16)
     rows = np.asarray(rows)
     out = np.zeros((len(rows), q.shape[1]))
     for t in np.unique(rows // 128):
@@ -324,18 +345,18 @@ def attention_rows(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, s
         sel = rows // 128 == t
         out[sel] = o[rows[sel] - 128 * t]
         if vsmooth:
-            out[sel] += vmean(v)
+            out[sel] += vmean(v, f16)
     return out
 
 
-def exact_attention(q_bits, k_bits, v_bits, sm_scale: float, causal: bool = False) -> np.ndarray:
+def exact_attention(q_bits, k_bits, v_bits, sm_scale: float, causal: bool = False, f16: bool = False) -> np.ndarray:
     """Unquantised float64 softmax attention (the accuracy reference)."""
     L, H, D = q_bits.shape
     out = np.zeros((L, H, D))
     for h in range(H):
-        q = bf16_bits_to_f32(q_bits[:, h]).astype(np.float64)
-        k = bf16_bits_to_f32(k_bits[:, h]).astype(np.float64)
-        v = bf16_bits_to_f32(v_bits[:, h]).astype(np.float64)
+        q = bits_to_f32(q_bits[:, h], f16).astype(np.float64)
+        k = bits_to_f32(k_bits[:, h], f16).astype(np.float64)
+        v = bits_to_f32(v_bits[:, h], f16).astype(np.float64)
         s = q @ k.T * sm_scale
         if causal:
             s = np.where(np.arange(L)[None, :] <= np.arange(L)[:, None], s, -np.inf)

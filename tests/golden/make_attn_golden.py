@@ -61,7 +61,7 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 
-# name -> (config, acc_dtype, distribution, B, H, L, query tiles (None = all)[, head dim])
+# name -> (config, acc_dtype, distribution, B, H, L, query tiles (None = all)[, head dim[, input dtype]])
 CASES = {
     # config 4 (Wan-2.1): the reference's Blackwell kernel, 64-key steps
     "mxfp4_hw_L1024": ("mxfp4_hw", "fp32", "c4", 1, 2, 1024, None),
@@ -80,6 +80,10 @@ CASES = {
     # accumulation, which the reference allows below D = 128)
     "mxfp4_hw_D64_L1024": ("mxfp4_hw", "fp32", "c4", 1, 2, 1024, None, 64),
     "nvfp4_D64_L1024": ("nvfp4", "fp32", "c5", 1, 2, 1024, None, 64),
+    # fp16 inputs: the reference's smoothing then runs in fp16 and its output is fp16
+    "mxfp4_hw_f16_L1024": ("mxfp4_hw", "fp32", "c4", 1, 2, 1024, None, 128, "fp16"),
+    "mxfp8_hw_f16_L1024": ("mxfp8_hw", "fp32", "c4", 1, 2, 1024, None, 128, "fp16"),
+    "nvfp4_f16pv_L1024": ("nvfp4", "fp16_pv_only", "c5", 1, 2, 1024, None, 128, "fp16"),
 }
 
 
@@ -87,8 +91,12 @@ def head_dim(name: str) -> int:
     return CASES[name][7] if len(CASES[name]) > 7 else 128
 
 
+def input_dtype(name: str) -> torch.dtype:
+    return torch.float16 if len(CASES[name]) > 8 and CASES[name][8] == "fp16" else torch.bfloat16
+
+
 def case_inputs(name: str) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Seeded bf16 HND inputs [B, H, L, D] of a case (CPU, deterministic).
+    """Seeded bf16 (or fp16) HND inputs [B, H, L, D] of a case (CPU, deterministic).
 
     c4: Q, V ~ N(0,1); K ~ N(0,1) + a per-(head, channel) offset ~ N(0, 3)
         shared by all tokens (BASELINE config 4's distribution).
@@ -106,7 +114,8 @@ def case_inputs(name: str) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     else:
         pick = torch.rand(B, H, L, 1, generator=g).argsort(dim=2) < max(1, L // 100)
         k = torch.where(pick, k * 20.0, k)
-    return q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
+    dt = input_dtype(name)
+    return q.to(dt), k.to(dt), v.to(dt)
 
 
 def input_checksum(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> str:
@@ -319,13 +328,13 @@ def _self_check() -> None:
 # running the reference
 # ---------------------------------------------------------------------------
 def run_case(name: str) -> np.ndarray:
-    """The reference's output for a case, as bf16 bits [B, H, rows, D]."""
+    """The reference's output for a case, as bits of the input dtype [B, H, rows, D]."""
     config, acc, _, B, H, L, tiles = CASES[name][:7]
     from sage3 import api
     q, k, v = case_inputs(name)
     if tiles is None:
         out = api.sageattn3_standalone(q, k, v, config=config, acc_dtype=acc)
-        return out.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+        return out.to(q.dtype).view(torch.int16).numpy().view(np.uint16)
     # Selected query tiles of the mxfp4_hw path: the steps of sage3/api.py:161-206
     # (smoothing over the whole sequence, padding, quantisation), then the
     # reference kernel on each chosen 128-row query tile with that tile's

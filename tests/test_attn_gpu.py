@@ -80,6 +80,32 @@ def test_emulated_configs_match_oracle(cuda_device, config, L, H):
     assert oa.rel_l2(got, exact) <= 1.1 * oa.rel_l2(want, exact) + 0.01
 
 
+@pytest.mark.parametrize("config", ["mxfp4_hw", "nvfp4", "mxfp8_hw", "mxfp4_s1_vsmooth"])
+@pytest.mark.parametrize("L,H,causal", [(300, 2, False), (1000, 1, False), (256, 1, True)])
+def test_fp16_inputs_match_oracle(cuda_device, config, L, H, causal):
+    """fp16 q/k/v: the smoothing rounds to fp16 (as the reference's torch ops
+    on fp16 tensors), delta_s is an fp16 MMA operand and the output is fp16.
+    Same bars as bf16: relative L2 vs the same-tile oracle (run with fp16
+    roundings) <= 2e-2, error vs exact attention within 1.1x (+0.01) of the
+    reference-tiled oracle's."""
+    q, k, v = (t.to(torch.float16) for t in _qkv(L, H, seed=L * 5 + H + len(config), v_offset=2.0))
+    sm = 1.0 / math.sqrt(128)
+    from vllm_qdq_plugin.sage3_attn.sage3 import sage3_attention_nhd
+    out = sage3_attention_nhd(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), config=config,
+                              is_causal=causal)
+    assert out.dtype == torch.float16
+    got = out.float().cpu().numpy()[0]
+    qb, kb, vb = _bits(q[0]), _bits(k[0]), _bits(v[0])
+    want = oa.attention(qb, kb, vb, sm, block_n=KERNEL_BLOCK_N, causal=causal, config=config, f16=True)
+    err = oa.rel_l2(got, want)
+    assert err < 2e-2, f"rel L2 vs oracle {err}"
+    exact = oa.exact_attention(qb, kb, vb, sm, causal=causal, f16=True)
+    ref = oa.attention(qb, kb, vb, sm, causal=causal, config=config, mask_padding=False, f16=True)
+    assert oa.rel_l2(got, exact) <= 1.1 * oa.rel_l2(ref, exact) + 0.01
+    from vllm_qdq_plugin import _native
+    assert _native.device_status() == 0
+
+
 SINGLE_LEVEL_AND_MIXED = ["mxfp4_s1", "mxfp8_s1", "mixed_fp8qk_fp4pv", "mixed_fp4qk_fp8pv",
                           "mixed_mxfp8qk_mxfp4pv_hw", "mixed_mxfp4qk_mxfp8pv_hw", "mxfp4_s1_vsmooth",
                           "mixed_fp8qk_fp4pv_vs", "mixed_fp4qk_fp8pv_vs", "mxfp4_s1_2level", "mxfp4_s1_e4m3"]

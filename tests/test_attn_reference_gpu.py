@@ -66,9 +66,9 @@ def test_matches_reference_outputs(cuda_device, name):
     rows = torch.from_numpy(fx[f"{name}/rows"].astype(np.int64)).to(cuda_device)
     qd, kd, vd = (t.to(cuda_device) for t in (q, k, v))
     ours = sageattn3_standalone(qd, kd, vd, config=config, acc_dtype=acc)
-    assert ours.shape == q.shape and ours.dtype == torch.bfloat16
+    assert ours.shape == q.shape and ours.dtype == q.dtype
     ours = ours[:, :, rows].double()
-    ref = torch.from_numpy(fx[f"{name}/out"].view(np.int16).copy()).view(torch.bfloat16)
+    ref = torch.from_numpy(fx[f"{name}/out"].view(np.int16).copy()).view(q.dtype)
     ref = ref.to(cuda_device).double()
     ex = _exact(qd, kd, vd, rows, 1.0 / math.sqrt(q.shape[-1]))
     e_ours, e_ref, dist = _rel(ours, ex), _rel(ref, ex), _rel(ours, ref)

@@ -2,7 +2,7 @@
 
 The backend advertises the reference's head sizes, 32-256
 (src/vllm_qdq_plugin/sage3_attn/backend.py:18-20); the FP4 kernels take 32,
-64, 96 and 128 with bf16 inputs.  A head dim or dtype outside that runs SDPA
+64, 96 and 128 with bf16 or fp16 inputs.  A head dim or dtype outside that runs SDPA
 with a warning instead of failing in forward; the acc_dtype knob is validated and a non-fp32 mode is logged once.
 """
 
@@ -25,10 +25,10 @@ def _sdpa_nhd(q, k, v, scale):
                                           scale=scale).transpose(1, 2)
 
 
-@pytest.mark.parametrize("d,dtype", [(256, torch.bfloat16), (160, torch.bfloat16), (224, torch.bfloat16),
-                                     (128, torch.float16), (64, torch.float32)])
+@pytest.mark.parametrize("d,dtype", [(256, torch.bfloat16), (160, torch.bfloat16), (224, torch.float16),
+                                     (128, torch.float32), (64, torch.float32)])
 def test_unsupported_head_dim_or_dtype_runs_sdpa(d, dtype, caplog):
-    assert d in Sage3TritonBackend.get_supported_head_sizes() or dtype != torch.bfloat16
+    assert d in Sage3TritonBackend.get_supported_head_sizes() or dtype == torch.float32
     g = torch.Generator().manual_seed(d)
     q, k, v = (torch.randn(1, 40, 2, d, generator=g).to(dtype) for _ in range(3))
     impl = Sage3TritonImpl(num_heads=2, head_size=d, softmax_scale=d ** -0.5)
@@ -43,8 +43,10 @@ def test_unsupported_head_dim_or_dtype_runs_sdpa(d, dtype, caplog):
 
 def test_supported_shape_is_not_rerouted():
     for d in (32, 64, 96, 128):
-        assert api.unsupported_reason(torch.zeros(1, 8, 2, d, dtype=torch.bfloat16)) is None
+        for dtype in (torch.bfloat16, torch.float16):
+            assert api.unsupported_reason(torch.zeros(1, 8, 2, d, dtype=dtype)) is None
     assert "head_dim 256" in api.unsupported_reason(torch.zeros(1, 8, 2, 256, dtype=torch.bfloat16))
+    assert "float32" in api.unsupported_reason(torch.zeros(1, 8, 2, 128, dtype=torch.float32))
 
 
 def test_acc_dtype_validated_and_logged_once(caplog):

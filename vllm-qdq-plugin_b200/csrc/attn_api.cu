@@ -20,7 +20,8 @@ extern "C" int sage3_fp4_attn(const void* q, const void* k, const void* v, void*
   if (!head_dim_ok(D))
     return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: head_dim %lld (this build supports 32, 64, 96 and 128)",
                 (long long)D);
-  if (dtype != QDQ_DTYPE_BF16) return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: inputs must be bf16");
+  if (dtype != QDQ_DTYPE_BF16 && dtype != QDQ_DTYPE_FP16)
+    return fail(QDQ_ERR_UNSUPPORTED, "sage3_fp4_attn: inputs must be bf16 or fp16 (dtype %d)", dtype);
   // quant_format -> (Q/K format, P/V format, emulated P, P prescale); see include/qdq_b200.h
   struct Variant { int qk, pv, emu; float pre; };
   static const Variant kVariants[] = {
@@ -62,6 +63,7 @@ extern "C" int sage3_fp4_attn(const void* q, const void* k, const void* v, void*
   p.L = static_cast<int>(L);
   p.Lp = static_cast<int>((L + 127) / 128 * 128);
   p.D = static_cast<int>(D);
+  p.f16 = dtype == QDQ_DTYPE_FP16 ? 1 : 0;
   p.q_sb = strides[0]; p.q_sn = strides[1]; p.q_sh = strides[2];
   p.k_sb = strides[3]; p.k_sn = strides[4]; p.k_sh = strides[5];
   p.v_sb = strides[6]; p.v_sn = strides[7]; p.v_sh = strides[8];

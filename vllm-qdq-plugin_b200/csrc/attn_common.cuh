@@ -39,6 +39,7 @@ struct Problem {
   int emulated;     // 1: the reference's emulated-config P handling (P times p_prescale before
                     //    block scaling, l = sum of quantised P); 0: its hardware kernels'
   float p_prescale; // 448*6 (two-level emulated configs) or 1
+  int f16;          // q, k, v, o (and the smoothing intermediates) are fp16, else bf16
 };
 
 // Device buffers of the pre-pass (carved out of the caller's workspace).

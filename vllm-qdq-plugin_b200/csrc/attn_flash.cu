@@ -25,13 +25,13 @@
 //                 S half-row -> registers, half-row block maxima and the row
 //                 max through the partner thread, O_A half-row rescale in TMEM
 //                 when the max grows, exp2, partial row sum, P -> codes +
-//                 block scales in shared memory; epilogue O_A / l -> bf16 NHD
+//                 block scales in shared memory; epilogue O_A / l -> bf16 (or fp16) NHD
 //   warps 8-15    softmax B (the same for tile B)
 //   warp 16       QK MMA issuer: per key tile j, S = delta_s_A + Q_A K_j^T, then
 //                 (once A has read S) S = delta_s_B + Q_B K_j^T
 //   warp 17       TMA producer: K tile [128 keys x 64 B], V^T tile [128 d x 64 B]
 //                 (64-byte swizzle; E4M3: 128 B rows, 128-byte swizzle), their
-//                 scale chunks and the two tiles' delta_s rows (bf16) into a
+//                 scale chunks and the two tiles' delta_s rows (bf16 / fp16) into a
 //                 4-stage ring (3 for E4M3); Q_A, Q_B once
 //   warp 18       PV MMA issuer: O_A += P_A V_j, O_B += P_B V_j as each P tile
 //                 is complete (warp 19 idle)
@@ -41,7 +41,7 @@
 // partial row sums) through shared memory and a 64-thread named barrier.
 // The single S buffer alternates between the two softmax warpgroups, which
 // therefore run out of phase and overlap their MUFU / FMA / ALU work.
-// delta_s on the tensor core: with QK smoothing, S starts as one bf16 MMA
+// delta_s on the tensor core: with QK smoothing, S starts as one bf16 (fp16) MMA
 // (kind::f16, K = 16) of a constant "ones" operand by the stage's delta_s tile,
 // and the block-scaled QK MMAs accumulate onto it.  A_t (128 x 16, K-major, no
 // swizzle) is 1 in column t and 0 elsewhere; B (128 keys x 16, MN-major,
@@ -73,6 +73,8 @@ constexpr int DS_TX = 2 * 2 * 64 * 2;  // bytes the two 64-key x 2-row delta_s b
 constexpr int ONES_TILE = 2048;      // "ones" MMA operand of one query tile: 128 rows x 16 B
 constexpr int ZERO_TILE = 2048;      // zero K-rows 8-15 of both delta_s MMA operands
 constexpr uint32_t IDESC_DS = idesc_bf16(BM, BN, true);
+// the same with fp16 A and B (format code 0 in bits 7-9 and 10-12), for fp16 inputs
+constexpr uint32_t IDESC_DS_F16 = IDESC_DS & ~((7u << 7) | (7u << 10));
 constexpr int THREADS = 640;         // 16 softmax warps; the two MMA issuers, TMA producer and an idle warp
 constexpr int MMA_WARP = 16, TMA_WARP = 17, PV_WARP = 18;
 constexpr int TMEM_COLS = 512;
@@ -139,7 +141,8 @@ struct Params {
   float p_prescale;      // emulated-config P prescale: 448*6 (two-level) or 1 (single-level _s1)
   float p_prescale_lg2;  // log2(p_prescale)
   int vsmooth;           // the V mean was subtracted before quantisation: add it back to O / l
-  const float* vmean;    // [BH, 128] the V means (bf16 values), when vsmooth
+  const float* vmean;    // [BH, 128] the V means (values of the input dtype), when vsmooth
+  int f16;               // inputs, delta_s and the output are fp16, else bf16
 };
 
 // Kernel variants are <Q/K format, P/V format, emulated P handling>:
@@ -591,7 +594,7 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
     tc_fence_before();
     mbar_arrive(&bars->p_full[wg]);
   }
-  // ---------------- epilogue: O / l -> bf16 NHD
+  // ---------------- epilogue: O / l -> bf16 / fp16 NHD
   const float l_row = l_run + pair_exchange(bars, wg, hf, quad, r, l_run, nkv);
   if (ok && nkv > 0) ok = mbar_wait(&bars->o_done[wg], (nkv - 1) & 1, status, 0x1304);
   ok = __all_sync(0xffffffffu, ok);
@@ -626,9 +629,11 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
       for (int q = 0; q < 4; ++q) {
         uint32_t w[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          w[i] = pack_bf16x2(fmaf(__uint_as_float(u[q * 8 + 2 * i]), inv_l, add[q * 8 + 2 * i]),
-                             fmaf(__uint_as_float(u[q * 8 + 2 * i + 1]), inv_l, add[q * 8 + 2 * i + 1]));
+        for (int i = 0; i < 4; ++i) {
+          const float lo = fmaf(__uint_as_float(u[q * 8 + 2 * i]), inv_l, add[q * 8 + 2 * i]);
+          const float hi = fmaf(__uint_as_float(u[q * 8 + 2 * i + 1]), inv_l, add[q * 8 + 2 * i + 1]);
+          w[i] = p.f16 ? pack_f16x2(lo, hi) : pack_bf16x2(lo, hi);
+        }
         dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
@@ -681,15 +686,16 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
   if (p.smoothing) {
     // delta_s MMA operands: every stage's delta_s tile and the zero tile start
     // at zero (the TMA writes only K-rows 0-1 of each atom); ones tile t has
-    // bf16 1.0 in column t of each 16-byte row
+    // 1.0 (the input dtype) in column t of each 16-byte row
     for (int s = 0; s < STAGES; ++s)
       for (int i = threadIdx.x; i < DS_TILE / 16; i += THREADS)
         *reinterpret_cast<uint4*>(smem + Lay::OFF_STAGE + s * Lay::STAGE_BYTES + Lay::ST_DS + 16 * i) =
             make_uint4(0, 0, 0, 0);
     for (int i = threadIdx.x; i < (2 * ONES_TILE + ZERO_TILE) / 16; i += THREADS) {
       const int t = i / (ONES_TILE / 16);  // 0, 1: ones tiles; 2: zero tile
-      *reinterpret_cast<uint4*>(smem + Lay::OFF_ONES + 16 * i) =  // element t of the row = 1.0 (0x3F80)
-          make_uint4(t == 0 ? 0x00003F80u : (t == 1 ? 0x3F800000u : 0u), 0u, 0u, 0u);
+      const uint32_t one = p.f16 ? 0x3C00u : 0x3F80u;  // 1.0 in fp16 / bf16, the delta_s rows' type
+      *reinterpret_cast<uint4*>(smem + Lay::OFF_ONES + 16 * i) =  // element t of the row = 1.0
+          make_uint4(t == 0 ? one : (t == 1 ? one << 16 : 0u), 0u, 0u, 0u);
     }
     fence_proxy_async_smem();  // visible to the TMA unit and the tensor core
   }
@@ -785,7 +791,7 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
             tc_fence_after();
             if (w == 0) cp_sf_d<kNVq>(tmem + T_SFK, ksf0 + su * kStage);
             if (p.smoothing)  // S = delta_s of this tile's query group
-              mma_f16(tmem + T_S, dsa[w], dsb0 + su * kDsStep, IDESC_DS, 0);
+              mma_f16(tmem + T_S, dsa[w], dsb0 + su * kDsStep, p.f16 ? IDESC_DS_F16 : IDESC_DS, 0);
             mma_k128<kQK>(tmem + T_S, qd0 + static_cast<uint64_t>(w) * (Lay::QK_TILE >> 4), kd0 + su * kStage,
                           tmem + T_SFQ + w * 8, tmem + T_SFK, p.smoothing != 0);
             tc_commit(&bars->s_full[w]);
@@ -879,7 +885,7 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   if (int st = code_map(&mq, w.qc, BH * pr.Lp, q8 ? 128 : 64, q8)) return st;
   if (int st = code_map(&mk, w.kc, BH * pr.Lp, q8 ? 128 : 64, q8)) return st;
   if (int st = code_map(&mv, w.vt, BH * HD, p8 ? pr.Lp : pr.Lp / 2, p8)) return st;
-  // delta_s [BH * G, Lp] bf16, boxes of 64 keys x 2 query groups, 128-byte swizzle
+  // delta_s [BH * G, Lp] bf16 / fp16, boxes of 64 keys x 2 query groups, 128-byte swizzle
   if (int st = make_tmap_u16_2d(&mds, w.ds, BH * (pr.Lp / 128), pr.Lp, static_cast<uint64_t>(pr.Lp) * 2, 64, 2, 128))
     return st;
   Params p;
@@ -898,6 +904,7 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   p.p_prescale_lg2 = static_cast<float>(std::log2(static_cast<double>(pr.p_prescale)));
   p.vsmooth = pr.vsmooth;
   p.vmean = w.vmean;
+  p.f16 = pr.f16;
   dim3 grid(static_cast<unsigned>((p.T + 1) / 2), static_cast<unsigned>(BH));
 #define QDQ_FLASH(QK, PV, EMU)                                                             \
   if (pr.qk_fmt == QK && pr.pv_fmt == PV && (pr.emulated != 0) == EMU)                     \

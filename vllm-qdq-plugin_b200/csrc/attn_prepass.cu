@@ -6,10 +6,12 @@
 //
 // Reference semantics (mxfp4_hw branch, sage3/api.py:161-206):
 //   qk_smoothing (sage3/transforms.py:47-95), applied before padding:
-//     k_c  = k - mean_L(k)                      (bf16 ops)
+//     k_c  = k - mean_L(k)                      (ops in the input dtype)
 //     q_m  = mean over each 128-row group of q, the last group zero-padded
 //     q_s  = q - q_m[group]
-//     delta_s[g, n] = (q_m[g] . k_c[n]) rounded to bf16 (bf16 matmul)
+//     delta_s[g, n] = (q_m[g] . k_c[n]) rounded to the input dtype (its matmul)
+//   The input dtype is bf16 or fp16 (kernels templated on kF16); every
+//   rounding above is to that dtype, as the reference's torch ops round.
 //   quantize_to_mxfp4 (sage3/mxfp4_hw_kernel.py:73-116) of q_s and k_c along
 //   D and of V along the sequence, per 32-group:
 //     e = clamp(ceil(log2(max(amax, 6*2^-126) / 6)), -127, 127), byte e+127
@@ -27,10 +29,10 @@
 // alone.  The flash kernel stores only the first D output channels.
 //
 // Outputs (workspace), with Lp = L rounded up to 128, BH = B*H, G = Lp/128:
-//   ksum   fp32 [BH, D]           per-channel sums of k (mean = bf16(ksum / L))
+//   ksum   fp32 [BH, D]           per-channel sums of k (mean = dtype(ksum / L))
 //   (kernels: colsum_kernel for the K (and V) sums; the Q pass; the K pass,
 //   which also writes delta_s; the V pass)
-//   qmean  bf16 [BH, G, D]        Q group means
+//   qmean  bf16/fp16 [BH, G, D]   Q group means (input dtype)
 //   qc, kc uint8 [BH*Lp, D/2]     E2M1 codes (element 2j low nibble), or [BH*Lp, D] E4M3
 //   qsf, ksf                      block scales, 1024 bytes per 128 rows: two 512-byte tcgen05
 //                                 scale chunks (NVFP4: 8 E4M3 per row; MXFP4: 4 E8M0 in the first;
@@ -38,7 +40,7 @@
 //   vt     uint8 [BH*D, Lp/2]     V transposed: row (bh, d), keys packed along the row
 //                                 ([BH*D, Lp] for E4M3)
 //   vsf                           1024 bytes per (bh, key tile): 128 d-rows x (4 E8M0 | 8 E4M3)
-//   ds     bf16 [BH, G, Lp]       delta_s (the reference's dtype)
+//   ds     bf16/fp16 [BH, G, Lp]  delta_s (the reference's dtype: the input's)
 #include "attn_common.cuh"
 
 namespace qdqb200 {
@@ -49,6 +51,22 @@ namespace {
 __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
+// The 16-bit input type: bf16 (kF16 = false) or fp16.  lo / hi read the two
+// halves of a 32-bit word, round rounds to the type (nearest even), pack
+// rounds two floats into one word, bits / val convert one element.
+template <bool kF16>
+struct In16 {
+  __device__ static float lo(uint32_t w) { return kF16 ? f16lo(w) : bf16lo(w); }
+  __device__ static float hi(uint32_t w) { return kF16 ? f16hi(w) : bf16hi(w); }
+  __device__ static float round(float x) { return kF16 ? __half2float(__float2half_rn(x)) : bf16_round(x); }
+  __device__ static uint32_t pack(float a, float b) { return kF16 ? pack_f16x2(a, b) : pack_bf16x2(a, b); }
+  __device__ static uint16_t bits(float x) {
+    return kF16 ? __half_as_ushort(__float2half_rn(x)) : __bfloat16_as_ushort(__float2bfloat16_rn(x));
+  }
+  __device__ static float val(uint16_t b) {
+    return kF16 ? __half2float(__ushort_as_half(b)) : __uint_as_float(static_cast<uint32_t>(b) << 16);
+  }
+};
 
 // Exact ceil(log2(r)) for r > 0 (r finite).
 __device__ __forceinline__ int ceil_log2(float r) {
@@ -112,10 +130,11 @@ __device__ __forceinline__ int64_t nhd_row(int b, int n, int h, int64_t sb, int6
   return b * sb + n * sn + h * sh;
 }
 
-// E8M0 group quantisers for inputs of bf16 precision (at most 8 significant
-// bits: q_s, k_c and V are bf16 values).  x * 2^-e is then exact, and its
-// distance to a midpoint between E2M1 values (0.25, 0.75, ... 5, at most 3
-// significant bits) is zero or at least 2^-8 relative.  Scaling by
+// E8M0 group quantisers for inputs of bf16 or fp16 precision (at most 8 or 11
+// significant bits: q_s, k_c and V are values of the input dtype).  x * 2^-e
+// is then exact, and its distance to a midpoint between E2M1 values (0.25,
+// 0.75, ... 5, at most 3 significant bits) is zero or at least 2^-11
+// relative (2^-8 for bf16).  Scaling by
 // (1 + 2^-12), also exact, lifts the midpoints themselves just above and moves
 // nothing else across one, so the hardware's round-to-nearest-even cvt yields
 // the reference's round-half-away codes (mxfp4_hw_kernel.py:43-61).  The
@@ -142,22 +161,24 @@ __device__ __forceinline__ uint32_t mx_quant32_bf(const float* v, uint8_t* out) 
 
 // E4M3-scaled blocks (the reference's nvfp4 / mxfp4_s1_e4m3 QuantConfigs,
 // quantize.py:21-81 with round_to_e4m3, on the hardware E2M1 grid): scale
-// s = e4m3(max(bf16(amax / 6), 1e-8)), codes of the quotient x / s rounded
-// half away from zero.  x has bf16 precision (8 significant bits) and s at
-// most 4, so x / s is either exactly an E2M1 midpoint (a value with at most 7
-// significant bits times s) or at least 2^-9 relative away from every
-// midpoint.  x * (RN(1 / s) * (1 + 2^-12)) is within 2^-11 relative of
-// x / s * (1 + 2^-12): above a midpoint that x / s equals, on the same side
-// of every other, so the round-to-nearest-even cvt gives the round-half-away
-// code (checked exhaustively on the CPU for every bf16 x and E4M3 s).
+// s = e4m3(max(dtype(amax / 6), 1e-8)), codes of the quotient x / s rounded
+// half away from zero.  x has bf16 or fp16 precision (8 or 11 significant
+// bits) and s at most 4, so x / s is either exactly an E2M1 midpoint (a value
+// with at most 7 significant bits times s) or at least 2^-11 relative away
+// from every midpoint (x and midpoint * s then differ by at least one unit in
+// x's last place).  x * (RN(1 / s) * (1 + 2^-12)) is within 3 * 2^-24
+// relative of x / s * (1 + 2^-12): above a midpoint that x / s equals, on the
+// same side of every other, so the round-to-nearest-even cvt gives the
+// round-half-away code (checked exhaustively on the CPU for every bf16 x and
+// E4M3 s, and for every fp16 x and E4M3 s).
 // fma(x, inv, +0) turns an exact -0 into +0 (the reference's sign is x < 0).
 // KB elements, KB / 2 code bytes; returns the scale byte (0: the block is 0).
-template <int KB>
+template <int KB, bool kF16>
 __device__ __forceinline__ uint32_t nv_quant_fast(const float* v, uint8_t* out) {
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < KB; ++i) amax = fmaxf(amax, fabsf(v[i]));
-  const float sc = fmaxf(bf16_round(amax / 6.0f), 1e-8f);
+  const float sc = fmaxf(In16<kF16>::round(amax / 6.0f), 1e-8f);
   const uint32_t sbyte = e4m3_byte(sc);
   const float s = round_e4m3(sc);
   const float inv = s > 0.f ? (1.0f / s) * (1.0f + 1.0f / 4096.0f) : 0.f;
@@ -176,16 +197,16 @@ __device__ __forceinline__ uint32_t nv_quant_fast(const float* v, uint8_t* out) 
 
 // One group of a row in format kFmt: codes to `crow`, the scale byte(s) to the
 // tcgen05 scale chunk(s) at sft (row r, group g of the tile).
-template <int kFmt>
+template <int kFmt, bool kF16>
 __device__ __forceinline__ void quant_group(const float* v, uint8_t* crow, uint8_t* sft, int r, int g) {
   const int slot = (r % 32) * 16 + (r / 32) * 4;
   if (kFmt == F_MX8) {
     sft[slot + g] = static_cast<uint8_t>(mx8_quant32(v, crow));
   } else if (kFmt == F_NV4) {
-    sft[(g / 4) * 512 + slot + (g % 4)] = static_cast<uint8_t>(nv_quant_fast<16>(v, crow));
+    sft[(g / 4) * 512 + slot + (g % 4)] = static_cast<uint8_t>(nv_quant_fast<16, kF16>(v, crow));
   } else if (kFmt == F_NV4B32) {
     *reinterpret_cast<uint16_t*>(sft + (g / 2) * 512 + slot + 2 * (g % 2)) =
-        static_cast<uint16_t>(nv_quant_fast<32>(v, crow) * 0x101u);
+        static_cast<uint16_t>(nv_quant_fast<32, kF16>(v, crow) * 0x101u);
   } else {
     sft[slot + g] = static_cast<uint8_t>(mx_quant32_bf(v, crow));
   }
@@ -197,6 +218,7 @@ __device__ __forceinline__ void quant_group(const float* v, uint8_t* crow, uint8
 // channels of 16-byte chunk t % 16 over rows t / 16 + 16 i of the block's 256
 // rows (16 independent loads in flight), then the 16 partial sums per channel
 // meet in shared memory.
+template <bool kF16>
 __global__ void __launch_bounds__(256) colsum_kernel(const __nv_bfloat16* __restrict__ x, int H, int L, int D,
                                                      int64_t sb, int64_t sn, int64_t sh, float* __restrict__ sum) {
   __shared__ __align__(16) float part[16][128];
@@ -212,8 +234,8 @@ __global__ void __launch_bounds__(256) colsum_kernel(const __nv_bfloat16* __rest
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        acc[2 * j] += bf16lo(w[j]);
-        acc[2 * j + 1] += bf16hi(w[j]);
+        acc[2 * j] += In16<kF16>::lo(w[j]);
+        acc[2 * j + 1] += In16<kF16>::hi(w[j]);
       }
     }
   }
@@ -242,6 +264,7 @@ constexpr int QK_TILE_BYTES = 128 * DS_LD * 2;
 constexpr int QK_SMEM_Q = QK_TILE_BYTES + 16 * 128 * 4;   // tile + column partial sums
 constexpr int QK_SMEM_K = QK_TILE_BYTES + 64 * DS_LD * 2;  // tile + 64 query-group means
 
+template <bool kF16>
 __device__ void ds_tile(const __nv_bfloat16* kcs, __nv_bfloat16* qms, const __nv_bfloat16* __restrict__ qmean,
                         __nv_bfloat16* __restrict__ ds, int bh, int G, int Lp, int n0);
 
@@ -267,7 +290,7 @@ __device__ __forceinline__ void qmean_chunk_async(__nv_bfloat16* qms, const __nv
   cp_async_commit();
 }
 
-template <bool kIsQ, int kFmt>
+template <bool kIsQ, int kFmt, bool kF16>
 __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __restrict__ x, int H, int L, int Lp, int D,
                                                        int64_t sb, int64_t sn, int64_t sh,
                                                        const float* __restrict__ ksum, __nv_bfloat16* __restrict__ qmean,
@@ -293,8 +316,8 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        acc[2 * j] += bf16lo(w[j]);
-        acc[2 * j + 1] += bf16hi(w[j]);
+        acc[2 * j] += In16<kF16>::lo(w[j]);
+        acc[2 * j + 1] += In16<kF16>::hi(w[j]);
       }
     }
   }
@@ -314,16 +337,17 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
         float sum = 0.f;
 #pragma unroll
         for (int r = 0; r < 16; ++r) sum += part[r * 128 + d];
-        m = bf16_round(sum / 128.0f);
-        qmean[(static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 128 + d] = __float2bfloat16_rn(m);
+        m = In16<kF16>::round(sum / 128.0f);
+        reinterpret_cast<uint16_t*>(qmean)[(static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 128 + d] =
+            In16<kF16>::bits(m);
       } else {
-        m = bf16_round(ksum[bh * 128 + d] / static_cast<float>(L));
+        m = In16<kF16>::round(ksum[bh * 128 + d] / static_cast<float>(L));
       }
     }
     mean[d] = m;
   }
   __syncthreads();
-  if (smoothing) {  // centre in place: bf16(x - mean) on real rows, padding rows stay 0
+  if (smoothing) {  // centre in place: dtype(x - mean) on real rows, padding rows stay 0
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int r = r0 + 16 * i;
@@ -334,7 +358,8 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
         uint32_t o[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          o[j] = pack_bf16x2(bf16lo(w[j]) - mean[c * 8 + 2 * j], bf16hi(w[j]) - mean[c * 8 + 2 * j + 1]);
+          o[j] = In16<kF16>::pack(In16<kF16>::lo(w[j]) - mean[c * 8 + 2 * j],
+                                  In16<kF16>::hi(w[j]) - mean[c * 8 + 2 * j + 1]);
         *pu = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
@@ -355,17 +380,18 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        v[q * 8 + 2 * j] = bf16lo(w[j]);
-        v[q * 8 + 2 * j + 1] = bf16hi(w[j]);
+        v[q * 8 + 2 * j] = In16<kF16>::lo(w[j]);
+        v[q * 8 + 2 * j + 1] = In16<kF16>::hi(w[j]);
       }
     }
     uint8_t* crow = kFmt == F_MX8 ? codes + (static_cast<int64_t>(bh) * Lp + n) * 128 + g * 32
                                   : codes + (static_cast<int64_t>(bh) * Lp + n) * 64 + g * (kGs / 2);
-    quant_group<kFmt>(v, crow, sft, r, g);
+    quant_group<kFmt, kF16>(v, crow, sft, r, g);
   }
   if (!kIsQ && smoothing) {
     __syncthreads();  // (the tile was only read above; ds_tile reuses the rest of the buffer)
-    ds_tile(tile, reinterpret_cast<__nv_bfloat16*>(qk_smem + QK_TILE_BYTES), qmean, ds, bh, Lp / 128, Lp, t0);
+    ds_tile<kF16>(tile, reinterpret_cast<__nv_bfloat16*>(qk_smem + QK_TILE_BYTES), qmean, ds, bh, Lp / 128, Lp,
+                  t0);
   }
 }
 
@@ -380,13 +406,13 @@ __host__ __device__ constexpr int v_code_ld() { return (kFmt == F_MX8 ? 128 : 64
 template <int kFmt>
 __host__ __device__ constexpr int v_smem_bytes() { return V_TILE_BYTES + 128 * v_code_ld<kFmt>(); }
 
-template <int kFmt>
+template <int kFmt, bool kF16>
 __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __restrict__ v, int H, int L, int Lp, int D,
                                                       int64_t sb, int64_t sn, int64_t sh,
                                                       uint8_t* __restrict__ vt, uint8_t* __restrict__ vsf,
                                                       const float* __restrict__ vsum, float* __restrict__ vmean) {
   extern __shared__ __align__(16) uint8_t v_smem[];
-  auto tile = reinterpret_cast<__nv_bfloat16 (*)[128 + 8]>(v_smem);
+  auto tile = reinterpret_cast<uint16_t (*)[128 + 8]>(v_smem);
   uint8_t* cst = v_smem + V_TILE_BYTES;  // [128][v_code_ld] staged code rows
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
   const int t0 = blockIdx.y * 128;
@@ -408,14 +434,14 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
   __syncthreads();
   const int d = threadIdx.x;
   constexpr bool kF8 = kFmt == F_MX8;
-  // V smoothing (transforms.py v_smoothing): quantise bf16(v - mean_L(v)); the
+  // V smoothing (transforms.py v_smoothing): quantise dtype(v - mean_L(v)); the
   // flash epilogue adds the mean back.  Padding rows stay zero.
+  using E = In16<kF16>;
   float vm = 0.f;
   if (vsum != nullptr) {
-    vm = bf16_round(vsum[bh * 128 + d] / static_cast<float>(L));
+    vm = E::round(vsum[bh * 128 + d] / static_cast<float>(L));
     if (blockIdx.y == 0) vmean[bh * 128 + d] = vm;
-    for (int r = 0; r < 128 && t0 + r < L; ++r)
-      tile[r][d] = __float2bfloat16_rn(__bfloat162float(tile[r][d]) - vm);
+    for (int r = 0; r < 128 && t0 + r < L; ++r) tile[r][d] = E::bits(E::val(tile[r][d]) - vm);
   }
   uint8_t* row = cst + d * v_code_ld<kFmt>();
   uint8_t* sft = vsf + (static_cast<int64_t>(bh) * (Lp / 128) + blockIdx.y) * 1024 + (d % 32) * 16 + (d / 32) * 4;
@@ -425,8 +451,8 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
     for (int g = 0; g < 4; ++g) {
       float x[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(tile[g * 32 + i][d]);
-      sfw[g / 2] |= (nv_quant_fast<32>(x, row + g * 16) * 0x101u) << (16 * (g % 2));
+      for (int i = 0; i < 32; ++i) x[i] = E::val(tile[g * 32 + i][d]);
+      sfw[g / 2] |= (nv_quant_fast<32, kF16>(x, row + g * 16) * 0x101u) << (16 * (g % 2));
     }
     *reinterpret_cast<uint32_t*>(sft) = sfw[0];
     *reinterpret_cast<uint32_t*>(sft + 512) = sfw[1];
@@ -436,8 +462,8 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
     for (int g = 0; g < 8; ++g) {
       float x[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) x[i] = __bfloat162float(tile[g * 16 + i][d]);
-      sfw[g / 4] |= nv_quant_fast<16>(x, row + g * 8) << (8 * (g % 4));
+      for (int i = 0; i < 16; ++i) x[i] = E::val(tile[g * 16 + i][d]);
+      sfw[g / 4] |= nv_quant_fast<16, kF16>(x, row + g * 8) << (8 * (g % 4));
     }
     *reinterpret_cast<uint32_t*>(sft) = sfw[0];
     *reinterpret_cast<uint32_t*>(sft + 512) = sfw[1];
@@ -447,7 +473,7 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
     for (int g = 0; g < 4; ++g) {
       float x[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(tile[g * 32 + i][d]);
+      for (int i = 0; i < 32; ++i) x[i] = E::val(tile[g * 32 + i][d]);
       sfw |= (kF8 ? mx8_quant32(x, row + g * 32) : mx_quant32_bf(x, row + g * 16)) << (8 * g);
     }
     *reinterpret_cast<uint32_t*>(sft) = sfw;
@@ -463,9 +489,10 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
 }
 
 // ---------------------------------------------------------------- delta_s
-// ds[bh, g, n] = bf16( sum_d qmean[bh, g, d] * kc[bh, n, d] ), kc = bf16(k - mean),
-// with bf16 tensor-core MMAs (mma.sync m16n8k16, fp32 accumulation), stored
-// as bf16 rows the flash kernel loads by TMA as an MMA operand.
+// ds[bh, g, n] = dtype( sum_d qmean[bh, g, d] * kc[bh, n, d] ), kc = dtype(k - mean),
+// with bf16 or fp16 tensor-core MMAs (mma.sync m16n8k16, fp32 accumulation),
+// stored as rows of the input dtype that the flash kernel loads by TMA as an
+// MMA operand.
 // Run by the K pass's 256 threads (8 warps) on its centred key tile kcs
 // ([128][DS_LD] bf16 in shared memory): walks the G query groups 64 at a
 // time through qms ([64][DS_LD]); each warp owns a 32 (g) x 32 (n) block of
@@ -476,14 +503,23 @@ __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(sm100::smem_u32(p)));
 }
-__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+template <bool kF16>
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if (kF16)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+template <bool kF16>
 __device__ void ds_tile(const __nv_bfloat16* kcs, __nv_bfloat16* qms, const __nv_bfloat16* __restrict__ qmean,
                         __nv_bfloat16* __restrict__ ds, int bh, int G, int Lp, int n0) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -513,8 +549,8 @@ __device__ void ds_tile(const __nv_bfloat16* kcs, __nv_bfloat16* qms, const __nv
         ldsm_x4(bb, kcs + nrow * DS_LD + col);
 #pragma unroll
         for (int mi = 0; mi < 2; ++mi) {
-          mma_bf16_16816(acc[mi][nj * 2 + 0], a[mi], bb[0], bb[1]);
-          mma_bf16_16816(acc[mi][nj * 2 + 1], a[mi], bb[2], bb[3]);
+          mma_16816<kF16>(acc[mi][nj * 2 + 0], a[mi], bb[0], bb[1]);
+          mma_16816<kF16>(acc[mi][nj * 2 + 1], a[mi], bb[2], bb[3]);
         }
       }
     }
@@ -528,8 +564,8 @@ __device__ void ds_tile(const __nv_bfloat16* kcs, __nv_bfloat16* qms, const __nv
           const int g = g0 + wm * 32 + mi * 16 + (lane >> 2) + hh * 8;
           const int n = n0 + wn * 32 + ni * 8 + (lane & 3) * 2;
           if (g < G) {
-            *reinterpret_cast<__nv_bfloat162*>(ds + (static_cast<int64_t>(bh) * G + g) * Lp + n) =
-                __floats2bfloat162_rn(acc[mi][ni][hh * 2], acc[mi][ni][hh * 2 + 1]);
+            *reinterpret_cast<uint32_t*>(ds + (static_cast<int64_t>(bh) * G + g) * Lp + n) =
+                In16<kF16>::pack(acc[mi][ni][hh * 2], acc[mi][ni][hh * 2 + 1]);
           }
         }
   }
@@ -539,74 +575,81 @@ __device__ void ds_tile(const __nv_bfloat16* kcs, __nv_bfloat16* qms, const __nv
 
 // The Q and K passes of format kFmt; their dynamic shared memory (above the
 // 48 KB default) is enabled once per device for this instantiation.
-template <int kFmt>
+template <int kFmt, bool kF16>
 int launch_qk(const Problem& p, const Workspace& w, cudaStream_t s) {
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr[dev]) {
-    if (cudaFuncSetAttribute(qk_quant_kernel<true, kFmt>, cudaFuncAttributeMaxDynamicSharedMemorySize, QK_SMEM_Q) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(qk_quant_kernel<false, kFmt>, cudaFuncAttributeMaxDynamicSharedMemorySize, QK_SMEM_K) !=
-            cudaSuccess)
+    if (cudaFuncSetAttribute(qk_quant_kernel<true, kFmt, kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             QK_SMEM_Q) != cudaSuccess ||
+        cudaFuncSetAttribute(qk_quant_kernel<false, kFmt, kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             QK_SMEM_K) != cudaSuccess)
       return fail(QDQ_ERR_CUDA, "sage3 prepass: smem attribute");
     attr[dev] = true;
   }
   const int BH = p.B * p.H, T = p.Lp / 128;
-  qk_quant_kernel<true, kFmt><<<dim3(BH, T), 256, QK_SMEM_Q, s>>>(p.q, p.H, p.L, p.Lp, p.D, p.q_sb, p.q_sn, p.q_sh, w.ksum,
-                                                                 w.qmean, w.qc, w.qsf, p.smoothing, w.ds);
-  qk_quant_kernel<false, kFmt><<<dim3(BH, T), 256, QK_SMEM_K, s>>>(p.k, p.H, p.L, p.Lp, p.D, p.k_sb, p.k_sn, p.k_sh,
-                                                                  w.ksum, w.qmean, w.kc, w.ksf, p.smoothing, w.ds);
+  qk_quant_kernel<true, kFmt, kF16><<<dim3(BH, T), 256, QK_SMEM_Q, s>>>(
+      p.q, p.H, p.L, p.Lp, p.D, p.q_sb, p.q_sn, p.q_sh, w.ksum, w.qmean, w.qc, w.qsf, p.smoothing, w.ds);
+  qk_quant_kernel<false, kFmt, kF16><<<dim3(BH, T), 256, QK_SMEM_K, s>>>(
+      p.k, p.H, p.L, p.Lp, p.D, p.k_sb, p.k_sn, p.k_sh, w.ksum, w.qmean, w.kc, w.ksf, p.smoothing, w.ds);
   return QDQ_OK;
 }
 
 // The V pass of format kFmt (dynamic shared memory above the 48 KB default).
-template <int kFmt>
+template <int kFmt, bool kF16>
 int launch_v(const Problem& p, const Workspace& w, const float* vs, cudaStream_t s) {
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr[dev]) {
-    if (cudaFuncSetAttribute(v_quant_kernel<kFmt>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(v_quant_kernel<kFmt, kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              v_smem_bytes<kFmt>()) != cudaSuccess)
       return fail(QDQ_ERR_CUDA, "sage3 prepass: smem attribute");
     attr[dev] = true;
   }
-  v_quant_kernel<kFmt><<<dim3(p.B * p.H, p.Lp / 128), 128, v_smem_bytes<kFmt>(), s>>>(
+  v_quant_kernel<kFmt, kF16><<<dim3(p.B * p.H, p.Lp / 128), 128, v_smem_bytes<kFmt>(), s>>>(
       p.v, p.H, p.L, p.Lp, p.D, p.v_sb, p.v_sn, p.v_sh, w.vt, w.vsf, vs, w.vmean);
   return QDQ_OK;
 }
 
-int launch_prepass(const Problem& p, const Workspace& w, cudaStream_t s) {
+template <bool kF16>
+int launch_prepass_t(const Problem& p, const Workspace& w, cudaStream_t s) {
   const int BH = p.B * p.H;
   if (cudaMemsetAsync(w.ksum, 0, sizeof(float) * BH * 128, s) != cudaSuccess)
     return fail(QDQ_ERR_CUDA, "sage3 prepass: memset failed");
   if (p.smoothing)
-    colsum_kernel<<<dim3(BH, (p.L + 255) / 256), 256, 0, s>>>(p.k, p.H, p.L, p.D, p.k_sb, p.k_sn, p.k_sh, w.ksum);
+    colsum_kernel<kF16><<<dim3(BH, (p.L + 255) / 256), 256, 0, s>>>(p.k, p.H, p.L, p.D, p.k_sb, p.k_sn, p.k_sh,
+                                                                    w.ksum);
   if (p.vsmooth) {
     if (cudaMemsetAsync(w.vsum, 0, sizeof(float) * BH * 128, s) != cudaSuccess)
       return fail(QDQ_ERR_CUDA, "sage3 prepass: memset failed");
-    colsum_kernel<<<dim3(BH, (p.L + 255) / 256), 256, 0, s>>>(p.v, p.H, p.L, p.D, p.v_sb, p.v_sn, p.v_sh, w.vsum);
+    colsum_kernel<kF16><<<dim3(BH, (p.L + 255) / 256), 256, 0, s>>>(p.v, p.H, p.L, p.D, p.v_sb, p.v_sn, p.v_sh,
+                                                                    w.vsum);
   }
   // Q (group means first: the K pass's delta_s reads them), then K, in the Q/K format
   int st = QDQ_OK;
   switch (p.qk_fmt) {
-    case F_MX8: st = launch_qk<F_MX8>(p, w, s); break;
-    case F_NV4: st = launch_qk<F_NV4>(p, w, s); break;
-    case F_NV4B32: st = launch_qk<F_NV4B32>(p, w, s); break;
-    default: st = launch_qk<F_MX4>(p, w, s); break;
+    case F_MX8: st = launch_qk<F_MX8, kF16>(p, w, s); break;
+    case F_NV4: st = launch_qk<F_NV4, kF16>(p, w, s); break;
+    case F_NV4B32: st = launch_qk<F_NV4B32, kF16>(p, w, s); break;
+    default: st = launch_qk<F_MX4, kF16>(p, w, s); break;
   }
   if (st != QDQ_OK) return st;
   // V^T in the P/V format
   const float* vs = p.vsmooth ? w.vsum : nullptr;
   switch (p.pv_fmt) {
-    case F_MX8: st = launch_v<F_MX8>(p, w, vs, s); break;
-    case F_NV4: st = launch_v<F_NV4>(p, w, vs, s); break;
-    case F_NV4B32: st = launch_v<F_NV4B32>(p, w, vs, s); break;
-    default: st = launch_v<F_MX4>(p, w, vs, s); break;
+    case F_MX8: st = launch_v<F_MX8, kF16>(p, w, vs, s); break;
+    case F_NV4: st = launch_v<F_NV4, kF16>(p, w, vs, s); break;
+    case F_NV4B32: st = launch_v<F_NV4B32, kF16>(p, w, vs, s); break;
+    default: st = launch_v<F_MX4, kF16>(p, w, vs, s); break;
   }
   if (st != QDQ_OK) return st;
   return check_launch("sage3 prepass");
+}
+
+int launch_prepass(const Problem& p, const Workspace& w, cudaStream_t s) {
+  return p.f16 ? launch_prepass_t<true>(p, w, s) : launch_prepass_t<false>(p, w, s);
 }
 
 }  // namespace attn

@@ -134,8 +134,8 @@ def _sage3_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layout_nhd: boo
     import ctypes
     arr = (ctypes.c_int64 * 12)(*strides)
     _native.call("sage3_fp4_attn", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b_, l_,
-                 h_, d_, arr, float(sm_scale), quant_format, acc_mode, int(causal), int(smoothing), 0,
-                 ws.data_ptr(), ws.numel(), _native.stream_ptr(q.device))
+                 h_, d_, arr, float(sm_scale), quant_format, acc_mode, int(causal), int(smoothing),
+                 1 if q.dtype == torch.float16 else 0, ws.data_ptr(), ws.numel(), _native.stream_ptr(q.device))
     return out
 
 
@@ -146,9 +146,10 @@ def _(q, k, v, layout_nhd, sm_scale, quant_format, acc_mode, causal, smoothing):
 
 # Head dims and input dtypes the FP4 kernels take (dims below 128 are
 # zero-extended to 128 in the pre-pass; the reference's hardware kernels take
-# 64 and 128, its emulated kernel any dim).
+# 64 and 128, its emulated kernel any dim).  fp16 inputs are smoothed with
+# fp16 roundings and give an fp16 output, as the reference's torch ops do.
 SUPPORTED_HEAD_DIMS = (32, 64, 96, 128)
-SUPPORTED_DTYPES = (torch.bfloat16,)
+SUPPORTED_DTYPES = (torch.bfloat16, torch.float16)
 
 
 def unsupported_reason(q: torch.Tensor) -> Optional[str]:
