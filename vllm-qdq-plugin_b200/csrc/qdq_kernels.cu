@@ -438,6 +438,28 @@ __device__ __forceinline__ uint32_t e4m3x2_roundtrip(float a, float b, uint32_t&
       : "f"(a), "f"(b));
   return out;
 }
+// The same two steps on an f16x2 pair of quotients: magnitudes in
+// [7, 8) * 2^-9 (fp16 0x2300 .. 0x23FF) lose their low mantissa bits, which
+// leaves 7 * 2^-9 with the sign; then E4M3 with the exact fp16x2 decode.  The
+// quotients of the fast path fit fp16 exactly: |x / scale| < 2^9, at most 11
+// significant bits, and those below 2^-14 (fp16 subnormals, rounded) are far
+// below 2^-10, where every E4M3 code is zero.
+__device__ __forceinline__ uint32_t mx8_pair_f16(uint32_t h, uint32_t& dec) {
+  uint32_t eq, out;
+  asm("{\n\t.reg .b32 m;\n\t"
+      "and.b32 m, %1, 0x7F007F00;\n\t"
+      "set.eq.u32.f16x2 %0, m, %2;\n\t}"
+      : "=r"(eq)
+      : "r"(h), "r"(0x23002300u));
+  h &= ~(eq & 0x00FF00FFu);
+  asm("{\n\t.reg .b16 t;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f16x2 t, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, t;\n\t"
+      "cvt.u32.u16 %0, t;\n\t}"
+      : "=r"(out), "=r"(dec)
+      : "r"(h));
+  return out;
+}
 // x / scale for a pair.  torch.sign makes a zero quotient +0 (mxfp8.py:46,
 // :70): with fma(x, inv, zero), zero = +0.0 a kernel argument, an exact -0
 // becomes +0.  That covers every zero quotient while no nonzero input can
@@ -497,8 +519,9 @@ mxfp8_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         float2 t = mx8_scaled(F::lo(w[j]), F::hi(w[j]), inv, zero, fast);
-        uint32_t h;
-        const uint32_t pair = e4m3x2_roundtrip(mx8_sub_clamp(t.x), mx8_sub_clamp(t.y), h);
+        uint32_t h, pair;
+        if (fast) pair = mx8_pair_f16(pack_f16x2(t.x, t.y), h);
+        else pair = e4m3x2_roundtrip(mx8_sub_clamp(t.x), mx8_sub_clamp(t.y), h);
         cw[j >> 1] |= pair << (16 * (j & 1));
         const float2 d = mul_f32x2(make_float2(f16lo(h), f16hi(h)), make_float2(sc, sc));
         o[j] = F::pack(d.x, d.y);
