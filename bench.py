@@ -1153,17 +1153,22 @@ def moe_marlin_reference(ctx: Ctx, a, codes, scales, sidd, eidd, ntpd, twd, bs, 
                                   use_atomic_add=False, use_fp32_reduce=True, is_zp_float=False)
 
     run(0, None)
+    torch.cuda.synchronize(ctx.dev)
     routed = sidd[: int(ntpd.item())]
     routed = routed[routed < m * top_k].long()
+    o, r = ours_out[routed].float(), out[routed].float()
     same = bool(torch.equal(out[routed].view(torch.int16), ours_out[routed].view(torch.int16)))
-    rel = float((ours_out[routed].float() - out[routed].float()).norm() / out[routed].float().norm())
+    fin = torch.isfinite(o) & torch.isfinite(r)
+    rel = float((o[fin] - r[fin]).norm() / r[fin].norm())
+    nonfinite = {"ours": int((~torch.isfinite(o)).sum()), "reference": int((~torch.isfinite(r)).sum())}
     for i in range(2):
         run(i, None)
     ms, _ = timed(ctx, run, steps, clocks=False)
     return {"impl": "mxfp4_qdq (this build's kernel, bit-exact with the reference's) + vLLM 0.22 "
                     "moe_wna16_marlin_gemm on vLLM-prepared experts, same routing, same GPU, CUDA graph",
             "ms_per_step": round(ms, 5), "speedup_of_ours": round(ms / ours_ms, 2),
-            "bit_identical_to_ours": same, "rel_l2_ours_vs_reference": round(rel, 6)}
+            "bit_identical_to_ours": same, "rel_l2_ours_vs_reference": round(rel, 6),
+            "nonfinite_routed_values": nonfinite}
 
 
 def moe_record(ctx: Ctx, sub: bool = False) -> dict:
