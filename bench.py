@@ -863,8 +863,12 @@ def gemm_record(ctx: Ctx, m: int, sub: bool = False, marlin: bool = True, nv: bo
     wsp = torch.empty((ws_bytes,), dtype=torch.uint8, device=ctx.dev)
     out = torch.empty((ml, n), dtype=torch.bfloat16, device=ctx.dev)
     # MXFP4: one fused launch for M <= 64, else codes (+ scale tiling when K % 256 != 0) and the GEMM;
-    # NVFP4: global amax, codes, scale tiling, GEMM
-    per_call = 4 if nv else (1 if ml <= 64 else (2 if k % 256 == 0 else 3))
+    # NVFP4: one fused launch for M <= 16 (global amax inside), amax + fused launch for M <= 64,
+    # else global amax, codes, scale tiling, GEMM
+    if nv:
+        per_call = 1 if ml <= 16 else (2 if ml <= 64 else 4)
+    else:
+        per_call = 1 if ml <= 64 else (2 if k % 256 == 0 else 3)
 
     def step(i, sp):
         wi = ws_list[i % n_w]
@@ -1253,9 +1257,9 @@ def linear_roofline(m: int, n: int, k: int, ms_step: float, flop: float, peak_tf
                     kind: str = "mxfp4_linear") -> dict:
     """The bound of one fused linear: the FP4 tensor peak or HBM, whichever
     takes longer for its algorithmic work.  Bytes = 2MK (bf16 A) + NK/2 (W
-    codes) + NK/32 (W scales) + 2MN (bf16 C); the decode shapes (M <= 256)
-    are HBM-bound, config 3's M = 4096 tensor-bound."""
-    nbytes = 2 * m * k + n * k // 2 + n * k // 32 + 2 * m * n
+    codes) + NK/32 (W scales; NK/16 for NVFP4) + 2MN (bf16 C); the decode
+    shapes (M <= 256) are HBM-bound, config 3's M = 4096 tensor-bound."""
+    nbytes = 2 * m * k + n * k // 2 + n * k // (16 if kind.startswith("nvfp4") else 32) + 2 * m * n
     hbm, hbm_src = measured_peak_hbm()
     traffic = ncu_traffic(kind if (m, n) == (4096, 14336) else f"{kind}_{m}") if n == 14336 else None
     if nbytes / (hbm * 1e9) > flop / (peak_tf * 1e12):
@@ -1292,6 +1296,7 @@ def run_ours(args) -> None:
                 subs["config3_linear_m4096"] = gemm_record(ctx, 4096, sub=True)
                 subs["config3_linear_m16"] = gemm_record(ctx, 16, sub=True)
                 subs["config3_nvfp4_linear_m4096"] = gemm_record(ctx, 4096, sub=True, nv=True)
+                subs["config3_nvfp4_linear_m16"] = gemm_record(ctx, 16, sub=True, nv=True)
                 subs["config4_sage3_mxfp4_hw"] = attn_record(ctx, "sage3_mxfp4", steps=2, sub=True, sdpa=True)
                 subs["config5_sage3_nvfp4"] = attn_record(ctx, "sage3_nvfp4", steps=5, sub=True)
                 subs["mxfp8_qdq_config1"] = qdq_record(ctx, "mxfp8_qdq", sub=True)

@@ -43,8 +43,11 @@ def _bad(got: torch.Tensor, want: np.ndarray, exact: np.ndarray, absum: np.ndarr
     return int((np.abs(g - want) > REL * np.abs(exact) + acc * absum + 1e-30).sum())
 
 
+# M <= 64 runs the swap-AB decode kernel (activation quantised in its producer),
+# larger M the block16 GEMM after a separate quantisation pass
 @pytest.mark.parametrize("m,n,k", [(128, 256, 256), (1, 1024, 4096), (16, 512, 4096), (300, 768, 2048),
-                                   (129, 257, 288), (512, 1024, 4096)])
+                                   (129, 257, 288), (512, 1024, 4096), (5, 384, 2080), (33, 256, 512),
+                                   (64, 640, 1024), (17, 14336, 4096)])
 def test_nvfp4_linear_matches_exact(cuda_device, m, n, k):
     from vllm_qdq_plugin.gemm import nvfp4_linear
     w, codes, scales, gs = _weight(n, k, m + n + k, cuda_device)
@@ -58,10 +61,11 @@ def test_nvfp4_linear_matches_exact(cuda_device, m, n, k):
     assert _native.device_status() == 0
 
 
-def test_nvfp4_linear_fp16_bias_and_given_global_scale(cuda_device):
+@pytest.mark.parametrize("m", [200, 24])
+def test_nvfp4_linear_fp16_bias_and_given_global_scale(cuda_device, m):
     from vllm_qdq_plugin.gemm import nvfp4_linear
     from vllm_qdq_plugin.qdq import nvfp4_global_scale
-    m, n, k = 200, 384, 1024
+    n, k = 384, 1024
     w, codes, scales, gs = _weight(n, k, 3, cuda_device)
     a = torch.randn(m, k, generator=torch.Generator().manual_seed(1)).to(torch.float16)
     bias = torch.randn(n, generator=torch.Generator().manual_seed(2)).to(torch.float16)

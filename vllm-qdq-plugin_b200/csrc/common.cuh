@@ -33,6 +33,13 @@ int qdq_mxfp4_codes_tiled(const void* x, void* codes, void* sf_tiled, int64_t M,
 int fp4_linear_decode(const void* a, int64_t lda, int dtype, const void* w_codes, const void* w_sf_tiled,
                       const void* bias, void* c, int64_t M, int64_t N, int64_t K, int64_t ldw_bytes,
                       int64_t ldc, void* stream);
+// The same for NVFP4 weights (E4M3 scales per 16 in the block-16 tiled layout,
+// tensor scale w_gs) with the activation quantised to NVFP4 against the device
+// scalar *a_gs (a_gs == nullptr: 2688 / max |a|, computed in the kernel); the
+// output is scaled by w_gs / gs_a.
+int fp4_linear_decode_nvf4(const void* a, int64_t lda, int dtype, const float* a_gs, const void* w_codes,
+                           const void* w_sf_tiled, float w_gs, const void* bias, void* c, int64_t M, int64_t N,
+                           int64_t K, int64_t ldw_bytes, int64_t ldc, void* stream);
 // Device address of the library's status word on the current device (kernels
 // record bounded-wait timeouts there); nullptr + error message on failure.
 int* device_status_ptr();

@@ -38,6 +38,8 @@ constexpr int DBKB = DBK / 2;            // code bytes per row per stage (one 12
 constexpr int NA_MAX = 64;               // activation rows per launch (UMMA N)
 constexpr int W_TILE = DBM * DBKB;       // 16 KB
 constexpr int SF_STAGE = 1024;           // two 512-byte scale chunks (8 scales per row)
+// NVFP4 (block16): four 512-byte scale chunks per stage (16 E4M3 scales per row)
+__host__ __device__ constexpr int sf_stage(bool nv) { return nv ? 2 * SF_STAGE : SF_STAGE; }
 constexpr int D_QUANT_THREADS = 256;                 // 8 quantiser / epilogue warps
 constexpr int D_THREADS = 64 + D_QUANT_THREADS;      // + producer and MMA warps
 // Quantiser teams (one stage each in flight) for M activation rows: few rows
@@ -45,15 +47,16 @@ constexpr int D_THREADS = 64 + D_QUANT_THREADS;      // + producer and MMA warps
 // many rows make it throughput-bound, so more threads share one stage.
 __host__ __device__ constexpr int decode_teams(int M) { return M <= 16 ? 4 : (M <= 32 ? 2 : 1); }
 constexpr int D_TMEM_COLS = 128;
-constexpr uint32_t T_ACC = 0, T_SFW = 64, T_SFA = 72;
+constexpr uint32_t T_ACC = 0, T_SFW = 64, T_SFA = 80;  // scale columns: 4 per 512-byte chunk
 
 // Stage layout for NA activation rows: W codes | A codes | W scales | A scales | raw A.
-template <int kNA>
+template <int kNA, bool kNV = false>
 struct DLayout {
   static constexpr int A_TILE = kNA * DBKB;
   static constexpr int RAW = kNA * DBK * 2;
-  static constexpr int ST_W = 0, ST_A = W_TILE, ST_SFW = W_TILE + A_TILE, ST_SFA = ST_SFW + SF_STAGE,
-                       ST_RAW = ST_SFA + SF_STAGE;
+  static constexpr int SFS = sf_stage(kNV);
+  static constexpr int ST_W = 0, ST_A = W_TILE, ST_SFW = W_TILE + A_TILE, ST_SFA = ST_SFW + SFS,
+                       ST_RAW = ST_SFA + SFS;
   static constexpr int STAGE = (ST_RAW + RAW + 1023) / 1024 * 1024;
   static constexpr int STAGES = kNA == 16 ? 7 : (kNA == 32 ? 5 : 3);
 };
@@ -66,13 +69,14 @@ struct __align__(8) DBars {
   uint32_t tmem_base;
   int abort;
   int preissued;       // stages whose loads thread 0 issued before the CTA-wide sync
+  uint32_t amax[8];    // NVFP4 without a given activation scale: per-warp |x| maxima (bit patterns)
 };
-template <int kNA>
+template <int kNA, bool kNV = false>
 constexpr size_t d_smem_bytes() {
-  return 1024 + static_cast<size_t>(DLayout<kNA>::STAGES) * DLayout<kNA>::STAGE + sizeof(DBars);
+  return 1024 + static_cast<size_t>(DLayout<kNA, kNV>::STAGES) * DLayout<kNA, kNV>::STAGE + sizeof(DBars);
 }
-static_assert(d_smem_bytes<16>() <= 227 * 1024 && d_smem_bytes<32>() <= 227 * 1024 &&
-              d_smem_bytes<64>() <= 227 * 1024, "decode stages exceed shared memory");
+static_assert(d_smem_bytes<16, true>() <= 227 * 1024 && d_smem_bytes<32, true>() <= 227 * 1024 &&
+              d_smem_bytes<64, true>() <= 227 * 1024, "decode stages exceed shared memory");
 
 template <bool kF16>
 struct DOut {
@@ -87,12 +91,17 @@ struct DOut<true> {
   __device__ static T one(float a) { return __float2half_rn(a); }
 };
 
-template <int kDtype, int kNA>
+// kNV: NVFP4 weights (E4M3 scales per 16, tensor scale w_gs) and the
+// activation quantised to NVFP4 with the per-tensor scale *a_gs (vLLM's
+// NVFP4 rule, nv_group_codes), block16 MMAs, output times w_gs / *a_gs.
+template <int kDtype, int kNA, bool kNV>
 __global__ void __launch_bounds__(D_THREADS, 1)
 mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
                    const uint8_t* __restrict__ sfw, const void* __restrict__ bias_v, void* __restrict__ c_v,
-                   int M, int N, int K, int64_t ldc, int kchunks, int* status) {
-  using Lay = DLayout<kNA>;
+                   int M, int N, int K, int64_t ldc, int kchunks, const float* __restrict__ a_gs, float w_gs,
+                   float zero, const uint16_t* __restrict__ a_raw, int64_t lda, int* status) {
+  using Lay = DLayout<kNA, kNV>;
+  constexpr int SFS = Lay::SFS, CPS = SFS / 512;  // scale bytes / chunks per stage
   constexpr int S = Lay::STAGES;
   constexpr bool kF16 = kDtype == QDQ_DTYPE_FP16;
   using O = DOut<kF16>;
@@ -111,9 +120,9 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
   auto issue_w = [&](int kt) {
     const int s = kt % S;
     uint8_t* st = smem + s * Lay::STAGE;
-    mbar_arrive_expect_tx(&bars->raw[s], W_TILE + SF_STAGE + Lay::RAW);
+    mbar_arrive_expect_tx(&bars->raw[s], W_TILE + SFS + Lay::RAW);
     tma_load_2d(st + Lay::ST_W, &tmap_w, kt * DBKB, n_blk * DBM, &bars->raw[s]);
-    bulk_load(st + Lay::ST_SFW, sfw + (static_cast<int64_t>(n_blk) * kchunks + 2 * kt) * 512, SF_STAGE,
+    bulk_load(st + Lay::ST_SFW, sfw + (static_cast<int64_t>(n_blk) * kchunks + CPS * kt) * 512, SFS,
               &bars->raw[s]);
   };
   auto issue_a = [&](int kt) {
@@ -146,10 +155,10 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
   pdl_launch_dependents();
   // Activation rows >= M and their scales stay zero for the whole launch
   // (disjoint from the W, W-scale and raw-A bytes the loads above write).
-  constexpr int kZero = (Lay::A_TILE + 2 * SF_STAGE) / 16;  // A codes + both scale chunks
+  constexpr int kZero = (Lay::A_TILE + 2 * SFS) / 16;  // A codes + W and A scale chunks
   for (int i = threadIdx.x; i < S * kZero; i += D_THREADS) {
     const int s = i / kZero, o = (i % kZero) * 16;
-    if (o < Lay::A_TILE || o >= Lay::A_TILE + SF_STAGE)  // skip the W scales (loaded every stage)
+    if (o < Lay::A_TILE || o >= Lay::A_TILE + SFS)  // skip the W scales (loaded every stage)
       *reinterpret_cast<uint4*>(smem + s * Lay::STAGE + Lay::ST_A + o) = make_uint4(0, 0, 0, 0);
   }
   if (warp == 0) {
@@ -187,7 +196,7 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (elect_one()) {
-      constexpr uint32_t idesc = idesc_mxf4(DBM, kNA, true);
+      constexpr uint32_t idesc = idesc_mxf4(DBM, kNA, !kNV);
       bool ok = true;
       for (int kt = 0; kt < num_kt; ++kt) {
         const int s = kt % S;
@@ -195,18 +204,24 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
         if (*(volatile int*)&bars->abort) { ok = false; break; }
         tc_fence_after();
         uint8_t* st = smem + s * Lay::STAGE;
-        tmem_cp_sf(tmem + T_SFW + 0, smem_desc_sf(st + Lay::ST_SFW));        // W rows, scales 0-3 of the stage
-        tmem_cp_sf(tmem + T_SFW + 4, smem_desc_sf(st + Lay::ST_SFW + 512));  // scales 4-7
-        tmem_cp_sf(tmem + T_SFA + 0, smem_desc_sf(st + Lay::ST_SFA));        // activation rows
-        tmem_cp_sf(tmem + T_SFA + 4, smem_desc_sf(st + Lay::ST_SFA + 512));
+#pragma unroll
+        for (int j = 0; j < CPS; ++j) {  // chunk j: scales 4j .. 4j+3 of the stage, W rows / activation rows
+          tmem_cp_sf(tmem + T_SFW + 4 * j, smem_desc_sf(st + Lay::ST_SFW + 512 * j));
+          tmem_cp_sf(tmem + T_SFA + 4 * j, smem_desc_sf(st + Lay::ST_SFA + 512 * j));
+        }
         const uint64_t dw = smem_desc_sw128(st + Lay::ST_W);
         const uint64_t da = smem_desc_sw128(st + Lay::ST_A);
 #pragma unroll
         for (int kk = 0; kk < DBK / 64; ++kk) {
-          const uint32_t j = kk >> 1, sf_id = (kk & 1) * 2;
-          mma_mxf4(tmem + T_ACC, dw + ((kk * 32) >> 4), da + ((kk * 32) >> 4),
-                   idesc_with_sf_ids(idesc, sf_id, sf_id), (tmem + T_SFW + 4 * j) | (sf_id << 30),
-                   (tmem + T_SFA + 4 * j) | (sf_id << 30), (kt | kk) != 0);
+          if (kNV) {  // block16: K-64 step kk reads the whole chunk kk
+            mma_nvf4(tmem + T_ACC, dw + ((kk * 32) >> 4), da + ((kk * 32) >> 4), idesc, tmem + T_SFW + 4 * kk,
+                     tmem + T_SFA + 4 * kk, (kt | kk) != 0);
+          } else {    // block32: chunk kk / 2, scale bytes 2 (kk % 2), +1
+            const uint32_t j = kk >> 1, sf_id = (kk & 1) * 2;
+            mma_mxf4(tmem + T_ACC, dw + ((kk * 32) >> 4), da + ((kk * 32) >> 4),
+                     idesc_with_sf_ids(idesc, sf_id, sf_id), (tmem + T_SFW + 4 * j) | (sf_id << 30),
+                     (tmem + T_SFA + 4 * j) | (sf_id << 30), (kt | kk) != 0);
+          }
         }
         tc_commit(&bars->empty[s]);
       }
@@ -221,6 +236,34 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
     const int tq = (threadIdx.x - 64) % team_threads;
     const int lane = threadIdx.x & 31;
     bool ok = true;
+    // NVFP4 activation scale, written by the previous kernel or computed here
+    // (after pdl_wait either way): gs = 2688 / max |a| over the whole [M, K]
+    // activation, the formula of qdq_nvfp4_global_scale, from the same
+    // maximum bit pattern, so the same fp32 value.  Every CTA reads the
+    // activation (the caller passes no scale only for M <= 16 rows, resident
+    // in L2) while its weight ring fills.
+    float gs = 0.f;
+    if (kNV) {
+      if (a_gs != nullptr) {
+        gs = __ldg(a_gs);
+      } else {
+        const int qt = threadIdx.x - 64, cpr = K / 8;  // 16-byte chunks per row
+        uint32_t m8 = 0;
+        for (int i = qt; i < M * cpr; i += D_QUANT_THREADS) {
+          const int row = i / cpr, c = i - row * cpr;
+          m8 = max(m8, absmax8(ld_stream(reinterpret_cast<const uint4*>(a_raw + row * lda + c * 8))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m8 = max(m8, __shfl_xor_sync(0xffffffffu, m8, o));
+        if (lane == 0) bars->amax[warp - 2] = m8;
+        asm volatile("bar.sync 1, %0;" ::"n"(D_QUANT_THREADS) : "memory");  // the quantiser warps only
+        uint32_t all = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) all = max(all, bars->amax[w]);
+        gs = __fdiv_rn(2688.0f, Fmt<kDtype>::amax_value(all));
+      }
+    }
+    const float rgs = kNV ? zero_safe_recip(gs) : 0.f;
     for (int kt = 0; kt < num_kt; ++kt) {
       const int s = kt % S;
       // A parity wait can only tell the current phase from the previous one,
@@ -229,7 +272,19 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
       if (ok) ok = mbar_wait(&bars->raw[s], (kt / S) & 1, status, 0x404);
       uint8_t* st = smem + s * Lay::STAGE;
       // groups (row m, 32-block g) of this stage's [M, 256] slice; columns past K read as zero
-      for (int it = tq; it < M * (DBK / 32); it += team_threads) {
+      if (kNV) {  // 16-blocks: 8 code bytes (half a 16-byte chunk) and one E4M3 scale each
+        for (int it = tq; it < M * (DBK / 16); it += team_threads) {
+          const int m = it >> 4, g = it & 15;
+          const uint4* src = reinterpret_cast<const uint4*>(st + Lay::ST_RAW + m * (DBK * 2) + g * 32);
+          uint4 v[2] = {src[0], src[1]};
+          uint32_t code[2];
+          const uint32_t sb = nv_group_codes<kDtype>(v, gs, rgs, zero, code);
+          *reinterpret_cast<uint2*>(st + Lay::ST_A + m * DBKB + (((g >> 1) ^ (m & 7)) << 4) + (g & 1) * 8) =
+              make_uint2(code[0], code[1]);
+          st[Lay::ST_SFA + (g >> 2) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4 + (g & 3)] = static_cast<uint8_t>(sb);
+        }
+      }
+      for (int it = tq; !kNV && it < M * (DBK / 32); it += team_threads) {
         const int m = it >> 3, g = it & 7;
         const uint4* src = reinterpret_cast<const uint4*>(st + Lay::ST_RAW + m * (DBK * 2) + g * 64);
         uint4 v[4] = {src[0], src[1], src[2], src[3]};
@@ -260,10 +315,12 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
       const int n = n_blk * DBM + q * 32 + lane;
       if (ok && !*(volatile int*)&bars->abort && n < N) {
         const float b = bias != nullptr ? O::load(bias + n) : 0.f;
+        const float alpha = kNV ? w_gs / gs : 1.0f;  // as the block16 GEMM's epilogue
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int m = 32 * half + i;
-          if (m < M) C[static_cast<int64_t>(m) * ldc + n] = O::one(__uint_as_float(r[i]) + b);
+          const float v = kNV ? __uint_as_float(r[i]) * alpha : __uint_as_float(r[i]);
+          if (m < M) C[static_cast<int64_t>(m) * ldc + n] = O::one(v + b);
         }
       }
     }
@@ -277,15 +334,16 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
   }
 }
 
-template <int kDtype, int kNA>
+template <int kDtype, int kNA, bool kNV>
 int launch_decode(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* sf, const void* bias, void* c,
-                  int64_t M, int64_t N, int64_t K, int64_t ldc, int kchunks, int* status, cudaStream_t s) {
-  constexpr size_t smem = d_smem_bytes<kNA>();
+                  int64_t M, int64_t N, int64_t K, int64_t ldc, int kchunks, const float* a_gs, float w_gs,
+                  const void* a_raw, int64_t lda, int* status, cudaStream_t s) {
+  constexpr size_t smem = d_smem_bytes<kNA, kNV>();
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(&mxf4_decode_kernel<kDtype, kNA>,
+    cudaError_t e = cudaFuncSetAttribute(&mxf4_decode_kernel<kDtype, kNA, kNV>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_linear_decode: smem attribute: %s", cudaGetErrorString(e));
     attr_set[dev] = true;
@@ -303,9 +361,11 @@ int launch_decode(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* s
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, mxf4_decode_kernel<kDtype, kNA>, tw, ta, sf, bias, c,
+  const float zero = 0.0f;  // +0.0 as an operand the compiler cannot fold (see nv_scale8)
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, mxf4_decode_kernel<kDtype, kNA, kNV>, tw, ta, sf, bias, c,
                                            static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), ldc,
-                                           kchunks, status);
+                                           kchunks, a_gs, w_gs, zero, static_cast<const uint16_t*>(a_raw), lda,
+                                           status);
   if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "fp4_linear_decode: launch: %s", cudaGetErrorString(e));
   return check_launch("fp4_linear_decode");
 }
@@ -717,9 +777,12 @@ int launch_moe(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* sf, 
 }  // namespace
 
 // Host entry used by fp4_linear_mxf4 for M <= 64 (declared in common.cuh).
-int fp4_linear_decode(const void* a, int64_t lda, int dtype, const void* w_codes, const void* w_sf_tiled,
-                      const void* bias, void* c, int64_t M, int64_t N, int64_t K, int64_t ldw_bytes,
-                      int64_t ldc, void* stream) {
+// Small-M fused linear, MXFP4 (nv == false) or NVFP4 (nv: E4M3 weight scales
+// per 16 with tensor scale w_gs; the activation quantised with the device
+// scalar *a_gs).  One launch.
+static int decode_common(const void* a, int64_t lda, int dtype, const void* w_codes, const void* w_sf_tiled,
+                         const void* bias, void* c, int64_t M, int64_t N, int64_t K, int64_t ldw_bytes,
+                         int64_t ldc, bool nv, const float* a_gs, float w_gs, void* stream) {
   if (M < 1 || M > NA_MAX) return fail(QDQ_ERR_INVALID_ARG, "fp4_linear_decode: M must be in [1, 64]");
   if ((reinterpret_cast<uintptr_t>(a) & 15) || ((lda * 2) & 15))
     return fail(QDQ_ERR_ALIGNMENT, "fp4_linear_decode: activation rows must be 16-byte aligned");
@@ -731,18 +794,40 @@ int fp4_linear_decode(const void* a, int64_t lda, int dtype, const void* w_codes
   CUtensorMap tw, ta;
   if (int st = make_tmap_u8_2d(&tw, w_codes, N, K / 2, ldw_bytes, DBKB, DBM, 128)) return st;
   if (int st = make_tmap_u16_2d(&ta, a, M, K, lda * 2, DBK, na)) return st;
-  const int kchunks = static_cast<int>(((K / 32) + 7) / 8 * 8 / 4);
+  // 512-byte chunks of 4 scales per 128 rows, scales per row padded to one K-256 stage
+  const int kchunks = nv ? static_cast<int>(((K / 16) + 15) / 16 * 16 / 4)
+                         : static_cast<int>(((K / 32) + 7) / 8 * 8 / 4);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto* sf = static_cast<const uint8_t*>(w_sf_tiled);
   const bool f16 = dtype == QDQ_DTYPE_FP16;
-  if (na == 16)
-    return f16 ? launch_decode<QDQ_DTYPE_FP16, 16>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, status, s)
-               : launch_decode<QDQ_DTYPE_BF16, 16>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, status, s);
-  if (na == 32)
-    return f16 ? launch_decode<QDQ_DTYPE_FP16, 32>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, status, s)
-               : launch_decode<QDQ_DTYPE_BF16, 32>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, status, s);
-  return f16 ? launch_decode<QDQ_DTYPE_FP16, 64>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, status, s)
-             : launch_decode<QDQ_DTYPE_BF16, 64>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, status, s);
+#define QDQ_DECODE(NA, NV)                                                                                  \
+  return f16 ? launch_decode<QDQ_DTYPE_FP16, NA, NV>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, a_gs, w_gs, \
+                                                      a, lda, status, s)                                      \
+             : launch_decode<QDQ_DTYPE_BF16, NA, NV>(tw, ta, sf, bias, c, M, N, K, ldc, kchunks, a_gs, w_gs, \
+                                                      a, lda, status, s);
+  if (nv) {
+    if (na == 16) { QDQ_DECODE(16, true) }
+    if (na == 32) { QDQ_DECODE(32, true) }
+    QDQ_DECODE(64, true)
+  }
+  if (na == 16) { QDQ_DECODE(16, false) }
+  if (na == 32) { QDQ_DECODE(32, false) }
+  QDQ_DECODE(64, false)
+#undef QDQ_DECODE
+}
+
+int fp4_linear_decode(const void* a, int64_t lda, int dtype, const void* w_codes, const void* w_sf_tiled,
+                      const void* bias, void* c, int64_t M, int64_t N, int64_t K, int64_t ldw_bytes,
+                      int64_t ldc, void* stream) {
+  return decode_common(a, lda, dtype, w_codes, w_sf_tiled, bias, c, M, N, K, ldw_bytes, ldc, false, nullptr, 0.f,
+                       stream);
+}
+
+int fp4_linear_decode_nvf4(const void* a, int64_t lda, int dtype, const float* a_gs, const void* w_codes,
+                           const void* w_sf_tiled, float w_gs, const void* bias, void* c, int64_t M, int64_t N,
+                           int64_t K, int64_t ldw_bytes, int64_t ldc, void* stream) {
+  return decode_common(a, lda, dtype, w_codes, w_sf_tiled, bias, c, M, N, K, ldw_bytes, ldc, true, a_gs, w_gs,
+                       stream);
 }
 
 }  // namespace qdqb200

@@ -889,11 +889,24 @@ extern "C" int fp4_linear_nvf4(const void* a, int64_t lda, int dtype, const floa
   uint8_t* a_sf = a_codes + up(M * K / 2);
   uint8_t* a_sf_t = a_sf + up(M * K / 16);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Small M: the swap-AB decode kernel quantises the activation in its
+  // producer.  Up to 16 rows it also takes their global amax itself (every CTA
+  // reads the rows from L2, cheaper than a separate pass); above that the
+  // separate pass is cheaper than 112 CTAs reading the same rows.
+  const bool decode = M <= 64 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 && ((lda * 2) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(w_sf_tiled) & 15) == 0 && lda >= K && ldc >= N &&
+                      ldw_bytes >= K / 2;
+  if (decode && (a_global_scale != nullptr || M <= 16))
+    return fp4_linear_decode_nvf4(a, lda, dtype, a_global_scale, w_codes, w_sf_tiled, w_global_scale, bias, c, M,
+                                  N, K, ldw_bytes, ldc, stream);
   const float* gs_a = a_global_scale;
   if (gs_a == nullptr) {
     if (int st = qdq_nvfp4_global_scale(a, gs, ws + 16, M, K, lda, dtype, stream)) return st;
     gs_a = gs;
   }
+  if (decode)
+    return fp4_linear_decode_nvf4(a, lda, dtype, gs_a, w_codes, w_sf_tiled, w_global_scale, bias, c, M, N, K,
+                                  ldw_bytes, ldc, stream);
   if (int st = qdq_nvfp4(a, nullptr, a_codes, a_sf, gs_a, M, K, lda, K, dtype, stream)) return st;
   if (int st = qdq_sf_tile(a_sf, a_sf_t, M, K, K / 16, 16, stream)) return st;
   return fp4_gemm_nvf4(a_codes, a_sf_t, gs_a, w_codes, w_sf_tiled, w_global_scale, bias, c, M, N, K, K / 2,

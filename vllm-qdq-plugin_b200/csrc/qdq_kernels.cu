@@ -23,7 +23,6 @@ namespace {
 constexpr uint32_t kFull = 0xFFFFFFFFu;
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;           // 16-byte chunks in flight per lane
-constexpr float kRecip6 = 1.0f / 6.0f;  // fp32 value of vLLM's FLOAT4_E2M1_MAX_RECIPROCAL
 
 // Resident CTAs per SM asked of the y-only MXFP4 kernel: at <= 32 registers
 // 8 CTAs fit instead of 6, keeping more 16-byte loads in flight (config 1:
@@ -181,66 +180,6 @@ mxfp4_generic_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
       if (codes) codes[r * ldc + gi * 16 + i / 2] = static_cast<uint8_t>(byte);
     }
     if (scales) scales[r * lds + gi] = static_cast<uint8_t>(e);
-  }
-}
-
-// ---------------------------------------------------------------------------
-// NVFP4 group math (nvfp4_emulation_utils.py:439-452 and :474-476)
-// ---------------------------------------------------------------------------
-struct NvGroup {
-  float out_scale;  // 1 / (scale * (1/gs))  with vLLM's zero-safe reciprocal
-  float deq;        // scale / gs
-  uint32_t sbyte;   // E4M3 byte of the block scale
-};
-
-__device__ __forceinline__ float zero_safe_recip(float t) {
-  // get_reciprocal(t) = 1 / (t + (t == 0) * 1e8)   (nvfp4_emulation_utils.py:415-418)
-  return __fdiv_rn(1.0f, __fadd_rn(t, t == 0.0f ? 1e8f : 0.0f));
-}
-
-__device__ __forceinline__ NvGroup nv_group(float vec_max, float gs, float rgs) {
-  float s = __fmul_rn(gs, __fmul_rn(vec_max, kRecip6));
-  s = fminf(fmaxf(s, -448.0f), 448.0f);
-  NvGroup g;
-  g.sbyte = e4m3_byte(s);
-  s = round_e4m3(s);
-  g.out_scale = zero_safe_recip(__fmul_rn(s, rgs));
-  g.deq = __fdiv_rn(s, gs);
-  return g;
-}
-
-// Codes of two elements x*out_scale.  The reference clamps to +-6 and rounds
-// to nearest-even (nvfp4_emulation_utils.py:450-451, :425-436): the
-// satfinite E2M1 conversion does both.  cast_to_fp4 multiplies by
-// torch.sign(), which is +0 for a -0 product (x == -0, or an underflow), so a
-// zero product is encoded as +0.
-__device__ __forceinline__ uint32_t nv_codes(float xa, float xb, float out_scale) {
-  const float2 p = mul_f32x2(make_float2(xa, xb), make_float2(out_scale, out_scale));
-  uint32_t byte = cvt_e2m1x2(p.x, p.y);
-  if (p.x == 0.0f) byte &= 0xF7u;
-  if (p.y == 0.0f) byte &= 0x7Fu;
-  return byte;
-}
-
-// With out_scale >= 2^-16 no nonzero bf16 or fp16 input (smallest magnitude
-// 2^-133, resp. 2^-24) has a product below the smallest fp32 subnormal
-// 2^-149, so the only zero products are those of x == +-0.
-constexpr float kNoUnderflowScale = 0x1p-16f;
-
-// x * out_scale for 8 elements, with a zero product made +0 (see nv_codes):
-// the product is formed as fma(x, out_scale, zero) with `zero` = +0.0 passed
-// in as a kernel argument (an operand the compiler cannot treat as a
-// constant), so an exact -0 product becomes -0 + +0 = +0 under RN while every
-// other product is rounded exactly once, as by a plain multiply.
-__device__ __forceinline__ void nv_scale8(const uint32_t (&w)[4], float out_scale, float zero, float (&sv)[8],
-                                          bool fp16) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float a = fp16 ? f16lo(w[j]) : bf16lo(w[j]);
-    const float b = fp16 ? f16hi(w[j]) : bf16hi(w[j]);
-    const float2 t = fma_f32x2(make_float2(a, b), make_float2(out_scale, out_scale), make_float2(zero, zero));
-    sv[2 * j] = t.x;
-    sv[2 * j + 1] = t.y;
   }
 }
 
