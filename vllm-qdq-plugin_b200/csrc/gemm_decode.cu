@@ -6,6 +6,13 @@
 // those of the reference's mxfp4_qdq(A) against W (reference:
 // src/vllm_qdq_plugin/patch.py:51-57 + vllm/_custom_ops.py:1277 marlin_gemm).
 //
+// NVFP4 mode (kNV): W carries E4M3 scales per 16 (block16 tiled layout) and a
+// tensor scale w_gs, the activation is quantised with vLLM's NVFP4 rule
+// against the per-tensor scale gs_a (given, or 2688 / max |a| computed by
+// every CTA from the rows), the MMAs are kind::mxf4nvf4.block16 and the
+// output is scaled by w_gs / gs_a (reference: the NVFP4 Marlin path of
+// vllm/model_executor/layers/quantization/utils/marlin_utils_fp4.py:149-202).
+//
 // "Swap AB": the tcgen05 MMA's M side is 128 rows of W and its N side the
 // activation rows, padded to NA = 16, 32 or 64.  One CTA per 128 rows of W
 // streams that slice of W once (N / 128 CTAs: 112 for N = 14336), so the
