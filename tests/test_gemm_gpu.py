@@ -216,6 +216,34 @@ def test_moe_grouped_gemm_matches_oracle(cuda_device, m, e, top_k, bs, n, k, mul
     assert _native.device_status() == 0
 
 
+@pytest.mark.parametrize("k", [288, 2880])
+def test_moe_result_independent_of_stale_workspace(cuda_device, k):
+    """K not a multiple of 256: the GEMM's last K stage reads scale bytes past
+    K / 32, which the pre-pass writes as E8M0 0.  A workspace left full of
+    0xFF (NaN scales) by earlier use must give the bit-identical result."""
+    from vllm_qdq_plugin import _native
+    from vllm_qdq_plugin.gemm import prepare_mxfp4_moe_weight
+    m, e, top_k, bs, n = 40, 4, 2, 16, 256
+    a, codes, scales, sid, eid, ntp, topk_w = _moe_case(m, e, top_k, bs, n, k, seed=k)
+    dev = cuda_device
+    w = prepare_mxfp4_moe_weight(torch.from_numpy(codes).to(dev), torch.from_numpy(scales).to(dev))
+    ad, sidd, eidd, ntpd, twd = (t.to(dev) for t in (a, torch.from_numpy(sid), torch.from_numpy(eid),
+                                                     torch.from_numpy(ntp), torch.from_numpy(topk_w).reshape(-1)))
+    lib = _native.lib()
+    outs = []
+    for fill in (0x00, 0xFF):
+        ws = torch.full((lib.fp4_moe_workspace_bytes(sidd.numel(), bs, k),), fill, dtype=torch.uint8, device=dev)
+        out = torch.zeros((m * top_k, n), dtype=torch.bfloat16, device=dev)
+        _native.check("fp4_moe_mxf4", lib.fp4_moe_mxf4(
+            ad.data_ptr(), k, 0, w.codes.data_ptr(), w.sf_tiled.data_ptr(), e, sidd.data_ptr(), eidd.data_ptr(),
+            ntpd.data_ptr(), twd.data_ptr(), sidd.numel(), bs, top_k, 1, out.data_ptr(), n, m, n, k,
+            ws.data_ptr(), ws.numel(), _native.stream_ptr(dev)))
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.isfinite(outs[1].float()).all()
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+
+
 def test_moe_skips_foreign_experts_and_padding_blocks(cuda_device):
     """Blocks whose expert id is -1 (not on this rank) and blocks past
     num_tokens_post_padded leave their rows untouched; fp16 activations."""

@@ -471,8 +471,12 @@ moe_gather_quant_kernel(const uint16_t* __restrict__ a, int64_t lda, const int32
                         int64_t num_sorted, int bs, int na, int top_k, int n_slots, int num_experts, int K,
                         int kchunks, uint8_t* __restrict__ codes, uint8_t* __restrict__ sf,
                         int32_t* __restrict__ seg_tab) {
-  const int gpr = K / 32;
-  const int64_t total = num_sorted * gpr;
+  // Every scale byte the GEMM reads is written here, the padding groups past
+  // K / 32 (up to kchunks * 4 per row, one K-256 stage) as E8M0 0 (2^-127):
+  // the workspace may hold stale bytes, and a stale 0xFF (NaN) would turn the
+  // padding's zero codes into NaN products.
+  const int gpr = K / 32, gpr_p = kchunks * 4;
+  const int64_t total = num_sorted * gpr_p;
   const int npp = __ldg(num_post_padded);
   if (blockIdx.x == 0) {
     const int64_t nb = num_sorted / bs;
@@ -481,17 +485,18 @@ moe_gather_quant_kernel(const uint16_t* __restrict__ a, int64_t lda, const int32
   }
   for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < total;
        it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t p = it / gpr;
-    const int g = static_cast<int>(it - p * gpr);
+    const int64_t p = it / gpr_p;
+    const int g = static_cast<int>(it - p * gpr_p);
     const int s = p < npp ? __ldg(sorted_ids + p) : -1;
     uint32_t code[4] = {0u, 0u, 0u, 0u};
     int e = 0;
-    if (s >= 0 && s < n_slots) {
+    if (g < gpr && s >= 0 && s < n_slots) {
       const uint4* src = reinterpret_cast<const uint4*>(a + static_cast<int64_t>(s / top_k) * lda + g * 32);
       uint4 v[4] = {src[0], src[1], src[2], src[3]};
       e = mx_group_codes<kDtype>(v, code);
     }
-    *reinterpret_cast<uint4*>(codes + p * (K / 2) + g * 16) = make_uint4(code[0], code[1], code[2], code[3]);
+    if (g < gpr)
+      *reinterpret_cast<uint4*>(codes + p * (K / 2) + g * 16) = make_uint4(code[0], code[1], code[2], code[3]);
     const int64_t b = p / bs;
     const int r = static_cast<int>(p - b * bs);
     // row r of block b sits at segment row na*i + r of the chunk of block b - i
