@@ -554,20 +554,30 @@ __device__ void ds_tile(const __nv_bfloat16* kcs, __nv_bfloat16* qms, const __nv
         }
       }
     }
-    // store: c fragment rows (lane/4) and (lane/4 + 8), cols 2*(lane%4) + {0,1}
+    // The chunk's 64 x 128 outputs are staged in qms (its query means are no
+    // longer read once every warp is past the MMAs) and leave as whole
+    // 256-byte rows: c fragment rows (lane/4) and (lane/4 + 8), cols
+    // 2*(lane%4) + {0,1}.
+    __syncthreads();
 #pragma unroll
     for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
       for (int ni = 0; ni < 4; ++ni)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          const int g = g0 + wm * 32 + mi * 16 + (lane >> 2) + hh * 8;
-          const int n = n0 + wn * 32 + ni * 8 + (lane & 3) * 2;
-          if (g < G) {
-            *reinterpret_cast<uint32_t*>(ds + (static_cast<int64_t>(bh) * G + g) * Lp + n) =
-                In16<kF16>::pack(acc[mi][ni][hh * 2], acc[mi][ni][hh * 2 + 1]);
-          }
+          const int gl = wm * 32 + mi * 16 + (lane >> 2) + hh * 8;
+          const int nl = wn * 32 + ni * 8 + (lane & 3) * 2;
+          *reinterpret_cast<uint32_t*>(qms + gl * DS_LD + nl) =
+              In16<kF16>::pack(acc[mi][ni][hh * 2], acc[mi][ni][hh * 2 + 1]);
         }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {  // 64 rows x 16 chunks of 16 bytes, four per thread
+      const int i = threadIdx.x + 256 * k, gl = i >> 4, c = i & 15;
+      if (g0 + gl < G)
+        *reinterpret_cast<uint4*>(ds + (static_cast<int64_t>(bh) * G + g0 + gl) * Lp + n0 + c * 8) =
+            *reinterpret_cast<const uint4*>(qms + gl * DS_LD + c * 8);
+    }
   }
 }
 
