@@ -280,6 +280,7 @@ class Ctx:
     dev: torch.device
     dist: object | None
     args: argparse.Namespace
+    host_cpus: list | None = None  # CPUs this rank is pinned to (NVML's list for its GPU), None if unchanged
 
     def barrier(self):
         if self.dist is not None:
@@ -763,7 +764,9 @@ def qdq_record(ctx: Ctx, workload: str, weak: bool = False, sub: bool = False) -
                 "path": (f"vllm_qdq_plugin.qdq.qdq_from_host(fmt={host_fmt!r}) on pinned host buffers: "
                          "16 MB row blocks through the C-ABI qdq_host_stream, H2D / QDQ / D2H overlapped "
                          "on three streams; bytes per rank"
-                         + ("; all ranks share the host's memory and PCIe" if ctx.world > 1 else ""))},
+                         + (f"; rank pinned to the {len(ctx.host_cpus)} CPUs NVML lists for its GPU"
+                            if ctx.host_cpus else "")
+                         + ("; all ranks' copies go through the one host's memory" if ctx.world > 1 else ""))},
         "gpu_launches": steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_src,
@@ -1286,7 +1289,11 @@ def run_ours(args) -> None:
 
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
-    ctx = Ctx(world=world, rank=rank, local=local, dev=dev, dist=dist, args=args)
+    host_cpus = None
+    if world > 1:  # pinned staging buffers on the GPU's own NUMA node, copies from cores near its PCIe root
+        from vllm_qdq_plugin import shard
+        host_cpus = shard.bind_to_gpu_cpus(local)
+    ctx = Ctx(world=world, rank=rank, local=local, dev=dev, dist=dist, args=args, host_cpus=host_cpus)
     try:
         if args.workload is None:
             line = qdq_record(ctx, "nvfp4_qdq")

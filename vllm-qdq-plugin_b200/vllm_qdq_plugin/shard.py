@@ -16,6 +16,10 @@ Two small exchanges sit outside it:
 * Timing takes the maximum over ranks; results are gathered only to verify
   them.
 
+Each process can also pin itself to the host CPUs NVML lists as local to its
+GPU (bind_to_gpu_cpus), so that its pinned staging buffers sit on that GPU's
+NUMA node.
+
 The reference runs one tensor per vLLM worker (src/vllm_qdq_plugin/patch.py:51-57
 calls mxfp4_qdq on the worker's own activation); its vLLM tensor-parallel
 ranks each quantise their own shard.  The global-scale rule follows vLLM's
@@ -24,6 +28,8 @@ scalar per tensor.
 """
 
 from __future__ import annotations
+
+import os
 
 import torch
 
@@ -111,3 +117,54 @@ def gather_rows(local: torch.Tensor, rows: int, group=None) -> torch.Tensor:
         s, e = row_range(rows, r, world)
         parts.append(block[: e - s])
     return torch.cat(parts, dim=0)
+
+
+def gpu_cpu_affinity(device: int, nvml=None) -> list[int] | None:
+    """The host CPUs NVML reports as local to CUDA device `device`.
+
+    The device is looked up by its PCI address (CUDA and NVML may number GPUs
+    differently).  Returns None when NVML is unavailable or reports nothing.
+    `nvml` is the NVML module (pynvml by default); tests pass a fake.
+    """
+    if nvml is None:
+        try:
+            import pynvml as nvml
+        except ImportError:
+            return None
+    try:
+        nvml.nvmlInit()
+    except Exception:
+        return None
+    try:
+        prop = torch.cuda.get_device_properties(device)
+        bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+        handle = nvml.nvmlDeviceGetHandleByPciBusId(bus)
+        words = nvml.nvmlDeviceGetCpuAffinity(handle, ((os.cpu_count() or 1) + 63) // 64)
+        cpus = [64 * w + b for w, word in enumerate(words) for b in range(64) if (int(word) >> b) & 1]
+        return cpus or None
+    except Exception:
+        return None
+    finally:
+        try:
+            nvml.nvmlShutdown()
+        except Exception:
+            pass
+
+
+def bind_to_gpu_cpus(device: int, nvml=None) -> list[int] | None:
+    """Pin this process to the CPUs local to `device` (one process per GPU).
+
+    Pinned host buffers allocated afterwards are then first touched on the
+    GPU's own NUMA node, and host copies run on cores near its PCIe root.
+    Only the calling process's CPU affinity changes; no GPU setting is
+    touched.  Returns the CPU list applied, or None (nothing changed) when
+    NVML gives no affinity or it names no CPU this process may use.
+    """
+    cpus = gpu_cpu_affinity(device, nvml)
+    if not cpus:
+        return None
+    allowed = sorted(set(cpus) & os.sched_getaffinity(0))
+    if not allowed:
+        return None
+    os.sched_setaffinity(0, allowed)
+    return allowed
