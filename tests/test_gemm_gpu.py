@@ -300,3 +300,43 @@ def test_moe_marlin_hook_routes_captured_layers(cuda_device):
     slots = np.array(sorted(rows))
     _check(out[torch.from_numpy(slots).to(dev)], np.stack([rows[s][0] for s in slots]),
            np.stack([rows[s][1] for s in slots]), "moe hook")
+
+
+@pytest.mark.parametrize("fmt", ["mxfp4", "nvfp4"])
+@pytest.mark.parametrize("m,k", [(16, 2880), (40, 288), (200, 2880), (300, 288)])
+def test_linear_result_independent_of_stale_workspace(cuda_device, fmt, m, k):
+    """The fused linears' workspaces come from torch.empty, so they may hold
+    anything an earlier tensor left, 0xFF (an E8M0 NaN) included.  With K not
+    a multiple of 256 the GEMM's last K stage reads scale bytes past the
+    activation's last group.  A 0x00- and a 0xFF-filled workspace must give
+    the bit-identical, finite result on the decode (M <= 64) and GEMM paths."""
+    from vllm_qdq_plugin import _native
+    from vllm_qdq_plugin.gemm import prepare_mxfp4_weight, prepare_nvfp4_weight
+    dev = cuda_device
+    n = 384
+    a, codes, scales = _inputs(m, n, k, seed=m + k)
+    ad = a.to(dev)
+    lib = _native.lib()
+    outs = []
+    for fill in (0x00, 0xFF):
+        out = torch.zeros((m, n), dtype=torch.bfloat16, device=dev)
+        if fmt == "mxfp4":
+            w = prepare_mxfp4_weight(torch.from_numpy(codes).to(dev), torch.from_numpy(scales).to(dev))
+            ws = torch.full((lib.fp4_linear_workspace_bytes(m, k),), fill, dtype=torch.uint8, device=dev)
+            _native.call("fp4_linear_mxf4", ad.data_ptr(), k, 0, w.codes.data_ptr(), w.sf_tiled.data_ptr(), 0,
+                         out.data_ptr(), m, n, k, w.codes.stride(0), n, ws.data_ptr(), ws.numel(),
+                         _native.stream_ptr(dev))
+        else:
+            # NVFP4 weight from the same nibbles with E4M3 scales per 16 in [2^-6, 2^2]
+            g = torch.Generator().manual_seed(k)
+            sf = (torch.randint(0x18, 0x48, (n, k // 16), generator=g)).to(torch.uint8)
+            w = prepare_nvfp4_weight(torch.from_numpy(codes).to(dev), sf.to(dev), 0.5)
+            ws = torch.full((lib.fp4_linear_nvf4_workspace_bytes(m, k),), fill, dtype=torch.uint8, device=dev)
+            _native.call("fp4_linear_nvf4", ad.data_ptr(), k, 0, 0, w.codes.data_ptr(), w.sf_tiled.data_ptr(),
+                         0.5, 0, out.data_ptr(), m, n, k, w.codes.stride(0), n, ws.data_ptr(), ws.numel(),
+                         _native.stream_ptr(dev))
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.isfinite(outs[1].float()).all(), f"{fmt} m={m} k={k}: non-finite with a 0xFF workspace"
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    assert _native.device_status() == 0

@@ -61,11 +61,14 @@ def test_nvfp4_linear_matches_exact(cuda_device, m, n, k):
     assert _native.device_status() == 0
 
 
-@pytest.mark.parametrize("m", [200, 24])
-def test_nvfp4_linear_fp16_bias_and_given_global_scale(cuda_device, m):
+# The activation's global scale inside the call comes from the GEMM path's
+# multi-CTA pass (M > 64), a CTA cluster's pass (8 < M <= 64) or the decode
+# kernel itself (M <= 8); all must equal nvfp4_global_scale bit for bit.
+@pytest.mark.parametrize("m,k", [(200, 1024), (64, 1024), (24, 1024), (9, 2080), (8, 1024), (3, 288)])
+def test_nvfp4_linear_fp16_bias_and_given_global_scale(cuda_device, m, k):
     from vllm_qdq_plugin.gemm import nvfp4_linear
     from vllm_qdq_plugin.qdq import nvfp4_global_scale
-    n, k = 384, 1024
+    n = 384
     w, codes, scales, gs = _weight(n, k, 3, cuda_device)
     a = torch.randn(m, k, generator=torch.Generator().manual_seed(1)).to(torch.float16)
     bias = torch.randn(n, generator=torch.Generator().manual_seed(2)).to(torch.float16)

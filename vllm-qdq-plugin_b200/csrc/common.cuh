@@ -40,6 +40,11 @@ int fp4_linear_decode(const void* a, int64_t lda, int dtype, const void* w_codes
 int fp4_linear_decode_nvf4(const void* a, int64_t lda, int dtype, const float* a_gs, const void* w_codes,
                            const void* w_sf_tiled, float w_gs, const void* bias, void* c, int64_t M, int64_t N,
                            int64_t K, int64_t ldw_bytes, int64_t ldc, void* stream);
+// gs = 2688 / max |x| of a small activation (the decode linear's rows) by one
+// cluster of CTAs, writing *gs_out; lets the next kernel launch early
+// (programmatic dependent launch).  16-byte aligned rows, K % 8 == 0.
+int launch_global_scale_small(const void* x, float* gs_out, int64_t M, int64_t K, int64_t ldx, int dtype,
+                              cudaStream_t s);
 // Device address of the library's status word on the current device (kernels
 // record bounded-wait timeouts there); nullptr + error message on failure.
 int* device_status_ptr();

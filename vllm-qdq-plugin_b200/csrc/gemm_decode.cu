@@ -247,7 +247,7 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
     // (after pdl_wait either way): gs = 2688 / max |a| over the whole [M, K]
     // activation, the formula of qdq_nvfp4_global_scale, from the same
     // maximum bit pattern, so the same fp32 value.  Every CTA reads the
-    // activation (the caller passes no scale only for M <= 16 rows, resident
+    // activation (the caller passes no scale only for M <= 8 rows, resident
     // in L2) while its weight ring fills.
     float gs = 0.f;
     if (kNV) {

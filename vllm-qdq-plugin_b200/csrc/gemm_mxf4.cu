@@ -890,23 +890,30 @@ extern "C" int fp4_linear_nvf4(const void* a, int64_t lda, int dtype, const floa
   uint8_t* a_sf_t = a_sf + up(M * K / 16);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // Small M: the swap-AB decode kernel quantises the activation in its
-  // producer.  Up to 16 rows it also takes their global amax itself (every CTA
-  // reads the rows from L2, cheaper than a separate pass); above that the
-  // separate pass is cheaper than 112 CTAs reading the same rows.
+  // producer.  Without a given scale, up to 8 rows every CTA also takes their
+  // global amax itself, reading the rows (8 KB each at K = 4096) from L2 while
+  // its weight ring fills.  Above that one CTA cluster takes it first, and
+  // the decode kernel's prologue and weight prefetch overlap it through
+  // programmatic dependent launch: at N = 14336, K = 4096 the two tie at
+  // M = 9, and at M = 16 the cluster pass takes 13.8 us against 15.0 with 112
+  // CTAs reading the same 128 KB (M = 64: 28.3 us, against 34.1 with the
+  // multi-CTA atomic pass before the decode kernel).
   const bool decode = M <= 64 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 && ((lda * 2) & 15) == 0 &&
                       (reinterpret_cast<uintptr_t>(w_sf_tiled) & 15) == 0 && lda >= K && ldc >= N &&
                       ldw_bytes >= K / 2;
-  if (decode && (a_global_scale != nullptr || M <= 16))
-    return fp4_linear_decode_nvf4(a, lda, dtype, a_global_scale, w_codes, w_sf_tiled, w_global_scale, bias, c, M,
-                                  N, K, ldw_bytes, ldc, stream);
   const float* gs_a = a_global_scale;
+  if (decode) {
+    if (gs_a == nullptr && M > 8) {
+      if (int st = launch_global_scale_small(a, gs, M, K, lda, dtype, s)) return st;
+      gs_a = gs;
+    }
+    return fp4_linear_decode_nvf4(a, lda, dtype, gs_a, w_codes, w_sf_tiled, w_global_scale, bias, c, M, N, K,
+                                  ldw_bytes, ldc, stream);
+  }
   if (gs_a == nullptr) {
     if (int st = qdq_nvfp4_global_scale(a, gs, ws + 16, M, K, lda, dtype, stream)) return st;
     gs_a = gs;
   }
-  if (decode)
-    return fp4_linear_decode_nvf4(a, lda, dtype, gs_a, w_codes, w_sf_tiled, w_global_scale, bias, c, M, N, K,
-                                  ldw_bytes, ldc, stream);
   if (int st = qdq_nvfp4(a, nullptr, a_codes, a_sf, gs_a, M, K, lda, K, dtype, stream)) return st;
   if (int st = qdq_sf_tile(a_sf, a_sf_t, M, K, K / 16, 16, stream)) return st;
   return fp4_gemm_nvf4(a_codes, a_sf_t, gs_a, w_codes, w_sf_tiled, w_global_scale, bias, c, M, N, K, K / 2,

@@ -16,6 +16,7 @@
 #include <algorithm>
 
 #include "mx_quant.cuh"
+#include "sm100.cuh"
 
 namespace qdqb200 {
 namespace {
@@ -335,6 +336,55 @@ amax_gs_kernel(const uint16_t* __restrict__ x, int64_t M, int64_t K, int64_t ldx
     *gs_out = __fdiv_rn(2688.0f, F::amax_value(bits));
     ws[0] = 0;
     ws[1] = 0;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// global amax of a small activation (the NVFP4 decode linear's rows): one
+// cluster of kAmaxCtas CTAs, each reducing a strided share of the 16-byte
+// chunks; the CTAs' maxima meet in CTA 0's shared memory (distributed shared
+// memory and one cluster barrier), so neither a cleared workspace nor
+// atomics are needed.  gs = 2688 / amax from the same maximum bit pattern as
+// amax_gs_kernel, so the same fp32 value.  Launched with programmatic
+// dependent launch, it waits for the previous kernel on the stream (which may
+// write x) before reading, and lets the next kernel launch at once: that
+// kernel's prologue and weight prefetch overlap this pass, and its
+// griddepcontrol.wait orders its read of gs after this kernel's write.
+// ---------------------------------------------------------------------------
+constexpr int kAmaxCtas = 8;
+
+template <int kDtype>
+__global__ void __cluster_dims__(kAmaxCtas, 1, 1) __launch_bounds__(kThreads)
+amax_gs_small_kernel(const uint16_t* __restrict__ x, int M, int K, int64_t ldx, float* __restrict__ gs_out) {
+  using F = Fmt<kDtype>;
+  __shared__ uint32_t warp_max[kThreads / 32];
+  __shared__ uint32_t cta_max[kAmaxCtas];
+  sm100::pdl_launch_dependents();
+  sm100::pdl_wait();
+  const uint32_t rank = sm100::cluster_rank();
+  const int cpr = K / 8, total = M * cpr;
+  uint32_t m = 0;
+#pragma unroll 4
+  for (int c = static_cast<int>(rank) * kThreads + threadIdx.x; c < total; c += kAmaxCtas * kThreads) {
+    const int row = c / cpr, col = c - row * cpr;
+    m = max(m, absmax8(ld_stream(reinterpret_cast<const uint4*>(x + row * ldx + col * 8))));
+  }
+  m = __reduce_max_sync(kFull, m);
+  if ((threadIdx.x & 31u) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    uint32_t b = threadIdx.x < (kThreads / 32) ? warp_max[threadIdx.x] : 0u;
+    b = __reduce_max_sync(kFull, b);
+    if (threadIdx.x == 0)
+      asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(sm100::cluster_addr(&cta_max[rank], 0)), "r"(b)
+                   : "memory");
+  }
+  sm100::cluster_sync();  // every CTA's maximum is in CTA 0's cta_max
+  if (rank == 0 && threadIdx.x == 0) {
+    uint32_t bits = 0;
+#pragma unroll
+    for (int i = 0; i < kAmaxCtas; ++i) bits = max(bits, cta_max[i]);
+    *gs_out = __fdiv_rn(2688.0f, F::amax_value(bits));
   }
 }
 
@@ -771,6 +821,32 @@ int launch_global_scale(const void* x, float* gs_out, uint32_t* ws, int64_t M, i
     else amax_gs_kernel<QDQ_DTYPE_FP16, false><<<grid, kThreads, 0, s>>>(xp, M, K, ldx, ws, gs_out);
   }
   return check_launch("qdq_nvfp4_global_scale");
+}
+}  // namespace qdqb200
+
+namespace qdqb200 {
+// gs of a small [M, K] activation (M * K / 8 < 2^31 chunks, 16-byte aligned
+// rows, K % 8 == 0) by one CTA cluster, for the NVFP4 decode linear.
+int launch_global_scale_small(const void* x, float* gs_out, int64_t M, int64_t K, int64_t ldx, int dtype,
+                              cudaStream_t s) {
+  if (!aligned16(x) || K % 8 != 0 || ldx % 8 != 0 || M * (K / 8) >= (int64_t(1) << 31))
+    return fail(QDQ_ERR_INVALID_ARG, "global scale (small): rows must be 16-byte aligned and M*K/8 < 2^31");
+  auto* xp = static_cast<const uint16_t*>(x);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kAmaxCtas);
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int m = static_cast<int>(M), k = static_cast<int>(K);
+  cudaError_t e = dtype == QDQ_DTYPE_BF16
+                      ? cudaLaunchKernelEx(&cfg, amax_gs_small_kernel<QDQ_DTYPE_BF16>, xp, m, k, ldx, gs_out)
+                      : cudaLaunchKernelEx(&cfg, amax_gs_small_kernel<QDQ_DTYPE_FP16>, xp, m, k, ldx, gs_out);
+  if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "global scale (small): launch failed: %s", cudaGetErrorString(e));
+  return check_launch("global scale (small)");
 }
 }  // namespace qdqb200
 
