@@ -65,7 +65,8 @@ struct DLayout {
   static constexpr int ST_W = 0, ST_A = W_TILE, ST_SFW = W_TILE + A_TILE, ST_SFA = ST_SFW + SFS,
                        ST_RAW = ST_SFA + SFS;
   static constexpr int STAGE = (ST_RAW + RAW + 1023) / 1024 * 1024;
-  static constexpr int STAGES = kNA == 16 ? 7 : (kNA == 32 ? 5 : 3);
+  // as many stages as fit 227 KB (MXFP4 at NA = 16: 8 x 28 KB; NVFP4 7 x 30 KB)
+  static constexpr int STAGES = kNA == 16 ? (kNV ? 7 : 8) : (kNA == 32 ? 5 : 3);
 };
 
 struct __align__(8) DBars {
