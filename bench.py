@@ -237,13 +237,22 @@ class ClockSampler:
             return self
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        # nvidia-smi's first sample can take a second on a fresh box: wait for
+        # it, so that the samples bracket even a timed region of a few ms
+        deadline = time.time() + 5.0
+        while not self.samples and time.time() < deadline and self.proc.poll() is None:
+            time.sleep(0.02)
         return self
 
     def _read(self):
         for line in self.proc.stdout:
             self.samples.append((time.time(), [f.strip() for f in line.split(",")]))
 
-    def stop(self):
+    def stop(self, after: float | None = None):
+        if after is not None:  # one sample past the end of the timed region
+            deadline = time.time() + 1.0
+            while time.time() < deadline and not any(t > after for t, _ in self.samples):
+                time.sleep(0.02)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -256,7 +265,11 @@ class ClockSampler:
     def summary(self, t0: float, t1: float):
         if not self.samples:
             return None
-        window = [s for t, s in self.samples if t0 <= t <= t1] or [s for _, s in self.samples]
+        # samples inside the timed region; a region shorter than the 100 ms
+        # sampling period has none, and then the samples next to it count
+        inside = [s for t, s in self.samples if t0 <= t <= t1]
+        window = inside or [s for t, s in self.samples if t0 - 0.25 <= t <= t1 + 0.25] or \
+            [s for _, s in self.samples]
         mhz = [float(s[1]) for s in window if s[1].replace(".", "").isdigit()]
         mx = [float(s[2]) for s in window if s[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -264,7 +277,7 @@ class ClockSampler:
                           if len(s) > 5 + i and s[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(mhz) if mhz else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(window)}
+                "samples": len(window), "samples_inside_timed_region": len(inside)}
 
 
 # ---------------------------------------------------------------------------
@@ -334,7 +347,7 @@ def timed(ctx: Ctx, run, steps: int, graph: bool = True, clocks: bool = True):
     ms = ctx.max_ms(e0.elapsed_time(e1))
     summary = None
     if sampler:
-        sampler.stop()
+        sampler.stop(after=t1)
         summary = sampler.summary(t0, t1)
     del g
     return ms / steps, summary
