@@ -34,6 +34,7 @@ from __future__ import annotations
 
 import argparse
 import ctypes
+import contextlib
 import dataclasses
 import json
 import math
@@ -294,6 +295,7 @@ class Ctx:
     dist: object | None
     args: argparse.Namespace
     host_cpus: list | None = None  # CPUs this rank is pinned to (NVML's list for its GPU), None if unchanged
+    all_cpus: set | None = None    # the CPUs the process started with (the CPU baselines use all of them)
 
     def barrier(self):
         if self.dist is not None:
@@ -370,6 +372,20 @@ def timed_host(ctx: Ctx, step, steps: int) -> float:
 # ---------------------------------------------------------------------------
 # CPU baselines (the oracle = the reference's algorithm restated; reported only)
 # ---------------------------------------------------------------------------
+
+
+@contextlib.contextmanager
+def all_host_cpus(ctx: "Ctx"):
+    """The CPU baselines run on every core the process started with, not only
+    the GPU-local ones the rank is pinned to."""
+    if not ctx.host_cpus or not ctx.all_cpus:
+        yield
+        return
+    os.sched_setaffinity(0, ctx.all_cpus)
+    try:
+        yield
+    finally:
+        os.sched_setaffinity(0, ctx.host_cpus)
 
 
 def cpu_baseline(workload: str, x: torch.Tensor, budget_s: float = 15.0) -> dict:
@@ -796,7 +812,8 @@ def qdq_record(ctx: Ctx, workload: str, weak: bool = False, sub: bool = False) -
     if workload == "nvfp4_qdq" and not sub:
         rec["reference_gpu"] = vllm_nvfp4_gpu(ctx, xs_local=x_cpu, gs=gs, ours_ms=ms_step)
     if ctx.world == 1 and not args.no_cpu_baseline and not sub:
-        rec["cpu_baseline"] = cpu_baseline(workload, x_full)
+        with all_host_cpus(ctx):
+            rec["cpu_baseline"] = cpu_baseline(workload, x_full)
     return rec
 
 
@@ -941,7 +958,8 @@ def gemm_record(ctx: Ctx, m: int, sub: bool = False, marlin: bool = True, nv: bo
     if ref:
         rec["reference_gpu"] = ref
     if ctx.world == 1 and not args.no_cpu_baseline and not sub and not nv:
-        rec["cpu_baseline"] = cpu_gemm_sample(m)
+        with all_host_cpus(ctx):
+            rec["cpu_baseline"] = cpu_gemm_sample(m)
     return rec
 
 
@@ -1105,7 +1123,8 @@ def attn_record(ctx: Ctx, workload: str, steps: int | None = None, sub: bool = F
     if same_box:
         rec["sdpa_bf16_same_gpu"] = same_box
     if ctx.world == 1 and not args.no_cpu_baseline and not sub:
-        rec["cpu_baseline"] = cpu_attn_sample(wl, L)
+        with all_host_cpus(ctx):
+            rec["cpu_baseline"] = cpu_attn_sample(wl, L)
     return rec
 
 
@@ -1265,7 +1284,8 @@ def moe_record(ctx: Ctx, sub: bool = False) -> dict:
     }
     rec["reference_gpu"] = ref
     if ctx.world == 1 and not args.no_cpu_baseline and not sub:
-        rec["cpu_baseline"] = cpu_moe_sample(wl, m)
+        with all_host_cpus(ctx):
+            rec["cpu_baseline"] = cpu_moe_sample(wl, m)
     return rec
 
 
@@ -1302,11 +1322,12 @@ def run_ours(args) -> None:
 
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
-    host_cpus = None
-    if world > 1:  # pinned staging buffers on the GPU's own NUMA node, copies from cores near its PCIe root
-        from vllm_qdq_plugin import shard
-        host_cpus = shard.bind_to_gpu_cpus(local)
-    ctx = Ctx(world=world, rank=rank, local=local, dev=dev, dist=dist, args=args, host_cpus=host_cpus)
+    # pinned staging buffers on the GPU's own NUMA node, copies from cores near its PCIe root
+    from vllm_qdq_plugin import shard
+    all_cpus = os.sched_getaffinity(0)
+    host_cpus = shard.bind_to_gpu_cpus(local)
+    ctx = Ctx(world=world, rank=rank, local=local, dev=dev, dist=dist, args=args, host_cpus=host_cpus,
+              all_cpus=all_cpus)
     try:
         if args.workload is None:
             line = qdq_record(ctx, "nvfp4_qdq")
