@@ -465,7 +465,9 @@ __device__ void moe_segments(const int32_t* __restrict__ expert_ids, int nlive, 
   if (t == 0) seg_tab[0] = s_carry_cnt;
 }
 
-template <int kDtype>
+// Item index type: 32-bit when num_sorted * gpr_p < 2^31 (the divisions by
+// gpr_p and bs per item are then 32-bit), else 64-bit.
+template <int kDtype, typename Idx>
 __global__ void __launch_bounds__(256)
 moe_gather_quant_kernel(const uint16_t* __restrict__ a, int64_t lda, const int32_t* __restrict__ sorted_ids,
                         const int32_t* __restrict__ expert_ids, const int32_t* __restrict__ num_post_padded,
@@ -476,19 +478,20 @@ moe_gather_quant_kernel(const uint16_t* __restrict__ a, int64_t lda, const int32
   // K / 32 (up to kchunks * 4 per row, one K-256 stage) as E8M0 0 (2^-127):
   // the workspace may hold stale bytes, and a stale 0xFF (NaN) would turn the
   // padding's zero codes into NaN products.
-  const int gpr = K / 32, gpr_p = kchunks * 4;
-  const int64_t total = num_sorted * gpr_p;
+  const int gpr = K / 32;
+  const Idx gpr_p = static_cast<Idx>(kchunks) * 4;
+  const Idx total = static_cast<Idx>(num_sorted) * gpr_p;
   const int npp = __ldg(num_post_padded);
   if (blockIdx.x == 0) {
     const int64_t nb = num_sorted / bs;
     const int64_t live = npp <= 0 ? 0 : (static_cast<int64_t>(npp) + bs - 1) / bs;
     moe_segments(expert_ids, static_cast<int>(live < nb ? live : nb), num_experts, seg_tab);
   }
-  for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < total;
-       it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t p = it / gpr_p;
+  for (Idx it = static_cast<Idx>(blockIdx.x) * blockDim.x + threadIdx.x; it < total;
+       it += static_cast<Idx>(gridDim.x) * blockDim.x) {
+    const Idx p = it / gpr_p;
     const int g = static_cast<int>(it - p * gpr_p);
-    const int s = p < npp ? __ldg(sorted_ids + p) : -1;
+    const int s = p < static_cast<Idx>(max(npp, 0)) ? __ldg(sorted_ids + p) : -1;
     uint32_t code[4] = {0u, 0u, 0u, 0u};
     int e = 0;
     if (g < gpr && s >= 0 && s < n_slots) {
@@ -497,15 +500,17 @@ moe_gather_quant_kernel(const uint16_t* __restrict__ a, int64_t lda, const int32
       e = mx_group_codes<kDtype>(v, code);
     }
     if (g < gpr)
-      *reinterpret_cast<uint4*>(codes + p * (K / 2) + g * 16) = make_uint4(code[0], code[1], code[2], code[3]);
-    const int64_t b = p / bs;
-    const int r = static_cast<int>(p - b * bs);
+      *reinterpret_cast<uint4*>(codes + static_cast<int64_t>(p) * (K / 2) + g * 16) =
+          make_uint4(code[0], code[1], code[2], code[3]);
+    const Idx b = p / static_cast<Idx>(bs);
+    const int r = static_cast<int>(p - b * static_cast<Idx>(bs));
     // row r of block b sits at segment row na*i + r of the chunk of block b - i
 #pragma unroll
     for (int i = 0; i < MOE_SEG_MAX; ++i) {
       const int row = i * na + r;
-      if (row >= 128 || b < i) break;
-      sf[((b - i) * kchunks + g / 4) * 512 + (row & 31) * 16 + (row >> 5) * 4 + (g & 3)] = static_cast<uint8_t>(e);
+      if (row >= 128 || b < static_cast<Idx>(i)) break;
+      sf[(static_cast<int64_t>(b - i) * kchunks + g / 4) * 512 + (row & 31) * 16 + (row >> 5) * 4 + (g & 3)] =
+          static_cast<uint8_t>(e);
     }
   }
 }
@@ -901,16 +906,21 @@ extern "C" int fp4_moe_mxf4(const void* a, int64_t lda, int dtype, const void* w
   {
     const int64_t items = num_sorted * (K / 32);
     const int grid = static_cast<int>(std::min<int64_t>((items + 255) / 256, static_cast<int64_t>(device_sm_count()) * 8));
-    if (dtype == QDQ_DTYPE_FP16)
-      moe_gather_quant_kernel<QDQ_DTYPE_FP16><<<grid, 256, 0, s>>>(
-          ap, lda, sorted_token_ids, expert_ids, num_tokens_post_padded, num_sorted, moe_block_size, na, top_k,
-          static_cast<int>(size_m * top_k), static_cast<int>(num_experts), static_cast<int>(K), kchunks, a_codes,
-          a_sf, seg_tab);
-    else
-      moe_gather_quant_kernel<QDQ_DTYPE_BF16><<<grid, 256, 0, s>>>(
-          ap, lda, sorted_token_ids, expert_ids, num_tokens_post_padded, num_sorted, moe_block_size, na, top_k,
-          static_cast<int>(size_m * top_k), static_cast<int>(num_experts), static_cast<int>(K), kchunks, a_codes,
-          a_sf, seg_tab);
+    // 32-bit items while the last grid-stride step cannot wrap
+    const bool narrow = num_sorted * kchunks * 4 < (int64_t(1) << 31);
+#define QDQ_MOE_GATHER(DT, IDX)                                                                                  \
+  moe_gather_quant_kernel<DT, IDX><<<grid, 256, 0, s>>>(                                                         \
+      ap, lda, sorted_token_ids, expert_ids, num_tokens_post_padded, num_sorted, moe_block_size, na, top_k,      \
+      static_cast<int>(size_m * top_k), static_cast<int>(num_experts), static_cast<int>(K), kchunks, a_codes, a_sf, \
+      seg_tab)
+    if (dtype == QDQ_DTYPE_FP16) {
+      if (narrow) QDQ_MOE_GATHER(QDQ_DTYPE_FP16, uint32_t);
+      else QDQ_MOE_GATHER(QDQ_DTYPE_FP16, int64_t);
+    } else {
+      if (narrow) QDQ_MOE_GATHER(QDQ_DTYPE_BF16, uint32_t);
+      else QDQ_MOE_GATHER(QDQ_DTYPE_BF16, int64_t);
+    }
+#undef QDQ_MOE_GATHER
     if (int st = check_launch("fp4_moe_mxf4 (gather)")) return st;
   }
   // 2) grouped GEMM
