@@ -21,7 +21,7 @@
 // CTA, 10 warps:
 //   warp 0 / one lane   TMA producer: W code tile [128 rows x 128 B] (128-byte
 //                       swizzle), its scale chunks and the raw [NA, 256]
-//                       bf16/fp16 slice of A into a ring of 3-7 stages
+//                       bf16/fp16 slice of A into a ring of 3-8 stages
 //   warp 1 / one lane   MMA issuer: per stage 4 x tcgen05.mma.kind::mxf4
 //                       (M = 128, N = NA, K = 64), commit frees the stage
 //   warps 2-9           activation quantiser in 1, 2 or 4 teams (decode_teams),
