@@ -341,6 +341,10 @@ def timed(ctx: Ctx, run, steps: int, graph: bool = True, clocks: bool = True):
     ctx.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.time()
+    # A ~100 us spin kernel ahead of the start event: the host submits the
+    # steps while it runs, so the timed region holds the K steps themselves,
+    # not the host's submission latency (about 29 us for a 20-node graph).
+    torch.cuda._sleep(200_000)
     e0.record(stream)
     body()
     e1.record(stream)
