@@ -298,7 +298,19 @@ amax_gs_kernel(const uint16_t* __restrict__ x, int64_t M, int64_t K, int64_t ldx
                uint32_t* __restrict__ ws, float* __restrict__ gs_out) {
   using F = Fmt<kDtype>;
   uint32_t m = 0;
-  if (kVec) {
+  if (kVec && ldx == K) {
+    // contiguous rows: one flat run of 16-byte chunks, four loads in flight per thread
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    const uint64_t total = static_cast<uint64_t>(M) * static_cast<uint64_t>(K / 8);
+    const uint64_t step = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    uint64_t c = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; c + 3 * step < total; c += 4 * step) {
+      const uint4 v0 = ld_stream(xv + c), v1 = ld_stream(xv + c + step), v2 = ld_stream(xv + c + 2 * step),
+                  v3 = ld_stream(xv + c + 3 * step);
+      m = max(m, max(max(absmax8(v0), absmax8(v1)), max(absmax8(v2), absmax8(v3))));
+    }
+    for (; c < total; c += step) m = max(m, absmax8(ld_stream(xv + c)));
+  } else if (kVec) {
     const uint32_t cpr = static_cast<uint32_t>(K / 8);
     const uint64_t total = static_cast<uint64_t>(M) * cpr;
     for (uint64_t c = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < total;
