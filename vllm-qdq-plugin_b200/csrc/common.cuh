@@ -30,6 +30,10 @@ int device_sm_count();  // SM count of the current device (cached)
 // MXFP4 codes + E8M0 scales in the GEMM's tiled layout in one pass (K % 256 == 0).
 int qdq_mxfp4_codes_tiled(const void* x, void* codes, void* sf_tiled, int64_t M, int64_t K, int64_t ldx,
                           int dtype, void* stream);
+// NVFP4 codes + E4M3 scales in the block16 GEMM's tiled layout in one pass
+// against the device scalar *global_scale (K % 256 == 0).
+int qdq_nvfp4_codes_tiled(const void* x, const float* global_scale, void* codes, void* sf_tiled, int64_t M,
+                          int64_t K, int64_t ldx, int dtype, void* stream);
 int fp4_linear_decode(const void* a, int64_t lda, int dtype, const void* w_codes, const void* w_sf_tiled,
                       const void* bias, void* c, int64_t M, int64_t N, int64_t K, int64_t ldw_bytes,
                       int64_t ldc, void* stream);

@@ -914,8 +914,14 @@ extern "C" int fp4_linear_nvf4(const void* a, int64_t lda, int dtype, const floa
     if (int st = qdq_nvfp4_global_scale(a, gs, ws + 16, M, K, lda, dtype, stream)) return st;
     gs_a = gs;
   }
-  if (int st = qdq_nvfp4(a, nullptr, a_codes, a_sf, gs_a, M, K, lda, K, dtype, stream)) return st;
-  if (int st = qdq_sf_tile(a_sf, a_sf_t, M, K, K / 16, 16, stream)) return st;
+  // codes and tiled scales in one pass when K % 256 == 0 (rows 16-byte aligned), else codes, scales and
+  // their tiling
+  if (K % 256 == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 && lda % 8 == 0) {
+    if (int st = qdq_nvfp4_codes_tiled(a, gs_a, a_codes, a_sf_t, M, K, lda, dtype, stream)) return st;
+  } else {
+    if (int st = qdq_nvfp4(a, nullptr, a_codes, a_sf, gs_a, M, K, lda, K, dtype, stream)) return st;
+    if (int st = qdq_sf_tile(a_sf, a_sf_t, M, K, K / 16, 16, stream)) return st;
+  }
   return fp4_gemm_nvf4(a_codes, a_sf_t, gs_a, w_codes, w_sf_tiled, w_global_scale, bias, c, M, N, K, K / 2,
                        ldw_bytes, ldc, dtype, s);
 }

@@ -82,8 +82,8 @@ mxfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
         co[u] = row * static_cast<uint64_t>(ldc) + col * 4u;
         so[u] = row * static_cast<uint64_t>(lds) + (col >> 2);
       }
-      if (kTiledSF) {
-        const uint32_t row = static_cast<uint32_t>(c / cpr);
+      if (kTiledSF) {  // 32-bit division while the chunk index fits
+        const uint32_t row = total <= 0xFFFFFFFFull ? static_cast<uint32_t>(c) / cpr : static_cast<uint32_t>(c / cpr);
         const uint32_t gi = static_cast<uint32_t>(c - static_cast<uint64_t>(row) * cpr) >> 2;
         so[u] = (static_cast<uint64_t>(row >> 7) * static_cast<uint64_t>(lds) + (gi >> 2)) * 512u +
                 (row & 31u) * 16u + ((row >> 5) & 3u) * 4u + (gi & 3u);
@@ -184,13 +184,23 @@ mxfp4_generic_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
   }
 }
 
-template <int kDtype, bool kContig, bool kY, bool kCodes, bool kScales>
+// kTiledSF: the E4M3 bytes go straight to the block16 GEMM's tiled scale
+// layout (qdq_sf_tile with block 16; `lds` then holds its K-chunk count,
+// K / 64), and the kernel takes part in programmatic dependent launch as
+// the MXFP4 one does.
+template <int kDtype, bool kContig, bool kY, bool kCodes, bool kScales, bool kTiledSF = false>
 __global__ void __launch_bounds__(kThreads)
 nvfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
                  uint8_t* __restrict__ codes, uint8_t* __restrict__ scales,
                  const float* __restrict__ gsp, uint32_t cpr, uint64_t total, int64_t ldx,
                  int64_t ldy, int64_t ldc, int64_t lds, float zero) {
   using F = Fmt<kDtype>;
+  if (kTiledSF) {
+    // the fused linear's activation pass: the GEMM after it may launch at
+    // once; the activation and gs come from the kernels before it
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+  }
   const float gs = __ldg(gsp);
   const float rgs = zero_safe_recip(gs);
   const uint32_t lane = threadIdx.x & 31u;
@@ -216,6 +226,12 @@ nvfp4_vec_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y,
         yo[u] = row * static_cast<uint64_t>(ldy) + col * 8u;
         co[u] = row * static_cast<uint64_t>(ldc) + col * 4u;
         so[u] = row * static_cast<uint64_t>(lds) + (col >> 1);
+      }
+      if (kTiledSF) {  // 16-element group gi of row `row`: chunk (row / 128, gi / 4) of the tiled layout
+        const uint32_t row = total <= 0xFFFFFFFFull ? static_cast<uint32_t>(c) / cpr : static_cast<uint32_t>(c / cpr);
+        const uint32_t gi = static_cast<uint32_t>(c - static_cast<uint64_t>(row) * cpr) >> 1;
+        so[u] = (static_cast<uint64_t>(row >> 7) * static_cast<uint64_t>(lds) + (gi >> 2)) * 512u +
+                (row & 31u) * 16u + ((row >> 5) & 3u) * 4u + (gi & 3u);
       }
       v[u] = ok[u] ? ld_stream(reinterpret_cast<const uint4*>(x + xo[u])) : make_uint4(0, 0, 0, 0);
     }
@@ -688,6 +704,50 @@ namespace qdqb200 {
 // the GEMM's tiled layout (qdq_sf_tile), one pass.  K % 256 == 0 (no padded
 // K chunk), 16-byte aligned rows; scale bytes of pad rows (>= M) are left as
 // they are: the GEMM multiplies them only with the zero codes TMA fills in.
+int qdq_nvfp4_codes_tiled(const void* x, const float* global_scale, void* codes, void* sf_tiled, int64_t M,
+                          int64_t K, int64_t ldx, int dtype, void* stream) {
+  if (M <= 0 || K <= 0) return QDQ_OK;
+  if (K % 256 != 0 || !aligned16(x) || ldx % 8 != 0 || !aligned4(codes))
+    return fail(QDQ_ERR_UNSUPPORTED, "qdq_nvfp4_codes_tiled: K %% 256 and 16-byte aligned rows required");
+  const uint64_t cpr = static_cast<uint64_t>(K / 8);
+  const uint64_t total = static_cast<uint64_t>(M) * cpr;
+  if (total >= (1ull << 32) && ldx != K)
+    return fail(QDQ_ERR_UNSUPPORTED, "qdq_nvfp4_codes_tiled: too many elements for a strided input");
+  const int64_t kchunks = K / 64;  // 512-byte chunks (4 E4M3 scales of 16 elements each) per 128 rows
+  const int grid = grid_for(total, kThreads * kUnroll);
+  auto* xp = static_cast<const uint16_t*>(x);
+  auto* cp = static_cast<uint8_t*>(codes);
+  auto* sp = static_cast<uint8_t*>(sf_tiled);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see the kernel's griddepcontrol
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  uint16_t* const no_y = nullptr;
+  const int64_t ldy_ = K, ldc_ = K / 2;
+  const uint32_t cpr32 = static_cast<uint32_t>(cpr);
+  const float zero = 0.0f;
+  const bool contig = ldx == K;
+  cudaError_t e = cudaSuccess;
+#define QDQ_NV_TILED(DT, CONTIG)                                                                                 \
+  e = cudaLaunchKernelEx(&cfg, nvfp4_vec_kernel<DT, CONTIG, false, true, true, true>, xp, no_y, cp, sp,           \
+                         global_scale, cpr32, total, static_cast<int64_t>(ldx), ldy_, ldc_, kchunks, zero)
+  if (dtype == QDQ_DTYPE_BF16) {
+    if (contig) QDQ_NV_TILED(QDQ_DTYPE_BF16, true);
+    else QDQ_NV_TILED(QDQ_DTYPE_BF16, false);
+  } else {
+    if (contig) QDQ_NV_TILED(QDQ_DTYPE_FP16, true);
+    else QDQ_NV_TILED(QDQ_DTYPE_FP16, false);
+  }
+#undef QDQ_NV_TILED
+  if (e != cudaSuccess) return fail(QDQ_ERR_CUDA, "qdq_nvfp4_codes_tiled: launch: %s", cudaGetErrorString(e));
+  return check_launch("qdq_nvfp4_codes_tiled");
+}
+
 int qdq_mxfp4_codes_tiled(const void* x, void* codes, void* sf_tiled, int64_t M, int64_t K, int64_t ldx,
                           int dtype, void* stream) {
   if (M <= 0 || K <= 0) return QDQ_OK;
