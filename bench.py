@@ -900,11 +900,12 @@ def gemm_record(ctx: Ctx, m: int, sub: bool = False, marlin: bool = True, nv: bo
     wsp = torch.empty((ws_bytes,), dtype=torch.uint8, device=ctx.dev)
     out = torch.empty((ml, n), dtype=torch.bfloat16, device=ctx.dev)
     # MXFP4: one fused launch for M <= 64, else codes (+ scale tiling when K % 256 != 0) and the GEMM;
-    # NVFP4: one fused launch for M <= 8 (global amax inside), the cluster amax pass + fused launch
-    # for M <= 64, else global amax, codes with tiled scales (K % 256 == 0; else codes and a
-    # scale tiling launch), GEMM
+    # NVFP4: one fused launch for M <= 24 when N / 128 is a multiple of 4 (global amax inside),
+    # else the cluster amax pass + fused launch for M <= 64; above that global amax, codes with
+    # tiled scales (K % 256 == 0; else codes and a scale tiling launch), GEMM
     if nv:
-        per_call = 1 if ml <= 8 else (2 if ml <= 64 else (3 if k % 256 == 0 else 4))
+        in_kernel_amax = ml <= 24 and ((n + 127) // 128) % 4 == 0
+        per_call = 1 if in_kernel_amax else (2 if ml <= 64 else (3 if k % 256 == 0 else 4))
     else:
         per_call = 1 if ml <= 64 else (2 if k % 256 == 0 else 3)
 

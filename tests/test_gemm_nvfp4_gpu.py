@@ -62,13 +62,14 @@ def test_nvfp4_linear_matches_exact(cuda_device, m, n, k):
 
 
 # The activation's global scale inside the call comes from the GEMM path's
-# multi-CTA pass (M > 64), a CTA cluster's pass (8 < M <= 64) or the decode
-# kernel itself (M <= 8); all must equal nvfp4_global_scale bit for bit.
+# multi-CTA pass (M > 64), or for M <= 64 from the decode kernel's clusters of
+# 4 CTAs (M <= 24 and N / 128 a multiple of 4: n = 1024) or a separate 8-CTA
+# cluster pass; all must equal nvfp4_global_scale bit for bit.
+@pytest.mark.parametrize("n", [384, 1024])
 @pytest.mark.parametrize("m,k", [(200, 1024), (64, 1024), (24, 1024), (9, 2080), (8, 1024), (3, 288)])
-def test_nvfp4_linear_fp16_bias_and_given_global_scale(cuda_device, m, k):
+def test_nvfp4_linear_fp16_bias_and_given_global_scale(cuda_device, m, k, n):
     from vllm_qdq_plugin.gemm import nvfp4_linear
     from vllm_qdq_plugin.qdq import nvfp4_global_scale
-    n = 384
     w, codes, scales, gs = _weight(n, k, 3, cuda_device)
     a = torch.randn(m, k, generator=torch.Generator().manual_seed(1)).to(torch.float16)
     bias = torch.randn(n, generator=torch.Generator().manual_seed(2)).to(torch.float16)

@@ -78,7 +78,12 @@ struct __align__(8) DBars {
   int abort;
   int preissued;       // stages whose loads thread 0 issued before the CTA-wide sync
   uint32_t amax[8];    // NVFP4 without a given activation scale: per-warp |x| maxima (bit patterns)
+  uint32_t camax[4];   // ... and the maxima of the cluster's CTAs, written by each of them
 };
+// NVFP4 without a given activation scale (the host passes none up to 24
+// rows): the kernel runs in clusters of kDecCluster CTAs that split the
+// activation rows' global amax between them.
+constexpr int kDecCluster = 4;
 template <int kNA, bool kNV = false>
 constexpr size_t d_smem_bytes() {
   return 1024 + static_cast<size_t>(DLayout<kNA, kNV>::STAGES) * DLayout<kNA, kNV>::STAGE + sizeof(DBars);
@@ -186,6 +191,7 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
 
   if (warp == 0) {
     // ---------------- producer: W, its scales, raw A
+    if (kNV && a_gs == nullptr) cluster_sync();  // the quantiser warps' amax exchange (every thread joins)
     if (elect_one()) {
       int issued = bars->preissued;
       for (int kt = issued; kt < num_kt; ++kt) {
@@ -203,6 +209,7 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
+    if (kNV && a_gs == nullptr) cluster_sync();  // the quantiser warps' amax exchange (every thread joins)
     if (elect_one()) {
       constexpr uint32_t idesc = idesc_mxf4(DBM, kNA, !kNV);
       bool ok = true;
@@ -247,17 +254,21 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
     // NVFP4 activation scale, written by the previous kernel or computed here
     // (after pdl_wait either way): gs = 2688 / max |a| over the whole [M, K]
     // activation, the formula of qdq_nvfp4_global_scale, from the same
-    // maximum bit pattern, so the same fp32 value.  Every CTA reads the
-    // activation (the caller passes no scale only for M <= 8 rows, resident
-    // in L2) while its weight ring fills.
+    // maximum bit pattern, so the same fp32 value.  Computed here, the CTAs
+    // of a cluster each reduce every kDecCluster-th 16-byte chunk of the
+    // rows (from L2, while their weight rings fill), write their maximum
+    // into every CTA of the cluster (distributed shared memory) and meet at
+    // the cluster barrier.
     float gs = 0.f;
     if (kNV) {
       if (a_gs != nullptr) {
         gs = __ldg(a_gs);
       } else {
+        const uint32_t crank = cluster_rank();
         const int qt = threadIdx.x - 64, cpr = K / 8;  // 16-byte chunks per row
         uint32_t m8 = 0;
-        for (int i = qt; i < M * cpr; i += D_QUANT_THREADS) {
+        for (int i = qt + D_QUANT_THREADS * static_cast<int>(crank); i < M * cpr;
+             i += D_QUANT_THREADS * kDecCluster) {
           const int row = i / cpr, c = i - row * cpr;
           m8 = max(m8, absmax8(ld_stream(reinterpret_cast<const uint4*>(a_raw + row * lda + c * 8))));
         }
@@ -265,9 +276,19 @@ mxf4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
         for (int o = 16; o > 0; o >>= 1) m8 = max(m8, __shfl_xor_sync(0xffffffffu, m8, o));
         if (lane == 0) bars->amax[warp - 2] = m8;
         asm volatile("bar.sync 1, %0;" ::"n"(D_QUANT_THREADS) : "memory");  // the quantiser warps only
+        if (qt == 0) {
+          uint32_t cta = 0;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) cta = max(cta, bars->amax[w]);
+#pragma unroll
+          for (int r = 0; r < kDecCluster; ++r)
+            asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr(&bars->camax[crank], r)), "r"(cta)
+                         : "memory");
+        }
+        cluster_sync();  // every CTA's maximum is in every CTA's camax
         uint32_t all = 0;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) all = max(all, bars->amax[w]);
+        for (int r = 0; r < kDecCluster; ++r) all = max(all, bars->camax[r]);
         gs = __fdiv_rn(2688.0f, Fmt<kDtype>::amax_value(all));
       }
     }
@@ -364,11 +385,21 @@ int launch_decode(const CUtensorMap& tw, const CUtensorMap& ta, const uint8_t* s
   cfg.blockDim = dim3(D_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
+  if (kNV && a_gs == nullptr) {  // the activation's amax split over clusters of kDecCluster CTAs
+    if (cfg.gridDim.x % kDecCluster != 0)
+      return fail(QDQ_ERR_INVALID_ARG, "fp4_linear_decode: in-kernel amax needs N / 128 to be a multiple of %d",
+                  kDecCluster);
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = kDecCluster;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   const float zero = 0.0f;  // +0.0 as an operand the compiler cannot fold (see nv_scale8)
   const cudaError_t e = cudaLaunchKernelEx(&cfg, mxf4_decode_kernel<kDtype, kNA, kNV>, tw, ta, sf, bias, c,
                                            static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), ldc,

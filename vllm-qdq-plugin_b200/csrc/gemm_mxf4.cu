@@ -890,20 +890,20 @@ extern "C" int fp4_linear_nvf4(const void* a, int64_t lda, int dtype, const floa
   uint8_t* a_sf_t = a_sf + up(M * K / 16);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // Small M: the swap-AB decode kernel quantises the activation in its
-  // producer.  Without a given scale, up to 8 rows every CTA also takes their
-  // global amax itself, reading the rows (8 KB each at K = 4096) from L2 while
-  // its weight ring fills.  Above that one CTA cluster takes it first, and
-  // the decode kernel's prologue and weight prefetch overlap it through
-  // programmatic dependent launch: at N = 14336, K = 4096 the two tie at
-  // M = 9, and at M = 16 the cluster pass takes 13.8 us against 15.0 with 112
-  // CTAs reading the same 128 KB (M = 64: 28.3 us, against 34.1 with the
-  // multi-CTA atomic pass before the decode kernel).
+  // producer.  Without a given scale, up to 24 rows it also takes their global
+  // amax, split over clusters of 4 CTAs (each reads a quarter of the rows from
+  // L2 while its weight ring fills), when N / 128 is a multiple of 4.
+  // Otherwise one 8-CTA cluster pass takes it first, overlapped with the
+  // decode kernel's prologue through programmatic dependent launch.  At
+  // N = 14336, K = 4096 the first takes M = 8 / 16 / 24 to 11.1 / 13.4 /
+  // 16.7 us against 11.8 / 13.8 / 17.0 us for the second; from M = 32 the
+  // second is faster (M = 64: 28.2 against 29.4 us).
   const bool decode = M <= 64 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 && ((lda * 2) & 15) == 0 &&
                       (reinterpret_cast<uintptr_t>(w_sf_tiled) & 15) == 0 && lda >= K && ldc >= N &&
                       ldw_bytes >= K / 2;
   const float* gs_a = a_global_scale;
   if (decode) {
-    if (gs_a == nullptr && M > 8) {
+    if (gs_a == nullptr && (M > 24 || ((N + 127) / 128) % 4 != 0)) {
       if (int st = launch_global_scale_small(a, gs, M, K, lda, dtype, s)) return st;
       gs_a = gs;
     }
