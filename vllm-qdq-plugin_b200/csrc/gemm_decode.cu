@@ -9,7 +9,7 @@
 // NVFP4 mode (kNV): W carries E4M3 scales per 16 (block16 tiled layout) and a
 // tensor scale w_gs, the activation is quantised with vLLM's NVFP4 rule
 // against the per-tensor scale gs_a (given, or 2688 / max |a| computed by
-// every CTA from the rows), the MMAs are kind::mxf4nvf4.block16 and the
+// the kernel, split over clusters of CTAs), the MMAs are kind::mxf4nvf4.block16 and the
 // output is scaled by w_gs / gs_a (reference: the NVFP4 Marlin path of
 // vllm/model_executor/layers/quantization/utils/marlin_utils_fp4.py:149-202).
 //
