@@ -4,7 +4,8 @@ TEST INFRASTRUCTURE ONLY (tests/).  Nothing in the package imports it.
 
 oracle/attn.py states the numerics this build's kernels implement (real E2M1
 codes for every FP4 operand).  This module states what the reference itself
-computes for its emulated configs ("nvfp4", "mxfp4"), operation by operation
+computes for its emulated configs (every config of sage3/quant_config.py:161-311
+that runs the generic Triton kernel), operation by operation
 and with every intermediate rounded to the type the reference holds it in, so
 that the distance between the two definitions can be measured on any input
 and the reference's accumulator modes (SAGE3_ACC_DTYPE) are covered:
@@ -29,9 +30,13 @@ and the reference's accumulator modes (SAGE3_ACC_DTYPE) are covered:
                               PV accumulator, its rescale and the final division
                               in the PV dtype of the accumulator mode
                               (ACC_DTYPE_MAP, api.py:25-35)
-  sage3/p_quant_kernels.py:37-150  p_quant_nvfp4 (p * 2688, E4M3 scale per 16,
-                              2688 left in) and p_quant_mxfp4 (E8M0 scale per
-                              32, divided by 2688 at the end)
+  sage3/p_quant_kernels.py:37-283  p_quant_nvfp4 (p * 2688, E4M3 scale per 16,
+                              2688 left in), p_quant_mxfp4 (E8M0 scale per
+                              32, divided by 2688 at the end), and the
+                              single-level mxfp4_s1, mxfp4_s1_e4m3 (E4M3 scale
+                              floored at 2^-9) and mxfp8_s1 (E4M3 data)
+  sage3/transforms.py:120-138 v_smoothing (V centred on its mean over the
+                              padded sequence, the mean added to the output)
 
 Roundings are modelled as the reference's CPU torch ops make them: an op on
 bf16/fp16 operands is computed in fp32 and rounded to nearest even.  Dots and
@@ -52,9 +57,31 @@ import numpy as np
 # state stay fp32 in the modes covered here.
 PV_DTYPE = {"fp32": "f32", "bf16_pv_only": "bf16", "fp16_pv_only": "f16"}
 
-# per emulated config: (block size, scale rounding), the same for Q/K, V and P
-# (sage3/quant_config.py:161-197)
-EMULATED = {"nvfp4": (16, "e4m3"), "mxfp4": (32, "e8m0")}
+# QuantConfigs of the emulated configs (sage3/quant_config.py:161-266):
+# name -> (block size along the quantised axis, scale rounding, data format, fp_max)
+QUANT = {
+    "nvfp4": (16, "e4m3", "e2m1", 6.0),
+    "mxfp4": (32, "e8m0", "e2m1", 6.0),
+    "mxfp4_s1": (32, "e8m0", "e2m1", 6.0),
+    "mxfp8_s1": (32, "e8m0", "e4m3", 448.0),
+    "mxfp4_s1_e4m3": (32, "e4m3", "e2m1", 6.0),
+}
+
+# AttentionConfigs (quant_config.py:174-311): config -> (Q/K QuantConfig,
+# V QuantConfig, P-quant function of p_quant_kernels.py, V smoothing)
+CONFIGS = {
+    "nvfp4": ("nvfp4", "nvfp4", "nvfp4", False),
+    "mxfp4": ("mxfp4", "mxfp4", "mxfp4", False),
+    "mxfp4_s1": ("mxfp4_s1", "mxfp4_s1", "mxfp4_s1", False),
+    "mxfp8_s1": ("mxfp8_s1", "mxfp8_s1", "mxfp8_s1", False),
+    "mxfp4_s1_2level": ("mxfp4_s1", "mxfp4_s1", "mxfp4", False),
+    "mxfp4_s1_e4m3": ("mxfp4_s1_e4m3", "mxfp4_s1_e4m3", "mxfp4_s1_e4m3", False),
+    "mixed_fp8qk_fp4pv": ("mxfp8_s1", "mxfp4_s1", "mxfp4_s1", False),
+    "mixed_fp4qk_fp8pv": ("mxfp4_s1", "mxfp8_s1", "mxfp8_s1", False),
+    "mxfp4_s1_vsmooth": ("mxfp4_s1", "mxfp4_s1", "mxfp4_s1", True),
+    "mixed_fp8qk_fp4pv_vs": ("mxfp8_s1", "mxfp4_s1", "mxfp4_s1", True),
+    "mixed_fp4qk_fp8pv_vs": ("mxfp4_s1", "mxfp8_s1", "mxfp8_s1", True),
+}
 
 COMBINED_MAX = 2688.0  # 448 * 6 (p_quant_kernels.py:60-62)
 _GRID_EDGES = np.array([0.25, 0.625, 0.875, 1.25, 1.75, 2.5, 3.5, 5.0])
@@ -110,26 +137,34 @@ def _round_scale(sc: np.ndarray, how: str, dt: str) -> np.ndarray:
     return rnd(np.exp2(np.clip(np.ceil(l2), -127, 127)), dt)
 
 
-def fake_quant(x: np.ndarray, block: int, how: str, dt: str) -> np.ndarray:
-    """quantize_qk on x [..., K] with blocks along the last axis (quantize_v is
-    this on the transposed V), x holding dtype-dt values; fp32 result."""
+def fake_quant(x: np.ndarray, quant: str, dt: str) -> tuple[np.ndarray, str]:
+    """quantize_qk with QuantConfig `quant` on x [..., K], blocks along the last
+    axis (quantize_v is this on the transposed V), x holding dtype-dt values.
+    Returns the values and the dtype the reference holds them in: fp32 for
+    E2M1 data (the grid's sign tensor is fp32), the input dtype for E4M3 data
+    (apply_e4m3_quantization_torch casts back to it; the products are exact)."""
+    block, how, data, fp_max = QUANT[quant]
     sh = x.shape
     assert sh[-1] % block == 0
     xb = x.reshape(*sh[:-1], sh[-1] // block, block)
     eps = rnd(1e-8, dt)
-    sc = rnd(np.abs(xb).max(axis=-1) / np.float32(6.0), dt)
+    sc = rnd(np.abs(xb).max(axis=-1) / np.float32(fp_max), dt)
     sc = np.maximum(sc, eps)
     sc = np.maximum(_round_scale(sc, how, dt), eps)
     with np.errstate(divide="ignore", invalid="ignore"):  # fp16 rounds the 1e-8 floor to 0
         xn = rnd(xb / sc[..., None], dt)
-    return _f32(grid9(xn) * sc[..., None]).reshape(sh)
+    if data == "e4m3":
+        return rnd(rnd(_e4m3(xn), dt) * sc[..., None], dt).reshape(sh), dt
+    return _f32(grid9(xn) * sc[..., None]).reshape(sh), "f32"
 
 
 def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, config: str, dt: str):
     """One (batch, head): q, k, v float32 [L, D] holding dtype-dt values.
-    Returns the fake-quantised Q, K, V [Lp, D] (fp32), delta_s [G, Lp] (fp32)
-    and Lp, for api.py:293-343 with qk_smoothing."""
-    block, how = EMULATED[config]
+    Returns the fake-quantised Q, K, V [Lp, D] (fp32 values), delta_s [G, Lp]
+    (fp32), the dtype the reference holds the quantised Q in (its output
+    buffer has that dtype) and V's mean ([D], None without V smoothing), for
+    api.py:293-343 with the config's pre-transforms."""
+    qk_quant, pv_quant, _, vsmooth = CONFIGS[config]
     L, D = q.shape
     Lp = (L + 127) // 128 * 128
     pad = lambda a: np.concatenate([a, np.zeros((Lp - L, D), np.float32)])  # noqa: E731
@@ -140,25 +175,43 @@ def prepass(q: np.ndarray, k: np.ndarray, v: np.ndarray, config: str, dt: str):
     qmeans = rnd(q.reshape(G, 128, D).astype(np.float64).mean(axis=1), dt)
     qs = rnd(q - np.repeat(qmeans, 128, axis=0), dt)
     ds = rnd(qmeans.astype(np.float64) @ kc.astype(np.float64).T, dt)
-    qd = fake_quant(qs, block, how, dt)
-    kd = fake_quant(kc, block, how, dt)
-    vd = np.ascontiguousarray(fake_quant(np.ascontiguousarray(v.T), block, how, dt).T)
-    return qd, kd, vd, ds, Lp
+    vmean = None
+    if vsmooth:  # transforms.py:120-138, also over the padded sequence
+        vmean = rnd(v.astype(np.float64).mean(axis=0), dt)
+        v = rnd(v - vmean, dt)
+    qd, out_dt = fake_quant(qs, qk_quant, dt)
+    kd, _ = fake_quant(kc, qk_quant, dt)
+    vd = np.ascontiguousarray(fake_quant(np.ascontiguousarray(v.T), pv_quant, dt)[0].T)
+    return qd, kd, vd, ds, out_dt, vmean
 
 
-def p_quant(p: np.ndarray, config: str) -> np.ndarray:
-    """p_quant_nvfp4 / p_quant_mxfp4 on a [rows, 128] fp32 tile."""
-    block, how = EMULATED[config]
+def _e8m0_f32(b: np.ndarray) -> np.ndarray:
+    """round_to_e8m0_triton on a positive fp32 value (quant_primitives.py:123-137)."""
+    return _f32(np.exp2(np.clip(np.ceil(_f32(np.log2(b))), -127, 127)))
+
+
+def p_quant(p: np.ndarray, kind: str) -> np.ndarray:
+    """The P-quant function `kind` of p_quant_kernels.py on a [rows, 128] fp32
+    tile: the two-level nvfp4 / mxfp4 (p * 2688 first) or the single-level
+    mxfp4_s1 / mxfp4_s1_e4m3 / mxfp8_s1."""
     rows, w = p.shape
-    p1 = _f32(p * np.float32(COMBINED_MAX)).reshape(rows, w // block, block)
-    b = _f32(np.maximum(_f32(p1.max(axis=-1) / np.float32(6.0)), np.float32(1e-8)))
-    if how == "e4m3":
+    block = 16 if kind == "nvfp4" else 32
+    two_level = kind in ("nvfp4", "mxfp4")
+    p1 = _f32(p * np.float32(COMBINED_MAX)) if two_level else _f32(p)
+    p1 = p1.reshape(rows, w // block, block)
+    fp_max = np.float32(448.0 if kind == "mxfp8_s1" else 6.0)
+    b = _f32(np.maximum(_f32(p1.max(axis=-1) / fp_max), np.float32(1e-8)))
+    if kind == "nvfp4":
         s = _e4m3(b)
+    elif kind == "mxfp4_s1_e4m3":
+        s = np.maximum(_e4m3(b), np.float32(2.0 ** -9))
     else:
-        s = _f32(np.exp2(np.clip(np.ceil(_f32(np.log2(b))), -127, 127)))
+        s = _e8m0_f32(b)
     with np.errstate(divide="ignore", invalid="ignore"):  # a zero E4M3 scale gives 0 codes, as in the reference
-        pq = _f32(grid9(_f32(p1 / s[..., None])) * s[..., None])
-    if how == "e8m0":
+        pm = _f32(p1 / s[..., None])
+    codes = _e4m3(pm) if kind == "mxfp8_s1" else grid9(pm)
+    pq = _f32(codes * s[..., None])
+    if kind == "mxfp4":
         pq = _f32(pq / np.float32(COMBINED_MAX))
     return pq.reshape(rows, w)
 
@@ -186,7 +239,7 @@ def flash(qd, kd, vd, ds, sm_scale: float, config: str, acc: str) -> np.ndarray:
         alpha = np.where(np.isneginf(m), np.float32(0.0), alpha)
         o = rnd(o * rnd(alpha, pv)[:, None], pv)
         p = _f32(np.exp(_f32(s - m_new[:, None])))
-        pq = p_quant(p, config)
+        pq = p_quant(p, CONFIGS[config][2])
         pvt = rnd(_f32(rnd(pq, pv).astype(np.float64) @ vp[n0:n0 + 128].astype(np.float64)), pv)
         l = _f32(_f32(l * alpha) + _f32(pq.astype(np.float64).sum(axis=1)))
         m = m_new
@@ -202,7 +255,13 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, sm_scale: float, conf
               acc: str = "bf16_pv_only", f16: bool = False) -> np.ndarray:
     """The reference's sageattn3_standalone(q, k, v, config=config, acc_dtype=acc)
     for one (batch, head), non-causal: q, k, v float32 [L, D] holding bf16
-    (fp16 if f16) values; returns O [L, D] rounded to the input dtype."""
+    (fp16 if f16) values; returns O [L, D] rounded to the input dtype.
+    The kernel stores O / l into a buffer of the quantised Q's dtype
+    (attention_kernel.py:259, tl.store's cast), V's mean is added in that
+    dtype (api.py:369-374), and the result is cast to the input dtype."""
     dt = "f16" if f16 else "bf16"
-    qd, kd, vd, ds, _ = prepass(q, k, v, config, dt)
-    return rnd(flash(qd, kd, vd, ds, sm_scale, config, acc)[: q.shape[0]], dt)
+    qd, kd, vd, ds, out_dt, vmean = prepass(q, k, v, config, dt)
+    o = rnd(flash(qd, kd, vd, ds, sm_scale, config, acc), out_dt)
+    if vmean is not None:
+        o = rnd(o + vmean, out_dt)
+    return rnd(o[: q.shape[0]], dt)

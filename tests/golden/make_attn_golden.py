@@ -84,6 +84,20 @@ CASES = {
     "mxfp4_hw_f16_L1024": ("mxfp4_hw", "fp32", "c4", 1, 2, 1024, None, 128, "fp16"),
     "mxfp8_hw_f16_L1024": ("mxfp8_hw", "fp32", "c4", 1, 2, 1024, None, 128, "fp16"),
     "nvfp4_f16pv_L1024": ("nvfp4", "fp16_pv_only", "c5", 1, 2, 1024, None, 128, "fp16"),
+    # the rest of the reference's config vocabulary (quant_config.py:199-346):
+    # single-level, mixed-format, V-smoothed and E4M3-per-32 emulated configs,
+    # and the two mixed hardware kernels (api.py:209-291)
+    "mxfp4_s1_L512": ("mxfp4_s1", "fp32", "c4", 1, 1, 512, None),
+    "mxfp8_s1_L512": ("mxfp8_s1", "fp32", "c4", 1, 1, 512, None),
+    "mxfp4_s1_2level_L512": ("mxfp4_s1_2level", "fp32", "c4", 1, 1, 512, None),
+    "mxfp4_s1_e4m3_L512": ("mxfp4_s1_e4m3", "fp32", "c4", 1, 1, 512, None),
+    "mixed_fp8qk_fp4pv_L512": ("mixed_fp8qk_fp4pv", "fp32", "c4", 1, 1, 512, None),
+    "mixed_fp4qk_fp8pv_L512": ("mixed_fp4qk_fp8pv", "fp32", "c4", 1, 1, 512, None),
+    "mxfp4_s1_vsmooth_L512": ("mxfp4_s1_vsmooth", "fp32", "c4", 1, 1, 512, None),
+    "mixed_fp8qk_fp4pv_vs_L512": ("mixed_fp8qk_fp4pv_vs", "fp32", "c4", 1, 1, 512, None),
+    "mixed_fp4qk_fp8pv_vs_L512": ("mixed_fp4qk_fp8pv_vs", "fp32", "c4", 1, 1, 512, None),
+    "mixed_mxfp8qk_mxfp4pv_hw_L512": ("mixed_mxfp8qk_mxfp4pv_hw", "fp32", "c4", 1, 1, 512, None),
+    "mixed_mxfp4qk_mxfp8pv_hw_L512": ("mixed_mxfp4qk_mxfp8pv_hw", "fp32", "c4", 1, 1, 512, None),
 }
 
 

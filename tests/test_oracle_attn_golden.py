@@ -3,7 +3,9 @@
 tests/golden/attn_reference.npz holds outputs of the unmodified reference run
 under Triton's interpreter (tests/golden/make_attn_golden.py).  For the
 hardware configs the oracle restates the reference's kernel step for step
-(sage3/mxfp4_hw_kernel.py:167-393, sage3/mxfp8_hw_kernel.py:100-246), so run at
+(sage3/mxfp4_hw_kernel.py:167-393, sage3/mxfp8_hw_kernel.py:100-246, and the
+mixed-format kernels mixed_mxfp8qk_mxfp4pv_hw_kernel.py:133-346 and
+mixed_mxfp4qk_mxfp8pv_hw_kernel.py:114-324, which run without smoothing), so run at
 the reference's 64-key tile with its padding keys attended it must agree to
 the bf16 rounding of the reference's output (relative L2 2^-9.2 ~ 0.0017;
 fp16 inputs give an fp16 output, rounded more finely).
@@ -45,7 +47,8 @@ def _case(name):
 
 
 @pytest.mark.parametrize("name", ["mxfp4_hw_L1024", "mxfp8_hw_L1024", "mxfp4_hw_D64_L1024", "mxfp4_hw_L75600",
-                                  "mxfp4_hw_f16_L1024", "mxfp8_hw_f16_L1024"])
+                                  "mxfp4_hw_f16_L1024", "mxfp8_hw_f16_L1024",
+                                  "mixed_mxfp8qk_mxfp4pv_hw_L512", "mixed_mxfp4qk_mxfp8pv_hw_L512"])
 def test_hardware_config_oracle_reproduces_reference(name):
     config = G.CASES[name][0]
     q, k, v, rows, ref = _case(name)
@@ -67,7 +70,13 @@ def test_hardware_config_oracle_reproduces_reference(name):
         assert oa.rel_l2(got, ref[0, h]) < 2.2e-3, (name, h, oa.rel_l2(got, ref[0, h]))
 
 
-@pytest.mark.parametrize("name", ["mxfp4_L1024", "nvfp4_bf16pv_L1024", "nvfp4_D64_L1024", "nvfp4_f16pv_L1024"])
+SINGLE_LEVEL_CASES = ["mxfp4_s1_L512", "mxfp8_s1_L512", "mxfp4_s1_2level_L512", "mxfp4_s1_e4m3_L512",
+                      "mixed_fp8qk_fp4pv_L512", "mixed_fp4qk_fp8pv_L512", "mxfp4_s1_vsmooth_L512",
+                      "mixed_fp8qk_fp4pv_vs_L512", "mixed_fp4qk_fp8pv_vs_L512"]
+
+
+@pytest.mark.parametrize("name", ["mxfp4_L1024", "nvfp4_bf16pv_L1024", "nvfp4_D64_L1024", "nvfp4_f16pv_L1024"]
+                         + SINGLE_LEVEL_CASES)
 def test_emulated_config_oracle_accuracy_against_reference(name):
     config = G.CASES[name][0]
     q, k, v, rows, ref = _case(name)
@@ -81,7 +90,7 @@ def test_emulated_config_oracle_accuracy_against_reference(name):
 
 
 EMULATED_CASES = ["mxfp4_L1024", "nvfp4_bf16pv_L1024", "nvfp4_bf16pv_L4608", "nvfp4_D64_L1024",
-                  "nvfp4_f16pv_L1024"]
+                  "nvfp4_f16pv_L1024"] + SINGLE_LEVEL_CASES
 
 
 @pytest.mark.parametrize("name", EMULATED_CASES)
@@ -117,7 +126,7 @@ def test_reference_fp16_pv_only_zeroes_rows_whose_sum_overflows():
     zero_rows = int((ref == 0).all(axis=-1).sum())
     assert zero_rows > 0
     args = [t[0, 0].float().numpy() for t in (q, k, v)]
-    qd, kd, vd, ds, _ = ae.prepass(*args, "nvfp4", "f16")
+    qd, kd, vd, ds, _, _ = ae.prepass(*args, "nvfp4", "f16")
     o32 = ae.flash(qd, kd, vd, ds, 1.0 / math.sqrt(128), "nvfp4", "fp32")
     with np.errstate(over="ignore"):
         o16 = ae.flash(qd, kd, vd, ds, 1.0 / math.sqrt(128), "nvfp4", "fp16_pv_only")
