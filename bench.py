@@ -504,7 +504,6 @@ def cpu_attn_sample(wl: dict, L: int, budget_s: float = 20.0) -> dict:
         q, k, v = c4_inputs(torch.device("cpu"), L=L, H=1)
     f = lambda t: t[0, :, 0].float().numpy()  # noqa: E731
     qk_fmt, pv_fmt, emulated, pre, vsmooth, qk_smooth = oa.CONFIGS[wl["sage3"]]
-    nv, fp8 = pv_fmt == "nv4", pv_fmt == "mx8"
     block_n = oa.REF_BLOCK_N[wl["sage3"]]
     sm = 1.0 / math.sqrt(128)
     t0 = time.perf_counter()
@@ -513,8 +512,8 @@ def cpu_attn_sample(wl: dict, L: int, budget_s: float = 20.0) -> dict:
     tiles = (L + 127) // 128
     done, t0 = 0, time.perf_counter()
     while done < tiles:
-        oa.flash(qd, kd, vd, ds, L, sm, block_n=block_n, nv=nv, emulated=emulated,
-                 q_rows=slice(128 * done, 128 * done + 128), fp8=fp8, pre=pre, e4s32=pv_fmt == "nv4b32")
+        oa.flash(qd, kd, vd, ds, L, sm, block_n=block_n, emulated=emulated,
+                 q_rows=slice(128 * done, 128 * done + 128), pre=pre, **oa.p_flags(pv_fmt))
         done += 1
         if time.perf_counter() - t0 > budget_s:
             break

@@ -285,17 +285,23 @@ int64_t sage3_attn_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t D);
  *                emulated-config P handling (P scaled by 448*6 before block
  *                scaling, l = sum of quantised P), p_quant_kernels.py:37-99 and
  *                attention_kernel.py:176-186;
- *            2 = config "mxfp4": MXFP4 with the emulated-config P handling
- *                (p_quant_kernels.py:106-150);
+ *            2 = config "mxfp4": the reference's emulated MXFP4 with the
+ *                emulated-config P handling (p_quant_kernels.py:106-150).
+ *                Q/K/V follow its quantize_qk / quantize_v steps (scale
+ *                arithmetic in the input dtype, quantize.py:21-141) onto its
+ *                9-level grid {0, .5, .75, 1, 1.5, 2, 3, 4, 6}, and so does
+ *                P; 0.75 is no E2M1 value, so all of them are held as E4M3
+ *                codes with E8M0 scales per 32 (kind::mxf8f6f4 MMAs);
  *            3 = config "mxfp8_hw": MXFP8 (E4M3 + E8M0 per 32) Q/K/V and P
  *                with the reference hardware kernel's P handling,
  *                mxfp8_hw_kernel.py:88-389 (kind::mxf8f6f4 MMAs);
- *            4 = "mxfp4_s1": MXFP4, emulated P without the 448*6 prescale
+ *            4 = "mxfp4_s1": as 2, P without the 448*6 prescale
  *                (p_quant_kernels.py:158-195);
- *            5 = "mxfp8_s1": MXFP8 Q/K/V, emulated single-level MXFP8 P
- *                (p_quant_kernels.py:238-275);
- *            6 = "mixed_fp8qk_fp4pv": MXFP8 Q/K, MXFP4 P/V (single-level P);
- *            7 = "mixed_fp4qk_fp8pv": MXFP4 Q/K, MXFP8 P/V (single-level P);
+ *            5 = "mxfp8_s1": the reference's emulated MXFP8 Q/K/V (its
+ *                quantize_qk / quantize_v steps, E4M3 codes), emulated
+ *                single-level MXFP8 P (p_quant_kernels.py:238-275);
+ *            6 = "mixed_fp8qk_fp4pv": Q/K as 5, P/V as 4;
+ *            7 = "mixed_fp4qk_fp8pv": Q/K as 4, P/V as 5;
  *            8 = "mixed_mxfp8qk_mxfp4pv_hw", 9 = "mixed_mxfp4qk_mxfp8pv_hw":
  *                the mixed hardware kernels (hardware P handling);
  *           10 = "mxfp4_s1_e4m3": E2M1 with an E4M3 scale per 32 for Q/K/V

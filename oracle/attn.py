@@ -18,6 +18,10 @@ The quantised P depends on the running max at each key tile, so the tile
 width is a parameter: the sm_100a kernel uses 128, the reference kernel 64.
 Keys beyond L are masked (mask_padding=True) or, as in the reference,
 attended as zero keys (mask_padding=False).
+The reference's emulated E8M0 configs (mxfp4, mxfp4_s1, mxfp8_s1, the mixed
+and V-smoothed ones) use its own quantize_qk / quantize_v steps (formats "g9",
+"e8", from oracle/attn_emulated.py) and, for "g9" P, its 9-level grid with ties
+upward; this is what the sm_100a kernels compute for them.
 The mxfp8_hw path (sage3/api.py:114-160, mxfp8_hw_kernel.py:37-246) is the
 same with quantize_to_mxfp8 (via the C oracle, pinned by
 tests/golden/mxfp8_hw_quant.npz) and P quantised to E4M3 with
@@ -28,6 +32,7 @@ from __future__ import annotations
 
 import numpy as np
 
+from . import attn_emulated as _ae
 from . import qdq as oq
 
 E2M1 = np.array([0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6], np.float64)
@@ -144,7 +149,16 @@ def _ceil_log2(r: np.ndarray) -> np.ndarray:
 def _quant_deq(x: np.ndarray, fmt: str, f16: bool = False) -> np.ndarray:
     """Dequantised x [rows, K] in operand format fmt, blocks along K:
     "mx4" quantize_to_mxfp4, "nv4" NVFP4 per 16, "mx8" quantize_to_mxfp8,
-    "nv4b32" E2M1 with an E4M3 scale per 32."""
+    "nv4b32" E2M1 with an E4M3 scale per 32; "g9" / "e8" the reference's own
+    emulated quantize_qk steps for its mxfp4 / mxfp8_s1 QuantConfigs (9-level
+    grid or E4M3 codes, E8M0 per 32, scale arithmetic in the input dtype),
+    restated in oracle/attn_emulated.py.  An all-zero fp16 group, whose
+    reference scale underflows to 0, dequantises to 0 here, as the sm_100a
+    pre-pass writes it."""
+    if fmt in ("g9", "e8"):
+        v, _ = _ae.fake_quant(np.asarray(x, np.float32), "mxfp4_s1" if fmt == "g9" else "mxfp8_s1",
+                              "f16" if f16 else "bf16")
+        return np.nan_to_num(v.astype(np.float64), nan=0.0)
     if fmt == "nv4":
         return nv_quant_deq(x, 16, f16)
     if fmt == "nv4b32":
@@ -200,7 +214,7 @@ def vmean(v: np.ndarray, f16: bool = False) -> np.ndarray:
 def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: bool = False,
           mask_padding: bool = True, nv: bool = False, emulated: bool = False,
           q_rows: slice | None = None, fp8: bool = False, pre: float | None = None,
-          e4s32: bool = False) -> np.ndarray:
+          e4s32: bool = False, g9: bool = False) -> np.ndarray:
     """The attention loop on dequantised operands; returns O [L, D] float64
     (or the rows q_rows of it, for timing a slice of the query tiles).
 
@@ -215,7 +229,9 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
     (448*6 by default, 1 for the single-level _s1 configs).  The emulated E8M0
     scales take the reference's max(., 1e-8) before the ceiling.  e4s32=True:
     p_quant_mxfp4_s1_e4m3 (p_quant_kernels.py:197-232), E2M1 with the scale
-    max(e4m3(max(b / 6, 1e-8)), 2^-9) per 32."""
+    max(e4m3(max(b / 6, 1e-8)), 2^-9) per 32.  g9=True (with emulated): the
+    reference's p_quant_mxfp4 / p_quant_mxfp4_s1 exactly, codes on its 9-level
+    grid with ties upward instead of round-to-nearest-even E2M1."""
     Lp, D = kd.shape
     n_keys = L if mask_padding else Lp
     qk_scale = sm_scale * LOG2E
@@ -265,7 +281,8 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
             if emulated:
                 e = np.maximum(e, -26)  # ceil(log2(1e-8))
             sc = np.exp2(e.astype(np.float64))[:, :, None]
-            pq = (_rne_e2m1(pg / sc) * sc).reshape(nq, w)
+            codes = _ae.grid9(pg / sc).astype(np.float64) if g9 else _rne_e2m1(pg / sc)
+            pq = (codes * sc).reshape(nq, w)
         l = l * alpha + (pq.sum(axis=1) if emulated else p.sum(axis=1))
         acc = acc + pq @ vd[n0:n1]
         m = m_new
@@ -276,21 +293,27 @@ def flash(qd, kd, vd, ds, L: int, sm_scale: float, block_n: int = 128, causal: b
 # (reference: sage3/quant_config.py:161-330 and the hardware branches of sage3/api.py)
 CONFIGS = {
     "mxfp4_hw": ("mx4", "mx4", False, 1.0, False, True),
-    "mxfp4": ("mx4", "mx4", True, 2688.0, False, True),
-    "mxfp4_s1_2level": ("mx4", "mx4", True, 2688.0, False, True),
+    "mxfp4": ("g9", "g9", True, 2688.0, False, True),
+    "mxfp4_s1_2level": ("g9", "g9", True, 2688.0, False, True),
     "nvfp4": ("nv4", "nv4", True, 2688.0, False, True),
     "mxfp8_hw": ("mx8", "mx8", False, 1.0, False, True),
-    "mxfp4_s1": ("mx4", "mx4", True, 1.0, False, True),
-    "mxfp8_s1": ("mx8", "mx8", True, 1.0, False, True),
-    "mixed_fp8qk_fp4pv": ("mx8", "mx4", True, 1.0, False, True),
-    "mixed_fp4qk_fp8pv": ("mx4", "mx8", True, 1.0, False, True),
+    "mxfp4_s1": ("g9", "g9", True, 1.0, False, True),
+    "mxfp8_s1": ("e8", "e8", True, 1.0, False, True),
+    "mixed_fp8qk_fp4pv": ("e8", "g9", True, 1.0, False, True),
+    "mixed_fp4qk_fp8pv": ("g9", "e8", True, 1.0, False, True),
     "mixed_mxfp8qk_mxfp4pv_hw": ("mx8", "mx4", False, 1.0, False, False),
     "mixed_mxfp4qk_mxfp8pv_hw": ("mx4", "mx8", False, 1.0, False, False),
-    "mxfp4_s1_vsmooth": ("mx4", "mx4", True, 1.0, True, True),
-    "mixed_fp8qk_fp4pv_vs": ("mx8", "mx4", True, 1.0, True, True),
-    "mixed_fp4qk_fp8pv_vs": ("mx4", "mx8", True, 1.0, True, True),
+    "mxfp4_s1_vsmooth": ("g9", "g9", True, 1.0, True, True),
+    "mixed_fp8qk_fp4pv_vs": ("e8", "g9", True, 1.0, True, True),
+    "mixed_fp4qk_fp8pv_vs": ("g9", "e8", True, 1.0, True, True),
     "mxfp4_s1_e4m3": ("nv4b32", "nv4b32", True, 1.0, False, True),
 }
+
+def p_flags(pv_fmt: str) -> dict:
+    """flash()'s P-quantisation switches for a P/V operand format."""
+    return {"nv": pv_fmt == "nv4", "fp8": pv_fmt in ("mx8", "e8"), "e4s32": pv_fmt == "nv4b32",
+            "g9": pv_fmt == "g9"}
+
 
 # Key tile of the reference's online softmax per config: the mxfp4_hw kernel
 # launches with BLOCK_N = 64 (sage3/mxfp4_hw_kernel.py:437); the emulated
@@ -317,8 +340,8 @@ def attention(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, sm_sca
         k = bits_to_f32(k_bits[:, h], f16)
         v = bits_to_f32(v_bits[:, h], f16)
         qd, kd, vd, ds = prepass(q, k, v, smoothing, qk_fmt=qk_fmt, pv_fmt=pv_fmt, vsmooth=vsmooth, f16=f16)
-        out[:, h] = flash(qd, kd, vd, ds, L, sm_scale, block_n, causal, mask_padding, pv_fmt == "nv4", emulated,
-                          fp8=pv_fmt == "mx8", pre=pre, e4s32=pv_fmt == "nv4b32")
+        out[:, h] = flash(qd, kd, vd, ds, L, sm_scale, block_n, causal, mask_padding, emulated=emulated, pre=pre,
+                          **p_flags(pv_fmt))
         if vsmooth:
             out[:, h] += vmean(v, f16)
     return out
@@ -339,9 +362,8 @@ def attention_rows(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, s
     rows = np.asarray(rows)
     out = np.zeros((len(rows), q.shape[1]))
     for t in np.unique(rows // 128):
-        o = flash(qd, kd, vd, ds, L, sm_scale, block_n, False, mask_padding, pv_fmt == "nv4", emulated,
-                  q_rows=slice(128 * t, 128 * t + 128), fp8=pv_fmt == "mx8", pre=pre,
-                  e4s32=pv_fmt == "nv4b32")
+        o = flash(qd, kd, vd, ds, L, sm_scale, block_n, False, mask_padding, emulated=emulated,
+                  q_rows=slice(128 * t, 128 * t + 128), pre=pre, **p_flags(pv_fmt))
         sel = rows // 128 == t
         out[sel] = o[rows[sel] - 128 * t]
         if vsmooth:

@@ -2,8 +2,9 @@
 
 TEST INFRASTRUCTURE ONLY (tests/).  Nothing in the package imports it.
 
-oracle/attn.py states the numerics this build's kernels implement (real E2M1
-codes for every FP4 operand).  This module states what the reference itself
+oracle/attn.py states the numerics this build's kernels implement (the
+reference's own grid for the emulated E8M0 configs, real E2M1 codes for
+nvfp4 and mxfp4_s1_e4m3).  This module states what the reference itself
 computes for its emulated configs (every config of sage3/quant_config.py:161-311
 that runs the generic Triton kernel), operation by operation
 and with every intermediate rounded to the type the reference holds it in, so

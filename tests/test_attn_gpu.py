@@ -144,11 +144,14 @@ def test_v_smoothing_reduces_error(cuda_device):
 
 
 @pytest.mark.parametrize("config", ["mixed_fp8qk_fp4pv", "mixed_mxfp4qk_mxfp8pv_hw", "mxfp4_s1_vsmooth",
-                                    "mxfp4_s1_e4m3"])
+                                    "mxfp4_s1_e4m3", "mxfp4", "mxfp8_s1"])
 def test_new_config_prepass_codes_bit_exact(cuda_device, config):
     """The pre-pass codes and scales of q_s, k_c and V (mean-subtracted for the
     V-smoothed configs), read back from the workspace, dequantise to exactly
-    the oracle's values in each operand format."""
+    the oracle's values in each operand format; for the emulated E8M0 configs
+    (mxfp4, mxfp8_s1, the mixed and V-smoothed ones) those are the
+    reference's own quantize_qk / quantize_v values (9-level grid or E4M3,
+    scale arithmetic in bf16)."""
     import ctypes
     from vllm_qdq_plugin import _native
     from vllm_qdq_plugin.sage3_attn.sage3 import api
@@ -169,10 +172,11 @@ def test_new_config_prepass_codes_bit_exact(cuda_device, config):
     w = ws.cpu().numpy()
     Lp, G = 384, 3
     up = lambda n: (n + 255) // 256 * 256  # noqa: E731
-    row = lambda fmt: 128 if fmt == "mx8" else 64  # noqa: E731
+    e4m3 = ("mx8", "g9", "e8")  # formats held as E4M3 codes (the 9-level grid values are E4M3 values)
+    row = lambda fmt: 128 if fmt in e4m3 else 64  # noqa: E731
 
     def deq(fmt, c, sc):
-        if fmt == "mx8":
+        if fmt in e4m3:
             return oa._deq8(c, sc)
         if fmt == "nv4b32":  # E2M1 codes, E4M3 scale bytes per 32
             vals = np.stack([oa.E2M1[c & 0xF], oa.E2M1[c >> 4]], axis=-1).reshape(c.shape[0], -1)
@@ -192,7 +196,7 @@ def test_new_config_prepass_codes_bit_exact(cuda_device, config):
     qsf = sf(w[off:]); off += up(G * 1024)
     kc = w[off: off + Lp * row(qk_fmt)].reshape(Lp, row(qk_fmt)); off += up(Lp * 128)
     ksf = sf(w[off:]); off += up(G * 1024)
-    vrow = Lp if pv_fmt == "mx8" else Lp // 2
+    vrow = Lp if pv_fmt in e4m3 else Lp // 2
     vt = w[off: off + 128 * vrow].reshape(128, vrow); off += up(128 * Lp)
     vsf = sf(w[off:]).reshape(G, 128, 4).transpose(1, 0, 2).reshape(128, G * 4)
     f = lambda t: oa.bf16_bits_to_f32(_bits(t[0, :, 0]))  # noqa: E731

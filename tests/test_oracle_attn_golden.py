@@ -9,10 +9,12 @@ mixed_mxfp4qk_mxfp8pv_hw_kernel.py:114-324, which run without smoothing), so run
 the reference's 64-key tile with its padding keys attended it must agree to
 the bf16 rounding of the reference's output (relative L2 2^-9.2 ~ 0.0017;
 fp16 inputs give an fp16 output, rounded more finely).
-For the emulated configs oracle/attn.py states this build's definition (real
-E2M1 codes where the reference fake-quantises on a 9-level grid), so only its
-accuracy is held against the reference's: err <= 1.1 * err(reference) + 0.005
-against float64 attention.  What the reference computes for those configs is
+For the emulated configs with E4M3 block scales (nvfp4, mxfp4_s1_e4m3)
+oracle/attn.py states this build's definition (real E2M1 codes where the
+reference fake-quantises on a 9-level grid), so only their accuracy is held
+against the reference's: err <= 1.1 * err(reference) + 0.005 against float64
+attention.  The emulated E8M0 configs compute the reference's own grid, and
+their statement reproduces its outputs to their bf16 rounding.  What the reference computes for those configs is
 restated separately, op by op, by oracle/attn_emulated.py (9-level grid,
 input-dtype scale arithmetic, the bf16 / fp16 PV accumulator of
 `bf16_pv_only` / `fp16_pv_only`); it reproduces the fixture's outputs bit for
@@ -164,3 +166,24 @@ def test_emulated_definition_accuracy_on_ragged_lengths(config, acc, dist, L):
     ref = ae.attention(*(t.float().numpy() for t in (q, k, v)), sm, config=config, acc=acc)
     e_ours, e_ref = oa.rel_l2(ours, ex), oa.rel_l2(ref, ex)
     assert e_ours <= 1.1 * e_ref + 0.005, (config, L, e_ours, e_ref)
+
+
+E8M0_EMULATED_CASES = ["mxfp4_L1024", "mxfp4_s1_L512", "mxfp8_s1_L512", "mxfp4_s1_2level_L512",
+                       "mixed_fp8qk_fp4pv_L512", "mixed_fp4qk_fp8pv_L512", "mxfp4_s1_vsmooth_L512",
+                       "mixed_fp8qk_fp4pv_vs_L512", "mixed_fp4qk_fp8pv_vs_L512"]
+
+
+@pytest.mark.parametrize("name", E8M0_EMULATED_CASES)
+def test_emulated_e8m0_definition_reproduces_reference(name):
+    """For the emulated E8M0 configs this build computes the reference's own
+    numerics (its quantize_qk / quantize_v steps and 9-level grid, held as
+    E4M3 codes), so oracle/attn.py's statement of the kernels, run at the
+    kernel's 128-key tile, reproduces the reference's outputs to their bf16
+    rounding (relative L2 2^-9.2 ~ 0.0017; 0.0023 for mixed_fp8qk_fp4pv_vs,
+    whose output the reference rounds to bf16 twice)."""
+    config = G.CASES[name][0]
+    q, k, v, rows, ref = _case(name)
+    for h in range(q.shape[1]):
+        bits = [t[0, h].contiguous().view(torch.int16).numpy().view(np.uint16)[:, None, :] for t in (q, k, v)]
+        got = oa.attention(*bits, 1.0 / math.sqrt(q.shape[-1]), config=config, block_n=128)[:, 0]
+        assert oa.rel_l2(got, ref[0, h]) < 2.5e-3, (name, h, oa.rel_l2(got, ref[0, h]))

@@ -27,12 +27,12 @@ extern "C" int sage3_fp4_attn(const void* q, const void* k, const void* v, void*
   static const Variant kVariants[] = {
       {attn::F_MX4, attn::F_MX4, 0, 1.f},      // 0 mxfp4_hw
       {attn::F_NV4, attn::F_NV4, 1, 2688.f},   // 1 nvfp4
-      {attn::F_MX4, attn::F_MX4, 1, 2688.f},   // 2 mxfp4 (= mxfp4_s1_2level)
+      {attn::F_G9, attn::F_G9, 1, 2688.f},     // 2 mxfp4 (= mxfp4_s1_2level)
       {attn::F_MX8, attn::F_MX8, 0, 1.f},      // 3 mxfp8_hw
-      {attn::F_MX4, attn::F_MX4, 1, 1.f},      // 4 mxfp4_s1
-      {attn::F_MX8, attn::F_MX8, 1, 1.f},      // 5 mxfp8_s1
-      {attn::F_MX8, attn::F_MX4, 1, 1.f},      // 6 mixed_fp8qk_fp4pv
-      {attn::F_MX4, attn::F_MX8, 1, 1.f},      // 7 mixed_fp4qk_fp8pv
+      {attn::F_G9, attn::F_G9, 1, 1.f},        // 4 mxfp4_s1
+      {attn::F_E8, attn::F_E8, 1, 1.f},        // 5 mxfp8_s1
+      {attn::F_E8, attn::F_G9, 1, 1.f},        // 6 mixed_fp8qk_fp4pv
+      {attn::F_G9, attn::F_E8, 1, 1.f},        // 7 mixed_fp4qk_fp8pv
       {attn::F_MX8, attn::F_MX4, 0, 1.f},      // 8 mixed_mxfp8qk_mxfp4pv_hw
       {attn::F_MX4, attn::F_MX8, 0, 1.f},      // 9 mixed_mxfp4qk_mxfp8pv_hw
       {attn::F_NV4B32, attn::F_NV4B32, 1, 1.f},  // 10 mxfp4_s1_e4m3

@@ -13,10 +13,18 @@ enum Fmt : int {
   F_MX8 = 2,  // E4M3 + E8M0 per 32 (kind::mxf8f6f4), 128-byte code rows
   F_NV4B32 = 3,  // E2M1 + E4M3 per 32: run as block16 (kind::mxf4nvf4) with each
                  // scale in both of its 16-element slots, 64-byte code rows
+  // The reference's emulated E8M0 QuantConfigs, quantised with its own steps
+  // (scale arithmetic in the input dtype, quantize.py:21-141) and stored as
+  // E4M3 codes + E8M0 per 32, run like F_MX8 (kind::mxf8f6f4, 128-byte rows):
+  F_G9 = 4,  // E2M1 configs: the 9 magnitudes {0, .5, .75, 1, 1.5, 2, 3, 4, 6}
+             // (quant_primitives.py:52-71; 0.75 is not E2M1, every one is E4M3)
+  F_E8 = 5,  // E4M3 configs (mxfp8_s1): E4M3 codes, round to nearest even
 };
 
 // Formats whose MMA is kind::mxf4nvf4.block16 (two 512-byte scale chunks per 128 K).
 __host__ __device__ constexpr bool fmt_block16(int f) { return f == F_NV4 || f == F_NV4B32; }
+// Formats held as E4M3 codes (128-byte rows, kind::mxf8f6f4).
+__host__ __device__ constexpr bool fmt_e4m3(int f) { return f == F_MX8 || f == F_G9 || f == F_E8; }
 
 // One attention problem: Q, K, V, O in the NHD layout [B, L, H, D] (D = 128,
 // element stride 1) with arbitrary batch / token / head strides (elements).
@@ -46,7 +54,7 @@ struct Problem {
 struct Workspace {
   float* ksum;            // [BH, 128]
   __nv_bfloat16* qmean;   // [BH, G, 128]
-  uint8_t* qc;            // [BH * Lp, 64] (E2M1) or [BH * Lp, 128] (E4M3)
+  uint8_t* qc;            // [BH * Lp, 64] (E2M1) or [BH * Lp, 128] (E4M3 formats)
   uint8_t* qsf;           // [BH * Lp / 128, 1024]
   uint8_t* kc;            // as qc
   uint8_t* ksf;           // [BH * Lp / 128, 1024]

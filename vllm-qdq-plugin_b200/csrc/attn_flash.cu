@@ -124,7 +124,7 @@ struct FL {
                 "128-byte-swizzle atoms of the delta_s operands must be 1024-byte aligned");
   static_assert(OFF_ZERO - OFF_STAGE < (1 << 18), "descriptor byte offsets are 14-bit multiples of 16");
 };
-__host__ __device__ constexpr int fmt_row(int f) { return f == F_MX8 ? 128 : 64; }
+__host__ __device__ constexpr int fmt_row(int f) { return fmt_e4m3(f) ? 128 : 64; }
 template <int kQK, int kPV>
 using FLay = FL<fmt_row(kQK), fmt_row(kPV)>;
 __device__ __forceinline__ uint64_t code_desc(bool f8, const void* p) {
@@ -235,7 +235,7 @@ template <int kFmt>
 __device__ __forceinline__ void mma_k128(uint32_t d, uint64_t da, uint64_t db, uint32_t sfa, uint32_t sfb,
                                          bool accumulate_first) {
   constexpr bool kNV = fmt_block16(kFmt);
-  if (kFmt == F_MX8) {
+  if (fmt_e4m3(kFmt)) {
     constexpr uint32_t idesc8 = idesc_mxf8(BM, BN);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {  // 32 E4M3 = 32 bytes per step; scale byte kk of the chunk
@@ -287,6 +287,16 @@ __device__ __forceinline__ float max32(const float* v) {
 // ---------------------------------------------------------------------------
 // softmax warpgroup: one query tile, thread = row
 // ---------------------------------------------------------------------------
+// The reference's 9-level grid for a >= 0 (quant_primitives.py:52-71): 0
+// below 0.25, 0.5 below 0.5, and from 0.5 up the value rounded to one
+// mantissa bit with ties upward (half of that bit added to the fp32 pattern),
+// capped at 6; the grid's midpoints are exactly those ties.  Every result is
+// an E4M3 value.
+__device__ __forceinline__ float grid9_mag(float a) {
+  const float r = __uint_as_float((__float_as_uint(a) + 0x00200000u) & 0xFFC00000u);
+  return a < 0.5f ? (a < 0.25f ? 0.0f : 0.5f) : fminf(r, 6.0f);
+}
+
 // Sum of four E4M3 bytes (exact in fp32).
 __device__ __forceinline__ float e4m3x4_sum(uint32_t w) {
   uint32_t h0, h1;
@@ -323,7 +333,8 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
                                            int quad, int qt, int bh, int nkv, __nv_bfloat16* __restrict__ out,
                                            int* status) {
   constexpr bool kNV = kPV == F_NV4;
-  constexpr bool kP8 = kPV == F_MX8;
+  constexpr bool kP8 = fmt_e4m3(kPV);
+  constexpr bool kG9 = kPV == F_G9;          // the reference's 9-level grid, as E4M3 codes
   constexpr bool kE4S32 = kPV == F_NV4B32;   // E4M3 scale per 32 keys
   using Lay = FLay<kQK, kPV>;
   constexpr int NG = kNV ? 8 : 4;            // scale blocks per row of 128 keys
@@ -462,6 +473,8 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
       // e = clamp(ceil(log2(max(max p / 448, 1e-8))), -127, 127), E4M3 codes
       // of p * 2^-e (the fp8 cast, round-to-nearest-even); l += sum of the
       // dequantised P.
+      // kG9 (p_quant_mxfp4 / p_quant_mxfp4_s1): the same with max / 6 and the
+      // reference's 9-level grid (ties upward), held as E4M3 codes.
       // The prescale and 2^-e are folded into the exponent:
       // p * prescale * 2^-e = exp2(x * qk - m + log2(prescale) - e).
       uint32_t sfw = 0;
@@ -470,7 +483,7 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
       for (int g = 0; g < NGH; ++g) {
         const int gg = hf * NGH + g;
         const float amax = __fmul_rn(ex2_approx(fmaf(gm[g], qk, -m_new)), p.p_prescale);
-        const int e = max(mx8_block_exp(amax), -26);  // ceil(log2(1e-8)) = -26
+        const int e = max(kG9 ? mx_block_exp(amax) : mx8_block_exp(amax), -26);  // ceil(log2(1e-8)) = -26
         const float cg = p.p_prescale_lg2 - m_new - static_cast<float>(e);
         const float2 c2 = make_float2(cg, cg);
         uint32_t w[8];
@@ -484,6 +497,10 @@ __device__ __forceinline__ void softmax_wg(uint8_t* smem, Bars* bars, uint32_t t
             const float2 t = fma_f32x2(make_float2(x[n], x[n + 1]), qk2, c2);
             v[2 * i] = ex2_approx(t.x);
             v[2 * i + 1] = ex2_approx(t.y);
+          }
+          if (kG9) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = grid9_mag(v[i]);
           }
           w[q] = cvt_e4m3x4(v[0], v[1], v[2], v[3]);
           gsum += e4m3x4_sum(w[q]);
@@ -647,7 +664,7 @@ sage3_fp4_flash_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_c
                        const uint8_t* __restrict__ qsf, const uint8_t* __restrict__ ksf,
                        const uint8_t* __restrict__ vsf, __nv_bfloat16* __restrict__ out, Params p, int* status) {
   constexpr bool kNVq = fmt_block16(kQK), kNVp = fmt_block16(kPV);   // two scale chunks per tile
-  constexpr bool kQ8 = kQK == F_MX8, kP8 = kPV == F_MX8;     // 128-byte code rows
+  constexpr bool kQ8 = fmt_e4m3(kQK), kP8 = fmt_e4m3(kPV);  // 128-byte code rows
   using Lay = FLay<kQK, kPV>;
   constexpr int STAGES = Lay::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -880,7 +897,7 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   int* status = device_status_ptr();
   if (status == nullptr) return QDQ_ERR_CUDA;
   const int64_t BH = static_cast<int64_t>(pr.B) * pr.H;
-  const bool q8 = pr.qk_fmt == F_MX8, p8 = pr.pv_fmt == F_MX8;
+  const bool q8 = fmt_e4m3(pr.qk_fmt), p8 = fmt_e4m3(pr.pv_fmt);
   CUtensorMap mq, mk, mv, mds;
   if (int st = code_map(&mq, w.qc, BH * pr.Lp, q8 ? 128 : 64, q8)) return st;
   if (int st = code_map(&mk, w.kc, BH * pr.Lp, q8 ? 128 : 64, q8)) return st;
@@ -906,16 +923,19 @@ int launch_flash(const Problem& pr, const Workspace& w, cudaStream_t s) {
   p.vmean = w.vmean;
   p.f16 = pr.f16;
   dim3 grid(static_cast<unsigned>((p.T + 1) / 2), static_cast<unsigned>(BH));
+  // The flash kernel sees Q / K codes of every E4M3 format alike (F_G9, F_E8
+  // and F_MX8 differ only in how the pre-pass quantised them), and P / V of
+  // F_E8 like F_MX8; F_G9 P / V keeps its own P quantiser.
+  const int qk_fmt = fmt_e4m3(pr.qk_fmt) ? static_cast<int>(F_MX8) : pr.qk_fmt;
+  const int pv_fmt = pr.pv_fmt == F_E8 ? static_cast<int>(F_MX8) : pr.pv_fmt;
 #define QDQ_FLASH(QK, PV, EMU)                                                             \
-  if (pr.qk_fmt == QK && pr.pv_fmt == PV && (pr.emulated != 0) == EMU)                     \
+  if (qk_fmt == QK && pv_fmt == PV && (pr.emulated != 0) == EMU)                           \
     return launch_mode<QK, PV, EMU>(mq, mk, mv, mds, w, pr, p, grid, status, s);
   QDQ_FLASH(F_MX4, F_MX4, false)   // mxfp4_hw
-  QDQ_FLASH(F_MX4, F_MX4, true)    // mxfp4, mxfp4_s1 (+ vsmooth)
   QDQ_FLASH(F_NV4, F_NV4, true)    // nvfp4
   QDQ_FLASH(F_MX8, F_MX8, false)   // mxfp8_hw
-  QDQ_FLASH(F_MX8, F_MX8, true)    // mxfp8_s1
-  QDQ_FLASH(F_MX8, F_MX4, true)    // mixed_fp8qk_fp4pv (+ _vs)
-  QDQ_FLASH(F_MX4, F_MX8, true)    // mixed_fp4qk_fp8pv (+ _vs)
+  QDQ_FLASH(F_MX8, F_MX8, true)    // mxfp8_s1, mixed_fp4qk_fp8pv (+ _vs)
+  QDQ_FLASH(F_MX8, F_G9, true)     // mxfp4, mxfp4_s1 (+ vsmooth), mixed_fp8qk_fp4pv (+ _vs)
   QDQ_FLASH(F_MX8, F_MX4, false)   // mixed_mxfp8qk_mxfp4pv_hw
   QDQ_FLASH(F_MX4, F_MX8, false)   // mixed_mxfp4qk_mxfp8pv_hw
   QDQ_FLASH(F_NV4B32, F_NV4B32, true)  // mxfp4_s1_e4m3

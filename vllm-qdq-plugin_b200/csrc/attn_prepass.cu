@@ -21,6 +21,10 @@
 //   quantize_to_mxfp8 (sage3/mxfp8_hw_kernel.py:37-65):
 //     e = ceil(log2(max(amax, 1e-12) / 448)), byte clamp(e + 127, 0, 254),
 //     code = E4M3 of x / 2^e, round-to-nearest-even (torch's float8_e4m3fn cast).
+//   The emulated E8M0 configs (mxfp4, mxfp4_s1, mxfp8_s1 and the mixed ones,
+//   formats F_G9 / F_E8) quantise q_s, k_c and V with the reference's own
+//   quantize_qk / quantize_v steps instead (emu8_quant32 below), into E4M3
+//   codes with E8M0 scales.
 //
 // Head dims D < 128 (32, 64, 96) are zero-extended to 128 as the rows are
 // loaded: the extra channels are zero in Q, K and V, so they add nothing to
@@ -126,6 +130,60 @@ __device__ __forceinline__ uint32_t mx8_quant32(const float* v, uint8_t* out) {
 
 
 
+// The 9-level grid of the reference's emulated E2M1 (quant_primitives.py:52-71)
+// for a >= 0: 0 below 0.25, 0.5 below 0.5, and from 0.5 up the value rounded
+// to one mantissa bit with ties upward (adding half of that bit to the fp32
+// pattern), capped at 6.  The midpoints 0.625, 0.875, 1.25, 1.75, 2.5, 3.5
+// and 5 are exactly the one-bit ties, so every threshold `a < t` of the
+// reference's compare chain is reproduced.  Every result is an E4M3 value.
+__device__ __forceinline__ float grid9_mag(float a) {
+  const float r = __uint_as_float((__float_as_uint(a) + 0x00200000u) & 0xFFC00000u);
+  return a < 0.5f ? (a < 0.25f ? 0.0f : 0.5f) : fminf(r, 6.0f);
+}
+
+// One 32-element group of the reference's emulated E8M0 QuantConfigs
+// (quantize_qk / quantize_v, quantize.py:21-141, with round_to_e8m0_torch,
+// quant_primitives.py:140-151), every step in the input dtype T:
+//   sc = max(T(amax / fp_max), T(1e-8));
+//   e  = clamp(ceil(T(log2(sc))), -127, 127): the logarithm rounded to fp32
+//        and then to T, as torch evaluates it on a T tensor (computed here in
+//        double precision and rounded once to fp32; over every bf16 and fp16
+//        sc its bf16 / fp16 rounding equals torch's);
+//   codes = grid9(T(x / 2^e)) (kGrid9, fp_max 6) or the E4M3 cast of T(x / 2^e)
+//        (fp_max 448, round to nearest even), stored as E4M3 bytes;
+// returns the E8M0 byte e + 127.  x / 2^e is exact, so T(x / 2^e) is x * 2^-e
+// rounded to T (a no-op except at the bottom of fp16's range).  With fp16
+// inputs an all-zero group has sc = 0, for which the reference divides by a
+// zero scale; its codes here are 0 (so is the reference's E2M1 result).
+template <bool kGrid9, bool kF16>
+__device__ __forceinline__ uint32_t emu8_quant32(const float* v, uint8_t* out) {
+  using E = In16<kF16>;
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const float sc = fmaxf(E::round(__fdiv_rn(amax, kGrid9 ? 6.0f : 448.0f)), E::round(1e-8f));
+  int e = -127;
+  if (sc > 0.f) {
+    const float lg = E::round(static_cast<float>(log2(static_cast<double>(sc))));
+    e = min(max(static_cast<int>(ceilf(lg)), -127), 127);
+  }
+  const float inv = sc > 0.f ? exp2_neg(e) : 0.f;
+  uint32_t w[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    float t[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float xn = E::round(v[4 * q + i] * inv);
+      t[i] = kGrid9 ? copysignf(grid9_mag(fabsf(xn)), xn) : xn;
+    }
+    w[q] = cvt_e4m3x4(t[0], t[1], t[2], t[3]);
+  }
+  reinterpret_cast<uint4*>(out)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  reinterpret_cast<uint4*>(out)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  return static_cast<uint32_t>(e + 127);
+}
+
 __device__ __forceinline__ int64_t nhd_row(int b, int n, int h, int64_t sb, int64_t sn, int64_t sh) {
   return b * sb + n * sn + h * sh;
 }
@@ -202,6 +260,8 @@ __device__ __forceinline__ void quant_group(const float* v, uint8_t* crow, uint8
   const int slot = (r % 32) * 16 + (r / 32) * 4;
   if (kFmt == F_MX8) {
     sft[slot + g] = static_cast<uint8_t>(mx8_quant32(v, crow));
+  } else if (kFmt == F_G9 || kFmt == F_E8) {
+    sft[slot + g] = static_cast<uint8_t>(emu8_quant32<kFmt == F_G9, kF16>(v, crow));
   } else if (kFmt == F_NV4) {
     sft[(g / 4) * 512 + slot + (g % 4)] = static_cast<uint8_t>(nv_quant_fast<16, kF16>(v, crow));
   } else if (kFmt == F_NV4B32) {
@@ -384,7 +444,7 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
         v[q * 8 + 2 * j + 1] = In16<kF16>::hi(w[j]);
       }
     }
-    uint8_t* crow = kFmt == F_MX8 ? codes + (static_cast<int64_t>(bh) * Lp + n) * 128 + g * 32
+    uint8_t* crow = fmt_e4m3(kFmt) ? codes + (static_cast<int64_t>(bh) * Lp + n) * 128 + g * 32
                                   : codes + (static_cast<int64_t>(bh) * Lp + n) * 64 + g * (kGs / 2);
     quant_group<kFmt, kF16>(v, crow, sft, r, g);
   }
@@ -402,7 +462,7 @@ __global__ void __launch_bounds__(256) qk_quant_kernel(const __nv_bfloat16* __re
 // written row by row in 16-byte pieces (coalesced).
 constexpr int V_TILE_BYTES = 128 * (128 + 8) * 2;
 template <int kFmt>
-__host__ __device__ constexpr int v_code_ld() { return (kFmt == F_MX8 ? 128 : 64) + 16; }  // staged code row (bytes, padded)
+__host__ __device__ constexpr int v_code_ld() { return (fmt_e4m3(kFmt) ? 128 : 64) + 16; }  // staged code row (bytes, padded)
 template <int kFmt>
 __host__ __device__ constexpr int v_smem_bytes() { return V_TILE_BYTES + 128 * v_code_ld<kFmt>(); }
 
@@ -433,7 +493,7 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
   }
   __syncthreads();
   const int d = threadIdx.x;
-  constexpr bool kF8 = kFmt == F_MX8;
+  constexpr bool kF8 = fmt_e4m3(kFmt);
   // V smoothing (transforms.py v_smoothing): quantise dtype(v - mean_L(v)); the
   // flash epilogue adds the mean back.  Padding rows stay zero.
   using E = In16<kF16>;
@@ -474,7 +534,10 @@ __global__ void __launch_bounds__(128) v_quant_kernel(const __nv_bfloat16* __res
       float x[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) x[i] = E::val(tile[g * 32 + i][d]);
-      sfw |= (kF8 ? mx8_quant32(x, row + g * 32) : mx_quant32_bf(x, row + g * 16)) << (8 * g);
+      uint32_t sb;
+      if (kFmt == F_G9 || kFmt == F_E8) sb = emu8_quant32<kFmt == F_G9, kF16>(x, row + g * 32);
+      else sb = kF8 ? mx8_quant32(x, row + g * 32) : mx_quant32_bf(x, row + g * 16);
+      sfw |= sb << (8 * g);
     }
     *reinterpret_cast<uint32_t*>(sft) = sfw;
   }
@@ -641,6 +704,8 @@ int launch_prepass_t(const Problem& p, const Workspace& w, cudaStream_t s) {
   int st = QDQ_OK;
   switch (p.qk_fmt) {
     case F_MX8: st = launch_qk<F_MX8, kF16>(p, w, s); break;
+    case F_G9: st = launch_qk<F_G9, kF16>(p, w, s); break;
+    case F_E8: st = launch_qk<F_E8, kF16>(p, w, s); break;
     case F_NV4: st = launch_qk<F_NV4, kF16>(p, w, s); break;
     case F_NV4B32: st = launch_qk<F_NV4B32, kF16>(p, w, s); break;
     default: st = launch_qk<F_MX4, kF16>(p, w, s); break;
@@ -650,6 +715,8 @@ int launch_prepass_t(const Problem& p, const Workspace& w, cudaStream_t s) {
   const float* vs = p.vsmooth ? w.vsum : nullptr;
   switch (p.pv_fmt) {
     case F_MX8: st = launch_v<F_MX8, kF16>(p, w, vs, s); break;
+    case F_G9: st = launch_v<F_G9, kF16>(p, w, vs, s); break;
+    case F_E8: st = launch_v<F_E8, kF16>(p, w, vs, s); break;
     case F_NV4: st = launch_v<F_NV4, kF16>(p, w, vs, s); break;
     case F_NV4B32: st = launch_v<F_NV4B32, kF16>(p, w, vs, s); break;
     default: st = launch_v<F_MX4, kF16>(p, w, vs, s); break;
