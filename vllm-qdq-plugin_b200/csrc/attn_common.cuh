@@ -26,6 +26,18 @@ __host__ __device__ constexpr bool fmt_block16(int f) { return f == F_NV4 || f =
 // Formats held as E4M3 codes (128-byte rows, kind::mxf8f6f4).
 __host__ __device__ constexpr bool fmt_e4m3(int f) { return f == F_MX8 || f == F_G9 || f == F_E8; }
 
+// The 9-level grid of the reference's emulated E2M1 (quant_primitives.py:52-71)
+// for a >= 0: 0 below 0.25, 0.5 below 0.5, and from 0.5 up the value rounded
+// to one mantissa bit with ties upward (adding half of that bit to the fp32
+// pattern), capped at 6.  The midpoints 0.625, 0.875, 1.25, 1.75, 2.5, 3.5
+// and 5 are exactly the one-bit ties, so every threshold `a < t` of the
+// reference's compare chain is reproduced.  Every result is an E4M3 value.
+// Used by the pre-pass (Q / K / V codes) and the flash kernel (P codes).
+__device__ __forceinline__ float grid9_mag(float a) {
+  const float r = __uint_as_float((__float_as_uint(a) + 0x00200000u) & 0xFFC00000u);
+  return a < 0.5f ? (a < 0.25f ? 0.0f : 0.5f) : fminf(r, 6.0f);
+}
+
 // One attention problem: Q, K, V, O in the NHD layout [B, L, H, D] (D = 128,
 // element stride 1) with arbitrary batch / token / head strides (elements).
 struct Problem {

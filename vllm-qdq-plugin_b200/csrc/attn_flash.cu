@@ -287,16 +287,6 @@ __device__ __forceinline__ float max32(const float* v) {
 // ---------------------------------------------------------------------------
 // softmax warpgroup: one query tile, thread = row
 // ---------------------------------------------------------------------------
-// The reference's 9-level grid for a >= 0 (quant_primitives.py:52-71): 0
-// below 0.25, 0.5 below 0.5, and from 0.5 up the value rounded to one
-// mantissa bit with ties upward (half of that bit added to the fp32 pattern),
-// capped at 6; the grid's midpoints are exactly those ties.  Every result is
-// an E4M3 value.
-__device__ __forceinline__ float grid9_mag(float a) {
-  const float r = __uint_as_float((__float_as_uint(a) + 0x00200000u) & 0xFFC00000u);
-  return a < 0.5f ? (a < 0.25f ? 0.0f : 0.5f) : fminf(r, 6.0f);
-}
-
 // Sum of four E4M3 bytes (exact in fp32).
 __device__ __forceinline__ float e4m3x4_sum(uint32_t w) {
   uint32_t h0, h1;

@@ -130,17 +130,6 @@ __device__ __forceinline__ uint32_t mx8_quant32(const float* v, uint8_t* out) {
 
 
 
-// The 9-level grid of the reference's emulated E2M1 (quant_primitives.py:52-71)
-// for a >= 0: 0 below 0.25, 0.5 below 0.5, and from 0.5 up the value rounded
-// to one mantissa bit with ties upward (adding half of that bit to the fp32
-// pattern), capped at 6.  The midpoints 0.625, 0.875, 1.25, 1.75, 2.5, 3.5
-// and 5 are exactly the one-bit ties, so every threshold `a < t` of the
-// reference's compare chain is reproduced.  Every result is an E4M3 value.
-__device__ __forceinline__ float grid9_mag(float a) {
-  const float r = __uint_as_float((__float_as_uint(a) + 0x00200000u) & 0xFFC00000u);
-  return a < 0.5f ? (a < 0.25f ? 0.0f : 0.5f) : fminf(r, 6.0f);
-}
-
 // One 32-element group of the reference's emulated E8M0 QuantConfigs
 // (quantize_qk / quantize_v, quantize.py:21-141, with round_to_e8m0_torch,
 // quant_primitives.py:140-151), every step in the input dtype T:
