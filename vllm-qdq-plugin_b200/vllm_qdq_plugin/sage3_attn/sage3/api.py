@@ -17,11 +17,15 @@ Every in-scope config runs one kernel pair in libqdq_b200.so
 Config mapping:
   "mxfp4_hw"  MXFP4 with the reference hardware kernel's semantics
               (sage3/mxfp4_hw_kernel.py): E8M0 per 32, l = sum of unquantised P.
-  "mxfp4"     the reference's emulated MXFP4 config (attention_kernel.py +
-              p_quant_mxfp4) runs on the same real-MXFP4 kernel; its 9-level
-              emulation grid has no hardware equivalent, so parity with it is
-              by tolerance.
-  "nvfp4"     NVFP4 (E4M3 per 16).
+  "mxfp4"     the reference's emulated MXFP4 config (quantize.py +
+              attention_kernel.py + p_quant_mxfp4) computed as the reference
+              does: its fake-quantisation steps and 9-level grid {0, .5, .75,
+              1, 1.5, 2, 3, 4, 6} (0.75 is no E2M1 value), held as E4M3 codes
+              with E8M0 scales on kind::mxf8f6f4 MMAs; the same holds for the
+              other emulated configs with E8M0 scales below.
+  "nvfp4"     NVFP4 (E4M3 per 16) on real E2M1 codes: a 9-level-grid value
+              times an E4M3 scale fits no block-scaled MMA operand, so parity
+              with the reference's emulation is by tolerance.
   "mxfp8_hw"  MXFP8 (E4M3 + E8M0 per 32) Q/K/V and P with the reference
               hardware kernel's semantics (sage3/mxfp8_hw_kernel.py,
               quantize_to_mxfp8), on kind::mxf8f6f4 tensor-core MMAs.
