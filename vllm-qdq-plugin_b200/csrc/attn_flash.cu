@@ -9,9 +9,11 @@
 //   P quantised per row and 32 keys: e = clamp(ceil(log2(max(p)/6)), -127, 127),
 //     codes = cvt.rn.satfinite.e2m1x2(p * 2^-e),
 //   O += dot_scaled(P, V), O / l at the end;
-// and, for the emulated configs (p_quant_kernels.py:37-150,
-// attention_kernel.py:176-186), P scaled by 448*6 before block scaling and
-// l = sum of the dequantised P.  The mxfp8_hw kernel
+// and, for the emulated configs (p_quant_kernels.py:37-283,
+// attention_kernel.py:176-186), P scaled by 448*6 (two-level configs) before
+// block scaling and l = sum of the dequantised P; those with E8M0 scales
+// encode P on the reference's 9-level grid as E4M3 codes (P/V format F_G9),
+// their Q / K / V arriving from the pre-pass the same way.  The mxfp8_hw kernel
 // (sage3/mxfp8_hw_kernel.py:88-246) is the mxfp4_hw one with E4M3 operands:
 // P scale e = clamp(ceil(log2(max(p)/448)), -127, 127), codes
 // E4M3(min(p * 2^-e, 448)) round-to-nearest-even.  Keys beyond L are masked
